@@ -1,0 +1,435 @@
+"""Benchmark of the decode hot path on B200 (one JSON line on rank 0).
+
+Workload (the config the metric is quoted on): the q4nx
+W4A16 GEMV sweep over a dense GQA 3B decoder's projection shapes -- QKV
+2560->3584, O 2560->2560, gate+up 2560->16384, down 8192->2560 -- for all 40
+layers, batch 1.  One step = the 160 GEMVs of one decode step's weight stream
+(1.966 GB, larger than L2), issued in decode order from one CUDA graph.
+Synthetic seeded weights with the BASELINE distributions (codes uniform 0..15,
+d = |N(0,.02)|, m = -|N(0,.02)|), x ~ N(0,1) bf16.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+N > 1 (torchrun): every rank streams its own full sweep (weak scaling, no
+data-path collective); time = max over ranks; value = all ranks' bytes / time.
+`--impl reference` times the reference's own CPU GEMV (designs/granite_gemv/
+cpu_baseline.cpp, compiled unmodified into oracle/_ref/) on this host's cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "q4/q8 GEMV HBM GB/s (% of peak); decode tokens/s at 1/2/4/8 B200"
+SHAPES = [("qkv", 112, 10), ("o", 80, 10), ("gate_up", 512, 10), ("down", 80, 32)]  # (tile-rows, K-tiles)
+Q4_TILE, Q8_TILE = 5120, 8704
+LAYERS = 40
+
+
+def peaks() -> dict:
+    try:
+        p = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return {"hbm_gbs": float(p["hbm_gbs"]), "src": "measured"}
+    except (OSError, KeyError, ValueError):
+        return {"hbm_gbs": 6650.0, "src": "fallback"}
+
+
+# ------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clock and throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.lines: list[str] = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", self.gpu_id], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def gpu_uuid(torch) -> str:
+    try:
+        u = str(torch.cuda.get_device_properties(torch.cuda.current_device()).uuid)
+        return u if u.startswith("GPU-") else f"GPU-{u}"
+    except Exception:
+        return str(torch.cuda.current_device())
+
+
+# -------------------------------------------------------------- CPU baselines
+def _write_sample_file(path: Path, n_tiles: int, rng) -> None:
+    import numpy as np
+    from oracle import q4nx_oracle as orc
+    with path.open("wb") as f:
+        left = n_tiles
+        while left:
+            n = min(left, 4096)
+            f.write(orc.synth_q4_tiles(rng, n).tobytes())
+            left -= n
+
+
+def run_reference_gemv(iters: int, layers: int = 8) -> dict:
+    """The reference's cpu_baseline.cpp (oracle/_ref) over `layers` layers' projections, all cores.
+
+    Falls back to the numpy oracle port when the compiled reference is absent.
+    Returns {"gbs", "cores", "kind", "sample", "seconds"}.
+    """
+    import numpy as np
+    exe = ROOT / "oracle" / "_ref" / "cpu_baseline"
+    cores = os.cpu_count() or 1
+    rng = np.random.default_rng(1234)
+    k2560_rows = sum(n for name, n, k in SHAPES if k == 10) * layers
+    k8192_rows = sum(n for name, n, k in SHAPES if k == 32) * layers
+    groups = [(k2560_rows, 10), (k8192_rows, 32)]
+    total_bytes = sum(r * k * Q4_TILE for r, k in groups)
+    t0 = time.time()
+    if exe.exists():
+        tot_ms = 0.0
+        with tempfile.TemporaryDirectory() as td:
+            for rows, kt in groups:
+                p = Path(td) / f"w{kt}.bin"
+                _write_sample_file(p, rows * kt, rng)
+                r = subprocess.run([str(exe), str(p), "0", str(rows), str(kt), str(cores), str(iters)],
+                                   capture_output=True, text=True, timeout=900)
+                if r.returncode != 0:
+                    raise RuntimeError(f"cpu_baseline failed: {r.stderr}")
+                line = next(ln for ln in r.stdout.splitlines() if ln.startswith("GEMV"))
+                tot_ms += float(line.split()[1])
+        gbs = total_bytes / (tot_ms * 1e-3) / 1e9
+        kind = "reference"
+    else:
+        from oracle import q4nx_oracle as orc
+        w = orc.synth_q4_tiles(rng, 80 * 10)
+        x = orc.synth_bf16(rng, 2560)
+        n = 0
+        t1 = time.time()
+        while time.time() - t1 < 5.0:
+            orc.gemv_q4(w, x, 80, 10)
+            n += 1
+        gbs = n * w.nbytes / (time.time() - t1) / 1e9
+        kind, cores = "port", 1
+    return {"gbs": gbs, "cores": cores, "kind": kind, "seconds": time.time() - t0,
+            "sample": (f"{layers} layers of the 4 projection shapes ({total_bytes / 1e6:.0f} MB of q4 tiles), "
+                       f"batch 1, {iters} passes each" if kind == "reference"
+                       else "one 80x10-tile O projection, numpy oracle, 5 s")}
+
+
+# --------------------------------------------------------------------- B200
+def make_q4_tiles(torch, n_tiles: int, gen, device):
+    w = torch.randint(0, 256, (n_tiles, Q4_TILE), dtype=torch.uint8, device=device, generator=gen)
+    d = (torch.randn(n_tiles, 256, device=device, generator=gen) * 0.02).abs().to(torch.bfloat16)
+    m = -(torch.randn(n_tiles, 256, device=device, generator=gen) * 0.02).abs().to(torch.bfloat16)
+    w[:, 0:512] = d.view(torch.uint8)
+    w[:, 512:1024] = m.view(torch.uint8)
+    return w.reshape(-1)
+
+
+def make_q8_tiles(torch, n_tiles: int, gen, device):
+    w = torch.randint(-127, 128, (n_tiles, Q8_TILE), dtype=torch.int16, device=device, generator=gen)
+    w = w.to(torch.int8).view(torch.uint8)
+    s = (torch.randn(n_tiles, 256, device=device, generator=gen) * 0.02).abs().to(torch.bfloat16)
+    w[:, 0:512] = s.view(torch.uint8)
+    return w.reshape(-1)
+
+
+def build_sweep(torch, ops, batch: int, layers: int, gen, device):
+    """Weights, inputs and outputs of the 40-layer sweep; returns (calls, bytes)."""
+    calls, nbytes = [], 0
+    for _ in range(layers):
+        for name, n_t, k_t in SHAPES:
+            w = make_q4_tiles(torch, n_t * k_t, gen, device)
+            x = torch.randn(batch, k_t * 256, device=device, generator=gen).to(torch.bfloat16)
+            y = torch.empty(batch, n_t * 32, device=device, dtype=torch.float32)
+            calls.append((name, w, n_t, k_t, x, y))
+            nbytes += w.numel()
+    return calls, nbytes
+
+
+def graph_of(torch, fn):
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()  # warm the launch plans outside capture
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    return g
+
+
+def time_graph(torch, g, steps: int, warmup: int) -> float:
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        g.replay()
+    b.record()
+    b.synchronize()
+    return a.elapsed_time(b) / steps  # ms per replay
+
+
+def run_b200(args, rank: int, world: int) -> dict | None:
+    import torch
+    import torch.distributed as dist
+    from llmnputest_b200 import ops
+
+    device = torch.device("cuda", torch.cuda.current_device())
+    gen = torch.Generator(device=device)
+    gen.manual_seed(1000 + rank)
+    pk = peaks()
+
+    calls, step_bytes = build_sweep(torch, ops, args.batch, args.layers, gen, device)
+
+    def sweep():
+        for _, w, n_t, k_t, x, y in calls:
+            ops.q4_gemv(w, n_t, k_t, x, out=y)
+
+    g = graph_of(torch, sweep)
+    n_launch = len(calls)
+
+    # ---- timed region (value): K replays, barrier + sync both sides, max over ranks
+    for _ in range(args.warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    with ClockSampler(gpu_uuid(torch)) as clk:
+        time.sleep(0.15)  # let the sampler start
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            g.replay()
+        b.record()
+        b.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    gbs_total = world * step_bytes / (ms * 1e-3) / 1e9
+    gbs_per_gpu = step_bytes / (ms * 1e-3) / 1e9
+
+    extras = {}
+    if rank == 0 and not args.quick:
+        # per-shape GB/s (40 launches of one shape per replay, > L2 except O/QKV pools)
+        per_shape = {}
+        for name, n_t, k_t in SHAPES:
+            sub = [c for c in calls if c[0] == name]
+            gs = graph_of(torch, lambda sub=sub: [ops.q4_gemv(w, n, k, x, out=y) for _, w, n, k, x, y in sub])
+            t_ms = time_graph(torch, gs, max(20, args.steps // 10), 3)
+            per_shape[name] = round(sum(c[1].numel() for c in sub) / (t_ms * 1e-3) / 1e9, 1)
+            del gs
+        extras["per_shape_gbs_b1"] = per_shape
+        # batch 8 (config 2's other batch size): same weights, 8-token activations
+        calls8 = [(n, w, nt, kt, torch.randn(8, kt * 256, device=device, generator=gen).to(torch.bfloat16),
+                   torch.empty(8, nt * 32, device=device)) for n, w, nt, kt, _, _ in calls]
+        g8 = graph_of(torch, lambda: [ops.q4_gemv(w, n, k, x, out=y) for _, w, n, k, x, y in calls8])
+        t8 = time_graph(torch, g8, max(20, args.steps // 10), 3)
+        extras["batch8_gbs"] = round(step_bytes / (t8 * 1e-3) / 1e9, 1)
+        del g8, calls8
+        # q8 lm_head (config 1): 248320 x 1024, batch 1, 270 MB > L2
+        w8 = make_q8_tiles(torch, 7760 * 4, gen, device)
+        x8 = torch.randn(1, 1024, device=device, generator=gen).to(torch.bfloat16)
+        y8 = torch.empty(1, 248320, device=device)
+        gl = graph_of(torch, lambda: ops.q8_gemv(w8, 7760, 4, x8, out=y8))
+        tl = time_graph(torch, gl, max(50, args.steps // 5), 5)
+        extras["q8_lm_head"] = {"us": round(tl * 1e3, 2), "gbs": round(w8.numel() / (tl * 1e-3) / 1e9, 1),
+                                "frac_of_measured_hbm": round(w8.numel() / (tl * 1e-3) / 1e9 / pk["hbm_gbs"], 3)}
+        del gl, w8
+
+    # ---- e2e: host buffers, copies inside the timed region
+    xs_host = torch.cat([c[4].reshape(-1) for c in calls]).cpu().pin_memory()
+    ys_host = torch.empty(sum(c[5].numel() for c in calls), dtype=torch.float32).pin_memory()
+    x_dev = torch.empty_like(xs_host, device=device)
+    y_dev = torch.empty(ys_host.numel(), dtype=torch.float32, device=device)
+    views, off_x, off_y = [], 0, 0
+    for name, w, n_t, k_t, x, y in calls:
+        views.append((w, n_t, k_t, x_dev[off_x:off_x + x.numel()].view(x.shape),
+                      y_dev[off_y:off_y + y.numel()].view(y.shape)))
+        off_x += x.numel()
+        off_y += y.numel()
+
+    def sweep_e2e():
+        for w, n_t, k_t, x, y in views:
+            ops.q4_gemv(w, n_t, k_t, x, out=y)
+
+    ge = graph_of(torch, sweep_e2e)
+    e2e_steps = max(10, args.steps // 10)
+
+    def e2e_step():
+        x_dev.copy_(xs_host, non_blocking=True)
+        ge.replay()
+        ys_host.copy_(y_dev, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+
+    for _ in range(args.warmup):
+        e2e_step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    b.record()
+    b.synchronize()
+    e2e_ms = a.elapsed_time(b) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_gbs = world * step_bytes / (e2e_ms * 1e-3) / 1e9
+    assert ops.device_error() == 0, "a kernel recorded a device-side error"
+
+    if rank != 0:
+        return None
+    out = {
+        "metric": METRIC,
+        "value": round(gbs_total, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded q4nx tiles with BASELINE distributions, x ~ N(0,1) bf16)",
+        "config": {
+            "workload": "config 2: q4nx W4A16 GEMV sweep, QKV 2560->3584 / O 2560->2560 / gate+up 2560->16384 / "
+                        "down 8192->2560, 40 layers, batch 1, one CUDA graph per step",
+            "batch": args.batch, "layers": args.layers, "bytes_per_step_per_gpu": step_bytes,
+            "l2": "inputs larger than L2 (1.97 GB of weights streamed per step)",
+            "parallelism": f"replicas x{world} (each rank streams its own weights, no collective)",
+        },
+        "gpu_launches": n_launch * args.steps,
+        "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s",
+                "h2d_bytes_per_step": int(xs_host.numel() * 2), "d2h_bytes_per_step": int(ys_host.numel() * 4)},
+        "roofline": {"bound": "hbm", "achieved": round(gbs_per_gpu, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(gbs_per_gpu / pk["hbm_gbs"], 4), "traffic": None,
+                     "kernel": "q4nx_gemv_kernel<q4,NB=1,f32>", "peak_src": pk["src"]},
+        "clocks": clk.summary(),
+    }
+    out.update(extras)
+    if world == 1 and not args.no_cpu_baseline:
+        cb = run_reference_gemv(iters=20)
+        out["cpu_baseline"] = {"value": round(cb["gbs"], 2), "unit": "GB/s", "cores": cb["cores"],
+                               "kind": cb["kind"], "sample": cb["sample"]}
+    return out
+
+
+def run_reference(args, rank: int) -> dict | None:
+    if rank != 0:
+        return None
+    t0 = time.time()
+    cb = run_reference_gemv(iters=max(1, args.steps // 10), layers=8)
+    sec = time.time() - t0
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(cb["gbs"], 2), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32 (bf16 codes -> fp32 AVX2 FMA)", "data": "synthetic",
+        "config": {"workload": "config 2: q4nx W4A16 GEMV sweep shapes, batch 1 (reference CPU GEMV)",
+                   "batch": 1},
+        "cpu_baseline": {"value": round(cb["gbs"], 2), "unit": "GB/s", "cores": cb["cores"], "kind": cb["kind"],
+                         "sample": cb["sample"]},
+        "e2e": {"value": round(cb["gbs"], 2), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "wall_s": round(sec, 1),
+    }
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--quick", action="store_true", help="skip the extra per-shape / q8 / batch-8 lines")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        res = run_reference(args, rank)
+    else:
+        import torch
+        torch.cuda.set_device(local)
+        if world > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
+        res = run_b200(args, rank, world)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+    if res is not None:
+        print(json.dumps(res), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,114 @@
+/*
+ * b2q4nx -- C ABI of the B200 decode-path library for FastFlowLM q4nx weights.
+ *
+ * This is the drop-in boundary of the framework: plain pointers, sizes and a
+ * CUDA stream passed as `void*`; no torch or CUDA types in any signature.  The
+ * Python host layer (llmnputest_b200.npu / .ops) binds it with ctypes; any other
+ * host language binds the same symbols.
+ *
+ * Conventions shared by every entry point:
+ *   - All data pointers are DEVICE pointers owned by the caller.  The library
+ *     allocates no device memory per call.
+ *   - bf16 values are passed as `uint16_t` bit patterns.
+ *   - `stream` is a cudaStream_t (NULL = the legacy default stream).  Calls are
+ *     stream-ordered and asynchronous; nothing synchronises the host except
+ *     b2_read_device_error().
+ *   - Return value: B2_OK (0) or a negative b2_status.  b2_last_error_message()
+ *     describes the last failure on the calling thread.
+ *   - Weights are q4nx tiles exactly as stored in the .q4nx file: tile-row major
+ *     [n_tile_rows][k_tiles][tile_bytes] (tile_bytes 5120 for q4, 8704 for q8),
+ *     32 output rows x 256 k per tile.  They must be 16-byte aligned.
+ *
+ * Reference interfaces replaced (file:line in vegah/LLMNpuTest):
+ *   NpuDesign.upload/run/download   reference/npu.py:89-114
+ *   NpuLmHead.forward               reference/npu.py:137-150
+ *   lmhead_q8_k{0..3}               designs/lm_head/lm_head.h:106-115
+ *   granite_gemv_p{P}b{B}_k{N}      designs/granite_gemv/granite_gemv.h:282-302
+ *   q4nx_unpack_tile                designs/q4nx_unpack/q4nx_unpack.cc:40-92
+ *   Q4NX.tensor dequant             tools/q4nx.py:127-197
+ */
+#ifndef B2Q4NX_H_
+#define B2Q4NX_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum b2_status {
+  B2_OK = 0,
+  B2_ERR_ARG = -1,         /* a size or pointer argument is invalid */
+  B2_ERR_ALIGN = -2,       /* a pointer or leading dimension is misaligned */
+  B2_ERR_CUDA = -3,        /* a CUDA runtime call or kernel launch failed */
+  B2_ERR_NO_DEVICE = -4,   /* no CUDA device is current */
+  B2_ERR_UNSUPPORTED = -5, /* the current device is not sm_100 (B200) */
+  B2_ERR_WORKSPACE = -6,   /* workspace missing or too small */
+  B2_ERR_DEVICE = -7       /* a kernel recorded a device-side error (bounded wait ran out) */
+} b2_status;
+
+/* Library version, (major << 16) | (minor << 8) | patch. */
+int b2_version(void);
+
+/* Human-readable text for a b2_status, and the detail of the last failure on
+ * this thread (empty string if none). */
+const char* b2_status_string(int status);
+const char* b2_last_error_message(void);
+
+/* Launch options for every later call on this process:
+ *   pdl != 0: launch with programmatic dependent launch, so a kernel's prologue
+ *   overlaps the tail of the previous kernel in the stream (default on). */
+int b2_set_launch_options(int pdl);
+
+/* Read and clear the device error word that kernels set when a bounded wait
+ * gives up (0 = none).  Synchronises `stream`.  Returns B2_OK or B2_ERR_CUDA. */
+int b2_read_device_error(int* code, void* stream);
+
+/* Flags for the GEMV entry points. */
+#define B2_GEMV_ACCUMULATE 1 /* y += W x (residual add) instead of y = W x */
+#define B2_GEMV_PREFETCH 2   /* weights are not written by earlier kernels in the
+                                stream: they may be streamed before the PDL wait */
+
+/* y[b][n] = sum_k W[n][k] x[b][k] for a q4nx q4 (W4A16) weight.
+ *   tiles     [n_tile_rows][k_tiles][5120] bytes
+ *   x         bf16 [batch][ldx], 16-byte aligned, ldx % 8 == 0, ldx >= 256*k_tiles
+ *   y         fp32 [batch][ldy], ldy >= 32*n_tile_rows
+ *   batch     1..16
+ * Replaces granite_gemv_p{P}b{B}_k{N} (designs/granite_gemv/granite_gemv.h:282-302)
+ * and its host oracle granite_gemv.reference (granite_gemv.py:256-272). */
+int b2_q4_gemv(const uint8_t* tiles, int n_tile_rows, int k_tiles, const uint16_t* x, int batch, int ldx,
+               float* y, int ldy, int flags, void* stream);
+
+/* Same for a q4nx q8 (W8A16) weight, tiles [n_tile_rows][k_tiles][8704].
+ * Replaces lmhead_q8_k{0..3} (designs/lm_head/lm_head.h:53-115) and
+ * lm_head.reference (designs/lm_head/lm_head.py:129-144). */
+int b2_q8_gemv(const uint8_t* tiles, int n_tile_rows, int k_tiles, const uint16_t* x, int batch, int ldx,
+               float* y, int ldy, int flags, void* stream);
+
+/* Fused gate/up GEMV + SwiGLU: h[b][n] = silu(bf16(G x)) * bf16(U x), bf16 out.
+ *   gate, up  q4 tiles [n_tile_rows][k_tiles][5120] each (same shape)
+ *   h         bf16 [batch][ldh], ldh >= 32*n_tile_rows
+ * Replaces the gate+up+SwiGLU design (designs/granite_gemv/granite_mlp.py:48-133,
+ * granite_swiglu_f32.h:27-51). */
+int b2_q4_swiglu_gemv(const uint8_t* gate, const uint8_t* up, int n_tile_rows, int k_tiles, const uint16_t* x,
+                      int batch, int ldx, uint16_t* h, int ldh, int flags, void* stream);
+
+/* Tile decode, weight-index order: out bf16 [n_tiles][8192] = RNE(code*d + m)
+ * (q4) or RNE(code*s) (q8).  Bit-exact with tools/q4nx.py dequant_q4 / dequant_q8
+ * (:97-111) and designs/q4nx_unpack/q4nx_unpack.cc:40-92. */
+int b2_q4_dequant_tiles(const uint8_t* tiles, int64_t n_tiles, uint16_t* out, void* stream);
+int b2_q8_dequant_tiles(const uint8_t* tiles, int64_t n_tiles, uint16_t* out, void* stream);
+
+/* Whole-tensor decode to an untiled fp32 matrix out[n_tile_rows*32][ld]
+ * (column k), bit-exact with Q4NX.tensor (tools/q4nx.py:127-197). */
+int b2_q4_dequant_matrix(const uint8_t* tiles, int n_tile_rows, int k_tiles, float* out, int64_t ld,
+                         void* stream);
+int b2_q8_dequant_matrix(const uint8_t* tiles, int n_tile_rows, int k_tiles, float* out, int64_t ld,
+                         void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2Q4NX_H_ */

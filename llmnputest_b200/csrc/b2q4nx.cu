@@ -1,0 +1,304 @@
+// b2q4nx: the C-ABI shared library (one translation unit; the kernels live in
+// the .cuh files it includes so that the device error word is a single symbol).
+//
+// Host responsibilities per call: validate shapes/alignment, pick the launch
+// plan (split-K cluster size, persistent grid, pipeline depth) from the device's
+// SM count and shared-memory limit, and launch on the caller's stream.
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/b2q4nx.h"
+#include "b2_common.cuh"
+#include "q4nx_dequant.cuh"
+#include "q4nx_gemv.cuh"
+
+namespace {
+
+thread_local char g_msg[512] = "";
+int g_pdl = 1;
+
+int fail(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  cudaGetLastError();  // clear the sticky-free error so later calls see their own
+  return fail(B2_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+struct DevInfo {
+  int ok = 0;
+  int sms = 0;
+  int smem_optin = 0;
+  int major = 0, minor = 0;
+};
+
+std::mutex g_mu;
+DevInfo g_dev[64];
+
+// Current device's properties; B2_OK or an error status.
+int device_info(DevInfo* out) {
+  int d = -1;
+  cudaError_t e = cudaGetDevice(&d);
+  if (e != cudaSuccess || d < 0) return fail(B2_ERR_NO_DEVICE, "no current CUDA device (%s)", cudaGetErrorString(e));
+  if (d >= 64) return fail(B2_ERR_NO_DEVICE, "device ordinal %d out of range", d);
+  std::lock_guard<std::mutex> lk(g_mu);
+  DevInfo& di = g_dev[d];
+  if (!di.ok) {
+    cudaDeviceProp prop;
+    e = cudaGetDeviceProperties(&prop, d);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceProperties");
+    di.sms = prop.multiProcessorCount;
+    di.smem_optin = static_cast<int>(prop.sharedMemPerBlockOptin);
+    di.major = prop.major;
+    di.minor = prop.minor;
+    di.ok = 1;
+  }
+  if (di.major != 10) return fail(B2_ERR_UNSUPPORTED, "device is sm_%d%d; this library is built for sm_100a", di.major, di.minor);
+  *out = di;
+  return B2_OK;
+}
+
+inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// ------------------------------------------------------------------ GEMV
+template <int QT, int NB, int EPI>
+int launch_gemv_t(b2::GemvParams p, const DevInfo& di, cudaStream_t stream) {
+  using namespace b2;
+  auto kernel = q4nx_gemv_kernel<QT, NB, EPI>;
+  constexpr int SLOT = QTraits<QT>::kSlot;
+  static int attr_set[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, di.smem_optin);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv smem)");
+    attr_set[dev] = 1;
+  }
+
+  const int G = p.n_groups;
+  // split-K: enough CTAs to cover the SMs when there are fewer groups than SMs
+  int S = 1;
+  if (G < di.sms) S = std::min(std::min(8, p.k_tiles), (di.sms + G - 1) / G);
+  // keep the staged x slice bounded (8*NB rows x kt*256 bf16)
+  const int kt_cap = 12 / NB;
+  S = std::max(S, std::min(8, (p.k_tiles + kt_cap - 1) / kt_cap));
+  S = std::min(S, p.k_tiles);
+  int ktps = (p.k_tiles + S - 1) / S;
+  S = (p.k_tiles + ktps - 1) / ktps;  // no empty split
+
+  const int x_stride = ktps * 256 + 8;
+  // fixed part of shared memory, then as many pipeline stages as fit
+  const GemvSmem base(SLOT, NB, 0, x_stride, ktps);
+  const int fixed = base.total + 2 * kMaxStages * 8;
+  int grid_y;
+  if (S == 1) {
+    grid_y = std::min(G, di.sms);  // persistent over groups
+  } else {
+    if (G > 65535) return fail(B2_ERR_ARG, "too many row groups (%d) for a split-K grid", G);
+    grid_y = G;
+  }
+  const int groups_per_cta = (G + grid_y - 1) / grid_y;
+  const int total_stages = ktps * groups_per_cta;
+  int stages = std::min(kMaxStages, (di.smem_optin - fixed) / (4 * SLOT));
+  stages = std::min(stages, total_stages);
+  if (stages < 1) return fail(B2_ERR_ARG, "K slice too large for shared memory");
+  const GemvSmem L(SLOT, NB, stages, x_stride, ktps);
+
+  p.kt_per_split = ktps;
+  p.n_splits = S;
+  p.stages = stages;
+  p.x_stride = x_stride;
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(S, grid_y, 1);
+  cfg.blockDim = dim3(kGemvThreads, 1, 1);
+  cfg.dynamicSmemBytes = L.total;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[2];
+  int na = 0;
+  if (S > 1) {
+    attrs[na].id = cudaLaunchAttributeClusterDimension;
+    attrs[na].val.clusterDim.x = S;
+    attrs[na].val.clusterDim.y = 1;
+    attrs[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (g_pdl) {
+    attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = na;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p);
+  if (e != cudaSuccess) return cuda_fail(e, "gemv launch");
+  return B2_OK;
+}
+
+int gemv_common(int qt, int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_rows, int k_tiles,
+                const uint16_t* x, int batch, int ldx, void* y, int ldy, int flags, void* stream) {
+  DevInfo di;
+  int st = device_info(&di);
+  if (st != B2_OK) return st;
+  if (!w0 || !x || !y || (epi == b2::kEpiSwiglu && !w1)) return fail(B2_ERR_ARG, "null pointer argument");
+  if (n_tile_rows < 1 || k_tiles < 1) return fail(B2_ERR_ARG, "n_tile_rows=%d k_tiles=%d", n_tile_rows, k_tiles);
+  if (batch < 1 || batch > 16) return fail(B2_ERR_ARG, "batch %d outside 1..16", batch);
+  if (ldx < k_tiles * 256) return fail(B2_ERR_ARG, "ldx %d < K %d", ldx, k_tiles * 256);
+  if (ldy < n_tile_rows * 32) return fail(B2_ERR_ARG, "ldy %d < N %d", ldy, n_tile_rows * 32);
+  if (!aligned(w0, 16) || (w1 && !aligned(w1, 16))) return fail(B2_ERR_ALIGN, "weights must be 16-byte aligned");
+  if (!aligned(x, 16) || (ldx % 8)) return fail(B2_ERR_ALIGN, "x must be 16-byte aligned with ldx %% 8 == 0");
+  if (!aligned(y, epi == b2::kEpiSwiglu ? 2 : 4)) return fail(B2_ERR_ALIGN, "y misaligned");
+  if ((flags & ~(B2_GEMV_ACCUMULATE | B2_GEMV_PREFETCH)) != 0) return fail(B2_ERR_ARG, "unknown flags 0x%x", flags);
+  if (epi == b2::kEpiSwiglu && (flags & B2_GEMV_ACCUMULATE)) return fail(B2_ERR_ARG, "SwiGLU cannot accumulate");
+
+  b2::GemvParams p = {};
+  p.w0 = w0;
+  p.w1 = w1;
+  p.n_tile_rows = n_tile_rows;
+  p.k_tiles = k_tiles;
+  p.x = reinterpret_cast<const __nv_bfloat16*>(x);
+  p.batch = batch;
+  p.ldx = ldx;
+  p.y = y;
+  p.ldy = ldy;
+  p.accumulate = (flags & B2_GEMV_ACCUMULATE) ? 1 : 0;
+  p.prefetch_before_wait = (flags & B2_GEMV_PREFETCH) ? 1 : 0;
+  p.n_groups = epi == b2::kEpiSwiglu ? (n_tile_rows + 1) / 2 : (n_tile_rows + 3) / 4;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int nb = batch <= 8 ? 1 : 2;
+  if (qt == b2::kQ4 && epi == b2::kEpiF32)
+    return nb == 1 ? launch_gemv_t<b2::kQ4, 1, b2::kEpiF32>(p, di, s) : launch_gemv_t<b2::kQ4, 2, b2::kEpiF32>(p, di, s);
+  if (qt == b2::kQ8 && epi == b2::kEpiF32)
+    return nb == 1 ? launch_gemv_t<b2::kQ8, 1, b2::kEpiF32>(p, di, s) : launch_gemv_t<b2::kQ8, 2, b2::kEpiF32>(p, di, s);
+  if (qt == b2::kQ4 && epi == b2::kEpiSwiglu)
+    return nb == 1 ? launch_gemv_t<b2::kQ4, 1, b2::kEpiSwiglu>(p, di, s)
+                   : launch_gemv_t<b2::kQ4, 2, b2::kEpiSwiglu>(p, di, s);
+  return fail(B2_ERR_ARG, "unsupported gemv variant");
+}
+
+// --------------------------------------------------------------- dequant
+int dequant_tiles(int qt, const uint8_t* tiles, int64_t n_tiles, uint16_t* out, void* stream) {
+  DevInfo di;
+  int st = device_info(&di);
+  if (st != B2_OK) return st;
+  if (!tiles || !out || n_tiles < 1) return fail(B2_ERR_ARG, "bad dequant arguments");
+  if (!aligned(tiles, 16) || !aligned(out, 16)) return fail(B2_ERR_ALIGN, "tiles and out must be 16-byte aligned");
+  const int grid = static_cast<int>(std::min<int64_t>(n_tiles, 8LL * di.sms));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out);
+  if (qt == 0)
+    b2::dequant_tiles_bf16_kernel<0><<<grid, 256, 0, s>>>(tiles, n_tiles, o);
+  else
+    b2::dequant_tiles_bf16_kernel<1><<<grid, 256, 0, s>>>(tiles, n_tiles, o);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "dequant launch");
+  return B2_OK;
+}
+
+int dequant_matrix(int qt, const uint8_t* tiles, int n_t, int k_t, float* out, int64_t ld, void* stream) {
+  DevInfo di;
+  int st = device_info(&di);
+  if (st != B2_OK) return st;
+  if (!tiles || !out || n_t < 1 || k_t < 1 || ld < static_cast<int64_t>(k_t) * 256)
+    return fail(B2_ERR_ARG, "bad dequant arguments");
+  if (!aligned(tiles, 16) || !aligned(out, 4)) return fail(B2_ERR_ALIGN, "tiles must be 16-byte aligned");
+  const int64_t n_tiles = static_cast<int64_t>(n_t) * k_t;
+  const int grid = static_cast<int>(std::min<int64_t>(n_tiles, 8LL * di.sms));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (qt == 0)
+    b2::dequant_matrix_f32_kernel<0><<<grid, 256, 0, s>>>(tiles, n_t, k_t, out, ld);
+  else
+    b2::dequant_matrix_f32_kernel<1><<<grid, 256, 0, s>>>(tiles, n_t, k_t, out, ld);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "dequant launch");
+  return B2_OK;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ C ABI
+extern "C" {
+
+int b2_version(void) { return (0 << 16) | (1 << 8) | 0; }
+
+const char* b2_status_string(int status) {
+  switch (status) {
+    case B2_OK: return "ok";
+    case B2_ERR_ARG: return "invalid argument";
+    case B2_ERR_ALIGN: return "misaligned pointer or leading dimension";
+    case B2_ERR_CUDA: return "CUDA error";
+    case B2_ERR_NO_DEVICE: return "no CUDA device";
+    case B2_ERR_UNSUPPORTED: return "unsupported device (needs sm_100)";
+    case B2_ERR_WORKSPACE: return "workspace missing or too small";
+    case B2_ERR_DEVICE: return "device-side error recorded";
+    default: return "unknown status";
+  }
+}
+
+const char* b2_last_error_message(void) { return g_msg; }
+
+int b2_set_launch_options(int pdl) {
+  g_pdl = pdl ? 1 : 0;
+  return B2_OK;
+}
+
+int b2_read_device_error(int* code, void* stream) {
+  if (!code) return fail(B2_ERR_ARG, "null code pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&v, b2::g_device_error, sizeof(int), 0, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
+  const int zero = 0;
+  e = cudaMemcpyToSymbolAsync(b2::g_device_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "clearing the device error word");
+  *code = v;
+  return B2_OK;
+}
+
+int b2_q4_gemv(const uint8_t* tiles, int n_tile_rows, int k_tiles, const uint16_t* x, int batch, int ldx,
+               float* y, int ldy, int flags, void* stream) {
+  return gemv_common(b2::kQ4, b2::kEpiF32, tiles, nullptr, n_tile_rows, k_tiles, x, batch, ldx, y, ldy, flags,
+                     stream);
+}
+
+int b2_q8_gemv(const uint8_t* tiles, int n_tile_rows, int k_tiles, const uint16_t* x, int batch, int ldx,
+               float* y, int ldy, int flags, void* stream) {
+  return gemv_common(b2::kQ8, b2::kEpiF32, tiles, nullptr, n_tile_rows, k_tiles, x, batch, ldx, y, ldy, flags,
+                     stream);
+}
+
+int b2_q4_swiglu_gemv(const uint8_t* gate, const uint8_t* up, int n_tile_rows, int k_tiles, const uint16_t* x,
+                      int batch, int ldx, uint16_t* h, int ldh, int flags, void* stream) {
+  return gemv_common(b2::kQ4, b2::kEpiSwiglu, gate, up, n_tile_rows, k_tiles, x, batch, ldx, h, ldh, flags,
+                     stream);
+}
+
+int b2_q4_dequant_tiles(const uint8_t* tiles, int64_t n_tiles, uint16_t* out, void* stream) {
+  return dequant_tiles(0, tiles, n_tiles, out, stream);
+}
+int b2_q8_dequant_tiles(const uint8_t* tiles, int64_t n_tiles, uint16_t* out, void* stream) {
+  return dequant_tiles(1, tiles, n_tiles, out, stream);
+}
+int b2_q4_dequant_matrix(const uint8_t* tiles, int n_tile_rows, int k_tiles, float* out, int64_t ld,
+                         void* stream) {
+  return dequant_matrix(0, tiles, n_tile_rows, k_tiles, out, ld, stream);
+}
+int b2_q8_dequant_matrix(const uint8_t* tiles, int n_tile_rows, int k_tiles, float* out, int64_t ld,
+                         void* stream) {
+  return dequant_matrix(1, tiles, n_tile_rows, k_tiles, out, ld, stream);
+}
+
+}  // extern "C"

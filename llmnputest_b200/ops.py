@@ -1,0 +1,140 @@
+"""torch-facing wrappers of the C ABI: device tensors in, device tensors out.
+
+Every function here checks dtype/device/contiguity and raises on anything the
+kernels do not support -- there is no eager or CPU fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _native
+from .format import Q4_TILE_BYTES, Q8_TILE_BYTES, TILE_K, TILE_ROWS
+
+GEMV_ACCUMULATE = 1
+GEMV_PREFETCH = 2
+
+
+def _stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _ptr(t: torch.Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _need(t: torch.Tensor, name: str, dtype: torch.dtype) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (no CPU fallback)")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+
+
+def _tiles(tiles: torch.Tensor, n_tile_rows: int, k_tiles: int, tile_bytes: int, name: str) -> None:
+    _need(tiles, name, torch.uint8)
+    if not tiles.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    want = n_tile_rows * k_tiles * tile_bytes
+    if tiles.numel() != want:
+        raise ValueError(f"{name}: {tiles.numel()} bytes, expected {n_tile_rows}x{k_tiles}x{tile_bytes} = {want}")
+
+
+def _x2d(x: torch.Tensor, k: int) -> torch.Tensor:
+    _need(x, "x", torch.bfloat16)
+    x2 = x.reshape(1, -1) if x.dim() == 1 else x
+    if x2.dim() != 2 or x2.shape[1] != k:
+        raise ValueError(f"x must be [K] or [B, K] with K={k}, got {tuple(x.shape)}")
+    if x2.stride(1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+        if k % 8:
+            raise ValueError("K must be a multiple of 8")
+    return x2
+
+
+def _gemv(name: str, tiles, n_tile_rows, k_tiles, tile_bytes, x, out, accumulate, prefetch):
+    _tiles(tiles, n_tile_rows, k_tiles, tile_bytes, "tiles")
+    k, n = k_tiles * TILE_K, n_tile_rows * TILE_ROWS
+    x2 = _x2d(x, k)
+    b = x2.shape[0]
+    if out is None:
+        if accumulate:
+            raise ValueError("accumulate=True needs out")
+        out = torch.empty((b, n), dtype=torch.float32, device=x2.device)
+    _need(out, "out", torch.float32)
+    if out.dim() != 2 or out.shape[0] != b or out.shape[1] < n or out.stride(1) != 1:
+        raise ValueError(f"out must be [B, >=N] row-major, got {tuple(out.shape)}")
+    flags = (GEMV_ACCUMULATE if accumulate else 0) | (GEMV_PREFETCH if prefetch else 0)
+    for b0 in range(0, b, 16):  # the kernel takes 16 tokens per weight pass
+        bb = min(16, b - b0)
+        _native.call(name, _ptr(tiles), n_tile_rows, k_tiles, ctypes.c_void_p(x2[b0].data_ptr()), bb,
+                     x2.stride(0), ctypes.c_void_p(out[b0].data_ptr()), out.stride(0), flags, _stream())
+    return out if x.dim() == 2 else out[0, :n]
+
+
+def q4_gemv(tiles: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tensor,
+            out: torch.Tensor | None = None, accumulate: bool = False, prefetch: bool = False) -> torch.Tensor:
+    """fp32 y = W x for a q4nx q4 weight (raw tiles as stored); x bf16 [K] or [B, K]."""
+    return _gemv("b2_q4_gemv", tiles, n_tile_rows, k_tiles, Q4_TILE_BYTES, x, out, accumulate, prefetch)
+
+
+def q8_gemv(tiles: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tensor,
+            out: torch.Tensor | None = None, accumulate: bool = False, prefetch: bool = False) -> torch.Tensor:
+    """fp32 y = W x for a q4nx q8 weight."""
+    return _gemv("b2_q8_gemv", tiles, n_tile_rows, k_tiles, Q8_TILE_BYTES, x, out, accumulate, prefetch)
+
+
+def q4_swiglu_gemv(gate: torch.Tensor, up: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tensor,
+                   out: torch.Tensor | None = None, prefetch: bool = False) -> torch.Tensor:
+    """bf16 h = silu(bf16(G x)) * bf16(U x), one fused kernel."""
+    _tiles(gate, n_tile_rows, k_tiles, Q4_TILE_BYTES, "gate")
+    _tiles(up, n_tile_rows, k_tiles, Q4_TILE_BYTES, "up")
+    k, n = k_tiles * TILE_K, n_tile_rows * TILE_ROWS
+    x2 = _x2d(x, k)
+    b = x2.shape[0]
+    if out is None:
+        out = torch.empty((b, n), dtype=torch.bfloat16, device=x2.device)
+    _need(out, "out", torch.bfloat16)
+    if out.dim() != 2 or out.shape[0] != b or out.shape[1] < n or out.stride(1) != 1:
+        raise ValueError(f"out must be [B, >=N] row-major, got {tuple(out.shape)}")
+    for b0 in range(0, b, 16):
+        bb = min(16, b - b0)
+        _native.call("b2_q4_swiglu_gemv", _ptr(gate), _ptr(up), n_tile_rows, k_tiles,
+                     ctypes.c_void_p(x2[b0].data_ptr()), bb, x2.stride(0),
+                     ctypes.c_void_p(out[b0].data_ptr()), out.stride(0), GEMV_PREFETCH if prefetch else 0,
+                     _stream())
+    return out if x.dim() == 2 else out[0, :n]
+
+
+def dequant_tiles(tiles: torch.Tensor, q8: bool = False) -> torch.Tensor:
+    """[T, tile] uint8 -> [T, 8192] bf16 in weight-index order (bit-exact decode)."""
+    tb = Q8_TILE_BYTES if q8 else Q4_TILE_BYTES
+    _need(tiles, "tiles", torch.uint8)
+    if not tiles.is_contiguous() or tiles.numel() % tb:
+        raise ValueError(f"tiles must be contiguous whole {tb}-byte tiles")
+    n = tiles.numel() // tb
+    out = torch.empty((n, 8192), dtype=torch.bfloat16, device=tiles.device)
+    _native.call("b2_q8_dequant_tiles" if q8 else "b2_q4_dequant_tiles", _ptr(tiles), n, _ptr(out), _stream())
+    return out
+
+
+def dequant_matrix(tiles: torch.Tensor, n_tile_rows: int, k_tiles: int, q8: bool = False) -> torch.Tensor:
+    """Whole tiled tensor -> float32 [N, K], untiled (the GPU form of Q4NX.tensor)."""
+    tb = Q8_TILE_BYTES if q8 else Q4_TILE_BYTES
+    _tiles(tiles, n_tile_rows, k_tiles, tb, "tiles")
+    out = torch.empty((n_tile_rows * TILE_ROWS, k_tiles * TILE_K), dtype=torch.float32, device=tiles.device)
+    _native.call("b2_q8_dequant_matrix" if q8 else "b2_q4_dequant_matrix", _ptr(tiles), n_tile_rows, k_tiles,
+                 _ptr(out), out.stride(0), _stream())
+    return out
+
+
+def set_launch_options(pdl: bool = True) -> None:
+    _native.call("b2_set_launch_options", 1 if pdl else 0)
+
+
+def device_error() -> int:
+    """Read and clear the device error word (synchronises the current stream)."""
+    return _native.read_device_error(torch.cuda.current_stream().cuda_stream)

@@ -1,0 +1,74 @@
+"""CPU-side checks of the boundary: the C-ABI library loads, exports every symbol
+include/b2q4nx.h declares, and its host-side logic behaves without a GPU.  The
+q4nx reader's host parts are checked against the golden container."""
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from llmnputest_b200 import _native, format as fmt
+from tests.conftest import bf16_from_bits
+
+
+def test_library_exports_every_header_symbol():
+    syms = _native.header_symbols()
+    assert len(syms) >= 10
+    lib = _native.lib()
+    missing = [s for s in syms if not hasattr(lib, s)]
+    assert not missing, missing
+    # and the ctypes table covers the header exactly
+    assert sorted(_native.SIGNATURES) == syms
+
+
+def test_version_and_status_strings():
+    lib = _native.lib()
+    assert lib.b2_version() == (0 << 16) | (1 << 8)
+    assert lib.b2_status_string(0) == b"ok"
+    assert lib.b2_status_string(-4) == b"no CUDA device"
+    assert lib.b2_status_string(12345) == b"unknown status"
+
+
+def test_calls_fail_cleanly_without_a_device():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present; covered by the gpu tests")
+    lib = _native.lib()
+    st = lib.b2_q4_gemv(None, 1, 1, None, 1, 256, None, 32, 0, None)
+    assert st == -4  # B2_ERR_NO_DEVICE: checked before any argument is touched
+    assert b"device" in lib.b2_last_error_message()
+
+
+def test_format_constants_match_oracle():
+    from oracle import q4nx_oracle as orc
+    assert (fmt.Q4_TILE_BYTES, fmt.Q8_TILE_BYTES) == (orc.Q4_TILE_BYTES, orc.Q8_TILE_BYTES) == (5120, 8704)
+    assert np.array_equal(fmt.meta_index(), orc.meta_of_weight())
+    t = np.arange(4096, dtype=np.uint8)
+    assert np.array_equal(fmt.unpack_nibbles(t), orc.q4_codes(t))
+    assert np.array_equal(fmt.to_matrix(np.arange(8192)), orc.tile_matrix(np.arange(8192)))
+
+
+def test_reader_header_and_raw(container_path, golden):
+    f = fmt.Q4NX(container_path)
+    assert f.names() == sorted(golden["ctr_names"].tolist())
+    assert "lm_head.weight" in f and "nope" not in f
+    assert np.array_equal(np.frombuffer(f.raw("model.layers.0.mlp.down_proj.weight"), np.uint8),
+                          golden["ctr_down_raw"])
+    norm = f.tensor("model.norm.weight")  # stored as-is, no decode needed
+    assert np.array_equal(norm.view(np.uint16), golden["ctr_norm"])
+    # tiled shapes: 3-D (Qwen) form is self-describing, 2-D (granite) needs N or K
+    assert f.tiled_shape("lm_head.weight") == (2, 4, 8704)
+    assert f.tiled_shape("model.layers.0.mlp.gate_proj.weight") == (3, 2, 5120)
+    assert f.tiled_shape("model.layers.0.mlp.down_proj.weight", n=64) == (2, 3, 5120)
+    assert f.tiled_shape("model.layers.0.mlp.down_proj.weight", k=768) == (2, 3, 5120)
+    with pytest.raises(ValueError):
+        f.tiled_shape("model.layers.0.mlp.down_proj.weight")
+    with pytest.raises(ValueError):
+        f.tiled_shape("model.layers.0.mlp.down_proj.weight", n=128, k=768)
+
+
+def test_split_q4_tile_roundtrip(golden):
+    t = golden["fmt_q4_tiles"][0]
+    nib, d, m = fmt.split_q4_tile(t.tobytes())
+    assert np.array_equal(nib, t[1024:])
+    assert np.array_equal(fmt.pack_meta(d, m).view(np.uint8), t[:1024])
