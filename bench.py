@@ -237,7 +237,7 @@ def run_b200(args, rank: int, world: int) -> dict | None:
 
     def sweep():
         for _, w, n_t, k_t, x, y in calls:
-            ops.q4_gemv(w, n_t, k_t, x, out=y)
+            ops.q4_gemv(w, n_t, k_t, x, out=y, prefetch=True)
 
     g = graph_of(torch, sweep)
     n_launch = len(calls)
@@ -271,7 +271,7 @@ def run_b200(args, rank: int, world: int) -> dict | None:
         per_shape = {}
         for name, n_t, k_t in SHAPES:
             sub = [c for c in calls if c[0] == name]
-            gs = graph_of(torch, lambda sub=sub: [ops.q4_gemv(w, n, k, x, out=y) for _, w, n, k, x, y in sub])
+            gs = graph_of(torch, lambda sub=sub: [ops.q4_gemv(w, n, k, x, out=y, prefetch=True) for _, w, n, k, x, y in sub])
             t_ms = time_graph(torch, gs, max(20, args.steps // 10), 3)
             per_shape[name] = round(sum(c[1].numel() for c in sub) / (t_ms * 1e-3) / 1e9, 1)
             del gs
@@ -279,7 +279,7 @@ def run_b200(args, rank: int, world: int) -> dict | None:
         # batch 8 (config 2's other batch size): same weights, 8-token activations
         calls8 = [(n, w, nt, kt, torch.randn(8, kt * 256, device=device, generator=gen).to(torch.bfloat16),
                    torch.empty(8, nt * 32, device=device)) for n, w, nt, kt, _, _ in calls]
-        g8 = graph_of(torch, lambda: [ops.q4_gemv(w, n, k, x, out=y) for _, w, n, k, x, y in calls8])
+        g8 = graph_of(torch, lambda: [ops.q4_gemv(w, n, k, x, out=y, prefetch=True) for _, w, n, k, x, y in calls8])
         t8 = time_graph(torch, g8, max(20, args.steps // 10), 3)
         extras["batch8_gbs"] = round(step_bytes / (t8 * 1e-3) / 1e9, 1)
         del g8, calls8
@@ -307,7 +307,7 @@ def run_b200(args, rank: int, world: int) -> dict | None:
 
     def sweep_e2e():
         for w, n_t, k_t, x, y in views:
-            ops.q4_gemv(w, n_t, k_t, x, out=y)
+            ops.q4_gemv(w, n_t, k_t, x, out=y, prefetch=True)
 
     ge = graph_of(torch, sweep_e2e)
     e2e_steps = max(10, args.steps // 10)

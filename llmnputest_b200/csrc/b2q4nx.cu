@@ -10,6 +10,7 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -40,6 +41,8 @@ struct DevInfo {
   int ok = 0;
   int sms = 0;
   int smem_optin = 0;
+  int smem_per_sm = 0;
+  int smem_reserved = 0;
   int major = 0, minor = 0;
 };
 
@@ -60,6 +63,8 @@ int device_info(DevInfo* out) {
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceProperties");
     di.sms = prop.multiProcessorCount;
     di.smem_optin = static_cast<int>(prop.sharedMemPerBlockOptin);
+    di.smem_per_sm = static_cast<int>(prop.sharedMemPerMultiprocessor);
+    di.smem_reserved = static_cast<int>(prop.reservedSharedMemPerBlock);
     di.major = prop.major;
     di.minor = prop.minor;
     di.ok = 1;
@@ -71,49 +76,87 @@ int device_info(DevInfo* out) {
 
 inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Launch-plan knobs, read once from the environment (for tuning experiments):
+//   B2Q4NX_MAX_CLUSTER   largest split-K cluster (1..16, default 16)
+//   B2Q4NX_CTAS_PER_SM   force 1 or 2 GEMV CTAs per SM (default: 2 when they fit)
+//   B2Q4NX_MAX_STAGES    cap on the shared-memory pipeline depth (1..8)
+struct Tuning {
+  int max_cluster = 16;
+  int ctas_per_sm = 0;
+  int max_stages = b2::kMaxStages;
+};
+const Tuning& tuning() {
+  static const Tuning t = [] {
+    Tuning v;
+    if (const char* e = getenv("B2Q4NX_MAX_CLUSTER")) v.max_cluster = std::max(1, std::min(16, atoi(e)));
+    if (const char* e = getenv("B2Q4NX_CTAS_PER_SM")) v.ctas_per_sm = std::max(0, std::min(2, atoi(e)));
+    if (const char* e = getenv("B2Q4NX_MAX_STAGES")) v.max_stages = std::max(1, std::min(b2::kMaxStages, atoi(e)));
+    return v;
+  }();
+  return t;
+}
+
 // ------------------------------------------------------------------ GEMV
 template <int QT, int NB, int EPI>
 int launch_gemv_t(b2::GemvParams p, const DevInfo& di, cudaStream_t stream) {
   using namespace b2;
   auto kernel = q4nx_gemv_kernel<QT, NB, EPI>;
   constexpr int SLOT = QTraits<QT>::kSlot;
+  constexpr int STAGE = 4 * SLOT;
   static int attr_set[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, di.smem_optin);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv smem)");
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv)");
     attr_set[dev] = 1;
   }
 
   const int G = p.n_groups;
-  // split-K: enough CTAs to cover the SMs when there are fewer groups than SMs
-  int S = 1;
-  if (G < di.sms) S = std::min(std::min(8, p.k_tiles), (di.sms + G - 1) / G);
-  // keep the staged x slice bounded (8*NB rows x kt*256 bf16)
-  const int kt_cap = 12 / NB;
-  S = std::max(S, std::min(8, (p.k_tiles + kt_cap - 1) / kt_cap));
-  S = std::min(S, p.k_tiles);
-  int ktps = (p.k_tiles + S - 1) / S;
-  S = (p.k_tiles + ktps - 1) / ktps;  // no empty split
+  const int batch = p.batch;
+  // largest K slice whose staged x (batch rows, fp16) stays within 48 KB
+  const int kt_cap = std::max(1, (48 * 1024) / (batch * 512 + 16));
+  // CTAs per SM: two when the register budget (NB == 1) and shared memory allow
+  auto fixed_bytes = [&](int ktps) {
+    const GemvSmem base(SLOT, NB, 0, ktps * 256 + 8, ktps, batch);
+    return base.total + 2 * kMaxStages * 8;
+  };
+  const int per_cta_2 = di.smem_per_sm / 2 - di.smem_reserved;
+
+  const Tuning& tu = tuning();
+  int cps = 1, S = 1, ktps = p.k_tiles;
+  for (int attempt = 0; attempt < 2; ++attempt) {
+    cps = (attempt == 0 && NB == 1 && tu.ctas_per_sm != 1) ? 2 : 1;
+    if (attempt == 1 && tu.ctas_per_sm == 2 && NB == 1) cps = 2;
+    const int cap = cps * di.sms;
+    S = 1;
+    if (G < cap) S = std::min(std::min(tu.max_cluster, p.k_tiles), std::max(1, cap / G));
+    S = std::max(S, (p.k_tiles + kt_cap - 1) / kt_cap);
+    S = std::min(S, p.k_tiles);
+    ktps = (p.k_tiles + S - 1) / S;
+    S = (p.k_tiles + ktps - 1) / ktps;
+    const int budget = cps == 2 ? per_cta_2 : di.smem_optin;
+    const int want = std::min(2, ktps);  // at least double-buffered, or the whole slice
+    if (fixed_bytes(ktps) + want * STAGE <= budget) break;
+  }
+  if (S > 16) return fail(B2_ERR_ARG, "K too large for one cluster (k_tiles=%d, batch=%d)", p.k_tiles, batch);
 
   const int x_stride = ktps * 256 + 8;
-  // fixed part of shared memory, then as many pipeline stages as fit
-  const GemvSmem base(SLOT, NB, 0, x_stride, ktps);
-  const int fixed = base.total + 2 * kMaxStages * 8;
   int grid_y;
   if (S == 1) {
-    grid_y = std::min(G, di.sms);  // persistent over groups
+    grid_y = std::min(G, cps * di.sms);  // persistent over groups
   } else {
     if (G > 65535) return fail(B2_ERR_ARG, "too many row groups (%d) for a split-K grid", G);
     grid_y = G;
   }
   const int groups_per_cta = (G + grid_y - 1) / grid_y;
   const int total_stages = ktps * groups_per_cta;
-  int stages = std::min(kMaxStages, (di.smem_optin - fixed) / (4 * SLOT));
+  const int budget = cps == 2 ? per_cta_2 : di.smem_optin;
+  int stages = std::min(tu.max_stages, (budget - fixed_bytes(ktps)) / STAGE);
   stages = std::min(stages, total_stages);
   if (stages < 1) return fail(B2_ERR_ARG, "K slice too large for shared memory");
-  const GemvSmem L(SLOT, NB, stages, x_stride, ktps);
+  const GemvSmem L(SLOT, NB, stages, x_stride, ktps, batch);
 
   p.kt_per_split = ktps;
   p.n_splits = S;

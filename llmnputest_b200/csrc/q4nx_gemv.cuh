@@ -10,35 +10,42 @@
 // (tools/q4nx.py:1-33, designs/granite_gemv/granite_gemv.h:31-45,
 //  designs/lm_head/lm_head.h:19-32.)
 //
-// The quantisation block factors out of the dot product exactly as in the
-// reference kernel (granite_gemv.h:19-29):
+// The quantisation block factors out of the dot product as in the reference
+// kernel (granite_gemv.h:19-29):
 //   y[r] = sum_kb  d[kb][r] * (sum_{k in kb} code*x)  +  m[kb][r] * (sum_{k in kb} x)
-// The inner sums run on the tensor core with *exact* bf16 codes:
-//   * a nibble n is turned into the bf16 value 128+n by one LOP3 against the
-//     exponent pattern 0x4300 (a bf16 in [128,256) has an ulp of 1) and 128 is
-//     subtracted exactly, so A holds the integer code itself;
-//   * q8 codes are split as c = 16*uh + ul - 128 (uh, ul the nibbles of c^0x80),
-//     two exact MMAs against x and 16*x, and the -128 folds into the sum-of-x term.
-// Products code*x are exact in fp32, so the only rounding is fp32 accumulation.
+// The inner sums run on the tensor core (mma.sync m16n8k16, fp16 operands, fp32
+// accumulate) with EXACT operands:
+//   * x is staged as fp16 x' = x * 2^e, e chosen per token and per K slice so
+//     that max|x'| lies in [2^14, 2^15): a bf16 value (8 significant bits)
+//     times a power of two is exact in fp16; e is undone exactly at the end.
+//   * a q4 byte holds rows 2j (low nibble) and 2j+1 (high nibble) at one k.  One
+//     LOP3 per nibble against an fp16 exponent pattern yields an exact value
+//     with no shift: low nibble n | 0x6400 = 1024 + n, high nibble (n<<4) |
+//     0x5400 = 64 + n; an exact f16x2 subtract leaves n.
+//   * a q8 byte c is split into the nibbles of u = c ^ 0x80 (= c + 128):
+//     (u & 0xF) | 0x6400 = 1024 + ul and (u & 0xF0) | 0x6400 = 1024 + 16*uh,
+//     both exact; two MMAs against x' sum to (2176 + c)*x', and the constant
+//     2176*s folds exactly into the sum-of-x term (m = -2176*s).
+// Every product is exact in fp32; the only rounding is fp32 accumulation.
 //
-// Data flow per CTA (one "row group" = 4 tile-rows = 128 outputs, or for the
-// fused SwiGLU 2 gate + 2 up tile-rows):
-//   producer warp: cp.async.bulk (TMA, no multicast) of the group's 4 tiles at
-//                  one K-tile into a stage of a shared-memory ring, mbarrier
-//                  complete_tx; L2 evict-first (weights are streamed once);
-//   8 consumer warps: warp w owns k-block w of every K-tile.  A thread (g,t)
-//                  of the warp owns row-block g of the stage (tile g%4, rb g/4)
-//                  and k-pairs {2t,2t+1}, {2t+8,2t+9} of each 16-k MMA step:
-//                  two 16-byte shared loads, PRMT+LOP3 into A fragments, 8 MMAs
-//                  (m16n8k16; the 16 "M" rows are rows 2s,2s+1 of 8 row-blocks)
-//                  with x as the B operand (N = batch), then the d/m scaling
-//                  into fp32 totals;
+// Data flow per CTA (a "row group" = 4 tile-rows = 128 outputs, or for the
+// fused SwiGLU 2 gate + 2 up tile-rows with matching rows):
+//   producer warp: cp.async.bulk (TMA engine, no multicast) of the group's 4
+//                  tiles at one K-tile into a stage of a shared-memory ring;
+//                  mbarrier complete_tx; L2 evict-first (weights stream once);
+//   8 consumer warps: warp w = (row-block rb = w&1, k-block pair kp = w>>1).
+//                  Lane (g,t) owns rows h*8..h*8+7 (h = g>>2) of row-block rb
+//                  of tile g&3, and k-pairs {2t,2t+1}, {2t+8,2t+9} of each
+//                  16-k MMA step: four 32-bit shared loads, PRMT pairs two k,
+//                  LOP3 decodes, 4 MMAs (the 16 "M" rows are rows 2s,2s+1 of
+//                  8 row-block halves), x' as the B operand (N = batch);
+//                  after each 32-k block the d/m scaling into fp32 totals;
 //   epilogue:      warp totals -> shared memory -> CTA sum (fixed order) ->
 //                  split-K sum across a thread-block cluster through
 //                  distributed shared memory (fixed order) -> store.
 // Split-K across CTAs uses a cluster (no global workspace, deterministic);
-// groups larger than the GPU use a persistent grid with the producer running
-// ahead across group boundaries.
+// when the groups outnumber the SMs the grid is persistent and the producer
+// runs ahead across group boundaries.
 #pragma once
 
 #include "b2_common.cuh"
@@ -53,18 +60,22 @@ struct QTraits;
 template <>
 struct QTraits<kQ4> {
   static constexpr int kTile = 5120;
-  static constexpr int kSlot = 5184;  // +64 B: row-blocks of adjacent tiles hit disjoint banks
+  // +32 B: the 4 tiles of a stage start 32 B apart modulo 128, which with the
+  // per-tile load order below makes every 32-bit nibble load conflict-free
+  static constexpr int kSlot = 5152;
 };
 template <>
 struct QTraits<kQ8> {
   static constexpr int kTile = 8704;
-  static constexpr int kSlot = 8720;  // +16 B, same reason for the 32-byte q8 reads
+  static constexpr int kSlot = 8720;
 };
 
-constexpr int kGemvConsumerWarps = 8;  // one per 32-k block of a K-tile
-constexpr int kGemvThreads = (kGemvConsumerWarps + 1) * 32;
+constexpr int kGemvConsumerWarps = 8;
+constexpr int kGemvConsumers = kGemvConsumerWarps * 32;
+constexpr int kGemvThreads = kGemvConsumers + 32;
 constexpr int kGroupRows = 128;
 constexpr int kMaxStages = 8;
+constexpr int kMaxBatch = 16;
 
 struct GemvParams {
   const uint8_t* w0;  // tile-rows [n_tile_rows][k_tiles][tile]
@@ -81,56 +92,113 @@ struct GemvParams {
   int n_splits;      // cluster size (split-K), 1 = no cluster
   int n_groups;
   int stages;
-  int x_stride;  // bf16 per shared-memory x row = kt_per_split*256 + 8
+  int x_stride;              // fp16 per shared-memory x row = kt_per_split*256 + 8
   int prefetch_before_wait;  // weights may stream before the PDL wait
 };
 
 // Shared-memory layout (bytes), computed identically on host and device.
 struct GemvSmem {
-  int ring, x, xs, red, csum, bar, flag, total;
-  __host__ __device__ static constexpr int red_warp_floats(int nb) { return kGroupRows * 8 * nb + 24; }
-  __host__ __device__ GemvSmem(int qt_slot, int nb, int stages, int x_stride, int kt_per_split) {
+  int ring, x, xs, red, csum, gather, misc, bar, flag, total;
+  int ncol;  // batch rounded up to even
+  __host__ __device__ GemvSmem(int slot, int nb, int stages, int x_stride, int kt_per_split, int batch) {
+    ncol = (batch + 1) & ~1;
     ring = 0;
-    x = stages * 4 * qt_slot;
-    xs = x + 8 * nb * x_stride * 2;
+    x = stages * 4 * slot;
+    xs = x + ((batch * x_stride * 2 + 15) & ~15);
     red = xs + kt_per_split * 8 * 8 * nb * 4;
-    csum = red + kGemvConsumerWarps * red_warp_floats(nb) * 4;
-    bar = csum + kGroupRows * 8 * nb * 4;
+    csum = red + kGemvConsumerWarps * 64 * ncol * 4;
+    gather = csum + kGroupRows * ncol * 4;  // split-K partials pushed by the cluster's ranks
+    misc = gather + 160 * ncol * 4;         // [kMaxBatch] max bits, [kMaxBatch] exponents
+    bar = misc + 2 * kMaxBatch * 4;
     bar = (bar + 15) & ~15;
     flag = bar + 2 * stages * 8;
     total = flag + 16;
   }
 };
 
-__device__ __forceinline__ int red_index(int row, int col, int nb) {
-  // row-major [128][8nb], each 32-row tile shifted by 8 floats so that the
-  // 4 tiles written by one quarter-warp land in different banks
-  return row * 8 * nb + col + 8 * (row >> 5);
+__device__ __forceinline__ float absmax8_bf16(uint4 v) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) m = fmaxf(m, fmaxf(fabsf(bf16lo_to_f32(w[i])), fabsf(bf16hi_to_f32(w[i]))));
+  return m;
+}
+
+// Scale exponent for a row whose max |x| has bit pattern `bits`: x*2^e has its
+// max in [2^14, 2^15).  Clamped so that 2^e and 2^-e are normal floats.
+__device__ __forceinline__ int gemv_scale_exp(uint32_t bits) {
+  const int ex = static_cast<int>((bits >> 23) & 255);
+  if (bits == 0 || ex == 255) return 0;
+  const int e = 14 - (ex - 127);
+  return max(-126, min(126, e));
+}
+__device__ __forceinline__ float pow2f(int e) { return __uint_as_float(static_cast<uint32_t>(e + 127) << 23); }
+
+// q4: decode the 8 rows of one k-pair from two 32-bit words (k_a and k_b bytes
+// of rows h*8..h*8+7, 2 rows per byte); out[r] = bf16x2-free f16x2 (row r @ k_a, row r @ k_b)
+__device__ __forceinline__ void decode_q4_pair(uint32_t w1, uint32_t w2, uint32_t sel_lo, uint32_t sel_hi,
+                                               uint32_t (&a)[8]) {
+  constexpr uint32_t kLoMagic = 0x64006400u;  // f16x2 (1024, 1024)
+  constexpr uint32_t kHiMagic = 0x54005400u;  // f16x2 (64, 64)
+  const uint32_t r0 = prmt(w1, w2, sel_lo);   // [k_a rows 0-3 | k_b rows 0-3]
+  const uint32_t r1 = prmt(w1, w2, sel_hi);   // rows 4-7
+  const uint32_t r0s = r0 >> 8, r1s = r1 >> 8;
+  a[0] = f16x2_sub(lop3<kLutAndOr>(r0, 0x000F000Fu, kLoMagic), kLoMagic);
+  a[1] = f16x2_sub(lop3<kLutAndOr>(r0, 0x00F000F0u, kHiMagic), kHiMagic);
+  a[2] = f16x2_sub(lop3<kLutAndOr>(r0s, 0x000F000Fu, kLoMagic), kLoMagic);
+  a[3] = f16x2_sub(lop3<kLutAndOr>(r0s, 0x00F000F0u, kHiMagic), kHiMagic);
+  a[4] = f16x2_sub(lop3<kLutAndOr>(r1, 0x000F000Fu, kLoMagic), kLoMagic);
+  a[5] = f16x2_sub(lop3<kLutAndOr>(r1, 0x00F000F0u, kHiMagic), kHiMagic);
+  a[6] = f16x2_sub(lop3<kLutAndOr>(r1s, 0x000F000Fu, kLoMagic), kLoMagic);
+  a[7] = f16x2_sub(lop3<kLutAndOr>(r1s, 0x00F000F0u, kHiMagic), kHiMagic);
+}
+
+// q8: two rows (bytes 0 and 1 of a PRMT result) -> (1024+ul) and (1024+16*uh) per row.
+__device__ __forceinline__ void decode_q8_res(uint32_t res, uint32_t& lo0, uint32_t& hi0, uint32_t& lo1,
+                                              uint32_t& hi1) {
+  constexpr uint32_t kMagic = 0x64006400u;
+  constexpr uint32_t kMagicFlip = 0x64806480u;  // 0x6400 | flip of the high nibble's top bit (c ^ 0x80)
+  const uint32_t rs = res >> 8;
+  lo0 = lop3<kLutAndOr>(res, 0x000F000Fu, kMagic);
+  hi0 = lop3<kLutAndXor>(res, 0x00F000F0u, kMagicFlip);
+  lo1 = lop3<kLutAndOr>(rs, 0x000F000Fu, kMagic);
+  hi1 = lop3<kLutAndXor>(rs, 0x00F000F0u, kMagicFlip);
 }
 
 template <int QT, int NB, int EPI>
-__global__ void __launch_bounds__(kGemvThreads, 1) q4nx_gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kernel(const GemvParams p) {
   constexpr int TILE = QTraits<QT>::kTile;
   constexpr int SLOT = QTraits<QT>::kSlot;
   constexpr int STAGE = 4 * SLOT;
   extern __shared__ __align__(128) uint8_t smem[];
 
-  const GemvSmem L(SLOT, NB, p.stages, p.x_stride, p.kt_per_split);
+  const GemvSmem L(SLOT, NB, p.stages, p.x_stride, p.kt_per_split, p.batch);
   uint8_t* ring = smem + L.ring;
-  __nv_bfloat16* x_s = reinterpret_cast<__nv_bfloat16*>(smem + L.x);
+  __half* x_s = reinterpret_cast<__half*>(smem + L.x);
   float* xs_s = reinterpret_cast<float*>(smem + L.xs);
   float* red = reinterpret_cast<float*>(smem + L.red);
   float* csum = reinterpret_cast<float*>(smem + L.csum);
+  uint32_t* maxbits = reinterpret_cast<uint32_t*>(smem + L.misc);
+  int* exps = reinterpret_cast<int*>(smem + L.misc) + kMaxBatch;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L.flag);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int stages = p.stages;
+  const int batch = p.batch;
+  const int ncol = L.ncol;
   const bool clustered = p.n_splits > 1;
   const int split = clustered ? static_cast<int>(cluster_ctarank()) : 0;
   const int kt0 = split * p.kt_per_split;
   const int kt_cnt = min(p.kt_per_split, p.k_tiles - kt0);  // >= 1 by construction
+  // cluster protocol (split-K).  f32: partials are added into y with global
+  // reductions; unless y is accumulated into, rank 0 first zeroes the group's
+  // rows and arrives on a cluster barrier that the others only wait on just
+  // before their adds (long complete by then).  SwiGLU: partials are pushed to
+  // the owning rank's shared memory and summed after one cluster barrier.
+  // Clustered launches always give each CTA exactly one group.
+  const int cl_mode = !clustered ? 0 : (EPI == kEpiSwiglu ? 2 : (p.accumulate ? 0 : 1));
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -140,11 +208,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) q4nx_gemv_kernel(const GemvPa
     *abort_flag = 0;
     fence_mbar_init();
   }
+  if (threadIdx.x < kMaxBatch) maxbits[threadIdx.x] = 0;
   __syncthreads();
   pdl_launch_dependents();
 
   if (warp == kGemvConsumerWarps) {
     // ------------------------------------------------------------ producer
+    if (cl_mode == 1) cluster_arrive_release();
     const uint64_t policy = l2_evict_first_policy();
     uint32_t seq = 0;
     bool waited_pdl = false;
@@ -193,13 +263,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1) q4nx_gemv_kernel(const GemvPa
         }
       }
       __syncwarp();
-      if (clustered) {  // mirror the consumers' two cluster barriers of this group
-        cluster_sync_all();
-        cluster_sync_all();
-      }
     }
     if (!waited_pdl) pdl_wait();
     __syncwarp();
+    if (cl_mode == 1) cluster_wait_acquire();  // mirror the consumers' barrier phases
+    if (cl_mode == 2) cluster_sync_all();
     if (lane == 0 && *abort_flag) {
       // abort path: let every copy this CTA issued land before the CTA exits
       const uint32_t first = seq > static_cast<uint32_t>(stages) ? seq - stages : 0;
@@ -219,45 +287,112 @@ __global__ void __launch_bounds__(kGemvThreads, 1) q4nx_gemv_kernel(const GemvPa
 
   // -------------------------------------------------------------- consumers
   pdl_wait();
-  const int ctid = threadIdx.x;  // 0..255
+  const int ctid = threadIdx.x;
+  if (cl_mode == 1) {
+    if (split == 0) {  // zero this group's outputs (after the PDL wait: y may be read upstream)
+      const int grp = blockIdx.y;
+      float* y = static_cast<float*>(p.y);
+      for (int e = ctid; e < kGroupRows * p.batch; e += kGemvConsumers) {
+        const int row = e % kGroupRows, b = e / kGroupRows;
+        if (grp * 4 + (row >> 5) < p.n_tile_rows) y[static_cast<size_t>(b) * p.ldy + grp * kGroupRows + row] = 0.f;
+      }
+    }
+    cluster_arrive_release();
+  }
   const int L_cta = kt_cnt * 256;
   {
-    // stage x[b][kt0*256 .. +L_cta) (zero rows for b >= batch), 16 bytes a thread at a time
+    // (1) per-token max |x| over this CTA's K slice (rows are whole multiples of
+    // 32 vectors, so every warp's 32 vectors belong to one token)
     const int vec_per_row = L_cta / 8;
-    for (int v = ctid; v < 8 * NB * vec_per_row; v += kGemvConsumerWarps * 32) {
+    const int total_vec = batch * vec_per_row;
+    constexpr int kVpt = 2;
+    const bool cached = total_vec <= kVpt * kGemvConsumers;
+    uint4 cache[kVpt];
+    auto xvec = [&](int v) {
       const int b = v / vec_per_row, c = v % vec_per_row;
-      uint4 val = make_uint4(0, 0, 0, 0);
-      if (b < p.batch)
-        val = *reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(b) * p.ldx + kt0 * 256 + c * 8);
-      *reinterpret_cast<uint4*>(x_s + b * p.x_stride + c * 8) = val;
-    }
-    named_barrier(1, kGemvConsumerWarps * 32);
-    // per-32-k-block sums of x (fp32), [kb_local][8*NB]
-    const int nsum = kt_cnt * 8 * 8 * NB;
-    for (int v = ctid; v < nsum; v += kGemvConsumerWarps * 32) {
-      const int kbl = v / (8 * NB), b = v % (8 * NB);
-      const __nv_bfloat16* xr = x_s + b * p.x_stride + kbl * 32;
-      float acc = 0.f;
+      return reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(b) * p.ldx + kt0 * 256)[c];
+    };
+    if (cached) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) acc += __bfloat162float(xr[j]);
+      for (int i = 0; i < kVpt; ++i) {
+        const int v = ctid + i * kGemvConsumers;
+        if (v < total_vec) {
+          cache[i] = xvec(v);
+          const float mx = warp_max(absmax8_bf16(cache[i]));
+          if (lane == 0) atomicMax(&maxbits[v / vec_per_row], __float_as_uint(mx));
+        }
+      }
+    } else {
+      for (int v0 = warp * 32; v0 < total_vec; v0 += kGemvConsumers) {
+        const float mx = warp_max(absmax8_bf16(xvec(v0 + lane)));
+        if (lane == 0) atomicMax(&maxbits[v0 / vec_per_row], __float_as_uint(mx));
+      }
+    }
+    named_barrier(1, kGemvConsumers);
+    if (ctid < batch) exps[ctid] = gemv_scale_exp(maxbits[ctid]);
+    // (2) x' = fp16(x * 2^e) into shared memory
+    auto put = [&](int v, uint4 in) {
+      const int b = v / vec_per_row, c = v % vec_per_row;
+      const float sc = pow2f(gemv_scale_exp(maxbits[b]));
+      const uint32_t w[4] = {in.x, in.y, in.z, in.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __half2 hv = __floats2half2_rn(bf16lo_to_f32(w[i]) * sc, bf16hi_to_f32(w[i]) * sc);
+        o[i] = *reinterpret_cast<const uint32_t*>(&hv);
+      }
+      *reinterpret_cast<uint4*>(x_s + b * p.x_stride + c * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+    };
+    if (cached) {
+#pragma unroll
+      for (int i = 0; i < kVpt; ++i) {
+        const int v = ctid + i * kGemvConsumers;
+        if (v < total_vec) put(v, cache[i]);
+      }
+    } else {
+      for (int v = ctid; v < total_vec; v += kGemvConsumers) put(v, xvec(v));
+    }
+    named_barrier(1, kGemvConsumers);
+    // (3) per-32-k-block sums of x' (fp32), [kb_local][8*NB], zero for b >= batch
+    const int nsum = kt_cnt * 8 * 8 * NB;
+    for (int v = ctid; v < nsum; v += kGemvConsumers) {
+      const int kbl = v / (8 * NB), b = v % (8 * NB);
+      float acc = 0.f;
+      if (b < batch) {
+        const uint4* xr = reinterpret_cast<const uint4*>(x_s + b * p.x_stride + kbl * 32);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint4 q = xr[j];
+          const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+            acc += f.x;
+            acc += f.y;
+          }
+        }
+      }
       xs_s[v] = acc;
     }
-    named_barrier(1, kGemvConsumerWarps * 32);
+    named_barrier(1, kGemvConsumers);
   }
 
   const int g = lane >> 2, t = lane & 3;
-  const int tslot = g & 3, rb = g >> 2;
-  const int kb = warp;
+  const int tile = g & 3, h = g >> 2, odd = tile & 1;
+  const int rb = warp & 1, kp = warp >> 1;
+  // load order: odd tiles read the k_b word first (bank spreading); the PRMT
+  // selector undoes the swap so r = [k_a bytes | k_b bytes] either way
+  const uint32_t sel_lo = odd ? 0x1054u : 0x5410u;
+  const uint32_t sel_hi = odd ? 0x3276u : 0x7632u;
+  const int off_first = odd ? 8 : 0, off_second = odd ? 0 : 8;
   const uint32_t* x32 = reinterpret_cast<const uint32_t*>(x_s);
   const int xw_stride = p.x_stride / 2;
-  const uint32_t kMagic = 0x43004300u;  // bf16x2 (128, 128)
-  const uint32_t kSixteen = 0x41804180u;  // bf16x2 (16, 16)
 
   uint32_t seq = 0;
   for (int grp = blockIdx.y; grp < p.n_groups; grp += gridDim.y) {
-    float tot[8][4 * NB];
+    float tot[4][4 * NB];
 #pragma unroll
-    for (int s = 0; s < 8; ++s)
+    for (int s = 0; s < 4; ++s)
 #pragma unroll
       for (int c = 0; c < 4 * NB; ++c) tot[s][c] = 0.f;
 
@@ -265,120 +400,96 @@ __global__ void __launch_bounds__(kGemvThreads, 1) q4nx_gemv_kernel(const GemvPa
       const int slot = seq % stages;
       const uint32_t ph = (seq / stages) & 1;
       mbar_wait_bounded(smem_u32(&bars[slot]), ph, abort_flag, kDevTimeoutFull);
-
-      const uint8_t* tile = ring + slot * STAGE + tslot * SLOT;
-      const int kl = kk * 256 + kb * 32;  // local k of this k-block
-      float part[8][4 * NB];
-#pragma unroll
-      for (int s = 0; s < 8; ++s)
-#pragma unroll
-        for (int c = 0; c < 4 * NB; ++c) part[s][c] = 0.f;
+      const uint8_t* tl = ring + slot * STAGE + tile * SLOT;
 
 #pragma unroll
-      for (int st = 0; st < 2; ++st) {
-        uint32_t bx[NB][2];
+      for (int j = 0; j < 2; ++j) {
+        const int kb = 2 * kp + j;
+        float part[4][4 * NB];
 #pragma unroll
-        for (int n = 0; n < NB; ++n) {
-          const uint32_t* xr = x32 + (g + 8 * n) * xw_stride + (kl + st * 16) / 2 + t;
-          bx[n][0] = xr[0];
-          bx[n][1] = xr[4];
-        }
-        if (QT == kQ4) {
-          const uint8_t* nb = tile + 1024 + rb * 2048 + kb * 256 + st * 128;
-          const uint4 P = *reinterpret_cast<const uint4*>(nb + 16 * t);
-          const uint4 Q = *reinterpret_cast<const uint4*>(nb + 64 + 16 * t);
-          uint32_t aP[16], aQ[16];
-          // P = [k_a rows 0-7 | k_a rows 8-15 | k_b rows 0-7 | k_b rows 8-15], 4 bytes each
-          const uint32_t pw[4] = {P.x, P.y, P.z, P.w};
-          const uint32_t qw[4] = {Q.x, Q.y, Q.z, Q.w};
+        for (int s = 0; s < 4; ++s)
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint32_t sel = (q & 1) ? 0x7632u : 0x5410u;
-            const uint32_t rp = prmt(pw[q >> 1], pw[2 + (q >> 1)], sel);
-            const uint32_t rq = prmt(qw[q >> 1], qw[2 + (q >> 1)], sel);
+          for (int c = 0; c < 4 * NB; ++c) part[s][c] = 0.f;
+
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              aP[4 * q + j] = bf16x2_sub(lop3<kLutAndOr>(rp >> (4 * j), 0x000F000Fu, kMagic), kMagic);
-              aQ[4 * q + j] = bf16x2_sub(lop3<kLutAndOr>(rq >> (4 * j), 0x000F000Fu, kMagic), kMagic);
-            }
-          }
-#pragma unroll
-          for (int s = 0; s < 8; ++s)
-#pragma unroll
-            for (int n = 0; n < NB; ++n)
-              mma_bf16_m16n8k16(part[s][4 * n], part[s][4 * n + 1], part[s][4 * n + 2], part[s][4 * n + 3],
-                                aP[2 * s], aP[2 * s + 1], aQ[2 * s], aQ[2 * s + 1], bx[n][0], bx[n][1]);
-        } else {
-          // q8: 16 bytes = 16 rows at one k; k_a, k_b (pair P) then k_c, k_d (pair Q)
-          const uint8_t* cb = tile + 512 + rb * 4096 + kb * 512 + st * 256;
-          const uint4 A = *reinterpret_cast<const uint4*>(cb + 32 * t);
-          const uint4 B = *reinterpret_cast<const uint4*>(cb + 32 * t + 16);
-          const uint4 C = *reinterpret_cast<const uint4*>(cb + 128 + 32 * t);
-          const uint4 D = *reinterpret_cast<const uint4*>(cb + 128 + 32 * t + 16);
-          const uint32_t aw[4] = {A.x, A.y, A.z, A.w}, bw[4] = {B.x, B.y, B.z, B.w};
-          const uint32_t cw[4] = {C.x, C.y, C.z, C.w}, dw[4] = {D.x, D.y, D.z, D.w};
-          uint32_t bx16[NB][2];
+        for (int st = 0; st < 2; ++st) {
+          const int kl = kk * 256 + kb * 32 + st * 16;
+          uint32_t bx[NB][2];
 #pragma unroll
           for (int n = 0; n < NB; ++n) {
-            bx16[n][0] = bf16x2_mul(bx[n][0], kSixteen);
-            bx16[n][1] = bf16x2_mul(bx[n][1], kSixteen);
+            const int row = g + 8 * n;
+            const uint32_t* xr = x32 + row * xw_stride + kl / 2 + t;
+            bx[n][0] = row < batch ? xr[0] : 0u;
+            bx[n][1] = row < batch ? xr[4] : 0u;
           }
+          if (QT == kQ4) {
+            const uint8_t* nb = tl + 1024 + rb * 2048 + kb * 256 + st * 128 + 16 * t + 4 * h;
+            const uint32_t p1 = *reinterpret_cast<const uint32_t*>(nb + off_first);
+            const uint32_t p2 = *reinterpret_cast<const uint32_t*>(nb + off_second);
+            const uint32_t q1 = *reinterpret_cast<const uint32_t*>(nb + 64 + off_first);
+            const uint32_t q2 = *reinterpret_cast<const uint32_t*>(nb + 64 + off_second);
+            uint32_t aP[8], aQ[8];
+            decode_q4_pair(p1, p2, sel_lo, sel_hi, aP);
+            decode_q4_pair(q1, q2, sel_lo, sel_hi, aQ);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {     // word q = rows 4q..4q+3
+            for (int s = 0; s < 4; ++s)
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {   // rows 4q+2h, 4q+2h+1
-              const uint32_t sel = h ? 0x7632u : 0x5410u;
-              const uint32_t rp = prmt(aw[q], bw[q], sel);
-              const uint32_t rq = prmt(cw[q], dw[q], sel);
-              // low nibbles (ul) and flipped high nibbles (uh = (c^0x80)>>4)
-              const uint32_t pl0 = bf16x2_sub(lop3<kLutAndOr>(rp, 0x000F000Fu, kMagic), kMagic);
-              const uint32_t pl1 = bf16x2_sub(lop3<kLutAndOr>(rp >> 8, 0x000F000Fu, kMagic), kMagic);
-              const uint32_t ph0 = bf16x2_sub(lop3<kLutAndXor>(rp >> 4, 0x000F000Fu, 0x43084308u), kMagic);
-              const uint32_t ph1 = bf16x2_sub(lop3<kLutAndXor>(rp >> 12, 0x000F000Fu, 0x43084308u), kMagic);
-              const uint32_t ql0 = bf16x2_sub(lop3<kLutAndOr>(rq, 0x000F000Fu, kMagic), kMagic);
-              const uint32_t ql1 = bf16x2_sub(lop3<kLutAndOr>(rq >> 8, 0x000F000Fu, kMagic), kMagic);
-              const uint32_t qh0 = bf16x2_sub(lop3<kLutAndXor>(rq >> 4, 0x000F000Fu, 0x43084308u), kMagic);
-              const uint32_t qh1 = bf16x2_sub(lop3<kLutAndXor>(rq >> 12, 0x000F000Fu, 0x43084308u), kMagic);
-              const int s = 2 * q + h;  // MMA index: rows 2s, 2s+1
+              for (int n = 0; n < NB; ++n)
+                mma_f16_m16n8k16(part[s][4 * n], part[s][4 * n + 1], part[s][4 * n + 2], part[s][4 * n + 3],
+                                 aP[2 * s], aP[2 * s + 1], aQ[2 * s], aQ[2 * s + 1], bx[n][0], bx[n][1]);
+          } else {
+            // 16 bytes = 16 rows at one k; this lane reads rows h*8..h*8+7 (8 bytes)
+            const uint8_t* cb = tl + 512 + rb * 4096 + kb * 512 + st * 256 + 8 * h + 32 * t;
+            const uint2 pa = *reinterpret_cast<const uint2*>(cb);        // k = 2t
+            const uint2 pb = *reinterpret_cast<const uint2*>(cb + 16);   // k = 2t+1
+            const uint2 qa = *reinterpret_cast<const uint2*>(cb + 128);  // k = 2t+8
+            const uint2 qb = *reinterpret_cast<const uint2*>(cb + 144);  // k = 2t+9
+            const uint32_t paw[2] = {pa.x, pa.y}, pbw[2] = {pb.x, pb.y};
+            const uint32_t qaw[2] = {qa.x, qa.y}, qbw[2] = {qb.x, qb.y};
 #pragma unroll
-              for (int n = 0; n < NB; ++n) {
-                mma_bf16_m16n8k16(part[s][4 * n], part[s][4 * n + 1], part[s][4 * n + 2],
-                                  part[s][4 * n + 3], pl0, pl1, ql0, ql1, bx[n][0], bx[n][1]);
-                mma_bf16_m16n8k16(part[s][4 * n], part[s][4 * n + 1], part[s][4 * n + 2],
-                                  part[s][4 * n + 3], ph0, ph1, qh0, qh1, bx16[n][0], bx16[n][1]);
+            for (int q = 0; q < 2; ++q) {    // rows 4q..4q+3 of the lane's 8
+#pragma unroll
+              for (int hh = 0; hh < 2; ++hh) {  // rows 4q+2hh, 4q+2hh+1 = MMA s
+                const uint32_t sel = hh ? 0x7632u : 0x5410u;
+                uint32_t pl0, ph0, pl1, ph1, ql0, qh0, ql1, qh1;
+                decode_q8_res(prmt(paw[q], pbw[q], sel), pl0, ph0, pl1, ph1);
+                decode_q8_res(prmt(qaw[q], qbw[q], sel), ql0, qh0, ql1, qh1);
+                const int s = 2 * q + hh;
+#pragma unroll
+                for (int n = 0; n < NB; ++n) {
+                  mma_f16_m16n8k16(part[s][4 * n], part[s][4 * n + 1], part[s][4 * n + 2], part[s][4 * n + 3],
+                                   pl0, pl1, ql0, ql1, bx[n][0], bx[n][1]);
+                  mma_f16_m16n8k16(part[s][4 * n], part[s][4 * n + 1], part[s][4 * n + 2], part[s][4 * n + 3],
+                                   ph0, ph1, qh0, qh1, bx[n][0], bx[n][1]);
+                }
               }
             }
           }
         }
-      }
 
-      // fold this k-block: tot += d*part + m*sum(x)   (q8: m = -128*s)
-      {
-        const uint8_t* meta = tile + (kb * 32 + rb * 16) * 2;
-        const uint4 d0 = *reinterpret_cast<const uint4*>(meta);
-        const uint4 d1 = *reinterpret_cast<const uint4*>(meta + 16);
-        const uint32_t dw[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
-        uint32_t mw[8];
+        // fold this k-block: tot += d*part + m*sum(x')   (q8: m = -2176*s)
+        const uint8_t* meta = tl + (kb * 32 + rb * 16 + h * 8) * 2;
+        const uint4 dv = *reinterpret_cast<const uint4*>(meta);
+        const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
+        uint32_t mw[4] = {0, 0, 0, 0};
         if (QT == kQ4) {
-          const uint4 m0 = *reinterpret_cast<const uint4*>(meta + 512);
-          const uint4 m1 = *reinterpret_cast<const uint4*>(meta + 528);
-          mw[0] = m0.x; mw[1] = m0.y; mw[2] = m0.z; mw[3] = m0.w;
-          mw[4] = m1.x; mw[5] = m1.y; mw[6] = m1.z; mw[7] = m1.w;
+          const uint4 mv = *reinterpret_cast<const uint4*>(meta + 512);
+          mw[0] = mv.x; mw[1] = mv.y; mw[2] = mv.z; mw[3] = mv.w;
         }
         float2 xsv[NB];
 #pragma unroll
         for (int n = 0; n < NB; ++n)
           xsv[n] = *reinterpret_cast<const float2*>(xs_s + (kk * 8 + kb) * 8 * NB + 8 * n + 2 * t);
 #pragma unroll
-        for (int s = 0; s < 8; ++s) {
+        for (int s = 0; s < 4; ++s) {
           const float da = bf16lo_to_f32(dw[s]), db = bf16hi_to_f32(dw[s]);
           float ma, mb;
           if (QT == kQ4) {
             ma = bf16lo_to_f32(mw[s]);
             mb = bf16hi_to_f32(mw[s]);
           } else {
-            ma = -128.f * da;
-            mb = -128.f * db;
+            ma = -2176.f * da;
+            mb = -2176.f * db;
           }
 #pragma unroll
           for (int n = 0; n < NB; ++n) {
@@ -395,74 +506,96 @@ __global__ void __launch_bounds__(kGemvThreads, 1) q4nx_gemv_kernel(const GemvPa
 
     // ------------------------------------------------------------ epilogue
     {
-      float* rw = red + warp * GemvSmem::red_warp_floats(NB);
+      // undo the x scale (exact power of two) and park the warp's totals:
+      // red[warp][64 local rows = tile*16 + h*8 + r][ncol]
+      float* rw = red + warp * 64 * ncol;
 #pragma unroll
-      for (int s = 0; s < 8; ++s) {
-        const int r0 = tslot * 32 + rb * 16 + 2 * s;
+      for (int n = 0; n < NB; ++n) {
+        const int c0 = 8 * n + 2 * t;
+        if (c0 < batch) {
+          const float u0 = pow2f(-exps[c0]);
+          const float u1 = (c0 + 1 < batch) ? pow2f(-exps[c0 + 1]) : 0.f;
 #pragma unroll
-        for (int n = 0; n < NB; ++n) {
-          *reinterpret_cast<float2*>(rw + red_index(r0, 8 * n + 2 * t, NB)) =
-              make_float2(tot[s][4 * n + 0], tot[s][4 * n + 1]);
-          *reinterpret_cast<float2*>(rw + red_index(r0 + 1, 8 * n + 2 * t, NB)) =
-              make_float2(tot[s][4 * n + 2], tot[s][4 * n + 3]);
+          for (int s = 0; s < 4; ++s) {
+            const int lr = tile * 16 + h * 8 + 2 * s;
+            *reinterpret_cast<float2*>(rw + lr * ncol + c0) = make_float2(tot[s][4 * n] * u0, tot[s][4 * n + 1] * u1);
+            *reinterpret_cast<float2*>(rw + (lr + 1) * ncol + c0) =
+                make_float2(tot[s][4 * n + 2] * u0, tot[s][4 * n + 3] * u1);
+          }
         }
       }
     }
-    named_barrier(1, kGemvConsumerWarps * 32);
-    for (int e = ctid; e < kGroupRows * 8 * NB; e += kGemvConsumerWarps * 32) {
-      const int row = e / (8 * NB), col = e % (8 * NB);
-      float v = 0.f;
-#pragma unroll
-      for (int w = 0; w < kGemvConsumerWarps; ++w) v += red[w * GemvSmem::red_warp_floats(NB) + red_index(row, col, NB)];
-      csum[e] = v;
-    }
-    if (clustered)
-      cluster_sync_all();
-    else
-      named_barrier(1, kGemvConsumerWarps * 32);
-
-    // split-K sum over the cluster (fixed rank order), then the epilogue
+    named_barrier(1, kGemvConsumers);
+    // CTA sum over the 4 warps that hold each row (fixed order).
     const int nsp = p.n_splits;
     const bool do_store = !*abort_flag;
-    const uint32_t csum_addr = smem_u32(csum);
     if (EPI == kEpiF32) {
-      const int rows_per = (kGroupRows + nsp - 1) / nsp;
-      const int r_lo = split * rows_per, r_hi = min(kGroupRows, r_lo + rows_per);
-      const int nrow = r_hi - r_lo;
       float* y = static_cast<float*>(p.y);
-      for (int e = ctid; e < nrow * p.batch; e += kGemvConsumerWarps * 32) {
-        const int row = r_lo + e % nrow, b = e / nrow;
-        const int idx = row * 8 * NB + b;
-        float v = 0.f;
-        if (clustered) {
-          for (int q = 0; q < nsp; ++q) v += ld_dsmem_f32(csum_addr + idx * 4, q);
-        } else {
-          v = csum[idx];
+      if (!clustered) {
+        for (int e = ctid; e < kGroupRows * batch; e += kGemvConsumers) {
+          const int row = e % kGroupRows, b = e / kGroupRows;
+          const int rbr = (row >> 4) & 1, lr = (row >> 5) * 16 + (row & 15);
+          float v = 0.f;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) v += red[(2 * q + rbr) * 64 * ncol + lr * ncol + b];
+          const int tr = grp * 4 + (row >> 5);
+          if (do_store && tr < p.n_tile_rows) {
+            float* dst = y + static_cast<size_t>(b) * p.ldy + grp * kGroupRows + row;
+            *dst = p.accumulate ? *dst + v : v;
+          }
         }
-        const int tr = grp * 4 + (row >> 5);
-        if (do_store && tr < p.n_tile_rows) {
-          float* dst = y + static_cast<size_t>(b) * p.ldy + grp * kGroupRows + row;
-          *dst = p.accumulate ? *dst + v : v;
+        named_barrier(1, kGemvConsumers);  // red is rewritten by the next group
+      } else {
+        if (cl_mode == 1) cluster_wait_acquire();  // rank 0 has zeroed y
+        for (int e = ctid; e < kGroupRows * batch; e += kGemvConsumers) {
+          const int row = e % kGroupRows, b = e / kGroupRows;
+          const int rbr = (row >> 4) & 1, lr = (row >> 5) * 16 + (row & 15);
+          float v = 0.f;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) v += red[(2 * q + rbr) * 64 * ncol + lr * ncol + b];
+          const int tr = grp * 4 + (row >> 5);
+          if (do_store && tr < p.n_tile_rows)
+            atomicAdd(y + static_cast<size_t>(b) * p.ldy + grp * kGroupRows + row, v);
         }
       }
     } else {
-      // SwiGLU: sum rows 0..63 are gate rows grp*64.., rows 64..127 the matching up rows
+      // SwiGLU: sum rows 0..63 are gate rows grp*64.., rows 64..127 the matching up rows.
+      // Clustered: push to the owning rank (gather[src rank][owned row][g|u]).
       const int rows_per = (64 + nsp - 1) / nsp;
+      float* gather = reinterpret_cast<float*>(smem + L.gather);
+      const uint32_t gather_addr = smem_u32(gather);
+      for (int e = ctid; e < kGroupRows * ncol; e += kGemvConsumers) {
+        const int row = e / ncol, col = e % ncol;
+        const int rbr = (row >> 4) & 1, lr = (row >> 5) * 16 + (row & 15);
+        float v = 0.f;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) v += red[(2 * q + rbr) * 64 * ncol + lr * ncol + col];
+        if (!clustered) {
+          csum[e] = v;
+        } else {
+          const int orow = row & 63;
+          const int o = orow / rows_per, ol = orow - o * rows_per;
+          st_dsmem_f32(gather_addr + (((split * rows_per + ol) * 2 + (row >> 6)) * ncol + col) * 4, o, v);
+        }
+      }
+      if (clustered)
+        cluster_sync_all();
+      else
+        named_barrier(1, kGemvConsumers);
       const int r_lo = split * rows_per, r_hi = min(64, r_lo + rows_per);
       const int nrow = r_hi - r_lo;
-      __nv_bfloat16* h = static_cast<__nv_bfloat16*>(p.y);
-      for (int e = ctid; e < nrow * p.batch; e += kGemvConsumerWarps * 32) {
-        const int row = r_lo + e % nrow, b = e / nrow;
-        const int ig = row * 8 * NB + b, iu = (row + 64) * 8 * NB + b;
+      __nv_bfloat16* hout = static_cast<__nv_bfloat16*>(p.y);
+      for (int e = ctid; e < nrow * batch; e += kGemvConsumers) {
+        const int ol = e % nrow, b = e / nrow, row = r_lo + ol;
         float gv = 0.f, uv = 0.f;
         if (clustered) {
           for (int q = 0; q < nsp; ++q) {
-            gv += ld_dsmem_f32(csum_addr + ig * 4, q);
-            uv += ld_dsmem_f32(csum_addr + iu * 4, q);
+            gv += gather[((q * rows_per + ol) * 2 + 0) * ncol + b];
+            uv += gather[((q * rows_per + ol) * 2 + 1) * ncol + b];
           }
         } else {
-          gv = csum[ig];
-          uv = csum[iu];
+          gv = csum[row * ncol + b];
+          uv = csum[(row + 64) * ncol + b];
         }
         // the reference narrows both accumulators to bf16 before SiLU (granite_mlp.py:172-181)
         const float gb = __bfloat162float(__float2bfloat16_rn(gv));
@@ -470,10 +603,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) q4nx_gemv_kernel(const GemvPa
         const float hv = gb / (1.f + expf(-gb)) * ub;
         const int tr = grp * 2 + (row >> 5);
         if (do_store && tr < p.n_tile_rows)
-          h[static_cast<size_t>(b) * p.ldy + grp * 64 + row] = __float2bfloat16_rn(hv);
+          hout[static_cast<size_t>(b) * p.ldy + grp * 64 + row] = __float2bfloat16_rn(hv);
       }
+      if (!clustered) named_barrier(1, kGemvConsumers);  // csum is rewritten by the next group
     }
-    if (clustered) cluster_sync_all();
   }
 }
 
