@@ -107,6 +107,41 @@ int b2_q4_dequant_matrix(const uint8_t* tiles, int n_tile_rows, int k_tiles, flo
 int b2_q8_dequant_matrix(const uint8_t* tiles, int n_tile_rows, int k_tiles, float* out, int64_t ld,
                          void* stream);
 
+/* GQA decode attention over a bf16 KV cache, RoPE fused on the new token's q/k.
+ *   q, k_new, v_new  fp32 rows of the new token, row stride ld_new floats per
+ *                    sequence (q head j at q + b*ld_new + j*D, kv head h at
+ *                    k_new/v_new + b*ld_new + h*D) -- e.g. slices of the QKV
+ *                    GEMV output [B][(Hq + 2*Hkv)*D]
+ *   k_cache, v_cache bf16 [B][Hkv][ctx_max][D]; the new token's rotated k and
+ *                    its v are written at position pos[b] (unless
+ *                    B2_ATTN_NO_APPEND), and positions 0..pos[b] are attended
+ *   pos              int32 [B] device array; max_len >= max(pos) + 1 sizes the
+ *                    context split (<= ctx_max)
+ *   theta, scale     RoPE base (half-split convention) and the score scale
+ *                    (head_dim^-0.5 for the reference model)
+ *   out              bf16 [B][ldo] (fp32 with B2_ATTN_OUT_F32), q head j at
+ *                    out + b*ldo + j*D
+ *   workspace        b2_gqa_decode_workspace_size() bytes (may be 0 bytes)
+ * head_dim 64, Hq/Hkv <= 8.  fp32 softmax and accumulation.
+ * Replaces granite_attn_block/_finish (designs/granite_gemv/granite_attention.h:80-213,
+ * design granite_attention.py:50-121) and the RoPE epilogues granite_rope /
+ * granite_qkv_rope (granite_elementwise.h:48-75, granite_qkv_rope.h:49-71). */
+#define B2_ATTN_NO_APPEND 1 /* the cache already holds position pos[b]; write nothing */
+#define B2_ATTN_NO_ROPE 2   /* use the new q/k as given (no rotation) */
+#define B2_ATTN_OUT_F32 4   /* fp32 output */
+int b2_gqa_decode_workspace_size(int batch, int n_q_heads, int n_kv_heads, int head_dim, int max_len,
+                                 size_t* bytes);
+int b2_gqa_decode(const float* q, const float* k_new, const float* v_new, int ld_new, uint16_t* k_cache,
+                  uint16_t* v_cache, const int32_t* pos, int batch, int n_q_heads, int n_kv_heads, int head_dim,
+                  int ctx_max, int max_len, float theta, float scale, uint16_t* out, int ldo, void* workspace,
+                  size_t workspace_bytes, int flags, void* stream);
+
+/* RMSNorm y = x * rsqrt(mean(x^2) + eps) * w over rows of n, bf16 out.
+ *   x  bf16 (x_is_f32 = 0) or fp32 (x_is_f32 = 1), [batch][ldx];  w bf16 [n]
+ * Replaces granite_rms_norm (designs/granite_gemv/granite_rmsnorm.h:45-80). */
+int b2_rmsnorm(const void* x, int x_is_f32, int ldx, const uint16_t* w, float eps, int batch, int n, uint16_t* y,
+               int ldy, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -17,7 +17,9 @@
 #include "../../include/b2q4nx.h"
 #include "b2_common.cuh"
 #include "q4nx_dequant.cuh"
+#include "gqa_decode.cuh"
 #include "q4nx_gemv.cuh"
+#include "rmsnorm.cuh"
 
 namespace {
 
@@ -268,6 +270,36 @@ int dequant_matrix(int qt, const uint8_t* tiles, int n_t, int k_t, float* out, i
   return B2_OK;
 }
 
+// ------------------------------------------------------------- attention
+struct AttnPlan {
+  int n_splits;
+  int split_len;
+  size_t ws_bytes;
+};
+
+AttnPlan attn_plan(int batch, int hq, int hkv, int head_dim, int max_len, int sms) {
+  AttnPlan pl;
+  const int pairs = batch * hkv;
+  const int target = 4 * sms;
+  const int max_splits = (max_len + 63) / 64;
+  int S = std::max(1, std::min(max_splits, (target + pairs - 1) / pairs));
+  int sl = (max_len + S - 1) / S;
+  sl = (sl + 63) / 64 * 64;
+  S = (max_len + sl - 1) / sl;
+  pl.n_splits = S;
+  pl.split_len = sl;
+  pl.ws_bytes = S > 1 ? static_cast<size_t>(batch) * hkv * S * (hq / hkv) * (head_dim + 2) * sizeof(float) : 0;
+  return pl;
+}
+
+int attn_check(int batch, int hq, int hkv, int head_dim, int ctx_max, int max_len) {
+  if (batch < 1 || hq < 1 || hkv < 1 || hq % hkv) return fail(B2_ERR_ARG, "bad head counts hq=%d hkv=%d", hq, hkv);
+  if (hq / hkv > 8) return fail(B2_ERR_ARG, "GQA group %d > 8 is not supported", hq / hkv);
+  if (head_dim != 64) return fail(B2_ERR_ARG, "head_dim %d: only 64 is built", head_dim);
+  if (max_len < 1 || max_len > ctx_max) return fail(B2_ERR_ARG, "max_len %d outside 1..ctx_max %d", max_len, ctx_max);
+  return B2_OK;
+}
+
 }  // namespace
 
 // ------------------------------------------------------------------ C ABI
@@ -327,6 +359,107 @@ int b2_q4_swiglu_gemv(const uint8_t* gate, const uint8_t* up, int n_tile_rows, i
                       int batch, int ldx, uint16_t* h, int ldh, int flags, void* stream) {
   return gemv_common(b2::kQ4, b2::kEpiSwiglu, gate, up, n_tile_rows, k_tiles, x, batch, ldx, h, ldh, flags,
                      stream);
+}
+
+int b2_gqa_decode_workspace_size(int batch, int n_q_heads, int n_kv_heads, int head_dim, int max_len,
+                                 size_t* bytes) {
+  DevInfo di;
+  int st = device_info(&di);
+  if (st != B2_OK) return st;
+  if (!bytes) return fail(B2_ERR_ARG, "null bytes pointer");
+  st = attn_check(batch, n_q_heads, n_kv_heads, head_dim, max_len, max_len);
+  if (st != B2_OK) return st;
+  *bytes = attn_plan(batch, n_q_heads, n_kv_heads, head_dim, max_len, di.sms).ws_bytes;
+  return B2_OK;
+}
+
+int b2_gqa_decode(const float* q, const float* k_new, const float* v_new, int ld_new, uint16_t* k_cache,
+                  uint16_t* v_cache, const int32_t* pos, int batch, int n_q_heads, int n_kv_heads, int head_dim,
+                  int ctx_max, int max_len, float theta, float scale, uint16_t* out, int ldo, void* workspace,
+                  size_t workspace_bytes, int flags, void* stream) {
+  DevInfo di;
+  int st = device_info(&di);
+  if (st != B2_OK) return st;
+  st = attn_check(batch, n_q_heads, n_kv_heads, head_dim, ctx_max, max_len);
+  if (st != B2_OK) return st;
+  if (!q || !k_new || !v_new || !k_cache || !v_cache || !pos || !out) return fail(B2_ERR_ARG, "null pointer argument");
+  if (ld_new < n_q_heads * head_dim) return fail(B2_ERR_ARG, "ld_new %d < Hq*D", ld_new);
+  if (ldo < n_q_heads * head_dim) return fail(B2_ERR_ARG, "ldo %d < Hq*D", ldo);
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16)) return fail(B2_ERR_ALIGN, "KV caches must be 16-byte aligned");
+  if ((flags & ~(B2_ATTN_NO_APPEND | B2_ATTN_NO_ROPE | B2_ATTN_OUT_F32)) != 0)
+    return fail(B2_ERR_ARG, "unknown flags 0x%x", flags);
+  const AttnPlan pl = attn_plan(batch, n_q_heads, n_kv_heads, head_dim, max_len, di.sms);
+  if (pl.n_splits > 1 && (!workspace || workspace_bytes < pl.ws_bytes))
+    return fail(B2_ERR_WORKSPACE, "workspace of %zu bytes needed (b2_gqa_decode_workspace_size)", pl.ws_bytes);
+  if (pl.n_splits > 65535) return fail(B2_ERR_ARG, "too many context splits");
+
+  b2::AttnParams p = {};
+  p.q = q;
+  p.k_new = k_new;
+  p.v_new = v_new;
+  p.ld_new = ld_new;
+  p.k_cache = reinterpret_cast<__nv_bfloat16*>(k_cache);
+  p.v_cache = reinterpret_cast<__nv_bfloat16*>(v_cache);
+  p.pos = pos;
+  p.batch = batch;
+  p.hq = n_q_heads;
+  p.hkv = n_kv_heads;
+  p.ctx_max = ctx_max;
+  p.theta = theta;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.ldo = ldo;
+  p.part = static_cast<float*>(workspace);
+  p.n_splits = pl.n_splits;
+  p.split_len = pl.split_len;
+  p.append = (flags & B2_ATTN_NO_APPEND) ? 0 : 1;
+  p.rope = (flags & B2_ATTN_NO_ROPE) ? 0 : 1;
+  p.out_f32 = (flags & B2_ATTN_OUT_F32) ? 1 : 0;
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.n_splits, n_kv_heads, batch);
+  cfg.blockDim = dim3(b2::kAttnThreads, 1, 1);
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, b2::gqa_decode_kernel<64>, p);
+  if (e != cudaSuccess) return cuda_fail(e, "attention launch");
+  if (pl.n_splits > 1) {
+    cfg.gridDim = dim3(n_q_heads, batch, 1);
+    cfg.blockDim = dim3(64, 1, 1);
+    e = cudaLaunchKernelEx(&cfg, b2::gqa_combine_kernel<64>, p);
+    if (e != cudaSuccess) return cuda_fail(e, "attention combine launch");
+  }
+  return B2_OK;
+}
+
+int b2_rmsnorm(const void* x, int x_is_f32, int ldx, const uint16_t* w, float eps, int batch, int n, uint16_t* y,
+               int ldy, void* stream) {
+  DevInfo di;
+  int st = device_info(&di);
+  if (st != B2_OK) return st;
+  if (!x || !w || !y) return fail(B2_ERR_ARG, "null pointer argument");
+  if (batch < 1 || n < 1 || ldx < n || ldy < n) return fail(B2_ERR_ARG, "bad rmsnorm shape");
+  if (!(eps >= 0.f)) return fail(B2_ERR_ARG, "eps must be >= 0");
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(batch, 1, 1);
+  cfg.blockDim = dim3(b2::kNormThreads, 1, 1);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cfg.attrs = attr;
+  cfg.numAttrs = g_pdl ? 1 : 0;
+  const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(w);
+  __nv_bfloat16* yb = reinterpret_cast<__nv_bfloat16*>(y);
+  cudaError_t e = x_is_f32 ? cudaLaunchKernelEx(&cfg, b2::rmsnorm_kernel<true>, x, ldx, wb, eps, n, yb, ldy)
+                           : cudaLaunchKernelEx(&cfg, b2::rmsnorm_kernel<false>, x, ldx, wb, eps, n, yb, ldy);
+  if (e != cudaSuccess) return cuda_fail(e, "rmsnorm launch");
+  return B2_OK;
 }
 
 int b2_q4_dequant_tiles(const uint8_t* tiles, int64_t n_tiles, uint16_t* out, void* stream) {

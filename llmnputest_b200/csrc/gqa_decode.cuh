@@ -1,0 +1,304 @@
+// GQA decode attention (flash-decode) for sm_100a, with RoPE fused on the
+// query/key load and the new token's K/V appended to the cache.
+//
+// Reference: designs/granite_gemv/granite_attention.h:80-213 (one q head
+// against a streamed KV cache, online softmax in log2 units, final divide),
+// oracle granite_attention.py:163-167; RoPE half-split granite_elementwise.h:40-75
+// with the table of granite_elementwise.py:136-138; q/k rotated, v not
+// (granite_qkv.py:176-207).
+//
+//   for each sequence b, kv head h, q head j of h's group (Hq/Hkv heads):
+//     q  = bf16(rope(q_new[b][j], pos_b)),  k_pos = bf16(rope(k_new[b][h], pos_b)),
+//     v_pos = bf16(v_new[b][h]);  cache[b][h][pos_b] = (k_pos, v_pos)
+//     s[t] = scale * q . K[t],  t = 0..pos_b  (causal: the new token sees itself)
+//     out  = sum_t softmax(s)[t] * V[t]                       (fp32 softmax)
+//
+// Layout: K, V caches bf16 [B][Hkv][ctx_max][D]; q/k/v of the new token fp32
+// rows (the QKV GEMV output), row stride ld_new; out bf16 [B][Hq*D].
+//
+// Work split: CTA (split, kv head, sequence), 4 warps, each warp a contiguous
+// run of positions in 16-position chunks.  The group's q heads are the 16 "M"
+// rows of mma.sync m16n8k16 (bf16 in, fp32 out), so every K/V byte is loaded
+// once for the whole group.  Per chunk: S = Q K^T (2 n-tiles x 4 k-steps), the
+// online softmax on the accumulator fragments (scores pre-scaled by log2 e,
+// exp2), P reused from the accumulator layout as the A operand of O += P V
+// (8 n-tiles of d), P split as bf16 hi + lo so the product keeps ~2^-17 of P.
+// K/V come straight from global memory with 16-byte loads (row-contiguous,
+// coalesced; the next chunk's loads are issued before the current chunk's
+// math).  Warps merge in shared memory; splits merge in a second kernel from a
+// caller-provided workspace (log-sum-exp).
+#pragma once
+
+#include "b2_common.cuh"
+
+namespace b2 {
+
+constexpr int kAttnWarps = 4;
+constexpr int kAttnThreads = kAttnWarps * 32;
+constexpr int kAttnChunk = 16;  // positions per inner step
+
+struct AttnParams {
+  const float* q;      // [B][ld_new] rows, q head j at q + b*ld_new + j*D
+  const float* k_new;  // kv head h at k_new + b*ld_new + h*D
+  const float* v_new;
+  int ld_new;
+  __nv_bfloat16* k_cache;  // [B][Hkv][ctx_max][D]
+  __nv_bfloat16* v_cache;
+  const int* pos;  // [B] position of the new token; attention length = pos + 1
+  int batch, hq, hkv, ctx_max;
+  float theta;
+  float scale_log2;  // scale * log2(e)
+  __nv_bfloat16* out;  // [B][ldo], q head j at out + b*ldo + j*D
+  int ldo;
+  float* part;   // [B][Hkv][n_splits][grp][D + 2] partials (o, m, l) when n_splits > 1
+  int n_splits;  // CTAs per (sequence, kv head)
+  int split_len;  // positions per split (multiple of 16)
+  int append;     // write the new token's k/v into the cache
+  int rope;       // rotate the new q/k (0: use them as given)
+  int out_f32;    // out is fp32 instead of bf16
+};
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// Half-split RoPE of one head (D fp32 values at src) into bf16 dst, fp64 angles;
+// this thread handles the pair (i, i + D/2).  rope == 0 rounds without rotating.
+template <int D>
+__device__ __forceinline__ void rope_head_bf16(const float* src, __nv_bfloat16* dst, int pos, float theta, int i,
+                                               int rope) {
+  if (!rope) {
+    dst[i] = __float2bfloat16_rn(src[i]);
+    dst[i + D / 2] = __float2bfloat16_rn(src[i + D / 2]);
+    return;
+  }
+  const double inv = pow(static_cast<double>(theta), -2.0 * i / D);
+  double sn, cs;
+  sincos(static_cast<double>(pos) * inv, &sn, &cs);
+  const float c = static_cast<float>(cs), s = static_cast<float>(sn);
+  const float x0 = src[i], x1 = src[i + D / 2];
+  dst[i] = __float2bfloat16_rn(x0 * c - x1 * s);
+  dst[i + D / 2] = __float2bfloat16_rn(x1 * c + x0 * s);
+}
+
+template <int D>
+__global__ void __launch_bounds__(kAttnThreads) gqa_decode_kernel(const AttnParams p) {
+  static_assert(D == 64, "this kernel is written for head_dim 64");
+  constexpr int QW = D / 2 + 4;  // q_s row stride in 32-bit words (bank spread)
+  __shared__ __align__(16) uint32_t q_s[16 * QW];        // bf16x2, 16 head rows (rows >= grp zero)
+  __shared__ float wm[kAttnWarps][16], wl[kAttnWarps][16];
+  __shared__ float wo[kAttnWarps][16][D + 1];
+
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int grp = p.hq / p.hkv;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+
+  pdl_wait();  // q/k/v come from the previous kernel
+  pdl_launch_dependents();
+  const int pos = p.pos[b];
+  const int len = pos + 1;
+  const int lo = split * p.split_len;
+  const int hi = min(len, lo + p.split_len);
+
+  // ---- q heads of the group: rope -> bf16 -> shared (rows >= grp are zero)
+  {
+    __nv_bfloat16* qh = reinterpret_cast<__nv_bfloat16*>(q_s);
+    for (int e = threadIdx.x; e < 16 * QW * 2; e += kAttnThreads) qh[e] = __float2bfloat16_rn(0.f);
+    __syncthreads();
+    for (int e = threadIdx.x; e < grp * (D / 2); e += kAttnThreads) {
+      const int j = e / (D / 2), i = e % (D / 2);
+      const float* src = p.q + static_cast<size_t>(b) * p.ld_new + (kvh * grp + j) * D;
+      rope_head_bf16<D>(src, qh + j * QW * 2, pos, p.theta, i, p.rope);
+    }
+    // the split that holds the new position appends its k (rotated) and v
+    if (p.append && pos >= lo && pos < hi) {
+      const size_t row = ((static_cast<size_t>(b) * p.hkv + kvh) * p.ctx_max + pos) * D;
+      const float* ks = p.k_new + static_cast<size_t>(b) * p.ld_new + kvh * D;
+      const float* vs = p.v_new + static_cast<size_t>(b) * p.ld_new + kvh * D;
+      for (int i = threadIdx.x; i < D / 2; i += kAttnThreads)
+        rope_head_bf16<D>(ks, p.k_cache + row, pos, p.theta, i, p.rope);
+      for (int i = threadIdx.x; i < D; i += kAttnThreads) p.v_cache[row + i] = __float2bfloat16_rn(vs[i]);
+    }
+    __syncthreads();
+  }
+
+  // Q A-fragments: logical d pair (2t,2t+1) of k-step j <-> physical d 16t+4j+{0,1},
+  // (2t+8,2t+9) <-> 16t+4j+{2,3}; head rows g+8 are always zero (grp <= 8).
+  uint32_t qa[4][2];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    qa[j][0] = q_s[g * QW + 8 * t + 2 * j];
+    qa[j][1] = q_s[g * QW + 8 * t + 2 * j + 1];
+  }
+
+  // ---- this warp's positions
+  const int n = max(0, hi - lo);
+  const int per_warp = ((n + kAttnWarps * kAttnChunk - 1) / (kAttnWarps * kAttnChunk)) * kAttnChunk;
+  const int w_lo = lo + warp * per_warp;
+  const int w_hi = min(hi, w_lo + per_warp);
+  const __nv_bfloat16* kbase = p.k_cache + (static_cast<size_t>(b) * p.hkv + kvh) * p.ctx_max * D;
+  const __nv_bfloat16* vbase = p.v_cache + (static_cast<size_t>(b) * p.hkv + kvh) * p.ctx_max * D;
+
+  float m_run = -INFINITY, l_run = 0.f;
+  float o[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+
+  auto load_chunk = [&](int c0, uint4 (&kr)[4], uint4 (&vr)[4]) {
+    // K rows c0+g and c0+8+g at d 16t..16t+15; V rows c0+{2t,2t+1,8+2t,9+2t} at d 8g..8g+7.
+    // Rows past the end are clamped to the last valid row (their scores are masked).
+    const int last = w_hi - 1;
+    const int r0 = min(c0 + g, last), r1 = min(c0 + 8 + g, last);
+    kr[0] = *reinterpret_cast<const uint4*>(kbase + static_cast<size_t>(r0) * D + 16 * t);
+    kr[1] = *reinterpret_cast<const uint4*>(kbase + static_cast<size_t>(r0) * D + 16 * t + 8);
+    kr[2] = *reinterpret_cast<const uint4*>(kbase + static_cast<size_t>(r1) * D + 16 * t);
+    kr[3] = *reinterpret_cast<const uint4*>(kbase + static_cast<size_t>(r1) * D + 16 * t + 8);
+    const int v0 = min(c0 + 2 * t, last), v1 = min(c0 + 2 * t + 1, last);
+    const int v2 = min(c0 + 8 + 2 * t, last), v3 = min(c0 + 9 + 2 * t, last);
+    vr[0] = *reinterpret_cast<const uint4*>(vbase + static_cast<size_t>(v0) * D + 8 * g);
+    vr[1] = *reinterpret_cast<const uint4*>(vbase + static_cast<size_t>(v1) * D + 8 * g);
+    vr[2] = *reinterpret_cast<const uint4*>(vbase + static_cast<size_t>(v2) * D + 8 * g);
+    vr[3] = *reinterpret_cast<const uint4*>(vbase + static_cast<size_t>(v3) * D + 8 * g);
+  };
+
+  if (w_lo < w_hi) {
+    uint4 kr[4], vr[4], kn[4], vn[4];
+    load_chunk(w_lo, kr, vr);
+    for (int c0 = w_lo; c0 < w_hi; c0 += kAttnChunk) {
+      const bool more = c0 + kAttnChunk < w_hi;
+      if (more) load_chunk(c0 + kAttnChunk, kn, vn);
+      // S = Q K^T for positions c0..c0+7 (n-tile 0) and c0+8..c0+15 (n-tile 1)
+      float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const uint32_t kw[8] = {kr[2 * nt].x, kr[2 * nt].y, kr[2 * nt].z, kr[2 * nt].w,
+                                kr[2 * nt + 1].x, kr[2 * nt + 1].y, kr[2 * nt + 1].z, kr[2 * nt + 1].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          mma_bf16_m16n8k16(s[nt][0], s[nt][1], s[nt][2], s[nt][3], qa[j][0], 0u, qa[j][1], 0u, kw[2 * j],
+                            kw[2 * j + 1]);
+      }
+      // scores (log2 units) with the causal / range mask; this lane: head g,
+      // positions c0 + 8nt + 2t + {0,1}
+      float sc[4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int pp = c0 + 8 * nt + 2 * t + e;
+          sc[2 * nt + e] = pp < w_hi ? s[nt][e] * p.scale_log2 : -INFINITY;
+        }
+      float mc = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+      mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, 1));
+      mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, 2));
+      const float m_new = fmaxf(m_run, mc);  // finite: every chunk holds >= 1 valid position
+      const float corr = exp2f(m_run - m_new);
+      float pr[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) pr[e] = exp2f(sc[e] - m_new);
+      l_run = l_run * corr + (pr[0] + pr[1] + pr[2] + pr[3]);
+      m_run = m_new;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        o[i][0] *= corr;
+        o[i][1] *= corr;
+      }
+      // P as the A operand (rows = heads, k = positions), split bf16 hi + lo
+      const uint32_t ph0 = pack_bf16x2(pr[0], pr[1]), ph1 = pack_bf16x2(pr[2], pr[3]);
+      const uint32_t pl0 = pack_bf16x2(pr[0] - bf16lo_to_f32(ph0), pr[1] - bf16hi_to_f32(ph0));
+      const uint32_t pl1 = pack_bf16x2(pr[2] - bf16lo_to_f32(ph1), pr[3] - bf16hi_to_f32(ph1));
+      const uint32_t va[4] = {vr[0].x, vr[0].y, vr[0].z, vr[0].w}, vb[4] = {vr[1].x, vr[1].y, vr[1].z, vr[1].w};
+      const uint32_t vc[4] = {vr[2].x, vr[2].y, vr[2].z, vr[2].w}, vd[4] = {vr[3].x, vr[3].y, vr[3].z, vr[3].w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {  // n-tile i: column g <-> d = 8g + i
+        const uint32_t sel = (i & 1) ? 0x7632u : 0x5410u;
+        const uint32_t b0 = prmt(va[i >> 1], vb[i >> 1], sel);
+        const uint32_t b1 = prmt(vc[i >> 1], vd[i >> 1], sel);
+        mma_bf16_m16n8k16(o[i][0], o[i][1], o[i][2], o[i][3], ph0, 0u, ph1, 0u, b0, b1);
+        mma_bf16_m16n8k16(o[i][0], o[i][1], o[i][2], o[i][3], pl0, 0u, pl1, 0u, b0, b1);
+      }
+      if (more) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          kr[i] = kn[i];
+          vr[i] = vn[i];
+        }
+      }
+    }
+  }
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+
+  // ---- merge the 4 warps (head g rows; lane t holds d = 16t + i and 16t + 8 + i)
+  if (t == 0) {
+    wm[warp][g] = m_run;
+    wl[warp][g] = l_run;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    wo[warp][g][16 * t + i] = o[i][0];
+    wo[warp][g][16 * t + 8 + i] = o[i][1];
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < grp * D; e += kAttnThreads) {
+    const int j = e / D, d = e % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wm[w][j]);
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kAttnWarps; ++w) {
+        const float f = wm[w][j] == -INFINITY ? 0.f : exp2f(wm[w][j] - M);
+        L += wl[w][j] * f;
+        O += wo[w][j][d] * f;
+      }
+    }
+    const int qhead = kvh * grp + j;
+    if (p.n_splits == 1) {
+      const size_t oi = static_cast<size_t>(b) * p.ldo + qhead * D + d;
+      if (p.out_f32)
+        reinterpret_cast<float*>(p.out)[oi] = O / L;
+      else
+        p.out[oi] = __float2bfloat16_rn(O / L);
+    } else {
+      float* pr = p.part + ((((static_cast<size_t>(b) * p.hkv + kvh) * p.n_splits + split) * grp + j) * (D + 2));
+      pr[d] = O;
+      if (d == 0) {
+        pr[D] = M;
+        pr[D + 1] = L;
+      }
+    }
+  }
+}
+
+// Log-sum-exp merge of the split partials: one CTA per (q head, sequence).
+template <int D>
+__global__ void __launch_bounds__(D) gqa_combine_kernel(const AttnParams p) {
+  const int qhead = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+  const int grp = p.hq / p.hkv;
+  const int kvh = qhead / grp, j = qhead % grp;
+  pdl_wait();
+  pdl_launch_dependents();
+  const float* base = p.part + ((static_cast<size_t>(b) * p.hkv + kvh) * p.n_splits * grp + j) * (D + 2);
+  const size_t stride = static_cast<size_t>(grp) * (D + 2);
+  float M = -INFINITY;
+  for (int s = 0; s < p.n_splits; ++s) M = fmaxf(M, base[s * stride + D]);
+  float L = 0.f, O = 0.f;
+  for (int s = 0; s < p.n_splits; ++s) {
+    const float ms = base[s * stride + D];
+    if (ms == -INFINITY) continue;  // split past this sequence's end
+    const float f = exp2f(ms - M);
+    L += base[s * stride + D + 1] * f;
+    O += base[s * stride + d] * f;
+  }
+  const size_t oi = static_cast<size_t>(b) * p.ldo + qhead * D + d;
+  if (p.out_f32)
+    reinterpret_cast<float*>(p.out)[oi] = O / L;
+  else
+    p.out[oi] = __float2bfloat16_rn(O / L);
+}
+
+}  // namespace b2

@@ -138,3 +138,79 @@ def set_launch_options(pdl: bool = True) -> None:
 def device_error() -> int:
     """Read and clear the device error word (synchronises the current stream)."""
     return _native.read_device_error(torch.cuda.current_stream().cuda_stream)
+
+
+ATTN_NO_APPEND = 1
+ATTN_NO_ROPE = 2
+ATTN_OUT_F32 = 4
+
+
+def gqa_decode_workspace_bytes(batch: int, n_q_heads: int, n_kv_heads: int, head_dim: int, max_len: int) -> int:
+    n = ctypes.c_size_t(0)
+    _native.check(_native.lib().b2_gqa_decode_workspace_size(batch, n_q_heads, n_kv_heads, head_dim, max_len,
+                                                              ctypes.byref(n)), "b2_gqa_decode_workspace_size")
+    return n.value
+
+
+def gqa_decode(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, k_cache: torch.Tensor,
+               v_cache: torch.Tensor, pos: torch.Tensor, *, n_q_heads: int, n_kv_heads: int,
+               theta: float = 10000.0, scale: float | None = None, max_len: int | None = None,
+               out: torch.Tensor | None = None, append: bool = True, rope: bool = True,
+               out_f32: bool = False, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """GQA flash-decode for one new token per sequence (see b2_gqa_decode).
+
+    q [B, >=Hq*D], k_new/v_new [B, >=Hkv*D] fp32 with a common row stride (e.g.
+    slices of the QKV GEMV output); caches bf16 [B, Hkv, ctx_max, D]; pos int32 [B].
+    Returns out [B, Hq*D] (bf16, or fp32 with out_f32).
+    """
+    for name, t in (("q", q), ("k_new", k_new), ("v_new", v_new)):
+        _need(t, name, torch.float32)
+        if t.dim() != 2 or t.stride(1) != 1:
+            raise ValueError(f"{name} must be a 2-D row-major view")
+    ld_new = q.stride(0)
+    if q.shape[0] == 1:  # one sequence: the row stride is never used
+        ld_new = max(q.shape[1], n_q_heads * k_cache.shape[-1])
+    elif not (q.stride(0) == k_new.stride(0) == v_new.stride(0)):
+        raise ValueError("q, k_new, v_new must share a row stride")
+    _need(k_cache, "k_cache", torch.bfloat16)
+    _need(v_cache, "v_cache", torch.bfloat16)
+    _need(pos, "pos", torch.int32)
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous() and pos.is_contiguous()):
+        raise ValueError("caches and pos must be contiguous")
+    b, hkv, ctx_max, d = k_cache.shape
+    if v_cache.shape != k_cache.shape or hkv != n_kv_heads or pos.numel() != b or q.shape[0] != b:
+        raise ValueError("inconsistent attention shapes")
+    max_len = ctx_max if max_len is None else max_len
+    scale = d ** -0.5 if scale is None else scale
+    odt = torch.float32 if out_f32 else torch.bfloat16
+    if out is None:
+        out = torch.empty((b, n_q_heads * d), dtype=odt, device=q.device)
+    _need(out, "out", odt)
+    ws_n = gqa_decode_workspace_bytes(b, n_q_heads, n_kv_heads, d, max_len)
+    if workspace is None or workspace.numel() < ws_n:
+        workspace = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=q.device)
+    flags = (0 if append else ATTN_NO_APPEND) | (0 if rope else ATTN_NO_ROPE) | (ATTN_OUT_F32 if out_f32 else 0)
+    _native.call("b2_gqa_decode", _ptr(q), _ptr(k_new), _ptr(v_new), ld_new, _ptr(k_cache), _ptr(v_cache),
+                 _ptr(pos), b, n_q_heads, n_kv_heads, d, ctx_max, max_len, float(theta), float(scale), _ptr(out),
+                 out.stride(0), _ptr(workspace), workspace.numel(), flags, _stream())
+    return out
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16 y = x * rsqrt(mean(x^2) + eps) * w over the last dim; x bf16 or fp32 [B, n] or [n]."""
+    if x.dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError("x must be bf16 or fp32")
+    _need(x, "x", x.dtype)
+    _need(w, "w", torch.bfloat16)
+    x2 = x.reshape(1, -1) if x.dim() == 1 else x
+    if x2.stride(1) != 1:
+        x2 = x2.contiguous()
+    b, n = x2.shape
+    if w.numel() != n:
+        raise ValueError("weight length mismatch")
+    if out is None:
+        out = torch.empty((b, n), dtype=torch.bfloat16, device=x.device)
+    _need(out, "out", torch.bfloat16)
+    _native.call("b2_rmsnorm", _ptr(x2), 1 if x2.dtype == torch.float32 else 0, x2.stride(0), _ptr(w),
+                 float(eps), b, n, _ptr(out), out.stride(0), _stream())
+    return out if x.dim() == 2 else out[0]
