@@ -136,6 +136,28 @@ int b2_gqa_decode(const float* q, const float* k_new, const float* v_new, int ld
                   int ctx_max, int max_len, float theta, float scale, uint16_t* out, int ldo, void* workspace,
                   size_t workspace_bytes, int flags, void* stream);
 
+/* b2_gqa_decode without a workspace argument, for callers that cannot allocate
+ * device memory: code that only receives input and output buffers from a host
+ * framework that owns the GPU allocator, or a service that forbids device
+ * allocation after start-up because cudaMalloc can block and synchronise the
+ * device.  It has no counterpart in the reference.
+ *   - Same arguments and results as b2_gqa_decode, minus the workspace.
+ *   - Its scratch is a fixed 2 MiB array inside the library, held by every GPU
+ *     that loads the library until the process exits.  A call whose split
+ *     partials would need more (b2_gqa_decode_workspace_size() > 2 MiB) returns
+ *     B2_ERR_WORKSPACE without launching anything.
+ *   - The first call on each device looks up the array's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture on the device.
+ *   - It allocates nothing: no cudaMalloc, cudaFree or allocating library call.
+ *   - All calls share the one array.  Each call writes every partial it later
+ *     reads, so nothing needs to start at zero, but calls that overlap on the
+ *     GPU (other streams, other threads) race on it: serialise them. */
+int b2_gqa_decode_static(const float* q, const float* k_new, const float* v_new, int ld_new, uint16_t* k_cache,
+                         uint16_t* v_cache, const int32_t* pos, int batch, int n_q_heads, int n_kv_heads,
+                         int head_dim, int ctx_max, int max_len, float theta, float scale, uint16_t* out, int ldo,
+                         int flags, void* stream);
+
 /* RMSNorm y = x * rsqrt(mean(x^2) + eps) * w over rows of n, bf16 out.
  *   x  bf16 (x_is_f32 = 0) or fp32 (x_is_f32 = 1), [batch][ldx];  w bf16 [n]
  * Replaces granite_rms_norm (designs/granite_gemv/granite_rmsnorm.h:45-80). */

@@ -300,6 +300,31 @@ int attn_check(int batch, int hq, int hkv, int head_dim, int ctx_max, int max_le
   return B2_OK;
 }
 
+// ------------------------------------------ attention with static scratch
+// Device scratch for b2_gqa_decode_static, for callers that cannot allocate
+// device memory.  Every GPU that loads this library holds these 2 MiB until the
+// process exits.  Host code must not pass the symbol itself to a kernel (on the
+// host it is only a stand-in); its device address is looked up once per device.
+constexpr size_t kAttnStaticScratchBytes = size_t(2) << 20;
+static __device__ __align__(256) unsigned char g_attn_static_scratch[kAttnStaticScratchBytes];
+void* g_attn_static_ptr[64] = {};
+
+// Device address of the static scratch on the current device (set up on first use).
+int attn_static_scratch(void** out) {
+  int d = -1;
+  cudaError_t e = cudaGetDevice(&d);
+  if (e != cudaSuccess || d < 0 || d >= 64) return fail(B2_ERR_NO_DEVICE, "no current CUDA device");
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_attn_static_ptr[d]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_attn_static_scratch);
+    if (e != cudaSuccess || !ptr) return cuda_fail(e, "cudaGetSymbolAddress(static attention scratch)");
+    g_attn_static_ptr[d] = ptr;
+  }
+  *out = g_attn_static_ptr[d];
+  return B2_OK;
+}
+
 }  // namespace
 
 // ------------------------------------------------------------------ C ABI
@@ -435,6 +460,28 @@ int b2_gqa_decode(const float* q, const float* k_new, const float* v_new, int ld
     if (e != cudaSuccess) return cuda_fail(e, "attention combine launch");
   }
   return B2_OK;
+}
+
+int b2_gqa_decode_static(const float* q, const float* k_new, const float* v_new, int ld_new, uint16_t* k_cache,
+                         uint16_t* v_cache, const int32_t* pos, int batch, int n_q_heads, int n_kv_heads,
+                         int head_dim, int ctx_max, int max_len, float theta, float scale, uint16_t* out, int ldo,
+                         int flags, void* stream) {
+  DevInfo di;
+  int st = device_info(&di);
+  if (st != B2_OK) return st;
+  st = attn_check(batch, n_q_heads, n_kv_heads, head_dim, ctx_max, max_len);
+  if (st != B2_OK) return st;
+  const AttnPlan pl = attn_plan(batch, n_q_heads, n_kv_heads, head_dim, max_len, di.sms);
+  if (pl.ws_bytes > kAttnStaticScratchBytes)
+    return fail(B2_ERR_WORKSPACE,
+                "this call needs %zu bytes of scratch, more than the %zu-byte static scratch of "
+                "b2_gqa_decode_static; call b2_gqa_decode with a workspace instead",
+                pl.ws_bytes, kAttnStaticScratchBytes);
+  void* ws = nullptr;
+  st = attn_static_scratch(&ws);
+  if (st != B2_OK) return st;
+  return b2_gqa_decode(q, k_new, v_new, ld_new, k_cache, v_cache, pos, batch, n_q_heads, n_kv_heads, head_dim,
+                       ctx_max, max_len, theta, scale, out, ldo, ws, kAttnStaticScratchBytes, flags, stream);
 }
 
 int b2_rmsnorm(const void* x, int x_is_f32, int ldx, const uint16_t* w, float eps, int batch, int n, uint16_t* y,
