@@ -223,6 +223,64 @@ def time_graph(torch, g, steps: int, warmup: int) -> float:
     return a.elapsed_time(b) / steps  # ms per replay
 
 
+def measure_decode(torch, world: int, rank: int, batch: int, ctx: int, steps: int, warmup: int) -> dict:
+    """Config 4: the full 40-layer decode step at `batch` tokens, context `ctx`, TP over `world` ranks."""
+    import torch.distributed as dist
+    from llmnputest_b200.decode import GRANITE_3B, Q4Decoder
+    from llmnputest_b200.tp import ShardPlan, TPDecoder, shard_weights
+
+    cfg = GRANITE_3B
+    if world == 1:
+        dec = Q4Decoder(cfg, batch, ctx, seed=11)
+    else:
+        full_dec = Q4Decoder(cfg, 1, 1, seed=11)  # weights only; the KV cache lives in the TP decoder
+        plan = ShardPlan(cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.hidden, cfg.intermediate, cfg.vocab,
+                         world, rank)
+        dec = TPDecoder(cfg, batch, ctx, shard_weights(full_dec.w, plan), plan)
+        del full_dec
+        torch.cuda.empty_cache()
+    dec.pos.fill_(ctx - 1)  # attend over the full context
+    dec.x_in.normal_()
+    try:
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            dec.step()
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            dec.step()
+        run, how = g.replay, "cuda graph"
+    except Exception as e:  # capture of the collectives failed: time the eager step instead
+        torch.cuda.synchronize()
+        run, how = dec.step, f"eager ({type(e).__name__})"
+    for _ in range(warmup):
+        run()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        run()
+    b.record()
+    b.synchronize()
+    ms = a.elapsed_time(b) / steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    wb = cfg.weight_bytes()
+    kv = batch * ctx * cfg.n_kv_heads * cfg.head_dim * 4 * cfg.n_layers
+    step_bytes = wb["layers"] + wb["lm_head"] + kv  # algorithmic: every weight and KV byte once
+    out = {"batch": batch, "ctx": ctx, "tp": world, "ms_per_step": round(ms, 4),
+           "tok_s": round(batch / (ms * 1e-3), 1), "how": how,
+           "hbm_gbs_per_gpu": round(step_bytes / world / (ms * 1e-3) / 1e9, 1)}
+    del dec
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_b200(args, rank: int, world: int) -> dict | None:
     import torch
     import torch.distributed as dist
@@ -292,6 +350,12 @@ def run_b200(args, rank: int, world: int) -> dict | None:
         extras["q8_lm_head"] = {"us": round(tl * 1e3, 2), "gbs": round(w8.numel() / (tl * 1e-3) / 1e9, 1),
                                 "frac_of_measured_hbm": round(w8.numel() / (tl * 1e-3) / 1e9 / pk["hbm_gbs"], 3)}
         del gl, w8
+
+    # ---- config 4: the full decode step (tensor-parallel across the ranks when N > 1)
+    if not args.quick:
+        del g
+        extras["decode"] = [measure_decode(torch, world, rank, b, 4096, max(10, args.steps // 30), 3)
+                            for b in (1, 32)]
 
     # ---- e2e: host buffers, copies inside the timed region
     xs_host = torch.cat([c[4].reshape(-1) for c in calls]).cpu().pin_memory()

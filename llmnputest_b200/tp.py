@@ -1,0 +1,210 @@
+"""Tensor-parallel decode over one node (NCCL over NVLink), one process per GPU.
+
+Sharding follows the natural seams of the q4nx tiles (all cuts are whole tiles;
+tile bytes are never modified):
+
+  QKV + attention  by kv head: rank r owns kv heads [r*Hkv/W, (r+1)*Hkv/W) and
+                   their q heads; its QKV weight is those heads' whole tile-rows
+                   (q: grp*D rows per kv head, k and v: D rows each), and its KV
+                   cache holds only its heads.  No collective.
+  O                the attention outputs are all-gathered (bf16), O is sharded by
+                   output rows (hidden/W rows = whole tile-rows) and its outputs
+                   all-gathered into every rank's replicated residual stream.
+                   (Sharding O by input columns would cut 256-wide K-tiles at
+                   W = 4 and 8: 640 or 320 columns per rank.)
+  FFN              gate/up by intermediate rows (I/W rows each), SwiGLU local;
+                   down by whole K-tiles of the intermediate axis (I/W/256 per
+                   rank), its fp32 partials all-reduced (sum) into the residual.
+  lm_head          by vocab tile-rows; fp32 logits all-gathered.
+
+ShardPlan and shard_weights are plain host logic (they run on CPU tensors too);
+TPDecoder runs the step on the GPU.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+from .format import Q4_TILE_BYTES, Q8_TILE_BYTES, TILE_K, TILE_ROWS
+
+
+@dataclass(frozen=True)
+class ShardPlan:
+    """Which rows / K-tiles / heads rank `rank` of `world` owns."""
+
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    hidden: int
+    intermediate: int
+    vocab: int
+    world: int
+    rank: int
+
+    def __post_init__(self):
+        w = self.world
+        if self.n_kv_heads % w:
+            raise ValueError(f"{self.n_kv_heads} kv heads do not split over {w} ranks")
+        if self.hidden % (TILE_ROWS * w) or self.intermediate % (TILE_K * w):
+            raise ValueError("hidden / intermediate do not split into whole tiles")
+        if (self.vocab // TILE_ROWS) % w:
+            raise ValueError("vocab tile-rows do not split evenly")
+
+    @property
+    def grp(self) -> int:
+        return self.n_heads // self.n_kv_heads
+
+    @property
+    def kv_local(self) -> int:
+        return self.n_kv_heads // self.world
+
+    @property
+    def q_local(self) -> int:
+        return self.kv_local * self.grp
+
+    def qkv_tile_rows(self) -> list[int]:
+        """Tile-rows of the full [q | k | v] QKV weight that this rank owns, in its order q|k|v."""
+        d, tpr = self.head_dim, self.head_dim // TILE_ROWS  # tile-rows per head
+        kv0 = self.rank * self.kv_local
+        q_rows = range(kv0 * self.grp * tpr, (kv0 + self.kv_local) * self.grp * tpr)
+        k_base = self.n_heads * d // TILE_ROWS
+        v_base = k_base + self.n_kv_heads * d // TILE_ROWS
+        k_rows = range(k_base + kv0 * tpr, k_base + (kv0 + self.kv_local) * tpr)
+        v_rows = range(v_base + kv0 * tpr, v_base + (kv0 + self.kv_local) * tpr)
+        return list(q_rows) + list(k_rows) + list(v_rows)
+
+    def row_range(self, n_rows: int) -> tuple[int, int]:
+        per = n_rows // self.world
+        return self.rank * per, (self.rank + 1) * per
+
+    def o_tile_rows(self) -> range:
+        return range(*self.row_range(self.hidden // TILE_ROWS))
+
+    def ffn_tile_rows(self) -> range:
+        return range(*self.row_range(self.intermediate // TILE_ROWS))
+
+    def down_k_tiles(self) -> range:
+        return range(*self.row_range(self.intermediate // TILE_K))
+
+    def vocab_tile_rows(self) -> range:
+        return range(*self.row_range(self.vocab // TILE_ROWS))
+
+
+def take_tile_rows(tiles: torch.Tensor, k_tiles: int, tile_bytes: int, rows) -> torch.Tensor:
+    """Gather whole tile-rows (each k_tiles*tile_bytes contiguous bytes) into a new contiguous buffer."""
+    t = tiles.view(-1, k_tiles * tile_bytes)
+    idx = torch.as_tensor(list(rows), dtype=torch.long, device=tiles.device)
+    return t.index_select(0, idx).reshape(-1).contiguous()
+
+
+def take_k_tiles(tiles: torch.Tensor, n_tile_rows: int, k_tiles: int, tile_bytes: int, ks) -> torch.Tensor:
+    """Keep K-tiles `ks` of every tile-row: [n_t][k_t][tile] -> [n_t][len(ks)][tile]."""
+    t = tiles.view(n_tile_rows, k_tiles, tile_bytes)
+    idx = torch.as_tensor(list(ks), dtype=torch.long, device=tiles.device)
+    return t.index_select(1, idx).reshape(-1).contiguous()
+
+
+def shard_weights(full: dict, plan: ShardPlan) -> dict:
+    """One rank's slice of a full (unsharded) weight dict in the layout of decode.Q4Decoder."""
+    kt_h = plan.hidden // TILE_K
+    kt_q = plan.n_heads * plan.head_dim // TILE_K
+    kt_i = plan.intermediate // TILE_K
+    nt_h = plan.hidden // TILE_ROWS
+    out = {"layers": []}
+    for L in full["layers"]:
+        out["layers"].append({
+            "qkv": take_tile_rows(L["qkv"], kt_h, Q4_TILE_BYTES, plan.qkv_tile_rows()),
+            "o": take_tile_rows(L["o"], kt_q, Q4_TILE_BYTES, plan.o_tile_rows()),
+            "gate": take_tile_rows(L["gate"], kt_h, Q4_TILE_BYTES, plan.ffn_tile_rows()),
+            "up": take_tile_rows(L["up"], kt_h, Q4_TILE_BYTES, plan.ffn_tile_rows()),
+            "down": take_k_tiles(L["down"], nt_h, kt_i, Q4_TILE_BYTES, plan.down_k_tiles()),
+            "attn_norm": L["attn_norm"],
+            "mlp_norm": L["mlp_norm"],
+        })
+    out["final_norm"] = full["final_norm"]
+    out["lm_head"] = take_tile_rows(full["lm_head"], kt_h, Q8_TILE_BYTES, plan.vocab_tile_rows())
+    return out
+
+
+class TPDecoder:
+    """Tensor-parallel decode step on this rank's shard; collectives on the default process group."""
+
+    def __init__(self, cfg, batch: int, ctx_max: int, shard: dict, plan: ShardPlan, device=None, ops=None):
+        if ops is None:
+            from . import ops  # the GPU path; tests of the host logic may pass another implementation
+        self.ops = ops
+        self.cfg, self.plan, self.batch, self.ctx_max = cfg, plan, batch, ctx_max
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        dev, c, p, W = self.device, cfg, plan, plan.world
+        self.w = shard
+        self.kt_h, self.kt_q, self.kt_i = c.hidden // TILE_K, c.n_heads * c.head_dim // TILE_K, c.intermediate // TILE_K
+        self.kt_i_local = self.kt_i // W
+        self.nt_qkv_local = len(p.qkv_tile_rows())
+        self.nt_o_local = c.hidden // TILE_ROWS // W
+        self.nt_i_local = c.intermediate // TILE_ROWS // W
+        self.nt_v_local = c.vocab // TILE_ROWS // W
+        d = c.head_dim
+        kv_shape = (batch, p.kv_local, ctx_max, d)
+        self.k_cache = [torch.zeros(kv_shape, dtype=torch.bfloat16, device=dev) for _ in range(c.n_layers)]
+        self.v_cache = [torch.zeros(kv_shape, dtype=torch.bfloat16, device=dev) for _ in range(c.n_layers)]
+        self.x_in = torch.zeros(batch, c.hidden, dtype=torch.float32, device=dev)
+        self.resid = torch.zeros(batch, c.hidden, dtype=torch.float32, device=dev)
+        self.xn = torch.zeros(batch, c.hidden, dtype=torch.bfloat16, device=dev)
+        self.qkv = torch.zeros(batch, self.nt_qkv_local * TILE_ROWS, dtype=torch.float32, device=dev)
+        self.attn_local = torch.zeros(batch, p.q_local * d, dtype=torch.bfloat16, device=dev)
+        # gathered buffers are [W*B, n] (rank-major), viewed as [W, B, n] when merged
+        self.attn_all = torch.zeros(W * batch, p.q_local * d, dtype=torch.bfloat16, device=dev)
+        self.attn = torch.zeros(batch, c.n_heads * d, dtype=torch.bfloat16, device=dev)
+        self.o_local = torch.zeros(batch, c.hidden // W, dtype=torch.float32, device=dev)
+        self.o_all = torch.zeros(W * batch, c.hidden // W, dtype=torch.float32, device=dev)
+        self.h = torch.zeros(batch, c.intermediate // W, dtype=torch.bfloat16, device=dev)
+        self.down = torch.zeros(batch, c.hidden, dtype=torch.float32, device=dev)
+        self.logits_local = torch.zeros(batch, c.vocab // W, dtype=torch.float32, device=dev)
+        self.logits_all = torch.zeros(W * batch, c.vocab // W, dtype=torch.float32, device=dev)
+        self.logits = torch.zeros(batch, c.vocab, dtype=torch.float32, device=dev)
+        self.pos = torch.zeros(batch, dtype=torch.int32, device=dev)
+        ws = ops.gqa_decode_workspace_bytes(batch, p.q_local, p.kv_local, d, ctx_max)
+        self.attn_ws = torch.empty(max(ws, 1), dtype=torch.uint8, device=dev)
+
+    def step(self) -> torch.Tensor:
+        ops, c, p, W = self.ops, self.cfg, self.plan, self.plan.world
+        d = c.head_dim
+        qd, kd = p.q_local * d, p.kv_local * d
+        self.resid.copy_(self.x_in)
+        for li, L in enumerate(self.w["layers"]):
+            ops.rmsnorm(self.resid, L["attn_norm"], c.rms_eps, out=self.xn)
+            ops.q4_gemv(L["qkv"], self.nt_qkv_local, self.kt_h, self.xn, out=self.qkv, prefetch=True)
+            ops.gqa_decode(self.qkv[:, :qd], self.qkv[:, qd:qd + kd], self.qkv[:, qd + kd:], self.k_cache[li],
+                           self.v_cache[li], self.pos, n_q_heads=p.q_local, n_kv_heads=p.kv_local,
+                           theta=c.rope_theta, scale=d ** -0.5, max_len=self.ctx_max, out=self.attn_local,
+                           workspace=self.attn_ws)
+            if W > 1:
+                dist.all_gather_into_tensor(self.attn_all, self.attn_local)
+                # rank-major [W][B][q_local*D] -> [B][Hq*D] (head order = rank order)
+                self.attn.view(self.batch, W, qd).copy_(self.attn_all.view(W, self.batch, qd).permute(1, 0, 2))
+                a = self.attn
+            else:
+                a = self.attn_local
+            ops.q4_gemv(L["o"], self.nt_o_local, self.kt_q, a, out=self.o_local, prefetch=True)
+            if W > 1:
+                dist.all_gather_into_tensor(self.o_all, self.o_local)
+                self.resid.view(self.batch, W, -1).add_(self.o_all.view(W, self.batch, -1).permute(1, 0, 2))
+            else:
+                self.resid.add_(self.o_local)
+            ops.rmsnorm(self.resid, L["mlp_norm"], c.rms_eps, out=self.xn)
+            ops.q4_swiglu_gemv(L["gate"], L["up"], self.nt_i_local, self.kt_h, self.xn, out=self.h, prefetch=True)
+            ops.q4_gemv(L["down"], c.hidden // TILE_ROWS, self.kt_i_local, self.h, out=self.down, prefetch=True)
+            if W > 1:
+                dist.all_reduce(self.down)
+            self.resid.add_(self.down)
+        ops.rmsnorm(self.resid, self.w["final_norm"], c.rms_eps, out=self.xn)
+        ops.q8_gemv(self.w["lm_head"], self.nt_v_local, self.kt_h, self.xn, out=self.logits_local, prefetch=True)
+        if W > 1:
+            dist.all_gather_into_tensor(self.logits_all, self.logits_local)
+            self.logits.view(self.batch, W, -1).copy_(self.logits_all.view(W, self.batch, -1).permute(1, 0, 2))
+        else:
+            self.logits.copy_(self.logits_local)
+        return self.logits

@@ -1,0 +1,156 @@
+"""Tensor-parallel host logic on CPU: shard plans reassemble the full projections,
+and a 2-rank gloo run of TPDecoder.step (collectives and reshapes) equals the
+unsharded step.  The GPU ops are replaced by an oracle-backed shim here -- this
+file tests the sharding and collective plumbing, not the kernels."""
+
+import os
+import socket
+from types import SimpleNamespace
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+from ml_dtypes import bfloat16
+
+from oracle import q4nx_oracle as orc
+from llmnputest_b200.decode import DecoderConfig
+from llmnputest_b200.tp import ShardPlan, TPDecoder, shard_weights
+
+CFG = DecoderConfig(n_layers=2, hidden=512, n_heads=8, n_kv_heads=2, head_dim=64, intermediate=1024, vocab=512)
+
+
+def _bf(t):
+    return torch.from_numpy(np.asarray(t, np.float32)).to(torch.bfloat16)
+
+
+def full_weights(cfg, seed=0):
+    rng = np.random.default_rng(seed)
+    kt_h, kt_q, kt_i = cfg.hidden // 256, cfg.n_heads * cfg.head_dim // 256, cfg.intermediate // 256
+    u8 = lambda a: torch.from_numpy(np.ascontiguousarray(a).reshape(-1))
+    norm = lambda: _bf(rng.standard_normal(cfg.hidden) * 0.1 + 1)
+    layers = [{"qkv": u8(orc.synth_q4_tiles(rng, cfg.qkv_rows // 32 * kt_h)),
+               "o": u8(orc.synth_q4_tiles(rng, cfg.hidden // 32 * kt_q)),
+               "gate": u8(orc.synth_q4_tiles(rng, cfg.intermediate // 32 * kt_h)),
+               "up": u8(orc.synth_q4_tiles(rng, cfg.intermediate // 32 * kt_h)),
+               "down": u8(orc.synth_q4_tiles(rng, cfg.hidden // 32 * kt_i)),
+               "attn_norm": norm(), "mlp_norm": norm()} for _ in range(cfg.n_layers)]
+    return {"layers": layers, "final_norm": norm(), "lm_head": u8(orc.synth_q8_tiles(rng, cfg.vocab // 32 * kt_h))}
+
+
+class OracleOps:
+    """The ops signatures of llmnputest_b200.ops, computed by the CPU oracle (test infrastructure)."""
+
+    @staticmethod
+    def _x(x):
+        return x.float().numpy()
+
+    def q4_gemv(self, tiles, n_t, k_t, x, out=None, accumulate=False, prefetch=False):
+        y = torch.from_numpy(orc.gemv_q4(tiles.numpy(), self._x(x).astype(bfloat16), n_t, k_t))
+        out.add_(y) if accumulate else out.copy_(y)
+        return out
+
+    def q8_gemv(self, tiles, n_t, k_t, x, out=None, accumulate=False, prefetch=False):
+        out.copy_(torch.from_numpy(orc.gemv_q8(tiles.numpy(), self._x(x).astype(bfloat16), n_t, k_t)))
+        return out
+
+    def q4_swiglu_gemv(self, gate, up, n_t, k_t, x, out=None, prefetch=False):
+        xb = self._x(x).astype(bfloat16)
+        h = orc.swiglu_from_accumulators(orc.gemv_q4(gate.numpy(), xb, n_t, k_t), orc.gemv_q4(up.numpy(), xb, n_t, k_t))
+        out.copy_(_bf(h))
+        return out
+
+    def rmsnorm(self, x, w, eps, out=None):
+        out.copy_(_bf(orc.rmsnorm(self._x(x), w.float().numpy(), eps)))
+        return out
+
+    def gqa_decode(self, q, k_new, v_new, k_cache, v_cache, pos, *, n_q_heads, n_kv_heads, theta, scale,
+                   max_len, out, workspace=None, **_):
+        d = k_cache.shape[-1]
+        bsz = q.shape[0]
+        qr = np.zeros((bsz, n_q_heads, d), np.float32)
+        for b in range(bsz):
+            p = int(pos[b])
+            qr[b] = orc.rope_half_split(q[b].numpy().reshape(n_q_heads, d), p, theta).astype(np.float32).astype(bfloat16)
+            k_cache[b, :, p] = _bf(orc.rope_half_split(k_new[b].numpy().reshape(n_kv_heads, d), p, theta))
+            v_cache[b, :, p] = _bf(v_new[b].numpy().reshape(n_kv_heads, d))
+        o = orc.gqa_decode(qr, k_cache.float().numpy(), v_cache.float().numpy(), pos.numpy() + 1, scale)
+        out.copy_(_bf(o.reshape(bsz, -1)))
+        return out
+
+    def gqa_decode_workspace_bytes(self, *a):
+        return 0
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_shards_reassemble_full_projections(world):
+    cfg = DecoderConfig(n_layers=1, hidden=2048, n_heads=16, n_kv_heads=8, head_dim=64, intermediate=4096, vocab=2048)
+    W = full_weights(cfg, seed=world)
+    L = W["layers"][0]
+    rng = np.random.default_rng(0)
+    x = orc.synth_bf16(rng, cfg.hidden)
+    kt_h, kt_i = cfg.hidden // 256, cfg.intermediate // 256
+    full_qkv = orc.gemv_q4(L["qkv"].numpy(), x, cfg.qkv_rows // 32, kt_h)
+    h = orc.synth_bf16(rng, cfg.intermediate)
+    full_down = orc.gemv_q4(L["down"].numpy(), h, cfg.hidden // 32, kt_i)
+    down_sum = np.zeros(cfg.hidden)
+    heads = []
+    for r in range(world):
+        plan = ShardPlan(cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.hidden, cfg.intermediate, cfg.vocab, world, r)
+        S = shard_weights(W, plan)["layers"][0]
+        qkv = orc.gemv_q4(S["qkv"].numpy(), x, len(plan.qkv_tile_rows()), kt_h)
+        rows = np.concatenate([np.arange(t * 32, t * 32 + 32) for t in plan.qkv_tile_rows()])
+        assert np.array_equal(qkv, full_qkv[rows])  # same tiles, same arithmetic: bit-identical
+        heads.append(qkv[:plan.q_local * 64])
+        ks = list(plan.down_k_tiles())
+        down_sum += orc.gemv_q4(S["down"].numpy(), h[ks[0] * 256:(ks[-1] + 1) * 256], cfg.hidden // 32, len(ks))
+    assert np.array_equal(np.concatenate(heads), full_qkv[:cfg.n_heads * 64])  # q heads in rank order
+    np.testing.assert_allclose(down_sum, full_down, rtol=1e-4, atol=1e-3 * np.abs(full_down).max())
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _run_rank(rank, world, port, x, pos, ctx, result_path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        W = full_weights(CFG)
+        plan = ShardPlan(CFG.n_heads, CFG.n_kv_heads, CFG.head_dim, CFG.hidden, CFG.intermediate, CFG.vocab,
+                         world, rank)
+        dec = TPDecoder(CFG, x.shape[0], ctx, shard_weights(W, plan), plan, device="cpu", ops=OracleOps())
+        for step in range(2):
+            dec.x_in.copy_(x[step])
+            dec.pos.copy_(pos + step)
+            logits = dec.step().clone()
+        if rank == 0:
+            torch.save(logits, result_path)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp_step_gloo_matches_single_rank(tmp_path):
+    rng = np.random.default_rng(5)
+    bsz, ctx = 2, 16
+    x = torch.from_numpy(rng.standard_normal((2, bsz, CFG.hidden)).astype(np.float32))
+    pos = torch.tensor([3, 9], dtype=torch.int32)
+    out1 = tmp_path / "w1.pt"
+    out2 = tmp_path / "w2.pt"
+    ctx_mp = mp.get_context("spawn")
+    for world, path in ((1, out1), (2, out2)):
+        port = _free_port()
+        procs = [ctx_mp.Process(target=_run_rank, args=(r, world, port, x, pos, ctx, str(path))) for r in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=240)
+            assert p.exitcode == 0
+    a, b = torch.load(out1), torch.load(out2)
+    cos, rel = orc.compare(b.numpy(), a.numpy())
+    assert cos >= 0.99999 and rel <= 1e-3, (cos, rel)
