@@ -94,6 +94,20 @@ int b2_q8_gemv(const uint8_t* tiles, int n_tile_rows, int k_tiles, const uint16_
 int b2_q4_swiglu_gemv(const uint8_t* gate, const uint8_t* up, int n_tile_rows, int k_tiles, const uint16_t* x,
                       int batch, int ldx, uint16_t* h, int ldh, int flags, void* stream);
 
+/* The three GEMVs above with RMSNorm fused into their input: the kernel reads the
+ * fp32 rows x [batch][ldx] (e.g. the residual stream; 16-byte aligned, ldx % 4 == 0),
+ * forms bf16(x * rsqrt(mean(x^2) + eps) * norm_w) (norm_w bf16 [K]) and multiplies
+ * that, as b2_rmsnorm followed by the plain GEMV would, without the extra launch.
+ * The norm is granite_rms_norm (designs/granite_gemv/granite_rmsnorm.h:45-80); the
+ * composition is the layer order of designs/granite_gemv/granite_layer.py:54-59. */
+int b2_q4_gemv_rmsnorm(const uint8_t* tiles, int n_tile_rows, int k_tiles, const float* x, int batch, int ldx,
+                       const uint16_t* norm_w, float eps, float* y, int ldy, int flags, void* stream);
+int b2_q8_gemv_rmsnorm(const uint8_t* tiles, int n_tile_rows, int k_tiles, const float* x, int batch, int ldx,
+                       const uint16_t* norm_w, float eps, float* y, int ldy, int flags, void* stream);
+int b2_q4_swiglu_gemv_rmsnorm(const uint8_t* gate, const uint8_t* up, int n_tile_rows, int k_tiles, const float* x,
+                              int batch, int ldx, const uint16_t* norm_w, float eps, uint16_t* h, int ldh,
+                              int flags, void* stream);
+
 /* Tile decode, weight-index order: out bf16 [n_tiles][8192] = RNE(code*d + m)
  * (q4) or RNE(code*s) (q8).  Bit-exact with tools/q4nx.py dequant_q4 / dequant_q8
  * (:97-111) and designs/q4nx_unpack/q4nx_unpack.cc:40-92. */

@@ -27,6 +27,9 @@ SIGNATURES: dict[str, tuple] = {
     "b2_q4_gemv": (_i32, [_vp, _i32, _i32, _vp, _i32, _i32, _vp, _i32, _i32, _vp]),
     "b2_q8_gemv": (_i32, [_vp, _i32, _i32, _vp, _i32, _i32, _vp, _i32, _i32, _vp]),
     "b2_q4_swiglu_gemv": (_i32, [_vp, _vp, _i32, _i32, _vp, _i32, _i32, _vp, _i32, _i32, _vp]),
+    "b2_q4_gemv_rmsnorm": (_i32, [_vp, _i32, _i32, _vp, _i32, _i32, _vp, _f32, _vp, _i32, _i32, _vp]),
+    "b2_q8_gemv_rmsnorm": (_i32, [_vp, _i32, _i32, _vp, _i32, _i32, _vp, _f32, _vp, _i32, _i32, _vp]),
+    "b2_q4_swiglu_gemv_rmsnorm": (_i32, [_vp, _vp, _i32, _i32, _vp, _i32, _i32, _vp, _f32, _vp, _i32, _i32, _vp]),
     "b2_gqa_decode_workspace_size": (_i32, [_i32, _i32, _i32, _i32, _i32, _c.POINTER(_c.c_size_t)]),
     "b2_gqa_decode": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _f32,
                              _vp, _i32, _vp, _c.c_size_t, _i32, _vp]),

@@ -127,10 +127,29 @@ int launch_gemv_t(b2::GemvParams p, const DevInfo& di, cudaStream_t stream) {
   const int per_cta_2 = di.smem_per_sm / 2 - di.smem_reserved;
 
   const Tuning& tu = tuning();
-  int cps = 1, S = 1, ktps = p.k_tiles;
+  // Plans, in order of preference.  Chained (weights may stream before the PDL
+  // wait): one CTA per SM in at most half of its shared memory, so the next
+  // kernel's CTAs can be resident alongside and prefetch their weights while
+  // this one runs.  Otherwise: two CTAs per SM if they fit, else one.
+  // The chained plan is used only when every CTA's whole weight slice fits its
+  // ring (complete prefetch); large GEMVs are bandwidth-bound and keep two CTAs/SM.
+  bool chained = false;
+  if (p.prefetch_before_wait && G <= di.sms) {
+    int S1 = std::min(std::min(tu.max_cluster, p.k_tiles), std::max(1, di.sms / G));
+    S1 = std::max(S1, (p.k_tiles + kt_cap - 1) / kt_cap);
+    const int kt1 = (p.k_tiles + S1 - 1) / S1;
+    chained = fixed_bytes(kt1) + kt1 * STAGE <= per_cta_2;
+  }
+  int cps = 1, S = 1, ktps = p.k_tiles, budget = di.smem_optin;
   for (int attempt = 0; attempt < 2; ++attempt) {
-    cps = (attempt == 0 && NB == 1 && tu.ctas_per_sm != 1) ? 2 : 1;
-    if (attempt == 1 && tu.ctas_per_sm == 2 && NB == 1) cps = 2;
+    if (chained) {
+      cps = 1;
+      budget = attempt == 0 ? per_cta_2 : di.smem_optin;
+    } else {
+      cps = (attempt == 0 && NB == 1 && tu.ctas_per_sm != 1) ? 2 : 1;
+      if (attempt == 1 && tu.ctas_per_sm == 2 && NB == 1) cps = 2;
+      budget = cps == 2 ? per_cta_2 : di.smem_optin;
+    }
     const int cap = cps * di.sms;
     S = 1;
     if (G < cap) S = std::min(std::min(tu.max_cluster, p.k_tiles), std::max(1, cap / G));
@@ -138,7 +157,6 @@ int launch_gemv_t(b2::GemvParams p, const DevInfo& di, cudaStream_t stream) {
     S = std::min(S, p.k_tiles);
     ktps = (p.k_tiles + S - 1) / S;
     S = (p.k_tiles + ktps - 1) / ktps;
-    const int budget = cps == 2 ? per_cta_2 : di.smem_optin;
     const int want = std::min(2, ktps);  // at least double-buffered, or the whole slice
     if (fixed_bytes(ktps) + want * STAGE <= budget) break;
   }
@@ -154,7 +172,6 @@ int launch_gemv_t(b2::GemvParams p, const DevInfo& di, cudaStream_t stream) {
   }
   const int groups_per_cta = (G + grid_y - 1) / grid_y;
   const int total_stages = ktps * groups_per_cta;
-  const int budget = cps == 2 ? per_cta_2 : di.smem_optin;
   int stages = std::min(tu.max_stages, (budget - fixed_bytes(ktps)) / STAGE);
   stages = std::min(stages, total_stages);
   if (stages < 1) return fail(B2_ERR_ARG, "K slice too large for shared memory");
@@ -192,10 +209,17 @@ int launch_gemv_t(b2::GemvParams p, const DevInfo& di, cudaStream_t stream) {
 }
 
 int gemv_common(int qt, int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_rows, int k_tiles,
-                const uint16_t* x, int batch, int ldx, void* y, int ldy, int flags, void* stream) {
+                const uint16_t* x, int batch, int ldx, void* y, int ldy, int flags, void* stream,
+                const float* xf = nullptr, const uint16_t* norm_w = nullptr, float eps = 0.f) {
   DevInfo di;
   int st = device_info(&di);
   if (st != B2_OK) return st;
+  if (xf) {  // fused RMSNorm: x is the fp32 residual row, normalised in the prologue
+    if (!norm_w) return fail(B2_ERR_ARG, "null norm weight");
+    if (!aligned(xf, 16) || (ldx % 4) || !aligned(norm_w, 16)) return fail(B2_ERR_ALIGN, "x/norm weight alignment");
+    if (!(eps >= 0.f)) return fail(B2_ERR_ARG, "eps must be >= 0");
+    x = reinterpret_cast<const uint16_t*>(xf);  // satisfies the checks below; the kernel reads xf
+  }
   if (!w0 || !x || !y || (epi == b2::kEpiSwiglu && !w1)) return fail(B2_ERR_ARG, "null pointer argument");
   if (n_tile_rows < 1 || k_tiles < 1) return fail(B2_ERR_ARG, "n_tile_rows=%d k_tiles=%d", n_tile_rows, k_tiles);
   if (batch < 1 || batch > 16) return fail(B2_ERR_ARG, "batch %d outside 1..16", batch);
@@ -220,6 +244,9 @@ int gemv_common(int qt, int epi, const uint8_t* w0, const uint8_t* w1, int n_til
   p.accumulate = (flags & B2_GEMV_ACCUMULATE) ? 1 : 0;
   p.prefetch_before_wait = (flags & B2_GEMV_PREFETCH) ? 1 : 0;
   p.n_groups = epi == b2::kEpiSwiglu ? (n_tile_rows + 1) / 2 : (n_tile_rows + 3) / 4;
+  p.xf = xf;
+  p.norm_w = reinterpret_cast<const __nv_bfloat16*>(norm_w);
+  p.eps = eps;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int nb = batch <= 8 ? 1 : 2;
   if (qt == b2::kQ4 && epi == b2::kEpiF32)
@@ -274,21 +301,35 @@ int dequant_matrix(int qt, const uint8_t* tiles, int n_t, int k_t, float* out, i
 struct AttnPlan {
   int n_splits;
   int split_len;
+  int clustered;  // splits merge through a thread-block cluster (<= 16 CTAs), no workspace
   size_t ws_bytes;
 };
 
+// Context split: enough CTAs to cover the SMs.  When one layer's KV is small
+// (decode-sized, < 64 MB) the splits of a (sequence, kv head) are capped at 16
+// and merged inside a cluster -- one launch; larger contexts take more splits
+// and merge in a second kernel through the caller's workspace.
 AttnPlan attn_plan(int batch, int hq, int hkv, int head_dim, int max_len, int sms) {
   AttnPlan pl;
   const int pairs = batch * hkv;
   const int target = 4 * sms;
   const int max_splits = (max_len + 63) / 64;
+  const double kv_bytes = static_cast<double>(pairs) * max_len * head_dim * 4;
   int S = std::max(1, std::min(max_splits, (target + pairs - 1) / pairs));
+  pl.clustered = 0;
+  if (S > 1 && kv_bytes < 64.0 * (1 << 20)) {
+    S = std::min(S, 16);
+    pl.clustered = 1;
+  }
   int sl = (max_len + S - 1) / S;
   sl = (sl + 63) / 64 * 64;
   S = (max_len + sl - 1) / sl;
   pl.n_splits = S;
   pl.split_len = sl;
-  pl.ws_bytes = S > 1 ? static_cast<size_t>(batch) * hkv * S * (hq / hkv) * (head_dim + 2) * sizeof(float) : 0;
+  if (S == 1) pl.clustered = 0;
+  pl.ws_bytes = (S > 1 && !pl.clustered)
+                    ? static_cast<size_t>(batch) * hkv * S * (hq / hkv) * (head_dim + 2) * sizeof(float)
+                    : 0;
   return pl;
 }
 
@@ -440,20 +481,42 @@ int b2_gqa_decode(const float* q, const float* k_new, const float* v_new, int ld
   p.append = (flags & B2_ATTN_NO_APPEND) ? 0 : 1;
   p.rope = (flags & B2_ATTN_NO_ROPE) ? 0 : 1;
   p.out_f32 = (flags & B2_ATTN_OUT_F32) ? 1 : 0;
+  p.clustered = pl.clustered;
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  static int attr_set[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(b2::gqa_decode_kernel<64>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attention)");
+    attr_set[dev] = 1;
+  }
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (g_pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (pl.clustered) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = pl.n_splits;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.n_splits, n_kv_heads, batch);
   cfg.blockDim = dim3(b2::kAttnThreads, 1, 1);
+  cfg.dynamicSmemBytes = pl.clustered ? pl.n_splits * (n_q_heads / n_kv_heads) * (head_dim + 2) * sizeof(float) : 0;
   cfg.stream = s;
   cfg.attrs = attr;
-  cfg.numAttrs = g_pdl ? 1 : 0;
+  cfg.numAttrs = na;
   cudaError_t e = cudaLaunchKernelEx(&cfg, b2::gqa_decode_kernel<64>, p);
   if (e != cudaSuccess) return cuda_fail(e, "attention launch");
-  if (pl.n_splits > 1) {
+  if (pl.n_splits > 1 && !pl.clustered) {
+    cfg.numAttrs = g_pdl ? 1 : 0;  // the combine kernel is not clustered
     cfg.gridDim = dim3(n_q_heads, batch, 1);
     cfg.blockDim = dim3(64, 1, 1);
     e = cudaLaunchKernelEx(&cfg, b2::gqa_combine_kernel<64>, p);
@@ -507,6 +570,25 @@ int b2_rmsnorm(const void* x, int x_is_f32, int ldx, const uint16_t* w, float ep
                            : cudaLaunchKernelEx(&cfg, b2::rmsnorm_kernel<false>, x, ldx, wb, eps, n, yb, ldy);
   if (e != cudaSuccess) return cuda_fail(e, "rmsnorm launch");
   return B2_OK;
+}
+
+int b2_q4_gemv_rmsnorm(const uint8_t* tiles, int n_tile_rows, int k_tiles, const float* x, int batch, int ldx,
+                       const uint16_t* norm_w, float eps, float* y, int ldy, int flags, void* stream) {
+  return gemv_common(b2::kQ4, b2::kEpiF32, tiles, nullptr, n_tile_rows, k_tiles, nullptr, batch, ldx, y, ldy,
+                     flags, stream, x, norm_w, eps);
+}
+
+int b2_q8_gemv_rmsnorm(const uint8_t* tiles, int n_tile_rows, int k_tiles, const float* x, int batch, int ldx,
+                       const uint16_t* norm_w, float eps, float* y, int ldy, int flags, void* stream) {
+  return gemv_common(b2::kQ8, b2::kEpiF32, tiles, nullptr, n_tile_rows, k_tiles, nullptr, batch, ldx, y, ldy,
+                     flags, stream, x, norm_w, eps);
+}
+
+int b2_q4_swiglu_gemv_rmsnorm(const uint8_t* gate, const uint8_t* up, int n_tile_rows, int k_tiles, const float* x,
+                              int batch, int ldx, const uint16_t* norm_w, float eps, uint16_t* h, int ldh,
+                              int flags, void* stream) {
+  return gemv_common(b2::kQ4, b2::kEpiSwiglu, gate, up, n_tile_rows, k_tiles, nullptr, batch, ldx, h, ldh, flags,
+                     stream, x, norm_w, eps);
 }
 
 int b2_q4_dequant_tiles(const uint8_t* tiles, int64_t n_tiles, uint16_t* out, void* stream) {

@@ -56,6 +56,7 @@ struct AttnParams {
   int append;     // write the new token's k/v into the cache
   int rope;       // rotate the new q/k (0: use them as given)
   int out_f32;    // out is fp32 instead of bf16
+  int clustered;  // splits of one (sequence, kv head) form a cluster and merge in rank 0's smem
 };
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -85,6 +86,7 @@ __device__ __forceinline__ void rope_head_bf16(const float* src, __nv_bfloat16* 
 template <int D>
 __global__ void __launch_bounds__(kAttnThreads) gqa_decode_kernel(const AttnParams p) {
   static_assert(D == 64, "this kernel is written for head_dim 64");
+  extern __shared__ __align__(16) float gather[];  // clustered: [n_splits][grp][D + 2] on rank 0
   constexpr int QW = D / 2 + 4;  // q_s row stride in 32-bit words (bank spread)
   __shared__ __align__(16) uint32_t q_s[16 * QW];        // bf16x2, 16 head rows (rows >= grp zero)
   __shared__ float wm[kAttnWarps][16], wl[kAttnWarps][16];
@@ -242,6 +244,7 @@ __global__ void __launch_bounds__(kAttnThreads) gqa_decode_kernel(const AttnPara
     wo[warp][g][16 * t + 8 + i] = o[i][1];
   }
   __syncthreads();
+  const uint32_t gather_addr = smem_u32(gather);
   for (int e = threadIdx.x; e < grp * D; e += kAttnThreads) {
     const int j = e / D, d = e % D;
     float M = -INFINITY;
@@ -263,6 +266,14 @@ __global__ void __launch_bounds__(kAttnThreads) gqa_decode_kernel(const AttnPara
         reinterpret_cast<float*>(p.out)[oi] = O / L;
       else
         p.out[oi] = __float2bfloat16_rn(O / L);
+    } else if (p.clustered) {
+      // push (o, m, l) into rank 0's gather[split][j]
+      const uint32_t base = gather_addr + ((split * grp + j) * (D + 2)) * 4;
+      st_dsmem_f32(base + d * 4, 0, O);
+      if (d == 0) {
+        st_dsmem_f32(base + D * 4, 0, M);
+        st_dsmem_f32(base + (D + 1) * 4, 0, L);
+      }
     } else {
       float* pr = p.part + ((((static_cast<size_t>(b) * p.hkv + kvh) * p.n_splits + split) * grp + j) * (D + 2));
       pr[d] = O;
@@ -270,6 +281,29 @@ __global__ void __launch_bounds__(kAttnThreads) gqa_decode_kernel(const AttnPara
         pr[D] = M;
         pr[D + 1] = L;
       }
+    }
+  }
+  if (p.clustered) {
+    cluster_arrive_release();
+    if (split != 0) return;  // nothing reads this CTA's shared memory
+    cluster_wait_acquire();
+    for (int e = threadIdx.x; e < grp * D; e += kAttnThreads) {
+      const int j = e / D, d = e % D;
+      float M = -INFINITY;
+      for (int sp = 0; sp < p.n_splits; ++sp) M = fmaxf(M, gather[(sp * grp + j) * (D + 2) + D]);
+      float L = 0.f, O = 0.f;
+      for (int sp = 0; sp < p.n_splits; ++sp) {
+        const float* g = gather + (sp * grp + j) * (D + 2);
+        if (g[D] == -INFINITY) continue;  // split past this sequence's end
+        const float f = exp2f(g[D] - M);
+        L += g[D + 1] * f;
+        O += g[d] * f;
+      }
+      const size_t oi = static_cast<size_t>(b) * p.ldo + (kvh * grp + j) * D + d;
+      if (p.out_f32)
+        reinterpret_cast<float*>(p.out)[oi] = O / L;
+      else
+        p.out[oi] = __float2bfloat16_rn(O / L);
     }
   }
 }

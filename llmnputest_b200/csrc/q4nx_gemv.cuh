@@ -94,6 +94,9 @@ struct GemvParams {
   int stages;
   int x_stride;              // fp16 per shared-memory x row = kt_per_split*256 + 8
   int prefetch_before_wait;  // weights may stream before the PDL wait
+  const float* xf;           // fused RMSNorm: fp32 input rows [batch][ldx] instead of x
+  const __nv_bfloat16* norm_w;  // [K] RMSNorm weight
+  float eps;
 };
 
 // Shared-memory layout (bytes), computed identically on host and device.
@@ -115,6 +118,11 @@ struct GemvSmem {
     total = flag + 16;
   }
 };
+
+__device__ __forceinline__ uint32_t pack_bf16x2_rn(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
 
 __device__ __forceinline__ float absmax8_bf16(uint4 v) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -301,79 +309,90 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
   }
   const int L_cta = kt_cnt * 256;
   {
-    // (1) per-token max |x| over this CTA's K slice (rows are whole multiples of
-    // 32 vectors, so every warp's 32 vectors belong to one token)
-    const int vec_per_row = L_cta / 8;
-    const int total_vec = batch * vec_per_row;
-    constexpr int kVpt = 2;
-    const bool cached = total_vec <= kVpt * kGemvConsumers;
-    uint4 cache[kVpt];
-    auto xvec = [&](int v) {
-      const int b = v / vec_per_row, c = v % vec_per_row;
-      return reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(b) * p.ldx + kt0 * 256)[c];
-    };
-    if (cached) {
-#pragma unroll
-      for (int i = 0; i < kVpt; ++i) {
-        const int v = ctid + i * kGemvConsumers;
-        if (v < total_vec) {
-          cache[i] = xvec(v);
-          const float mx = warp_max(absmax8_bf16(cache[i]));
-          if (lane == 0) atomicMax(&maxbits[v / vec_per_row], __float_as_uint(mx));
+    // x rows as bf16: given (p.x), or bf16(rmsnorm(p.xf) * norm_w) computed here
+    // (the norm fused into the GEMV, granite_rmsnorm.h:45-80 arithmetic).
+    const int vec_per_row = L_cta / 8;  // 16-byte vectors of 8 values, a multiple of 32
+    float* inv_rms = reinterpret_cast<float*>(maxbits);
+    if (p.xf) {
+      const int K = p.k_tiles * 256;
+      for (int b = warp; b < batch; b += kGemvConsumerWarps) {
+        const float4* xr = reinterpret_cast<const float4*>(p.xf + static_cast<size_t>(b) * p.ldx);
+        float ss = 0.f;
+        for (int c = lane; c < K / 4; c += 32) {
+          const float4 v = xr[c];
+          ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
         }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (lane == 0) inv_rms[b] = rsqrtf(ss / static_cast<float>(K) + p.eps);
       }
-    } else {
-      for (int v0 = warp * 32; v0 < total_vec; v0 += kGemvConsumers) {
-        const float mx = warp_max(absmax8_bf16(xvec(v0 + lane)));
-        if (lane == 0) atomicMax(&maxbits[v0 / vec_per_row], __float_as_uint(mx));
-      }
+      named_barrier(1, kGemvConsumers);
     }
-    named_barrier(1, kGemvConsumers);
-    if (ctid < batch) exps[ctid] = gemv_scale_exp(maxbits[ctid]);
-    // (2) x' = fp16(x * 2^e) into shared memory
-    auto put = [&](int v, uint4 in) {
-      const int b = v / vec_per_row, c = v % vec_per_row;
-      const float sc = pow2f(gemv_scale_exp(maxbits[b]));
+    auto xvec = [&](int b, int c) -> uint4 {
+      if (!p.xf) return reinterpret_cast<const uint4*>(p.x + static_cast<size_t>(b) * p.ldx + kt0 * 256)[c];
+      const int k0 = kt0 * 256 + c * 8;
+      const float4 a0 = *reinterpret_cast<const float4*>(p.xf + static_cast<size_t>(b) * p.ldx + k0);
+      const float4 a1 = *reinterpret_cast<const float4*>(p.xf + static_cast<size_t>(b) * p.ldx + k0 + 4);
+      const uint4 wv = *reinterpret_cast<const uint4*>(p.norm_w + k0);
+      const float r = inv_rms[b];
+      auto nb = [&](float xv, float wf) { return xv * r * wf; };
+      uint4 o;
+      o.x = pack_bf16x2_rn(nb(a0.x, bf16lo_to_f32(wv.x)), nb(a0.y, bf16hi_to_f32(wv.x)));
+      o.y = pack_bf16x2_rn(nb(a0.z, bf16lo_to_f32(wv.y)), nb(a0.w, bf16hi_to_f32(wv.y)));
+      o.z = pack_bf16x2_rn(nb(a1.x, bf16lo_to_f32(wv.z)), nb(a1.y, bf16hi_to_f32(wv.z)));
+      o.w = pack_bf16x2_rn(nb(a1.z, bf16lo_to_f32(wv.w)), nb(a1.w, bf16hi_to_f32(wv.w)));
+      return o;
+    };
+    // x' = fp16(x * 2^e) for this warp's K-tiles and the per-32-k sums of x'
+    auto put = [&](int b, int c, uint4 in, float sc) {
       const uint32_t w[4] = {in.x, in.y, in.z, in.w};
       uint32_t o[4];
+      float s8 = 0.f;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const __half2 hv = __floats2half2_rn(bf16lo_to_f32(w[i]) * sc, bf16hi_to_f32(w[i]) * sc);
         o[i] = *reinterpret_cast<const uint32_t*>(&hv);
+        const float2 f = __half22float2(hv);
+        s8 += f.x;
+        s8 += f.y;
       }
       *reinterpret_cast<uint4*>(x_s + b * p.x_stride + c * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+      s8 += __shfl_xor_sync(0xffffffffu, s8, 1);
+      s8 += __shfl_xor_sync(0xffffffffu, s8, 2);
+      if ((lane & 3) == 0) xs_s[(c >> 2) * 8 * NB + b] = s8;
     };
-    if (cached) {
+    constexpr int kVecLane = 8;  // a slice of up to 8 K-tiles is held in registers
+    for (int b = 0; b < batch; ++b) {
+      if (vec_per_row <= 32 * kVecLane) {
+        // one pass: every warp loads the whole slice (one L2 round trip), finds the
+        // max itself (no barrier), and converts its own K-tiles from registers
+        uint4 v[kVecLane];
+        float mx = 0.f;
 #pragma unroll
-      for (int i = 0; i < kVpt; ++i) {
-        const int v = ctid + i * kGemvConsumers;
-        if (v < total_vec) put(v, cache[i]);
-      }
-    } else {
-      for (int v = ctid; v < total_vec; v += kGemvConsumers) put(v, xvec(v));
-    }
-    named_barrier(1, kGemvConsumers);
-    // (3) per-32-k-block sums of x' (fp32), [kb_local][8*NB], zero for b >= batch
-    const int nsum = kt_cnt * 8 * 8 * NB;
-    for (int v = ctid; v < nsum; v += kGemvConsumers) {
-      const int kbl = v / (8 * NB), b = v % (8 * NB);
-      float acc = 0.f;
-      if (b < batch) {
-        const uint4* xr = reinterpret_cast<const uint4*>(x_s + b * p.x_stride + kbl * 32);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint4 q = xr[j];
-          const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-            acc += f.x;
-            acc += f.y;
+        for (int i = 0; i < kVecLane; ++i)
+          if (32 * i < vec_per_row) {
+            v[i] = xvec(b, lane + 32 * i);
+            mx = fmaxf(mx, absmax8_bf16(v[i]));
           }
-        }
+        mx = warp_max(mx);
+        const int e = gemv_scale_exp(__float_as_uint(mx));
+        const float sc = pow2f(e);
+        if (warp == 0 && lane == 0) exps[b] = e;
+#pragma unroll
+        for (int i = 0; i < kVecLane; ++i)
+          if (32 * i < vec_per_row && (i % kGemvConsumerWarps) == warp) put(b, lane + 32 * i, v[i], sc);
+      } else {
+        float mx = 0.f;
+        for (int c = lane; c < vec_per_row; c += 32) mx = fmaxf(mx, absmax8_bf16(xvec(b, c)));
+        mx = warp_max(mx);
+        const int e = gemv_scale_exp(__float_as_uint(mx));
+        const float sc = pow2f(e);
+        if (warp == 0 && lane == 0) exps[b] = e;
+        for (int c = warp * 32 + lane; c < vec_per_row; c += kGemvConsumers) put(b, c, xvec(b, c), sc);
       }
-      xs_s[v] = acc;
     }
+    for (int v = ctid; v < kt_cnt * 8 * 8 * NB; v += kGemvConsumers)
+      if (v % (8 * NB) >= batch) xs_s[v] = 0.f;
     named_barrier(1, kGemvConsumers);
   }
 

@@ -3,15 +3,16 @@
 Per layer, in the order of designs/granite_gemv/granite_layer.py:54-59 (one GEMV
 per group of projections that share an input):
 
-    xn   = rmsnorm(resid, attn_norm)                     b2_rmsnorm (fp32 in, bf16 out)
-    qkv  = W_qkv xn                                      b2_q4_gemv (q|k|v rows concatenated)
+    qkv  = W_qkv bf16(rmsnorm(resid, attn_norm))         b2_q4_gemv_rmsnorm (q|k|v rows concatenated,
+                                                         the norm fused into the GEMV prologue)
     attn = attention(rope(q), rope(k) -> cache, v -> cache)   b2_gqa_decode
     resid += W_o attn                                    b2_q4_gemv, accumulate
-    xn   = rmsnorm(resid, mlp_norm)
-    h    = silu(W_gate xn) * (W_up xn)                   b2_q4_swiglu_gemv (fused)
+    h    = silu(W_gate xn) * (W_up xn),
+           xn = bf16(rmsnorm(resid, mlp_norm))           b2_q4_swiglu_gemv_rmsnorm (norm + gate/up + SiLU*up)
     resid += W_down h                                    b2_q4_gemv, accumulate
 
-then rmsnorm(final) and the q8 lm_head (b2_q8_gemv).  The residual stream is
+then the final norm fused into the q8 lm_head (b2_q8_gemv_rmsnorm): five
+launches per layer.  The residual stream is
 fp32; GEMV inputs are bf16 as in the reference.  Weights are the raw q4nx tiles,
 resident on the device; the step is captured in one CUDA graph.
 
@@ -141,18 +142,18 @@ class Q4Decoder:
         kd = c.n_kv_heads * d
         self.resid.copy_(self.x_in)
         for li, L in enumerate(self.w["layers"]):
-            ops.rmsnorm(self.resid, L["attn_norm"], c.rms_eps, out=self.xn)
-            ops.q4_gemv(L["qkv"], self.nt_qkv, self.kt_h, self.xn, out=self.qkv, prefetch=prefetch)
+            ops.gemv_rmsnorm(L["qkv"], self.nt_qkv, self.kt_h, self.resid, L["attn_norm"], c.rms_eps, out=self.qkv,
+                             prefetch=prefetch)
             ops.gqa_decode(self.qkv[:, :qd], self.qkv[:, qd:qd + kd], self.qkv[:, qd + kd:],
                            self.k_cache[li], self.v_cache[li], self.pos, n_q_heads=c.n_heads,
                            n_kv_heads=c.n_kv_heads, theta=c.rope_theta, scale=d ** -0.5, max_len=self.ctx_max,
                            out=self.attn, workspace=self.attn_ws)
             ops.q4_gemv(L["o"], self.nt_h, self.kt_q, self.attn, out=self.resid, accumulate=True, prefetch=prefetch)
-            ops.rmsnorm(self.resid, L["mlp_norm"], c.rms_eps, out=self.xn)
-            ops.q4_swiglu_gemv(L["gate"], L["up"], self.nt_i, self.kt_h, self.xn, out=self.h, prefetch=prefetch)
+            ops.swiglu_gemv_rmsnorm(L["gate"], L["up"], self.nt_i, self.kt_h, self.resid, L["mlp_norm"], c.rms_eps,
+                                    out=self.h, prefetch=prefetch)
             ops.q4_gemv(L["down"], self.nt_h, self.kt_i, self.h, out=self.resid, accumulate=True, prefetch=prefetch)
-        ops.rmsnorm(self.resid, self.w["final_norm"], c.rms_eps, out=self.xn)
-        ops.q8_gemv(self.w["lm_head"], self.nt_v, self.kt_h, self.xn, out=self.logits, prefetch=prefetch)
+        ops.gemv_rmsnorm(self.w["lm_head"], self.nt_v, self.kt_h, self.resid, self.w["final_norm"], c.rms_eps,
+                         out=self.logits, prefetch=prefetch, q8=True)
         return self.logits
 
     def capture(self) -> torch.cuda.CUDAGraph:

@@ -109,6 +109,60 @@ def q4_swiglu_gemv(gate: torch.Tensor, up: torch.Tensor, n_tile_rows: int, k_til
     return out if x.dim() == 2 else out[0, :n]
 
 
+def _norm_in(x: torch.Tensor, w: torch.Tensor, k: int) -> torch.Tensor:
+    _need(x, "x", torch.float32)
+    _need(w, "norm_w", torch.bfloat16)
+    x2 = x.reshape(1, -1) if x.dim() == 1 else x
+    if x2.dim() != 2 or x2.shape[1] != k or w.numel() != k:
+        raise ValueError(f"x must be [B, {k}] fp32 and norm_w [{k}]")
+    if x2.stride(1) != 1 or x2.stride(0) % 4 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    if not w.is_contiguous() or w.data_ptr() % 16:
+        raise ValueError("norm_w must be contiguous and 16-byte aligned")
+    return x2
+
+
+def gemv_rmsnorm(tiles: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tensor, norm_w: torch.Tensor,
+                 eps: float, out: torch.Tensor | None = None, accumulate: bool = False, prefetch: bool = False,
+                 q8: bool = False) -> torch.Tensor:
+    """fp32 y = W bf16(rmsnorm(x) * norm_w) in one kernel; x fp32 [B, K] (e.g. the residual stream)."""
+    tb = Q8_TILE_BYTES if q8 else Q4_TILE_BYTES
+    _tiles(tiles, n_tile_rows, k_tiles, tb, "tiles")
+    k, n = k_tiles * TILE_K, n_tile_rows * TILE_ROWS
+    x2 = _norm_in(x, norm_w, k)
+    b = x2.shape[0]
+    if out is None:
+        out = torch.empty((b, n), dtype=torch.float32, device=x2.device)
+    _need(out, "out", torch.float32)
+    flags = (GEMV_ACCUMULATE if accumulate else 0) | (GEMV_PREFETCH if prefetch else 0)
+    name = "b2_q8_gemv_rmsnorm" if q8 else "b2_q4_gemv_rmsnorm"
+    for b0 in range(0, b, 16):
+        bb = min(16, b - b0)
+        _native.call(name, _ptr(tiles), n_tile_rows, k_tiles, ctypes.c_void_p(x2[b0].data_ptr()), bb, x2.stride(0),
+                     _ptr(norm_w), float(eps), ctypes.c_void_p(out[b0].data_ptr()), out.stride(0), flags, _stream())
+    return out if x.dim() == 2 else out[0, :n]
+
+
+def swiglu_gemv_rmsnorm(gate: torch.Tensor, up: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tensor,
+                        norm_w: torch.Tensor, eps: float, out: torch.Tensor | None = None,
+                        prefetch: bool = False) -> torch.Tensor:
+    """bf16 h = silu(G xn) * (U xn) with xn = bf16(rmsnorm(x) * norm_w), one kernel."""
+    _tiles(gate, n_tile_rows, k_tiles, Q4_TILE_BYTES, "gate")
+    _tiles(up, n_tile_rows, k_tiles, Q4_TILE_BYTES, "up")
+    k, n = k_tiles * TILE_K, n_tile_rows * TILE_ROWS
+    x2 = _norm_in(x, norm_w, k)
+    b = x2.shape[0]
+    if out is None:
+        out = torch.empty((b, n), dtype=torch.bfloat16, device=x2.device)
+    _need(out, "out", torch.bfloat16)
+    for b0 in range(0, b, 16):
+        bb = min(16, b - b0)
+        _native.call("b2_q4_swiglu_gemv_rmsnorm", _ptr(gate), _ptr(up), n_tile_rows, k_tiles,
+                     ctypes.c_void_p(x2[b0].data_ptr()), bb, x2.stride(0), _ptr(norm_w), float(eps),
+                     ctypes.c_void_p(out[b0].data_ptr()), out.stride(0), GEMV_PREFETCH if prefetch else 0, _stream())
+    return out if x.dim() == 2 else out[0, :n]
+
+
 def dequant_tiles(tiles: torch.Tensor, q8: bool = False) -> torch.Tensor:
     """[T, tile] uint8 -> [T, 8192] bf16 in weight-index order (bit-exact decode)."""
     tb = Q8_TILE_BYTES if q8 else Q4_TILE_BYTES

@@ -175,8 +175,8 @@ class TPDecoder:
         qd, kd = p.q_local * d, p.kv_local * d
         self.resid.copy_(self.x_in)
         for li, L in enumerate(self.w["layers"]):
-            ops.rmsnorm(self.resid, L["attn_norm"], c.rms_eps, out=self.xn)
-            ops.q4_gemv(L["qkv"], self.nt_qkv_local, self.kt_h, self.xn, out=self.qkv, prefetch=True)
+            ops.gemv_rmsnorm(L["qkv"], self.nt_qkv_local, self.kt_h, self.resid, L["attn_norm"], c.rms_eps,
+                             out=self.qkv, prefetch=True)
             ops.gqa_decode(self.qkv[:, :qd], self.qkv[:, qd:qd + kd], self.qkv[:, qd + kd:], self.k_cache[li],
                            self.v_cache[li], self.pos, n_q_heads=p.q_local, n_kv_heads=p.kv_local,
                            theta=c.rope_theta, scale=d ** -0.5, max_len=self.ctx_max, out=self.attn_local,
@@ -194,14 +194,14 @@ class TPDecoder:
                 self.resid.view(self.batch, W, -1).add_(self.o_all.view(W, self.batch, -1).permute(1, 0, 2))
             else:
                 self.resid.add_(self.o_local)
-            ops.rmsnorm(self.resid, L["mlp_norm"], c.rms_eps, out=self.xn)
-            ops.q4_swiglu_gemv(L["gate"], L["up"], self.nt_i_local, self.kt_h, self.xn, out=self.h, prefetch=True)
+            ops.swiglu_gemv_rmsnorm(L["gate"], L["up"], self.nt_i_local, self.kt_h, self.resid, L["mlp_norm"],
+                                    c.rms_eps, out=self.h, prefetch=True)
             ops.q4_gemv(L["down"], c.hidden // TILE_ROWS, self.kt_i_local, self.h, out=self.down, prefetch=True)
             if W > 1:
                 dist.all_reduce(self.down)
             self.resid.add_(self.down)
-        ops.rmsnorm(self.resid, self.w["final_norm"], c.rms_eps, out=self.xn)
-        ops.q8_gemv(self.w["lm_head"], self.nt_v_local, self.kt_h, self.xn, out=self.logits_local, prefetch=True)
+        ops.gemv_rmsnorm(self.w["lm_head"], self.nt_v_local, self.kt_h, self.resid, self.w["final_norm"], c.rms_eps,
+                         out=self.logits_local, prefetch=True, q8=True)
         if W > 1:
             dist.all_gather_into_tensor(self.logits_all, self.logits_local)
             self.logits.view(self.batch, W, -1).copy_(self.logits_all.view(W, self.batch, -1).permute(1, 0, 2))

@@ -184,3 +184,47 @@ def test_argument_errors(ops):
 def test_no_device_error(ops):
     torch.cuda.synchronize()
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("q8,n_t,k_t,batch", [(False, 112, 10, 1), (False, 80, 32, 3), (True, 130, 10, 2)])
+def test_gemv_fused_rmsnorm(ops, q8, n_t, k_t, batch):
+    """GEMV with RMSNorm fused into its input == rmsnorm (bf16 out) then the GEMV."""
+    rng = np.random.default_rng(40 + n_t)
+    w = (orc.synth_q8_tiles if q8 else orc.synth_q4_tiles)(rng, n_t * k_t)
+    x = (rng.standard_normal((batch, k_t * 256)) * 4).astype(np.float32)
+    nw = (rng.standard_normal(k_t * 256) * 0.1 + 1).astype(np.float32).astype(bfloat16)
+    y = ops.gemv_rmsnorm(dev_u8(w), n_t, k_t, torch.from_numpy(x).cuda(), dev_bf16(nw.astype(np.float32)), 1e-6,
+                         q8=q8).cpu().numpy()
+    xn = orc.rmsnorm(x, nw, 1e-6).astype(np.float32).astype(bfloat16)
+    ref = (orc.gemv_q8 if q8 else orc.gemv_q4)(w, xn, n_t, k_t)
+    for b in range(batch):
+        # the fused norm rounds x*inv*w in fp32 rather than fp64: a few bf16 inputs differ by 1 ulp
+        assert_close(y[b], ref[b], NS_COS, NS_REL, f"token {b}")
+
+
+def test_swiglu_fused_rmsnorm(ops):
+    rng = np.random.default_rng(71)
+    n_t, k_t = 256, 10
+    g = orc.synth_q4_tiles(rng, n_t * k_t)
+    u = orc.synth_q4_tiles(rng, n_t * k_t)
+    x = (rng.standard_normal((2, k_t * 256)) * 3).astype(np.float32)
+    nw = (rng.standard_normal(k_t * 256) * 0.1 + 1).astype(np.float32).astype(bfloat16)
+    h = ops.swiglu_gemv_rmsnorm(dev_u8(g), dev_u8(u), n_t, k_t, torch.from_numpy(x).cuda(),
+                                dev_bf16(nw.astype(np.float32)), 1e-6).float().cpu().numpy()
+    xn = orc.rmsnorm(x, nw, 1e-6).astype(np.float32).astype(bfloat16)
+    for b in range(2):
+        ref = orc.swiglu_from_accumulators(orc.gemv_q4(g, xn[b], n_t, k_t), orc.gemv_q4(u, xn[b], n_t, k_t))
+        assert_close(h[b], ref, NS_COS, 4e-3, f"token {b}")
+
+
+@pytest.mark.parametrize("shape", ["qkv", "down", "gate_up"])
+def test_chained_prefetch_plan(ops, shape):
+    """The prefetch (chained) launch plan gives the same results as the default plan."""
+    n_t, k_t = SHAPES[shape]
+    rng = np.random.default_rng(7)
+    w = dev_u8(orc.synth_q4_tiles(rng, n_t * k_t))
+    x = dev_bf16(orc.synth_bf16(rng, (2, k_t * 256)).astype(np.float32))
+    a = ops.q4_gemv(w, n_t, k_t, x).cpu().numpy()
+    b = ops.q4_gemv(w, n_t, k_t, x, prefetch=True).cpu().numpy()
+    for i in range(2):
+        assert_close(b[i], a[i], REF_COS, REF_REL, f"token {i}")

@@ -61,6 +61,14 @@ class OracleOps:
         out.copy_(_bf(h))
         return out
 
+    def gemv_rmsnorm(self, tiles, n_t, k_t, x, norm_w, eps, out=None, accumulate=False, prefetch=False, q8=False):
+        xn = _bf(orc.rmsnorm(self._x(x), norm_w.float().numpy(), eps))
+        return (self.q8_gemv if q8 else self.q4_gemv)(tiles, n_t, k_t, xn, out=out, accumulate=accumulate)
+
+    def swiglu_gemv_rmsnorm(self, gate, up, n_t, k_t, x, norm_w, eps, out=None, prefetch=False):
+        xn = _bf(orc.rmsnorm(self._x(x), norm_w.float().numpy(), eps))
+        return self.q4_swiglu_gemv(gate, up, n_t, k_t, xn, out=out)
+
     def rmsnorm(self, x, w, eps, out=None):
         out.copy_(_bf(orc.rmsnorm(self._x(x), w.float().numpy(), eps)))
         return out

@@ -68,7 +68,8 @@ def _with_workspace(qkv, kc, vc, pos, hq, hkv, max_len):
 
 def test_static_scratch_matches_workspace_entry_point(lib):
     from llmnputest_b200 import ops
-    cases = [(2, 40, 8, 4096, [4096, 1000], 11), (1, 40, 8, 2048, [1500], 12)]
+    # contexts large enough that the split partials go through scratch (small ones merge in a cluster)
+    cases = [(2, 40, 8, 32768, [32768, 20000], 11), (3, 40, 8, 32768, [32768, 100, 5000], 12)]
     for bsz, hq, hkv, ctx, lens, seed in cases:  # two calls in a row through the shared scratch
         assert ops.gqa_decode_workspace_bytes(bsz, hq, hkv, 64, max(lens)) > 0  # the scratch is really used
         qkv, kc, vc, pos = _case(bsz, hq, hkv, ctx, lens, seed)
