@@ -281,6 +281,45 @@ def measure_decode(torch, world: int, rank: int, batch: int, ctx: int, steps: in
     return out
 
 
+def measure_attention(torch, ops, gen, device, hbm_peak: float, steps: int) -> list:
+    """Config 3: GQA flash-decode (40/8 heads, D 64, RoPE fused, new k/v appended at pos = ctx-1).
+
+    Algorithmic bytes per call: B*ctx*8*64*2*2 (the bf16 K and V read once).  Each graph
+    replay rotates over a pool of caches whose total is above L2, so every call reads HBM.
+    """
+    hq, hkv, d = 40, 8, 64
+    out = []
+    for ctx in (512, 4096, 32768):
+        for bsz in (1, 16, 64):
+            kv_bytes = bsz * ctx * hkv * d * 2 * 2
+            n_pool = max(1, min(512, -(-300_000_000 // kv_bytes)))
+            pool = []
+            for _ in range(n_pool):
+                kc = torch.randn(bsz, hkv, ctx, d, device=device, generator=gen).to(torch.bfloat16)
+                vc = torch.randn(bsz, hkv, ctx, d, device=device, generator=gen).to(torch.bfloat16)
+                pool.append((kc, vc))
+            qkv = torch.randn(bsz, (hq + 2 * hkv) * d, device=device, generator=gen)
+            pos = torch.full((bsz,), ctx - 1, dtype=torch.int32, device=device)
+            o = torch.empty(bsz, hq * d, dtype=torch.bfloat16, device=device)
+            ws = torch.empty(max(1, ops.gqa_decode_workspace_bytes(bsz, hq, hkv, d, ctx)), dtype=torch.uint8,
+                             device=device)
+
+            def calls(pool=pool, qkv=qkv, pos=pos, o=o, ws=ws, ctx=ctx):
+                for kc, vc in pool:
+                    ops.gqa_decode(qkv[:, :hq * d], qkv[:, hq * d:(hq + hkv) * d], qkv[:, (hq + hkv) * d:], kc, vc,
+                                   pos, n_q_heads=hq, n_kv_heads=hkv, max_len=ctx, out=o, workspace=ws)
+
+            g = graph_of(torch, calls)
+            reps = max(3, min(200, int(steps * 2e6 / (kv_bytes * n_pool) + 1)))
+            t_ms = time_graph(torch, g, reps, 3) / n_pool
+            gbs = kv_bytes / (t_ms * 1e-3) / 1e9
+            out.append({"batch": bsz, "ctx": ctx, "us": round(t_ms * 1e3, 2), "gbs": round(gbs, 1),
+                        "frac_of_measured_hbm": round(gbs / hbm_peak, 3), "pool": n_pool})
+            del g, pool, ws
+            torch.cuda.empty_cache()
+    return out
+
+
 def run_b200(args, rank: int, world: int) -> dict | None:
     import torch
     import torch.distributed as dist
@@ -350,6 +389,7 @@ def run_b200(args, rank: int, world: int) -> dict | None:
         extras["q8_lm_head"] = {"us": round(tl * 1e3, 2), "gbs": round(w8.numel() / (tl * 1e-3) / 1e9, 1),
                                 "frac_of_measured_hbm": round(w8.numel() / (tl * 1e-3) / 1e9 / pk["hbm_gbs"], 3)}
         del gl, w8
+        extras["attention"] = measure_attention(torch, ops, gen, device, pk["hbm_gbs"], args.steps)
 
     # ---- config 4: the full decode step (tensor-parallel across the ranks when N > 1)
     if not args.quick:

@@ -36,6 +36,12 @@ SIGNATURES: dict[str, tuple] = {
     "b2_gqa_decode_static": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _f32,
                                     _f32, _vp, _i32, _i32, _vp]),
     "b2_rmsnorm": (_i32, [_vp, _i32, _i32, _vp, _f32, _i32, _i32, _vp, _i32, _vp]),
+    "b2_phase_struct_bytes": (_c.c_size_t, []),
+    "b2_program_attention_plan": (_i32, [_i32, _i32, _i32, _i32, _i32, _c.POINTER(_i32), _c.POINTER(_i32),
+                                         _c.POINTER(_c.c_size_t)]),
+    "b2_program_scratch_size": (_i32, [_i32, _c.POINTER(_c.c_size_t)]),
+    "b2_program_upload": (_i32, [_vp, _i32, _i32, _vp, _c.c_size_t, _vp]),
+    "b2_program_launch": (_i32, [_vp, _i32, _i32, _vp, _f32, _vp, _c.c_size_t, _vp]),
     "b2_q4_dequant_tiles": (_i32, [_vp, _i64, _vp, _vp]),
     "b2_q8_dequant_tiles": (_i32, [_vp, _i64, _vp, _vp]),
     "b2_q4_dequant_matrix": (_i32, [_vp, _i32, _i32, _vp, _i64, _vp]),
@@ -56,7 +62,7 @@ class B2Error(RuntimeError):
 def header_symbols() -> list[str]:
     """Every function the public header declares."""
     text = HEADER.read_text()
-    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(b2_\w+)\s*\(", text, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|size_t|const char\*)\s+(b2_\w+)\s*\(", text, re.M)))
 
 
 def lib() -> ctypes.CDLL:
