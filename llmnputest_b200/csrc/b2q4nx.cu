@@ -748,6 +748,10 @@ int b2_program_launch(const void* dev_phases, int n_phases, int batch, const int
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaMemsetAsync(scratch, 0, 16, s);
   if (e != cudaSuccess) return cuda_fail(e, "clearing the program barrier");
+  float* rope = reinterpret_cast<float*>(static_cast<char*>(scratch) + kProgRopeOffset);
+  b2::prog_rope_kernel<<<batch, 32, 0, s>>>(pos, theta, rope);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "RoPE table launch");
   b2::ProgParams p = {};
   p.phases = static_cast<const b2::ProgPhase*>(dev_phases);
   p.n_phases = n_phases;
@@ -755,7 +759,7 @@ int b2_program_launch(const void* dev_phases, int n_phases, int batch, const int
   p.stages = stages;
   p.theta = theta;
   p.pos = pos;
-  p.rope = reinterpret_cast<float*>(static_cast<char*>(scratch) + kProgRopeOffset);
+  p.rope = rope;
   p.barrier = static_cast<unsigned int*>(scratch);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;

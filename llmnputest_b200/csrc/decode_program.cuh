@@ -11,9 +11,9 @@
 // the phase boundaries.
 //
 // A step of the dense GQA decoder (designs/granite_gemv/granite_layer.py:54-59):
-//   prep    resid = x_in; zero the first split-K targets; RoPE table cos/sin
-//           per sequence (fp64 angles, rounded to fp32 as in the one-shot
-//           attention kernel); barrier
+//   (a small kernel before the launch: RoPE cos/sin per sequence, fp64 angles
+//   rounded to fp32 as in the one-shot attention kernel)
+//   prep    resid = x_in; zero the first split-K targets; barrier
 //   per layer
 //     GEMV  qkv[l&1] += W_qkv bf16(rmsnorm(resid))           barrier
 //     ATTN  rope(q), rope(k) -> cache, v -> cache; split partials (o, m, l)
@@ -33,7 +33,8 @@
 // operands: codes 0..15 and the bf16 x are both exact in bf16, so x needs no
 // per-row rescaling), the same q4_1 factoring, RMSNorm, SwiGLU, RoPE and online
 // softmax (q4nx_gemv.cuh, gqa_decode.cuh); only fp32 summation order differs.
-// Consumers: 16 warps, one (row-block, 32-k block) of each stage per warp; a
+// Consumers: 12 warps.  Batch >= 2: 8 of them split each stage by (row-block,
+// pair of 32-k blocks).  Batch 1: a different split (prog_gemv_phase_b1).  A
 // unit's warp sums meet in shared memory and leave as one fp32 reduction per
 // output at L2.
 //
@@ -58,7 +59,10 @@ namespace b2 {
 enum ProgKind : int { kPhGemv = 0, kPhAttn = 1, kPhPrep = 2 };
 enum ProgXSrc : int { kXBf16 = 0, kXNorm = 1, kXAttn = 2, kXSwiglu = 3 };
 
-constexpr int kProgWarps = 16;  // consumer warps: (row-block, 32-k block) of a stage each
+// Consumer warps.  13 warps per CTA (with the producer) are budgeted as 16 by the
+// register allocator, so each thread may hold 128 registers.
+constexpr int kProgWarps = 12;
+constexpr int kNbWarps = 8;  // batch >= 2: warps (row-block, pair of 32-k blocks) of a stage
 constexpr int kProgConsumers = kProgWarps * 32;
 constexpr int kProgThreads = kProgConsumers + 32;
 constexpr int kProgMaxBatch = 8;
@@ -104,7 +108,7 @@ struct ProgParams {
   int stages;
   float theta;
   const int* pos;         // [batch] position of the new token
-  float* rope;            // [batch][32][2] cos, sin (written by the prep phase)
+  float* rope;            // [batch][32][2] cos, sin (written by prog_rope_kernel)
   unsigned int* barrier;  // [0] arrivals, [1] abort word; zeroed before the launch
 };
 
@@ -123,7 +127,7 @@ struct ProgSmem {
     xs_slot = prog_unit_kt(batch) * 8 * 8 * 4;
     red = xs + 2 * xs_slot;  // warp partial sums [warp][64 rows][ncol]
     misc = red + kProgWarps * 64 * ncol * 4;
-    const int gemv_end = misc + kProgMaxBatch * 4;
+    const int gemv_end = misc + (kProgMaxBatch + kProgMaxBatch * kProgWarps) * 4;
     const int attn_end = work + kProgAttnBytes;
     bar = ((gemv_end > attn_end ? gemv_end : attn_end) + 15) & ~15;
     flag = bar + 2 * stages * 8;  // [0] abort flag, [1] grid-barrier verdict
@@ -247,21 +251,41 @@ __device__ __forceinline__ uint4 prog_x_vec(const ProgPhase& P, int b, int K0, i
       const float* base = P.part +
                           ((static_cast<size_t>(b) * P.n_kv_heads + kvh) * P.n_splits * grp + j) * kPartStride;
       const size_t stride = static_cast<size_t>(grp) * kPartStride;
+      // splits in groups of 8: all loads of a group are issued before any is used
       float M = -INFINITY;
-#pragma unroll 8
-      for (int s = 0; s < P.n_splits; ++s) M = fmaxf(M, base[s * stride + 64]);
+      for (int s0 = 0; s0 < P.n_splits; s0 += 8) {
+        float mv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mv[i] = s0 + i < P.n_splits ? base[(s0 + i) * stride + 64] : -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) M = fmaxf(M, mv[i]);
+      }
       float Lsum = 0.f, O[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-      for (int s = 0; s < P.n_splits; ++s) {
-        const float* ps = base + s * stride;
-        const float2 ml = *reinterpret_cast<const float2*>(ps + 64);
-        const float f = ml.x == -INFINITY ? 0.f : exp2f(ml.x - M);  // a split past the sequence end adds 0
-        Lsum += ml.y * f;
+      for (int s0 = 0; s0 < P.n_splits; s0 += 4) {
+        float2 ml[4];
+        float4 ov[4][2];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const float2 v = *reinterpret_cast<const float2*>(ps + d0 + 2 * i);
-          O[2 * i] += v.x * f;
-          O[2 * i + 1] += v.y * f;
+          const float* ps = base + min(s0 + i, P.n_splits - 1) * stride;
+          ml[i] = *reinterpret_cast<const float2*>(ps + 64);
+          const float2 a = *reinterpret_cast<const float2*>(ps + d0), b2 = *reinterpret_cast<const float2*>(ps + d0 + 2);
+          const float2 c = *reinterpret_cast<const float2*>(ps + d0 + 4), e = *reinterpret_cast<const float2*>(ps + d0 + 6);
+          ov[i][0] = make_float4(a.x, a.y, b2.x, b2.y);
+          ov[i][1] = make_float4(c.x, c.y, e.x, e.y);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          // a split past the sequence end (m = -inf), or past n_splits, adds 0
+          const float f = (s0 + i >= P.n_splits || ml[i].x == -INFINITY) ? 0.f : exp2f(ml[i].x - M);
+          Lsum += ml[i].y * f;
+          O[0] += ov[i][0].x * f;
+          O[1] += ov[i][0].y * f;
+          O[2] += ov[i][0].z * f;
+          O[3] += ov[i][0].w * f;
+          O[4] += ov[i][1].x * f;
+          O[5] += ov[i][1].y * f;
+          O[6] += ov[i][1].z * f;
+          O[7] += ov[i][1].w * f;
         }
       }
       uint32_t o[4];
@@ -308,19 +332,29 @@ __device__ __forceinline__ void prog_stage_x(const ProgPhase& P, int batch, int 
   const int nvec = (kb - ka) * 32;  // 16-byte vectors per row, a multiple of 32 (warp-uniform tests)
   const int K0 = ka * 256;
 
-  if (P.x_source == kXNorm && first_unit) {  // 1/rms of whole rows: once per phase (kept in misc)
+  if (P.x_source == kXNorm && first_unit) {
+    // 1/rms of whole rows, once per phase (kept in misc): every thread sums a few
+    // float4 of each row (one L2 round trip), warps reduce, then one thread per row
+    float* wss = inv_rms + kProgMaxBatch;  // [batch][kProgWarps]
     const int K = P.k_tiles * 256;
-    for (int b = warp; b < batch; b += kProgWarps) {
+    for (int b = 0; b < batch; ++b) {
       const float4* xr = reinterpret_cast<const float4*>(static_cast<const float*>(P.x) + static_cast<size_t>(b) * P.ldx);
       float ss = 0.f;
-#pragma unroll 4
-      for (int q = lane; q < K / 4; q += 32) {
+#pragma unroll 2
+      for (int q = ctid; q < K / 4; q += kProgConsumers) {
         const float4 v = xr[q];
         ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      if (lane == 0) inv_rms[b] = rsqrtf(ss / static_cast<float>(K) + P.eps);
+      if (lane == 0) wss[b * kProgWarps + warp] = ss;
+    }
+    named_barrier(1, kProgConsumers);
+    if (ctid < batch) {
+      float ss = 0.f;
+#pragma unroll
+      for (int w = 0; w < kProgWarps; ++w) ss += wss[ctid * kProgWarps + w];
+      inv_rms[ctid] = rsqrtf(ss / static_cast<float>(K) + P.eps);
     }
     named_barrier(1, kProgConsumers);
   }
@@ -346,11 +380,13 @@ __device__ __forceinline__ void prog_gemv_phase(const ProgParams& p, const ProgP
   const int xw_stride = prog_x_stride(batch) / 2;
   float* red = reinterpret_cast<float*>(smem + L.red);
 
-  // warp = (row-block rb, 32-k block kblk); lane (g, t): tile g&3, rows h*8.. of the
-  // row-block, k pairs {2t, 2t+1} and {2t+8, 2t+9} of each 16-k MMA step
+  // warps 0-7 = (row-block rb, 32-k blocks 2kp and 2kp+1); lane (g, t): tile g&3,
+  // rows h*8.. of the row-block, k pairs {2t, 2t+1} and {2t+8, 2t+9} of each
+  // 16-k MMA step.  Warps 8-11 only stage x.
   const int g = lane >> 2, t = lane & 3;
   const int tile = g & 3, h = g >> 2, odd = tile & 1;
-  const int rb = warp & 1, kblk = warp >> 1;
+  const int rb = warp & 1, kp = (warp >> 1) & 3;
+  const bool mma_warp = warp < kNbWarps;
   const uint32_t sel_lo = odd ? 0x1054u : 0x5410u;
   const uint32_t sel_hi = odd ? 0x3276u : 0x7632u;
   const int off_first = odd ? 8 : 0, off_second = odd ? 0 : 8;
@@ -369,54 +405,60 @@ __device__ __forceinline__ void prog_gemv_phase(const ProgParams& p, const ProgP
 #pragma unroll
     for (int s = 0; s < 4; ++s) tot[s][0] = tot[s][1] = tot[s][2] = tot[s][3] = 0.f;
 
-    for (int kk = 0; kk < kb - ka; ++kk, ++seq) {
-      const int rs = seq % stages;
-      mbar_wait_bounded(smem_u32(&bars[rs]), (seq / stages) & 1, abort_flag, kDevTimeoutFull);
+    for (int kk = 0; kk < kb - ka && mma_warp; ++kk) {
+      const uint32_t sq = seq + kk;
+      const int rs = sq % stages;
+      mbar_wait_bounded(smem_u32(&bars[rs]), (sq / stages) & 1, abort_flag, kDevTimeoutFull);
       const uint8_t* tl = smem + L.ring + rs * kProgStage + tile * kProgSlot;
-      float part[4][4];
 #pragma unroll
-      for (int s = 0; s < 4; ++s) part[s][0] = part[s][1] = part[s][2] = part[s][3] = 0.f;
+      for (int j = 0; j < 2; ++j) {
+        const int kblk = 2 * kp + j;
+        float part[4][4];
 #pragma unroll
-      for (int st = 0; st < 2; ++st) {
-        const int kl = kk * 256 + kblk * 32 + st * 16;
-        const uint32_t* xr = x32 + g * xw_stride + kl / 2 + t;
-        const uint32_t bx0 = g < batch ? xr[0] : 0u;
-        const uint32_t bx1 = g < batch ? xr[4] : 0u;
-        const uint8_t* nb = tl + 1024 + rb * 2048 + kblk * 256 + st * 128 + 16 * t + 4 * h;
-        const uint32_t p1 = *reinterpret_cast<const uint32_t*>(nb + off_first);
-        const uint32_t p2 = *reinterpret_cast<const uint32_t*>(nb + off_second);
-        const uint32_t q1 = *reinterpret_cast<const uint32_t*>(nb + 64 + off_first);
-        const uint32_t q2 = *reinterpret_cast<const uint32_t*>(nb + 64 + off_second);
-        uint32_t aP[8], aQ[8];
-        decode_q4_pair_bf16(p1, p2, sel_lo, sel_hi, aP);
-        decode_q4_pair_bf16(q1, q2, sel_lo, sel_hi, aQ);
+        for (int s = 0; s < 4; ++s) part[s][0] = part[s][1] = part[s][2] = part[s][3] = 0.f;
 #pragma unroll
-        for (int s = 0; s < 4; ++s)
-          mma_bf16_m16n8k16(part[s][0], part[s][1], part[s][2], part[s][3], aP[2 * s], aP[2 * s + 1], aQ[2 * s],
-                            aQ[2 * s + 1], bx0, bx1);
-      }
-      // tot += d*part + m*sum(x) for this 32-k block
-      const uint8_t* meta = tl + (kblk * 32 + rb * 16 + h * 8) * 2;
-      const uint4 dv = *reinterpret_cast<const uint4*>(meta);
-      const uint4 mv = *reinterpret_cast<const uint4*>(meta + 512);
-      const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
-      const uint32_t mw[4] = {mv.x, mv.y, mv.z, mv.w};
-      const float2 xsv = *reinterpret_cast<const float2*>(xs_s + (kk * 8 + kblk) * 8 + 2 * t);
+        for (int st = 0; st < 2; ++st) {
+          const int kl = kk * 256 + kblk * 32 + st * 16;
+          const uint32_t* xr = x32 + g * xw_stride + kl / 2 + t;
+          const uint32_t bx0 = g < batch ? xr[0] : 0u;
+          const uint32_t bx1 = g < batch ? xr[4] : 0u;
+          const uint8_t* nb = tl + 1024 + rb * 2048 + kblk * 256 + st * 128 + 16 * t + 4 * h;
+          const uint32_t p1 = *reinterpret_cast<const uint32_t*>(nb + off_first);
+          const uint32_t p2 = *reinterpret_cast<const uint32_t*>(nb + off_second);
+          const uint32_t q1 = *reinterpret_cast<const uint32_t*>(nb + 64 + off_first);
+          const uint32_t q2 = *reinterpret_cast<const uint32_t*>(nb + 64 + off_second);
+          uint32_t aP[8], aQ[8];
+          decode_q4_pair_bf16(p1, p2, sel_lo, sel_hi, aP);
+          decode_q4_pair_bf16(q1, q2, sel_lo, sel_hi, aQ);
 #pragma unroll
-      for (int s = 0; s < 4; ++s) {
-        const float da = bf16lo_to_f32(dw[s]), db = bf16hi_to_f32(dw[s]);
-        const float ma = bf16lo_to_f32(mw[s]), mb = bf16hi_to_f32(mw[s]);
-        tot[s][0] = fmaf(da, part[s][0], fmaf(ma, xsv.x, tot[s][0]));
-        tot[s][1] = fmaf(da, part[s][1], fmaf(ma, xsv.y, tot[s][1]));
-        tot[s][2] = fmaf(db, part[s][2], fmaf(mb, xsv.x, tot[s][2]));
-        tot[s][3] = fmaf(db, part[s][3], fmaf(mb, xsv.y, tot[s][3]));
+          for (int s = 0; s < 4; ++s)
+            mma_bf16_m16n8k16(part[s][0], part[s][1], part[s][2], part[s][3], aP[2 * s], aP[2 * s + 1], aQ[2 * s],
+                              aQ[2 * s + 1], bx0, bx1);
+        }
+        // tot += d*part + m*sum(x) for this 32-k block
+        const uint8_t* meta = tl + (kblk * 32 + rb * 16 + h * 8) * 2;
+        const uint4 dv = *reinterpret_cast<const uint4*>(meta);
+        const uint4 mv = *reinterpret_cast<const uint4*>(meta + 512);
+        const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
+        const uint32_t mw[4] = {mv.x, mv.y, mv.z, mv.w};
+        const float2 xsv = *reinterpret_cast<const float2*>(xs_s + (kk * 8 + kblk) * 8 + 2 * t);
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+          const float da = bf16lo_to_f32(dw[s]), db = bf16hi_to_f32(dw[s]);
+          const float ma = bf16lo_to_f32(mw[s]), mb = bf16hi_to_f32(mw[s]);
+          tot[s][0] = fmaf(da, part[s][0], fmaf(ma, xsv.x, tot[s][0]));
+          tot[s][1] = fmaf(da, part[s][1], fmaf(ma, xsv.y, tot[s][1]));
+          tot[s][2] = fmaf(db, part[s][2], fmaf(mb, xsv.x, tot[s][2]));
+          tot[s][3] = fmaf(db, part[s][3], fmaf(mb, xsv.y, tot[s][3]));
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&bars[stages + rs]));
     }
+    seq += kb - ka;
 
     // park the warp's sums: red[warp][64 local rows = tile*16 + h*8 + r][ncol]
-    {
+    if (mma_warp) {
       float* rw = red + warp * 64 * ncol;
       const int c0 = 2 * t;
       if (c0 < batch) {
@@ -436,10 +478,142 @@ __device__ __forceinline__ void prog_gemv_phase(const ProgParams& p, const ProgP
         const int rbr = (row >> 4) & 1, lr = (row >> 5) * 16 + (row & 15);
         float v = 0.f;
 #pragma unroll
-        for (int q = 0; q < kProgWarps / 2; ++q) v += red[(2 * q + rbr) * 64 * ncol + lr * ncol + b];
+        for (int q = 0; q < kNbWarps / 2; ++q) v += red[(2 * q + rbr) * 64 * ncol + lr * ncol + b];
         if (grp * 4 + (row >> 5) < P.n_tile_rows)
           atomicAdd(P.y + static_cast<size_t>(b) * P.ldy + grp * kGroupRows + row, v);
       }
+    }
+  }
+}
+
+// ------------------------------------------------------- GEMV unit, batch 1
+// At batch 1 seven of the MMA's eight N columns would be padding.  Here column
+// j of the B operand carries x of 32-k block j of the K-tile (x in column j,
+// zero elsewhere), so one m16n8 accumulator collects all eight per-block dot
+// products of the K-tile and the d/m scale fold runs once per K-tile instead of
+// once per block.  Codes enter the MMA as the bf16 value 128 + n (no subtract);
+// the 128 * sum(x) this adds folds into the m term: y += d*D + (m - 128 d)*S.
+// Warp w: row-block rb = w & 1, rows half sh = (w >> 1) & 1 (rows 0-3 or 4-7 of
+// each lane's 8-row group), stage phase ph = w >> 2 (stages with seq % 3 == ph).
+constexpr int kB1Phases = kProgWarps / 4;
+
+__device__ __forceinline__ void decode_q4_half_bf16(uint32_t w1, uint32_t w2, uint32_t sel, uint32_t (&a)[4]) {
+  constexpr uint32_t kMagic = 0x43004300u;  // bf16x2 (128, 128): n | magic = 128 + n
+  const uint32_t r = prmt(w1, w2, sel);     // 4 rows at (k_a, k_b)
+  a[0] = lop3<kLutAndOr>(r, 0x000F000Fu, kMagic);
+  a[1] = lop3<kLutAndOr>(r >> 4, 0x000F000Fu, kMagic);
+  a[2] = lop3<kLutAndOr>(r >> 8, 0x000F000Fu, kMagic);
+  a[3] = lop3<kLutAndOr>(r >> 12, 0x000F000Fu, kMagic);
+}
+
+__device__ __forceinline__ void prog_gemv_phase_b1(const ProgPhase& P, uint8_t* smem, const ProgSmem& L,
+                                                   uint64_t* bars, volatile int* abort_flag, int stages,
+                                                   uint32_t& seq, uint32_t& unit_seq) {
+  const int ctid = threadIdx.x, warp = ctid >> 5, lane = ctid & 31;
+  constexpr int ncol = 2;
+  float* red = reinterpret_cast<float*>(smem + L.red);
+  const int g = lane >> 2, t = lane & 3;
+  const int tile = g & 3, h = g >> 2, odd = tile & 1;
+  const int rb = warp & 1, sh = (warp >> 1) & 1, ph = warp >> 2;
+  const uint32_t sel = sh ? (odd ? 0x3276u : 0x7632u) : (odd ? 0x1054u : 0x5410u);
+  const int off_first = odd ? 8 : 0, off_second = odd ? 0 : 8;
+
+  ProgUnits it((P.n_tile_rows + 3) / 4, P.k_tiles, blockIdx.x, gridDim.x, prog_unit_kt(1));
+  int grp, ka, kb;
+  bool first_unit = true;
+  while (it.next(grp, ka, kb)) {
+    const int slot = unit_seq & 1;
+    ++unit_seq;
+    prog_stage_x(P, 1, ka, kb, first_unit, slot, smem, L);
+    first_unit = false;
+    const uint32_t* x32 = reinterpret_cast<const uint32_t*>(smem + L.work + slot * L.xslot);
+    const float* xs_s = reinterpret_cast<const float*>(smem + L.xs + slot * L.xs_slot);
+    float tot[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+    const uint32_t seq0 = seq;
+    const int n_st = kb - ka;
+    for (int kk = 0; kk < n_st; ++kk) {
+      const uint32_t sq = seq0 + kk;
+      if (static_cast<int>(sq % kB1Phases) != ph) continue;
+      const int rs = sq % stages;
+      mbar_wait_bounded(smem_u32(&bars[rs]), (sq / stages) & 1, abort_flag, kDevTimeoutFull);
+      const uint8_t* tl = smem + L.ring + rs * kProgStage + tile * kProgSlot;
+      // x of block g (this lane's column) at k = g*32 + st*16 + {2t, 2t+8}
+      uint32_t xw[2][2];
+#pragma unroll
+      for (int st = 0; st < 2; ++st) {
+        const uint32_t* xr = x32 + (kk * 256 + g * 32 + st * 16) / 2 + t;
+        xw[st][0] = xr[0];
+        xw[st][1] = xr[4];
+      }
+      float acc[2][4];
+#pragma unroll
+      for (int s = 0; s < 2; ++s) acc[s][0] = acc[s][1] = acc[s][2] = acc[s][3] = 0.f;
+#pragma unroll
+      for (int kblk = 0; kblk < 8; ++kblk) {
+        const bool mine = g == kblk;
+#pragma unroll
+        for (int st = 0; st < 2; ++st) {
+          const uint8_t* nb = tl + 1024 + rb * 2048 + kblk * 256 + st * 128 + 16 * t + 4 * h;
+          const uint32_t p1 = *reinterpret_cast<const uint32_t*>(nb + off_first);
+          const uint32_t p2 = *reinterpret_cast<const uint32_t*>(nb + off_second);
+          const uint32_t q1 = *reinterpret_cast<const uint32_t*>(nb + 64 + off_first);
+          const uint32_t q2 = *reinterpret_cast<const uint32_t*>(nb + 64 + off_second);
+          uint32_t aP[4], aQ[4];
+          decode_q4_half_bf16(p1, p2, sel, aP);
+          decode_q4_half_bf16(q1, q2, sel, aQ);
+          const uint32_t b0 = mine ? xw[st][0] : 0u, b1 = mine ? xw[st][1] : 0u;
+#pragma unroll
+          for (int s = 0; s < 2; ++s)
+            mma_bf16_m16n8k16(acc[s][0], acc[s][1], acc[s][2], acc[s][3], aP[2 * s], aP[2 * s + 1], aQ[2 * s],
+                              aQ[2 * s + 1], b0, b1);
+        }
+      }
+      // fold columns 2t, 2t+1 (blocks 2t + c): rows 4sh + 2s (c0, c1) and 4sh + 2s + 1 (c2, c3)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int kbl = 2 * t + c;
+        const uint8_t* meta = tl + (kbl * 32 + rb * 16 + h * 8 + 4 * sh) * 2;
+        const uint2 dv = *reinterpret_cast<const uint2*>(meta);
+        const uint2 mv = *reinterpret_cast<const uint2*>(meta + 512);
+        const float sx = xs_s[(kk * 8 + kbl) * 8];
+        const uint32_t dw[2] = {dv.x, dv.y}, mw[2] = {mv.x, mv.y};
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {
+          const float da = bf16lo_to_f32(dw[s]), db = bf16hi_to_f32(dw[s]);
+          const float ma = fmaf(-128.f, da, bf16lo_to_f32(mw[s]));
+          const float mb = fmaf(-128.f, db, bf16hi_to_f32(mw[s]));
+          tot[s][0] = fmaf(da, acc[s][c], fmaf(ma, sx, tot[s][0]));
+          tot[s][1] = fmaf(db, acc[s][2 + c], fmaf(mb, sx, tot[s][1]));
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bars[stages + rs]));
+    }
+    seq = seq0 + n_st;
+
+    // sum the four t lanes (their block columns), park, then sum the stage phases
+#pragma unroll
+    for (int s = 0; s < 2; ++s)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        tot[s][e] += __shfl_xor_sync(0xffffffffu, tot[s][e], 1);
+        tot[s][e] += __shfl_xor_sync(0xffffffffu, tot[s][e], 2);
+      }
+    if (t == 0) {
+      float* rw = red + warp * 64 * ncol;
+#pragma unroll
+      for (int s = 0; s < 2; ++s)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) rw[(tile * 16 + h * 8 + 4 * sh + 2 * s + e) * ncol] = tot[s][e];
+    }
+    named_barrier(1, kProgConsumers);
+    if (!*abort_flag && ctid < kGroupRows) {
+      const int row = ctid;
+      const int rbr = (row >> 4) & 1, lr = (row >> 5) * 16 + (row & 15), shr = (row >> 2) & 1;
+      float v = 0.f;
+#pragma unroll
+      for (int q = 0; q < kB1Phases; ++q) v += red[(rbr + 2 * shr + 4 * q) * 64 * ncol + lr * ncol];
+      if (grp * 4 + (row >> 5) < P.n_tile_rows) atomicAdd(P.y + grp * kGroupRows + row, v);
     }
   }
 }
@@ -618,6 +792,18 @@ __device__ __forceinline__ void prog_attention_phase(const ProgParams& p, const 
   }
 }
 
+// RoPE cos/sin of each sequence's position, half-split pairs i = 0..31
+// (granite_elementwise.py:135-138): fp64 angle, rounded to fp32 exactly as the
+// one-shot attention kernel does.  One block of 32 threads per sequence.
+__global__ void prog_rope_kernel(const int* pos, float theta, float* rope) {
+  const int b = blockIdx.x, i = threadIdx.x;
+  const double inv = pow(static_cast<double>(theta), -2.0 * i / 64);
+  double sn, cs;
+  sincos(static_cast<double>(pos[b]) * inv, &sn, &cs);
+  rope[(b * 32 + i) * 2] = static_cast<float>(cs);
+  rope[(b * 32 + i) * 2 + 1] = static_cast<float>(sn);
+}
+
 __global__ void __launch_bounds__(kProgThreads, 1) decode_program_kernel(const ProgParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const ProgSmem L(p.stages, p.batch);
@@ -629,7 +815,8 @@ __global__ void __launch_bounds__(kProgThreads, 1) decode_program_kernel(const P
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(smem_u32(&bars[s]), 1);
-      mbar_init(smem_u32(&bars[stages + s]), kProgWarps);
+      // empty: the 8 MMA warps per stage, or at batch 1 the four warps of the stage's phase
+      mbar_init(smem_u32(&bars[stages + s]), p.batch == 1 ? 4 : kNbWarps);
     }
     abort_flag[0] = 0;
     abort_flag[1] = 1;
@@ -708,21 +895,14 @@ __global__ void __launch_bounds__(kProgThreads, 1) decode_program_kernel(const P
       for (int i = gtid; i < P.copy_n; i += gstride) P.copy_dst[i] = P.copy_src[i];
     }
     if (P.kind == kPhPrep) {
-      if (blockIdx.x == 0) {
-        // RoPE cos/sin per sequence, half-split pairs i = 0..31 (granite_elementwise.py:135-138)
-        for (int e = ctid; e < p.batch * 32; e += kProgConsumers) {
-          const int b = e / 32, i = e % 32;
-          const double inv = pow(static_cast<double>(p.theta), -2.0 * i / 64);
-          double sn, cs;
-          sincos(static_cast<double>(p.pos[b]) * inv, &sn, &cs);
-          p.rope[2 * e] = static_cast<float>(cs);
-          p.rope[2 * e + 1] = static_cast<float>(sn);
-        }
-      }
+      // side tasks only (the RoPE table comes from prog_rope_kernel, launched just before)
     } else if (P.kind == kPhAttn) {
       prog_attention_phase(p, P, smem + L.work);
     } else {
-      prog_gemv_phase(p, P, smem, L, bars, abort_flag, seq, unit_seq);
+      if (p.batch == 1)
+        prog_gemv_phase_b1(P, smem, L, bars, abort_flag, stages, seq, unit_seq);
+      else
+        prog_gemv_phase(p, P, smem, L, bars, abort_flag, seq, unit_seq);
     }
     if (P.barrier_after) {
       ++n_barriers;

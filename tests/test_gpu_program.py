@@ -88,13 +88,16 @@ def test_program_step_matches_per_op_step(cuda, bsz, ctx, start):
         torch.cuda.synchronize()
         # same arithmetic per element; fp32 summation order differs and is re-rounded to bf16 between ops
         _compare_rows(b.logits, a.logits, 0.9999, 1e-2, ("logits", step))
+        # appended cache rows: the two paths compute 1/rms in different fp32 orders, so a normed
+        # input that lands on a bf16 midpoint can round differently (one x element moves by an
+        # ulp and every projection row by w * ulp); compare each row by the logits metric
         for li in range(cfg.n_layers):
             for s in range(bsz):
                 p = int(pos[s])
-                torch.testing.assert_close(b.k_cache[li][s, :, p].float(), a.k_cache[li][s, :, p].float(),
-                                           rtol=2 ** -6, atol=1e-3)
-                torch.testing.assert_close(b.v_cache[li][s, :, p].float(), a.v_cache[li][s, :, p].float(),
-                                           rtol=2 ** -6, atol=1e-3)
+                for cache in ("k_cache", "v_cache"):
+                    got = getattr(b, cache)[li][s, :, p].reshape(1, -1)
+                    ref = getattr(a, cache)[li][s, :, p].reshape(1, -1)
+                    _compare_rows(got, ref, 0.9999, 1e-2, (cache, li, s, step))
         pos = pos + 1
     assert ops.device_error() == 0
 
