@@ -179,6 +179,25 @@ int b2_rmsnorm(const void* x, int x_is_f32, int ldx, const uint16_t* w, float ep
                int ldy, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Large-batch W4A16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM):
+ * the GEMV entry points' arithmetic for batches up to 256, where the
+ * projection is a dense contraction (granite_gemv32.py:90-100
+ * is the reference's batched layout).  Weights are dequantised in shared memory
+ * to fp16 (w = code*d + m rounded once, relative error <= 2^-11) and x is staged
+ * as fp16 x*2^e per token; accumulation fp32.
+ *   y   fp32 [batch][ldy] = (or += with B2_GEMV_ACCUMULATE) W x
+ *   h   bf16 [batch][ldh] = silu(bf16(G x)) * bf16(U x)        (SwiGLU form)
+ *   batch 1..256; x bf16 [batch][ldx], 16-byte aligned, ldx % 8 == 0.
+ *   workspace: device memory of b2_q4_gemm_workspace_size bytes, 256-byte
+ *   aligned (the staged fp16 x and exponents); not kept between calls. */
+int b2_q4_gemm_workspace_size(int batch, int k_tiles, size_t* bytes);
+int b2_q4_gemm(const uint8_t* tiles, int n_tile_rows, int k_tiles, const uint16_t* x, int batch, int ldx, float* y,
+               int ldy, int flags, void* workspace, size_t workspace_bytes, void* stream);
+int b2_q4_swiglu_gemm(const uint8_t* gate, const uint8_t* up, int n_tile_rows, int k_tiles, const uint16_t* x,
+                      int batch, int ldx, uint16_t* h, int ldh, int flags, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+/* ------------------------------------------------------------------------
  * Decode program: a whole decode step (or any chain of q4 GEMVs and GQA
  * attention) as ONE persistent launch.  Replaces the per-op token loop that
  * chat.py:74-78 drives through model.generate (one call per projection,

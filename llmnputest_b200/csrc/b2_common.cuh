@@ -97,6 +97,12 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   return p;
 }
 
+__device__ __forceinline__ uint64_t l2_evict_last_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
 // Global -> this CTA's shared memory, completion counted on `bar` in bytes.
 // dst/src 16-byte aligned, bytes a multiple of 16.  No multicast.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,

@@ -18,6 +18,7 @@
 #include "../../include/b2q4nx.h"
 #include "b2_common.cuh"
 #include "decode_program.cuh"
+#include "q4_gemm_tc.cuh"
 #include "q4nx_dequant.cuh"
 #include "gqa_decode.cuh"
 #include "q4nx_gemv.cuh"
@@ -84,10 +85,13 @@ inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_
 //   B2Q4NX_MAX_CLUSTER   largest split-K cluster (1..16, default 16)
 //   B2Q4NX_CTAS_PER_SM   force 1 or 2 GEMV CTAs per SM (default: 2 when they fit)
 //   B2Q4NX_MAX_STAGES    cap on the shared-memory pipeline depth (1..8)
+//   B2Q4NX_TC_SPLITS / _TC_RAW / _TC_XSTAGES / _TC_ABUFS   tensor-core GEMM split-K
+//                        count, raw and x pipeline depths, A buffers per slice
 struct Tuning {
   int max_cluster = 16;
   int ctas_per_sm = 0;
   int max_stages = b2::kMaxStages;
+  int tc_splits = 0, tc_raw = 0, tc_xst = 0, tc_abufs = 0;  // tensor-core GEMM overrides (0 = plan)
 };
 const Tuning& tuning() {
   static const Tuning t = [] {
@@ -95,6 +99,10 @@ const Tuning& tuning() {
     if (const char* e = getenv("B2Q4NX_MAX_CLUSTER")) v.max_cluster = std::max(1, std::min(16, atoi(e)));
     if (const char* e = getenv("B2Q4NX_CTAS_PER_SM")) v.ctas_per_sm = std::max(0, std::min(2, atoi(e)));
     if (const char* e = getenv("B2Q4NX_MAX_STAGES")) v.max_stages = std::max(1, std::min(b2::kMaxStages, atoi(e)));
+    if (const char* e = getenv("B2Q4NX_TC_SPLITS")) v.tc_splits = std::max(0, atoi(e));
+    if (const char* e = getenv("B2Q4NX_TC_RAW")) v.tc_raw = std::max(0, std::min(4, atoi(e)));
+    if (const char* e = getenv("B2Q4NX_TC_XSTAGES")) v.tc_xst = std::max(0, std::min(8, atoi(e)));
+    if (const char* e = getenv("B2Q4NX_TC_ABUFS")) v.tc_abufs = std::max(0, std::min(2, atoi(e)));
     return v;
   }();
   return t;
@@ -446,6 +454,115 @@ int prog_check_phase(const b2_phase& P, int i) {
   }
 }
 
+// ------------------------------------------------- tcgen05 GEMM (large batch)
+inline int tc_npad(int batch) { return (batch + 15) / 16 * 16; }
+inline size_t tc_ws_bytes(int batch, int k_tiles) {
+  const size_t img = static_cast<size_t>(tc_npad(batch)) * k_tiles * 256 * 2;
+  return ((img + 255) & ~static_cast<size_t>(255)) + static_cast<size_t>(tc_npad(batch)) * sizeof(int);
+}
+
+int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_rows, int k_tiles, const uint16_t* x,
+                   int batch, int ldx, void* y, int ldy, int flags, void* workspace, size_t ws_bytes,
+                   void* stream) {
+  DevInfo di;
+  int st = device_info(&di);
+  if (st != B2_OK) return st;
+  if (!w0 || !x || !y || (epi == b2::kTcEpiSwiglu && !w1)) return fail(B2_ERR_ARG, "null pointer argument");
+  if (n_tile_rows < 1 || k_tiles < 1) return fail(B2_ERR_ARG, "bad tile shape %d x %d", n_tile_rows, k_tiles);
+  if (batch < 1 || batch > b2::kTcMaxN) return fail(B2_ERR_ARG, "batch %d outside 1..%d", batch, b2::kTcMaxN);
+  if (ldx < k_tiles * 256 || ldx % 8) return fail(B2_ERR_ALIGN, "ldx %d: need >= K and a multiple of 8", ldx);
+  if (ldy < n_tile_rows * 32) return fail(B2_ERR_ARG, "ldy %d < output rows %d", ldy, n_tile_rows * 32);
+  if (!aligned(w0, 16) || (w1 && !aligned(w1, 16)) || !aligned(x, 16)) return fail(B2_ERR_ALIGN, "tiles and x must be 16-byte aligned");
+  if (flags & ~B2_GEMV_ACCUMULATE) return fail(B2_ERR_ARG, "unknown flags 0x%x", flags);
+  if (epi == b2::kTcEpiSwiglu && (flags & B2_GEMV_ACCUMULATE)) return fail(B2_ERR_ARG, "SwiGLU output cannot accumulate");
+  const size_t need = tc_ws_bytes(batch, k_tiles);
+  if (!workspace || ws_bytes < need) return fail(B2_ERR_WORKSPACE, "workspace of %zu bytes needed", need);
+  if (!aligned(workspace, 256)) return fail(B2_ERR_ALIGN, "workspace must be 256-byte aligned");
+
+  const int npad = tc_npad(batch);
+  const int budget = di.smem_optin - 1024;  // alignment slack for the 1024-byte operand atoms
+  // pipeline: double-buffered A slices when they fit beside >= 2 raw and >= 2 x stages
+  int raw_stages = 0, x_stages = 0, a_bufs = tuning().tc_abufs > 0 ? tuning().tc_abufs : 2;
+  const int max_raw = tuning().tc_raw > 0 ? tuning().tc_raw : 3;
+  const int max_x = tuning().tc_xst > 0 ? tuning().tc_xst : 8;
+  for (; a_bufs >= 1 && x_stages < 2; --a_bufs) {
+    for (raw_stages = max_raw; raw_stages >= 2; --raw_stages) {
+      const b2::TcSmem base(npad, raw_stages, 0, a_bufs);
+      x_stages = std::min(max_x, (budget - base.total) / (npad * 128 + 16));
+      if (x_stages >= 2) break;
+    }
+  }
+  ++a_bufs;  // undo the loop's last decrement
+  if (x_stages < 2) return fail(B2_ERR_UNSUPPORTED, "shared memory too small for the tensor-core GEMM");
+  const int smem = b2::TcSmem(npad, raw_stages, x_stages, a_bufs).total + 1024;
+  const int n_row_tiles = epi == b2::kTcEpiSwiglu ? (n_tile_rows + 1) / 2 : (n_tile_rows + 3) / 4;
+  // split-K (fp32 form only) so that small projections still occupy every SM
+  // split-K (fp32 form only) so that small projections still occupy every SM, in
+  // one wave: row tiles x splits <= SMs
+  int n_splits = 1, kt_per_split = k_tiles;
+  if (epi == b2::kTcEpiF32 && 2 * n_row_tiles <= di.sms) {
+    n_splits = std::min(k_tiles, di.sms / n_row_tiles);
+    kt_per_split = (k_tiles + n_splits - 1) / n_splits;
+    n_splits = (k_tiles + kt_per_split - 1) / kt_per_split;
+  }
+  if (tuning().tc_splits > 0) {  // tuning experiments
+    n_splits = std::min(k_tiles, tuning().tc_splits);
+    kt_per_split = (k_tiles + n_splits - 1) / n_splits;
+    n_splits = (k_tiles + kt_per_split - 1) / kt_per_split;
+  }
+  float* yzero = (n_splits > 1 && !(flags & B2_GEMV_ACCUMULATE)) ? static_cast<float*>(y) : nullptr;
+
+  uint8_t* xsw = static_cast<uint8_t*>(workspace);
+  int* xexp = reinterpret_cast<int*>(xsw + ((static_cast<size_t>(npad) * k_tiles * 512 + 255) & ~static_cast<size_t>(255)));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(npad, 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, b2::tc_x_prep_kernel, reinterpret_cast<const __nv_bfloat16*>(x), ldx,
+                                     batch, k_tiles * 256, npad, xsw, xexp, yzero, ldy, n_tile_rows * 32);
+  if (e != cudaSuccess) return cuda_fail(e, "x pre-pass launch");
+
+  b2::TcParams p = {};
+  p.w0 = w0;
+  p.w1 = w1;
+  p.n_tile_rows = n_tile_rows;
+  p.k_tiles = k_tiles;
+  p.xsw = xsw;
+  p.xexp = xexp;
+  p.batch = batch;
+  p.npad = npad;
+  p.raw_stages = raw_stages;
+  p.x_stages = x_stages;
+  p.a_bufs = a_bufs;
+  p.y = y;
+  p.ldy = ldy;
+  p.accumulate = (flags & B2_GEMV_ACCUMULATE) ? 1 : 0;
+  p.n_row_tiles = n_row_tiles;
+  p.n_splits = n_splits;
+  p.kt_per_split = kt_per_split;
+  auto kernel = epi == b2::kTcEpiSwiglu ? b2::q4_gemm_tc_kernel<b2::kTcEpiSwiglu> : b2::q4_gemm_tc_kernel<b2::kTcEpiF32>;
+  static int attr_set[64][2] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev][epi]) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, di.smem_optin);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tensor-core GEMM)");
+    attr_set[dev][epi] = 1;
+  }
+  cfg.gridDim = dim3(std::min(n_row_tiles * n_splits, di.sms), 1, 1);
+  cfg.blockDim = dim3(b2::kTcThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  e = cudaLaunchKernelEx(&cfg, kernel, p);
+  if (e != cudaSuccess) return cuda_fail(e, "tensor-core GEMM launch");
+  return B2_OK;
+}
+
 }  // namespace
 
 // ------------------------------------------------------------------ C ABI
@@ -774,6 +891,26 @@ int b2_program_launch(const void* dev_phases, int n_phases, int batch, const int
   e = cudaLaunchKernelEx(&cfg, b2::decode_program_kernel, p);
   if (e != cudaSuccess) return cuda_fail(e, "decode program launch");
   return B2_OK;
+}
+
+int b2_q4_gemm_workspace_size(int batch, int k_tiles, size_t* bytes) {
+  if (!bytes) return fail(B2_ERR_ARG, "null bytes pointer");
+  if (batch < 1 || batch > b2::kTcMaxN || k_tiles < 1) return fail(B2_ERR_ARG, "bad batch %d / k_tiles %d", batch, k_tiles);
+  *bytes = tc_ws_bytes(batch, k_tiles);
+  return B2_OK;
+}
+
+int b2_q4_gemm(const uint8_t* tiles, int n_tile_rows, int k_tiles, const uint16_t* x, int batch, int ldx, float* y,
+               int ldy, int flags, void* workspace, size_t workspace_bytes, void* stream) {
+  return tc_gemm_common(b2::kTcEpiF32, tiles, nullptr, n_tile_rows, k_tiles, x, batch, ldx, y, ldy, flags,
+                        workspace, workspace_bytes, stream);
+}
+
+int b2_q4_swiglu_gemm(const uint8_t* gate, const uint8_t* up, int n_tile_rows, int k_tiles, const uint16_t* x,
+                      int batch, int ldx, uint16_t* h, int ldh, int flags, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  return tc_gemm_common(b2::kTcEpiSwiglu, gate, up, n_tile_rows, k_tiles, x, batch, ldx, h, ldh, flags, workspace,
+                        workspace_bytes, stream);
 }
 
 int b2_q4_dequant_tiles(const uint8_t* tiles, int64_t n_tiles, uint16_t* out, void* stream) {

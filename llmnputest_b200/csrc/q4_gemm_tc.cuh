@@ -1,0 +1,500 @@
+// q4nx W4A16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM), for
+// decode batches where the GEMV becomes a dense contraction (16 < B <= 256).
+//
+//   y[b][n] = sum_k W[n][k] * x[b][k]        (or, fused, h = silu(bf16 g) * bf16 u)
+//
+// Operands (both fp16, as one tcgen05.mma kind::f16 requires):
+//   A = weights, M = 128 rows of a CTA tile (4 q4nx tile-rows), dequantised in
+//       shared memory by 8 warps: w = code*d + m in fp32, rounded once to fp16
+//       (relative error <= 2^-11 per weight; codes and the block scales come
+//       from the tiles exactly as stored, tools/q4nx.py:80-111).
+//   B = x, N = batch rounded up to 16 (<= 256): staged by a pre-pass as fp16
+//       x*2^e (e per token, exact power of two, undone in the epilogue) in the
+//       exact byte image of the shared-memory operand (K-major, 128-byte
+//       swizzle), so a plain 1-D bulk copy (cp.async.bulk, no multicast, no
+//       tensor map) lands each 64-k slice ready for the tensor core.
+//   D = fp32 in TMEM, 2 x N columns (double-buffered across row tiles).
+//
+// Warp roles (14 warps):
+//   warp 0       producer: bulk copies of the raw tiles (one K-tile stage) and
+//                of the x slices, mbarrier complete_tx
+//   warp 1       TMEM allocation; lane 0 issues tcgen05.mma (4 per 64-k slice)
+//                and tcgen05.commit to release the slices and publish D
+//   warps 2-5    epilogue: tcgen05.ld 32x32b (warp w reads TMEM lanes
+//                32*(w%4) ..), scale by 2^-e, store y / SwiGLU through smem
+//   warps 6-13   dequant: four pairs, pair j converts 64-k slice j of every
+//                K-tile (raw ring -> A ring slot j)
+// Every mbarrier wait is bounded; on a timeout the kernel records an error,
+// stops issuing, waits (bounded) for the MMAs it issued, frees TMEM and exits.
+#pragma once
+
+#include "b2_common.cuh"
+#include "q4nx_gemv.cuh"
+
+namespace b2 {
+
+constexpr int kTcM = 128;
+constexpr int kTcWarps = 14;
+constexpr int kTcThreads = kTcWarps * 32;
+constexpr int kTcEpiWarp0 = 2;
+constexpr int kTcDqWarp0 = 6;
+constexpr int kTcMaxASlots = 8;              // per 64-k slice of a K-tile: 1 or 2 (double-buffered)
+constexpr int kTcASlotBytes = kTcM * 128;    // 128 rows x 64 fp16
+constexpr int kTcRawSlot = QTraits<kQ4>::kSlot;
+constexpr int kTcRawStage = 4 * kTcRawSlot;
+constexpr int kTcMaxN = 256;
+constexpr int kTcXchgStride = 33;            // SwiGLU exchange row stride in floats (bank spread)
+constexpr int kTcXchgBytes = 64 * kTcXchgStride * 4;  // 64 up rows x 32 tokens
+
+enum TcEpi : int { kTcEpiF32 = 0, kTcEpiSwiglu = 1 };
+
+struct TcParams {
+  const uint8_t* w0;  // [n_tile_rows][k_tiles][5120]
+  const uint8_t* w1;  // SwiGLU: up tiles (w0 = gate), else null
+  int n_tile_rows;    // per source
+  int k_tiles;
+  const uint8_t* xsw;  // x image [k_tiles*4][npad][64] fp16, swizzled
+  const int* xexp;     // [npad] exponents e (x' = x * 2^e)
+  int batch, npad;
+  int raw_stages, x_stages;
+  int a_bufs;  // A slots per 64-k slice (1 or 2)
+  void* y;     // fp32 [batch][ldy], or SwiGLU bf16 [batch][ldy]
+  int ldy;
+  int accumulate;
+  int n_row_tiles;  // CTA tiles of 128 output rows (SwiGLU: 64 gate + 64 up rows)
+  int n_splits;     // split-K: work item = (row tile, K range); partials added with fp32 reductions
+  int kt_per_split;
+};
+
+struct TcSmem {
+  int a, x, raw, xchg, bar, total;
+  __host__ __device__ TcSmem(int npad, int raw_stages, int x_stages, int a_bufs) {
+    a = 0;  // 1024-aligned base (the kernel aligns the dynamic smem pointer)
+    x = a + 4 * a_bufs * kTcASlotBytes;
+    raw = x + x_stages * npad * 128;
+    xchg = raw + raw_stages * kTcRawStage;
+    bar = (xchg + kTcXchgBytes + 15) & ~15;
+    // raw full/empty, a full/empty, x full/empty, acc full/empty x2, done, tmem addr
+    total = bar + (2 * raw_stages + 2 * kTcMaxASlots + 2 * x_stages + 4 + 1) * 8 + 16;
+  }
+};
+
+// ---------------------------------------------------------------- tcgen05
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem] * B[smem]^T, fp16 x fp16 -> fp32
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// arrive on `bar` once every MMA this thread issued so far has completed
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms of
+// 1024 B (stride between atoms = 1024 B), start 16-byte aligned.
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(1) << 16) |
+         (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+         (static_cast<uint64_t>(2) << 61);
+}
+// Instruction descriptor, kind::f16: D fp32, A and B fp16, both K-major, M x N.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int m, int n) {
+  return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+// Byte offset of element (row, k) of a [rows][64] fp16 operand slice in the
+// K-major 128-byte-swizzle layout: 16-byte chunk c of row r sits at chunk c ^ (r % 8).
+__host__ __device__ __forceinline__ uint32_t sw128_offset(int row, int k) {
+  return static_cast<uint32_t>((row >> 3) * 1024 + (row & 7) * 128 + ((((k >> 3) ^ row) & 7) << 4) + (k & 7) * 2);
+}
+
+// ------------------------------------------------------------ x pre-pass
+// One CTA per token row n < npad: e = exponent putting max|x| in [2^14, 2^15),
+// x' = fp16(x * 2^e) written into the swizzled slice image; rows >= batch are 0.
+__global__ void __launch_bounds__(256) tc_x_prep_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int batch,
+                                                        int k, int npad, uint8_t* __restrict__ xsw,
+                                                        int* __restrict__ xexp, float* __restrict__ yzero, int ldy,
+                                                        int n_out) {
+  __shared__ float wmax[8];
+  const int n = blockIdx.x;
+  pdl_wait();
+  pdl_launch_dependents();
+  const bool live = n < batch;
+  float m = 0.f;
+  if (live)
+    for (int c = threadIdx.x; c < k / 8; c += blockDim.x)
+      m = fmaxf(m, absmax8_bf16(*reinterpret_cast<const uint4*>(x + static_cast<size_t>(n) * ldx + c * 8)));
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = m;
+  __syncthreads();
+  m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m = fmaxf(m, wmax[i]);
+  const int e = live ? gemv_scale_exp(__float_as_uint(m)) : 0;
+  const float sc = pow2f(e);
+  if (threadIdx.x == 0) xexp[n] = e;
+  if (yzero && live)  // split-K partials are added into y: start it at zero
+    for (int i = threadIdx.x; i < n_out; i += blockDim.x) yzero[static_cast<size_t>(n) * ldy + i] = 0.f;
+  for (int c = threadIdx.x; c < k / 8; c += blockDim.x) {
+    uint4 o = make_uint4(0u, 0u, 0u, 0u);
+    if (live) {
+      const uint4 v = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(n) * ldx + c * 8);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      uint32_t h[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __half2 hv = __floats2half2_rn(bf16lo_to_f32(w[i]) * sc, bf16hi_to_f32(w[i]) * sc);
+        h[i] = *reinterpret_cast<const uint32_t*>(&hv);
+      }
+      o = make_uint4(h[0], h[1], h[2], h[3]);
+    }
+    const int kc = (c * 8) >> 6, kin = (c * 8) & 63;
+    *reinterpret_cast<uint4*>(xsw + static_cast<size_t>(kc) * npad * 128 + sw128_offset(n, kin)) = o;
+  }
+}
+
+// ------------------------------------------------------------ the GEMM
+template <int EPI>
+__global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment for the swizzled operand slices
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  const TcSmem L(p.npad, p.raw_stages, p.x_stages, p.a_bufs);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar);
+  const int RS = p.raw_stages, XS = p.x_stages;
+  uint64_t* raw_full = bars;
+  uint64_t* raw_empty = raw_full + RS;
+  uint64_t* a_full = raw_empty + RS;
+  uint64_t* a_empty = a_full + kTcMaxASlots;
+  uint64_t* x_full = a_empty + kTcMaxASlots;
+  uint64_t* x_empty = x_full + XS;
+  uint64_t* acc_full = x_empty + XS;  // [2]
+  uint64_t* acc_empty = acc_full + 2;  // [2]
+  uint64_t* mma_done = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int npad = p.npad;
+  const uint32_t ncols = npad <= 32 ? 32u : (npad <= 64 ? 64u : (npad <= 128 ? 128u : 256u));  // per buffer
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < RS; ++s) {
+      mbar_init(smem_u32(&raw_full[s]), 1);
+      mbar_init(smem_u32(&raw_empty[s]), 8);  // the 8 dequant warps
+    }
+    for (int s = 0; s < kTcMaxASlots; ++s) {
+      mbar_init(smem_u32(&a_full[s]), 2);   // the dequant pair of slice s % 4, buffer s / 4
+      mbar_init(smem_u32(&a_empty[s]), 1);  // [0..1]: buffer free again (tcgen05.commit per K-tile)
+    }
+    for (int s = 0; s < XS; ++s) {
+      mbar_init(smem_u32(&x_full[s]), 1);
+      mbar_init(smem_u32(&x_empty[s]), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&acc_full[s]), 1);
+      mbar_init(smem_u32(&acc_empty[s]), 4);  // the 4 epilogue warps
+    }
+    mbar_init(smem_u32(mma_done), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 2 * ncols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_launch_dependents();
+
+  const int KT = p.k_tiles;
+  const int n_items = p.n_row_tiles * p.n_splits;  // work item -> (row tile, K-tile range)
+  const int AB = p.a_bufs;
+  auto item_tile = [&](int it) { return it / p.n_splits; };
+  auto item_k0 = [&](int it) { return (it % p.n_splits) * p.kt_per_split; };
+  auto item_k1 = [&](int it) { return min(KT, item_k0(it) + p.kt_per_split); };
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0) {
+      pdl_wait();  // x image comes from the pre-pass
+      const uint64_t policy = l2_evict_first_policy();  // weights stream once
+      const uint64_t keep = l2_evict_last_policy();     // every CTA reads the same x slices
+      uint32_t rseq = 0, xseq = 0;
+      for (int it = blockIdx.x; it < n_items && !*abort_flag; it += gridDim.x) {
+        const int tile = item_tile(it);
+        for (int kt = item_k0(it); kt < item_k1(it); ++kt, ++rseq) {
+          const int rs = rseq % RS;
+          if (rseq >= static_cast<uint32_t>(RS) &&
+              !mbar_wait_bounded(smem_u32(&raw_empty[rs]), ((rseq / RS) & 1) ^ 1, abort_flag, kDevTimeoutEmpty))
+            break;
+          const uint8_t* src[4];
+          uint32_t bytes = 0;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            int tr;
+            const uint8_t* base;
+            if (EPI == kTcEpiSwiglu) {
+              tr = tile * 2 + (j & 1);
+              base = j < 2 ? p.w0 : p.w1;
+            } else {
+              tr = tile * 4 + j;
+              base = p.w0;
+            }
+            src[j] = tr < p.n_tile_rows ? base + (static_cast<size_t>(tr) * KT + kt) * QTraits<kQ4>::kTile : nullptr;
+            bytes += src[j] ? QTraits<kQ4>::kTile : 0;
+          }
+          mbar_arrive_expect_tx(smem_u32(&raw_full[rs]), bytes);
+          const uint32_t dst = smem_u32(smem + L.raw + rs * kTcRawStage);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (src[j]) bulk_g2s(dst + j * kTcRawSlot, src[j], QTraits<kQ4>::kTile, smem_u32(&raw_full[rs]), policy);
+          for (int js = 0; js < 4; ++js, ++xseq) {
+            const int xs = xseq % XS;
+            if (xseq >= static_cast<uint32_t>(XS) &&
+                !mbar_wait_bounded(smem_u32(&x_empty[xs]), ((xseq / XS) & 1) ^ 1, abort_flag, kDevTimeoutEmpty))
+              break;
+            const uint32_t xbytes = static_cast<uint32_t>(npad) * 128;
+            mbar_arrive_expect_tx(smem_u32(&x_full[xs]), xbytes);
+            bulk_g2s(smem_u32(smem + L.x + xs * xbytes), p.xsw + static_cast<size_t>(kt * 4 + js) * xbytes, xbytes,
+                     smem_u32(&x_full[xs]), keep);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA
+    if (lane == 0) {
+      pdl_wait();
+      const uint32_t idesc = umma_idesc_f16(kTcM, npad);
+      // ring positions advance by increments (no division in the issue loop: the
+      // tensor pipe drains if the issuing thread spends ~100 cycles between MMAs)
+      int ab = 0, xs = 0;
+      uint32_t aph = 0, xph = 0, t_it = 0;
+      const uint32_t a0 = smem_u32(smem + L.a), x0 = smem_u32(smem + L.x);
+      const uint32_t xbytes = static_cast<uint32_t>(npad) * 128;
+      bool issued_any = false;
+      for (int it = blockIdx.x; it < n_items && !*abort_flag; it += gridDim.x, ++t_it) {
+        const int buf = t_it & 1;
+        if (t_it >= 2)
+          mbar_wait_bounded(smem_u32(&acc_empty[buf]), ((t_it >> 1) & 1) ^ 1, abort_flag, kDevTimeoutEmpty);
+        const uint32_t d_tmem = tmem_base + buf * ncols;
+        const int k0 = item_k0(it), k1 = item_k1(it);
+        for (int kt = k0; kt < k1; ++kt) {
+          for (int js = 0; js < 4; ++js) {
+            const bool ok_a = mbar_wait_bounded(smem_u32(&a_full[4 * ab + js]), aph, abort_flag, kDevTimeoutFull);
+            const bool ok_x = mbar_wait_bounded(smem_u32(&x_full[xs]), xph, abort_flag, kDevTimeoutFull);
+            if (!ok_a || !ok_x) break;
+            tc_fence_after();
+            const uint64_t ad = umma_desc_sw128(a0 + (4 * ab + js) * kTcASlotBytes);
+            const uint64_t bd = umma_desc_sw128(x0 + xs * xbytes);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)  // +32 bytes along K = +2 in the descriptor's address field
+              tc_mma_f16(d_tmem, ad + 2 * kk, bd + 2 * kk, idesc, ((kt - k0) | js | kk) != 0);
+            issued_any = true;
+            tc_commit(smem_u32(&x_empty[xs]));
+            if (++xs == XS) {
+              xs = 0;
+              xph ^= 1;
+            }
+          }
+          if (*abort_flag) break;
+          tc_commit(smem_u32(&a_empty[ab]));
+          if (++ab == AB) {
+            ab = 0;
+            aph ^= 1;
+          }
+        }
+        if (*abort_flag) break;
+        tc_commit(smem_u32(&acc_full[buf]));
+      }
+      // every MMA issued here has completed before TMEM is released
+      if (issued_any) {
+        tc_commit(smem_u32(mma_done));
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(smem_u32(mma_done), 0)) {
+          if (globaltimer() - t0 > B2_WAIT_TIMEOUT_NS) {
+            record_error(kDevTimeoutDrain);
+            break;
+          }
+        }
+      }
+    }
+  } else if (warp < kTcDqWarp0) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may read
+    const int row_local = q * 32 + lane;
+    float* xchg = reinterpret_cast<float*>(smem + L.xchg);
+    pdl_wait();  // the exponents come from the pre-pass
+    uint32_t t_it = 0;
+    for (int it = blockIdx.x; it < n_items; it += gridDim.x, ++t_it) {
+      const int tile = item_tile(it);
+      const int buf = t_it & 1;
+      const bool ok = mbar_wait_bounded(smem_u32(&acc_full[buf]), (t_it >> 1) & 1, abort_flag, kDevTimeoutFull);
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + buf * ncols + (static_cast<uint32_t>(q * 32) << 16);
+      for (int c0 = 0; c0 < npad; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(t_row + c0, r);
+        if (EPI == kTcEpiF32) {
+          const int tr = tile * 4 + (row_local >> 5);
+          const int grow = tile * kTcM + row_local;
+          if (ok && !*abort_flag && tr < p.n_tile_rows) {
+            float* y = static_cast<float*>(p.y);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int n = c0 + j;
+              if (n < p.batch) {
+                const float v = __uint_as_float(r[j]) * pow2f(-p.xexp[n]);
+                float* dst = y + static_cast<size_t>(n) * p.ldy + grow;
+                if (p.n_splits > 1)
+                  atomicAdd(dst, v);  // zeroed by the pre-pass unless accumulating
+                else
+                  *dst = p.accumulate ? *dst + v : v;
+              }
+            }
+          }
+        } else {
+          // rows 0-63 gate, 64-127 the matching up rows: up warps hand their values over
+          if (q >= 2) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) xchg[(row_local - 64) * kTcXchgStride + j] = __uint_as_float(r[j]);
+          }
+          named_barrier(2, 128);
+          if (q < 2) {
+            const int tr = tile * 2 + (row_local >> 5);
+            const int grow = tile * 64 + row_local;
+            if (ok && !*abort_flag && tr < p.n_tile_rows) {
+              __nv_bfloat16* h = static_cast<__nv_bfloat16*>(p.y);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const int n = c0 + j;
+                if (n < p.batch) {
+                  const float u2 = pow2f(-p.xexp[n]);
+                  // both accumulators narrowed to bf16 before SiLU (granite_mlp.py:172-181)
+                  const float gb = __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[j]) * u2));
+                  const float ub = __bfloat162float(__float2bfloat16_rn(xchg[row_local * kTcXchgStride + j] * u2));
+                  h[static_cast<size_t>(n) * p.ldy + grow] = __float2bfloat16_rn(gb / (1.f + expf(-gb)) * ub);
+                }
+              }
+            }
+          }
+          named_barrier(2, 128);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&acc_empty[buf]));
+    }
+  } else {
+    // ------------------------------------------------------------ dequant
+    // pair js (warps 6+2js, 7+2js) converts slice js (k 64*js .. +63) of every K-tile.
+    // thread: chunk c = 8 k (lane & 7), tile-row t and row-block rb (idx >> 3)
+    const int idx = threadIdx.x - kTcDqWarp0 * 32;  // 0..255
+    const int js = idx >> 6;
+    const int pidx = idx & 63;
+    const int c = pidx & 7, qq = pidx >> 3;
+    const int t = qq >> 1, rb = qq & 1;
+    const int row0 = t * 32 + rb * 16;          // first of this thread's 16 A rows
+    const int kb = (js * 64 + c * 8) >> 5;      // this chunk's 32-k block
+    uint32_t rseq = 0;  // K-tiles of this CTA so far (= the MMA thread's kseq)
+    bool ok = true;
+    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+      for (int kt = item_k0(it); kt < item_k1(it); ++kt, ++rseq) {
+        const int rs = rseq % RS;
+        const int abuf = static_cast<int>(rseq % AB);
+        const int as = js + 4 * abuf;
+        ok = ok && mbar_wait_bounded(smem_u32(&raw_full[rs]), (rseq / RS) & 1, abort_flag, kDevTimeoutFull);
+        if (rseq >= static_cast<uint32_t>(AB))
+          ok = ok && mbar_wait_bounded(smem_u32(&a_empty[abuf]), ((rseq / AB) & 1) ^ 1, abort_flag,
+                                       kDevTimeoutEmpty);
+        if (ok) {
+          const uint8_t* tl = smem + L.raw + rs * kTcRawStage + t * kTcRawSlot;
+          // scales of the 16 rows at block kb: d, m bf16 -> fp16 pairs (d, d), (m, m)
+          const uint4* dp = reinterpret_cast<const uint4*>(tl + (kb * 32 + rb * 16) * 2);
+          const uint4 d0 = dp[0], d1 = dp[1], m0 = dp[32], m1 = dp[33];
+          const uint32_t dw[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+          const uint32_t mw[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+          // nibbles of k = 64 js + 8 c + 2i (+1): 16 bytes = 16 rows at k, then at k + 1
+          uint4 nv[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            nv[i] = *reinterpret_cast<const uint4*>(tl + 1024 + rb * 2048 + (js * 64 + c * 8 + 2 * i) * 8);
+          uint8_t* a_slot = smem + L.a + as * kTcASlotBytes;
+#pragma unroll
+          for (int rp = 0; rp < 8; ++rp) {  // row pair (2 rp, 2 rp + 1) = byte rp of each 8-byte row group
+            const float de = bf16lo_to_f32(dw[rp]), dodd = bf16hi_to_f32(dw[rp]);
+            const float me = bf16lo_to_f32(mw[rp]), modd = bf16hi_to_f32(mw[rp]);
+            const __half2 de2 = __floats2half2_rn(de, de), do2 = __floats2half2_rn(dodd, dodd);
+            const __half2 me2 = __floats2half2_rn(me, me), mo2 = __floats2half2_rn(modd, modd);
+            uint32_t ev[4], ov[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint32_t wl = (rp < 4) ? nv[i].x : nv[i].y;  // k bytes 0-7
+              const uint32_t wh = (rp < 4) ? nv[i].z : nv[i].w;  // k+1 bytes 8-15
+              const uint32_t bsel = static_cast<uint32_t>(rp & 3);
+              const uint32_t r2 = prmt(wl, wh, bsel | ((bsel + 4) << 8));  // k byte -> bits 0-7, k+1 byte -> 16-23
+              const uint32_t lo = f16x2_sub(lop3<kLutAndOr>(r2, 0x000F000Fu, 0x64006400u), 0x64006400u);
+              const uint32_t hi = f16x2_sub(lop3<kLutAndOr>(r2, 0x00F000F0u, 0x54005400u), 0x54005400u);
+              const __half2 we = __hfma2(*reinterpret_cast<const __half2*>(&lo), de2, me2);
+              const __half2 wo = __hfma2(*reinterpret_cast<const __half2*>(&hi), do2, mo2);
+              ev[i] = *reinterpret_cast<const uint32_t*>(&we);
+              ov[i] = *reinterpret_cast<const uint32_t*>(&wo);
+            }
+            const int re = row0 + 2 * rp;
+            *reinterpret_cast<uint4*>(a_slot + sw128_offset(re, c * 8)) = make_uint4(ev[0], ev[1], ev[2], ev[3]);
+            *reinterpret_cast<uint4*>(a_slot + sw128_offset(re + 1, c * 8)) = make_uint4(ov[0], ov[1], ov[2], ov[3]);
+          }
+        }
+        fence_async_smem();  // generic-proxy stores -> visible to the tensor core
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(smem_u32(&a_full[as]));
+          mbar_arrive(smem_u32(&raw_empty[rs]));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * ncols);
+  }
+}
+
+}  // namespace b2

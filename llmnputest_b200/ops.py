@@ -109,6 +109,62 @@ def q4_swiglu_gemv(gate: torch.Tensor, up: torch.Tensor, n_tile_rows: int, k_til
     return out if x.dim() == 2 else out[0, :n]
 
 
+def gemm_workspace_bytes(batch: int, k_tiles: int) -> int:
+    """Workspace of the tensor-core GEMM (staged fp16 x + exponents)."""
+    nb = ctypes.c_size_t(0)
+    _native.call("b2_q4_gemm_workspace_size", batch, k_tiles, ctypes.byref(nb))
+    return nb.value
+
+
+def _gemm_ws(workspace, batch: int, k_tiles: int, device) -> torch.Tensor:
+    need = gemm_workspace_bytes(batch, k_tiles)
+    if workspace is None:
+        return torch.empty(need + 256, dtype=torch.uint8, device=device)
+    if workspace.numel() < need or workspace.data_ptr() % 256:
+        raise ValueError(f"workspace must hold {need} bytes, 256-byte aligned")
+    return workspace
+
+
+def _aligned_ws(ws: torch.Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p((ws.data_ptr() + 255) // 256 * 256)
+
+
+def q4_gemm(tiles: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tensor, out: torch.Tensor | None = None,
+            accumulate: bool = False, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """fp32 y [B, N] = W x on the tcgen05 tensor cores (batches up to 256)."""
+    _tiles(tiles, n_tile_rows, k_tiles, Q4_TILE_BYTES, "tiles")
+    k, n = k_tiles * TILE_K, n_tile_rows * TILE_ROWS
+    x2 = _x2d(x, k)
+    b = x2.shape[0]
+    if out is None:
+        out = torch.zeros((b, n), dtype=torch.float32, device=x2.device)
+    _need(out, "out", torch.float32)
+    ws = _gemm_ws(workspace, b, k_tiles, x2.device)
+    _native.call("b2_q4_gemm", _ptr(tiles), n_tile_rows, k_tiles, _ptr(x2), b, x2.stride(0), _ptr(out),
+                 out.stride(0), GEMV_ACCUMULATE if accumulate else 0,
+                 _aligned_ws(ws) if workspace is None else _ptr(ws), ws.numel() - (256 if workspace is None else 0),
+                 _stream())
+    return out
+
+
+def q4_swiglu_gemm(gate: torch.Tensor, up: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tensor,
+                   out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16 h = silu(bf16(G x)) * bf16(U x) on the tensor cores (batches up to 256)."""
+    _tiles(gate, n_tile_rows, k_tiles, Q4_TILE_BYTES, "gate")
+    _tiles(up, n_tile_rows, k_tiles, Q4_TILE_BYTES, "up")
+    k, n = k_tiles * TILE_K, n_tile_rows * TILE_ROWS
+    x2 = _x2d(x, k)
+    b = x2.shape[0]
+    if out is None:
+        out = torch.empty((b, n), dtype=torch.bfloat16, device=x2.device)
+    _need(out, "out", torch.bfloat16)
+    ws = _gemm_ws(workspace, b, k_tiles, x2.device)
+    _native.call("b2_q4_swiglu_gemm", _ptr(gate), _ptr(up), n_tile_rows, k_tiles, _ptr(x2), b, x2.stride(0),
+                 _ptr(out), out.stride(0), 0, _aligned_ws(ws) if workspace is None else _ptr(ws),
+                 ws.numel() - (256 if workspace is None else 0), _stream())
+    return out
+
+
 def _norm_in(x: torch.Tensor, w: torch.Tensor, k: int) -> torch.Tensor:
     _need(x, "x", torch.float32)
     _need(w, "norm_w", torch.bfloat16)

@@ -1,0 +1,96 @@
+"""Tensor-core (tcgen05 / TMEM) W4A16 GEMM for large decode batches against the
+numpy oracle (tools/q4nx.py dequant + fp32 matmul, granite_gemv.py:256-272) and
+against the mma.sync GEMV on the same inputs.
+
+The weights reach the tensor core as fp16 (w = code*d + m rounded once), so the
+bar is the north-star tolerance: cosine >= 0.99999 and max rel <= 1e-3 per
+token, fp32 accumulation."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import q4nx_oracle as orc
+from tests.test_gpu_gemv import dev_bf16, dev_u8
+
+pytestmark = pytest.mark.gpu
+
+COS, REL = 0.99999, 1e-3
+
+
+@pytest.fixture(scope="module")
+def cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda", 0)
+
+
+def _check(got, ref, cos_min=COS, rel_max=REL, what=""):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    for b in range(ref.shape[0]):
+        cos, rel = orc.compare(got[b], ref[b])
+        assert cos >= cos_min and rel <= rel_max, (what, b, cos, rel)
+
+
+@pytest.mark.parametrize("n_t,k_t,bsz", [(4, 1, 17), (7, 3, 32), (12, 10, 100), (5, 2, 256), (4, 4, 1)])
+def test_gemm_vs_oracle(cuda, n_t, k_t, bsz):
+    from llmnputest_b200 import ops
+    rng = np.random.default_rng(1000 + n_t * 37 + k_t * 5 + bsz)
+    w = orc.synth_q4_tiles(rng, n_t * k_t)
+    x = orc.synth_bf16(rng, (bsz, k_t * 256)).astype(np.float32)
+    y = ops.q4_gemm(dev_u8(w), n_t, k_t, dev_bf16(x))
+    torch.cuda.synchronize()
+    ref = np.stack([orc.gemv_q4(w, x[b], n_t, k_t) for b in range(bsz)])
+    _check(y.cpu().numpy(), ref, what=(n_t, k_t, bsz))
+    assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("name,n_t,k_t", [("qkv", 112, 10), ("down", 80, 32)])
+@pytest.mark.parametrize("bsz", [32, 64])
+def test_gemm_matches_gemv_at_decode_shapes(cuda, name, n_t, k_t, bsz):
+    """Config-4 projection shapes at batch 32/64: same weights and x through the
+    GEMV (16 tokens per pass) and the tensor-core GEMM, plus accumulate mode."""
+    from llmnputest_b200 import ops
+    from llmnputest_b200.decode import synth_q4
+    g = torch.Generator(device=cuda)
+    g.manual_seed(n_t + bsz)
+    w = synth_q4(n_t * k_t, g, cuda)
+    x = torch.randn(bsz, k_t * 256, device=cuda, generator=g).to(torch.bfloat16)
+    ref = ops.q4_gemv(w, n_t, k_t, x)
+    y = ops.q4_gemm(w, n_t, k_t, x)
+    base = torch.randn(bsz, n_t * 32, device=cuda, generator=g)
+    acc = ops.q4_gemm(w, n_t, k_t, x, out=base.clone(), accumulate=True)
+    torch.cuda.synchronize()
+    _check(y.cpu().numpy(), ref.cpu().numpy(), what=name)
+    _check((acc - base).cpu().numpy(), ref.cpu().numpy(), what=(name, "acc"))
+    assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("n_t,k_t,bsz", [(8, 4, 32), (512, 10, 48)])
+def test_swiglu_gemm_matches_gemv(cuda, n_t, k_t, bsz):
+    """Fused gate/up + SiLU*up: both paths narrow g and u to bf16 before SiLU, so
+    an accumulator on a bf16 rounding boundary may land one bf16 ulp apart."""
+    from llmnputest_b200 import ops
+    from llmnputest_b200.decode import synth_q4
+    g = torch.Generator(device=cuda)
+    g.manual_seed(77 + bsz)
+    gate = synth_q4(n_t * k_t, g, cuda)
+    up = synth_q4(n_t * k_t, g, cuda)
+    x = torch.randn(bsz, k_t * 256, device=cuda, generator=g).to(torch.bfloat16)
+    ref = ops.q4_swiglu_gemv(gate, up, n_t, k_t, x)
+    h = ops.q4_swiglu_gemm(gate, up, n_t, k_t, x)
+    torch.cuda.synchronize()
+    _check(h.float().cpu().numpy(), ref.float().cpu().numpy(), 0.9999, 1e-2, "swiglu")
+    assert ops.device_error() == 0
+
+
+def test_gemm_argument_errors(cuda):
+    from llmnputest_b200 import _native, ops
+    w = torch.zeros(4 * 5120, dtype=torch.uint8, device=cuda)
+    x = torch.zeros(257, 256, dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(_native.B2Error):
+        ops.q4_gemm(w, 4, 1, x)  # batch above 256
+    small = torch.empty(256, dtype=torch.uint8, device=cuda)
+    with pytest.raises((_native.B2Error, ValueError)):
+        ops.q4_gemm(w, 4, 1, x[:32], workspace=small)
