@@ -14,7 +14,9 @@ per group of projections that share an input):
 then the final norm fused into the q8 lm_head (b2_q8_gemv_rmsnorm): five
 launches per layer.  The residual stream is
 fp32; GEMV inputs are bf16 as in the reference.  Weights are the raw q4nx tiles,
-resident on the device; the step is captured in one CUDA graph.
+resident on the device; the step is captured in one CUDA graph.  Batches of 9
+and more run the projections on the tcgen05 GEMM (b2_q4_gemm / _swiglu_gemm)
+after a separate RMSNorm launch.
 
 The reference never ran a granite token loop (README.md:299-301); this module
 is the composition its layer design estimates (granite_layer.py:158-164).
@@ -78,7 +80,7 @@ class Q4Decoder:
     """Resident weights, KV cache and buffers for batched decode; `step()` is graph-capturable."""
 
     def __init__(self, cfg: DecoderConfig, batch: int, ctx_max: int, device=None, seed: int = 0,
-                 weights: dict | None = None):
+                 weights: dict | None = None, gemm_min_batch: int = 9):
         self.cfg = cfg
         self.batch = batch
         self.ctx_max = ctx_max
@@ -110,6 +112,13 @@ class Q4Decoder:
         self.pos = torch.zeros(batch, dtype=torch.int32, device=dev)
         ws = ops.gqa_decode_workspace_bytes(batch, c.n_heads, c.n_kv_heads, c.head_dim, ctx_max)
         self.attn_ws = torch.empty(max(ws, 1), dtype=torch.uint8, device=dev)
+        # batches of gemm_min_batch and more run the projections on the tcgen05 GEMM
+        self.use_gemm = batch >= gemm_min_batch
+        if self.use_gemm:
+            nbytes = ops.gemm_workspace_bytes(batch, max(self.kt_h, self.kt_q, self.kt_i))
+            self.gemm_ws_raw = torch.empty(nbytes + 256, dtype=torch.uint8, device=dev)
+            off = (256 - self.gemm_ws_raw.data_ptr() % 256) % 256
+            self.gemm_ws = self.gemm_ws_raw[off:off + nbytes]
 
     def _synthetic(self, seed: int) -> dict:
         c, dev = self.cfg, self.device
@@ -141,6 +150,8 @@ class Q4Decoder:
         qd = c.n_heads * d
         kd = c.n_kv_heads * d
         self.resid.copy_(self.x_in)
+        if self.use_gemm:
+            return self._step_gemm()
         for li, L in enumerate(self.w["layers"]):
             ops.gemv_rmsnorm(L["qkv"], self.nt_qkv, self.kt_h, self.resid, L["attn_norm"], c.rms_eps, out=self.qkv,
                              prefetch=prefetch)
@@ -154,6 +165,27 @@ class Q4Decoder:
             ops.q4_gemv(L["down"], self.nt_h, self.kt_i, self.h, out=self.resid, accumulate=True, prefetch=prefetch)
         ops.gemv_rmsnorm(self.w["lm_head"], self.nt_v, self.kt_h, self.resid, self.w["final_norm"], c.rms_eps,
                          out=self.logits, prefetch=prefetch, q8=True)
+        return self.logits
+
+    def _step_gemm(self) -> torch.Tensor:
+        """Large-batch step: RMSNorm launches + tcgen05 GEMMs for every projection."""
+        c = self.cfg
+        d = c.head_dim
+        qd, kd = c.n_heads * d, c.n_kv_heads * d
+        ws = self.gemm_ws
+        for li, L in enumerate(self.w["layers"]):
+            ops.rmsnorm(self.resid, L["attn_norm"], c.rms_eps, out=self.xn)
+            ops.q4_gemm(L["qkv"], self.nt_qkv, self.kt_h, self.xn, out=self.qkv, workspace=ws)
+            ops.gqa_decode(self.qkv[:, :qd], self.qkv[:, qd:qd + kd], self.qkv[:, qd + kd:],
+                           self.k_cache[li], self.v_cache[li], self.pos, n_q_heads=c.n_heads,
+                           n_kv_heads=c.n_kv_heads, theta=c.rope_theta, scale=d ** -0.5, max_len=self.ctx_max,
+                           out=self.attn, workspace=self.attn_ws)
+            ops.q4_gemm(L["o"], self.nt_h, self.kt_q, self.attn, out=self.resid, accumulate=True, workspace=ws)
+            ops.rmsnorm(self.resid, L["mlp_norm"], c.rms_eps, out=self.xn)
+            ops.q4_swiglu_gemm(L["gate"], L["up"], self.nt_i, self.kt_h, self.xn, out=self.h, workspace=ws)
+            ops.q4_gemm(L["down"], self.nt_h, self.kt_i, self.h, out=self.resid, accumulate=True, workspace=ws)
+        ops.gemv_rmsnorm(self.w["lm_head"], self.nt_v, self.kt_h, self.resid, self.w["final_norm"], c.rms_eps,
+                         out=self.logits, q8=True)
         return self.logits
 
     # ------------------------------------------------------ persistent program

@@ -94,3 +94,35 @@ def test_gemm_argument_errors(cuda):
     small = torch.empty(256, dtype=torch.uint8, device=cuda)
     with pytest.raises((_native.B2Error, ValueError)):
         ops.q4_gemm(w, 4, 1, x[:32], workspace=small)
+
+
+@pytest.mark.parametrize("bsz,ctx", [(32, 512), (20, 300)])
+def test_decode_step_gemm_matches_gemv(cuda, bsz, ctx):
+    """A two-layer decode step at batch 20/32: projections on the tensor-core GEMM
+    against the same step on the GEMV path (same weights, caches and inputs)."""
+    from llmnputest_b200 import ops
+    from llmnputest_b200.decode import DecoderConfig, Q4Decoder
+    cfg = DecoderConfig(n_layers=2, vocab=2048)
+    a = Q4Decoder(cfg, bsz, ctx, seed=31, gemm_min_batch=10 ** 9)  # GEMV path
+    b = Q4Decoder(cfg, bsz, ctx, weights=a.w)
+    assert b.use_gemm and not a.use_gemm
+    g = torch.Generator(device=cuda)
+    g.manual_seed(9)
+    for li in range(cfg.n_layers):
+        kc = torch.randn(a.k_cache[li].shape, device=cuda, generator=g).to(torch.bfloat16)
+        vc = torch.randn(a.v_cache[li].shape, device=cuda, generator=g).to(torch.bfloat16)
+        for dec in (a, b):
+            dec.k_cache[li].copy_(kc)
+            dec.v_cache[li].copy_(vc)
+    pos = torch.randint(0, ctx - 2, (bsz,), device=cuda, generator=g, dtype=torch.int32)
+    for step in range(2):
+        x = torch.randn(bsz, cfg.hidden, device=cuda, generator=g)
+        for dec in (a, b):
+            dec.x_in.copy_(x)
+            dec.pos.copy_(pos)
+        la, lb = a.step().clone(), b.step().clone()
+        torch.cuda.synchronize()
+        # fp16 weights on one side, exact products on the other, re-rounded to bf16 between ops
+        _check(lb.cpu().numpy(), la.cpu().numpy(), 0.9999, 1e-2, ("step", step))
+        pos = pos + 1
+    assert ops.device_error() == 0
