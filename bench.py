@@ -41,9 +41,9 @@ LAYERS = 40
 def peaks() -> dict:
     try:
         p = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
-        return {"hbm_gbs": float(p["hbm_gbs"]), "src": "measured"}
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p.get("bf16_tflops", 1590.0)), "src": "measured"}
     except (OSError, KeyError, ValueError):
-        return {"hbm_gbs": 6650.0, "src": "fallback"}
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
 
 
 # ------------------------------------------------------------------- clocks
@@ -223,8 +223,47 @@ def time_graph(torch, g, steps: int, warmup: int) -> float:
     return a.elapsed_time(b) / steps  # ms per replay
 
 
-def measure_decode(torch, world: int, rank: int, batch: int, ctx: int, steps: int, warmup: int) -> dict:
-    """Config 4: the full 40-layer decode step at `batch` tokens, context `ctx`, TP over `world` ranks."""
+def measure_tc_gemm(torch, ops, gen, device, tensor_peak: float, steps: int) -> list:
+    """Tensor-core GEMM (b2_q4_gemm / b2_q4_swiglu_gemm): config-5 MLP shapes at batch 256
+    (hidden 1024, intermediate 3584) and config-4 projections at batch 32.  A weight
+    pool above L2 is rotated; algorithmic bytes = the q4 tiles, flops = 2*B*N*K."""
+    cases = [("c5_gate_up_swiglu", 112, 4, 256, True), ("c5_down", 32, 14, 256, False),
+             ("c4_qkv", 112, 10, 32, False), ("c4_gate_up_swiglu", 256, 10, 32, True), ("c4_down", 80, 32, 32, False)]
+    out = []
+    for name, n_t, k_t, bsz, swiglu in cases:
+        per = n_t * k_t * Q4_TILE * (2 if swiglu else 1)
+        pool = max(1, min(64, -(-300_000_000 // per)))
+        ws_ = [(make_q4_tiles(torch, n_t * k_t, gen, device), make_q4_tiles(torch, n_t * k_t, gen, device) if swiglu
+                else None) for _ in range(pool)]
+        x = torch.randn(bsz, k_t * 256, device=device, generator=gen).to(torch.bfloat16)
+        y = torch.empty(bsz, n_t * 32, device=device, dtype=torch.bfloat16 if swiglu else torch.float32)
+        nb = ops.gemm_workspace_bytes(bsz, k_t)
+        raw = torch.empty(nb + 256, dtype=torch.uint8, device=device)
+        wsb = raw[(256 - raw.data_ptr() % 256) % 256:][:nb]
+
+        def calls(ws_=ws_, x=x, y=y, wsb=wsb, n_t=n_t, k_t=k_t, swiglu=swiglu):
+            for g_, u_ in ws_:
+                if swiglu:
+                    ops.q4_swiglu_gemm(g_, u_, n_t, k_t, x, out=y, workspace=wsb)
+                else:
+                    ops.q4_gemm(g_, n_t, k_t, x, out=y, workspace=wsb)
+
+        g = graph_of(torch, calls)
+        t_ms = time_graph(torch, g, max(5, steps // 50), 3) / pool
+        flops = 2 * bsz * n_t * 32 * k_t * 256 * (2 if swiglu else 1)
+        out.append({"case": name, "batch": bsz, "us": round(t_ms * 1e3, 2), "gbs": round(per / (t_ms * 1e-3) / 1e9, 1),
+                    "tflops": round(flops / (t_ms * 1e-3) / 1e12, 1),
+                    "frac_of_measured_tensor": round(flops / (t_ms * 1e-3) / 1e12 / tensor_peak, 3)})
+        del g, ws_
+        torch.cuda.empty_cache()
+    return out
+
+
+def measure_decode(torch, world: int, rank: int, batch: int, ctx: int, steps: int, warmup: int,
+                   program: bool = False) -> dict:
+    """Config 4: the full 40-layer decode step at `batch` tokens, context `ctx`, TP over `world` ranks.
+
+    program=True (single GPU, batch <= 8): the persistent decode program + lm_head launch."""
     import torch.distributed as dist
     from llmnputest_b200.decode import GRANITE_3B, Q4Decoder
     from llmnputest_b200.tp import ShardPlan, TPDecoder, shard_weights
@@ -247,10 +286,13 @@ def measure_decode(torch, world: int, rank: int, batch: int, ctx: int, steps: in
         with torch.cuda.stream(s):
             dec.step()
         torch.cuda.current_stream().wait_stream(s)
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            dec.step()
-        run, how = g.replay, "cuda graph"
+        g = dec.capture(program=True) if program else None
+        if g is None:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                dec.step()
+        run, how = g.replay, ("persistent program, cuda graph" if program else
+                              ("tcgen05 GEMM, cuda graph" if getattr(dec, "use_gemm", False) else "cuda graph"))
     except Exception as e:  # capture of the collectives failed: time the eager step instead
         torch.cuda.synchronize()
         run, how = dec.step, f"eager ({type(e).__name__})"
@@ -273,7 +315,7 @@ def measure_decode(torch, world: int, rank: int, batch: int, ctx: int, steps: in
     wb = cfg.weight_bytes()
     kv = batch * ctx * cfg.n_kv_heads * cfg.head_dim * 4 * cfg.n_layers
     step_bytes = wb["layers"] + wb["lm_head"] + kv  # algorithmic: every weight and KV byte once
-    out = {"batch": batch, "ctx": ctx, "tp": world, "ms_per_step": round(ms, 4),
+    out = {"batch": batch, "ctx": ctx, "tp": world, "ms_per_step": round(ms, 4), "program": program,
            "tok_s": round(batch / (ms * 1e-3), 1), "how": how,
            "hbm_gbs_per_gpu": round(step_bytes / world / (ms * 1e-3) / 1e9, 1)}
     del dec
@@ -390,12 +432,16 @@ def run_b200(args, rank: int, world: int) -> dict | None:
                                 "frac_of_measured_hbm": round(w8.numel() / (tl * 1e-3) / 1e9 / pk["hbm_gbs"], 3)}
         del gl, w8
         extras["attention"] = measure_attention(torch, ops, gen, device, pk["hbm_gbs"], args.steps)
+        extras["tc_gemm"] = measure_tc_gemm(torch, ops, gen, device, pk["bf16_tflops"], args.steps)
 
     # ---- config 4: the full decode step (tensor-parallel across the ranks when N > 1)
     if not args.quick:
         del g
         extras["decode"] = [measure_decode(torch, world, rank, b, 4096, max(10, args.steps // 30), 3)
-                            for b in (1, 32)]
+                            for b in (1, 8, 32)]
+        if world == 1:
+            extras["decode"] += [measure_decode(torch, world, rank, b, 4096, max(10, args.steps // 30), 3,
+                                                program=True) for b in (1, 8)]
 
     # ---- e2e: host buffers, copies inside the timed region
     xs_host = torch.cat([c[4].reshape(-1) for c in calls]).cpu().pin_memory()
