@@ -497,15 +497,6 @@ __device__ __forceinline__ void prog_gemv_phase(const ProgParams& p, const ProgP
 // each lane's 8-row group), stage phase ph = w >> 2 (stages with seq % 3 == ph).
 constexpr int kB1Phases = kProgWarps / 4;
 
-__device__ __forceinline__ void decode_q4_half_bf16(uint32_t w1, uint32_t w2, uint32_t sel, uint32_t (&a)[4]) {
-  constexpr uint32_t kMagic = 0x43004300u;  // bf16x2 (128, 128): n | magic = 128 + n
-  const uint32_t r = prmt(w1, w2, sel);     // 4 rows at (k_a, k_b)
-  a[0] = lop3<kLutAndOr>(r, 0x000F000Fu, kMagic);
-  a[1] = lop3<kLutAndOr>(r >> 4, 0x000F000Fu, kMagic);
-  a[2] = lop3<kLutAndOr>(r >> 8, 0x000F000Fu, kMagic);
-  a[3] = lop3<kLutAndOr>(r >> 12, 0x000F000Fu, kMagic);
-}
-
 __device__ __forceinline__ void prog_gemv_phase_b1(const ProgPhase& P, uint8_t* smem, const ProgSmem& L,
                                                    uint64_t* bars, volatile int* abort_flag, int stages,
                                                    uint32_t& seq, uint32_t& unit_seq) {

@@ -173,6 +173,18 @@ __device__ __forceinline__ void decode_q8_res(uint32_t res, uint32_t& lo0, uint3
   hi1 = lop3<kLutAndXor>(rs, 0x00F000F0u, kMagicFlip);
 }
 
+// q4 nibbles of 4 rows at (k_a, k_b) -> bf16x2 codes 128 + n (exact, no subtract:
+// the offset folds into the m term).  r = PRMT of the two k words; bf16 has 7
+// mantissa bits, so each nibble is shifted to bits 0-3 first.
+__device__ __forceinline__ void decode_q4_half_bf16(uint32_t w1, uint32_t w2, uint32_t sel, uint32_t (&a)[4]) {
+  constexpr uint32_t kMagic = 0x43004300u;  // bf16x2 (128, 128): n | magic = 128 + n
+  const uint32_t r = prmt(w1, w2, sel);
+  a[0] = lop3<kLutAndOr>(r, 0x000F000Fu, kMagic);
+  a[1] = lop3<kLutAndOr>(r >> 4, 0x000F000Fu, kMagic);
+  a[2] = lop3<kLutAndOr>(r >> 8, 0x000F000Fu, kMagic);
+  a[3] = lop3<kLutAndOr>(r >> 12, 0x000F000Fu, kMagic);
+}
+
 template <int QT, int NB, int EPI>
 __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kernel(const GemvParams p) {
   constexpr int TILE = QTraits<QT>::kTile;
@@ -207,11 +219,18 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
   // the owning rank's shared memory and summed after one cluster barrier.
   // Clustered launches always give each CTA exactly one group.
   const int cl_mode = !clustered ? 0 : (EPI == kEpiSwiglu ? 2 : (p.accumulate ? 0 : 1));
+  // Batch 1 (q4): each 32-k block of a K-tile gets its own MMA column (x in
+  // column j, zero elsewhere), so one accumulator holds the eight block sums and
+  // the d/m fold runs once per K-tile instead of once per block; x stays bf16
+  // (codes 128 + n, exact in bf16; the offset folds into m).  Warps split a
+  // stage by (row-block, rows half) and take alternate stages.
+  constexpr bool kB1able = (QT == kQ4 && NB == 1);
+  const bool b1 = kB1able && batch == 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(smem_u32(&bars[s]), 1);                             // full: producer + tx
-      mbar_init(smem_u32(&bars[stages + s]), kGemvConsumerWarps);  // empty: one per warp
+      mbar_init(smem_u32(&bars[stages + s]), b1 ? 4 : kGemvConsumerWarps);  // empty: one per consuming warp
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -350,11 +369,17 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
       float s8 = 0.f;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const __half2 hv = __floats2half2_rn(bf16lo_to_f32(w[i]) * sc, bf16hi_to_f32(w[i]) * sc);
-        o[i] = *reinterpret_cast<const uint32_t*>(&hv);
-        const float2 f = __half22float2(hv);
-        s8 += f.x;
-        s8 += f.y;
+        if (b1) {  // bf16 kept as is
+          o[i] = w[i];
+          s8 += bf16lo_to_f32(w[i]);
+          s8 += bf16hi_to_f32(w[i]);
+        } else {
+          const __half2 hv = __floats2half2_rn(bf16lo_to_f32(w[i]) * sc, bf16hi_to_f32(w[i]) * sc);
+          o[i] = *reinterpret_cast<const uint32_t*>(&hv);
+          const float2 f = __half22float2(hv);
+          s8 += f.x;
+          s8 += f.y;
+        }
       }
       *reinterpret_cast<uint4*>(x_s + b * p.x_stride + c * 8) = make_uint4(o[0], o[1], o[2], o[3]);
       s8 += __shfl_xor_sync(0xffffffffu, s8, 1);
@@ -377,7 +402,7 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
         mx = warp_max(mx);
         const int e = gemv_scale_exp(__float_as_uint(mx));
         const float sc = pow2f(e);
-        if (warp == 0 && lane == 0) exps[b] = e;
+        if (warp == 0 && lane == 0) exps[b] = b1 ? 0 : e;
 #pragma unroll
         for (int i = 0; i < kVecLane; ++i)
           if (32 * i < vec_per_row && (i % kGemvConsumerWarps) == warp) put(b, lane + 32 * i, v[i], sc);
@@ -387,7 +412,7 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
         mx = warp_max(mx);
         const int e = gemv_scale_exp(__float_as_uint(mx));
         const float sc = pow2f(e);
-        if (warp == 0 && lane == 0) exps[b] = e;
+        if (warp == 0 && lane == 0) exps[b] = b1 ? 0 : e;
         for (int c = warp * 32 + lane; c < vec_per_row; c += kGemvConsumers) put(b, c, xvec(b, c), sc);
       }
     }
@@ -409,6 +434,89 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
 
   uint32_t seq = 0;
   for (int grp = blockIdx.y; grp < p.n_groups; grp += gridDim.y) {
+    if (kB1able && b1) {
+      const int sh = (warp >> 1) & 1, phs = warp >> 2;
+      const uint32_t sel = sh ? sel_hi : sel_lo;
+      float tb[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+      const uint32_t seq0 = seq;
+      for (int kk = 0; kk < kt_cnt; ++kk) {
+        const uint32_t sq = seq0 + kk;
+        if (static_cast<int>(sq & 1) != phs) continue;
+        const int slot = sq % stages;
+        mbar_wait_bounded(smem_u32(&bars[slot]), (sq / stages) & 1, abort_flag, kDevTimeoutFull);
+        const uint8_t* tl = ring + slot * STAGE + tile * SLOT;
+        uint32_t xw[2][2];
+#pragma unroll
+        for (int st = 0; st < 2; ++st) {
+          const uint32_t* xr = x32 + (kk * 256 + g * 32 + st * 16) / 2 + t;
+          xw[st][0] = xr[0];
+          xw[st][1] = xr[4];
+        }
+        float acc[2][4];
+#pragma unroll
+        for (int s = 0; s < 2; ++s) acc[s][0] = acc[s][1] = acc[s][2] = acc[s][3] = 0.f;
+#pragma unroll
+        for (int kblk = 0; kblk < 8; ++kblk) {
+          const bool mine = g == kblk;
+#pragma unroll
+          for (int st = 0; st < 2; ++st) {
+            const uint8_t* nb = tl + 1024 + rb * 2048 + kblk * 256 + st * 128 + 16 * t + 4 * h;
+            const uint32_t p1 = *reinterpret_cast<const uint32_t*>(nb + off_first);
+            const uint32_t p2 = *reinterpret_cast<const uint32_t*>(nb + off_second);
+            const uint32_t q1 = *reinterpret_cast<const uint32_t*>(nb + 64 + off_first);
+            const uint32_t q2 = *reinterpret_cast<const uint32_t*>(nb + 64 + off_second);
+            uint32_t aP[4], aQ[4];
+            decode_q4_half_bf16(p1, p2, sel, aP);
+            decode_q4_half_bf16(q1, q2, sel, aQ);
+            const uint32_t b0 = mine ? xw[st][0] : 0u, b1v = mine ? xw[st][1] : 0u;
+#pragma unroll
+            for (int s = 0; s < 2; ++s)
+              mma_bf16_m16n8k16(acc[s][0], acc[s][1], acc[s][2], acc[s][3], aP[2 * s], aP[2 * s + 1], aQ[2 * s],
+                                aQ[2 * s + 1], b0, b1v);
+          }
+        }
+        // fold columns 2t, 2t+1 (blocks 2t + c): rows 4sh + 2s (c0, c1) and 4sh + 2s + 1 (c2, c3)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int kbl = 2 * t + c;
+          const uint8_t* meta = tl + (kbl * 32 + rb * 16 + h * 8 + 4 * sh) * 2;
+          const uint2 dv = *reinterpret_cast<const uint2*>(meta);
+          const uint2 mv = *reinterpret_cast<const uint2*>(meta + 512);
+          const float sx = xs_s[(kk * 8 + kbl) * 8];
+          const uint32_t dw[2] = {dv.x, dv.y}, mw[2] = {mv.x, mv.y};
+#pragma unroll
+          for (int s = 0; s < 2; ++s) {
+            const float da = bf16lo_to_f32(dw[s]), db = bf16hi_to_f32(dw[s]);
+            const float ma = fmaf(-128.f, da, bf16lo_to_f32(mw[s]));
+            const float mb = fmaf(-128.f, db, bf16hi_to_f32(mw[s]));
+            tb[s][0] = fmaf(da, acc[s][c], fmaf(ma, sx, tb[s][0]));
+            tb[s][1] = fmaf(db, acc[s][2 + c], fmaf(mb, sx, tb[s][1]));
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&bars[stages + slot]));
+      }
+      seq = seq0 + kt_cnt;
+      // sum the four t lanes (their block columns); park this warp's rows and zeros
+      // for the other half, so the shared reduction below sums the right warps
+#pragma unroll
+      for (int s = 0; s < 2; ++s)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          tb[s][e] += __shfl_xor_sync(0xffffffffu, tb[s][e], 1);
+          tb[s][e] += __shfl_xor_sync(0xffffffffu, tb[s][e], 2);
+        }
+      if (t == 0) {
+        float* rw = red + warp * 64 * ncol;
+#pragma unroll
+        for (int s = 0; s < 2; ++s)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            rw[(tile * 16 + h * 8 + 4 * sh + 2 * s + e) * ncol] = tb[s][e];
+            rw[(tile * 16 + h * 8 + 4 * (1 - sh) + 2 * s + e) * ncol] = 0.f;
+          }
+      }
+    } else {
     float tot[4][4 * NB];
 #pragma unroll
     for (int s = 0; s < 4; ++s)
@@ -544,6 +652,7 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
         }
       }
     }
+    }  // batch-1 / general stage loop
     named_barrier(1, kGemvConsumers);
     // CTA sum over the 4 warps that hold each row (fixed order).
     const int nsp = p.n_splits;
