@@ -114,7 +114,7 @@ struct GemvSmem {
     misc = gather + 160 * ncol * 4;         // [kMaxBatch] max bits, [kMaxBatch] exponents
     bar = misc + 2 * kMaxBatch * 4;
     bar = (bar + 15) & ~15;
-    flag = bar + 2 * stages * 8;
+    flag = bar + (2 * stages + 1) * 8;  // full[stages], empty[stages], x
     total = flag + 16;
   }
 };
@@ -226,12 +226,16 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
   // stage by (row-block, rows half) and take alternate stages.
   constexpr bool kB1able = (QT == kQ4 && NB == 1);
   const bool b1 = kB1able && batch == 1;
+  // batch 1 without the fused norm: x needs no conversion, so the producer copies
+  // the K slice into shared memory right after its PDL wait (one bulk copy)
+  const bool x_bulk = b1 && !p.xf;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(smem_u32(&bars[s]), 1);                             // full: producer + tx
       mbar_init(smem_u32(&bars[stages + s]), b1 ? 4 : kGemvConsumerWarps);  // empty: one per consuming warp
     }
+    mbar_init(smem_u32(&bars[2 * stages]), 1);  // x slice
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -243,11 +247,23 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
     // ------------------------------------------------------------ producer
     if (cl_mode == 1) cluster_arrive_release();
     const uint64_t policy = l2_evict_first_policy();
+    // after the PDL wait x is final: copy this CTA's K slice (batch 1, no norm)
+    auto wait_and_copy_x = [&]() {
+      pdl_wait();
+      if (x_bulk && lane == 0) {
+        const uint32_t xb = smem_u32(&bars[2 * stages]);
+        mbar_arrive_expect_tx(xb, static_cast<uint32_t>(kt_cnt) * 512);
+        bulk_g2s(smem_u32(x_s), p.x + static_cast<size_t>(kt0) * 256, static_cast<uint32_t>(kt_cnt) * 512, xb,
+                 l2_evict_last_policy());
+      }
+    };
     uint32_t seq = 0;
     bool waited_pdl = false;
     if (!p.prefetch_before_wait) {
-      pdl_wait();
+      wait_and_copy_x();
       waited_pdl = true;
+    } else if (x_bulk && lane == 0) {
+      bulk_prefetch_l2(p.x + static_cast<size_t>(kt0) * 256, static_cast<uint32_t>(kt_cnt) * 512);  // L2 only
     }
     for (int grp = blockIdx.y; grp < p.n_groups; grp += gridDim.y) {
       for (int kk = 0; kk < kt_cnt; ++kk, ++seq) {
@@ -257,7 +273,7 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
           bool ok = true;
           if (seq >= static_cast<uint32_t>(stages)) {
             if (!waited_pdl) {  // ring full: nothing more to prefetch before the dependency
-              pdl_wait();
+              wait_and_copy_x();
               waited_pdl = true;
             }
             ok = mbar_wait_bounded(smem_u32(&bars[stages + slot]), ph ^ 1, abort_flag, kDevTimeoutEmpty);
@@ -291,10 +307,21 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
       }
       __syncwarp();
     }
-    if (!waited_pdl) pdl_wait();
+    __syncwarp();
+    if (!waited_pdl) wait_and_copy_x();  // issues the x copy if the loop did not
     __syncwarp();
     if (cl_mode == 1) cluster_wait_acquire();  // mirror the consumers' barrier phases
     if (cl_mode == 2) cluster_sync_all();
+    if (lane == 0 && *abort_flag && x_bulk) {
+      // lane 0 has issued the x copy by now, right after its PDL wait
+      const uint64_t t0 = globaltimer();
+      while (!mbar_try_wait(smem_u32(&bars[2 * stages]), 0)) {
+        if (globaltimer() - t0 > B2_WAIT_TIMEOUT_NS) {
+          record_error(kDevTimeoutDrain);
+          break;
+        }
+      }
+    }
     if (lane == 0 && *abort_flag) {
       // abort path: let every copy this CTA issued land before the CTA exits
       const uint32_t first = seq > static_cast<uint32_t>(stages) ? seq - stages : 0;
@@ -327,7 +354,7 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
     cluster_arrive_release();
   }
   const int L_cta = kt_cnt * 256;
-  {
+  if (!x_bulk) {
     // x rows as bf16: given (p.x), or bf16(rmsnorm(p.xf) * norm_w) computed here
     // (the norm fused into the GEMV, granite_rmsnorm.h:45-80 arithmetic).
     const int vec_per_row = L_cta / 8;  // 16-byte vectors of 8 values, a multiple of 32
@@ -432,6 +459,7 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
   const uint32_t* x32 = reinterpret_cast<const uint32_t*>(x_s);
   const int xw_stride = p.x_stride / 2;
 
+  if (x_bulk) mbar_wait_bounded(smem_u32(&bars[2 * stages]), 0, abort_flag, kDevTimeoutFull);
   uint32_t seq = 0;
   for (int grp = blockIdx.y; grp < p.n_groups; grp += gridDim.y) {
     if (kB1able && b1) {
@@ -446,12 +474,17 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
         mbar_wait_bounded(smem_u32(&bars[slot]), (sq / stages) & 1, abort_flag, kDevTimeoutFull);
         const uint8_t* tl = ring + slot * STAGE + tile * SLOT;
         uint32_t xw[2][2];
+        float bsum = 0.f;  // this lane's 8 x of block g; the 4 t lanes hold all 32
 #pragma unroll
         for (int st = 0; st < 2; ++st) {
           const uint32_t* xr = x32 + (kk * 256 + g * 32 + st * 16) / 2 + t;
           xw[st][0] = xr[0];
           xw[st][1] = xr[4];
+          bsum += (bf16lo_to_f32(xw[st][0]) + bf16hi_to_f32(xw[st][0])) +
+                  (bf16lo_to_f32(xw[st][1]) + bf16hi_to_f32(xw[st][1]));
         }
+        bsum += __shfl_xor_sync(0xffffffffu, bsum, 1);
+        bsum += __shfl_xor_sync(0xffffffffu, bsum, 2);  // sum of block g
         float acc[2][4];
 #pragma unroll
         for (int s = 0; s < 2; ++s) acc[s][0] = acc[s][1] = acc[s][2] = acc[s][3] = 0.f;
@@ -482,7 +515,7 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
           const uint8_t* meta = tl + (kbl * 32 + rb * 16 + h * 8 + 4 * sh) * 2;
           const uint2 dv = *reinterpret_cast<const uint2*>(meta);
           const uint2 mv = *reinterpret_cast<const uint2*>(meta + 512);
-          const float sx = xs_s[(kk * 8 + kbl) * 8];
+          const float sx = __shfl_sync(0xffffffffu, bsum, kbl * 4);
           const uint32_t dw[2] = {dv.x, dv.y}, mw[2] = {mv.x, mv.y};
 #pragma unroll
           for (int s = 0; s < 2; ++s) {
