@@ -161,6 +161,23 @@ __device__ __forceinline__ void decode_q4_pair(uint32_t w1, uint32_t w2, uint32_
   a[7] = f16x2_sub(lop3<kLutAndOr>(r1s, 0x00F000F0u, kHiMagic), kHiMagic);
 }
 
+// As decode_q4_pair without the subtract: even rows come out as 1024 + n, odd
+// rows as 64 + n (both exact in f16); the caller folds the offsets.
+__device__ __forceinline__ void decode_q4_pair_biased(uint32_t w1, uint32_t w2, uint32_t sel_lo, uint32_t sel_hi,
+                                                      uint32_t (&a)[8]) {
+  constexpr uint32_t kLoMagic = 0x64006400u, kHiMagic = 0x54005400u;
+  const uint32_t r0 = prmt(w1, w2, sel_lo), r1 = prmt(w1, w2, sel_hi);
+  const uint32_t r0s = r0 >> 8, r1s = r1 >> 8;
+  a[0] = lop3<kLutAndOr>(r0, 0x000F000Fu, kLoMagic);
+  a[1] = lop3<kLutAndOr>(r0, 0x00F000F0u, kHiMagic);
+  a[2] = lop3<kLutAndOr>(r0s, 0x000F000Fu, kLoMagic);
+  a[3] = lop3<kLutAndOr>(r0s, 0x00F000F0u, kHiMagic);
+  a[4] = lop3<kLutAndOr>(r1, 0x000F000Fu, kLoMagic);
+  a[5] = lop3<kLutAndOr>(r1, 0x00F000F0u, kHiMagic);
+  a[6] = lop3<kLutAndOr>(r1s, 0x000F000Fu, kLoMagic);
+  a[7] = lop3<kLutAndOr>(r1s, 0x00F000F0u, kHiMagic);
+}
+
 // q8: two rows (bytes 0 and 1 of a PRMT result) -> (1024+ul) and (1024+16*uh) per row.
 __device__ __forceinline__ void decode_q8_res(uint32_t res, uint32_t& lo0, uint32_t& hi0, uint32_t& lo1,
                                               uint32_t& hi1) {
@@ -221,9 +238,8 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
   const int cl_mode = !clustered ? 0 : (EPI == kEpiSwiglu ? 2 : (p.accumulate ? 0 : 1));
   // Batch 1 (q4): each 32-k block of a K-tile gets its own MMA column (x in
   // column j, zero elsewhere), so one accumulator holds the eight block sums and
-  // the d/m fold runs once per K-tile instead of once per block; x stays bf16
-  // (codes 128 + n, exact in bf16; the offset folds into m).  Warps split a
-  // stage by (row-block, rows half) and take alternate stages.
+  // the d/m fold runs once per K-tile instead of once per block.  Warps split a
+  // stage by (row block, half of the k-blocks) and take alternate stages.
   constexpr bool kB1able = (QT == kQ4 && NB == 1);
   const bool b1 = kB1able && batch == 1;
   // batch 1 without the fused norm: x needs no conversion, so the producer copies
@@ -460,80 +476,119 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
   const int xw_stride = p.x_stride / 2;
 
   if (x_bulk) mbar_wait_bounded(smem_u32(&bars[2 * stages]), 0, abort_flag, kDevTimeoutFull);
+  if (b1) {
+    // x (bf16, this CTA's K slice) -> f16 in place, scaled per 32-k block by 2^e
+    // (exact: bf16's 8-bit mantissa fits f16's 11), with the block's sum of x and
+    // 2^-e beside it: xs_s[block * 8 + 0 / 1].  Four lanes hold one block.
+    uint4* xv = reinterpret_cast<uint4*>(x_s);
+    for (int v = ctid; v < kt_cnt * 32; v += kGemvConsumers) {  // warp-uniform trip count
+      const uint4 u = xv[v];
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+      float f[8], mx = 0.f, sm = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        f[2 * i] = bf16lo_to_f32(w[i]);
+        f[2 * i + 1] = bf16hi_to_f32(w[i]);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        mx = fmaxf(mx, fabsf(f[i]));
+        sm += f[i];
+      }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+      sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+      const int e = gemv_scale_exp(__float_as_uint(mx));
+      const float sc = pow2f(e);
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __half2 hv = __floats2half2_rn(f[2 * i] * sc, f[2 * i + 1] * sc);
+        o[i] = *reinterpret_cast<const uint32_t*>(&hv);
+      }
+      xv[v] = make_uint4(o[0], o[1], o[2], o[3]);
+      if ((lane & 3) == 0) {
+        xs_s[(v >> 2) * 8] = sm;
+        xs_s[(v >> 2) * 8 + 1] = pow2f(-e);
+      }
+    }
+    named_barrier(1, kGemvConsumers);
+  }
   uint32_t seq = 0;
   for (int grp = blockIdx.y; grp < p.n_groups; grp += gridDim.y) {
     if (kB1able && b1) {
-      const int sh = (warp >> 1) & 1, phs = warp >> 2;
-      const uint32_t sel = sh ? sel_hi : sel_lo;
-      float tb[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+      // warp = (row block rb, k-block half kh, stage parity phs): 4 warps share a
+      // stage.  Block 4*kh + j of a K-tile goes to MMA column 2*j + kh, so lane t
+      // folds exactly one block (4*kh + t) and lanes with g = 2*j + kh feed B.
+      const int kh = (warp >> 1) & 1, phs = warp >> 2;
+      const int xblk = 4 * kh + (g >> 1);  // the block whose x this lane feeds
+      float tb[4][2];
+#pragma unroll
+      for (int s = 0; s < 4; ++s) tb[s][0] = tb[s][1] = 0.f;
       const uint32_t seq0 = seq;
       for (int kk = 0; kk < kt_cnt; ++kk) {
         const uint32_t sq = seq0 + kk;
         if (static_cast<int>(sq & 1) != phs) continue;
         const int slot = sq % stages;
-        mbar_wait_bounded(smem_u32(&bars[slot]), (sq / stages) & 1, abort_flag, kDevTimeoutFull);
-        const uint8_t* tl = ring + slot * STAGE + tile * SLOT;
         uint32_t xw[2][2];
-        float bsum = 0.f;  // this lane's 8 x of block g; the 4 t lanes hold all 32
 #pragma unroll
         for (int st = 0; st < 2; ++st) {
-          const uint32_t* xr = x32 + (kk * 256 + g * 32 + st * 16) / 2 + t;
+          const uint32_t* xr = x32 + (kk * 256 + xblk * 32 + st * 16) / 2 + t;
           xw[st][0] = xr[0];
           xw[st][1] = xr[4];
-          bsum += (bf16lo_to_f32(xw[st][0]) + bf16hi_to_f32(xw[st][0])) +
-                  (bf16lo_to_f32(xw[st][1]) + bf16hi_to_f32(xw[st][1]));
         }
-        bsum += __shfl_xor_sync(0xffffffffu, bsum, 1);
-        bsum += __shfl_xor_sync(0xffffffffu, bsum, 2);  // sum of block g
-        float acc[2][4];
+        mbar_wait_bounded(smem_u32(&bars[slot]), (sq / stages) & 1, abort_flag, kDevTimeoutFull);
+        const uint8_t* tl = ring + slot * STAGE + tile * SLOT;
+        float acc[4][4];
 #pragma unroll
-        for (int s = 0; s < 2; ++s) acc[s][0] = acc[s][1] = acc[s][2] = acc[s][3] = 0.f;
+        for (int s = 0; s < 4; ++s) acc[s][0] = acc[s][1] = acc[s][2] = acc[s][3] = 0.f;
 #pragma unroll
-        for (int kblk = 0; kblk < 8; ++kblk) {
-          const bool mine = g == kblk;
+        for (int j = 0; j < 4; ++j) {
+          const uint8_t* nbj = tl + 1024 + rb * 2048 + (4 * kh + j) * 256 + 16 * t + 4 * h;
+          const bool mine = g == 2 * j + kh;
 #pragma unroll
           for (int st = 0; st < 2; ++st) {
-            const uint8_t* nb = tl + 1024 + rb * 2048 + kblk * 256 + st * 128 + 16 * t + 4 * h;
+            const uint8_t* nb = nbj + st * 128;
             const uint32_t p1 = *reinterpret_cast<const uint32_t*>(nb + off_first);
             const uint32_t p2 = *reinterpret_cast<const uint32_t*>(nb + off_second);
             const uint32_t q1 = *reinterpret_cast<const uint32_t*>(nb + 64 + off_first);
             const uint32_t q2 = *reinterpret_cast<const uint32_t*>(nb + 64 + off_second);
-            uint32_t aP[4], aQ[4];
-            decode_q4_half_bf16(p1, p2, sel, aP);
-            decode_q4_half_bf16(q1, q2, sel, aQ);
+            uint32_t aP[8], aQ[8];
+            decode_q4_pair_biased(p1, p2, sel_lo, sel_hi, aP);
+            decode_q4_pair_biased(q1, q2, sel_lo, sel_hi, aQ);
             const uint32_t b0 = mine ? xw[st][0] : 0u, b1v = mine ? xw[st][1] : 0u;
 #pragma unroll
-            for (int s = 0; s < 2; ++s)
-              mma_bf16_m16n8k16(acc[s][0], acc[s][1], acc[s][2], acc[s][3], aP[2 * s], aP[2 * s + 1], aQ[2 * s],
-                                aQ[2 * s + 1], b0, b1v);
+            for (int s = 0; s < 4; ++s)
+              mma_f16_m16n8k16(acc[s][0], acc[s][1], acc[s][2], acc[s][3], aP[2 * s], aP[2 * s + 1], aQ[2 * s],
+                               aQ[2 * s + 1], b0, b1v);
           }
         }
-        // fold columns 2t, 2t+1 (blocks 2t + c): rows 4sh + 2s (c0, c1) and 4sh + 2s + 1 (c2, c3)
+        // fold block 4*kh + t (column 2t + kh): rows 2s (c0/c1) and 2s + 1 (c2/c3)
+        // of the lane's 8.  Codes carry +1024 (even rows) / +64 (odd rows):
+        // y += d * 2^-e * acc + (m - off * d) * sum(x)
+        {
+          const int kbl = 4 * kh + t;
+          const uint8_t* meta = tl + (kbl * 32 + rb * 16 + h * 8) * 2;
+          const uint4 dv = *reinterpret_cast<const uint4*>(meta);
+          const uint4 mv = *reinterpret_cast<const uint4*>(meta + 512);
+          const float2 si = *reinterpret_cast<const float2*>(xs_s + (kk * 8 + kbl) * 8);  // sum, 2^-e
+          const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w}, mw[4] = {mv.x, mv.y, mv.z, mv.w};
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const int kbl = 2 * t + c;
-          const uint8_t* meta = tl + (kbl * 32 + rb * 16 + h * 8 + 4 * sh) * 2;
-          const uint2 dv = *reinterpret_cast<const uint2*>(meta);
-          const uint2 mv = *reinterpret_cast<const uint2*>(meta + 512);
-          const float sx = __shfl_sync(0xffffffffu, bsum, kbl * 4);
-          const uint32_t dw[2] = {dv.x, dv.y}, mw[2] = {mv.x, mv.y};
-#pragma unroll
-          for (int s = 0; s < 2; ++s) {
+          for (int s = 0; s < 4; ++s) {
             const float da = bf16lo_to_f32(dw[s]), db = bf16hi_to_f32(dw[s]);
-            const float ma = fmaf(-128.f, da, bf16lo_to_f32(mw[s]));
-            const float mb = fmaf(-128.f, db, bf16hi_to_f32(mw[s]));
-            tb[s][0] = fmaf(da, acc[s][c], fmaf(ma, sx, tb[s][0]));
-            tb[s][1] = fmaf(db, acc[s][2 + c], fmaf(mb, sx, tb[s][1]));
+            const float ca = kh ? acc[s][1] : acc[s][0], cb = kh ? acc[s][3] : acc[s][2];
+            tb[s][0] = fmaf(da * si.y, ca, fmaf(fmaf(-1024.f, da, bf16lo_to_f32(mw[s])), si.x, tb[s][0]));
+            tb[s][1] = fmaf(db * si.y, cb, fmaf(fmaf(-64.f, db, bf16hi_to_f32(mw[s])), si.x, tb[s][1]));
           }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&bars[stages + slot]));
       }
       seq = seq0 + kt_cnt;
-      // sum the four t lanes (their block columns); park this warp's rows and zeros
-      // for the other half, so the shared reduction below sums the right warps
+      // sum the four t lanes (their blocks) and park this warp's 8 rows per lane
 #pragma unroll
-      for (int s = 0; s < 2; ++s)
+      for (int s = 0; s < 4; ++s)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           tb[s][e] += __shfl_xor_sync(0xffffffffu, tb[s][e], 1);
@@ -542,12 +597,9 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
       if (t == 0) {
         float* rw = red + warp * 64 * ncol;
 #pragma unroll
-        for (int s = 0; s < 2; ++s)
+        for (int s = 0; s < 4; ++s)
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            rw[(tile * 16 + h * 8 + 4 * sh + 2 * s + e) * ncol] = tb[s][e];
-            rw[(tile * 16 + h * 8 + 4 * (1 - sh) + 2 * s + e) * ncol] = 0.f;
-          }
+          for (int e = 0; e < 2; ++e) rw[(tile * 16 + h * 8 + 2 * s + e) * ncol] = tb[s][e];
       }
     } else {
     float tot[4][4 * NB];
