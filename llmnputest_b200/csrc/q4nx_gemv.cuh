@@ -230,9 +230,10 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
   const int kt0 = split * p.kt_per_split;
   const int kt_cnt = min(p.kt_per_split, p.k_tiles - kt0);  // >= 1 by construction
   // cluster protocol (split-K).  f32: partials are added into y with global
-  // reductions; unless y is accumulated into, rank 0 first zeroes the group's
-  // rows and arrives on a cluster barrier that the others only wait on just
-  // before their adds (long complete by then).  SwiGLU: partials are pushed to
+  // reductions; unless y is accumulated into, rank 0's producer warp zeroes the
+  // group's rows once its loads are issued (after its PDL wait) and arrives on a
+  // cluster barrier that the consumers only wait on just before their adds, so
+  // the zeroing stays off the consumers' path.  SwiGLU: partials are pushed to
   // the owning rank's shared memory and summed after one cluster barrier.
   // Clustered launches always give each CTA exactly one group.
   const int cl_mode = !clustered ? 0 : (EPI == kEpiSwiglu ? 2 : (p.accumulate ? 0 : 1));
@@ -261,16 +262,31 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
 
   if (warp == kGemvConsumerWarps) {
     // ------------------------------------------------------------ producer
-    if (cl_mode == 1) cluster_arrive_release();
     const uint64_t policy = l2_evict_first_policy();
-    // after the PDL wait x is final: copy this CTA's K slice (batch 1, no norm)
+    // Called by the whole warp exactly once: after the PDL wait x and y are
+    // final/free, so copy this CTA's x slice (batch 1, no norm), zero the
+    // group's y rows (rank 0 of an f32 split-K cluster) and arrive on the
+    // cluster barrier the consumers wait on before their adds.
     auto wait_and_copy_x = [&]() {
+      __syncwarp();
       pdl_wait();
       if (x_bulk && lane == 0) {
         const uint32_t xb = smem_u32(&bars[2 * stages]);
         mbar_arrive_expect_tx(xb, static_cast<uint32_t>(kt_cnt) * 512);
         bulk_g2s(smem_u32(x_s), p.x + static_cast<size_t>(kt0) * 256, static_cast<uint32_t>(kt_cnt) * 512, xb,
                  l2_evict_last_policy());
+      }
+      if (cl_mode == 1) {
+        if (split == 0) {
+          float* y = static_cast<float*>(p.y);
+          for (int e = lane; e < kGroupRows * p.batch; e += 32) {
+            const int row = e % kGroupRows, b = e / kGroupRows;
+            if (blockIdx.y * 4 + (row >> 5) < p.n_tile_rows)
+              y[static_cast<size_t>(b) * p.ldy + blockIdx.y * kGroupRows + row] = 0.f;
+          }
+        }
+        __syncwarp();
+        cluster_arrive_release();
       }
     };
     uint32_t seq = 0;
@@ -283,17 +299,16 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
     }
     for (int grp = blockIdx.y; grp < p.n_groups; grp += gridDim.y) {
       for (int kk = 0; kk < kt_cnt; ++kk, ++seq) {
+        if (seq >= static_cast<uint32_t>(stages) && !waited_pdl) {  // warp-uniform
+          wait_and_copy_x();  // ring full: nothing more to prefetch before the dependency
+          waited_pdl = true;
+        }
         if (lane == 0 && !*abort_flag) {
           const int slot = seq % stages;
           const uint32_t ph = (seq / stages) & 1;
           bool ok = true;
-          if (seq >= static_cast<uint32_t>(stages)) {
-            if (!waited_pdl) {  // ring full: nothing more to prefetch before the dependency
-              wait_and_copy_x();
-              waited_pdl = true;
-            }
+          if (seq >= static_cast<uint32_t>(stages))
             ok = mbar_wait_bounded(smem_u32(&bars[stages + slot]), ph ^ 1, abort_flag, kDevTimeoutEmpty);
-          }
           if (ok) {
             const int kt = kt0 + kk;
             const uint8_t* src[4];
@@ -324,9 +339,9 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
       __syncwarp();
     }
     __syncwarp();
-    if (!waited_pdl) wait_and_copy_x();  // issues the x copy if the loop did not
+    if (!waited_pdl) wait_and_copy_x();  // the whole slice fit the ring
     __syncwarp();
-    if (cl_mode == 1) cluster_wait_acquire();  // mirror the consumers' barrier phases
+    if (cl_mode == 1) cluster_wait_acquire();  // completes this thread's barrier phase
     if (cl_mode == 2) cluster_sync_all();
     if (lane == 0 && *abort_flag && x_bulk) {
       // lane 0 has issued the x copy by now, right after its PDL wait
@@ -358,17 +373,7 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
   // -------------------------------------------------------------- consumers
   pdl_wait();
   const int ctid = threadIdx.x;
-  if (cl_mode == 1) {
-    if (split == 0) {  // zero this group's outputs (after the PDL wait: y may be read upstream)
-      const int grp = blockIdx.y;
-      float* y = static_cast<float*>(p.y);
-      for (int e = ctid; e < kGroupRows * p.batch; e += kGemvConsumers) {
-        const int row = e % kGroupRows, b = e / kGroupRows;
-        if (grp * 4 + (row >> 5) < p.n_tile_rows) y[static_cast<size_t>(b) * p.ldy + grp * kGroupRows + row] = 0.f;
-      }
-    }
-    cluster_arrive_release();
-  }
+  if (cl_mode == 1) cluster_arrive_relaxed();  // nothing to publish: the producer carries the zeroing
   const int L_cta = kt_cnt * 256;
   if (!x_bulk) {
     // x rows as bf16: given (p.x), or bf16(rmsnorm(p.xf) * norm_w) computed here
