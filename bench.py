@@ -35,6 +35,9 @@ sys.path.insert(0, str(ROOT))
 METRIC = "q4/q8 GEMV HBM GB/s (% of peak); decode tokens/s at 1/2/4/8 B200"
 SHAPES = [("qkv", 112, 10), ("o", 80, 10), ("gate_up", 512, 10), ("down", 80, 32)]  # (tile-rows, K-tiles)
 Q4_TILE, Q8_TILE = 5120, 8704
+# dram__bytes_read.sum + dram__bytes_write.sum over tile bytes for the GEMV launches
+# that stream from DRAM (ncu capture summarised in profiles/q4nx_gemv_b1_one_layer.md)
+GEMV_DRAM_RATIO = 1.003
 LAYERS = 40
 
 
@@ -513,7 +516,10 @@ def run_b200(args, rank: int, world: int) -> dict | None:
         "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s",
                 "h2d_bytes_per_step": int(xs_host.numel() * 2), "d2h_bytes_per_step": int(ys_host.numel() * 4)},
         "roofline": {"bound": "hbm", "achieved": round(gbs_per_gpu, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(gbs_per_gpu / pk["hbm_gbs"], 4), "traffic": None,
+                     "frac": round(gbs_per_gpu / pk["hbm_gbs"], 4),
+                     "traffic": int(step_bytes / n_launch * GEMV_DRAM_RATIO),
+                     "traffic_unit": "DRAM bytes read+written per launch (mean over the sweep's launches): "
+                                     "algorithmic bytes x the ncu ratio in profiles/q4nx_gemv_b1_one_layer.md",
                      "kernel": "q4nx_gemv_kernel<q4,NB=1,f32>", "peak_src": pk["src"]},
         "clocks": clk.summary(),
     }
