@@ -143,6 +143,10 @@ int b2_q8_dequant_matrix(const uint8_t* tiles, int n_tile_rows, int k_tiles, flo
 #define B2_ATTN_NO_APPEND 1 /* the cache already holds position pos[b]; write nothing */
 #define B2_ATTN_NO_ROPE 2   /* use the new q/k as given (no rotation) */
 #define B2_ATTN_OUT_F32 4   /* fp32 output */
+#define B2_ATTN_PREFETCH_KV 8 /* pos[] and the cache rows before pos[b] are final when the
+                               * call is launched (no kernel still in flight writes them):
+                               * their first chunks are read before the wait on the
+                               * preceding kernel (programmatic dependent launch) */
 int b2_gqa_decode_workspace_size(int batch, int n_q_heads, int n_kv_heads, int head_dim, int max_len,
                                  size_t* bytes);
 int b2_gqa_decode(const float* q, const float* k_new, const float* v_new, int ld_new, uint16_t* k_cache,

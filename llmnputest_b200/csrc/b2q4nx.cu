@@ -649,7 +649,7 @@ int b2_gqa_decode(const float* q, const float* k_new, const float* v_new, int ld
   if (ld_new < n_q_heads * head_dim) return fail(B2_ERR_ARG, "ld_new %d < Hq*D", ld_new);
   if (ldo < n_q_heads * head_dim) return fail(B2_ERR_ARG, "ldo %d < Hq*D", ldo);
   if (!aligned(k_cache, 16) || !aligned(v_cache, 16)) return fail(B2_ERR_ALIGN, "KV caches must be 16-byte aligned");
-  if ((flags & ~(B2_ATTN_NO_APPEND | B2_ATTN_NO_ROPE | B2_ATTN_OUT_F32)) != 0)
+  if ((flags & ~(B2_ATTN_NO_APPEND | B2_ATTN_NO_ROPE | B2_ATTN_OUT_F32 | B2_ATTN_PREFETCH_KV)) != 0)
     return fail(B2_ERR_ARG, "unknown flags 0x%x", flags);
   const AttnPlan pl = attn_plan(batch, n_q_heads, n_kv_heads, head_dim, max_len, di.sms);
   if (pl.n_splits > 1 && (!workspace || workspace_bytes < pl.ws_bytes))
@@ -679,14 +679,24 @@ int b2_gqa_decode(const float* q, const float* k_new, const float* v_new, int ld
   p.rope = (flags & B2_ATTN_NO_ROPE) ? 0 : 1;
   p.out_f32 = (flags & B2_ATTN_OUT_F32) ? 1 : 0;
   p.clustered = pl.clustered;
+  p.prefetch_kv = (flags & B2_ATTN_PREFETCH_KV) ? 1 : 0;
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // 8 warps per CTA when the launch has at most one CTA per SM or long splits,
+  // 4 otherwise (short splits over many CTAs keep more, smaller CTAs resident)
+  const long long n_cta = static_cast<long long>(pl.n_splits) * n_kv_heads * batch;
+  const bool wide = n_cta <= di.sms || pl.split_len >= 1024;
+  auto kernel = wide ? b2::gqa_decode_kernel<64, 8> : b2::gqa_decode_kernel<64, 4>;
   static int attr_set[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(b2::gqa_decode_kernel<64>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attention)");
+    for (auto kf : {b2::gqa_decode_kernel<64, 8>, b2::gqa_decode_kernel<64, 4>}) {
+      cudaError_t e = cudaFuncSetAttribute(kf, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      // the cluster merge buffer (<= 16 splits x 8 heads x 66 floats) beside up to ~37 KB of static smem
+      if (e == cudaSuccess) e = cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attention)");
+    }
     attr_set[dev] = 1;
   }
   cudaLaunchAttribute attr[2];
@@ -705,12 +715,11 @@ int b2_gqa_decode(const float* q, const float* k_new, const float* v_new, int ld
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.n_splits, n_kv_heads, batch);
-  cfg.blockDim = dim3(b2::kAttnThreads, 1, 1);
+  cfg.blockDim = dim3(wide ? 256 : 128, 1, 1);
   cfg.dynamicSmemBytes = pl.clustered ? pl.n_splits * (n_q_heads / n_kv_heads) * (head_dim + 2) * sizeof(float) : 0;
   cfg.stream = s;
   cfg.attrs = attr;
-  cfg.numAttrs = na;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, b2::gqa_decode_kernel<64>, p);
+  cfg.numAttrs = na;  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p);
   if (e != cudaSuccess) return cuda_fail(e, "attention launch");
   if (pl.n_splits > 1 && !pl.clustered) {
     cfg.numAttrs = g_pdl ? 1 : 0;  // the combine kernel is not clustered

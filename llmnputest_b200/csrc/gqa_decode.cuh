@@ -33,8 +33,9 @@
 
 namespace b2 {
 
-constexpr int kAttnWarps = 4;
-constexpr int kAttnThreads = kAttnWarps * 32;
+// Warps per CTA (template W): 8 when a launch has few CTAs or long splits (more
+// K/V bytes in flight per SM, shorter chunk chains per warp), else 4.
+constexpr int kAttnMaxWarps = 8;
 constexpr int kAttnChunk = 16;  // positions per inner step
 
 struct AttnParams {
@@ -57,6 +58,7 @@ struct AttnParams {
   int rope;       // rotate the new q/k (0: use them as given)
   int out_f32;    // out is fp32 instead of bf16
   int clustered;  // splits of one (sequence, kv head) form a cluster and merge in rank 0's smem
+  int prefetch_kv;  // pos[] and cache rows < pos are final at launch: load them before the PDL wait
 };
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -83,8 +85,9 @@ __device__ __forceinline__ void rope_head_bf16(const float* src, __nv_bfloat16* 
   dst[i + D / 2] = __float2bfloat16_rn(x1 * c + x0 * s);
 }
 
-template <int D>
-__global__ void __launch_bounds__(kAttnThreads) gqa_decode_kernel(const AttnParams p) {
+template <int D, int W>
+__global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) gqa_decode_kernel(const AttnParams p) {
+  constexpr int kAttnWarps = W, kAttnThreads = W * 32;
   static_assert(D == 64, "this kernel is written for head_dim 64");
   extern __shared__ __align__(16) float gather[];  // clustered: [n_splits][grp][D + 2] on rank 0
   constexpr int QW = D / 2 + 4;  // q_s row stride in 32-bit words (bank spread)
@@ -97,12 +100,47 @@ __global__ void __launch_bounds__(kAttnThreads) gqa_decode_kernel(const AttnPara
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
 
-  pdl_wait();  // q/k/v come from the previous kernel
+  if (!p.prefetch_kv) pdl_wait();  // q/k/v come from the previous kernel
   pdl_launch_dependents();
   const int pos = p.pos[b];
   const int len = pos + 1;
   const int lo = split * p.split_len;
   const int hi = min(len, lo + p.split_len);
+
+  // ---- this warp's positions
+  const int n = max(0, hi - lo);
+  const int per_warp = ((n + kAttnWarps * kAttnChunk - 1) / (kAttnWarps * kAttnChunk)) * kAttnChunk;
+  const int w_lo = lo + warp * per_warp;
+  const int w_hi = min(hi, w_lo + per_warp);
+  const __nv_bfloat16* kbase = p.k_cache + (static_cast<size_t>(b) * p.hkv + kvh) * p.ctx_max * D;
+  const __nv_bfloat16* vbase = p.v_cache + (static_cast<size_t>(b) * p.hkv + kvh) * p.ctx_max * D;
+
+  auto load_chunk = [&](int c0, uint4 (&kr)[4], uint4 (&vr)[4]) {
+    // K rows c0+g and c0+8+g at d 16t..16t+15; V rows c0+{2t,2t+1,8+2t,9+2t} at d 8g..8g+7.
+    // Rows past the end are clamped to the last valid row (their scores are masked).
+    const int last = w_hi - 1;
+    const int r0 = min(c0 + g, last), r1 = min(c0 + 8 + g, last);
+    kr[0] = *reinterpret_cast<const uint4*>(kbase + static_cast<size_t>(r0) * D + 16 * t);
+    kr[1] = *reinterpret_cast<const uint4*>(kbase + static_cast<size_t>(r0) * D + 16 * t + 8);
+    kr[2] = *reinterpret_cast<const uint4*>(kbase + static_cast<size_t>(r1) * D + 16 * t);
+    kr[3] = *reinterpret_cast<const uint4*>(kbase + static_cast<size_t>(r1) * D + 16 * t + 8);
+    const int v0 = min(c0 + 2 * t, last), v1 = min(c0 + 2 * t + 1, last);
+    const int v2 = min(c0 + 8 + 2 * t, last), v3 = min(c0 + 9 + 2 * t, last);
+    vr[0] = *reinterpret_cast<const uint4*>(vbase + static_cast<size_t>(v0) * D + 8 * g);
+    vr[1] = *reinterpret_cast<const uint4*>(vbase + static_cast<size_t>(v1) * D + 8 * g);
+    vr[2] = *reinterpret_cast<const uint4*>(vbase + static_cast<size_t>(v2) * D + 8 * g);
+    vr[3] = *reinterpret_cast<const uint4*>(vbase + static_cast<size_t>(v3) * D + 8 * g);
+  };
+  // With prefetch_kv the warp's first two chunks are loaded before the PDL wait,
+  // unless a chunk reaches row pos (appended below, after the wait): rows read
+  // are min(c0 + r, w_hi - 1), which include pos only when w_hi == len.
+  auto early_ok = [&](int c0) { return p.prefetch_kv && (w_hi != len || c0 + kAttnChunk - 1 < pos); };
+  uint4 kr[4], vr[4], kn[4], vn[4];
+  const bool pre0 = w_lo < w_hi && early_ok(w_lo);
+  const bool pre1 = pre0 && w_lo + kAttnChunk < w_hi && early_ok(w_lo + kAttnChunk);
+  if (pre0) load_chunk(w_lo, kr, vr);
+  if (pre1) load_chunk(w_lo + kAttnChunk, kn, vn);
+  if (p.prefetch_kv) pdl_wait();
 
   // ---- q heads of the group: rope -> bf16 -> shared (rows >= grp are zero)
   {
@@ -135,42 +173,16 @@ __global__ void __launch_bounds__(kAttnThreads) gqa_decode_kernel(const AttnPara
     qa[j][1] = q_s[g * QW + 8 * t + 2 * j + 1];
   }
 
-  // ---- this warp's positions
-  const int n = max(0, hi - lo);
-  const int per_warp = ((n + kAttnWarps * kAttnChunk - 1) / (kAttnWarps * kAttnChunk)) * kAttnChunk;
-  const int w_lo = lo + warp * per_warp;
-  const int w_hi = min(hi, w_lo + per_warp);
-  const __nv_bfloat16* kbase = p.k_cache + (static_cast<size_t>(b) * p.hkv + kvh) * p.ctx_max * D;
-  const __nv_bfloat16* vbase = p.v_cache + (static_cast<size_t>(b) * p.hkv + kvh) * p.ctx_max * D;
-
   float m_run = -INFINITY, l_run = 0.f;
   float o[8][4];
 #pragma unroll
   for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
 
-  auto load_chunk = [&](int c0, uint4 (&kr)[4], uint4 (&vr)[4]) {
-    // K rows c0+g and c0+8+g at d 16t..16t+15; V rows c0+{2t,2t+1,8+2t,9+2t} at d 8g..8g+7.
-    // Rows past the end are clamped to the last valid row (their scores are masked).
-    const int last = w_hi - 1;
-    const int r0 = min(c0 + g, last), r1 = min(c0 + 8 + g, last);
-    kr[0] = *reinterpret_cast<const uint4*>(kbase + static_cast<size_t>(r0) * D + 16 * t);
-    kr[1] = *reinterpret_cast<const uint4*>(kbase + static_cast<size_t>(r0) * D + 16 * t + 8);
-    kr[2] = *reinterpret_cast<const uint4*>(kbase + static_cast<size_t>(r1) * D + 16 * t);
-    kr[3] = *reinterpret_cast<const uint4*>(kbase + static_cast<size_t>(r1) * D + 16 * t + 8);
-    const int v0 = min(c0 + 2 * t, last), v1 = min(c0 + 2 * t + 1, last);
-    const int v2 = min(c0 + 8 + 2 * t, last), v3 = min(c0 + 9 + 2 * t, last);
-    vr[0] = *reinterpret_cast<const uint4*>(vbase + static_cast<size_t>(v0) * D + 8 * g);
-    vr[1] = *reinterpret_cast<const uint4*>(vbase + static_cast<size_t>(v1) * D + 8 * g);
-    vr[2] = *reinterpret_cast<const uint4*>(vbase + static_cast<size_t>(v2) * D + 8 * g);
-    vr[3] = *reinterpret_cast<const uint4*>(vbase + static_cast<size_t>(v3) * D + 8 * g);
-  };
-
   if (w_lo < w_hi) {
-    uint4 kr[4], vr[4], kn[4], vn[4];
-    load_chunk(w_lo, kr, vr);
+    if (!pre0) load_chunk(w_lo, kr, vr);
     for (int c0 = w_lo; c0 < w_hi; c0 += kAttnChunk) {
       const bool more = c0 + kAttnChunk < w_hi;
-      if (more) load_chunk(c0 + kAttnChunk, kn, vn);
+      if (more && !(pre1 && c0 == w_lo)) load_chunk(c0 + kAttnChunk, kn, vn);
       // S = Q K^T for positions c0..c0+7 (n-tile 0) and c0+8..c0+15 (n-tile 1)
       float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll

@@ -143,7 +143,10 @@ class Q4Decoder:
     def step(self, prefetch: bool = True) -> torch.Tensor:
         """One decode step: x_in (fp32 [B, hidden]) at positions `pos` -> logits (fp32 [B, vocab]).
 
-        Appends each layer's k/v at `pos`; the caller advances `pos` between steps.
+        Appends each layer's k/v at `pos`; the caller advances `pos` between steps
+        (with an ordinary stream operation, so that pos and the cache rows before it
+        are final when the step's kernels launch: attention reads them before its
+        wait on the preceding kernel).
         """
         c = self.cfg
         d = c.head_dim
@@ -158,7 +161,7 @@ class Q4Decoder:
             ops.gqa_decode(self.qkv[:, :qd], self.qkv[:, qd:qd + kd], self.qkv[:, qd + kd:],
                            self.k_cache[li], self.v_cache[li], self.pos, n_q_heads=c.n_heads,
                            n_kv_heads=c.n_kv_heads, theta=c.rope_theta, scale=d ** -0.5, max_len=self.ctx_max,
-                           out=self.attn, workspace=self.attn_ws)
+                           out=self.attn, workspace=self.attn_ws, prefetch_kv=prefetch)
             ops.q4_gemv(L["o"], self.nt_h, self.kt_q, self.attn, out=self.resid, accumulate=True, prefetch=prefetch)
             ops.swiglu_gemv_rmsnorm(L["gate"], L["up"], self.nt_i, self.kt_h, self.resid, L["mlp_norm"], c.rms_eps,
                                     out=self.h, prefetch=prefetch)
@@ -179,7 +182,7 @@ class Q4Decoder:
             ops.gqa_decode(self.qkv[:, :qd], self.qkv[:, qd:qd + kd], self.qkv[:, qd + kd:],
                            self.k_cache[li], self.v_cache[li], self.pos, n_q_heads=c.n_heads,
                            n_kv_heads=c.n_kv_heads, theta=c.rope_theta, scale=d ** -0.5, max_len=self.ctx_max,
-                           out=self.attn, workspace=self.attn_ws)
+                           out=self.attn, workspace=self.attn_ws, prefetch_kv=True)
             ops.q4_gemm(L["o"], self.nt_h, self.kt_q, self.attn, out=self.resid, accumulate=True, workspace=ws)
             ops.rmsnorm(self.resid, L["mlp_norm"], c.rms_eps, out=self.xn)
             ops.q4_swiglu_gemm(L["gate"], L["up"], self.nt_i, self.kt_h, self.xn, out=self.h, workspace=ws)

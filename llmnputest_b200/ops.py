@@ -253,6 +253,7 @@ def device_error() -> int:
 ATTN_NO_APPEND = 1
 ATTN_NO_ROPE = 2
 ATTN_OUT_F32 = 4
+ATTN_PREFETCH_KV = 8
 
 
 def gqa_decode_workspace_bytes(batch: int, n_q_heads: int, n_kv_heads: int, head_dim: int, max_len: int) -> int:
@@ -266,8 +267,13 @@ def gqa_decode(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, k_cach
                v_cache: torch.Tensor, pos: torch.Tensor, *, n_q_heads: int, n_kv_heads: int,
                theta: float = 10000.0, scale: float | None = None, max_len: int | None = None,
                out: torch.Tensor | None = None, append: bool = True, rope: bool = True,
-               out_f32: bool = False, workspace: torch.Tensor | None = None) -> torch.Tensor:
+               out_f32: bool = False, workspace: torch.Tensor | None = None,
+               prefetch_kv: bool = False) -> torch.Tensor:
     """GQA flash-decode for one new token per sequence (see b2_gqa_decode).
+
+    prefetch_kv (B2_ATTN_PREFETCH_KV): pos and the cache rows before pos are final
+    when the call is made (no kernel still in flight writes them), so the kernel
+    reads its first K/V chunks before waiting on the preceding kernel.
 
     q [B, >=Hq*D], k_new/v_new [B, >=Hkv*D] fp32 with a common row stride (e.g.
     slices of the QKV GEMV output); caches bf16 [B, Hkv, ctx_max, D]; pos int32 [B].
@@ -300,6 +306,7 @@ def gqa_decode(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, k_cach
     if workspace is None or workspace.numel() < ws_n:
         workspace = torch.empty(max(ws_n, 1), dtype=torch.uint8, device=q.device)
     flags = (0 if append else ATTN_NO_APPEND) | (0 if rope else ATTN_NO_ROPE) | (ATTN_OUT_F32 if out_f32 else 0)
+    flags |= ATTN_PREFETCH_KV if prefetch_kv else 0
     _native.call("b2_gqa_decode", _ptr(q), _ptr(k_new), _ptr(v_new), ld_new, _ptr(k_cache), _ptr(v_cache),
                  _ptr(pos), b, n_q_heads, n_kv_heads, d, ctx_max, max_len, float(theta), float(scale), _ptr(out),
                  out.stride(0), _ptr(workspace), workspace.numel(), flags, _stream())

@@ -180,7 +180,7 @@ class TPDecoder:
             ops.gqa_decode(self.qkv[:, :qd], self.qkv[:, qd:qd + kd], self.qkv[:, qd + kd:], self.k_cache[li],
                            self.v_cache[li], self.pos, n_q_heads=p.q_local, n_kv_heads=p.kv_local,
                            theta=c.rope_theta, scale=d ** -0.5, max_len=self.ctx_max, out=self.attn_local,
-                           workspace=self.attn_ws)
+                           workspace=self.attn_ws, prefetch_kv=True)
             if W > 1:
                 dist.all_gather_into_tensor(self.attn_all, self.attn_local)
                 # rank-major [W][B][q_local*D] -> [B][Hq*D] (head order = rank order)

@@ -69,7 +69,7 @@ def test_rope_append_golden(ops, golden, pos):
                           x.astype(bfloat16).astype(np.float32).reshape(-1))
 
 
-def _gqa_case(ops, bsz, hq, hkv, ctx_max, lens, seed, out_f32=True):
+def _gqa_case(ops, bsz, hq, hkv, ctx_max, lens, seed, out_f32=True, prefetch_kv=False):
     rng = np.random.default_rng(seed)
     d = 64
     kc_np = orc.synth_bf16(rng, (bsz, hkv, ctx_max, d))
@@ -81,7 +81,7 @@ def _gqa_case(ops, bsz, hq, hkv, ctx_max, lens, seed, out_f32=True):
     qkv_d = f32dev(qkv)
     qd, kd, vd = qkv_d[:, :hq * d], qkv_d[:, hq * d:(hq + hkv) * d], qkv_d[:, (hq + hkv) * d:]
     out = ops.gqa_decode(qd, kd, vd, kc, vc, torch.from_numpy(pos).cuda(), n_q_heads=hq, n_kv_heads=hkv,
-                         theta=10000.0, max_len=int(max(lens)), out_f32=out_f32)
+                         theta=10000.0, max_len=int(max(lens)), out_f32=out_f32, prefetch_kv=prefetch_kv)
     # oracle: rotate the new q/k in float64, narrow to bf16 (the QKV epilogue), append, attend
     kref = kc_np.astype(np.float32).copy()
     vref = vc_np.astype(np.float32).copy()
@@ -112,6 +112,18 @@ def _gqa_case(ops, bsz, hq, hkv, ctx_max, lens, seed, out_f32=True):
 def test_gqa_vs_oracle(ops, bsz, ctx, lens):
     got, ref = _gqa_case(ops, bsz, 40, 8, ctx, lens, seed=ctx + bsz)
     for b in range(bsz):  # every sequence, every head
+        assert_close(got[b], ref[b], NS_COS, NS_REL, f"seq {b} len {lens[b]}")
+
+
+@pytest.mark.parametrize("bsz,ctx,lens", [(1, 4096, [4096]), (1, 100, [17]), (3, 2048, [2048, 31, 1500]),
+                                          (64, 512, None)])
+def test_gqa_prefetch_kv(ops, bsz, ctx, lens):
+    """B2_ATTN_PREFETCH_KV: K/V chunks read before the wait on the preceding kernel;
+    the chunk that reaches the appended row pos is read after it, so the result is
+    the oracle's (8-warp and 4-warp launches, appended row in the first or a later chunk)."""
+    lens = lens or list(np.random.default_rng(64).integers(1, ctx + 1, bsz))
+    got, ref = _gqa_case(ops, bsz, 40, 8, ctx, lens, seed=ctx + 7 * bsz, prefetch_kv=True)
+    for b in range(bsz):
         assert_close(got[b], ref[b], NS_COS, NS_REL, f"seq {b} len {lens[b]}")
 
 
