@@ -127,11 +127,13 @@ int launch_gemv_t(b2::GemvParams p, const DevInfo& di, cudaStream_t stream) {
 
   const int G = p.n_groups;
   const int batch = p.batch;
+  // batch-1 q4 with the fused norm keeps the fp32 row in shared memory (kernel: x_norm_bulk)
+  const int norm_k = (QT == kQ4 && NB == 1 && batch == 1 && p.xf) ? p.k_tiles * 256 : 0;
   // largest K slice whose staged x (batch rows, fp16) stays within 48 KB
   const int kt_cap = std::max(1, (48 * 1024) / (batch * 512 + 16));
   // CTAs per SM: two when the register budget (NB == 1) and shared memory allow
   auto fixed_bytes = [&](int ktps) {
-    const GemvSmem base(SLOT, NB, 0, ktps * 256 + 8, ktps, batch);
+    const GemvSmem base(SLOT, NB, 0, ktps * 256 + 8, ktps, batch, norm_k);
     return base.total + 2 * kMaxStages * 8;
   };
   const int per_cta_2 = di.smem_per_sm / 2 - di.smem_reserved;
@@ -185,7 +187,7 @@ int launch_gemv_t(b2::GemvParams p, const DevInfo& di, cudaStream_t stream) {
   int stages = std::min(tu.max_stages, (budget - fixed_bytes(ktps)) / STAGE);
   stages = std::min(stages, total_stages);
   if (stages < 1) return fail(B2_ERR_ARG, "K slice too large for shared memory");
-  const GemvSmem L(SLOT, NB, stages, x_stride, ktps, batch);
+  const GemvSmem L(SLOT, NB, stages, x_stride, ktps, batch, norm_k);
 
   p.kt_per_split = ktps;
   p.n_splits = S;

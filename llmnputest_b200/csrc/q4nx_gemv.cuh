@@ -101,9 +101,12 @@ struct GemvParams {
 
 // Shared-memory layout (bytes), computed identically on host and device.
 struct GemvSmem {
-  int ring, x, xs, red, csum, gather, misc, bar, flag, total;
+  int ring, x, xs, red, csum, gather, misc, xf, nw, bar, flag, total;
   int ncol;  // batch rounded up to even
-  __host__ __device__ GemvSmem(int slot, int nb, int stages, int x_stride, int kt_per_split, int batch) {
+  // norm_k > 0: batch-1 fused RMSNorm with the fp32 row (norm_k floats) and this
+  // CTA's slice of the norm weight copied into shared memory
+  __host__ __device__ GemvSmem(int slot, int nb, int stages, int x_stride, int kt_per_split, int batch,
+                               int norm_k = 0) {
     ncol = (batch + 1) & ~1;
     ring = 0;
     x = stages * 4 * slot;
@@ -112,7 +115,9 @@ struct GemvSmem {
     csum = red + kGemvConsumerWarps * 64 * ncol * 4;
     gather = csum + kGroupRows * ncol * 4;  // split-K partials pushed by the cluster's ranks
     misc = gather + 160 * ncol * 4;         // [kMaxBatch] max bits, [kMaxBatch] exponents
-    bar = misc + 2 * kMaxBatch * 4;
+    xf = (misc + 2 * kMaxBatch * 4 + 15) & ~15;
+    nw = xf + norm_k * 4;
+    bar = nw + (norm_k > 0 ? kt_per_split * 256 * 2 : 0);
     bar = (bar + 15) & ~15;
     flag = bar + (2 * stages + 1) * 8;  // full[stages], empty[stages], x
     total = flag + 16;
@@ -209,7 +214,10 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
   constexpr int STAGE = 4 * SLOT;
   extern __shared__ __align__(128) uint8_t smem[];
 
-  const GemvSmem L(SLOT, NB, p.stages, p.x_stride, p.kt_per_split, p.batch);
+  // batch 1 with the fused norm (q4): the fp32 row and the norm weight slice are
+  // bulk-copied after the PDL wait and the norm is reduced by all consumer threads
+  const bool x_norm_bulk = QT == kQ4 && NB == 1 && p.batch == 1 && p.xf != nullptr;
+  const GemvSmem L(SLOT, NB, p.stages, p.x_stride, p.kt_per_split, p.batch, x_norm_bulk ? p.k_tiles * 256 : 0);
   uint8_t* ring = smem + L.ring;
   __half* x_s = reinterpret_cast<__half*>(smem + L.x);
   float* xs_s = reinterpret_cast<float*>(smem + L.xs);
@@ -276,6 +284,14 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
         bulk_g2s(smem_u32(x_s), p.x + static_cast<size_t>(kt0) * 256, static_cast<uint32_t>(kt_cnt) * 512, xb,
                  l2_evict_last_policy());
       }
+      if (x_norm_bulk && lane == 0) {  // the whole fp32 row (for the norm) and this CTA's weight slice
+        const uint32_t xb = smem_u32(&bars[2 * stages]);
+        const uint32_t row_bytes = static_cast<uint32_t>(p.k_tiles) * 1024, w_bytes = static_cast<uint32_t>(kt_cnt) * 512;
+        mbar_arrive_expect_tx(xb, row_bytes + w_bytes);
+        bulk_g2s(smem_u32(smem + L.xf), p.xf, row_bytes, xb, l2_evict_last_policy());
+        bulk_g2s(smem_u32(smem + L.nw), p.norm_w + static_cast<size_t>(kt0) * 256, w_bytes, xb,
+                 l2_evict_last_policy());
+      }
       if (cl_mode == 1) {
         if (split == 0) {
           float* y = static_cast<float*>(p.y);
@@ -296,6 +312,8 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
       waited_pdl = true;
     } else if (x_bulk && lane == 0) {
       bulk_prefetch_l2(p.x + static_cast<size_t>(kt0) * 256, static_cast<uint32_t>(kt_cnt) * 512);  // L2 only
+    } else if (x_norm_bulk && lane == 0) {
+      bulk_prefetch_l2(p.xf, static_cast<uint32_t>(p.k_tiles) * 1024);
     }
     for (int grp = blockIdx.y; grp < p.n_groups; grp += gridDim.y) {
       for (int kk = 0; kk < kt_cnt; ++kk, ++seq) {
@@ -343,7 +361,7 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
     __syncwarp();
     if (cl_mode == 1) cluster_wait_acquire();  // completes this thread's barrier phase
     if (cl_mode == 2) cluster_sync_all();
-    if (lane == 0 && *abort_flag && x_bulk) {
+    if (lane == 0 && *abort_flag && (x_bulk || x_norm_bulk)) {
       // lane 0 has issued the x copy by now, right after its PDL wait
       const uint64_t t0 = globaltimer();
       while (!mbar_try_wait(smem_u32(&bars[2 * stages]), 0)) {
@@ -375,7 +393,7 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
   const int ctid = threadIdx.x;
   if (cl_mode == 1) cluster_arrive_relaxed();  // nothing to publish: the producer carries the zeroing
   const int L_cta = kt_cnt * 256;
-  if (!x_bulk) {
+  if (!x_bulk && !x_norm_bulk) {
     // x rows as bf16: given (p.x), or bf16(rmsnorm(p.xf) * norm_w) computed here
     // (the norm fused into the GEMV, granite_rmsnorm.h:45-80 arithmetic).
     const int vec_per_row = L_cta / 8;  // 16-byte vectors of 8 values, a multiple of 32
@@ -480,14 +498,44 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
   const uint32_t* x32 = reinterpret_cast<const uint32_t*>(x_s);
   const int xw_stride = p.x_stride / 2;
 
-  if (x_bulk) mbar_wait_bounded(smem_u32(&bars[2 * stages]), 0, abort_flag, kDevTimeoutFull);
+  if (x_bulk || x_norm_bulk) mbar_wait_bounded(smem_u32(&bars[2 * stages]), 0, abort_flag, kDevTimeoutFull);
+  float inv_rms1 = 0.f;
+  if (x_norm_bulk) {
+    // sum of squares of the fp32 row by all consumer threads (granite_rmsnorm.h:45-80 arithmetic)
+    const float4* xr = reinterpret_cast<const float4*>(smem + L.xf);
+    float ss = 0.f;
+    for (int c = ctid; c < p.k_tiles * 64; c += kGemvConsumers) {
+      const float4 v = xr[c];
+      ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[warp] = ss;  // red is free until the first park
+    named_barrier(1, kGemvConsumers);
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < kGemvConsumerWarps; ++w) tot += red[w];
+    inv_rms1 = rsqrtf(tot / static_cast<float>(p.k_tiles * 256) + p.eps);
+  }
   if (b1) {
     // x (bf16, this CTA's K slice) -> f16 in place, scaled per 32-k block by 2^e
     // (exact: bf16's 8-bit mantissa fits f16's 11), with the block's sum of x and
     // 2^-e beside it: xs_s[block * 8 + 0 / 1].  Four lanes hold one block.
     uint4* xv = reinterpret_cast<uint4*>(x_s);
     for (int v = ctid; v < kt_cnt * 32; v += kGemvConsumers) {  // warp-uniform trip count
-      const uint4 u = xv[v];
+      uint4 u;
+      if (x_norm_bulk) {  // bf16(x * inv_rms * w) from the row and weight slice in shared memory
+        const float4 a0 = reinterpret_cast<const float4*>(smem + L.xf)[kt0 * 64 + 2 * v];
+        const float4 a1 = reinterpret_cast<const float4*>(smem + L.xf)[kt0 * 64 + 2 * v + 1];
+        const uint4 wv = reinterpret_cast<const uint4*>(smem + L.nw)[v];
+        auto nb = [&](float xv_, float wf) { return xv_ * inv_rms1 * wf; };
+        u.x = pack_bf16x2_rn(nb(a0.x, bf16lo_to_f32(wv.x)), nb(a0.y, bf16hi_to_f32(wv.x)));
+        u.y = pack_bf16x2_rn(nb(a0.z, bf16lo_to_f32(wv.y)), nb(a0.w, bf16hi_to_f32(wv.y)));
+        u.z = pack_bf16x2_rn(nb(a1.x, bf16lo_to_f32(wv.z)), nb(a1.y, bf16hi_to_f32(wv.z)));
+        u.w = pack_bf16x2_rn(nb(a1.z, bf16lo_to_f32(wv.w)), nb(a1.w, bf16hi_to_f32(wv.w)));
+      } else {
+        u = xv[v];
+      }
       const uint32_t w[4] = {u.x, u.y, u.z, u.w};
       float f[8], mx = 0.f, sm = 0.f;
 #pragma unroll
