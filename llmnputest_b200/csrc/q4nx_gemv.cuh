@@ -453,7 +453,36 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
       if ((lane & 3) == 0) xs_s[(c >> 2) * 8 * NB + b] = s8;
     };
     constexpr int kVecLane = 8;  // a slice of up to 8 K-tiles is held in registers
-    for (int b = 0; b < batch; ++b) {
+    if (batch > 1) {
+      // one warp per row: the rows' loads, maxima and conversions run in parallel
+      for (int b = warp; b < batch; b += kGemvConsumerWarps) {
+        float mx = 0.f;
+        if (vec_per_row <= 32 * kVecLane) {
+          uint4 v[kVecLane];
+#pragma unroll
+          for (int i = 0; i < kVecLane; ++i)
+            if (32 * i < vec_per_row) {
+              v[i] = xvec(b, lane + 32 * i);
+              mx = fmaxf(mx, absmax8_bf16(v[i]));
+            }
+          mx = warp_max(mx);
+          const int e = gemv_scale_exp(__float_as_uint(mx));
+          const float sc = pow2f(e);
+          if (lane == 0) exps[b] = e;
+#pragma unroll
+          for (int i = 0; i < kVecLane; ++i)
+            if (32 * i < vec_per_row) put(b, lane + 32 * i, v[i], sc);
+        } else {
+          for (int c = lane; c < vec_per_row; c += 32) mx = fmaxf(mx, absmax8_bf16(xvec(b, c)));
+          mx = warp_max(mx);
+          const int e = gemv_scale_exp(__float_as_uint(mx));
+          const float sc = pow2f(e);
+          if (lane == 0) exps[b] = e;
+          for (int c = lane; c < vec_per_row; c += 32) put(b, c, xvec(b, c), sc);
+        }
+      }
+    }
+    for (int b = 0; b < (batch > 1 ? 0 : batch); ++b) {
       if (vec_per_row <= 32 * kVecLane) {
         // one pass: every warp loads the whole slice (one L2 round trip), finds the
         // max itself (no barrier), and converts its own K-tiles from registers
@@ -693,9 +722,9 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
             const uint32_t p2 = *reinterpret_cast<const uint32_t*>(nb + off_second);
             const uint32_t q1 = *reinterpret_cast<const uint32_t*>(nb + 64 + off_first);
             const uint32_t q2 = *reinterpret_cast<const uint32_t*>(nb + 64 + off_second);
-            uint32_t aP[8], aQ[8];
-            decode_q4_pair(p1, p2, sel_lo, sel_hi, aP);
-            decode_q4_pair(q1, q2, sel_lo, sel_hi, aQ);
+            uint32_t aP[8], aQ[8];  // codes + 1024 (even rows) / + 64 (odd rows), folded below
+            decode_q4_pair_biased(p1, p2, sel_lo, sel_hi, aP);
+            decode_q4_pair_biased(q1, q2, sel_lo, sel_hi, aQ);
 #pragma unroll
             for (int s = 0; s < 4; ++s)
 #pragma unroll
@@ -732,7 +761,8 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
           }
         }
 
-        // fold this k-block: tot += d*part + m*sum(x')   (q8: m = -2176*s)
+        // fold this k-block: tot += d*part + m'*sum(x'), m' = m - code offset * d
+        // (q4: offset 1024 for even rows, 64 for odd rows; q8: m' = -2176*s)
         const uint8_t* meta = tl + (kb * 32 + rb * 16 + h * 8) * 2;
         const uint4 dv = *reinterpret_cast<const uint4*>(meta);
         const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
@@ -750,8 +780,8 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
           const float da = bf16lo_to_f32(dw[s]), db = bf16hi_to_f32(dw[s]);
           float ma, mb;
           if (QT == kQ4) {
-            ma = bf16lo_to_f32(mw[s]);
-            mb = bf16hi_to_f32(mw[s]);
+            ma = fmaf(-1024.f, da, bf16lo_to_f32(mw[s]));
+            mb = fmaf(-64.f, db, bf16hi_to_f32(mw[s]));
           } else {
             ma = -2176.f * da;
             mb = -2176.f * db;
