@@ -44,7 +44,7 @@ constexpr int kTcRawSlot = QTraits<kQ4>::kSlot;
 constexpr int kTcRawStage = 4 * kTcRawSlot;
 constexpr int kTcMaxN = 256;
 constexpr int kTcXchgStride = 33;            // SwiGLU exchange row stride in floats (bank spread)
-constexpr int kTcXchgBytes = 64 * kTcXchgStride * 4;  // 64 up rows x 32 tokens
+constexpr int kTcXchgBytes = 64 * kTcXchgStride * 4 + 256 * 4;  // 64 rows x 32 tokens, then 2^-e per token
 
 enum TcEpi : int { kTcEpiF32 = 0, kTcEpiSwiglu = 1 };
 
@@ -358,7 +358,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
     const int q = warp & 3;  // TMEM lane quarter this warp may read
     const int row_local = q * 32 + lane;
     float* xchg = reinterpret_cast<float*>(smem + L.xchg);
+    float* inv_sc = xchg + 64 * kTcXchgStride;  // [npad] 2^-e per token column
     pdl_wait();  // the exponents come from the pre-pass
+    for (int i = threadIdx.x - 64; i < npad; i += 128) inv_sc[i] = pow2f(-p.xexp[i]);  // xexp has npad entries
+    named_barrier(2, 128);
     uint32_t t_it = 0;
     for (int it = blockIdx.x; it < n_items; it += gridDim.x, ++t_it) {
       const int tile = item_tile(it);
@@ -369,47 +372,75 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
       for (int c0 = 0; c0 < npad; c0 += 32) {
         uint32_t r[32];
         tmem_ld32(t_row + c0, r);
+        // the 32 columns' x scales (shared table), read before any store below
+        float u2v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) u2v[j] = inv_sc[c0 + j];
         if (EPI == kTcEpiF32) {
           const int tr = tile * 4 + (row_local >> 5);
           const int grow = tile * kTcM + row_local;
           if (ok && !*abort_flag && tr < p.n_tile_rows) {
-            float* y = static_cast<float*>(p.y);
+            float* y = static_cast<float*>(p.y) + grow;
+            if (p.n_splits > 1) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int n = c0 + j;
-              if (n < p.batch) {
-                const float v = __uint_as_float(r[j]) * pow2f(-p.xexp[n]);
-                float* dst = y + static_cast<size_t>(n) * p.ldy + grow;
-                if (p.n_splits > 1)
-                  atomicAdd(dst, v);  // zeroed by the pre-pass unless accumulating
-                else
-                  *dst = p.accumulate ? *dst + v : v;
+              for (int j = 0; j < 32; ++j)  // zeroed by the pre-pass unless accumulating
+                if (c0 + j < p.batch) atomicAdd(y + static_cast<size_t>(c0 + j) * p.ldy, __uint_as_float(r[j]) * u2v[j]);
+            } else {
+#pragma unroll
+              for (int hh = 0; hh < 32; hh += 16) {
+                float old[16];  // the half's loads before its first store (no load waits behind a store)
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                  old[j] = (p.accumulate && c0 + hh + j < p.batch) ? y[static_cast<size_t>(c0 + hh + j) * p.ldy] : 0.f;
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                  if (c0 + hh + j < p.batch)
+                    y[static_cast<size_t>(c0 + hh + j) * p.ldy] = old[j] + __uint_as_float(r[hh + j]) * u2v[hh + j];
               }
             }
           }
         } else {
-          // rows 0-63 gate, 64-127 the matching up rows: up warps hand their values over
-          if (q >= 2) {
+          // rows 0-63 gate, 64-127 the matching up rows.  Gate warps finish columns
+          // 0-15 of the chunk and up warps columns 16-31: each hands the other half
+          // of its values over (disjoint columns of the exchange rows).  Indices stay
+          // compile-time (warp-uniform branches), all loads precede the stores.
+          const bool gate_w = q < 2;
+          const int orow = gate_w ? row_local : row_local - 64;  // output row 0..63
+          float* xrow = xchg + orow * kTcXchgStride;
+          if (gate_w) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) xchg[(row_local - 64) * kTcXchgStride + j] = __uint_as_float(r[j]);
+            for (int j = 0; j < 16; ++j) xrow[16 + j] = __uint_as_float(r[16 + j]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) xrow[j] = __uint_as_float(r[j]);
           }
           named_barrier(2, 128);
-          if (q < 2) {
-            const int tr = tile * 2 + (row_local >> 5);
-            const int grow = tile * 64 + row_local;
-            if (ok && !*abort_flag && tr < p.n_tile_rows) {
-              __nv_bfloat16* h = static_cast<__nv_bfloat16*>(p.y);
+          float hv[16];
+          if (gate_w) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const int n = c0 + j;
-                if (n < p.batch) {
-                  const float u2 = pow2f(-p.xexp[n]);
-                  // both accumulators narrowed to bf16 before SiLU (granite_mlp.py:172-181)
-                  const float gb = __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[j]) * u2));
-                  const float ub = __bfloat162float(__float2bfloat16_rn(xchg[row_local * kTcXchgStride + j] * u2));
-                  h[static_cast<size_t>(n) * p.ldy + grow] = __float2bfloat16_rn(gb / (1.f + expf(-gb)) * ub);
-                }
-              }
+            for (int j = 0; j < 16; ++j) {
+              // both accumulators narrowed to bf16 before SiLU (granite_mlp.py:172-181)
+              const float gb = __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[j]) * u2v[j]));
+              const float ub = __bfloat162float(__float2bfloat16_rn(xrow[j] * u2v[j]));
+              hv[j] = __fdividef(gb, 1.f + __expf(-gb)) * ub;  // error ~2^-21, far below bf16's
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float gb = __bfloat162float(__float2bfloat16_rn(xrow[16 + j] * u2v[16 + j]));
+              const float ub = __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[16 + j]) * u2v[16 + j]));
+              hv[j] = __fdividef(gb, 1.f + __expf(-gb)) * ub;
+            }
+          }
+          const int jm = gate_w ? 0 : 16;  // this warp's columns
+          const int tr = tile * 2 + (orow >> 5);
+          const int grow = tile * 64 + orow;
+          if (ok && !*abort_flag && tr < p.n_tile_rows) {
+            __nv_bfloat16* h = static_cast<__nv_bfloat16*>(p.y);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int n = c0 + jm + j;
+              if (n < p.batch) h[static_cast<size_t>(n) * p.ldy + grow] = __float2bfloat16_rn(hv[j]);
             }
           }
           named_barrier(2, 128);
