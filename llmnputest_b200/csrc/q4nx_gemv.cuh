@@ -147,27 +147,11 @@ __device__ __forceinline__ int gemv_scale_exp(uint32_t bits) {
 }
 __device__ __forceinline__ float pow2f(int e) { return __uint_as_float(static_cast<uint32_t>(e + 127) << 23); }
 
-// q4: decode the 8 rows of one k-pair from two 32-bit words (k_a and k_b bytes
-// of rows h*8..h*8+7, 2 rows per byte); out[r] = bf16x2-free f16x2 (row r @ k_a, row r @ k_b)
-__device__ __forceinline__ void decode_q4_pair(uint32_t w1, uint32_t w2, uint32_t sel_lo, uint32_t sel_hi,
-                                               uint32_t (&a)[8]) {
-  constexpr uint32_t kLoMagic = 0x64006400u;  // f16x2 (1024, 1024)
-  constexpr uint32_t kHiMagic = 0x54005400u;  // f16x2 (64, 64)
-  const uint32_t r0 = prmt(w1, w2, sel_lo);   // [k_a rows 0-3 | k_b rows 0-3]
-  const uint32_t r1 = prmt(w1, w2, sel_hi);   // rows 4-7
-  const uint32_t r0s = r0 >> 8, r1s = r1 >> 8;
-  a[0] = f16x2_sub(lop3<kLutAndOr>(r0, 0x000F000Fu, kLoMagic), kLoMagic);
-  a[1] = f16x2_sub(lop3<kLutAndOr>(r0, 0x00F000F0u, kHiMagic), kHiMagic);
-  a[2] = f16x2_sub(lop3<kLutAndOr>(r0s, 0x000F000Fu, kLoMagic), kLoMagic);
-  a[3] = f16x2_sub(lop3<kLutAndOr>(r0s, 0x00F000F0u, kHiMagic), kHiMagic);
-  a[4] = f16x2_sub(lop3<kLutAndOr>(r1, 0x000F000Fu, kLoMagic), kLoMagic);
-  a[5] = f16x2_sub(lop3<kLutAndOr>(r1, 0x00F000F0u, kHiMagic), kHiMagic);
-  a[6] = f16x2_sub(lop3<kLutAndOr>(r1s, 0x000F000Fu, kLoMagic), kLoMagic);
-  a[7] = f16x2_sub(lop3<kLutAndOr>(r1s, 0x00F000F0u, kHiMagic), kHiMagic);
-}
-
-// As decode_q4_pair without the subtract: even rows come out as 1024 + n, odd
-// rows as 64 + n (both exact in f16); the caller folds the offsets.
+// q4: decode the 8 rows of one k-pair from two 32-bit words (k_a and k_b bytes of
+// rows h*8..h*8+7, 2 rows per byte); out[r] = f16x2 (row r @ k_a, row r @ k_b).
+// Even rows come out as 1024 + n (low nibble under the 1024 exponent pattern),
+// odd rows as 64 + n (high nibble under 64's): both exact in f16, no subtract;
+// the caller folds the offsets into the m term.
 __device__ __forceinline__ void decode_q4_pair_biased(uint32_t w1, uint32_t w2, uint32_t sel_lo, uint32_t sel_hi,
                                                       uint32_t (&a)[8]) {
   constexpr uint32_t kLoMagic = 0x64006400u, kHiMagic = 0x54005400u;
