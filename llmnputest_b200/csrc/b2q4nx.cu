@@ -482,6 +482,15 @@ int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_row
   if (!aligned(workspace, 256)) return fail(B2_ERR_ALIGN, "workspace must be 256-byte aligned");
 
   const int npad = tc_npad(batch);
+  const int n_row_tiles = epi == b2::kTcEpiSwiglu ? (n_tile_rows + 1) / 2 : (n_tile_rows + 3) / 4;
+  // SwiGLU cannot split K (its epilogue needs whole sums), so when the row tiles
+  // leave SMs idle the token columns are split over CTAs instead (each CTA
+  // dequantises the same tiles, runs 1/n of the MMAs and reads 1/n of x)
+  int n_nsplit = 1;
+  if (epi == b2::kTcEpiSwiglu)
+    while (npad % (2 * n_nsplit * 16) == 0 && npad / (2 * n_nsplit) >= 64 && n_row_tiles * 2 * n_nsplit <= di.sms)
+      n_nsplit *= 2;  // columns per CTA stay a multiple of 16 (MMA N) and >= 64
+  const int ncta = npad / n_nsplit;
   const int budget = di.smem_optin - 1024;  // alignment slack for the 1024-byte operand atoms
   // pipeline: double-buffered A slices when they fit beside >= 2 raw and >= 2 x stages
   int raw_stages = 0, x_stages = 0, a_bufs = tuning().tc_abufs > 0 ? tuning().tc_abufs : 2;
@@ -489,15 +498,14 @@ int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_row
   const int max_x = tuning().tc_xst > 0 ? tuning().tc_xst : 8;
   for (; a_bufs >= 1 && x_stages < 2; --a_bufs) {
     for (raw_stages = max_raw; raw_stages >= 2; --raw_stages) {
-      const b2::TcSmem base(npad, raw_stages, 0, a_bufs);
-      x_stages = std::min(max_x, (budget - base.total) / (npad * 128 + 16));
+      const b2::TcSmem base(ncta, raw_stages, 0, a_bufs);
+      x_stages = std::min(max_x, (budget - base.total) / (ncta * 128 + 16));
       if (x_stages >= 2) break;
     }
   }
   ++a_bufs;  // undo the loop's last decrement
   if (x_stages < 2) return fail(B2_ERR_UNSUPPORTED, "shared memory too small for the tensor-core GEMM");
-  const int smem = b2::TcSmem(npad, raw_stages, x_stages, a_bufs).total + 1024;
-  const int n_row_tiles = epi == b2::kTcEpiSwiglu ? (n_tile_rows + 1) / 2 : (n_tile_rows + 3) / 4;
+  const int smem = b2::TcSmem(ncta, raw_stages, x_stages, a_bufs).total + 1024;
   // split-K (fp32 form only) so that small projections still occupy every SM
   // split-K (fp32 form only) so that small projections still occupy every SM, in
   // one wave: row tiles x splits <= SMs
@@ -548,6 +556,8 @@ int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_row
   p.n_row_tiles = n_row_tiles;
   p.n_splits = n_splits;
   p.kt_per_split = kt_per_split;
+  p.n_nsplit = n_nsplit;
+  p.ncta = ncta;
   auto kernel = epi == b2::kTcEpiSwiglu ? b2::q4_gemm_tc_kernel<b2::kTcEpiSwiglu> : b2::q4_gemm_tc_kernel<b2::kTcEpiF32>;
   static int attr_set[64][2] = {};
   int dev = 0;
@@ -557,7 +567,7 @@ int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_row
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tensor-core GEMM)");
     attr_set[dev][epi] = 1;
   }
-  cfg.gridDim = dim3(std::min(n_row_tiles * n_splits, di.sms), 1, 1);
+  cfg.gridDim = dim3(std::min(n_row_tiles * n_splits * n_nsplit, di.sms), 1, 1);
   cfg.blockDim = dim3(b2::kTcThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   e = cudaLaunchKernelEx(&cfg, kernel, p);

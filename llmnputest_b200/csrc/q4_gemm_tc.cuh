@@ -64,6 +64,8 @@ struct TcParams {
   int n_row_tiles;  // CTA tiles of 128 output rows (SwiGLU: 64 gate + 64 up rows)
   int n_splits;     // split-K: work item = (row tile, K range); partials added with fp32 reductions
   int kt_per_split;
+  int n_nsplit;     // token columns split over CTAs: item = (row tile, K range, column block)
+  int ncta;         // token columns per CTA (npad / n_nsplit, a multiple of 16)
 };
 
 struct TcSmem {
@@ -190,7 +192,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled operand slices
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  const TcSmem L(p.npad, p.raw_stages, p.x_stages, p.a_bufs);
+  const TcSmem L(p.ncta, p.raw_stages, p.x_stages, p.a_bufs);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar);
   const int RS = p.raw_stages, XS = p.x_stages;
   uint64_t* raw_full = bars;
@@ -206,8 +208,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int npad = p.npad;
-  const uint32_t ncols = npad <= 32 ? 32u : (npad <= 64 ? 64u : (npad <= 128 ? 128u : 256u));  // per buffer
+  const int npad = p.npad, ncta = p.ncta;
+  const uint32_t ncols = ncta <= 32 ? 32u : (ncta <= 64 ? 64u : (ncta <= 128 ? 128u : 256u));  // per buffer
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < RS; ++s) {
@@ -241,10 +243,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
   pdl_launch_dependents();
 
   const int KT = p.k_tiles;
-  const int n_items = p.n_row_tiles * p.n_splits;  // work item -> (row tile, K-tile range)
+  const int n_items = p.n_row_tiles * p.n_splits * p.n_nsplit;  // -> (row tile, K-tile range, column block)
   const int AB = p.a_bufs;
-  auto item_tile = [&](int it) { return it / p.n_splits; };
-  auto item_k0 = [&](int it) { return (it % p.n_splits) * p.kt_per_split; };
+  auto item_tile = [&](int it) { return (it / p.n_nsplit) / p.n_splits; };
+  auto item_k0 = [&](int it) { return ((it / p.n_nsplit) % p.n_splits) * p.kt_per_split; };
+  auto item_n0 = [&](int it) { return (it % p.n_nsplit) * ncta; };
   auto item_k1 = [&](int it) { return min(KT, item_k0(it) + p.kt_per_split); };
 
   if (warp == 0) {
@@ -287,9 +290,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
             if (xseq >= static_cast<uint32_t>(XS) &&
                 !mbar_wait_bounded(smem_u32(&x_empty[xs]), ((xseq / XS) & 1) ^ 1, abort_flag, kDevTimeoutEmpty))
               break;
-            const uint32_t xbytes = static_cast<uint32_t>(npad) * 128;
+            // this CTA's token rows n0.. of the slice: contiguous, and their swizzle
+            // pattern is the slice's (n0 is a multiple of 8 rows)
+            const uint32_t xbytes = static_cast<uint32_t>(ncta) * 128;
             mbar_arrive_expect_tx(smem_u32(&x_full[xs]), xbytes);
-            bulk_g2s(smem_u32(smem + L.x + xs * xbytes), p.xsw + static_cast<size_t>(kt * 4 + js) * xbytes, xbytes,
+            bulk_g2s(smem_u32(smem + L.x + xs * xbytes),
+                     p.xsw + (static_cast<size_t>(kt * 4 + js) * npad + item_n0(it)) * 128, xbytes,
                      smem_u32(&x_full[xs]), keep);
           }
         }
@@ -299,13 +305,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
     // ------------------------------------------------------------ MMA
     if (lane == 0) {
       pdl_wait();
-      const uint32_t idesc = umma_idesc_f16(kTcM, npad);
+      const uint32_t idesc = umma_idesc_f16(kTcM, ncta);
       // ring positions advance by increments (no division in the issue loop: the
       // tensor pipe drains if the issuing thread spends ~100 cycles between MMAs)
       int ab = 0, xs = 0;
       uint32_t aph = 0, xph = 0, t_it = 0;
       const uint32_t a0 = smem_u32(smem + L.a), x0 = smem_u32(smem + L.x);
-      const uint32_t xbytes = static_cast<uint32_t>(npad) * 128;
+      const uint32_t xbytes = static_cast<uint32_t>(ncta) * 128;
       bool issued_any = false;
       for (int it = blockIdx.x; it < n_items && !*abort_flag; it += gridDim.x, ++t_it) {
         const int buf = t_it & 1;
@@ -365,13 +371,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
     uint32_t t_it = 0;
     for (int it = blockIdx.x; it < n_items; it += gridDim.x, ++t_it) {
       const int tile = item_tile(it);
+      const int n0 = item_n0(it);
       const int buf = t_it & 1;
       const bool ok = mbar_wait_bounded(smem_u32(&acc_full[buf]), (t_it >> 1) & 1, abort_flag, kDevTimeoutFull);
       tc_fence_after();
       const uint32_t t_row = tmem_base + buf * ncols + (static_cast<uint32_t>(q * 32) << 16);
-      for (int c0 = 0; c0 < npad; c0 += 32) {
+      for (int c0 = n0; c0 < n0 + ncta; c0 += 32) {  // c0: global token column
         uint32_t r[32];
-        tmem_ld32(t_row + c0, r);
+        tmem_ld32(t_row + (c0 - n0), r);
         // the 32 columns' x scales (shared table), read before any store below
         float u2v[32];
 #pragma unroll

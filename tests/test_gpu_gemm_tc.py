@@ -85,6 +85,34 @@ def test_swiglu_gemm_matches_gemv(cuda, n_t, k_t, bsz):
     assert ops.device_error() == 0
 
 
+@pytest.mark.parametrize("n_t,k_t,bsz", [(8, 2, 256), (6, 3, 192), (10, 1, 128)])
+def test_swiglu_gemm_column_split_vs_oracle(cuda, n_t, k_t, bsz):
+    """Large batches split the token columns of the SwiGLU GEMM over CTAs (each CTA
+    one column block of one row tile): every token against the numpy oracle
+    (gate/up GEMVs in fp32, both narrowed to bf16 before SiLU, granite_mlp.py:172-181)."""
+    from llmnputest_b200 import ops
+    rng = np.random.default_rng(500 + n_t * 7 + bsz)
+    gate = orc.synth_q4_tiles(rng, n_t * k_t)
+    up = orc.synth_q4_tiles(rng, n_t * k_t)
+    x = orc.synth_bf16(rng, (bsz, k_t * 256)).astype(np.float32)
+    h = ops.q4_swiglu_gemm(dev_u8(gate), dev_u8(up), n_t, k_t, dev_bf16(x))
+    torch.cuda.synchronize()
+    bf = lambda a: torch.from_numpy(np.asarray(a, np.float32)).to(torch.bfloat16).float().numpy()
+    g = bf(orc.gemv_q4(gate, x, n_t, k_t))
+    u = bf(orc.gemv_q4(up, x, n_t, k_t))
+    ref = g / (1.0 + np.exp(-g.astype(np.float64))) * u
+    # fp16 weights vs exact ones, then two bf16 roundings before SiLU: a token can
+    # move a bf16 ulp on both g and u (2 x 2^-8)
+    _check(h.float().cpu().numpy(), ref, 0.9999, 2e-2, ("swiglu split", bsz))
+    # the column blocks compute exactly what one unsplit CTA computes for the same
+    # tokens (batches of <= 48 are never split): bit-identical
+    hd = h.cpu()
+    for t0 in range(0, bsz, 48):
+        sub = ops.q4_swiglu_gemm(dev_u8(gate), dev_u8(up), n_t, k_t, dev_bf16(x[t0:t0 + 48]))
+        assert torch.equal(sub.cpu(), hd[t0:t0 + 48]), ("column block differs", t0)
+    assert ops.device_error() == 0
+
+
 def test_gemm_argument_errors(cuda):
     from llmnputest_b200 import _native, ops
     w = torch.zeros(4 * 5120, dtype=torch.uint8, device=cuda)
