@@ -85,7 +85,7 @@ def test_swiglu_gemm_matches_gemv(cuda, n_t, k_t, bsz):
     assert ops.device_error() == 0
 
 
-@pytest.mark.parametrize("n_t,k_t,bsz", [(8, 2, 256), (6, 3, 192), (10, 1, 128)])
+@pytest.mark.parametrize("n_t,k_t,bsz", [(8, 2, 256), (6, 3, 192), (10, 1, 128), (112, 4, 256)])
 def test_swiglu_gemm_column_split_vs_oracle(cuda, n_t, k_t, bsz):
     """Large batches split the token columns of the SwiGLU GEMM over CTAs (each CTA
     one column block of one row tile): every token against the numpy oracle
