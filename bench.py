@@ -331,6 +331,8 @@ def measure_attention(torch, ops, gen, device, hbm_peak: float, steps: int) -> l
 
     Algorithmic bytes per call: B*ctx*8*64*2*2 (the bf16 K and V read once).  Each graph
     replay rotates over a pool of caches whose total is above L2, so every call reads HBM.
+    Calls use B2_ATTN_PREFETCH_KV as the decoders do: pos is constant and a call writes
+    only row pos of its cache, so rows before pos are final when the next call launches.
     """
     hq, hkv, d = 40, 8, 64
     out = []
@@ -352,7 +354,8 @@ def measure_attention(torch, ops, gen, device, hbm_peak: float, steps: int) -> l
             def calls(pool=pool, qkv=qkv, pos=pos, o=o, ws=ws, ctx=ctx):
                 for kc, vc in pool:
                     ops.gqa_decode(qkv[:, :hq * d], qkv[:, hq * d:(hq + hkv) * d], qkv[:, (hq + hkv) * d:], kc, vc,
-                                   pos, n_q_heads=hq, n_kv_heads=hkv, max_len=ctx, out=o, workspace=ws)
+                                   pos, n_q_heads=hq, n_kv_heads=hkv, max_len=ctx, out=o, workspace=ws,
+                                   prefetch_kv=True)
 
             g = graph_of(torch, calls)
             reps = max(3, min(200, int(steps * 2e6 / (kv_bytes * n_pool) + 1)))

@@ -66,24 +66,27 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-// Half-split RoPE of one head (D fp32 values at src) into bf16 dst, fp64 angles;
-// this thread handles the pair (i, i + D/2).  rope == 0 rounds without rotating.
+// Half-split RoPE: the angle of pair (i, i + D/2) at pos, evaluated in fp64 and
+// rounded to fp32 cos/sin.
 template <int D>
-__device__ __forceinline__ void rope_head_bf16(const float* src, __nv_bfloat16* dst, int pos, float theta, int i,
-                                               int rope) {
-  if (!rope) {
-    dst[i] = __float2bfloat16_rn(src[i]);
-    dst[i + D / 2] = __float2bfloat16_rn(src[i + D / 2]);
-    return;
-  }
+__device__ __forceinline__ void rope_angle(int pos, float theta, int i, float& c, float& s) {
   const double inv = pow(static_cast<double>(theta), -2.0 * i / D);
   double sn, cs;
   sincos(static_cast<double>(pos) * inv, &sn, &cs);
-  const float c = static_cast<float>(cs), s = static_cast<float>(sn);
-  const float x0 = src[i], x1 = src[i + D / 2];
-  dst[i] = __float2bfloat16_rn(x0 * c - x1 * s);
-  dst[i + D / 2] = __float2bfloat16_rn(x1 * c + x0 * s);
+  c = static_cast<float>(cs);
+  s = static_cast<float>(sn);
 }
+
+// Rotation of one head's pair (i, i + D/2) (D fp32 values at src) by the angle
+// (c, s) of pair i into bf16 dst; rope == 0 rounds without rotating.
+template <int D>
+__device__ __forceinline__ void rope_apply_bf16(const float* src, __nv_bfloat16* dst, int i, float c, float s,
+                                                int rope) {
+  const float x0 = src[i], x1 = src[i + D / 2];
+  dst[i] = __float2bfloat16_rn(rope ? x0 * c - x1 * s : x0);
+  dst[i + D / 2] = __float2bfloat16_rn(rope ? x1 * c + x0 * s : x1);
+}
+
 
 template <int D, int W>
 __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) gqa_decode_kernel(const AttnParams p) {
@@ -94,6 +97,7 @@ __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) gqa_decode_kernel(cons
   __shared__ __align__(16) uint32_t q_s[16 * QW];        // bf16x2, 16 head rows (rows >= grp zero)
   __shared__ float wm[kAttnWarps][16], wl[kAttnWarps][16];
   __shared__ float wo[kAttnWarps][16][D + 1];
+  __shared__ float rope_cs[2][D / 2];  // cos, sin of each pair's angle at pos
 
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int grp = p.hq / p.hkv;
@@ -140,17 +144,21 @@ __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) gqa_decode_kernel(cons
   const bool pre1 = pre0 && w_lo + kAttnChunk < w_hi && early_ok(w_lo + kAttnChunk);
   if (pre0) load_chunk(w_lo, kr, vr);
   if (pre1) load_chunk(w_lo + kAttnChunk, kn, vn);
+  // the rotation angles depend on pos only: with prefetch_kv (pos final at launch)
+  // their fp64 evaluation runs before the wait, off the dependent path
+  if (p.prefetch_kv && threadIdx.x < D / 2 && p.rope) rope_angle<D>(pos, p.theta, threadIdx.x, rope_cs[0][threadIdx.x], rope_cs[1][threadIdx.x]);
   if (p.prefetch_kv) pdl_wait();
+  if (!p.prefetch_kv && threadIdx.x < D / 2 && p.rope) rope_angle<D>(pos, p.theta, threadIdx.x, rope_cs[0][threadIdx.x], rope_cs[1][threadIdx.x]);
 
   // ---- q heads of the group: rope -> bf16 -> shared (rows >= grp are zero)
   {
     __nv_bfloat16* qh = reinterpret_cast<__nv_bfloat16*>(q_s);
     for (int e = threadIdx.x; e < 16 * QW * 2; e += kAttnThreads) qh[e] = __float2bfloat16_rn(0.f);
-    __syncthreads();
+    __syncthreads();  // also publishes rope_cs
     for (int e = threadIdx.x; e < grp * (D / 2); e += kAttnThreads) {
       const int j = e / (D / 2), i = e % (D / 2);
       const float* src = p.q + static_cast<size_t>(b) * p.ld_new + (kvh * grp + j) * D;
-      rope_head_bf16<D>(src, qh + j * QW * 2, pos, p.theta, i, p.rope);
+      rope_apply_bf16<D>(src, qh + j * QW * 2, i, rope_cs[0][i], rope_cs[1][i], p.rope);
     }
     // the split that holds the new position appends its k (rotated) and v
     if (p.append && pos >= lo && pos < hi) {
@@ -158,7 +166,7 @@ __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) gqa_decode_kernel(cons
       const float* ks = p.k_new + static_cast<size_t>(b) * p.ld_new + kvh * D;
       const float* vs = p.v_new + static_cast<size_t>(b) * p.ld_new + kvh * D;
       for (int i = threadIdx.x; i < D / 2; i += kAttnThreads)
-        rope_head_bf16<D>(ks, p.k_cache + row, pos, p.theta, i, p.rope);
+        rope_apply_bf16<D>(ks, p.k_cache + row, i, rope_cs[0][i], rope_cs[1][i], p.rope);
       for (int i = threadIdx.x; i < D; i += kAttnThreads) p.v_cache[row + i] = __float2bfloat16_rn(vs[i]);
     }
     __syncthreads();
