@@ -22,10 +22,9 @@
 //     LOP3 per nibble against an fp16 exponent pattern yields an exact value
 //     with no shift: low nibble n | 0x6400 = 1024 + n, high nibble (n<<4) |
 //     0x5400 = 64 + n; an exact f16x2 subtract leaves n.
-//   * a q8 byte c is split into the nibbles of u = c ^ 0x80 (= c + 128):
-//     (u & 0xF) | 0x6400 = 1024 + ul and (u & 0xF0) | 0x6400 = 1024 + 16*uh,
-//     both exact; two MMAs against x' sum to (2176 + c)*x', and the constant
-//     2176*s folds exactly into the sum-of-x term (m = -2176*s).
+//   * a q8 byte c becomes one exact fp16 with one LOP3: (c & 0xFF) ^ 0x6480 =
+//     0x6400 | (c + 128) = 1152 + c; one MMA against x' gives (1152 + c)*x', and
+//     the constant 1152*s folds into the sum-of-x term (m = -1152*s).
 // Every product is exact in fp32; the only rounding is fp32 accumulation.
 //
 // Data flow per CTA (a "row group" = 4 tile-rows = 128 outputs, or for the
@@ -167,16 +166,12 @@ __device__ __forceinline__ void decode_q4_pair_biased(uint32_t w1, uint32_t w2, 
   a[7] = lop3<kLutAndOr>(r1s, 0x00F000F0u, kHiMagic);
 }
 
-// q8: two rows (bytes 0 and 1 of a PRMT result) -> (1024+ul) and (1024+16*uh) per row.
-__device__ __forceinline__ void decode_q8_res(uint32_t res, uint32_t& lo0, uint32_t& hi0, uint32_t& lo1,
-                                              uint32_t& hi1) {
-  constexpr uint32_t kMagic = 0x64006400u;
-  constexpr uint32_t kMagicFlip = 0x64806480u;  // 0x6400 | flip of the high nibble's top bit (c ^ 0x80)
-  const uint32_t rs = res >> 8;
-  lo0 = lop3<kLutAndOr>(res, 0x000F000Fu, kMagic);
-  hi0 = lop3<kLutAndXor>(res, 0x00F000F0u, kMagicFlip);
-  lo1 = lop3<kLutAndOr>(rs, 0x000F000Fu, kMagic);
-  hi1 = lop3<kLutAndXor>(rs, 0x00F000F0u, kMagicFlip);
+// q8: a PRMT result [row A @k, row B @k, row A @k+1, row B @k+1] -> f16x2
+// (A @k, A @k+1) and (B @k, B @k+1), each code c as 1152 + c (exact).
+__device__ __forceinline__ void decode_q8_pair(uint32_t res, uint32_t& ra, uint32_t& rb) {
+  constexpr uint32_t kMagicFlip = 0x64806480u;  // 0x6400 | flip of bit 7 (c ^ 0x80 = c + 128)
+  ra = lop3<kLutAndXor>(res, 0x00FF00FFu, kMagicFlip);
+  rb = lop3<kLutAndXor>(res >> 8, 0x00FF00FFu, kMagicFlip);
 }
 
 // q4 nibbles of 4 rows at (k_a, k_b) -> bf16x2 codes 128 + n (exact, no subtract:
@@ -729,24 +724,21 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
 #pragma unroll
               for (int hh = 0; hh < 2; ++hh) {  // rows 4q+2hh, 4q+2hh+1 = MMA s
                 const uint32_t sel = hh ? 0x7632u : 0x5410u;
-                uint32_t pl0, ph0, pl1, ph1, ql0, qh0, ql1, qh1;
-                decode_q8_res(prmt(paw[q], pbw[q], sel), pl0, ph0, pl1, ph1);
-                decode_q8_res(prmt(qaw[q], qbw[q], sel), ql0, qh0, ql1, qh1);
+                uint32_t pA, pB, qA, qB;  // rows 4q+2hh (A) and 4q+2hh+1 (B) at (k, k+1), (k+8, k+9)
+                decode_q8_pair(prmt(paw[q], pbw[q], sel), pA, pB);
+                decode_q8_pair(prmt(qaw[q], qbw[q], sel), qA, qB);
                 const int s = 2 * q + hh;
 #pragma unroll
-                for (int n = 0; n < NB; ++n) {
+                for (int n = 0; n < NB; ++n)
                   mma_f16_m16n8k16(part[s][4 * n], part[s][4 * n + 1], part[s][4 * n + 2], part[s][4 * n + 3],
-                                   pl0, pl1, ql0, ql1, bx[n][0], bx[n][1]);
-                  mma_f16_m16n8k16(part[s][4 * n], part[s][4 * n + 1], part[s][4 * n + 2], part[s][4 * n + 3],
-                                   ph0, ph1, qh0, qh1, bx[n][0], bx[n][1]);
-                }
+                                   pA, pB, qA, qB, bx[n][0], bx[n][1]);
               }
             }
           }
         }
 
         // fold this k-block: tot += d*part + m'*sum(x'), m' = m - code offset * d
-        // (q4: offset 1024 for even rows, 64 for odd rows; q8: m' = -2176*s)
+        // (q4: offset 1024 for even rows, 64 for odd rows; q8: m' = -1152*s)
         const uint8_t* meta = tl + (kb * 32 + rb * 16 + h * 8) * 2;
         const uint4 dv = *reinterpret_cast<const uint4*>(meta);
         const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
@@ -767,8 +759,8 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 2 : 1) q4nx_gemv_kerne
             ma = fmaf(-1024.f, da, bf16lo_to_f32(mw[s]));
             mb = fmaf(-64.f, db, bf16hi_to_f32(mw[s]));
           } else {
-            ma = -2176.f * da;
-            mb = -2176.f * db;
+            ma = -1152.f * da;
+            mb = -1152.f * db;
           }
 #pragma unroll
           for (int n = 0; n < NB; ++n) {
