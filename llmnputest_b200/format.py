@@ -106,6 +106,62 @@ def dequant_q8(raw: bytes) -> np.ndarray:
     return _decode_tiles_bf16(bytes(raw), q8=True)
 
 
+def upload_segments(segs: list[np.ndarray], device=None, chunk_bytes: int = 32 << 20):
+    """Concatenate uint8 host arrays into one device tensor through pinned staging.
+
+    Two pinned buffers alternate: while the DMA of chunk i runs on a side stream the
+    host fills the other buffer with chunk i + 1 (from page cache or disk when the
+    segments are views of a mapped file).  The call returns once the copies are done
+    (the staging buffers are released with it).
+    """
+    import torch
+    dev = torch.device(device) if device is not None else _device()
+    total = sum(int(s.size) for s in segs)
+    out = torch.empty(total, dtype=torch.uint8, device=dev)
+    if dev.type != "cuda":
+        o = out.numpy()
+        off = 0
+        for s in segs:
+            o[off:off + s.size] = s
+            off += s.size
+        return out
+    if total == 0:
+        return out
+    chunk = max(1, min(int(chunk_bytes), total))
+    stage = [torch.empty(chunk, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
+    done = [torch.cuda.Event(), torch.cuda.Event()]
+    used = [False, False]
+    cs = torch.cuda.Stream(dev)
+    cs.wait_stream(torch.cuda.current_stream(dev))  # `out` was allocated on the current stream
+    i = 0
+    dst = 0
+    pieces = iter(segs)
+    cur, pos = next(pieces), 0
+    while dst < total:
+        b = i & 1
+        if used[b]:
+            done[b].synchronize()  # the DMA that last read this buffer has finished
+        buf = stage[b].numpy()
+        fill = 0
+        while fill < chunk and dst + fill < total:  # gather the next chunk from the segments
+            if pos == cur.size:
+                cur, pos = next(pieces), 0
+                continue
+            m = min(chunk - fill, cur.size - pos)
+            buf[fill:fill + m] = cur[pos:pos + m]
+            fill += m
+            pos += m
+        with torch.cuda.stream(cs):
+            out[dst:dst + fill].copy_(stage[b][:fill], non_blocking=True)
+            done[b].record(cs)
+        used[b] = True
+        dst += fill
+        i += 1
+    cs.synchronize()
+    out.record_stream(cs)
+    return out
+
+
 class Q4NX:
     """A .q4nx model file (tools/q4nx.py:152-197 interface)."""
 
@@ -117,6 +173,7 @@ class Q4NX:
             self.header = read_header(f)
             self._data_start = f.tell()
         self.header.pop("__metadata__", None)
+        self._mm = None
 
     def __contains__(self, name: str) -> bool:
         return name in self.header
@@ -158,11 +215,56 @@ class Q4NX:
             raise ValueError(f"{name}: K={k} but the file holds {k_t} K-tiles")
         return int(n_t), int(k_t), int(tb)
 
-    def device_tiles(self, name: str, device=None):
-        """The tensor's raw tile bytes as a resident uint8 CUDA tensor (uploaded once)."""
-        import torch
-        dev = device if device is not None else _device()
-        return torch.frombuffer(bytearray(self.raw(name)), dtype=torch.uint8).to(dev)
+    def raw_view(self, name: str) -> np.ndarray:
+        """The tensor's bytes as a read-only uint8 view of the file (mmap, no copy)."""
+        if self._mm is None:
+            self._mm = np.memmap(self.path, dtype=np.uint8, mode="r")
+        first, last = self.header[name]["data_offsets"]
+        return self._mm[self._data_start + first:self._data_start + last]
+
+    def tile_segments(self, name: str, tile_rows=None, k_tiles=None, n: int | None = None,
+                      k: int | None = None) -> list[np.ndarray]:
+        """Contiguous pieces of a tiled weight's bytes, as stored, for a slice of it.
+
+        tile_rows: the tile-rows to keep, in the order given (a TP shard's rows, e.g.
+        `ShardPlan.qkv_tile_rows()`), default all; k_tiles: (k0, k1), the K-tiles to
+        keep of each row (a K shard, whole 256-wide tiles), default all.  The slice of
+        a [n_t][k_t][tile] weight is itself [rows][k1 - k0][tile].  n / k: the logical
+        shape, needed when the stored shape is 2-D (see `tiled_shape`).
+        """
+        n_t, k_t, tb = self.tiled_shape(name, n, k)
+        view = self.raw_view(name)
+        rows = list(range(n_t)) if tile_rows is None else [int(r) for r in tile_rows]
+        k0, k1 = (0, k_t) if k_tiles is None else (int(k_tiles[0]), int(k_tiles[1]))
+        if not 0 <= k0 < k1 <= k_t:
+            raise ValueError(f"{name}: K-tiles {k0}..{k1} outside 0..{k_t}")
+        if not rows or min(rows) < 0 or max(rows) >= n_t:
+            raise ValueError(f"{name}: tile-rows must lie in 0..{n_t - 1}")
+        segs: list[np.ndarray] = []
+        start = prev = None
+        for r in rows + [None]:  # whole rows: merge consecutive ones into one piece
+            if r is not None and prev is not None and r == prev + 1 and (k0, k1) == (0, k_t):
+                prev = r
+                continue
+            if start is not None:
+                segs.append(view[(start * k_t + k0) * tb:(prev * k_t + k1) * tb])
+            start = prev = r
+        return segs
+
+    def device_tiles(self, name: str, device=None, *, tile_rows=None, k_tiles=None, n: int | None = None,
+                     k: int | None = None, chunk_bytes: int = 32 << 20):
+        """The tensor's raw tile bytes (or a slice of them, see `tile_segments`) as a
+        resident uint8 tensor, uploaded once.
+
+        The bytes go from the mmap of the file through two pinned staging buffers of
+        `chunk_bytes`: the host copy of one chunk overlaps the DMA of the previous one
+        on a side stream.  Returns once the data is on the device.
+        """
+        if tile_rows is None and k_tiles is None:
+            segs = [self.raw_view(name)]
+        else:
+            segs = self.tile_segments(name, tile_rows, k_tiles, n, k)
+        return upload_segments(segs, device, chunk_bytes)
 
     def device_tensor(self, name: str, shape: tuple[int, int] | None = None, device=None):
         """Dequantised, untiled float32 [N, K] CUDA tensor (decoded on the GPU)."""

@@ -67,6 +67,26 @@ def test_reader_header_and_raw(container_path, golden):
         f.tiled_shape("model.layers.0.mlp.down_proj.weight", n=128, k=768)
 
 
+def test_reader_mmap_slices(container_path):
+    """raw_view (mmap) equals raw(); TP slices of whole tile-rows / K-tiles are the
+    stored bytes of exactly those tiles (tools/q4nx.py:170-197 layout), in the order asked."""
+    f = fmt.Q4NX(container_path)
+    for name in f.names():
+        assert bytes(f.raw_view(name)) == f.raw(name)
+    lm = np.frombuffer(f.raw("lm_head.weight"), np.uint8).reshape(2, 4, 8704)  # [n_t][k_t][tile]
+    got = f.device_tiles("lm_head.weight", "cpu", tile_rows=[1]).numpy()
+    assert np.array_equal(got, lm[1].reshape(-1))
+    got = f.device_tiles("lm_head.weight", "cpu", tile_rows=[1, 0], k_tiles=(1, 3)).numpy()
+    assert np.array_equal(got, lm[[1, 0], 1:3].reshape(-1))
+    down = np.frombuffer(f.raw("model.layers.0.mlp.down_proj.weight"), np.uint8).reshape(2, 3, 5120)
+    got = f.device_tiles("model.layers.0.mlp.down_proj.weight", "cpu", k_tiles=(2, 3), n=64).numpy()
+    assert np.array_equal(got, down[:, 2:3].reshape(-1))
+    assert len(f.tile_segments("model.layers.0.mlp.gate_proj.weight", [0, 1, 2])) == 1  # merged rows
+    for bad in ({"tile_rows": [2]}, {"tile_rows": []}, {"k_tiles": (3, 3)}, {"k_tiles": (0, 5)}):
+        with pytest.raises(ValueError):
+            f.tile_segments("lm_head.weight", **bad)
+
+
 def test_split_q4_tile_roundtrip(golden):
     t = golden["fmt_q4_tiles"][0]
     nib, d, m = fmt.split_q4_tile(t.tobytes())

@@ -80,6 +80,23 @@ def test_attach_lm_head(container_path, monkeypatch):
 
 
 @pytest.mark.gpu
+def test_reader_upload_through_pinned_staging(container_path):
+    """Chunked pinned-staging uploads land the stored bytes on the GPU unchanged: whole
+    tensors and TP slices, with chunks smaller than, equal to and larger than a segment."""
+    import torch
+    f = fmt.Q4NX(container_path)
+    lm = np.frombuffer(f.raw("lm_head.weight"), np.uint8).reshape(2, 4, 8704)
+    for chunk in (1000, 8704, 1 << 20):
+        t = f.device_tiles("lm_head.weight", chunk_bytes=chunk)
+        assert t.is_cuda and np.array_equal(t.cpu().numpy(), lm.reshape(-1))
+        t = f.device_tiles("lm_head.weight", tile_rows=[1, 0], k_tiles=(1, 4), chunk_bytes=chunk)
+        assert np.array_equal(t.cpu().numpy(), lm[[1, 0], 1:4].reshape(-1))
+    gate = f.device_tiles("model.layers.0.mlp.gate_proj.weight", chunk_bytes=4096)
+    assert np.array_equal(gate.cpu().numpy(), np.frombuffer(f.raw("model.layers.0.mlp.gate_proj.weight"), np.uint8))
+    torch.cuda.synchronize()
+
+
+@pytest.mark.gpu
 def test_reader_decodes_on_gpu(container_path, golden):
     """Q4NX.tensor() (GPU decode) equals the reference reader's float32 output bit for bit."""
     f = fmt.Q4NX(container_path)
