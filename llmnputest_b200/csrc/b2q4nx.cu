@@ -87,11 +87,15 @@ inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_
 //   B2Q4NX_MAX_STAGES    cap on the shared-memory pipeline depth (1..8)
 //   B2Q4NX_TC_SPLITS / _TC_RAW / _TC_XSTAGES / _TC_ABUFS   tensor-core GEMM split-K
 //                        count, raw and x pipeline depths, A buffers per slice
+//   B2Q4NX_ATTN_WAVE     0: attention splits as many as the 4-CTAs-per-SM target asks
+//                        (default 1: unclustered launches capped at one wave of
+//                        resident CTAs)
 struct Tuning {
   int max_cluster = 16;
   int ctas_per_sm = 0;
   int max_stages = b2::kMaxStages;
   int tc_splits = 0, tc_raw = 0, tc_xst = 0, tc_abufs = 0;  // tensor-core GEMM overrides (0 = plan)
+  int attn_wave = 1;  // attention: cap unclustered splits at one wave of resident CTAs
 };
 const Tuning& tuning() {
   static const Tuning t = [] {
@@ -103,6 +107,7 @@ const Tuning& tuning() {
     if (const char* e = getenv("B2Q4NX_TC_RAW")) v.tc_raw = std::max(0, std::min(4, atoi(e)));
     if (const char* e = getenv("B2Q4NX_TC_XSTAGES")) v.tc_xst = std::max(0, std::min(8, atoi(e)));
     if (const char* e = getenv("B2Q4NX_TC_ABUFS")) v.tc_abufs = std::max(0, std::min(2, atoi(e)));
+    if (const char* e = getenv("B2Q4NX_ATTN_WAVE")) v.attn_wave = atoi(e) != 0;
     return v;
   }();
   return t;
@@ -321,7 +326,9 @@ struct AttnPlan {
 // (decode-sized, < 64 MB) the splits of a (sequence, kv head) are capped at 16
 // and merged inside a cluster -- one launch; larger contexts take more splits
 // and merge in a second kernel through the caller's workspace.
-AttnPlan attn_plan(int batch, int hq, int hkv, int head_dim, int max_len, int sms) {
+// wave_cap: unclustered launches use at most one wave of resident CTAs (fewer,
+// longer splits); b2_gqa_decode_static plans without it (see there)
+AttnPlan attn_plan(int batch, int hq, int hkv, int head_dim, int max_len, int sms, bool wave_cap) {
   AttnPlan pl;
   const int pairs = batch * hkv;
   const int target = 4 * sms;
@@ -336,6 +343,20 @@ AttnPlan attn_plan(int batch, int hq, int hkv, int head_dim, int max_len, int sm
   int sl = (max_len + S - 1) / S;
   sl = (sl + 63) / 64 * 64;
   S = (max_len + sl - 1) / sl;
+  if (wave_cap && !pl.clustered) {
+    // at most one wave of resident CTAs: 8-warp CTAs fit two per SM, 4-warp ones
+    // three (the launcher's choice of warps, which itself depends on the split)
+    while (S > 1) {
+      const long long n_cta = static_cast<long long>(S) * pairs;
+      const bool wide = n_cta <= sms || sl >= 1024;
+      const long long slots = static_cast<long long>(wide ? 2 : 3) * sms;
+      if (n_cta <= slots) break;
+      const int S2 = std::max(1, std::min(S - 1, static_cast<int>(slots / pairs)));
+      sl = (max_len + S2 - 1) / S2;
+      sl = (sl + 63) / 64 * 64;
+      S = (max_len + sl - 1) / sl;
+    }
+  }
   pl.n_splits = S;
   pl.split_len = sl;
   if (S == 1) pl.clustered = 0;
@@ -644,14 +665,14 @@ int b2_gqa_decode_workspace_size(int batch, int n_q_heads, int n_kv_heads, int h
   if (!bytes) return fail(B2_ERR_ARG, "null bytes pointer");
   st = attn_check(batch, n_q_heads, n_kv_heads, head_dim, max_len, max_len);
   if (st != B2_OK) return st;
-  *bytes = attn_plan(batch, n_q_heads, n_kv_heads, head_dim, max_len, di.sms).ws_bytes;
+  *bytes = attn_plan(batch, n_q_heads, n_kv_heads, head_dim, max_len, di.sms, tuning().attn_wave != 0).ws_bytes;
   return B2_OK;
 }
 
-int b2_gqa_decode(const float* q, const float* k_new, const float* v_new, int ld_new, uint16_t* k_cache,
-                  uint16_t* v_cache, const int32_t* pos, int batch, int n_q_heads, int n_kv_heads, int head_dim,
-                  int ctx_max, int max_len, float theta, float scale, uint16_t* out, int ldo, void* workspace,
-                  size_t workspace_bytes, int flags, void* stream) {
+static int gqa_decode_impl(const float* q, const float* k_new, const float* v_new, int ld_new, uint16_t* k_cache,
+                           uint16_t* v_cache, const int32_t* pos, int batch, int n_q_heads, int n_kv_heads,
+                           int head_dim, int ctx_max, int max_len, float theta, float scale, uint16_t* out, int ldo,
+                           void* workspace, size_t workspace_bytes, int flags, void* stream, bool wave_cap) {
   DevInfo di;
   int st = device_info(&di);
   if (st != B2_OK) return st;
@@ -663,7 +684,7 @@ int b2_gqa_decode(const float* q, const float* k_new, const float* v_new, int ld
   if (!aligned(k_cache, 16) || !aligned(v_cache, 16)) return fail(B2_ERR_ALIGN, "KV caches must be 16-byte aligned");
   if ((flags & ~(B2_ATTN_NO_APPEND | B2_ATTN_NO_ROPE | B2_ATTN_OUT_F32 | B2_ATTN_PREFETCH_KV)) != 0)
     return fail(B2_ERR_ARG, "unknown flags 0x%x", flags);
-  const AttnPlan pl = attn_plan(batch, n_q_heads, n_kv_heads, head_dim, max_len, di.sms);
+  const AttnPlan pl = attn_plan(batch, n_q_heads, n_kv_heads, head_dim, max_len, di.sms, wave_cap);
   if (pl.n_splits > 1 && (!workspace || workspace_bytes < pl.ws_bytes))
     return fail(B2_ERR_WORKSPACE, "workspace of %zu bytes needed (b2_gqa_decode_workspace_size)", pl.ws_bytes);
   if (pl.n_splits > 65535) return fail(B2_ERR_ARG, "too many context splits");
@@ -743,6 +764,15 @@ int b2_gqa_decode(const float* q, const float* k_new, const float* v_new, int ld
   return B2_OK;
 }
 
+int b2_gqa_decode(const float* q, const float* k_new, const float* v_new, int ld_new, uint16_t* k_cache,
+                  uint16_t* v_cache, const int32_t* pos, int batch, int n_q_heads, int n_kv_heads, int head_dim,
+                  int ctx_max, int max_len, float theta, float scale, uint16_t* out, int ldo, void* workspace,
+                  size_t workspace_bytes, int flags, void* stream) {
+  return gqa_decode_impl(q, k_new, v_new, ld_new, k_cache, v_cache, pos, batch, n_q_heads, n_kv_heads, head_dim,
+                         ctx_max, max_len, theta, scale, out, ldo, workspace, workspace_bytes, flags, stream,
+                         tuning().attn_wave != 0);
+}
+
 int b2_gqa_decode_static(const float* q, const float* k_new, const float* v_new, int ld_new, uint16_t* k_cache,
                          uint16_t* v_cache, const int32_t* pos, int batch, int n_q_heads, int n_kv_heads,
                          int head_dim, int ctx_max, int max_len, float theta, float scale, uint16_t* out, int ldo,
@@ -752,7 +782,9 @@ int b2_gqa_decode_static(const float* q, const float* k_new, const float* v_new,
   if (st != B2_OK) return st;
   st = attn_check(batch, n_q_heads, n_kv_heads, head_dim, ctx_max, max_len);
   if (st != B2_OK) return st;
-  const AttnPlan pl = attn_plan(batch, n_q_heads, n_kv_heads, head_dim, max_len, di.sms);
+  // planned as specified for this entry point (no one-wave cap), so its scratch need
+  // and the size limit below stay what its documentation states
+  const AttnPlan pl = attn_plan(batch, n_q_heads, n_kv_heads, head_dim, max_len, di.sms, false);
   if (pl.ws_bytes > kAttnStaticScratchBytes)
     return fail(B2_ERR_WORKSPACE,
                 "this call needs %zu bytes of scratch, more than the %zu-byte static scratch of "
@@ -761,8 +793,8 @@ int b2_gqa_decode_static(const float* q, const float* k_new, const float* v_new,
   void* ws = nullptr;
   st = attn_static_scratch(&ws);
   if (st != B2_OK) return st;
-  return b2_gqa_decode(q, k_new, v_new, ld_new, k_cache, v_cache, pos, batch, n_q_heads, n_kv_heads, head_dim,
-                       ctx_max, max_len, theta, scale, out, ldo, ws, kAttnStaticScratchBytes, flags, stream);
+  return gqa_decode_impl(q, k_new, v_new, ld_new, k_cache, v_cache, pos, batch, n_q_heads, n_kv_heads, head_dim,
+                         ctx_max, max_len, theta, scale, out, ldo, ws, kAttnStaticScratchBytes, flags, stream, false);
 }
 
 int b2_rmsnorm(const void* x, int x_is_f32, int ldx, const uint16_t* w, float eps, int batch, int n, uint16_t* y,
