@@ -96,6 +96,9 @@ struct Tuning {
   int max_stages = b2::kMaxStages;
   int tc_splits = 0, tc_raw = 0, tc_xst = 0, tc_abufs = 0;  // tensor-core GEMM overrides (0 = plan)
   int attn_wave = 1;  // attention: cap unclustered splits at one wave of resident CTAs
+  // attention warps per CTA: 1 always 8 (measured equal or faster on every bench
+  // shape), 2 always 4, 0 by launch shape (8 for <= one CTA per SM or long splits)
+  int attn_wide = 1;
 };
 const Tuning& tuning() {
   static const Tuning t = [] {
@@ -108,6 +111,7 @@ const Tuning& tuning() {
     if (const char* e = getenv("B2Q4NX_TC_XSTAGES")) v.tc_xst = std::max(0, std::min(8, atoi(e)));
     if (const char* e = getenv("B2Q4NX_TC_ABUFS")) v.tc_abufs = std::max(0, std::min(2, atoi(e)));
     if (const char* e = getenv("B2Q4NX_ATTN_WAVE")) v.attn_wave = atoi(e) != 0;
+    if (const char* e = getenv("B2Q4NX_ATTN_WIDE")) v.attn_wide = std::max(0, std::min(2, atoi(e)));
     return v;
   }();
   return t;
@@ -326,6 +330,13 @@ struct AttnPlan {
 // (decode-sized, < 64 MB) the splits of a (sequence, kv head) are capped at 16
 // and merged inside a cluster -- one launch; larger contexts take more splits
 // and merge in a second kernel through the caller's workspace.
+// warps per attention CTA: 8, or under attn_wide 0, 4 for short splits over
+// more CTAs than SMs (more, smaller CTAs resident)
+bool attn_wide(long long n_cta, int split_len, int sms) {
+  if (tuning().attn_wide) return tuning().attn_wide == 1;
+  return n_cta <= sms || split_len >= 1024;
+}
+
 // wave_cap: unclustered launches use at most one wave of resident CTAs (fewer,
 // longer splits); b2_gqa_decode_static plans without it (see there)
 AttnPlan attn_plan(int batch, int hq, int hkv, int head_dim, int max_len, int sms, bool wave_cap) {
@@ -348,7 +359,7 @@ AttnPlan attn_plan(int batch, int hq, int hkv, int head_dim, int max_len, int sm
     // three (the launcher's choice of warps, which itself depends on the split)
     while (S > 1) {
       const long long n_cta = static_cast<long long>(S) * pairs;
-      const bool wide = n_cta <= sms || sl >= 1024;
+      const bool wide = attn_wide(n_cta, sl, sms);
       const long long slots = static_cast<long long>(wide ? 2 : 3) * sms;
       if (n_cta <= slots) break;
       const int S2 = std::max(1, std::min(S - 1, static_cast<int>(slots / pairs)));
@@ -715,10 +726,8 @@ static int gqa_decode_impl(const float* q, const float* k_new, const float* v_ne
   p.prefetch_kv = (flags & B2_ATTN_PREFETCH_KV) ? 1 : 0;
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // 8 warps per CTA when the launch has at most one CTA per SM or long splits,
-  // 4 otherwise (short splits over many CTAs keep more, smaller CTAs resident)
   const long long n_cta = static_cast<long long>(pl.n_splits) * n_kv_heads * batch;
-  const bool wide = n_cta <= di.sms || pl.split_len >= 1024;
+  const bool wide = attn_wide(n_cta, pl.split_len, di.sms);
   auto kernel = wide ? b2::gqa_decode_kernel<64, 8> : b2::gqa_decode_kernel<64, 4>;
   static int attr_set[64] = {0};
   int dev = 0;
