@@ -368,6 +368,56 @@ def measure_attention(torch, ops, gen, device, hbm_peak: float, steps: int) -> l
     return out
 
 
+DELTA_KH, DELTA_VH, DELTA_D = 16, 16, 128  # config 5's linear-attention heads (synthetic dims)
+
+
+def delta_bytes(bsz: int) -> int:
+    """Algorithmic bytes of one gated DeltaNet decode step: the fp32 recurrent state and
+    conv state read and written, the fp32 qkv / z / b / a read, the bf16 output written."""
+    conv_dim = (2 * DELTA_KH + DELTA_VH) * DELTA_D
+    per_seq = (DELTA_VH * DELTA_D * DELTA_D * 4 * 2 + conv_dim * 16 * 2 + conv_dim * 4
+               + DELTA_VH * DELTA_D * 4 + DELTA_VH * 8 + DELTA_VH * DELTA_D * 2)
+    return bsz * per_seq + conv_dim * 16 + DELTA_VH * 8 + DELTA_D * 4
+
+
+def measure_deltanet(torch, ops, gen, device, hbm_peak: float, steps: int) -> list:
+    """Config 5's linear-attention layers: one fused gated DeltaNet decode step
+    (16 k / 16 v heads of 128, conv width 4) at batch 1, 16 and 256.  Each graph
+    replay rotates over a pool of recurrent states whose total is above L2; a call
+    reads its state before the PDL wait (B2_DELTA_PREFETCH_STATE): a pool entry's
+    state was last written one replay earlier."""
+    conv_dim = (2 * DELTA_KH + DELTA_VH) * DELTA_D
+    out = []
+    for bsz in (1, 16, 256):
+        nbytes = delta_bytes(bsz)
+        n_pool = max(1, min(512, -(-300_000_000 // nbytes)))
+        pool = [(0.1 * torch.randn(bsz, DELTA_VH, DELTA_D, DELTA_D, device=device, generator=gen),
+                 torch.randn(bsz, conv_dim, 4, device=device, generator=gen)) for _ in range(n_pool)]
+        proj = torch.randn(bsz, conv_dim + DELTA_VH * DELTA_D + 2 * DELTA_VH, device=device, generator=gen)
+        c0, c1 = conv_dim, conv_dim + DELTA_VH * DELTA_D
+        conv_w = 0.5 * torch.randn(conv_dim, 4, device=device, generator=gen)
+        a_log = torch.log(torch.rand(DELTA_VH, device=device, generator=gen) * 15 + 1)
+        dt_bias = torch.randn(DELTA_VH, device=device, generator=gen)
+        norm_w = 1 + 0.1 * torch.randn(DELTA_D, device=device, generator=gen)
+        o = torch.empty(bsz, DELTA_VH * DELTA_D, dtype=torch.bfloat16, device=device)
+
+        def calls(pool=pool, proj=proj, o=o):
+            for st, cs in pool:
+                ops.gated_delta_step(proj[:, :c0], proj[:, c0:c1], proj[:, c1:c1 + DELTA_VH],
+                                     proj[:, c1 + DELTA_VH:], cs, conv_w, a_log, dt_bias, norm_w, st,
+                                     DELTA_KH, DELTA_VH, out=o, prefetch_state=True)
+
+        g = graph_of(torch, calls)
+        reps = max(3, min(200, int(steps * 2e6 / (nbytes * n_pool) + 1)))
+        t_ms = time_graph(torch, g, reps, 3) / n_pool
+        gbs = nbytes / (t_ms * 1e-3) / 1e9
+        out.append({"batch": bsz, "heads": f"{DELTA_KH}k/{DELTA_VH}v x {DELTA_D}", "us": round(t_ms * 1e3, 2),
+                    "gbs": round(gbs, 1), "frac_of_measured_hbm": round(gbs / hbm_peak, 3), "pool": n_pool})
+        del g, pool
+        torch.cuda.empty_cache()
+    return out
+
+
 def run_b200(args, rank: int, world: int) -> dict | None:
     import torch
     import torch.distributed as dist
@@ -439,6 +489,7 @@ def run_b200(args, rank: int, world: int) -> dict | None:
         del gl, w8
         extras["attention"] = measure_attention(torch, ops, gen, device, pk["hbm_gbs"], args.steps)
         extras["tc_gemm"] = measure_tc_gemm(torch, ops, gen, device, pk["bf16_tflops"], args.steps)
+        extras["deltanet"] = measure_deltanet(torch, ops, gen, device, pk["hbm_gbs"], args.steps)
 
     # ---- config 4: the full decode step (tensor-parallel across the ranks when N > 1)
     if not args.quick:

@@ -182,6 +182,34 @@ int b2_gqa_decode_static(const float* q, const float* k_new, const float* v_new,
 int b2_rmsnorm(const void* x, int x_is_f32, int ldx, const uint16_t* w, float eps, int batch, int n, uint16_t* y,
                int ldy, void* stream);
 
+/* One decode step of a gated DeltaNet (linear-attention) layer, fused: conv
+ * update + silu over q|k|v, q/k l2norm (q scaled by 1/sqrt(128)), the gated delta
+ * rule on the recurrent state, and the gated RMSNorm of the output.  Per
+ * sequence b and v head h (k head h / (n_v_heads / n_k_heads)):
+ *   beta = sigmoid(b), decay = exp(-exp(A_log[h]) * softplus(a + dt_bias[h]))
+ *   S = decay * S;  S += k (beta (v - S^T k))^T;  o = S^T q
+ *   out = o * rsqrt(mean(o^2) + eps) * norm_w * silu(z)
+ *   qkv         fp32 [batch][ld_qkv]: q (nk*128) | k (nk*128) | v (nv*128), the
+ *               in_proj_qkv output before the conv
+ *   z           fp32 [batch][ld_z], nv*128;  b, a  fp32 [batch][ld_ab], nv
+ *   conv_state  fp32 [batch][conv_dim = 2*nk*128 + nv*128][4], updated in place
+ *   conv_w      fp32 [conv_dim][4];  A_log, dt_bias fp32 [nv];  norm_w fp32 [128]
+ *   state       fp32 [batch][nv][128][128] (transformers' cache layout), updated
+ *   out         bf16 (fp32 with B2_DELTA_OUT_F32) [batch][ldo], nv*128 used
+ *   head_dim 128 only; n_v_heads a multiple of n_k_heads, at most 8x.
+ *   conv_state, conv_w and state 16-byte aligned.
+ * The reference has no kernel for it: it runs transformers 5.5.0's
+ * Qwen3_5GatedDeltaNet.forward (models/qwen3_5/modeling_qwen3_5.py:422-533) in
+ * float32 (reference/from_q4nx.py:140-171, chat.py:74-78); this replaces that
+ * call's decode branch between in_proj_* and out_proj. */
+#define B2_DELTA_OUT_F32 1        /* fp32 output */
+#define B2_DELTA_PREFETCH_STATE 2 /* state and conv_state are final at launch (no earlier kernel in
+                                     the PDL chain writes them): read them before the PDL wait */
+int b2_gated_delta_step(const float* qkv, int ld_qkv, const float* z, int ld_z, const float* b, const float* a,
+                        int ld_ab, float* conv_state, const float* conv_w, const float* A_log, const float* dt_bias,
+                        const float* norm_w, float* state, int batch, int n_k_heads, int n_v_heads, int head_dim,
+                        float eps, void* out, int ldo, int flags, void* stream);
+
 /* ------------------------------------------------------------------------
  * Large-batch W4A16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM):
  * the GEMV entry points' arithmetic for batches up to 256, where the

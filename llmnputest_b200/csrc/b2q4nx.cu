@@ -20,6 +20,7 @@
 #include "decode_program.cuh"
 #include "q4_gemm_tc.cuh"
 #include "q4nx_dequant.cuh"
+#include "gated_delta.cuh"
 #include "gqa_decode.cuh"
 #include "q4nx_gemv.cuh"
 #include "rmsnorm.cuh"
@@ -828,6 +829,74 @@ int b2_rmsnorm(const void* x, int x_is_f32, int ldx, const uint16_t* w, float ep
   cudaError_t e = x_is_f32 ? cudaLaunchKernelEx(&cfg, b2::rmsnorm_kernel<true>, x, ldx, wb, eps, n, yb, ldy)
                            : cudaLaunchKernelEx(&cfg, b2::rmsnorm_kernel<false>, x, ldx, wb, eps, n, yb, ldy);
   if (e != cudaSuccess) return cuda_fail(e, "rmsnorm launch");
+  return B2_OK;
+}
+
+int b2_gated_delta_step(const float* qkv, int ld_qkv, const float* z, int ld_z, const float* b, const float* a,
+                        int ld_ab, float* conv_state, const float* conv_w, const float* A_log, const float* dt_bias,
+                        const float* norm_w, float* state, int batch, int n_k_heads, int n_v_heads, int head_dim,
+                        float eps, void* out, int ldo, int flags, void* stream) {
+  DevInfo di;
+  int st = device_info(&di);
+  if (st != B2_OK) return st;
+  if (!qkv || !z || !b || !a || !conv_state || !conv_w || !A_log || !dt_bias || !norm_w || !state || !out)
+    return fail(B2_ERR_ARG, "null pointer argument");
+  if (head_dim != b2::kDeltaHeadDim) return fail(B2_ERR_ARG, "head_dim %d: only 128 is built", head_dim);
+  if (batch < 1 || batch > 65535 || n_k_heads < 1 || n_v_heads < n_k_heads || n_v_heads % n_k_heads)
+    return fail(B2_ERR_ARG, "bad gated delta shape (batch %d, k heads %d, v heads %d)", batch, n_k_heads,
+                n_v_heads);
+  const int ratio = n_v_heads / n_k_heads;
+  if (ratio > 8) return fail(B2_ERR_ARG, "v heads per k head %d > 8", ratio);
+  const long long conv_dim = 2LL * n_k_heads * head_dim + (long long)n_v_heads * head_dim;
+  if (ld_qkv < conv_dim || ld_z < n_v_heads * head_dim || ld_ab < n_v_heads || ldo < n_v_heads * head_dim)
+    return fail(B2_ERR_ARG, "leading dimension too small");
+  if (!(eps >= 0.f)) return fail(B2_ERR_ARG, "eps must be >= 0");
+  if ((reinterpret_cast<uintptr_t>(conv_state) | reinterpret_cast<uintptr_t>(conv_w) |
+       reinterpret_cast<uintptr_t>(state)) & 15)
+    return fail(B2_ERR_ALIGN, "conv_state, conv_w and state must be 16-byte aligned");
+  b2::DeltaParams p = {};
+  p.qkv = qkv;
+  p.z = z;
+  p.b = b;
+  p.a = a;
+  p.conv_state = conv_state;
+  p.conv_w = conv_w;
+  p.A_log = A_log;
+  p.dt_bias = dt_bias;
+  p.norm_w = norm_w;
+  p.state = state;
+  p.out = out;
+  p.ld_qkv = ld_qkv;
+  p.ld_z = ld_z;
+  p.ld_ab = ld_ab;
+  p.ldo = ldo;
+  p.nk = n_k_heads;
+  p.nv = n_v_heads;
+  p.eps = eps;
+  p.out_f32 = (flags & B2_DELTA_OUT_F32) ? 1 : 0;
+  p.prefetch_state = (flags & B2_DELTA_PREFETCH_STATE) ? 1 : 0;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (g_pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (ratio > 1) {  // the v heads of one k head share its q/k conv state
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = ratio;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(n_v_heads, batch, 1);
+  cfg.blockDim = dim3(b2::kDeltaThreads, 1, 1);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, b2::gated_delta_step_kernel, p);
+  if (e != cudaSuccess) return cuda_fail(e, "gated delta launch");
   return B2_OK;
 }
 

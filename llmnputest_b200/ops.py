@@ -331,3 +331,66 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor | No
     _native.call("b2_rmsnorm", _ptr(x2), 1 if x2.dtype == torch.float32 else 0, x2.stride(0), _ptr(w),
                  float(eps), b, n, _ptr(out), out.stride(0), _stream())
     return out if x.dim() == 2 else out[0]
+
+
+DELTA_OUT_F32 = 1
+DELTA_PREFETCH_STATE = 2
+DELTA_HEAD_DIM = 128
+
+
+def _rows(t: torch.Tensor, name: str, width: int) -> torch.Tensor:
+    """fp32 [B, >= width] with unit column stride (a slice of a wider projection output is fine)."""
+    _need(t, name, torch.float32)
+    if t.dim() != 2 or t.shape[1] < width or t.stride(1) != 1:
+        raise ValueError(f"{name} must be fp32 [B, >= {width}] with unit column stride, got {tuple(t.shape)}")
+    return t
+
+
+def _dense(t: torch.Tensor, name: str, shape: tuple) -> None:
+    _need(t, name, torch.float32)
+    if tuple(t.shape) != shape or not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous fp32 {shape}, got {tuple(t.shape)}")
+
+
+def gated_delta_step(qkv: torch.Tensor, z: torch.Tensor, b: torch.Tensor, a: torch.Tensor,
+                     conv_state: torch.Tensor, conv_w: torch.Tensor, A_log: torch.Tensor, dt_bias: torch.Tensor,
+                     norm_w: torch.Tensor, state: torch.Tensor, n_k_heads: int, n_v_heads: int,
+                     eps: float = 1e-6, out: torch.Tensor | None = None, out_f32: bool = False,
+                     prefetch_state: bool = False) -> torch.Tensor:
+    """One gated DeltaNet decode step (see b2_gated_delta_step); conv_state and state update in place.
+
+    qkv [B, >= conv_dim], z [B, >= nv*128], b and a [B, >= nv] fp32 (slices of one
+    projection output are accepted); conv_state [B, conv_dim, 4], conv_w [conv_dim, 4],
+    state [B, nv, 128, 128], A_log / dt_bias [nv], norm_w [128], all fp32.
+    Mirrors the decode branch of transformers' Qwen3_5GatedDeltaNet.forward between
+    its in_proj_* and out_proj calls."""
+    d = DELTA_HEAD_DIM
+    bsz = qkv.shape[0]
+    conv_dim = 2 * n_k_heads * d + n_v_heads * d
+    _rows(qkv, "qkv", conv_dim)
+    _rows(z, "z", n_v_heads * d)
+    _rows(b, "b", n_v_heads)
+    _rows(a, "a", n_v_heads)
+    if b.stride(0) != a.stride(0):
+        raise ValueError("b and a must share one row stride")
+    for t, name in ((z, "z"), (b, "b"), (a, "a")):
+        if t.shape[0] != bsz:
+            raise ValueError(f"{name} batch {t.shape[0]} != {bsz}")
+    _dense(conv_state, "conv_state", (bsz, conv_dim, 4))
+    _dense(conv_w, "conv_w", (conv_dim, 4))
+    _dense(A_log, "A_log", (n_v_heads,))
+    _dense(dt_bias, "dt_bias", (n_v_heads,))
+    _dense(norm_w, "norm_w", (d,))
+    _dense(state, "state", (bsz, n_v_heads, d, d))
+    odt = torch.float32 if out_f32 else torch.bfloat16
+    if out is None:
+        out = torch.empty((bsz, n_v_heads * d), dtype=odt, device=qkv.device)
+    _need(out, "out", odt)
+    if out.dim() != 2 or out.stride(1) != 1 or out.shape[0] != bsz:
+        raise ValueError("out must be [B, >= nv*128] with unit column stride")
+    flags = (DELTA_OUT_F32 if out_f32 else 0) | (DELTA_PREFETCH_STATE if prefetch_state else 0)
+    _native.call("b2_gated_delta_step", _ptr(qkv), qkv.stride(0), _ptr(z), z.stride(0), _ptr(b), _ptr(a),
+                 b.stride(0), _ptr(conv_state), _ptr(conv_w), _ptr(A_log), _ptr(dt_bias), _ptr(norm_w),
+                 _ptr(state), bsz, n_k_heads, n_v_heads, d, float(eps), _ptr(out), out.stride(0), flags,
+                 _stream())
+    return out
