@@ -153,3 +153,19 @@ def test_rejected_before_launch(ops):
     with pytest.raises(_native.B2Error):  # state not 16-byte aligned
         _native.call("b2_gated_delta_step", *args[:12], p(misaligned), 1, 1, 2, 128, 1e-6, p(out), 256, 0,
                      ops._stream())
+
+
+def test_config5_full_batch_sampled(ops):
+    """Config 5's size, B=256 x 16 v heads (268 MB of state, above L2): the step of a
+    sequence depends on that sequence alone, so three sampled sequences are checked
+    against the oracle run on those sequences only."""
+    bsz, nk, nv = 256, 16, 16
+    inp = dn.synth_step_inputs(np.random.default_rng(256), bsz, nk, nv, 128, 128)
+    out, conv, state = run_step(ops, inp, nk, nv, out_f32=True)
+    pick = [0, 97, 255]
+    sub = {k: (v[pick] if k in ("qkv", "z", "b", "a", "conv_state", "state") else v) for k, v in inp.items()}
+    r_out, r_conv, r_state = oracle_step(sub, nk, nv)
+    assert_close(out[pick], r_out, NS_COS, NS_REL, "out")
+    assert np.array_equal(conv[pick], r_conv)
+    assert_close(state[pick], r_state, 0.9999999, 1e-4, "state")
+    assert np.isfinite(out).all()
