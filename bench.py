@@ -418,6 +418,35 @@ def measure_deltanet(torch, ops, gen, device, hbm_peak: float, steps: int) -> li
     return out
 
 
+def measure_deltanet_layers(torch, device, hbm_peak: float, steps: int, n_layers: int = 18) -> list:
+    """Config 5's 18 linear-attention layers as one graph: per layer input RMSNorm, the
+    fused q4 in_proj (q|k|v|z|b|a, 8224 rows x 1024), the gated DeltaNet step and the q4
+    out_proj (1024 x 2048) added into the residual (llmnputest_b200.deltanet), at batch
+    1 (GEMV) and 256 (tcgen05 GEMM).  Each layer's states were last written one graph
+    replay earlier, so its step reads them before its PDL wait."""
+    from llmnputest_b200.deltanet import DeltaNetLayer
+    out = []
+    for bsz in (1, 256):
+        layers = [DeltaNetLayer(1024, DELTA_KH, DELTA_VH, bsz, device=device, seed=50 + i) for i in range(n_layers)]
+        resid = torch.randn(bsz, 1024, device=device)
+
+        def chain(layers=layers, resid=resid):
+            for layer in layers:
+                layer.step(resid, prefetch_state=True)
+
+        g = graph_of(torch, chain)
+        nbytes = sum(layer.bytes_per_step() for layer in layers)
+        reps = max(5, min(100, int(steps * 4e6 / nbytes + 1)))
+        t_ms = time_graph(torch, g, reps, 3)
+        gbs = nbytes / (t_ms * 1e-3) / 1e9
+        out.append({"batch": bsz, "layers": n_layers, "ms": round(t_ms, 4), "gbs": round(gbs, 1),
+                    "frac_of_measured_hbm": round(gbs / hbm_peak, 3), "bytes_per_step": nbytes,
+                    "how": "tcgen05 GEMM" if layers[0].use_gemm else "GEMV (RMSNorm fused)"})
+        del g, layers
+        torch.cuda.empty_cache()
+    return out
+
+
 def run_b200(args, rank: int, world: int) -> dict | None:
     import torch
     import torch.distributed as dist
@@ -490,6 +519,7 @@ def run_b200(args, rank: int, world: int) -> dict | None:
         extras["attention"] = measure_attention(torch, ops, gen, device, pk["hbm_gbs"], args.steps)
         extras["tc_gemm"] = measure_tc_gemm(torch, ops, gen, device, pk["bf16_tflops"], args.steps)
         extras["deltanet"] = measure_deltanet(torch, ops, gen, device, pk["hbm_gbs"], args.steps)
+        extras["deltanet_layers"] = measure_deltanet_layers(torch, device, pk["hbm_gbs"], args.steps)
 
     # ---- config 4: the full decode step (tensor-parallel across the ranks when N > 1)
     if not args.quick:

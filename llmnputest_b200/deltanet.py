@@ -1,0 +1,111 @@
+"""One gated DeltaNet (linear-attention) layer half for batched decode.
+
+The token mixer of Qwen3.5's linear-attention layers (transformers 5.5.0
+`Qwen3_5GatedDeltaNet.forward`, models/qwen3_5/modeling_qwen3_5.py:422-533, run
+by the reference in float32: reference/from_q4nx.py:140-171) with its input
+RMSNorm and residual add (`Qwen3_5DecoderLayer.forward`, :744-785):
+
+    resid += out_proj(gated_delta_step(in_proj(rmsnorm(resid))))
+
+as three launches on resident q4nx weights.  in_proj is ONE q4nx weight whose
+output rows are q | k | v | z | b | a (transformers' in_proj_qkv, in_proj_z,
+in_proj_b and in_proj_a stacked, padded to whole 32-row tiles), so the step
+kernel reads its four inputs as column slices of one fp32 projection output.
+Batches below `gemm_min_batch` use the GEMV with the RMSNorm fused into its input;
+larger batches run RMSNorm and the tcgen05 GEMM.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import ops
+from .decode import synth_q4
+from .format import TILE_K, TILE_ROWS
+
+HEAD_DIM = ops.DELTA_HEAD_DIM
+
+
+class DeltaNetLayer:
+    """Resident weights and states of one linear-attention layer; `step()` is graph-capturable."""
+
+    def __init__(self, hidden: int, n_k_heads: int, n_v_heads: int, batch: int, device=None, seed: int = 0,
+                 weights: dict | None = None, eps: float = 1e-6, gemm_min_batch: int = 9):
+        if hidden % TILE_K or (n_v_heads * HEAD_DIM) % TILE_K:
+            raise ValueError("hidden and n_v_heads*128 must be multiples of 256 (whole K-tiles)")
+        self.hidden, self.nk, self.nv, self.batch, self.eps = hidden, n_k_heads, n_v_heads, batch, eps
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        d = HEAD_DIM
+        self.conv_dim = (2 * n_k_heads + n_v_heads) * d
+        # column offsets of q|k|v, z, b, a in the in_proj output
+        self.c_z = self.conv_dim
+        self.c_b = self.c_z + n_v_heads * d
+        self.c_a = self.c_b + n_v_heads
+        n_rows = self.c_a + n_v_heads
+        self.nt_in = -(-n_rows // TILE_ROWS)
+        self.kt_h = hidden // TILE_K
+        self.nt_h = hidden // TILE_ROWS
+        self.kt_v = n_v_heads * d // TILE_K
+        self.w = weights if weights is not None else self._synthetic(seed)
+        dev = self.device
+        self.conv_state = torch.zeros(batch, self.conv_dim, 4, dtype=torch.float32, device=dev)
+        self.state = torch.zeros(batch, n_v_heads, d, d, dtype=torch.float32, device=dev)
+        self.xn = torch.zeros(batch, hidden, dtype=torch.bfloat16, device=dev)
+        self.proj = torch.zeros(batch, self.nt_in * TILE_ROWS, dtype=torch.float32, device=dev)
+        self.h = torch.zeros(batch, n_v_heads * d, dtype=torch.bfloat16, device=dev)
+        self.use_gemm = batch >= gemm_min_batch
+        if self.use_gemm:
+            nbytes = ops.gemm_workspace_bytes(batch, max(self.kt_h, self.kt_v))
+            self._ws_raw = torch.empty(nbytes + 256, dtype=torch.uint8, device=dev)
+            off = (256 - self._ws_raw.data_ptr() % 256) % 256
+            self.gemm_ws = self._ws_raw[off:off + nbytes]
+
+    def _synthetic(self, seed: int) -> dict:
+        dev, d = self.device, HEAD_DIM
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        return {
+            "in_proj": synth_q4(self.nt_in * self.kt_h, g, dev),
+            "out_proj": synth_q4(self.nt_h * self.kt_v, g, dev),
+            "conv_w": 0.5 * torch.randn(self.conv_dim, 4, device=dev, generator=g),
+            "A_log": torch.log(1.0 + 15.0 * torch.rand(self.nv, device=dev, generator=g)),
+            "dt_bias": torch.randn(self.nv, device=dev, generator=g),
+            "norm_w": 1.0 + 0.1 * torch.randn(d, device=dev, generator=g),
+            # input RMSNorm weight N(1, 0.1), as the decoders' norms
+            "input_norm": (1.0 + 0.1 * torch.randn(self.hidden, device=dev, generator=g)).to(torch.bfloat16),
+        }
+
+    def bytes_per_step(self) -> int:
+        """Algorithmic HBM bytes of one step: both weights' tiles, the states read and
+        written, the projection output written and read, the residual read and written."""
+        d, b = HEAD_DIM, self.batch
+        w = self.w["in_proj"].numel() + self.w["out_proj"].numel()
+        states = 2 * 4 * b * (self.nv * d * d + self.conv_dim * 4)
+        proj = 2 * 4 * b * self.nt_in * TILE_ROWS
+        return w + states + proj + 2 * b * self.nv * d + 2 * 4 * b * self.hidden
+
+    def step(self, resid: torch.Tensor, prefetch_state: bool = False) -> torch.Tensor:
+        """resid (fp32 [B, hidden]) += the layer's token mixer; returns resid.
+
+        prefetch_state=True lets the step kernel read its states before its wait on the
+        preceding kernel.  The projections launch their dependents early, so this is only
+        correct when a non-PDL stream operation or a graph boundary separates this
+        layer's consecutive steps (the state's previous write is that earlier step)."""
+        w, nv = self.w, self.nv
+        if self.use_gemm:
+            ops.rmsnorm(resid, w["input_norm"], self.eps, out=self.xn)
+            ops.q4_gemm(w["in_proj"], self.nt_in, self.kt_h, self.xn, out=self.proj, workspace=self.gemm_ws)
+        else:
+            ops.gemv_rmsnorm(w["in_proj"], self.nt_in, self.kt_h, resid, w["input_norm"], self.eps, out=self.proj,
+                             prefetch=True)
+        p = self.proj
+        ops.gated_delta_step(p[:, :self.c_z], p[:, self.c_z:self.c_b], p[:, self.c_b:self.c_a],
+                             p[:, self.c_a:self.c_a + nv], self.conv_state, w["conv_w"], w["A_log"], w["dt_bias"],
+                             w["norm_w"], self.state, self.nk, nv, eps=self.eps, out=self.h,
+                             prefetch_state=prefetch_state)
+        if self.use_gemm:
+            ops.q4_gemm(w["out_proj"], self.nt_h, self.kt_v, self.h, out=resid, accumulate=True,
+                        workspace=self.gemm_ws)
+        else:
+            ops.q4_gemv(w["out_proj"], self.nt_h, self.kt_v, self.h, out=resid, accumulate=True, prefetch=True)
+        return resid

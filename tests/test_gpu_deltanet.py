@@ -169,3 +169,40 @@ def test_config5_full_batch_sampled(ops):
     assert np.array_equal(conv[pick], r_conv)
     assert_close(state[pick], r_state, 0.9999999, 1e-4, "state")
     assert np.isfinite(out).all()
+
+
+@pytest.mark.parametrize("bsz", [3, 12])
+def test_layer_step_vs_oracle_composition(ops, bsz):
+    """DeltaNetLayer (input RMSNorm -> fused q4 in_proj -> step -> q4 out_proj + residual),
+    two chained steps, GEMV path at batch 3 and tcgen05 GEMM path at batch 12, against the
+    oracle composition.  Gate: the decode-composition bar (cos >= 0.9999, rel <= 1e-2),
+    bf16 re-rounding on both sides of each projection."""
+    from ml_dtypes import bfloat16
+
+    from llmnputest_b200.deltanet import DeltaNetLayer
+    from oracle import q4nx_oracle as orc
+    hidden, nk, nv = 1024, 2, 4
+    layer = DeltaNetLayer(hidden, nk, nv, bsz, seed=3)
+    w = {k: v.cpu() for k, v in layer.w.items()}
+    in_t, out_t = w["in_proj"].numpy(), w["out_proj"].numpy()
+    norm_in = w["input_norm"].float().numpy()
+    prm = {k: w[k].numpy() for k in ("conv_w", "A_log", "dt_bias", "norm_w")}
+    r_conv = np.zeros((bsz, layer.conv_dim, 4), np.float32)
+    r_state = np.zeros((bsz, nv, 128, 128), np.float64)
+    rng = np.random.default_rng(bsz)
+    for t in range(2):
+        x = rng.standard_normal((bsz, hidden), dtype=np.float32)
+        resid = dev(x)
+        layer.step(resid)
+        torch.cuda.synchronize()
+        xn = orc.rmsnorm(x, norm_in, layer.eps).astype(bfloat16).astype(np.float32)
+        proj = orc.gemv_q4(in_t, xn, layer.nt_in, layer.kt_h)
+        o, r_conv, r_state = dn.gated_delta_step(
+            proj[:, :layer.c_z], proj[:, layer.c_z:layer.c_b], proj[:, layer.c_b:layer.c_a],
+            proj[:, layer.c_a:layer.c_a + nv], r_conv, prm["conv_w"], prm["A_log"], prm["dt_bias"],
+            prm["norm_w"], r_state, nk, nv, 128, 128)
+        h = o.astype(bfloat16).astype(np.float32)
+        ref = x + orc.gemv_q4(out_t, h, layer.nt_h, layer.kt_v)
+        assert_close(resid.cpu().numpy(), ref, 0.9999, 1e-2, f"resid step {t}")
+    assert_close(layer.state.cpu().numpy(), r_state, 0.9999, 1e-2, "state after 2 steps")
+    assert ops.device_error() == 0
