@@ -447,6 +447,47 @@ def measure_deltanet_layers(torch, device, hbm_peak: float, steps: int, n_layers
     return out
 
 
+GATED_Q, GATED_KV, GATED_D, GATED_CTX = 8, 2, 256, 2048  # config 5's gated full-attention layers
+
+
+def measure_gated_attention(torch, ops, gen, device, hbm_peak: float, steps: int) -> list:
+    """Config 5's gated full-attention decode (8 q / 2 kv heads, head_dim 256, q/k RMSNorm,
+    partial RoPE over 64 dims, sigmoid output gate) at ctx 2048, pos 2047.  Algorithmic bytes
+    per call: B*2*2048*256*2*2 (the bf16 K and V read once).  Each graph replay rotates over
+    a pool of caches whose total is above L2."""
+    out = []
+    inv_freq = (1.0 / (10000.0 ** (torch.arange(0, 64, 2, device=device).float() / 64))).contiguous()
+    qn = 0.1 * torch.randn(GATED_D, device=device, generator=gen)
+    kn = 0.1 * torch.randn(GATED_D, device=device, generator=gen)
+    for bsz in (1, 16, 256):
+        kv_bytes = bsz * GATED_KV * GATED_CTX * GATED_D * 2 * 2
+        n_pool = max(1, min(512, -(-300_000_000 // kv_bytes)))
+        pool = [(torch.randn(bsz, GATED_KV, GATED_CTX, GATED_D, device=device, generator=gen).to(torch.bfloat16),
+                 torch.randn(bsz, GATED_KV, GATED_CTX, GATED_D, device=device, generator=gen).to(torch.bfloat16))
+                for _ in range(n_pool)]
+        proj = torch.randn(bsz, (2 * GATED_Q + 2 * GATED_KV) * GATED_D, device=device, generator=gen)
+        c0, c1 = 2 * GATED_Q * GATED_D, (2 * GATED_Q + GATED_KV) * GATED_D
+        pos = torch.full((bsz,), GATED_CTX - 1, dtype=torch.int32, device=device)
+        o = torch.empty(bsz, GATED_Q * GATED_D, dtype=torch.bfloat16, device=device)
+        ws_n = ops.gated_attn_workspace_bytes(bsz, GATED_Q, GATED_KV, GATED_CTX)
+        ws = torch.empty(max(ws_n, 16), dtype=torch.uint8, device=device)
+
+        def calls(pool=pool, proj=proj, pos=pos, o=o, ws=ws):
+            for kc, vc in pool:
+                ops.gated_attn_decode(proj[:, :c0], proj[:, c0:c1], proj[:, c1:], qn, kn, inv_freq, kc, vc, pos,
+                                      GATED_Q, GATED_KV, out=o, workspace=ws)
+
+        g = graph_of(torch, calls)
+        reps = max(3, min(200, int(steps * 2e6 / (kv_bytes * n_pool) + 1)))
+        t_ms = time_graph(torch, g, reps, 3) / n_pool
+        gbs = kv_bytes / (t_ms * 1e-3) / 1e9
+        out.append({"batch": bsz, "ctx": GATED_CTX, "heads": "8q/2kv x 256", "us": round(t_ms * 1e3, 2),
+                    "gbs": round(gbs, 1), "frac_of_measured_hbm": round(gbs / hbm_peak, 3), "pool": n_pool})
+        del g, pool, ws
+        torch.cuda.empty_cache()
+    return out
+
+
 def run_b200(args, rank: int, world: int) -> dict | None:
     import torch
     import torch.distributed as dist
@@ -520,6 +561,7 @@ def run_b200(args, rank: int, world: int) -> dict | None:
         extras["tc_gemm"] = measure_tc_gemm(torch, ops, gen, device, pk["bf16_tflops"], args.steps)
         extras["deltanet"] = measure_deltanet(torch, ops, gen, device, pk["hbm_gbs"], args.steps)
         extras["deltanet_layers"] = measure_deltanet_layers(torch, device, pk["hbm_gbs"], args.steps)
+        extras["gated_attention"] = measure_gated_attention(torch, ops, gen, device, pk["hbm_gbs"], args.steps)
 
     # ---- config 4: the full decode step (tensor-parallel across the ranks when N > 1)
     if not args.quick:

@@ -182,6 +182,35 @@ int b2_gqa_decode_static(const float* q, const float* k_new, const float* v_new,
 int b2_rmsnorm(const void* x, int x_is_f32, int ldx, const uint16_t* w, float eps, int batch, int n, uint16_t* y,
                int ldy, void* stream);
 
+/* Decode step of Qwen3.5's gated full-attention layer (head_dim 256), between its
+ * q/k/v projections and o_proj, for one new token per sequence at pos[b]:
+ *   q_h, k: RMSNorm over the head with weight (1 + w) (q_norm_w, k_norm_w fp32 [256]);
+ *   RoPE (rotate_half) on the first rot_dim dims, pair (i, i + rot_dim/2) turned by
+ *   pos * inv_freq[i] (inv_freq fp32 [rot_dim/2], the rotary module's own buffer);
+ *   the rotated k and the raw v appended to the bf16 cache at row pos[b];
+ *   out_h = softmax(q_h K^T / 16) V * sigmoid(gate_h).
+ *   qg     fp32 [batch][ld_qg]: q head h at h*512 is q (256) | gate (256), the q_proj
+ *          output as transformers lays it out
+ *   k_new, v_new  fp32 [batch][ld_kv], kv head g at g*256
+ *   k_cache, v_cache  bf16 [batch][n_kv_heads][ctx_max][256], 16-byte aligned
+ *   pos    int32 [batch], 0 <= pos < max_len <= ctx_max (a kernel records device
+ *          error 5 and writes nothing for a sequence outside that range)
+ *   out    bf16 (fp32 with B2_GATED_OUT_F32) [batch][ldo], n_q_heads*256 used
+ *   n_q_heads / n_kv_heads in {1, 2, 4}.
+ *   workspace: b2_gated_attn_decode_workspace_size bytes, 16-byte aligned (0 when
+ *   the (kv head, sequence) pairs fill the SMs and no split is needed).
+ * The reference has no kernel for it: it runs transformers 5.5.0's
+ * Qwen3_5Attention.forward (models/qwen3_5/modeling_qwen3_5.py:647-692) in float32
+ * (reference/from_q4nx.py:140-171). */
+#define B2_GATED_OUT_F32 1
+int b2_gated_attn_decode_workspace_size(int batch, int n_q_heads, int n_kv_heads, int head_dim, int max_len,
+                                        size_t* bytes);
+int b2_gated_attn_decode(const float* qg, int ld_qg, const float* k_new, const float* v_new, int ld_kv,
+                         const float* q_norm_w, const float* k_norm_w, const float* inv_freq, int rot_dim,
+                         uint16_t* k_cache, uint16_t* v_cache, const int32_t* pos, int batch, int n_q_heads,
+                         int n_kv_heads, int head_dim, int ctx_max, int max_len, float eps, void* out, int ldo,
+                         int flags, void* workspace, size_t workspace_bytes, void* stream);
+
 /* One decode step of a gated DeltaNet (linear-attention) layer, fused: conv
  * update + silu over q|k|v, q/k l2norm (q scaled by 1/sqrt(128)), the gated delta
  * rule on the recurrent state, and the gated RMSNorm of the output.  Per

@@ -36,6 +36,9 @@ SIGNATURES: dict[str, tuple] = {
     "b2_gqa_decode_static": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _f32,
                                     _f32, _vp, _i32, _i32, _vp]),
     "b2_rmsnorm": (_i32, [_vp, _i32, _i32, _vp, _f32, _i32, _i32, _vp, _i32, _vp]),
+    "b2_gated_attn_decode_workspace_size": (_i32, [_i32, _i32, _i32, _i32, _i32, _c.POINTER(_c.c_size_t)]),
+    "b2_gated_attn_decode": (_i32, [_vp, _i32, _vp, _vp, _i32, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _i32, _i32, _i32,
+                                    _i32, _i32, _i32, _f32, _vp, _i32, _i32, _vp, _c.c_size_t, _vp]),
     "b2_gated_delta_step": (_i32, [_vp, _i32, _vp, _i32, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32,
                                    _i32, _i32, _f32, _vp, _i32, _i32, _vp]),
     "b2_q4_gemm_workspace_size": (_i32, [_i32, _i32, _c.POINTER(_c.c_size_t)]),

@@ -20,6 +20,7 @@
 #include "decode_program.cuh"
 #include "q4_gemm_tc.cuh"
 #include "q4nx_dequant.cuh"
+#include "gated_attention.cuh"
 #include "gated_delta.cuh"
 #include "gqa_decode.cuh"
 #include "q4nx_gemv.cuh"
@@ -829,6 +830,108 @@ int b2_rmsnorm(const void* x, int x_is_f32, int ldx, const uint16_t* w, float ep
   cudaError_t e = x_is_f32 ? cudaLaunchKernelEx(&cfg, b2::rmsnorm_kernel<true>, x, ldx, wb, eps, n, yb, ldy)
                            : cudaLaunchKernelEx(&cfg, b2::rmsnorm_kernel<false>, x, ldx, wb, eps, n, yb, ldy);
   if (e != cudaSuccess) return cuda_fail(e, "rmsnorm launch");
+  return B2_OK;
+}
+
+// splits of the gated attention: one per (kv head, sequence) when those fill the SMs,
+// else enough for about two CTAs per SM, each at least 256 keys
+static void gated_attn_plan(int batch, int nkv, int max_len, int sms, int* n_splits, int* split_len) {
+  const long long pairs = (long long)batch * nkv;
+  int S = 1;
+  if (pairs < sms) S = (int)std::max(1LL, std::min<long long>((2LL * sms + pairs - 1) / pairs, (max_len + 255) / 256));
+  int sl = (max_len + S - 1) / S;
+  sl = (sl + 63) / 64 * 64;
+  *split_len = sl;
+  *n_splits = (max_len + sl - 1) / sl;
+}
+
+static size_t gated_attn_ws_bytes(int batch, int nq, int nkv, int n_splits) {
+  return n_splits > 1 ? (size_t)batch * nq * n_splits * (b2::kGaD + 2) * sizeof(float) : 0;
+}
+
+int b2_gated_attn_decode_workspace_size(int batch, int n_q_heads, int n_kv_heads, int head_dim, int max_len,
+                                        size_t* bytes) {
+  if (!bytes) return fail(B2_ERR_ARG, "null bytes");
+  if (batch < 1 || n_kv_heads < 1 || n_q_heads < n_kv_heads || max_len < 1 || head_dim != b2::kGaD)
+    return fail(B2_ERR_ARG, "bad gated attention shape");
+  DevInfo di;
+  int st = device_info(&di);
+  if (st != B2_OK) return st;
+  int S, sl;
+  gated_attn_plan(batch, n_kv_heads, max_len, di.sms, &S, &sl);
+  *bytes = gated_attn_ws_bytes(batch, n_q_heads, n_kv_heads, S);
+  return B2_OK;
+}
+
+int b2_gated_attn_decode(const float* qg, int ld_qg, const float* k_new, const float* v_new, int ld_kv,
+                         const float* q_norm_w, const float* k_norm_w, const float* inv_freq, int rot_dim,
+                         uint16_t* k_cache, uint16_t* v_cache, const int32_t* pos, int batch, int n_q_heads,
+                         int n_kv_heads, int head_dim, int ctx_max, int max_len, float eps, void* out, int ldo,
+                         int flags, void* workspace, size_t workspace_bytes, void* stream) {
+  DevInfo di;
+  int st = device_info(&di);
+  if (st != B2_OK) return st;
+  if (!qg || !k_new || !v_new || !q_norm_w || !k_norm_w || !inv_freq || !k_cache || !v_cache || !pos || !out)
+    return fail(B2_ERR_ARG, "null pointer argument");
+  if (head_dim != b2::kGaD) return fail(B2_ERR_ARG, "head_dim %d: only 256 is built", head_dim);
+  if (batch < 1 || batch > 65535 || n_kv_heads < 1 || n_kv_heads > 65535 || n_q_heads % n_kv_heads)
+    return fail(B2_ERR_ARG, "bad gated attention heads (q %d, kv %d)", n_q_heads, n_kv_heads);
+  const int G = n_q_heads / n_kv_heads;
+  if (G != 1 && G != 2 && G != 4) return fail(B2_ERR_ARG, "q heads per kv head %d: 1, 2 or 4 are built", G);
+  if (rot_dim < 2 || rot_dim > head_dim || rot_dim % 2) return fail(B2_ERR_ARG, "bad rotary dim %d", rot_dim);
+  if (ctx_max < 1 || max_len < 1 || max_len > ctx_max) return fail(B2_ERR_ARG, "need 1 <= max_len <= ctx_max");
+  if (ld_qg < n_q_heads * 2 * head_dim || ld_kv < n_kv_heads * head_dim || ldo < n_q_heads * head_dim)
+    return fail(B2_ERR_ARG, "leading dimension too small");
+  if (!(eps >= 0.f)) return fail(B2_ERR_ARG, "eps must be >= 0");
+  if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15)
+    return fail(B2_ERR_ALIGN, "k_cache and v_cache must be 16-byte aligned");
+  int S, sl;
+  gated_attn_plan(batch, n_kv_heads, max_len, di.sms, &S, &sl);
+  const size_t need = gated_attn_ws_bytes(batch, n_q_heads, n_kv_heads, S);
+  if (need && (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15)))
+    return fail(B2_ERR_WORKSPACE, "gated attention needs %zu bytes of 16-byte aligned workspace", need);
+  b2::GatedAttnParams p = {};
+  p.qg = qg;
+  p.k_new = k_new;
+  p.v_new = v_new;
+  p.q_norm_w = q_norm_w;
+  p.k_norm_w = k_norm_w;
+  p.inv_freq = inv_freq;
+  p.k_cache = reinterpret_cast<__nv_bfloat16*>(k_cache);
+  p.v_cache = reinterpret_cast<__nv_bfloat16*>(v_cache);
+  p.pos = pos;
+  p.out = out;
+  p.part = static_cast<float*>(workspace);
+  p.ld_qg = ld_qg;
+  p.ld_kv = ld_kv;
+  p.ldo = ldo;
+  p.rot_half = rot_dim / 2;
+  p.ctx_max = ctx_max;
+  p.max_len = max_len;
+  p.nq = n_q_heads;
+  p.nkv = n_kv_heads;
+  p.n_splits = S;
+  p.split_len = sl;
+  p.eps = eps;
+  p.out_f32 = (flags & B2_GATED_OUT_F32) ? 1 : 0;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(S, n_kv_heads, batch);
+  cfg.blockDim = dim3(b2::kGaThreads, 1, 1);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cfg.attrs = attr;
+  cfg.numAttrs = g_pdl ? 1 : 0;
+  cudaError_t e = G == 4   ? cudaLaunchKernelEx(&cfg, b2::gated_attn_kernel<4>, p)
+                  : G == 2 ? cudaLaunchKernelEx(&cfg, b2::gated_attn_kernel<2>, p)
+                           : cudaLaunchKernelEx(&cfg, b2::gated_attn_kernel<1>, p);
+  if (e != cudaSuccess) return cuda_fail(e, "gated attention launch");
+  if (S > 1) {
+    cfg.gridDim = dim3(n_q_heads, batch, 1);
+    e = cudaLaunchKernelEx(&cfg, b2::gated_attn_combine_kernel, p);
+    if (e != cudaSuccess) return cuda_fail(e, "gated attention combine launch");
+  }
   return B2_OK;
 }
 

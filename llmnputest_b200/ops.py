@@ -394,3 +394,67 @@ def gated_delta_step(qkv: torch.Tensor, z: torch.Tensor, b: torch.Tensor, a: tor
                  _ptr(state), bsz, n_k_heads, n_v_heads, d, float(eps), _ptr(out), out.stride(0), flags,
                  _stream())
     return out
+
+
+GATED_OUT_F32 = 1
+GATED_HEAD_DIM = 256
+
+
+def gated_attn_workspace_bytes(batch: int, n_q_heads: int, n_kv_heads: int, max_len: int) -> int:
+    n = ctypes.c_size_t()
+    _native.check(_native.lib().b2_gated_attn_decode_workspace_size(batch, n_q_heads, n_kv_heads, GATED_HEAD_DIM,
+                                                                     max_len, ctypes.byref(n)),
+                  "b2_gated_attn_decode_workspace_size")
+    return n.value
+
+
+def gated_attn_decode(qg: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, q_norm_w: torch.Tensor,
+                      k_norm_w: torch.Tensor, inv_freq: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                      pos: torch.Tensor, n_q_heads: int, n_kv_heads: int, max_len: int | None = None,
+                      eps: float = 1e-6, out: torch.Tensor | None = None, out_f32: bool = False,
+                      workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Qwen3.5 gated full-attention decode step (see b2_gated_attn_decode); appends k/v at pos.
+
+    qg [B, >= nq*512] (q | gate per head), k_new / v_new [B, >= nkv*256] fp32 (slices of
+    one projection output are accepted, unit column stride); q_norm_w / k_norm_w [256]
+    and inv_freq [rot_dim/2] fp32; k_cache / v_cache bf16 [B, nkv, ctx_max, 256]; pos
+    int32 [B].  max_len (default ctx_max) bounds pos + 1 and sets the split plan."""
+    d = GATED_HEAD_DIM
+    bsz = qg.shape[0]
+    _rows(qg, "qg", n_q_heads * 2 * d)
+    _rows(k_new, "k_new", n_kv_heads * d)
+    _rows(v_new, "v_new", n_kv_heads * d)
+    if k_new.stride(0) != v_new.stride(0):
+        raise ValueError("k_new and v_new must share one row stride")
+    _dense(q_norm_w, "q_norm_w", (d,))
+    _dense(k_norm_w, "k_norm_w", (d,))
+    _need(inv_freq, "inv_freq", torch.float32)
+    if inv_freq.dim() != 1 or not inv_freq.is_contiguous():
+        raise ValueError("inv_freq must be contiguous fp32 [rot_dim/2]")
+    for c, name in ((k_cache, "k_cache"), (v_cache, "v_cache")):
+        _need(c, name, torch.bfloat16)
+        if c.dim() != 4 or c.shape[0] != bsz or c.shape[1] != n_kv_heads or c.shape[3] != d or not c.is_contiguous():
+            raise ValueError(f"{name} must be contiguous bf16 [B, nkv, ctx_max, 256], got {tuple(c.shape)}")
+    if k_cache.shape != v_cache.shape:
+        raise ValueError("k_cache and v_cache shapes differ")
+    _need(pos, "pos", torch.int32)
+    if pos.numel() != bsz or not pos.is_contiguous():
+        raise ValueError("pos must be contiguous int32 [B]")
+    ctx_max = k_cache.shape[2]
+    max_len = ctx_max if max_len is None else max_len
+    odt = torch.float32 if out_f32 else torch.bfloat16
+    if out is None:
+        out = torch.empty((bsz, n_q_heads * d), dtype=odt, device=qg.device)
+    _need(out, "out", odt)
+    if out.dim() != 2 or out.stride(1) != 1 or out.shape[0] != bsz:
+        raise ValueError("out must be [B, >= nq*256] with unit column stride")
+    ws_n = gated_attn_workspace_bytes(bsz, n_q_heads, n_kv_heads, max_len)
+    if workspace is None and ws_n:
+        workspace = torch.empty(ws_n, dtype=torch.uint8, device=qg.device)
+    wp = _ptr(workspace) if workspace is not None else ctypes.c_void_p(0)
+    wn = workspace.numel() * workspace.element_size() if workspace is not None else 0
+    _native.call("b2_gated_attn_decode", _ptr(qg), qg.stride(0), _ptr(k_new), _ptr(v_new), k_new.stride(0),
+                 _ptr(q_norm_w), _ptr(k_norm_w), _ptr(inv_freq), 2 * inv_freq.numel(), _ptr(k_cache), _ptr(v_cache),
+                 _ptr(pos), bsz, n_q_heads, n_kv_heads, d, ctx_max, max_len, float(eps), _ptr(out), out.stride(0),
+                 GATED_OUT_F32 if out_f32 else 0, wp, wn, _stream())
+    return out
