@@ -101,6 +101,7 @@ struct Tuning {
   // attention warps per CTA: 1 always 8 (measured equal or faster on every bench
   // shape), 2 always 4, 0 by launch shape (8 for <= one CTA per SM or long splits)
   int attn_wide = 1;
+  int gated_min_split = 256;  // gated attention: fewest keys per split
 };
 const Tuning& tuning() {
   static const Tuning t = [] {
@@ -114,6 +115,7 @@ const Tuning& tuning() {
     if (const char* e = getenv("B2Q4NX_TC_ABUFS")) v.tc_abufs = std::max(0, std::min(2, atoi(e)));
     if (const char* e = getenv("B2Q4NX_ATTN_WAVE")) v.attn_wave = atoi(e) != 0;
     if (const char* e = getenv("B2Q4NX_ATTN_WIDE")) v.attn_wide = std::max(0, std::min(2, atoi(e)));
+    if (const char* e = getenv("B2Q4NX_GATED_MIN_SPLIT")) v.gated_min_split = std::max(64, std::min(4096, atoi(e)));
     return v;
   }();
   return t;
@@ -834,11 +836,12 @@ int b2_rmsnorm(const void* x, int x_is_f32, int ldx, const uint16_t* w, float ep
 }
 
 // splits of the gated attention: one per (kv head, sequence) when those fill the SMs,
-// else enough for about two CTAs per SM, each at least 256 keys
+// else enough for about two CTAs per SM, each at least tuning().gated_min_split keys
 static void gated_attn_plan(int batch, int nkv, int max_len, int sms, int* n_splits, int* split_len) {
   const long long pairs = (long long)batch * nkv;
   int S = 1;
-  if (pairs < sms) S = (int)std::max(1LL, std::min<long long>((2LL * sms + pairs - 1) / pairs, (max_len + 255) / 256));
+  const int mk = tuning().gated_min_split;
+  if (pairs < sms) S = (int)std::max(1LL, std::min<long long>((2LL * sms + pairs - 1) / pairs, (max_len + mk - 1) / mk));
   int sl = (max_len + S - 1) / S;
   sl = (sl + 63) / 64 * 64;
   *split_len = sl;

@@ -49,11 +49,13 @@ def rope_partial(x: np.ndarray, pos: int, inv_freq: np.ndarray) -> np.ndarray:
 
 
 def gated_attention_step(qg, k_new, v_new, q_norm_w, k_norm_w, inv_freq, k_cache, v_cache, pos,
-                         nq: int, nkv: int, eps: float = 1e-6):
+                         nq: int, nkv: int, eps: float = 1e-6, stored=None):
     """One decode token per sequence at positions pos[b] (cache rows 0..pos-1 valid).
 
     Returns (out [B][nq*D] float64 = attention * sigmoid(gate), k_row, v_row [B][nkv][D]),
-    k_row / v_row being what the step appends to the cache at pos."""
+    k_row / v_row being what the step appends to the cache at pos.  `stored` (None:
+    transformers' float32 cache) maps the appended rows to the values a cache of
+    another precision holds, which the attention at pos then reads."""
     qg = np.asarray(qg, np.float64)
     bsz = qg.shape[0]
     d = qg.shape[1] // (2 * nq)
@@ -71,8 +73,10 @@ def gated_attention_step(qg, k_new, v_new, q_norm_w, k_norm_w, inv_freq, k_cache
         kr = rope_partial(kn[b], p, inv_freq)
         k_row[b] = kr
         for g in range(nkv):
-            keys = np.concatenate([np.asarray(k_cache[b, g, :p], np.float64), kr[g][None]], 0)
-            vals = np.concatenate([np.asarray(v_cache[b, g, :p], np.float64), vr[b, g][None]], 0)
+            k_at = kr[g] if stored is None else np.asarray(stored(kr[g]), np.float64)
+            v_at = vr[b, g] if stored is None else np.asarray(stored(vr[b, g]), np.float64)
+            keys = np.concatenate([np.asarray(k_cache[b, g, :p], np.float64), k_at[None]], 0)
+            vals = np.concatenate([np.asarray(v_cache[b, g, :p], np.float64), v_at[None]], 0)
             for j in range(grp):
                 h = g * grp + j
                 s = keys @ qr[h] * d ** -0.5

@@ -2,7 +2,7 @@
 
 Checked against transformers' own module outputs (tests/golden/gated_attn_golden.npz)
 and against the float64 oracle.  The kernel's KV cache is bf16: against the oracle run
-on the same bf16 cache values the gate is the north star's (cos >= 0.99999, max rel
+on the same bf16 cache values (the appended row included) the gate is the north star's (cos >= 0.99999, max rel
 err <= 1e-3, fp32 output); against the module, whose float32 cache the bf16 cache
 rounds, cos >= 0.9999 and rel <= 1e-2.  The appended v row is bit-exact (one bf16
 rounding of the projection output); the appended k row within one bf16 ulp."""
@@ -71,6 +71,11 @@ def synth(rng, bsz, nq, nkv, ctx_max, rot=64, theta=10000.0):
     }
 
 
+def to_bf16(x):
+    """The values the bf16 cache holds for an appended row (the kernel reads the row back)."""
+    return np.asarray(x, np.float32).astype(bfloat16).astype(np.float32)
+
+
 def bf16_ulp_close(got, ref):
     r = np.asarray(ref, np.float32)
     ulp = np.abs(r.astype(bfloat16).astype(np.float32)) * 2.0 ** -7 + 1e-30
@@ -89,7 +94,7 @@ def test_matches_transformers_golden(ops, name):
     out, kc, vc, kc32, vc32 = run(ops, inp, nq, nkv, [pos] * bsz, ctx_max)
     assert_close(out, g[f"{name}/out"], 0.9999, 1e-2, f"{name} vs module")
     ref, _, _ = ga.gated_attention_step(inp["qg"], inp["k_new"], inp["v_new"], inp["q_norm_w"], inp["k_norm_w"],
-                                        inp["inv_freq"], kc32, vc32, [pos] * bsz, nq, nkv)
+                                        inp["inv_freq"], kc32, vc32, [pos] * bsz, nq, nkv, stored=to_bf16)
     assert_close(out, ref, NS_COS, NS_REL, f"{name} vs oracle on the bf16 cache")
     v_row = vc.float().cpu().numpy()[:, :, pos]
     assert np.array_equal(v_row, g[f"{name}/v_row"].astype(bfloat16).astype(np.float32))
@@ -113,7 +118,8 @@ def test_vs_oracle(ops, bsz, nq, nkv, ctx, pos, rot):
     pos = list(rng.integers(0, ctx, bsz)) if pos is None else pos
     out, kc, vc, kc32, vc32 = run(ops, inp, nq, nkv, pos, ctx)
     ref, k_row, v_row = ga.gated_attention_step(inp["qg"], inp["k_new"], inp["v_new"], inp["q_norm_w"],
-                                                inp["k_norm_w"], inp["inv_freq"], kc32, vc32, pos, nq, nkv)
+                                                inp["k_norm_w"], inp["inv_freq"], kc32, vc32, pos, nq, nkv,
+                                                stored=to_bf16)
     assert_close(out, ref, NS_COS, NS_REL, "out")
     for b in range(bsz):  # every sequence and head on its own
         for h in range(nq):
@@ -145,7 +151,8 @@ def test_bf16_output_and_chained_steps(ops):
                                     prm["k_norm_w"], prm["inv_freq"], kc, vc,
                                     torch.tensor(pos, dtype=torch.int32, device="cuda"), nq, nkv)
         ref, k_row, v_row = ga.gated_attention_step(step["qg"], step["k_new"], step["v_new"], inp["q_norm_w"],
-                                                    inp["k_norm_w"], inp["inv_freq"], kc32, vc32, pos, nq, nkv)
+                                                    inp["k_norm_w"], inp["inv_freq"], kc32, vc32, pos, nq, nkv,
+                                                    stored=to_bf16)
         torch.cuda.synchronize()
         assert_close(out.float().cpu().numpy(), ref, 0.9999, 4e-3, f"step {t} (bf16 out)")
         for b in range(bsz):  # the oracle's cache takes the kernel's appended rows
@@ -171,7 +178,7 @@ def test_config5_full_batch_sampled(ops):
     vp = vc[pick].float().cpu().numpy()
     sub = {k: small[k][pick] for k in ("qg", "k_new", "v_new")}
     ref, _, _ = ga.gated_attention_step(sub["qg"], sub["k_new"], sub["v_new"], small["q_norm_w"], small["k_norm_w"],
-                                        small["inv_freq"], kp, vp, [ctx - 1] * 3, nq, nkv)
+                                        small["inv_freq"], kp, vp, [ctx - 1] * 3, nq, nkv, stored=to_bf16)
     assert_close(out[pick], ref, NS_COS, NS_REL, "sampled sequences")
     assert np.isfinite(out).all()
 
