@@ -559,9 +559,11 @@ def run_b200(args, rank: int, world: int) -> dict | None:
         del gl, w8
         extras["attention"] = measure_attention(torch, ops, gen, device, pk["hbm_gbs"], args.steps)
         extras["tc_gemm"] = measure_tc_gemm(torch, ops, gen, device, pk["bf16_tflops"], args.steps)
-        extras["deltanet"] = measure_deltanet(torch, ops, gen, device, pk["hbm_gbs"], args.steps)
-        extras["deltanet_layers"] = measure_deltanet_layers(torch, device, pk["hbm_gbs"], args.steps)
-        extras["gated_attention"] = measure_gated_attention(torch, ops, gen, device, pk["hbm_gbs"], args.steps)
+        if world == 1:  # config 5's single-GPU layer kernels; the other ranks would wait meanwhile
+            extras["deltanet"] = measure_deltanet(torch, ops, gen, device, pk["hbm_gbs"], args.steps)
+            extras["deltanet_layers"] = measure_deltanet_layers(torch, device, pk["hbm_gbs"], args.steps)
+            extras["gated_attention"] = measure_gated_attention(torch, ops, gen, device, pk["hbm_gbs"],
+                                                                args.steps)
 
     # ---- config 4: the full decode step (tensor-parallel across the ranks when N > 1)
     if not args.quick:
