@@ -92,3 +92,26 @@ def test_split_q4_tile_roundtrip(golden):
     nib, d, m = fmt.split_q4_tile(t.tobytes())
     assert np.array_equal(nib, t[1024:])
     assert np.array_equal(fmt.pack_meta(d, m).view(np.uint8), t[:1024])
+
+
+def test_config5_layer_entry_points_fail_cleanly_without_a_device():
+    """The gated DeltaNet and gated attention entry points check the device before any
+    argument, and the torch wrappers refuse host tensors (no CPU fallback)."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present; covered by the gpu tests")
+    lib = _native.lib()
+    st = lib.b2_gated_delta_step(None, 512, None, 256, None, None, 2, None, None, None, None, None, None, 1, 1, 2,
+                                 128, ctypes.c_float(1e-6), None, 256, 0, None)
+    assert st == -4
+    n = ctypes.c_size_t()
+    assert lib.b2_gated_attn_decode_workspace_size(1, 8, 2, 256, 2048, ctypes.byref(n)) == -4
+    st = lib.b2_gated_attn_decode(None, 4096, None, None, 512, None, None, None, 64, None, None, None, 1, 8, 2, 256,
+                                  2048, 2048, ctypes.c_float(1e-6), None, 2048, 0, None, 0, None)
+    assert st == -4
+    from llmnputest_b200 import ops
+    x = torch.zeros(1, 8192)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.gated_delta_step(x, x, x, x, x, x, x, x, x, x, 1, 2)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.gated_attn_decode(x, x, x, x, x, x, x, x, x, 8, 2)
