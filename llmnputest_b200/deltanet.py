@@ -30,9 +30,15 @@ class DeltaNetLayer:
     """Resident weights and states of one linear-attention layer; `step()` is graph-capturable."""
 
     def __init__(self, hidden: int, n_k_heads: int, n_v_heads: int, batch: int, device=None, seed: int = 0,
-                 weights: dict | None = None, eps: float = 1e-6, gemm_min_batch: int = 9):
+                 weights: dict | None = None, eps: float = 1e-6, gemm_min_batch: int = 9, *, ops_impl=None,
+                 cols: tuple[int, int] | None = None, n_in_tile_rows: int | None = None):
+        """cols / n_in_tile_rows: the columns of b and a in the in_proj output and its tile-row
+        count, when the in_proj is not the plain q|k|v|z|b|a stack of these heads (a
+        tensor-parallel shard, llmnputest_b200.tp).  ops_impl: the op implementation (default
+        the GPU path; host-logic tests pass another)."""
         if hidden % TILE_K or (n_v_heads * HEAD_DIM) % TILE_K:
             raise ValueError("hidden and n_v_heads*128 must be multiples of 256 (whole K-tiles)")
+        self.ops = ops_impl if ops_impl is not None else ops
         self.hidden, self.nk, self.nv, self.batch, self.eps = hidden, n_k_heads, n_v_heads, batch, eps
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         d = HEAD_DIM
@@ -43,6 +49,9 @@ class DeltaNetLayer:
         self.c_a = self.c_b + n_v_heads
         n_rows = self.c_a + n_v_heads
         self.nt_in = -(-n_rows // TILE_ROWS)
+        if cols is not None:
+            self.c_b, self.c_a = cols
+            self.nt_in = n_in_tile_rows
         self.kt_h = hidden // TILE_K
         self.nt_h = hidden // TILE_ROWS
         self.kt_v = n_v_heads * d // TILE_K
@@ -55,7 +64,7 @@ class DeltaNetLayer:
         self.h = torch.zeros(batch, n_v_heads * d, dtype=torch.bfloat16, device=dev)
         self.use_gemm = batch >= gemm_min_batch
         if self.use_gemm:
-            nbytes = ops.gemm_workspace_bytes(batch, max(self.kt_h, self.kt_v))
+            nbytes = self.ops.gemm_workspace_bytes(batch, max(self.kt_h, self.kt_v))
             self._ws_raw = torch.empty(nbytes + 256, dtype=torch.uint8, device=dev)
             off = (256 - self._ws_raw.data_ptr() % 256) % 256
             self.gemm_ws = self._ws_raw[off:off + nbytes]
@@ -91,7 +100,21 @@ class DeltaNetLayer:
         preceding kernel.  The projections launch their dependents early, so this is only
         correct when a non-PDL stream operation or a graph boundary separates this
         layer's consecutive steps (the state's previous write is that earlier step)."""
-        w, nv = self.w, self.nv
+        self.mix(resid, prefetch_state)
+        self.out_proj(self.h, resid, accumulate=True)
+        return resid
+
+    def out_proj(self, h: torch.Tensor, out: torch.Tensor, accumulate: bool) -> torch.Tensor:
+        """out (fp32 [B, hidden]) = (or +=) out_proj h."""
+        ops, w = self.ops, self.w
+        if self.use_gemm:
+            return ops.q4_gemm(w["out_proj"], self.nt_h, self.kt_v, h, out=out, accumulate=accumulate,
+                               workspace=self.gemm_ws)
+        return ops.q4_gemv(w["out_proj"], self.nt_h, self.kt_v, h, out=out, accumulate=accumulate, prefetch=True)
+
+    def mix(self, resid: torch.Tensor, prefetch_state: bool = False) -> torch.Tensor:
+        """Input RMSNorm, in_proj and the gated delta step; returns the bf16 [B, nv*128] step output."""
+        ops, w, nv = self.ops, self.w, self.nv
         if self.use_gemm:
             ops.rmsnorm(resid, w["input_norm"], self.eps, out=self.xn)
             ops.q4_gemm(w["in_proj"], self.nt_in, self.kt_h, self.xn, out=self.proj, workspace=self.gemm_ws)
@@ -103,9 +126,4 @@ class DeltaNetLayer:
                              p[:, self.c_a:self.c_a + nv], self.conv_state, w["conv_w"], w["A_log"], w["dt_bias"],
                              w["norm_w"], self.state, self.nk, nv, eps=self.eps, out=self.h,
                              prefetch_state=prefetch_state)
-        if self.use_gemm:
-            ops.q4_gemm(w["out_proj"], self.nt_h, self.kt_v, self.h, out=resid, accumulate=True,
-                        workspace=self.gemm_ws)
-        else:
-            ops.q4_gemv(w["out_proj"], self.nt_h, self.kt_v, self.h, out=resid, accumulate=True, prefetch=True)
-        return resid
+        return self.h

@@ -208,3 +208,124 @@ class TPDecoder:
         else:
             self.logits.copy_(self.logits_local)
         return self.logits
+
+
+# ------------------------------------------------------------------ Qwen3.5 linear attention
+DELTA_D = 128  # linear-attention head dim
+
+
+@dataclass(frozen=True)
+class DeltaNetShardPlan:
+    """Tensor-parallel gated DeltaNet layer: rank `rank` of `world` owns k heads
+    [r*nk/W, (r+1)*nk/W) and the v heads that read them, so its recurrent and conv
+    states, and its step kernel, hold only its heads and need no collective.  Its in_proj
+    is those heads' whole tile-rows of the stacked q|k|v|z|b|a weight plus the b|a
+    tile-rows (one per 32 of the 2*nv b/a rows), which every rank keeps whole; out_proj is
+    split by its heads' whole 256-wide K-tiles and the fp32 partial outputs are
+    all-reduced (sum) into the replicated residual."""
+
+    hidden: int
+    n_k_heads: int
+    n_v_heads: int
+    world: int
+    rank: int
+
+    def __post_init__(self):
+        if self.n_k_heads % self.world or self.n_v_heads % self.n_k_heads:
+            raise ValueError(f"{self.n_k_heads} k heads do not split over {self.world} ranks")
+        if (self.nv_local * DELTA_D) % TILE_K:
+            raise ValueError("each rank's v heads must fill whole 256-wide out_proj K-tiles")
+
+    @property
+    def ratio(self) -> int:
+        return self.n_v_heads // self.n_k_heads
+
+    @property
+    def nk_local(self) -> int:
+        return self.n_k_heads // self.world
+
+    @property
+    def nv_local(self) -> int:
+        return self.nk_local * self.ratio
+
+    @property
+    def k0(self) -> int:
+        return self.rank * self.nk_local
+
+    @property
+    def v0(self) -> int:
+        return self.rank * self.nv_local
+
+    @property
+    def c_b_full(self) -> int:
+        """First b column of the full stacked in_proj output (a multiple of 32)."""
+        return (2 * self.n_k_heads + 2 * self.n_v_heads) * DELTA_D
+
+    def in_proj_tile_rows(self) -> list[int]:
+        """Tile-rows of the full stacked in_proj this rank owns, in its order q|k|v|z|b+a."""
+        tph = DELTA_D // TILE_ROWS  # tile-rows per head
+        nk, nv = self.n_k_heads, self.n_v_heads
+        q = range(self.k0 * tph, (self.k0 + self.nk_local) * tph)
+        k = range((nk + self.k0) * tph, (nk + self.k0 + self.nk_local) * tph)
+        v = range((2 * nk + self.v0) * tph, (2 * nk + self.v0 + self.nv_local) * tph)
+        z = range((2 * nk + nv + self.v0) * tph, (2 * nk + nv + self.v0 + self.nv_local) * tph)
+        ba = range(self.c_b_full // TILE_ROWS, -(-(self.c_b_full + 2 * nv) // TILE_ROWS))
+        return [*q, *k, *v, *z, *ba]
+
+    def local_cols(self) -> tuple[int, int]:
+        """(b, a) columns of this rank's first v head in its in_proj output."""
+        c_ba = (2 * self.nk_local + 2 * self.nv_local) * DELTA_D
+        return c_ba + self.v0, c_ba + self.n_v_heads + self.v0
+
+    def conv_channels(self) -> list[int]:
+        """Channels of the full conv (q|k|v, conv_dim wide) this rank owns, in its order q|k|v."""
+        d, nk = DELTA_D, self.n_k_heads
+        return [*range(self.k0 * d, (self.k0 + self.nk_local) * d),
+                *range((nk + self.k0) * d, (nk + self.k0 + self.nk_local) * d),
+                *range((2 * nk + self.v0) * d, (2 * nk + self.v0 + self.nv_local) * d)]
+
+    def out_proj_k_tiles(self) -> range:
+        per = self.nv_local * DELTA_D // TILE_K
+        return range(self.rank * per, (self.rank + 1) * per)
+
+
+def shard_deltanet(full: dict, plan: DeltaNetShardPlan) -> dict:
+    """One rank's slice of a full DeltaNetLayer weight dict (llmnputest_b200.deltanet)."""
+    kt_h = plan.hidden // TILE_K
+    kt_v = plan.n_v_heads * DELTA_D // TILE_K
+    ch = torch.as_tensor(plan.conv_channels(), dtype=torch.long, device=full["conv_w"].device)
+    vh = slice(plan.v0, plan.v0 + plan.nv_local)
+    return {
+        "in_proj": take_tile_rows(full["in_proj"], kt_h, Q4_TILE_BYTES, plan.in_proj_tile_rows()),
+        "out_proj": take_k_tiles(full["out_proj"], plan.hidden // TILE_ROWS, kt_v, Q4_TILE_BYTES,
+                                 plan.out_proj_k_tiles()),
+        "conv_w": full["conv_w"].index_select(0, ch).contiguous(),
+        "A_log": full["A_log"][vh].contiguous(),
+        "dt_bias": full["dt_bias"][vh].contiguous(),
+        "norm_w": full["norm_w"],
+        "input_norm": full["input_norm"],
+    }
+
+
+class TPDeltaNetLayer:
+    """This rank's part of a gated DeltaNet layer: the local heads' mixer, the out_proj
+    K-slice, and an all-reduce of its fp32 partial into the residual."""
+
+    def __init__(self, plan: DeltaNetShardPlan, batch: int, shard: dict, device=None, eps: float = 1e-6,
+                 ops=None, gemm_min_batch: int = 9):
+        from .deltanet import DeltaNetLayer
+        self.plan = plan
+        self.layer = DeltaNetLayer(plan.hidden, plan.nk_local, plan.nv_local, batch, device=device, weights=shard,
+                                   eps=eps, gemm_min_batch=gemm_min_batch, ops_impl=ops, cols=plan.local_cols(),
+                                   n_in_tile_rows=len(plan.in_proj_tile_rows()))
+        self.partial = torch.zeros(batch, plan.hidden, dtype=torch.float32, device=self.layer.device)
+
+    def step(self, resid: torch.Tensor) -> torch.Tensor:
+        """resid (fp32 [B, hidden], the same on every rank) += the layer's token mixer."""
+        h = self.layer.mix(resid)
+        if self.plan.world == 1:
+            return self.layer.out_proj(h, resid, accumulate=True)
+        self.layer.out_proj(h, self.partial, accumulate=False)
+        dist.all_reduce(self.partial)
+        resid.add_(self.partial)
+        return resid
