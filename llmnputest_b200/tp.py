@@ -329,3 +329,96 @@ class TPDeltaNetLayer:
         dist.all_reduce(self.partial)
         resid.add_(self.partial)
         return resid
+
+
+# ------------------------------------------------------------------ Qwen3.5 gated full attention
+GATED_D = 256  # gated-attention head dim
+
+
+@dataclass(frozen=True)
+class GatedAttnShardPlan:
+    """Tensor-parallel gated full-attention layer: rank `rank` of `world` owns kv heads
+    [r*nkv/W, (r+1)*nkv/W) and their q heads, so its KV cache and attention kernel hold
+    only its heads; its in_proj is those heads' whole tile-rows of the stacked
+    q_proj (q|gate per head) | k_proj | v_proj weight, its o_proj the heads' whole
+    256-wide K-tiles, and the fp32 partial outputs are all-reduced into the residual."""
+
+    hidden: int
+    n_q_heads: int
+    n_kv_heads: int
+    world: int
+    rank: int
+
+    def __post_init__(self):
+        if self.n_kv_heads % self.world or self.n_q_heads % self.n_kv_heads:
+            raise ValueError(f"{self.n_kv_heads} kv heads do not split over {self.world} ranks")
+
+    @property
+    def kv_local(self) -> int:
+        return self.n_kv_heads // self.world
+
+    @property
+    def q_local(self) -> int:
+        return self.kv_local * (self.n_q_heads // self.n_kv_heads)
+
+    @property
+    def kv0(self) -> int:
+        return self.rank * self.kv_local
+
+    @property
+    def q0(self) -> int:
+        return self.rank * self.q_local
+
+    def in_proj_tile_rows(self) -> list[int]:
+        """Tile-rows of the full stacked in_proj this rank owns, in its order q|k|v."""
+        tq, tkv = 2 * GATED_D // TILE_ROWS, GATED_D // TILE_ROWS  # tile-rows per q head (q|gate), per k/v head
+        k_base = self.n_q_heads * tq
+        v_base = k_base + self.n_kv_heads * tkv
+        return [*range(self.q0 * tq, (self.q0 + self.q_local) * tq),
+                *range(k_base + self.kv0 * tkv, k_base + (self.kv0 + self.kv_local) * tkv),
+                *range(v_base + self.kv0 * tkv, v_base + (self.kv0 + self.kv_local) * tkv)]
+
+    def o_proj_k_tiles(self) -> range:
+        per = GATED_D // TILE_K
+        return range(self.q0 * per, (self.q0 + self.q_local) * per)
+
+
+def shard_gated_attention(full: dict, plan: GatedAttnShardPlan) -> dict:
+    """One rank's slice of a full GatedAttentionLayer weight dict (llmnputest_b200.gated_attention)."""
+    kt_h = plan.hidden // TILE_K
+    kt_o = plan.n_q_heads * GATED_D // TILE_K
+    return {
+        "in_proj": take_tile_rows(full["in_proj"], kt_h, Q4_TILE_BYTES, plan.in_proj_tile_rows()),
+        "o_proj": take_k_tiles(full["o_proj"], plan.hidden // TILE_ROWS, kt_o, Q4_TILE_BYTES, plan.o_proj_k_tiles()),
+        "q_norm_w": full["q_norm_w"],
+        "k_norm_w": full["k_norm_w"],
+        "inv_freq": full["inv_freq"],
+        "input_norm": full["input_norm"],
+    }
+
+
+class TPGatedAttentionLayer:
+    """This rank's part of a gated full-attention layer: its heads' attention, the o_proj
+    K-slice, and an all-reduce of its fp32 partial into the residual."""
+
+    def __init__(self, plan: GatedAttnShardPlan, batch: int, ctx_max: int, shard: dict, device=None,
+                 eps: float = 1e-6, ops=None, gemm_min_batch: int = 9):
+        from .gated_attention import GatedAttentionLayer
+        self.plan = plan
+        self.layer = GatedAttentionLayer(plan.hidden, plan.q_local, plan.kv_local, batch, ctx_max, device=device,
+                                         weights=shard, eps=eps, gemm_min_batch=gemm_min_batch, ops_impl=ops)
+        self.partial = torch.zeros(batch, plan.hidden, dtype=torch.float32, device=self.layer.device)
+
+    @property
+    def pos(self) -> torch.Tensor:
+        return self.layer.pos
+
+    def step(self, resid: torch.Tensor) -> torch.Tensor:
+        """resid (fp32 [B, hidden], the same on every rank) += the layer's token mixer at `pos`."""
+        a = self.layer.mix(resid)
+        if self.plan.world == 1:
+            return self.layer.o_proj(a, resid, accumulate=True)
+        self.layer.o_proj(a, self.partial, accumulate=False)
+        dist.all_reduce(self.partial)
+        resid.add_(self.partial)
+        return resid
