@@ -49,6 +49,15 @@ class DeltaNetLayer:
         self.c_a = self.c_b + n_v_heads
         n_rows = self.c_a + n_v_heads
         self.nt_in = -(-n_rows // TILE_ROWS)
+        # in_proj_b / in_proj_a as a dense fp32 matrix [2*nv][hidden] (a q4nx file stores them
+        # as plain bf16, not tiles): the q4 in_proj is then q|k|v|z only, and b|a follow it
+        self.ba_dense = weights is not None and "ba_dense" in weights
+        if self.ba_dense:
+            if cols is not None:
+                raise ValueError("a tensor-parallel shard keeps b|a as tile-rows, not ba_dense")
+            self.nt_in = (self.c_z + n_v_heads * d) // TILE_ROWS
+            self.c_b = self.nt_in * TILE_ROWS
+            self.c_a = self.c_b + n_v_heads
         if cols is not None:
             self.c_b, self.c_a = cols
             self.nt_in = n_in_tile_rows
@@ -60,7 +69,12 @@ class DeltaNetLayer:
         self.conv_state = torch.zeros(batch, self.conv_dim, 4, dtype=torch.float32, device=dev)
         self.state = torch.zeros(batch, n_v_heads, d, d, dtype=torch.float32, device=dev)
         self.xn = torch.zeros(batch, hidden, dtype=torch.bfloat16, device=dev)
-        self.proj = torch.zeros(batch, self.nt_in * TILE_ROWS, dtype=torch.float32, device=dev)
+        self.proj = torch.zeros(batch, max(self.nt_in * TILE_ROWS, self.c_a + n_v_heads), dtype=torch.float32,
+                                device=dev)
+        if self.ba_dense:
+            self.w_ba_t = self.w["ba_dense"].t().contiguous()  # [hidden][2*nv]
+            self.xn_f = torch.zeros(batch, hidden, dtype=torch.float32, device=dev)
+            self.ba_out = torch.zeros(batch, 2 * n_v_heads, dtype=torch.float32, device=dev)
         self.h = torch.zeros(batch, n_v_heads * d, dtype=torch.bfloat16, device=dev)
         self.use_gemm = batch >= gemm_min_batch
         if self.use_gemm:
@@ -89,6 +103,8 @@ class DeltaNetLayer:
         written, the projection output written and read, the residual read and written."""
         d, b = HEAD_DIM, self.batch
         w = self.w["in_proj"].numel() + self.w["out_proj"].numel()
+        if self.ba_dense:
+            w += self.w["ba_dense"].numel() * 4
         states = 2 * 4 * b * (self.nv * d * d + self.conv_dim * 4)
         proj = 2 * 4 * b * self.nt_in * TILE_ROWS
         return w + states + proj + 2 * b * self.nv * d + 2 * 4 * b * self.hidden
@@ -115,12 +131,19 @@ class DeltaNetLayer:
     def mix(self, resid: torch.Tensor, prefetch_state: bool = False) -> torch.Tensor:
         """Input RMSNorm, in_proj and the gated delta step; returns the bf16 [B, nv*128] step output."""
         ops, w, nv = self.ops, self.w, self.nv
+        q4_out = self.proj[:, :self.nt_in * TILE_ROWS]  # the whole buffer unless b|a follow the q4 rows
         if self.use_gemm:
             ops.rmsnorm(resid, w["input_norm"], self.eps, out=self.xn)
-            ops.q4_gemm(w["in_proj"], self.nt_in, self.kt_h, self.xn, out=self.proj, workspace=self.gemm_ws)
+            ops.q4_gemm(w["in_proj"], self.nt_in, self.kt_h, self.xn, out=q4_out, workspace=self.gemm_ws)
         else:
-            ops.gemv_rmsnorm(w["in_proj"], self.nt_in, self.kt_h, resid, w["input_norm"], self.eps, out=self.proj,
+            ops.gemv_rmsnorm(w["in_proj"], self.nt_in, self.kt_h, resid, w["input_norm"], self.eps, out=q4_out,
                              prefetch=True)
+        if self.ba_dense:  # b|a = bf16(rmsnorm(x)) W_ba^T in fp32 (a plain library GEMM of 2*nv columns)
+            if not self.use_gemm:
+                ops.rmsnorm(resid, w["input_norm"], self.eps, out=self.xn)
+            self.xn_f.copy_(self.xn)
+            torch.mm(self.xn_f, self.w_ba_t, out=self.ba_out)
+            self.proj[:, self.c_b:self.c_a + nv].copy_(self.ba_out)
         p = self.proj
         ops.gated_delta_step(p[:, :self.c_z], p[:, self.c_z:self.c_b], p[:, self.c_b:self.c_a],
                              p[:, self.c_a:self.c_a + nv], self.conv_state, w["conv_w"], w["A_log"], w["dt_bias"],
