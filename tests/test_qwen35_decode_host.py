@@ -6,6 +6,7 @@ the host-logic tests: this checks the composition (layer order, residual adds,
 norms, shared positions, cache and state carried across steps), not the kernels."""
 
 import numpy as np
+import pytest
 import torch
 from ml_dtypes import bfloat16
 
@@ -22,16 +23,27 @@ CFG = Qwen35Config(hidden=256, n_layers=4, layer_types=("linear_attention",) * 3
 
 
 class Q35Ops(DeltaOracleOps, GatedOracleOps):
-    pass
+    """Adds the tensor-core GEMM entry points (same arithmetic as the GEMV shim)."""
+
+    def gemm_workspace_bytes(self, *a):
+        return 0
+
+    def q4_gemm(self, tiles, n_t, k_t, x, out=None, accumulate=False, workspace=None):
+        return self.q4_gemv(tiles, n_t, k_t, x, out=out, accumulate=accumulate)
+
+    def q4_swiglu_gemm(self, gate, up, n_t, k_t, x, out=None, workspace=None):
+        return self.q4_swiglu_gemv(gate, up, n_t, k_t, x, out=out)
 
 
 def _bf(x):
     return np.asarray(x, np.float32).astype(bfloat16).astype(np.float32)
 
 
-def test_qwen35_decoder_matches_oracle_composition():
-    bsz, ctx = 2, 8
+@pytest.mark.parametrize("bsz", [2, 10])  # GEMV path, tensor-core GEMM path (norm launches apart)
+def test_qwen35_decoder_matches_oracle_composition(bsz):
+    ctx = 8
     dec = Qwen35Decoder(CFG, bsz, ctx, device="cpu", seed=1, ops_impl=Q35Ops())
+    assert dec.use_gemm == (bsz >= 9)
     c = CFG
     W = [{k: (v.float().numpy() if v.dtype != torch.uint8 else v.numpy()) for k, v in L["mixer"].items()}
          for L in dec.w["layers"]]
@@ -45,7 +57,7 @@ def test_qwen35_decoder_matches_oracle_composition():
     kt_h, nt_h = c.hidden // 256, c.hidden // 32
     for t in range(2):
         x = rng.standard_normal((bsz, c.hidden)).astype(np.float32)
-        pos = np.array([3, 5]) + t
+        pos = (np.arange(bsz) % 5 + 2) + t
         dec.x_in.copy_(torch.from_numpy(x))
         dec.pos.copy_(torch.from_numpy(pos.astype(np.int32)))
         logits = dec.step().numpy().copy()
