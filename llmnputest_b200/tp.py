@@ -272,6 +272,11 @@ class DeltaNetShardPlan:
         ba = range(self.c_b_full // TILE_ROWS, -(-(self.c_b_full + 2 * nv) // TILE_ROWS))
         return [*q, *k, *v, *z, *ba]
 
+    @property
+    def n_ba_tile_rows(self) -> int:
+        """Tile-rows of the b|a rows at the end of the stacked in_proj."""
+        return -(-(self.c_b_full + 2 * self.n_v_heads) // TILE_ROWS) - self.c_b_full // TILE_ROWS
+
     def local_cols(self) -> tuple[int, int]:
         """(b, a) columns of this rank's first v head in its in_proj output."""
         c_ba = (2 * self.nk_local + 2 * self.nv_local) * DELTA_D
@@ -290,13 +295,24 @@ class DeltaNetShardPlan:
 
 
 def shard_deltanet(full: dict, plan: DeltaNetShardPlan) -> dict:
-    """One rank's slice of a full DeltaNetLayer weight dict (llmnputest_b200.deltanet)."""
+    """One rank's slice of a full DeltaNetLayer weight dict (llmnputest_b200.deltanet).
+
+    With b|a as q4 tile-rows the rank keeps those rows whole (`local_cols` locates its
+    heads); with b|a dense ("ba_dense", as read from a q4nx file) it keeps its heads'
+    rows of b and of a, and its in_proj is q|k|v|z only: the layer's own dense layout."""
     kt_h = plan.hidden // TILE_K
     kt_v = plan.n_v_heads * DELTA_D // TILE_K
     ch = torch.as_tensor(plan.conv_channels(), dtype=torch.long, device=full["conv_w"].device)
     vh = slice(plan.v0, plan.v0 + plan.nv_local)
+    rows = plan.in_proj_tile_rows()
+    extra = {}
+    if "ba_dense" in full:
+        rows = rows[:len(rows) - plan.n_ba_tile_rows]
+        nv = plan.n_v_heads
+        extra["ba_dense"] = torch.cat([full["ba_dense"][vh], full["ba_dense"][nv + plan.v0:nv + plan.v0 + plan.nv_local]])
     return {
-        "in_proj": take_tile_rows(full["in_proj"], kt_h, Q4_TILE_BYTES, plan.in_proj_tile_rows()),
+        **extra,
+        "in_proj": take_tile_rows(full["in_proj"], kt_h, Q4_TILE_BYTES, rows),
         "out_proj": take_k_tiles(full["out_proj"], plan.hidden // TILE_ROWS, kt_v, Q4_TILE_BYTES,
                                  plan.out_proj_k_tiles()),
         "conv_w": full["conv_w"].index_select(0, ch).contiguous(),
@@ -315,9 +331,11 @@ class TPDeltaNetLayer:
                  ops=None, gemm_min_batch: int = 9):
         from .deltanet import DeltaNetLayer
         self.plan = plan
+        dense = "ba_dense" in shard  # b|a dense: the layer's own layout for its heads
         self.layer = DeltaNetLayer(plan.hidden, plan.nk_local, plan.nv_local, batch, device=device, weights=shard,
-                                   eps=eps, gemm_min_batch=gemm_min_batch, ops_impl=ops, cols=plan.local_cols(),
-                                   n_in_tile_rows=len(plan.in_proj_tile_rows()))
+                                   eps=eps, gemm_min_batch=gemm_min_batch, ops_impl=ops,
+                                   cols=None if dense else plan.local_cols(),
+                                   n_in_tile_rows=None if dense else len(plan.in_proj_tile_rows()))
         self.partial = torch.zeros(batch, plan.hidden, dtype=torch.float32, device=self.layer.device)
 
     def step(self, resid: torch.Tensor) -> torch.Tensor:

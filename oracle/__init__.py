@@ -13,4 +13,11 @@ Parity is pinned: `tests/test_oracle_golden.py` checks every function here
 against golden vectors produced by running the reference's own Python code
 (`tests/golden/make_golden.py`), and against the reference's compiled
 `cpu_baseline.cpp` (`oracle/Makefile` -> `oracle/_ref/`).
+
+The Qwen3.5 layers the reference runs through transformers (its gated DeltaNet and
+gated attention decode steps) are restated in `deltanet_oracle.py` and
+`gated_attention_oracle.py`, pinned the same way against golden vectors recorded
+from transformers' own modules (`tests/golden/make_deltanet_golden.py`,
+`make_gated_attn_golden.py`; `tests/test_deltanet_oracle.py`,
+`test_gated_attn_oracle.py`).
 """

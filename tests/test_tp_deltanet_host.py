@@ -36,10 +36,12 @@ class DeltaOracleOps(OracleOps):
         return out
 
 
-def full_layer(nk, nv, seed=0):
+def full_layer(nk, nv, seed=0, dense=False):
+    """Seeded full layer weights; dense=True keeps b|a as a dense fp32 matrix (as a q4nx
+    file's bf16 in_proj_b / in_proj_a are loaded) instead of q4 tile-rows."""
     rng = np.random.default_rng(seed)
     d = 128
-    n_in = -(-((2 * nk + 2 * nv) * d + 2 * nv) // 32)
+    n_in = -(-((2 * nk + 2 * nv) * d + (0 if dense else 2 * nv)) // 32)
     u8 = lambda t: torch.from_numpy(np.ascontiguousarray(t).reshape(-1))
     f32 = lambda t: torch.from_numpy(np.asarray(t, np.float32))
     return {
@@ -50,6 +52,7 @@ def full_layer(nk, nv, seed=0):
         "dt_bias": f32(rng.standard_normal(nv)),
         "norm_w": f32(1 + 0.1 * rng.standard_normal(d)),
         "input_norm": _bf(1 + 0.1 * rng.standard_normal(HIDDEN)),
+        **({"ba_dense": f32(0.05 * rng.standard_normal((2 * nv, HIDDEN)))} if dense else {}),
     }, n_in
 
 
@@ -95,11 +98,11 @@ def test_plan_refuses_cuts_inside_tiles():
 NK, NV = 2, 4
 
 
-def _run_rank(rank, world, port, xs, result_path):
+def _run_rank(rank, world, port, xs, result_path, dense=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        full, _ = full_layer(NK, NV, seed=3)
+        full, _ = full_layer(NK, NV, seed=3, dense=dense)
         plan = DeltaNetShardPlan(HIDDEN, NK, NV, world, rank)
         layer = TPDeltaNetLayer(plan, xs.shape[1], shard_deltanet(full, plan), device="cpu", ops=DeltaOracleOps())
         # the same nonzero starting states on every world size: rank's heads of one seeded full state
@@ -118,7 +121,8 @@ def _run_rank(rank, world, port, xs, result_path):
         dist.destroy_process_group()
 
 
-def test_tp_deltanet_gloo_matches_single_rank(tmp_path):
+@pytest.mark.parametrize("dense", [False, True])  # b|a as tile-rows / dense (from a q4nx file)
+def test_tp_deltanet_gloo_matches_single_rank(tmp_path, dense):
     rng = np.random.default_rng(11)
     xs = torch.from_numpy(rng.standard_normal((2, 2, HIDDEN)).astype(np.float32))
     ctx_mp = mp.get_context("spawn")
@@ -126,7 +130,7 @@ def test_tp_deltanet_gloo_matches_single_rank(tmp_path):
     for world in (1, 2):
         paths[world] = tmp_path / f"w{world}.pt"
         port = _free_port()
-        procs = [ctx_mp.Process(target=_run_rank, args=(r, world, port, xs, str(paths[world])))
+        procs = [ctx_mp.Process(target=_run_rank, args=(r, world, port, xs, str(paths[world]), dense))
                  for r in range(world)]
         for p in procs:
             p.start()
