@@ -61,8 +61,10 @@ const char* b2_last_error_message(void);
  *   overlaps the tail of the previous kernel in the stream (default on). */
 int b2_set_launch_options(int pdl);
 
-/* Read and clear the device error word that kernels set when a bounded wait
- * gives up (0 = none).  Synchronises `stream`.  Returns B2_OK or B2_ERR_CUDA. */
+/* Read and clear the device error word (0 = none; the first error wins): 1-4 a
+ * bounded wait gave up (1 full-wait, 2 empty-wait, 3 drain, 4 grid barrier), 5 an
+ * attention call met a sequence position outside its cache or planned length.
+ * Synchronises `stream`.  Returns B2_OK or B2_ERR_CUDA. */
 int b2_read_device_error(int* code, void* stream);
 
 /* Flags for the GEMV entry points. */
@@ -130,7 +132,9 @@ int b2_q8_dequant_matrix(const uint8_t* tiles, int n_tile_rows, int k_tiles, flo
  *                    its v are written at position pos[b] (unless
  *                    B2_ATTN_NO_APPEND), and positions 0..pos[b] are attended
  *   pos              int32 [B] device array; max_len >= max(pos) + 1 sizes the
- *                    context split (<= ctx_max)
+ *                    context split (<= ctx_max).  A kernel records device
+ *                    error 5 and reads and writes nothing for a sequence
+ *                    whose pos lies outside 0..ctx_max-1
  *   theta, scale     RoPE base (half-split convention) and the score scale
  *                    (head_dim^-0.5 for the reference model)
  *   out              bf16 [B][ldo] (fp32 with B2_ATTN_OUT_F32), q head j at

@@ -107,6 +107,11 @@ __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) gqa_decode_kernel(cons
   if (!p.prefetch_kv) pdl_wait();  // q/k/v come from the previous kernel
   pdl_launch_dependents();
   const int pos = p.pos[b];
+  if (pos < 0 || pos >= p.ctx_max) {  // outside the cache: record, read and write nothing
+    if (p.prefetch_kv) pdl_wait();     // leave only after the preceding kernel, as every path does
+    if (threadIdx.x == 0) record_error(5);
+    return;  // uniform over the CTA and its cluster (one sequence), before any barrier
+  }
   const int len = pos + 1;
   const int lo = split * p.split_len;
   const int hi = min(len, lo + p.split_len);
