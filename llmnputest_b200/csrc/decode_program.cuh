@@ -631,7 +631,11 @@ __device__ __forceinline__ void prog_attention_phase(const ProgParams& p, const 
     const int kvh = (u / P.n_splits) % hkv;
     const int b = u / (P.n_splits * hkv);
     const int pos = p.pos[b];
-    const int len = pos + 1;
+    // a position outside the cache makes the unit empty (no keys, no append), as a split
+    // past pos is: every barrier of the launch is still reached
+    const bool bad_pos = pos < 0 || pos >= P.ctx_max;
+    if (bad_pos && split == 0 && kvh == 0 && ctid == 0) record_error(5);
+    const int len = bad_pos ? 0 : pos + 1;
     const int lo = split * P.split_len;
     const int hi = min(len, lo + P.split_len);
     const float* rope = p.rope + b * 64;
@@ -650,7 +654,7 @@ __device__ __forceinline__ void prog_attention_phase(const ProgParams& p, const 
       const int j = e / (D / 2), i = e % (D / 2);
       rot(qrow + (kvh * grp + j) * D, qh + j * kAttnQW * 2, i);
     }
-    if (pos >= lo && pos < hi) {  // append the new token's k (rotated) and v
+    if (!bad_pos && pos >= lo && pos < hi) {  // append the new token's k (rotated) and v
       const size_t row = ((static_cast<size_t>(b) * hkv + kvh) * P.ctx_max + pos) * D;
       const float* ks = qrow + hq * D + kvh * D;
       const float* vs = qrow + (hq + hkv) * D + kvh * D;
