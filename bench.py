@@ -488,6 +488,46 @@ def measure_gated_attention(torch, ops, gen, device, hbm_peak: float, steps: int
     return out
 
 
+def measure_qwen35_step(torch, device, hbm_peak: float, steps: int) -> list:
+    """Config 5 as one decode step (llmnputest_b200.qwen35_decode.Qwen35Decoder: 18 gated
+    DeltaNet + 6 gated attention layers of hidden 1024, SwiGLU MLPs of 3584, the q8
+    lm_head 248320 x 1024) at ctx 2048 (pos 2047), batch 1 (GEMVs) and 256 (tcgen05 GEMMs;
+    the lm_head GEMV in passes of 16 tokens), one CUDA graph per step.  Algorithmic bytes:
+    every weight tile once, the DeltaNet states read and written, each attention layer's
+    bf16 K/V read.  Measured last: an exception is recorded instead of a number."""
+    from llmnputest_b200 import ops
+    from llmnputest_b200.qwen35_decode import Qwen35Config, Qwen35Decoder
+    out = []
+    try:
+        cfg = Qwen35Config()
+        for bsz in (1, 256):
+            dec = Qwen35Decoder(cfg, bsz, GATED_CTX, device=device, seed=11)
+            dec.pos.fill_(GATED_CTX - 1)
+            dec.x_in.normal_()
+            nbytes = dec.w["lm_head"].numel()
+            for m, L in zip(dec.mixers, dec.w["layers"]):
+                nbytes += L["gate"].numel() + L["up"].numel() + L["down"].numel()
+                if hasattr(m, "state"):  # DeltaNetLayer: its weights, states, projection, residual
+                    nbytes += m.bytes_per_step()
+                else:
+                    nbytes += (m.w["in_proj"].numel() + m.w["o_proj"].numel()
+                               + bsz * cfg.n_kv_heads * GATED_CTX * GATED_D * 2 * 2)
+            g = graph_of(torch, dec.step)
+            t_ms = time_graph(torch, g, max(5, min(50, steps // 4)), 3)
+            gbs = nbytes / (t_ms * 1e-3) / 1e9
+            out.append({"batch": bsz, "ctx": GATED_CTX, "ms_per_step": round(t_ms, 4),
+                        "tok_s": round(bsz / (t_ms * 1e-3), 1), "gbs": round(gbs, 1),
+                        "frac_of_measured_hbm": round(gbs / hbm_peak, 3), "bytes_per_step": nbytes,
+                        "how": "tcgen05 GEMM, cuda graph" if dec.use_gemm else "GEMV, cuda graph"})
+            del g, dec
+            torch.cuda.empty_cache()
+        if ops.device_error() != 0:
+            out.append({"error": "a kernel recorded a device-side error"})
+    except Exception as e:  # recorded, so the rest of the line stands
+        out.append({"error": f"{type(e).__name__}: {str(e)[:300]}"})
+    return out
+
+
 def run_b200(args, rank: int, world: int) -> dict | None:
     import torch
     import torch.distributed as dist
@@ -651,6 +691,8 @@ def run_b200(args, rank: int, world: int) -> dict | None:
                      "kernel": "q4nx_gemv_kernel<q4,NB=1,f32>", "peak_src": pk["src"]},
         "clocks": clk.summary(),
     }
+    if world == 1 and not args.quick:  # config 5 as one step, last (see measure_qwen35_step)
+        extras["qwen35_step"] = measure_qwen35_step(torch, device, pk["hbm_gbs"], args.steps)
     out.update(extras)
     if world == 1 and not args.no_cpu_baseline:
         cb = run_reference_gemv(iters=20)
