@@ -94,7 +94,7 @@ class TPQwen35Decoder:
     """This rank's part of the Qwen3.5 step; collectives on the default process group."""
 
     def __init__(self, cfg: Qwen35Config, batch: int, ctx_max: int, shard: dict, plan: Qwen35ShardPlan, device=None,
-                 ops=None):
+                 ops=None, gemm_min_batch: int = 9):
         if ops is None:
             from . import ops  # the GPU path; host-logic tests pass another implementation
         from .gated_attention import GatedAttentionLayer
@@ -106,15 +106,15 @@ class TPQwen35Decoder:
         for kind, L in zip(c.layer_types, shard["layers"]):
             if kind == "linear_attention":
                 m = TPDeltaNetLayer(plan.delta(), batch, L["mixer"], device=dev, eps=c.eps, ops=ops,
-                                    gemm_min_batch=1 << 30)
+                                    gemm_min_batch=gemm_min_batch)
             elif plan.attn() is not None:
                 m = TPGatedAttentionLayer(plan.attn(), batch, ctx_max, L["mixer"], device=dev, eps=c.eps, ops=ops,
-                                          gemm_min_batch=1 << 30)
+                                          gemm_min_batch=gemm_min_batch)
                 m.layer.pos = self.pos
             else:
                 m = GatedAttentionLayer(c.hidden, c.n_q_heads, c.n_kv_heads, batch, ctx_max, device=dev,
                                         weights=L["mixer"], eps=c.eps, rot_dim=c.rot_dim, theta=c.rope_theta,
-                                        gemm_min_batch=1 << 30, ops_impl=ops)
+                                        gemm_min_batch=gemm_min_batch, ops_impl=ops)
                 m.pos = self.pos
             self.mixers.append(m)
         self.w = shard
@@ -125,20 +125,34 @@ class TPQwen35Decoder:
         self.x_in = torch.zeros(batch, c.hidden, dtype=torch.float32, device=dev)
         self.resid = torch.zeros(batch, c.hidden, dtype=torch.float32, device=dev)
         self.h = torch.zeros(batch, self.nt_i_local * TILE_ROWS, dtype=torch.bfloat16, device=dev)
+        self.xn = torch.zeros(batch, c.hidden, dtype=torch.bfloat16, device=dev)
+        self.use_gemm = batch >= gemm_min_batch
+        if self.use_gemm:
+            nbytes = ops.gemm_workspace_bytes(batch, max(self.kt_h, self.kt_i_local))
+            self._ws_raw = torch.empty(nbytes + 256, dtype=torch.uint8, device=dev)
+            off = (256 - self._ws_raw.data_ptr() % 256) % 256
+            self.gemm_ws = self._ws_raw[off:off + nbytes]
         self.down = torch.zeros(batch, c.hidden, dtype=torch.float32, device=dev)
         self.logits_local = torch.zeros(batch, self.nt_v_local * TILE_ROWS, dtype=torch.float32, device=dev)
         self.logits_all = torch.zeros(W * batch, self.nt_v_local * TILE_ROWS, dtype=torch.float32, device=dev)
         self.logits = torch.zeros(batch, c.vocab, dtype=torch.float32, device=dev)
 
     def step(self) -> torch.Tensor:
-        """One decode step (GEMV path): x_in at positions `pos` -> logits [B, vocab] on every rank."""
+        """One decode step: x_in at positions `pos` -> logits [B, vocab] on every rank (GEMVs
+        below gemm_min_batch, tcgen05 GEMMs from it; the lm_head GEMV in passes of 16 tokens)."""
         ops, c, W = self.ops, self.cfg, self.plan.world
         self.resid.copy_(self.x_in)
         for m, L in zip(self.mixers, self.w["layers"]):
             m.step(self.resid)
-            ops.swiglu_gemv_rmsnorm(L["gate"], L["up"], self.nt_i_local, self.kt_h, self.resid, L["post_norm"], c.eps,
-                                    out=self.h, prefetch=True)
-            ops.q4_gemv(L["down"], self.nt_h, self.kt_i_local, self.h, out=self.down, prefetch=True)
+            if self.use_gemm:
+                ops.rmsnorm(self.resid, L["post_norm"], c.eps, out=self.xn)
+                ops.q4_swiglu_gemm(L["gate"], L["up"], self.nt_i_local, self.kt_h, self.xn, out=self.h,
+                                   workspace=self.gemm_ws)
+                ops.q4_gemm(L["down"], self.nt_h, self.kt_i_local, self.h, out=self.down, workspace=self.gemm_ws)
+            else:
+                ops.swiglu_gemv_rmsnorm(L["gate"], L["up"], self.nt_i_local, self.kt_h, self.resid, L["post_norm"],
+                                        c.eps, out=self.h, prefetch=True)
+                ops.q4_gemv(L["down"], self.nt_h, self.kt_i_local, self.h, out=self.down, prefetch=True)
             if W > 1:
                 dist.all_reduce(self.down)
             self.resid.add_(self.down)

@@ -37,19 +37,19 @@ def test_split_even_covers_every_unit_once():
 def _inputs(cfg, bsz=2):
     rng = np.random.default_rng(21)
     xs = torch.from_numpy(rng.standard_normal((2, bsz, cfg.hidden)).astype(np.float32))
-    return xs, torch.tensor([3, 6], dtype=torch.int32)
+    return xs, torch.from_numpy((np.arange(bsz) % 6 + 3).astype(np.int32))
 
 
 def _full(cfg):
     return Qwen35Decoder(cfg, 1, 1, device="cpu", seed=7, ops_impl=Q35Ops()).w
 
 
-def _run_rank(rank, world, port, nkv, result_path):
+def _run_rank(rank, world, port, nkv, result_path, bsz):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         cfg = cfg_of(nkv)
-        xs, pos = _inputs(cfg)
+        xs, pos = _inputs(cfg, bsz)
         plan = Qwen35ShardPlan(cfg, world, rank)
         dec = TPQwen35Decoder(cfg, xs.shape[1], 12, shard_qwen35(_full(cfg), plan), plan, device="cpu",
                               ops=Q35Ops())
@@ -64,14 +64,15 @@ def _run_rank(rank, world, port, nkv, result_path):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("nkv", [2, 1])  # attention sharded by kv head / replicated (1 kv head, 2 ranks)
-def test_tp_qwen35_gloo_matches_single_rank(tmp_path, nkv):
+# attention sharded by kv head / replicated (1 kv head, 2 ranks); GEMV path / tcgen05 GEMM path
+@pytest.mark.parametrize("nkv,bsz", [(2, 2), (1, 2), (2, 10)])
+def test_tp_qwen35_gloo_matches_single_rank(tmp_path, nkv, bsz):
     ctx_mp = mp.get_context("spawn")
     paths = {}
     for world in (1, 2):
         paths[world] = tmp_path / f"w{world}.pt"
         port = _free_port()
-        procs = [ctx_mp.Process(target=_run_rank, args=(r, world, port, nkv, str(paths[world])))
+        procs = [ctx_mp.Process(target=_run_rank, args=(r, world, port, nkv, str(paths[world]), bsz))
                  for r in range(world)]
         for p in procs:
             p.start()
@@ -84,7 +85,7 @@ def test_tp_qwen35_gloo_matches_single_rank(tmp_path, nkv):
         assert cos >= 0.99999 and rel <= 1e-3, (t, cos, rel)
     # and the single-rank TP stack is the plain stack
     cfg = cfg_of(nkv)
-    xs, pos = _inputs(cfg)
+    xs, pos = _inputs(cfg, bsz)
     dec = Qwen35Decoder(cfg, xs.shape[1], 12, device="cpu", weights=_full(cfg), ops_impl=Q35Ops())
     for t in range(2):
         dec.x_in.copy_(xs[t])
