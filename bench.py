@@ -441,7 +441,10 @@ def measure_deltanet_layers(torch, device, hbm_peak: float, steps: int, n_layers
         gbs = nbytes / (t_ms * 1e-3) / 1e9
         out.append({"batch": bsz, "layers": n_layers, "ms": round(t_ms, 4), "gbs": round(gbs, 1),
                     "frac_of_measured_hbm": round(gbs / hbm_peak, 3), "bytes_per_step": nbytes,
-                    "how": "tcgen05 GEMM" if layers[0].use_gemm else "GEMV (RMSNorm fused)"})
+                    "how": "tcgen05 GEMM" if layers[0].use_gemm else "GEMV (RMSNorm fused)",
+                    "us_per_layer": round(t_ms * 1e3 / n_layers, 2),
+                    # the reference's CPU path for the same layer (transformers, float32), beside it
+                    "cpu_reference": cpu_reference_qwen35("linear_attention", bsz)})
         del g, layers
         torch.cuda.empty_cache()
     return out
@@ -481,8 +484,11 @@ def measure_gated_attention(torch, ops, gen, device, hbm_peak: float, steps: int
         reps = max(3, min(200, int(steps * 2e6 / (kv_bytes * n_pool) + 1)))
         t_ms = time_graph(torch, g, reps, 3) / n_pool
         gbs = kv_bytes / (t_ms * 1e-3) / 1e9
-        out.append({"batch": bsz, "ctx": GATED_CTX, "heads": "8q/2kv x 256", "us": round(t_ms * 1e3, 2),
-                    "gbs": round(gbs, 1), "frac_of_measured_hbm": round(gbs / hbm_peak, 3), "pool": n_pool})
+        row = {"batch": bsz, "ctx": GATED_CTX, "heads": "8q/2kv x 256", "us": round(t_ms * 1e3, 2),
+               "gbs": round(gbs, 1), "frac_of_measured_hbm": round(gbs / hbm_peak, 3), "pool": n_pool}
+        if bsz <= 16:  # the reference's CPU path (transformers, float32; a whole layer: projections included)
+            row["cpu_reference"] = cpu_reference_qwen35("full_attention", bsz)
+        out.append(row)
         del g, pool, ws
         torch.cuda.empty_cache()
     return out
@@ -526,6 +532,56 @@ def measure_qwen35_step(torch, device, hbm_peak: float, steps: int) -> list:
     except Exception as e:  # recorded, so the rest of the line stands
         out.append({"error": f"{type(e).__name__}: {str(e)[:300]}"})
     return out
+
+
+def cpu_reference_qwen35(kind: str, bsz: int, ctx: int = GATED_CTX, steps: int = 3) -> dict:
+    """The reference's own CPU path for a config-5 layer: transformers 5.5.0's module
+    (Qwen3_5GatedDeltaNet or Qwen3_5Attention, float32, as reference/from_q4nx.py:140-171
+    builds the model) stepping one decode token with a filled cache, on all host threads.
+    Returns {"us_per_layer", "threads", "sample"} or {"error"}."""
+    try:
+        import torch
+        from transformers.cache_utils import DynamicCache
+        from transformers.models.qwen3_5 import configuration_qwen3_5 as conf
+        from transformers.models.qwen3_5 import modeling_qwen3_5 as mq
+        torch.manual_seed(0)
+        linear = kind == "linear_attention"
+        cfg = conf.Qwen3_5TextConfig(
+            hidden_size=1024, num_hidden_layers=1, layer_types=[kind], linear_num_key_heads=DELTA_KH,
+            linear_num_value_heads=DELTA_VH, linear_key_head_dim=DELTA_D, linear_value_head_dim=DELTA_D,
+            num_attention_heads=GATED_Q, num_key_value_heads=GATED_KV, head_dim=GATED_D,
+            rope_parameters={"rope_type": "default", "rope_theta": 1e7, "partial_rotary_factor": 0.25})
+        cfg._attn_implementation = "eager"
+        cache = DynamicCache(config=cfg)
+        with torch.no_grad():
+            if linear:
+                mod = mq.Qwen3_5GatedDeltaNet(cfg, 0).float().eval()
+                mod(torch.randn(bsz, 2, 1024), cache_params=cache)  # creates the conv / recurrent states
+                run = lambda: mod(torch.randn(bsz, 1, 1024), cache_params=cache)
+            else:
+                mod = mq.Qwen3_5Attention(cfg, 0).float().eval()
+                rope = mq.Qwen3_5TextRotaryEmbedding(cfg)
+                layer = cache.layers[0]
+                layer.lazy_initialization(torch.zeros(bsz, GATED_KV, 1, GATED_D), torch.zeros(bsz, GATED_KV, 1, GATED_D))
+                layer.keys = torch.randn(bsz, GATED_KV, ctx - 1, GATED_D)
+                layer.values = torch.randn(bsz, GATED_KV, ctx - 1, GATED_D)
+                pos = torch.full((bsz, 1), ctx - 1)
+
+                def run():
+                    h = torch.randn(bsz, 1, 1024)
+                    out = mod(h, rope(h, pos), None, past_key_values=cache)
+                    layer.keys, layer.values = layer.keys[:, :, :ctx - 1], layer.values[:, :, :ctx - 1]
+                    return out
+            run()
+            t0 = time.perf_counter()
+            for _ in range(steps):
+                run()
+            dt = (time.perf_counter() - t0) / steps
+        return {"us_per_layer": round(dt * 1e6, 1), "threads": torch.get_num_threads(),
+                "sample": f"transformers {kind} module, float32, batch {bsz}"
+                          + ("" if linear else f", ctx {ctx}") + f", {steps} decode steps"}
+    except Exception as e:
+        return {"error": f"{type(e).__name__}: {str(e)[:200]}"}
 
 
 def run_b200(args, rank: int, world: int) -> dict | None:
