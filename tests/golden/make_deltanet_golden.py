@@ -39,6 +39,7 @@ CASES = [
     ("d32", 2, 1, 2, 32, 3, "all"),        # every tensor, three chained steps
     ("d128", 2, 1, 2, 128, 2, "sample"),   # the kernel's head dim, GQA ratio 2
     ("d128r1", 1, 2, 2, 128, 1, "sample"),  # ratio 1
+    ("d32r4", 1, 1, 4, 32, 2, "all"),      # four v heads per k head
 ]
 SAMPLE_STRIDE = 61  # recurrent-state entries kept for the head-dim-128 cases
 HIDDEN = 64

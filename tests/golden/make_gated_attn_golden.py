@@ -34,6 +34,7 @@ CASES = [
     ("g4", 2, 4, 1, 37, 10000.0, 0.25),
     ("c5", 1, 8, 2, 45, 10000000.0, 0.25),   # config 5's heads: 8 q / 2 kv, head_dim 256
     ("g2full", 1, 2, 1, 20, 10000.0, 1.0),   # rotary over the whole head
+    ("g1", 2, 2, 2, 30, 10000.0, 0.25),       # one q head per kv head
 ]
 
 

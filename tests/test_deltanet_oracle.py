@@ -11,7 +11,7 @@ from oracle import deltanet_oracle as dn
 from oracle.q4nx_oracle import compare
 
 GOLDEN = Path(__file__).resolve().parent / "golden" / "deltanet_golden.npz"
-CASES = ["d32", "d128", "d128r1"]
+CASES = ["d32", "d128", "d128r1", "d32r4"]
 
 
 @pytest.fixture(scope="module")

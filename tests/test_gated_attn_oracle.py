@@ -11,7 +11,7 @@ from oracle import gated_attention_oracle as ga
 from oracle.q4nx_oracle import compare
 
 GOLDEN = Path(__file__).resolve().parent / "golden" / "gated_attn_golden.npz"
-CASES = ["g4", "c5", "g2full"]
+CASES = ["g4", "c5", "g2full", "g1"]
 
 
 @pytest.fixture(scope="module")
