@@ -4,7 +4,7 @@
  * This is the drop-in boundary of the framework: plain pointers, sizes and a
  * CUDA stream passed as `void*`; no torch or CUDA types in any signature.  The
  * Python host layer (llmnputest_b200.npu / .ops) binds it with ctypes; any other
- * host language binds the same symbols.
+ * host language binds the same symbols through its own C FFI.
  *
  * Conventions shared by every entry point:
  *   - All data pointers are DEVICE pointers owned by the caller.  The library
@@ -63,7 +63,8 @@ int b2_set_launch_options(int pdl);
 
 /* Read and clear the device error word (0 = none; the first error wins): 1-4 a
  * bounded wait gave up (1 full-wait, 2 empty-wait, 3 drain, 4 grid barrier), 5 an
- * attention call met a sequence position outside its cache or planned length.
+ * attention call met a sequence position outside its cache or planned length, 6 a
+ * tensor-parallel exchange waited too long for another rank (b2_tp_*).
  * Synchronises `stream`.  Returns B2_OK or B2_ERR_CUDA. */
 int b2_read_device_error(int* code, void* stream);
 
@@ -165,9 +166,11 @@ int b2_gqa_decode(const float* q, const float* k_new, const float* v_new, int ld
  * device.  It has no counterpart in the reference.
  *   - Same arguments and results as b2_gqa_decode, minus the workspace.
  *   - Its scratch is a fixed 2 MiB array inside the library, held by every GPU
- *     that loads the library until the process exits.  A call whose split
- *     partials would need more (b2_gqa_decode_workspace_size() > 2 MiB) returns
- *     B2_ERR_WORKSPACE without launching anything.
+ *     that loads the library until the process exits.  It plans its splits
+ *     exactly as b2_gqa_decode does, so b2_gqa_decode_workspace_size() is its
+ *     scratch need: a call needing more than 2 MiB returns B2_ERR_WORKSPACE
+ *     without launching anything.  (With the default plan, at most one wave of
+ *     resident CTAs, no call on a 148-SM B200 needs more than about 0.65 MiB.)
  *   - The first call on each device looks up the array's device address
  *     (cudaGetSymbolAddress) with that device current; make that first call
  *     before any stream capture on the device.
@@ -179,6 +182,49 @@ int b2_gqa_decode_static(const float* q, const float* k_new, const float* v_new,
                          uint16_t* v_cache, const int32_t* pos, int batch, int n_q_heads, int n_kv_heads,
                          int head_dim, int ctx_max, int max_len, float theta, float scale, uint16_t* out, int ldo,
                          int flags, void* stream);
+
+/* ---- Tensor-parallel exchanges over NVLink peer memory (one process per GPU) ----
+ * The collective seams of tensor-parallel decode (designs/granite_gemv/granite_layer.py
+ * gives the layer; the shards are the q4nx tiles' natural cuts: kv heads, output rows,
+ * K-tiles, vocab rows), as small kernels that store straight into the other GPUs'
+ * memory instead of NCCL calls.  No reference counterpart: the reference runs on one
+ * NPU.
+ *
+ * Peer regions: each rank allocates one with b2_peer_alloc (device memory plus a CUDA
+ * IPC handle of B2_IPC_HANDLE_BYTES bytes), hands the handle to the other ranks (any
+ * host channel), and maps theirs with b2_peer_open.  Plain peer mappings: no multicast
+ * object.  The first 4096 bytes of a region are control words (zeroed by the
+ * allocation); exchanged buffers sit at higher offsets, the same on every rank.
+ * `peers` below is a DEVICE array of `world` pointers: the regions as mapped in the
+ * calling process, peers[rank] being its own.
+ *
+ * Every rank must issue the same exchanges in the same order.  Each exchange waits for
+ * the other ranks' data with a bounded spin (b2_set_peer_timeout_ms, default 2000 ms);
+ * when it runs out the kernel records device error 6 (b2_read_device_error) and
+ * returns without waiting further. */
+#define B2_IPC_HANDLE_BYTES 64
+int b2_peer_alloc(size_t bytes, void** ptr, uint8_t* ipc_handle);
+int b2_peer_free(void* ptr);
+int b2_peer_open(const uint8_t* ipc_handle, void** ptr);
+int b2_peer_close(void* ptr);
+int b2_set_peer_timeout_ms(int ms);
+
+/* All-gather of column blocks: src [rows][cols] (elem_bytes 2 or 4, row stride ld_src
+ * elements) of every rank lands in every rank's region at dst_offset as
+ * [rows][ld_dst] with this rank's block at column rank*cols.  With add_base (fp32
+ * only), the value stored is add_base[r][rank*cols + c] + src[r][c]: add_base is this
+ * rank's copy of a buffer every rank holds identically, so the exchange adds each
+ * rank's block into all copies (the residual stream after a row-sharded projection).
+ * Replaces NCCL all_gather at the attention, O and lm_head seams. */
+int b2_tp_gather(void* const* peers, int world, int rank, const void* src, int rows, int cols, int ld_src,
+                 int elem_bytes, long long dst_offset, int ld_dst, const float* add_base, void* stream);
+
+/* All-reduce (sum) into a replicated fp32 buffer: y[r][c] += sum over ranks of their
+ * src[r][c], added in rank order on every rank so all copies stay bit-identical.  The
+ * partials pass through world * rows * cols floats at slots_offset of every region.
+ * Replaces NCCL all_reduce after the K-sharded down projection. */
+int b2_tp_allreduce(void* const* peers, int world, int rank, const float* src, int rows, int cols, int ld_src,
+                    long long slots_offset, float* y, int ldy, void* stream);
 
 /* RMSNorm y = x * rsqrt(mean(x^2) + eps) * w over rows of n, bf16 out.
  *   x  bf16 (x_is_f32 = 0) or fp32 (x_is_f32 = 1), [batch][ldx];  w bf16 [n]

@@ -36,6 +36,13 @@ SIGNATURES: dict[str, tuple] = {
     "b2_gqa_decode_static": (_i32, [_vp, _vp, _vp, _i32, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _f32,
                                     _f32, _vp, _i32, _i32, _vp]),
     "b2_rmsnorm": (_i32, [_vp, _i32, _i32, _vp, _f32, _i32, _i32, _vp, _i32, _vp]),
+    "b2_peer_alloc": (_i32, [_c.c_size_t, _c.POINTER(_vp), _c.c_char_p]),
+    "b2_peer_free": (_i32, [_vp]),
+    "b2_peer_open": (_i32, [_c.c_char_p, _c.POINTER(_vp)]),
+    "b2_peer_close": (_i32, [_vp]),
+    "b2_set_peer_timeout_ms": (_i32, [_i32]),
+    "b2_tp_gather": (_i32, [_vp, _i32, _i32, _vp, _i32, _i32, _i32, _i32, _c.c_longlong, _i32, _vp, _vp]),
+    "b2_tp_allreduce": (_i32, [_vp, _i32, _i32, _vp, _i32, _i32, _i32, _c.c_longlong, _vp, _i32, _vp]),
     "b2_gated_attn_decode_workspace_size": (_i32, [_i32, _i32, _i32, _i32, _i32, _c.POINTER(_c.c_size_t)]),
     "b2_gated_attn_decode": (_i32, [_vp, _i32, _vp, _vp, _i32, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _i32, _i32, _i32,
                                     _i32, _i32, _i32, _f32, _vp, _i32, _i32, _vp, _c.c_size_t, _vp]),

@@ -25,6 +25,7 @@
 #include "gqa_decode.cuh"
 #include "q4nx_gemv.cuh"
 #include "rmsnorm.cuh"
+#include "tp_exchange.cuh"
 
 namespace {
 
@@ -342,7 +343,7 @@ bool attn_wide(long long n_cta, int split_len, int sms) {
 }
 
 // wave_cap: unclustered launches use at most one wave of resident CTAs (fewer,
-// longer splits); b2_gqa_decode_static plans without it (see there)
+// longer splits); the cap only ever lowers the split count, never the scratch need
 AttnPlan attn_plan(int batch, int hq, int hkv, int head_dim, int max_len, int sms, bool wave_cap) {
   AttnPlan pl;
   const int pairs = batch * hkv;
@@ -396,7 +397,7 @@ int attn_check(int batch, int hq, int hkv, int head_dim, int ctx_max, int max_le
 // host it is only a stand-in); its device address is looked up once per device.
 constexpr size_t kAttnStaticScratchBytes = size_t(2) << 20;
 static __device__ __align__(256) unsigned char g_attn_static_scratch[kAttnStaticScratchBytes];
-void* g_attn_static_ptr[64] = {};
+static void* g_attn_static_ptr[64] = {};
 
 // Device address of the static scratch on the current device (set up on first use).
 int attn_static_scratch(void** out) {
@@ -795,9 +796,10 @@ int b2_gqa_decode_static(const float* q, const float* k_new, const float* v_new,
   if (st != B2_OK) return st;
   st = attn_check(batch, n_q_heads, n_kv_heads, head_dim, ctx_max, max_len);
   if (st != B2_OK) return st;
-  // planned as specified for this entry point (no one-wave cap), so its scratch need
-  // and the size limit below stay what its documentation states
-  const AttnPlan pl = attn_plan(batch, n_q_heads, n_kv_heads, head_dim, max_len, di.sms, false);
+  // the same plan as b2_gqa_decode, so b2_gqa_decode_workspace_size() is exactly
+  // this call's scratch need and the limit below can be checked in advance
+  const bool wave_cap = tuning().attn_wave != 0;
+  const AttnPlan pl = attn_plan(batch, n_q_heads, n_kv_heads, head_dim, max_len, di.sms, wave_cap);
   if (pl.ws_bytes > kAttnStaticScratchBytes)
     return fail(B2_ERR_WORKSPACE,
                 "this call needs %zu bytes of scratch, more than the %zu-byte static scratch of "
@@ -807,7 +809,150 @@ int b2_gqa_decode_static(const float* q, const float* k_new, const float* v_new,
   st = attn_static_scratch(&ws);
   if (st != B2_OK) return st;
   return gqa_decode_impl(q, k_new, v_new, ld_new, k_cache, v_cache, pos, batch, n_q_heads, n_kv_heads, head_dim,
-                         ctx_max, max_len, theta, scale, out, ldo, ws, kAttnStaticScratchBytes, flags, stream, false);
+                         ctx_max, max_len, theta, scale, out, ldo, ws, kAttnStaticScratchBytes, flags, stream,
+                         wave_cap);
+}
+
+// ------------------------------------------------- tensor-parallel exchanges
+namespace {
+unsigned long long g_peer_timeout_ns = B2_WAIT_TIMEOUT_NS;
+
+int xchg_check(void* const* peers, int world, int rank, const void* src, int rows, int cols, int ld_src,
+               long long dst_offset) {
+  if (!peers || !src) return fail(B2_ERR_ARG, "null pointer argument");
+  if (world < 1 || world > b2::kPeerMaxRanks || rank < 0 || rank >= world)
+    return fail(B2_ERR_ARG, "rank %d of world %d", rank, world);
+  if (rows < 1 || cols < 1 || ld_src < cols) return fail(B2_ERR_ARG, "bad block %dx%d (ld %d)", rows, cols, ld_src);
+  if (dst_offset < b2::kPeerCtlBytes) return fail(B2_ERR_ARG, "dst_offset inside the control words");
+  return B2_OK;
+}
+
+int xchg_chunks(long long bytes_per_peer, int rows) {
+  const long long c = (bytes_per_peer + 16383) / 16384;  // ~16 KB per CTA (to every rank)
+  return static_cast<int>(std::max(1LL, std::min<long long>({c, 64LL, static_cast<long long>(rows)})));
+}
+
+int xchg_launch(const void* kernel, const b2::XchgParams& p, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.chunks, 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_pdl ? 1 : 0;
+  void* args[] = {const_cast<b2::XchgParams*>(&p)};
+  cudaError_t e = cudaLaunchKernelExC(&cfg, kernel, args);
+  if (e != cudaSuccess) return cuda_fail(e, "exchange launch");
+  return B2_OK;
+}
+}  // namespace
+
+int b2_peer_alloc(size_t bytes, void** ptr, uint8_t* ipc_handle) {
+  DevInfo di;
+  int st = device_info(&di);
+  if (st != B2_OK) return st;
+  if (!ptr || !ipc_handle || bytes < static_cast<size_t>(b2::kPeerCtlBytes))
+    return fail(B2_ERR_ARG, "peer region needs >= %d bytes and out pointers", b2::kPeerCtlBytes);
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(peer region)");
+  e = cudaMemset(p, 0, b2::kPeerCtlBytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "peer region set-up");
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == B2_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(ipc_handle, &h, sizeof(h));
+  *ptr = p;
+  return B2_OK;
+}
+
+int b2_peer_free(void* ptr) {
+  if (!ptr) return B2_OK;
+  cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? B2_OK : cuda_fail(e, "cudaFree(peer region)");
+}
+
+int b2_peer_open(const uint8_t* ipc_handle, void** ptr) {
+  if (!ipc_handle || !ptr) return fail(B2_ERR_ARG, "null pointer argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? B2_OK : cuda_fail(e, "cudaIpcOpenMemHandle");
+}
+
+int b2_peer_close(void* ptr) {
+  if (!ptr) return B2_OK;
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? B2_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+int b2_set_peer_timeout_ms(int ms) {
+  if (ms < 1) return fail(B2_ERR_ARG, "timeout must be >= 1 ms");
+  g_peer_timeout_ns = static_cast<unsigned long long>(ms) * 1000000ull;
+  return B2_OK;
+}
+
+int b2_tp_gather(void* const* peers, int world, int rank, const void* src, int rows, int cols, int ld_src,
+                 int elem_bytes, long long dst_offset, int ld_dst, const float* add_base, void* stream) {
+  DevInfo di;
+  int st = device_info(&di);
+  if (st != B2_OK) return st;
+  st = xchg_check(peers, world, rank, src, rows, cols, ld_src, dst_offset);
+  if (st != B2_OK) return st;
+  if (elem_bytes != 2 && elem_bytes != 4) return fail(B2_ERR_ARG, "elem_bytes %d (2 or 4)", elem_bytes);
+  if (add_base && elem_bytes != 4) return fail(B2_ERR_ARG, "add_base needs fp32 elements");
+  if (ld_dst < cols * world) return fail(B2_ERR_ARG, "ld_dst %d < cols*world %d", ld_dst, cols * world);
+  if (dst_offset % elem_bytes) return fail(B2_ERR_ALIGN, "dst_offset misaligned");
+  b2::XchgParams p = {};
+  p.peers = peers;
+  p.world = world;
+  p.rank = rank;
+  p.src = src;
+  p.rows = rows;
+  p.cols = cols;
+  p.ld_src = ld_src;
+  p.elem_bytes = elem_bytes;
+  p.dst_offset = dst_offset;
+  p.ld_dst = ld_dst;
+  p.add_base = add_base;
+  p.chunks = xchg_chunks(static_cast<long long>(rows) * cols * elem_bytes, rows);
+  p.timeout_ns = g_peer_timeout_ns;
+  const void* k = elem_bytes == 2 ? reinterpret_cast<const void*>(b2::tp_gather_kernel<uint16_t>)
+                                  : reinterpret_cast<const void*>(b2::tp_gather_kernel<uint32_t>);
+  return xchg_launch(k, p, static_cast<cudaStream_t>(stream));
+}
+
+int b2_tp_allreduce(void* const* peers, int world, int rank, const float* src, int rows, int cols, int ld_src,
+                    long long slots_offset, float* y, int ldy, void* stream) {
+  DevInfo di;
+  int st = device_info(&di);
+  if (st != B2_OK) return st;
+  st = xchg_check(peers, world, rank, src, rows, cols, ld_src, slots_offset);
+  if (st != B2_OK) return st;
+  if (!y || ldy < cols) return fail(B2_ERR_ARG, "bad output (ldy %d < cols %d)", ldy, cols);
+  if (slots_offset % 16) return fail(B2_ERR_ALIGN, "slots_offset must be 16-byte aligned");
+  b2::XchgParams p = {};
+  p.peers = peers;
+  p.world = world;
+  p.rank = rank;
+  p.src = src;
+  p.rows = rows;
+  p.cols = cols;
+  p.ld_src = ld_src;
+  p.elem_bytes = 4;
+  p.dst_offset = slots_offset;
+  p.ld_dst = cols;
+  p.y = y;
+  p.ldy = ldy;
+  p.chunks = xchg_chunks(static_cast<long long>(rows) * cols * 4, rows);
+  p.timeout_ns = g_peer_timeout_ns;
+  return xchg_launch(reinterpret_cast<const void*>(b2::tp_allreduce_kernel), p, static_cast<cudaStream_t>(stream));
 }
 
 int b2_rmsnorm(const void* x, int x_is_f32, int ldx, const uint16_t* w, float eps, int batch, int n, uint16_t* y,

@@ -130,15 +130,35 @@ def shard_weights(full: dict, plan: ShardPlan) -> dict:
 
 
 class TPDecoder:
-    """Tensor-parallel decode step on this rank's shard; collectives on the default process group."""
+    """Tensor-parallel decode step on this rank's shard.
 
-    def __init__(self, cfg, batch: int, ctx_max: int, shard: dict, plan: ShardPlan, device=None, ops=None):
+    comm selects how the ranks meet at the seams of a layer:
+      "peer"        (GPU default) the exchanges of peer.py: the attention heads are
+                    gathered into every rank's copy of the attention output, each rank
+                    adds its O rows into every rank's copy of the residual stream, and
+                    the down projection's partials are all-reduced into it (in rank order,
+                    so every copy is bit-identical): three small kernels per layer that
+                    store straight into the other GPUs' memory, captured in the step's
+                    CUDA graph.
+      "collective"  torch.distributed all_gather / all_reduce (NCCL on GPUs, gloo on CPU).
+    `xchg` (comm="peer"): an exchange object with .buffers, .gather(src, name, add_base)
+    and .allreduce_add(src, name, y); built from peer.PeerRegion when not given.
+    Batches of gemm_min_batch and more run the projections on the tcgen05 GEMM, as
+    decode.Q4Decoder does."""
+
+    def __init__(self, cfg, batch: int, ctx_max: int, shard: dict, plan: ShardPlan, device=None, ops=None,
+                 comm: str | None = None, xchg=None, gemm_min_batch: int = 9):
         if ops is None:
             from . import ops  # the GPU path; tests of the host logic may pass another implementation
         self.ops = ops
         self.cfg, self.plan, self.batch, self.ctx_max = cfg, plan, batch, ctx_max
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         dev, c, p, W = self.device, cfg, plan, plan.world
+        if comm is None:
+            comm = "peer" if (dev.type == "cuda" and W > 1) else "collective"
+        if comm not in ("peer", "collective"):
+            raise ValueError(f"unknown comm {comm!r}")
+        self.comm = comm
         self.w = shard
         self.kt_h, self.kt_q, self.kt_i = c.hidden // TILE_K, c.n_heads * c.head_dim // TILE_K, c.intermediate // TILE_K
         self.kt_i_local = self.kt_i // W
@@ -151,63 +171,139 @@ class TPDecoder:
         self.k_cache = [torch.zeros(kv_shape, dtype=torch.bfloat16, device=dev) for _ in range(c.n_layers)]
         self.v_cache = [torch.zeros(kv_shape, dtype=torch.bfloat16, device=dev) for _ in range(c.n_layers)]
         self.x_in = torch.zeros(batch, c.hidden, dtype=torch.float32, device=dev)
-        self.resid = torch.zeros(batch, c.hidden, dtype=torch.float32, device=dev)
         self.xn = torch.zeros(batch, c.hidden, dtype=torch.bfloat16, device=dev)
         self.qkv = torch.zeros(batch, self.nt_qkv_local * TILE_ROWS, dtype=torch.float32, device=dev)
         self.attn_local = torch.zeros(batch, p.q_local * d, dtype=torch.bfloat16, device=dev)
-        # gathered buffers are [W*B, n] (rank-major), viewed as [W, B, n] when merged
-        self.attn_all = torch.zeros(W * batch, p.q_local * d, dtype=torch.bfloat16, device=dev)
-        self.attn = torch.zeros(batch, c.n_heads * d, dtype=torch.bfloat16, device=dev)
         self.o_local = torch.zeros(batch, c.hidden // W, dtype=torch.float32, device=dev)
-        self.o_all = torch.zeros(W * batch, c.hidden // W, dtype=torch.float32, device=dev)
         self.h = torch.zeros(batch, c.intermediate // W, dtype=torch.bfloat16, device=dev)
         self.down = torch.zeros(batch, c.hidden, dtype=torch.float32, device=dev)
         self.logits_local = torch.zeros(batch, c.vocab // W, dtype=torch.float32, device=dev)
-        self.logits_all = torch.zeros(W * batch, c.vocab // W, dtype=torch.float32, device=dev)
-        self.logits = torch.zeros(batch, c.vocab, dtype=torch.float32, device=dev)
         self.pos = torch.zeros(batch, dtype=torch.int32, device=dev)
+        if comm == "peer":
+            if xchg is None:
+                from .peer import PeerExchange
+                xchg = PeerExchange([("attn", (batch, c.n_heads * d), torch.bfloat16),
+                                     ("resid", (batch, c.hidden), torch.float32),
+                                     ("slots", (W, batch, c.hidden), torch.float32),
+                                     ("logits", (batch, c.vocab), torch.float32)], device=dev)
+            self.xchg = xchg
+            self.attn = xchg.buffers["attn"]
+            self.resid = xchg.buffers["resid"]
+            self.logits = xchg.buffers["logits"]
+        else:
+            self.xchg = None
+            # gathered buffers are [W*B, n] (rank-major), viewed as [W, B, n] when merged
+            self.attn_all = torch.zeros(W * batch, p.q_local * d, dtype=torch.bfloat16, device=dev)
+            self.attn = torch.zeros(batch, c.n_heads * d, dtype=torch.bfloat16, device=dev)
+            self.o_all = torch.zeros(W * batch, c.hidden // W, dtype=torch.float32, device=dev)
+            self.logits_all = torch.zeros(W * batch, c.vocab // W, dtype=torch.float32, device=dev)
+            self.resid = torch.zeros(batch, c.hidden, dtype=torch.float32, device=dev)
+            self.logits = torch.zeros(batch, c.vocab, dtype=torch.float32, device=dev)
         ws = ops.gqa_decode_workspace_bytes(batch, p.q_local, p.kv_local, d, ctx_max)
         self.attn_ws = torch.empty(max(ws, 1), dtype=torch.uint8, device=dev)
+        self.use_gemm = batch >= gemm_min_batch
+        if self.use_gemm:
+            nbytes = ops.gemm_workspace_bytes(batch, max(self.kt_h, self.kt_q, self.kt_i_local))
+            self.gemm_ws_raw = torch.empty(nbytes + 256, dtype=torch.uint8, device=dev)
+            off = (256 - self.gemm_ws_raw.data_ptr() % 256) % 256
+            self.gemm_ws = self.gemm_ws_raw[off:off + nbytes]
 
+    def close(self) -> None:
+        """Release the peer mappings (every rank, after its last step)."""
+        if self.xchg is not None and hasattr(self.xchg, "close"):
+            self.xchg.close()
+        self.xchg = None
+
+    # ---------------------------------------------------------------- seams
+    def _gather_heads(self) -> torch.Tensor:
+        W, B, qd = self.plan.world, self.batch, self.attn_local.shape[1]
+        if W == 1:
+            return self.attn_local
+        if self.comm == "peer":
+            self.xchg.gather(self.attn_local, "attn")
+        else:
+            dist.all_gather_into_tensor(self.attn_all, self.attn_local)
+            # rank-major [W][B][q_local*D] -> [B][Hq*D] (head order = rank order)
+            self.attn.view(B, W, qd).copy_(self.attn_all.view(W, B, qd).permute(1, 0, 2))
+        return self.attn
+
+    def _add_o_rows(self) -> None:
+        W, B = self.plan.world, self.batch
+        if self.comm == "peer":
+            self.xchg.gather(self.o_local, "resid", add_base=self.resid)
+        elif W > 1:
+            dist.all_gather_into_tensor(self.o_all, self.o_local)
+            self.resid.view(B, W, -1).add_(self.o_all.view(W, B, -1).permute(1, 0, 2))
+        else:
+            self.resid.add_(self.o_local)
+
+    def _reduce_down(self) -> None:
+        if self.comm == "peer":
+            self.xchg.allreduce_add(self.down, "slots", self.resid)
+        else:
+            if self.plan.world > 1:
+                dist.all_reduce(self.down)
+            self.resid.add_(self.down)
+
+    def _gather_logits(self) -> None:
+        W, B = self.plan.world, self.batch
+        if self.comm == "peer":
+            self.xchg.gather(self.logits_local, "logits")
+        elif W > 1:
+            dist.all_gather_into_tensor(self.logits_all, self.logits_local)
+            self.logits.view(B, W, -1).copy_(self.logits_all.view(W, B, -1).permute(1, 0, 2))
+        else:
+            self.logits.copy_(self.logits_local)
+
+    # ---------------------------------------------------------------- step
     def step(self) -> torch.Tensor:
-        ops, c, p, W = self.ops, self.cfg, self.plan, self.plan.world
+        ops, c, p = self.ops, self.cfg, self.plan
         d = c.head_dim
         qd, kd = p.q_local * d, p.kv_local * d
+        ws = self.gemm_ws if self.use_gemm else None
         self.resid.copy_(self.x_in)
         for li, L in enumerate(self.w["layers"]):
-            ops.gemv_rmsnorm(L["qkv"], self.nt_qkv_local, self.kt_h, self.resid, L["attn_norm"], c.rms_eps,
-                             out=self.qkv, prefetch=True)
+            if self.use_gemm:
+                ops.rmsnorm(self.resid, L["attn_norm"], c.rms_eps, out=self.xn)
+                ops.q4_gemm(L["qkv"], self.nt_qkv_local, self.kt_h, self.xn, out=self.qkv, workspace=ws)
+            else:
+                ops.gemv_rmsnorm(L["qkv"], self.nt_qkv_local, self.kt_h, self.resid, L["attn_norm"], c.rms_eps,
+                                 out=self.qkv, prefetch=True)
             ops.gqa_decode(self.qkv[:, :qd], self.qkv[:, qd:qd + kd], self.qkv[:, qd + kd:], self.k_cache[li],
                            self.v_cache[li], self.pos, n_q_heads=p.q_local, n_kv_heads=p.kv_local,
                            theta=c.rope_theta, scale=d ** -0.5, max_len=self.ctx_max, out=self.attn_local,
                            workspace=self.attn_ws, prefetch_kv=True)
-            if W > 1:
-                dist.all_gather_into_tensor(self.attn_all, self.attn_local)
-                # rank-major [W][B][q_local*D] -> [B][Hq*D] (head order = rank order)
-                self.attn.view(self.batch, W, qd).copy_(self.attn_all.view(W, self.batch, qd).permute(1, 0, 2))
-                a = self.attn
+            a = self._gather_heads()
+            if self.use_gemm:
+                ops.q4_gemm(L["o"], self.nt_o_local, self.kt_q, a, out=self.o_local, workspace=ws)
             else:
-                a = self.attn_local
-            ops.q4_gemv(L["o"], self.nt_o_local, self.kt_q, a, out=self.o_local, prefetch=True)
-            if W > 1:
-                dist.all_gather_into_tensor(self.o_all, self.o_local)
-                self.resid.view(self.batch, W, -1).add_(self.o_all.view(W, self.batch, -1).permute(1, 0, 2))
+                ops.q4_gemv(L["o"], self.nt_o_local, self.kt_q, a, out=self.o_local, prefetch=True)
+            self._add_o_rows()
+            if self.use_gemm:
+                ops.rmsnorm(self.resid, L["mlp_norm"], c.rms_eps, out=self.xn)
+                ops.q4_swiglu_gemm(L["gate"], L["up"], self.nt_i_local, self.kt_h, self.xn, out=self.h, workspace=ws)
+                ops.q4_gemm(L["down"], c.hidden // TILE_ROWS, self.kt_i_local, self.h, out=self.down, workspace=ws)
             else:
-                self.resid.add_(self.o_local)
-            ops.swiglu_gemv_rmsnorm(L["gate"], L["up"], self.nt_i_local, self.kt_h, self.resid, L["mlp_norm"],
-                                    c.rms_eps, out=self.h, prefetch=True)
-            ops.q4_gemv(L["down"], c.hidden // TILE_ROWS, self.kt_i_local, self.h, out=self.down, prefetch=True)
-            if W > 1:
-                dist.all_reduce(self.down)
-            self.resid.add_(self.down)
+                ops.swiglu_gemv_rmsnorm(L["gate"], L["up"], self.nt_i_local, self.kt_h, self.resid, L["mlp_norm"],
+                                        c.rms_eps, out=self.h, prefetch=True)
+                ops.q4_gemv(L["down"], c.hidden // TILE_ROWS, self.kt_i_local, self.h, out=self.down, prefetch=True)
+            self._reduce_down()
         ops.gemv_rmsnorm(self.w["lm_head"], self.nt_v_local, self.kt_h, self.resid, self.w["final_norm"], c.rms_eps,
                          out=self.logits_local, prefetch=True, q8=True)
-        if W > 1:
-            dist.all_gather_into_tensor(self.logits_all, self.logits_local)
-            self.logits.view(self.batch, W, -1).copy_(self.logits_all.view(W, self.batch, -1).permute(1, 0, 2))
-        else:
-            self.logits.copy_(self.logits_local)
+        self._gather_logits()
         return self.logits
+
+    def capture(self) -> torch.cuda.CUDAGraph:
+        """The step as one CUDA graph (warm once outside the capture first)."""
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            self.step()
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.step()
+        return g
 
 
 # ------------------------------------------------------------------ Qwen3.5 linear attention

@@ -125,14 +125,53 @@ def _free_port():
     return p
 
 
-def _run_rank(rank, world, port, x, pos, ctx, result_path):
+class GlooExchange:
+    """The peer exchanges' semantics (llmnputest_b200.peer) over gloo, for the host logic of
+    TPDecoder(comm="peer"): gather places every rank's block at column rank*cols of every
+    rank's buffer (adding it when add_base is given), allreduce_add sums the partials in
+    rank order into y."""
+
+    def __init__(self, layout):
+        self.buffers = {name: torch.zeros(shape, dtype=dtype) for name, shape, dtype in layout}
+
+    def gather(self, src, name, add_base=None):
+        w = dist.get_world_size()
+        parts = [torch.empty(src.shape, dtype=torch.float32) for _ in range(w)]
+        dist.all_gather(parts, src.float().contiguous())
+        dst, cols = self.buffers[name], src.shape[1]
+        for r, part in enumerate(parts):
+            blk = dst[:, r * cols:(r + 1) * cols]
+            if add_base is not None:
+                assert add_base.data_ptr() == dst.data_ptr()  # the replicated copy itself
+                blk.add_(part.to(dst.dtype))
+            else:
+                blk.copy_(part.to(dst.dtype))
+
+    def allreduce_add(self, src, name, y):
+        w = dist.get_world_size()
+        parts = [torch.empty_like(src) for _ in range(w)]
+        dist.all_gather(parts, src.contiguous())
+        total = parts[0].clone()
+        for part in parts[1:]:
+            total += part
+        y += total
+
+
+def _run_rank(rank, world, port, x, pos, ctx, result_path, comm="collective"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         W = full_weights(CFG)
         plan = ShardPlan(CFG.n_heads, CFG.n_kv_heads, CFG.head_dim, CFG.hidden, CFG.intermediate, CFG.vocab,
                          world, rank)
-        dec = TPDecoder(CFG, x.shape[0], ctx, shard_weights(W, plan), plan, device="cpu", ops=OracleOps())
+        xchg = None
+        if comm == "peer":
+            b, d = x.shape[1], CFG.head_dim
+            xchg = GlooExchange([("attn", (b, CFG.n_heads * d), torch.bfloat16), ("resid", (b, CFG.hidden), torch.float32),
+                                 ("slots", (world, b, CFG.hidden), torch.float32),
+                                 ("logits", (b, CFG.vocab), torch.float32)])
+        dec = TPDecoder(CFG, x.shape[1], ctx, shard_weights(W, plan), plan, device="cpu", ops=OracleOps(), comm=comm,
+                        xchg=xchg)
         for step in range(2):
             dec.x_in.copy_(x[step])
             dec.pos.copy_(pos + step)
@@ -143,7 +182,8 @@ def _run_rank(rank, world, port, x, pos, ctx, result_path):
         dist.destroy_process_group()
 
 
-def test_tp_step_gloo_matches_single_rank(tmp_path):
+@pytest.mark.parametrize("comm", ["collective", "peer"])
+def test_tp_step_gloo_matches_single_rank(tmp_path, comm):
     rng = np.random.default_rng(5)
     bsz, ctx = 2, 16
     x = torch.from_numpy(rng.standard_normal((2, bsz, CFG.hidden)).astype(np.float32))
@@ -153,7 +193,8 @@ def test_tp_step_gloo_matches_single_rank(tmp_path):
     ctx_mp = mp.get_context("spawn")
     for world, path in ((1, out1), (2, out2)):
         port = _free_port()
-        procs = [ctx_mp.Process(target=_run_rank, args=(r, world, port, x, pos, ctx, str(path))) for r in range(world)]
+        procs = [ctx_mp.Process(target=_run_rank, args=(r, world, port, x, pos, ctx, str(path), comm))
+                 for r in range(world)]
         for p in procs:
             p.start()
         for p in procs:
