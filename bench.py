@@ -1,19 +1,28 @@
 """Benchmark of the decode hot path on B200 (one JSON line on rank 0).
 
-Workload (the config the metric is quoted on): the q4nx
-W4A16 GEMV sweep over a dense GQA 3B decoder's projection shapes -- QKV
-2560->3584, O 2560->2560, gate+up 2560->16384, down 8192->2560 -- for all 40
-layers, batch 1.  One step = the 160 GEMVs of one decode step's weight stream
-(1.966 GB, larger than L2), issued in decode order from one CUDA graph.
-Synthetic seeded weights with the BASELINE distributions (codes uniform 0..15,
-d = |N(0,.02)|, m = -|N(0,.02)|), x ~ N(0,1) bf16.
+Value (the metric's "decode tokens/s at 1/2/4/8 B200"): one
+full random-init decode step of the dense GQA 3B -- 40 layers of RMSNorm, q4nx QKV,
+RoPE + GQA flash-decode, q4nx O, RMSNorm + fused SwiGLU gate/up, q4nx down; final
+RMSNorm and q8 lm_head -- at batch 32 (--batch) and context 4096, one CUDA graph per
+step, tensor-parallel over the ranks at N > 1 (kv heads, O rows, FFN rows / down
+K-tiles, vocab rows; the seams are peer-memory exchanges over NVLink).  Strong
+scaling: the same step, split over more GPUs.  tokens/s = batch / step time (max over
+ranks).  `roofline` is the step's dominant kernel, timed alone on the step's own
+buffers; `e2e` is the same step with its inputs copied in from pinned host memory and
+its logits copied out, every step.
+
+Extra keys: the GEMV sweep (the 160 q4nx GEMVs of a step's weight
+stream, batch 1 and 8, GB/s against HBM), the q8 lm_head GEMV, GQA
+flash-decode, the decode step at batch 1 and 8, config 5's kernels and
+step, and the CPU baselines of configs 1-4 timed on this host; at N > 1 the tensor-
+parallel parity checks (config 4 and config 5 against one GPU) and config 5's
+tensor-parallel step.  Synthetic seeded data with the BASELINE distributions.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
-N > 1 (torchrun): every rank streams its own full sweep (weak scaling, no
-data-path collective); time = max over ranks; value = all ranks' bytes / time.
-`--impl reference` times the reference's own CPU GEMV (designs/granite_gemv/
-cpu_baseline.cpp, compiled unmodified into oracle/_ref/) on this host's cores.
+`--impl reference` times config 4's step composed from the reference's own CPU parts
+(its cpu_baseline.cpp GEMV, compiled unmodified into oracle/_ref/, its attention oracle,
+its --cpu torch lm_head) on this host's cores.
 """
 
 from __future__ import annotations
@@ -36,7 +45,7 @@ METRIC = "q4/q8 GEMV HBM GB/s (% of peak); decode tokens/s at 1/2/4/8 B200"
 SHAPES = [("qkv", 112, 10), ("o", 80, 10), ("gate_up", 512, 10), ("down", 80, 32)]  # (tile-rows, K-tiles)
 Q4_TILE, Q8_TILE = 5120, 8704
 # dram__bytes_read.sum + dram__bytes_write.sum over tile bytes for the GEMV launches
-# that stream from DRAM (ncu capture summarised in profiles/q4nx_gemv_b1_one_layer.md)
+# that stream from DRAM (one ncu capture of a layer's four GEMVs)
 GEMV_DRAM_RATIO = 1.003
 LAYERS = 40
 
@@ -170,6 +179,111 @@ def run_reference_gemv(iters: int, layers: int = 8) -> dict:
                        else "one 80x10-tile O projection, numpy oracle, 5 s")}
 
 
+def cpu_lm_head(n_t: int = 7760, k_t: int = 4, seconds: float = 4.0) -> dict:
+    """Config 1 (q8 lm_head, batch 1) on the host cores, two ways:
+    numpy   the restatement of lm_head.reference (designs/lm_head/lm_head.py:129-144: chunked
+            float32 dequant, then a float32 matmul) over the whole head, once;
+    torch   the reference's --cpu path: torch bf16 F.linear on the dequantised weight
+            (chat.py:26-28, reference/npu.py:138-140) on all threads, the dequant not timed.
+    GB/s against the head's algorithmic bytes (tiles + x + y)."""
+    import numpy as np
+    import torch
+    from oracle import q4nx_oracle as orc
+    rng = np.random.default_rng(77)
+    w = orc.synth_q8_tiles(rng, n_t * k_t)
+    x = orc.synth_bf16(rng, k_t * 256)
+    nbytes = w.nbytes + k_t * 256 * 2 + n_t * 32 * 4
+    t0 = time.perf_counter()
+    orc.gemv_q8(w, x, n_t, k_t)
+    t_np = time.perf_counter() - t0
+    wd = torch.from_numpy(orc.q8_matrix(w, n_t, k_t)).to(torch.bfloat16)
+    xt = torch.from_numpy(x.astype(np.float32)).to(torch.bfloat16)[None, :]
+    torch.nn.functional.linear(xt, wd)
+    n, t1 = 0, time.perf_counter()
+    while time.perf_counter() - t1 < seconds:
+        torch.nn.functional.linear(xt, wd)
+        n += 1
+    t_t = (time.perf_counter() - t1) / n
+    return {"numpy_ms": round(t_np * 1e3, 1), "numpy_gbs": round(nbytes / t_np / 1e9, 2),
+            "torch_bf16_ms": round(t_t * 1e3, 2), "torch_bf16_gbs": round(nbytes / t_t / 1e9, 2),
+            "threads": torch.get_num_threads(), "cores": os.cpu_count(),
+            "sample": f"{n_t * 32}x{k_t * 256} q8 head, batch 1; numpy once, torch {n} calls"}
+
+
+def cpu_attention(bsz: int, ctx: int, hq: int = 40, hkv: int = 8, d: int = 64, seconds: float = 2.0) -> dict:
+    """Config 3 on the host cores: the reference's attention oracle (designs/granite_gemv/
+    granite_attention.py:163-167: scores, softmax, weighted sum) vectorised over sequences and
+    kv heads in float32 numpy, and torch's CPU scaled_dot_product_attention (float32, GQA), one
+    new query token per sequence over ctx cached positions.  GB/s against the bf16 K/V bytes
+    the GPU kernel reads (B*ctx*Hkv*D*2*2)."""
+    import numpy as np
+    import torch
+    rng = np.random.default_rng(ctx + bsz)
+    grp = hq // hkv
+    q = rng.standard_normal((bsz, hkv, grp, d), dtype=np.float32)
+    k = rng.standard_normal((bsz, hkv, ctx, d), dtype=np.float32)
+    v = rng.standard_normal((bsz, hkv, ctx, d), dtype=np.float32)
+
+    def numpy_attn():
+        s = (q @ k.transpose(0, 1, 3, 2)) * np.float32(d ** -0.5)
+        p = np.exp(s - s.max(axis=-1, keepdims=True))
+        return (p / p.sum(axis=-1, keepdims=True)) @ v
+
+    def timed(fn):
+        fn()
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds or n < 2:
+            fn()
+            n += 1
+        return (time.perf_counter() - t0) / n
+
+    t_np = timed(numpy_attn)
+    qt = torch.from_numpy(q.reshape(bsz, hq, 1, d))
+    kt, vt = torch.from_numpy(k), torch.from_numpy(v)
+    t_sdpa = timed(lambda: torch.nn.functional.scaled_dot_product_attention(qt, kt, vt, enable_gqa=True))
+    nbytes = bsz * ctx * hkv * d * 2 * 2
+    return {"batch": bsz, "ctx": ctx, "numpy_ms": round(t_np * 1e3, 3), "numpy_gbs": round(nbytes / t_np / 1e9, 2),
+            "sdpa_ms": round(t_sdpa * 1e3, 3), "sdpa_gbs": round(nbytes / t_sdpa / 1e9, 2),
+            "threads": torch.get_num_threads(), "cores": os.cpu_count()}
+
+
+def cpu_decode_step(bsz: int, ctx: int, gemv: dict | None = None) -> dict:
+    """Config 4's decode step on the host cores, composed from the reference's CPU parts as the
+    layer runs them (designs/granite_gemv/granite_layer.py:54-59), one layer timed and counted
+    40 times:
+      projections  the reference's own cpu_baseline.cpp GEMV (oracle/_ref, its batch-1 kernel run
+                   once per token) at the GB/s it reaches on the four projection shapes;
+      attention    the reference's attention oracle, vectorised float32 numpy, at (bsz, ctx);
+      lm_head      the reference's --cpu path, torch bf16 F.linear over all tokens at once
+                   (chat.py:26-28), the 100352 x 2560 head;
+    RMSNorm, RoPE and SwiGLU add < 1 % and are left out.  Returns tok/s and the parts."""
+    import numpy as np
+    import torch
+    from llmnputest_b200.decode import GRANITE_3B as cfg
+    gemv = gemv or run_reference_gemv(iters=10, layers=2)
+    wb = cfg.weight_bytes()
+    t_proj = bsz * wb["per_layer"] / (gemv["gbs"] * 1e9)
+    att = cpu_attention(bsz, ctx, seconds=1.0)
+    t_att = att["numpy_ms"] * 1e-3
+    rng = np.random.default_rng(5)
+    wd = torch.from_numpy(rng.standard_normal((cfg.vocab, cfg.hidden), dtype=np.float32)).to(torch.bfloat16)
+    xt = torch.from_numpy(rng.standard_normal((bsz, cfg.hidden), dtype=np.float32)).to(torch.bfloat16)
+    torch.nn.functional.linear(xt, wd)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < 1.0 or n < 2:
+        torch.nn.functional.linear(xt, wd)
+        n += 1
+    t_lm = (time.perf_counter() - t0) / n
+    step = cfg.n_layers * (t_proj + t_att) + t_lm
+    return {"tok_s": round(bsz / step, 3), "ms_per_step": round(step * 1e3, 1), "batch": bsz, "ctx": ctx,
+            "cores": gemv["cores"], "kind": gemv["kind"],
+            "parts_ms": {"projections_per_layer": round(t_proj * 1e3, 2), "attention_per_layer": round(t_att * 1e3, 2),
+                         "lm_head": round(t_lm * 1e3, 2)},
+            "sample": f"one layer's parts timed, x {cfg.n_layers} layers + lm_head; projections: {gemv['sample']} "
+                      f"at {gemv['gbs']:.1f} GB/s, once per token; attention: numpy float32 at batch {bsz}, ctx {ctx}; "
+                      "lm_head: torch bf16 F.linear"}
+
+
 # --------------------------------------------------------------------- B200
 def make_q4_tiles(torch, n_tiles: int, gen, device):
     w = torch.randint(0, 256, (n_tiles, Q4_TILE), dtype=torch.uint8, device=device, generator=gen)
@@ -262,67 +376,389 @@ def measure_tc_gemm(torch, ops, gen, device, tensor_peak: float, steps: int) -> 
     return out
 
 
-def measure_decode(torch, world: int, rank: int, batch: int, ctx: int, steps: int, warmup: int,
-                   program: bool = False) -> dict:
-    """Config 4: the full 40-layer decode step at `batch` tokens, context `ctx`, TP over `world` ranks.
+def graph_kernel_nodes(g) -> int | None:
+    """Kernel nodes in a CUDA graph captured with keep_graph=True (cuda-python), else None."""
+    try:
+        from cuda.bindings import runtime as rt
+        h = rt.cudaGraph_t(init_value=g.raw_cuda_graph())
+        err, _, n = rt.cudaGraphGetNodes(h, 0)
+        err, nodes, n = rt.cudaGraphGetNodes(h, n)
+        kern = rt.cudaGraphNodeType.cudaGraphNodeTypeKernel
+        return sum(1 for nd in nodes if rt.cudaGraphNodeGetType(nd)[1] == kern)
+    except Exception:
+        return None
 
-    program=True (single GPU, batch <= 8): the persistent decode program + lm_head launch."""
-    import torch.distributed as dist
+
+def build_decoder(torch, world: int, rank: int, batch: int, ctx: int, seed: int = 11, cfg=None):
+    """Config 4's decoder on this rank: decode.Q4Decoder on one GPU, else tp.TPDecoder on this
+    rank's shard (every rank draws the same seeded full weights, then keeps its shard), with
+    the peer exchanges."""
     from llmnputest_b200.decode import GRANITE_3B, Q4Decoder
     from llmnputest_b200.tp import ShardPlan, TPDecoder, shard_weights
-
-    cfg = GRANITE_3B
+    cfg = cfg or GRANITE_3B
     if world == 1:
-        dec = Q4Decoder(cfg, batch, ctx, seed=11)
-    else:
-        full_dec = Q4Decoder(cfg, 1, 1, seed=11)  # weights only; the KV cache lives in the TP decoder
-        plan = ShardPlan(cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.hidden, cfg.intermediate, cfg.vocab,
-                         world, rank)
-        dec = TPDecoder(cfg, batch, ctx, shard_weights(full_dec.w, plan), plan)
-        del full_dec
-        torch.cuda.empty_cache()
+        return Q4Decoder(cfg, batch, ctx, seed=seed)
+    full = Q4Decoder(cfg, 1, 1, seed=seed)  # weights only; the KV cache lives in the TP decoder
+    plan = ShardPlan(cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.hidden, cfg.intermediate, cfg.vocab, world, rank)
+    dec = TPDecoder(cfg, batch, ctx, shard_weights(full.w, plan), plan)
+    del full
+    torch.cuda.empty_cache()
+    return dec
+
+
+def capture_step(torch, dec, program: bool = False):
+    """The decoder's step in one CUDA graph (kept, so its kernel nodes can be counted)."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        dec.step_program() if program else dec.step()
+    torch.cuda.current_stream().wait_stream(s)
+    if program:
+        return dec.capture(program=True)
+    g = torch.cuda.CUDAGraph(keep_graph=True)
+    with torch.cuda.graph(g):
+        dec.step()
+    return g
+
+
+def step_bytes(cfg, batch: int, ctx: int) -> int:
+    """Algorithmic HBM bytes of one config-4 step: every weight byte and every K/V byte once."""
+    wb = cfg.weight_bytes()
+    return wb["layers"] + wb["lm_head"] + batch * ctx * cfg.n_kv_heads * cfg.head_dim * 4 * cfg.n_layers
+
+
+def _max_over_ranks(torch, world: int, v: float) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def measure_decode(torch, world: int, rank: int, batch: int, ctx: int, steps: int, warmup: int,
+                   program: bool = False) -> dict:
+    """Config 4: the full 40-layer decode step at `batch` tokens, context `ctx`, TP over `world`
+    ranks (the persistent program instead of one launch per op with program=True, one GPU)."""
+    import torch.distributed as dist
+    from llmnputest_b200.decode import GRANITE_3B as cfg
+    dec = build_decoder(torch, world, rank, batch, ctx)
     dec.pos.fill_(ctx - 1)  # attend over the full context
     dec.x_in.normal_()
-    try:
-        s = torch.cuda.Stream()
-        s.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s):
-            dec.step()
-        torch.cuda.current_stream().wait_stream(s)
-        g = dec.capture(program=True) if program else None
-        if g is None:
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                dec.step()
-        run, how = g.replay, ("persistent program, cuda graph" if program else
-                              ("tcgen05 GEMM, cuda graph" if getattr(dec, "use_gemm", False) else "cuda graph"))
-    except Exception as e:  # capture of the collectives failed: time the eager step instead
-        torch.cuda.synchronize()
-        run, how = dec.step, f"eager ({type(e).__name__})"
+    g = capture_step(torch, dec, program)
+    how = ("persistent program, cuda graph" if program else
+           ("tcgen05 GEMM, cuda graph" if getattr(dec, "use_gemm", False) else "GEMV, cuda graph"))
+    if world > 1:
+        how += ", peer exchanges"
     for _ in range(warmup):
-        run()
+        g.replay()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for _ in range(steps):
-        run()
+        g.replay()
     b.record()
     b.synchronize()
-    ms = a.elapsed_time(b) / steps
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    wb = cfg.weight_bytes()
-    kv = batch * ctx * cfg.n_kv_heads * cfg.head_dim * 4 * cfg.n_layers
-    step_bytes = wb["layers"] + wb["lm_head"] + kv  # algorithmic: every weight and KV byte once
+    ms = _max_over_ranks(torch, world, a.elapsed_time(b) / steps)
+    nbytes = step_bytes(cfg, batch, ctx)
     out = {"batch": batch, "ctx": ctx, "tp": world, "ms_per_step": round(ms, 4), "program": program,
            "tok_s": round(batch / (ms * 1e-3), 1), "how": how,
-           "hbm_gbs_per_gpu": round(step_bytes / world / (ms * 1e-3) / 1e9, 1)}
+           "hbm_gbs_per_gpu": round(nbytes / world / (ms * 1e-3) / 1e9, 1)}
+    torch.cuda.synchronize()
+    del g
+    if hasattr(dec, "close"):
+        dec.close()
     del dec
     torch.cuda.empty_cache()
+    return out
+
+
+def decode_kernel_split(torch, dec, hbm_peak: float, reps: int = 10) -> dict:
+    """Time, with CUDA events, each kind of kernel of a decoder's step on its own buffers:
+    the 40 layers' attention calls, and their projection launches by kind (one graph each,
+    replayed `reps` times).  Algorithmic bytes per launch: attention the bf16 K/V read,
+    projections their q4 tiles."""
+    from llmnputest_b200 import ops
+    c = dec.cfg
+    d = c.head_dim
+    p = getattr(dec, "plan", None)
+    hq = p.q_local if p else c.n_heads
+    hkv = p.kv_local if p else c.n_kv_heads
+    qd, kd = hq * d, hkv * d
+    n_l = len(dec.w["layers"])
+    out = {}
+
+    def timed(fn, nbytes, launches, name):
+        g = graph_of(torch, fn)
+        t_ms = time_graph(torch, g, reps, 2)
+        del g
+        us = t_ms * 1e3 / launches
+        gbs = nbytes / launches / (us * 1e-6) / 1e9
+        out[name] = {"launches_per_step": launches, "us_per_launch": round(us, 2), "bytes_per_launch": nbytes // launches,
+                     "gbs": round(gbs, 1), "frac_of_measured_hbm": round(gbs / hbm_peak, 4),
+                     "ms_per_step": round(t_ms, 4)}
+
+    kv = dec.batch * dec.ctx_max * hkv * d * 4 * n_l
+    timed(lambda: [ops.gqa_decode(dec.qkv[:, :qd], dec.qkv[:, qd:qd + kd], dec.qkv[:, qd + kd:], dec.k_cache[li],
+                                  dec.v_cache[li], dec.pos, n_q_heads=hq, n_kv_heads=hkv, theta=c.rope_theta,
+                                  scale=d ** -0.5, max_len=dec.ctx_max, out=getattr(dec, "attn_local", dec.attn),
+                                  workspace=dec.attn_ws, prefetch_kv=True) for li in range(n_l)],
+          kv, n_l, "gqa_decode")
+    if getattr(dec, "use_gemm", False):
+        ws = dec.gemm_ws
+        kt_i = getattr(dec, "kt_i_local", dec.kt_i)
+        nt_qkv = getattr(dec, "nt_qkv_local", getattr(dec, "nt_qkv", None))
+        nt_o = getattr(dec, "nt_o_local", getattr(dec, "nt_h", None))
+        nt_i = getattr(dec, "nt_i_local", getattr(dec, "nt_i", None))
+        o_out = getattr(dec, "o_local", None)
+        down_out = getattr(dec, "down", None)
+        L = dec.w["layers"]
+        qkv_b = sum(l["qkv"].numel() for l in L)
+        timed(lambda: [ops.q4_gemm(l["qkv"], nt_qkv, dec.kt_h, dec.xn, out=dec.qkv, workspace=ws) for l in L],
+              qkv_b, n_l, "q4_gemm_qkv")
+        timed(lambda: [ops.q4_gemm(l["o"], nt_o, dec.kt_q, dec.attn, out=o_out if o_out is not None else dec.resid,
+                                   accumulate=o_out is None, workspace=ws) for l in L],
+              sum(l["o"].numel() for l in L), n_l, "q4_gemm_o")
+        timed(lambda: [ops.q4_swiglu_gemm(l["gate"], l["up"], nt_i, dec.kt_h, dec.xn, out=dec.h, workspace=ws)
+                       for l in L], sum(l["gate"].numel() + l["up"].numel() for l in L), n_l, "q4_swiglu_gemm")
+        timed(lambda: [ops.q4_gemm(l["down"], c.hidden // 32, kt_i, dec.h,
+                                   out=down_out if down_out is not None else dec.resid, accumulate=down_out is None,
+                                   workspace=ws) for l in L], sum(l["down"].numel() for l in L), n_l, "q4_gemm_down")
+    return out
+
+
+def measure_headline(torch, world: int, rank: int, batch: int, ctx: int, steps: int, warmup: int,
+                     hbm_peak: float) -> dict:
+    """The bench line's value: config 4's decode step (tokens/s over all ranks), K timed graph
+    replays between a barrier and a synchronize on both sides, max over ranks, clocks sampled
+    during the timed region; then the same step end to end with host buffers (the step's input
+    rows and positions copied in, its logits copied out, inside the timed region); then the
+    per-kernel split that names the dominant kernel."""
+    import torch.distributed as dist
+    from llmnputest_b200.decode import GRANITE_3B as cfg
+    dec = build_decoder(torch, world, rank, batch, ctx)
+    dec.pos.fill_(ctx - 1)
+    dec.x_in.normal_()
+    g = capture_step(torch, dec)
+    kernels_per_step = graph_kernel_nodes(g)
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    with ClockSampler(gpu_uuid(torch)) as clk:
+        time.sleep(0.15)  # let the sampler start
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            g.replay()
+        b.record()
+        b.synchronize()
+    ms = _max_over_ranks(torch, world, a.elapsed_time(b) / steps)
+    # end to end: the step's inputs from pinned host memory, its logits back, every step
+    x_host = torch.randn(batch, cfg.hidden).pin_memory()
+    pos_host = torch.full((batch,), ctx - 1, dtype=torch.int32).pin_memory()
+    logits_host = torch.empty(batch, cfg.vocab).pin_memory()
+
+    def e2e_step():
+        dec.x_in.copy_(x_host, non_blocking=True)
+        dec.pos.copy_(pos_host, non_blocking=True)
+        g.replay()
+        logits_host.copy_(dec.logits, non_blocking=True)
+
+    for _ in range(max(2, warmup // 2)):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e2e_steps = max(5, steps // 2)
+    a.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    b.record()
+    b.synchronize()
+    e2e_ms = _max_over_ranks(torch, world, a.elapsed_time(b) / e2e_steps)
+    del g
+    torch.cuda.synchronize()
+    split = decode_kernel_split(torch, dec, hbm_peak)
+    if hasattr(dec, "close"):
+        dec.close()
+    del dec
+    torch.cuda.empty_cache()
+    nbytes = step_bytes(cfg, batch, ctx)
+    return {"ms": ms, "tok_s": batch / (ms * 1e-3), "e2e_ms": e2e_ms, "e2e_tok_s": batch / (e2e_ms * 1e-3),
+            "h2d": x_host.numel() * 4 + pos_host.numel() * 4, "d2h": logits_host.numel() * 4,
+            "kernels_per_step": kernels_per_step, "bytes_per_step": nbytes, "clocks": clk.summary(),
+            "split": split}
+
+
+def _compare(torch, got, ref) -> tuple[float, float]:
+    """(cosine, max rel err) in float64 over every token, as the tests measure."""
+    g, r = got.double().flatten(), ref.double().flatten()
+    cos = float((g @ r) / (g.norm() * r.norm() + 1e-30))
+    rel = float((g - r).abs().max() / (r.abs().max() + 1e-30))
+    return cos, rel
+
+
+def tp_parity(torch, world: int, rank: int) -> dict:
+    """Before the timed region at N > 1: the tensor-parallel steps against the one-GPU steps
+    on the same weights, two steps each (every rank draws the same seeded full weights and
+    cache history and keeps its shard; rank 0 also runs the one-GPU decoder and compares the
+    full logits, every token, float64; the worst step is reported).
+      config 4: 2 layers of the 3B's real widths (vocab 100352), batch 1 (GEMVs) and 32
+                (tcgen05 GEMMs), peer exchanges, ctx 256 with a random history;
+      config 5: one gated DeltaNet and one gated attention layer of config 5's widths
+                (vocab 248320, the logits gathered), batch 1 and 256, from zero states."""
+    import torch.distributed as dist
+    from llmnputest_b200.decode import DecoderConfig, Q4Decoder
+    from llmnputest_b200.qwen35_decode import Qwen35Config, Qwen35Decoder
+    from llmnputest_b200.tp import ShardPlan, TPDecoder, shard_weights
+    from llmnputest_b200.tp_qwen35 import Qwen35ShardPlan, TPQwen35Decoder, shard_qwen35
+    out = {"config4": {}, "config5": {}}
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cfg = DecoderConfig(n_layers=2)
+    ctx = 256
+    for bsz in (1, 32):
+        try:
+            full = Q4Decoder(cfg, 1, 1, seed=23)
+            plan = ShardPlan(cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.hidden, cfg.intermediate, cfg.vocab,
+                             world, rank)
+            tp = TPDecoder(cfg, bsz, ctx, shard_weights(full.w, plan), plan)
+            one = Q4Decoder(cfg, bsz, ctx, weights=full.w) if rank == 0 else None
+            gen = torch.Generator(device=dev)
+            gen.manual_seed(5)
+            h0 = rank * plan.kv_local
+            for li in range(cfg.n_layers):
+                kc = torch.randn(bsz, cfg.n_kv_heads, ctx, cfg.head_dim, device=dev, generator=gen).to(torch.bfloat16)
+                vc = torch.randn(bsz, cfg.n_kv_heads, ctx, cfg.head_dim, device=dev, generator=gen).to(torch.bfloat16)
+                tp.k_cache[li].copy_(kc[:, h0:h0 + plan.kv_local])
+                tp.v_cache[li].copy_(vc[:, h0:h0 + plan.kv_local])
+                if one is not None:
+                    one.k_cache[li].copy_(kc)
+                    one.v_cache[li].copy_(vc)
+            g = tp.capture()
+            worst = (1.0, 0.0)
+            pos = (torch.arange(bsz, dtype=torch.int32, device=dev) * 7 + 100) % (ctx - 4)
+            for _ in range(2):
+                x = torch.randn(bsz, cfg.hidden, device=dev, generator=gen)
+                tp.x_in.copy_(x)
+                tp.pos.copy_(pos)
+                g.replay()
+                if one is not None:
+                    one.x_in.copy_(x)
+                    one.pos.copy_(pos)
+                    ref = one.step()
+                    cos, rel = _compare(torch, tp.logits, ref)
+                    worst = (min(worst[0], cos), max(worst[1], rel))
+                pos = pos + 1
+                torch.cuda.synchronize()
+                dist.barrier()  # rank 0's extra work stays on the host side of the next exchange
+            torch.cuda.synchronize()
+            dist.barrier()
+            del g
+            tp.close()
+            out["config4"][f"b{bsz}"] = {"cos": round(worst[0], 9), "rel": float(f"{worst[1]:.3e}"),
+                                         "how": "tcgen05 GEMM" if tp.use_gemm else "GEMV"} if rank == 0 else None
+            del tp, one, full
+            torch.cuda.empty_cache()
+        except Exception as e:  # recorded in the line; every rank raises alike or the barrier times out
+            out["config4"][f"b{bsz}"] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+    cfg5 = Qwen35Config(n_layers=2, layer_types=("linear_attention", "full_attention"))
+    for bsz in (1, 256):
+        try:
+            full = Qwen35Decoder(cfg5, 1, 1, seed=29)
+            plan5 = Qwen35ShardPlan(cfg5, world, rank)
+            tp = TPQwen35Decoder(cfg5, bsz, 64, shard_qwen35(full.w, plan5), plan5)
+            one = Qwen35Decoder(cfg5, bsz, 64, weights=full.w) if rank == 0 else None
+            gen = torch.Generator(device=dev)
+            gen.manual_seed(6)
+            worst = (1.0, 0.0)
+            for step in range(2):
+                x = torch.randn(bsz, cfg5.hidden, device=dev, generator=gen)
+                tp.x_in.copy_(x)
+                tp.pos.fill_(step)
+                got = tp.step()
+                if one is not None:
+                    one.x_in.copy_(x)
+                    one.pos.fill_(step)
+                    cos, rel = _compare(torch, got, one.step())
+                    worst = (min(worst[0], cos), max(worst[1], rel))
+            torch.cuda.synchronize()
+            dist.barrier()
+            out["config5"][f"b{bsz}"] = {"cos": round(worst[0], 9), "rel": float(f"{worst[1]:.3e}"),
+                                         "how": "tcgen05 GEMM" if tp.use_gemm else "GEMV",
+                                         "attention": "kv-head shards" if plan5.attn() is not None
+                                         else "replicated (2 kv heads)"} if rank == 0 else None
+            del tp, one, full
+            torch.cuda.empty_cache()
+        except Exception as e:
+            out["config5"][f"b{bsz}"] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+    return out
+
+
+def measure_qwen35_tp(torch, world: int, rank: int, steps: int, warmup: int) -> list:
+    """Config 5 on `world` GPUs (tp_qwen35.TPQwen35Decoder: DeltaNet by k head, attention by kv
+    head or replicated, MLP by down K-tiles, the q8 lm_head by vocab rows with the fp32 logits
+    all-gathered), ctx 2048, batch 1 and 256, one CUDA graph per step, max over ranks.  The
+    lm_head GEMV and the logits all-gather are also timed alone, each in its own graph."""
+    import torch.distributed as dist
+    from llmnputest_b200 import ops
+    from llmnputest_b200.qwen35_decode import Qwen35Config, Qwen35Decoder
+    from llmnputest_b200.tp_qwen35 import Qwen35ShardPlan, TPQwen35Decoder, shard_qwen35
+    out = []
+    cfg = Qwen35Config()
+    try:
+        full = Qwen35Decoder(cfg, 1, 1, seed=11)
+        plan = Qwen35ShardPlan(cfg, world, rank)
+        shard = shard_qwen35(full.w, plan)
+        del full
+        torch.cuda.empty_cache()
+        for bsz in (1, 256):
+            dec = TPQwen35Decoder(cfg, bsz, GATED_CTX, shard, plan)
+            dec.pos.fill_(GATED_CTX - 1)
+            dec.x_in.normal_()
+            g = graph_of(torch, dec.step)
+            for _ in range(warmup):
+                g.replay()
+            torch.cuda.synchronize()
+            dist.barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            n = max(5, steps // 2)
+            a.record()
+            for _ in range(n):
+                g.replay()
+            b.record()
+            b.synchronize()
+            ms = _max_over_ranks(torch, world, a.elapsed_time(b) / n)
+            del g
+            # the lm_head GEMV alone, and the logits all-gather alone
+            gl = graph_of(torch, lambda: ops.gemv_rmsnorm(dec.w["lm_head"], dec.nt_v_local, dec.kt_h, dec.resid,
+                                                           dec.w["final_norm"], cfg.eps, out=dec.logits_local,
+                                                           prefetch=True, q8=True))
+            dist.barrier()
+            t_lm = _max_over_ranks(torch, world, time_graph(torch, gl, 10, 2))
+            del gl
+            ga = graph_of(torch, lambda: dist.all_gather_into_tensor(dec.logits_all, dec.logits_local))
+            dist.barrier()
+            t_ag = _max_over_ranks(torch, world, time_graph(torch, ga, 10, 2))
+            del ga
+            torch.cuda.synchronize()
+            dist.barrier()
+            out.append({"batch": bsz, "ctx": GATED_CTX, "tp": world, "ms_per_step": round(ms, 4),
+                        "tok_s": round(bsz / (ms * 1e-3), 1), "lm_head_gemv_ms": round(t_lm, 4),
+                        "logits_all_gather_ms": round(t_ag, 4),
+                        "logits_all_gather_mb": round(bsz * cfg.vocab * 4 / 1e6, 1),
+                        "how": ("tcgen05 GEMM" if dec.use_gemm else "GEMV") + ", cuda graph, NCCL collectives",
+                        "attention": "kv-head shards" if plan.attn() is not None else "replicated (2 kv heads)"})
+            del dec
+            torch.cuda.empty_cache()
+    except Exception as e:
+        out.append({"error": f"{type(e).__name__}: {str(e)[:300]}"})
     return out
 
 
@@ -539,11 +975,20 @@ def cpu_reference_qwen35(kind: str, bsz: int, ctx: int = GATED_CTX, steps: int =
     (Qwen3_5GatedDeltaNet or Qwen3_5Attention, float32, as reference/from_q4nx.py:140-171
     builds the model) stepping one decode token with a filled cache, on all host threads.
     Returns {"us_per_layer", "threads", "sample"} or {"error"}."""
+    saved = {}
     try:
         import torch
         from transformers.cache_utils import DynamicCache
         from transformers.models.qwen3_5 import configuration_qwen3_5 as conf
         from transformers.models.qwen3_5 import modeling_qwen3_5 as mq
+        # With a GPU present transformers binds flash-linear-attention's Triton kernels (and
+        # causal-conv1d's), which cannot take CPU tensors: the CPU path is the module's
+        # torch implementation, so its fast-path hooks are cleared while it is built.
+        for name in ("FusedRMSNormGated", "chunk_gated_delta_rule", "fused_recurrent_gated_delta_rule",
+                     "causal_conv1d_fn", "causal_conv1d_update"):
+            if hasattr(mq, name):
+                saved[name] = getattr(mq, name)
+                setattr(mq, name, None)
         torch.manual_seed(0)
         linear = kind == "linear_attention"
         cfg = conf.Qwen3_5TextConfig(
@@ -577,214 +1022,244 @@ def cpu_reference_qwen35(kind: str, bsz: int, ctx: int = GATED_CTX, steps: int =
             for _ in range(steps):
                 run()
             dt = (time.perf_counter() - t0) / steps
-        return {"us_per_layer": round(dt * 1e6, 1), "threads": torch.get_num_threads(),
-                "sample": f"transformers {kind} module, float32, batch {bsz}"
+        return {"us_per_layer": round(dt * 1e6, 1), "threads": torch.get_num_threads(), "cores": os.cpu_count(),
+                "sample": f"transformers {kind} module (its torch implementation), float32, batch {bsz}"
                           + ("" if linear else f", ctx {ctx}") + f", {steps} decode steps"}
     except Exception as e:
         return {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+    finally:
+        if saved:
+            from transformers.models.qwen3_5 import modeling_qwen3_5 as mq
+            for name, v in saved.items():
+                setattr(mq, name, v)
 
 
-def run_b200(args, rank: int, world: int) -> dict | None:
-    import torch
+def gemv_sweep(torch, ops, args, rank: int, world: int, gen, device, pk: dict) -> dict:
+    """Config 2: the q4nx W4A16 GEMV sweep -- the 160 GEMVs of a 40-layer 3B step's weight
+    stream (QKV, O, gate+up, down; 1.966 GB, above L2) at batch 1 from one CUDA graph with
+    PDL, K replays timed with CUDA events (max over ranks; at N > 1 every rank streams its
+    own copy, weak scaling).  Also, on rank 0 of one GPU: GB/s per shape, batch 8, and the
+    sweep end to end with host buffers."""
     import torch.distributed as dist
-    from llmnputest_b200 import ops
-
-    device = torch.device("cuda", torch.cuda.current_device())
-    gen = torch.Generator(device=device)
-    gen.manual_seed(1000 + rank)
-    pk = peaks()
-
-    calls, step_bytes = build_sweep(torch, ops, args.batch, args.layers, gen, device)
+    calls, nbytes = build_sweep(torch, ops, 1, args.layers, gen, device)
 
     def sweep():
         for _, w, n_t, k_t, x, y in calls:
             ops.q4_gemv(w, n_t, k_t, x, out=y, prefetch=True)
 
     g = graph_of(torch, sweep)
-    n_launch = len(calls)
-
-    # ---- timed region (value): K replays, barrier + sync both sides, max over ranks
+    steps = max(20, args.steps)
     for _ in range(args.warmup):
         g.replay()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    with ClockSampler(gpu_uuid(torch)) as clk:
-        time.sleep(0.15)  # let the sampler start
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        for _ in range(args.steps):
-            g.replay()
-        b.record()
-        b.synchronize()
-    ms = a.elapsed_time(b) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-        dist.barrier()
-    gbs_total = world * step_bytes / (ms * 1e-3) / 1e9
-    gbs_per_gpu = step_bytes / (ms * 1e-3) / 1e9
-
-    extras = {}
-    if rank == 0 and not args.quick:
-        # per-shape GB/s (40 launches of one shape per replay, > L2 except O/QKV pools)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        g.replay()
+    b.record()
+    b.synchronize()
+    ms = _max_over_ranks(torch, world, a.elapsed_time(b) / steps)
+    per_gpu = nbytes / (ms * 1e-3) / 1e9
+    out = {"gbs": round(world * per_gpu, 1), "gbs_per_gpu": round(per_gpu, 1),
+           "frac_of_measured_hbm": round(per_gpu / pk["hbm_gbs"], 4), "ms_per_step": round(ms, 4),
+           "launches_per_step": len(calls), "bytes_per_step_per_gpu": nbytes, "batch": 1, "layers": args.layers,
+           "kernel": "q4nx_gemv_kernel<q4,NB=1,f32>",
+           "traffic_per_launch": int(nbytes / len(calls) * GEMV_DRAM_RATIO),
+           "parallelism": f"replicas x{world} (each rank streams its own weights, no collective)"}
+    if rank == 0 and world == 1 and not args.quick:
         per_shape = {}
         for name, n_t, k_t in SHAPES:
             sub = [c for c in calls if c[0] == name]
-            gs = graph_of(torch, lambda sub=sub: [ops.q4_gemv(w, n, k, x, out=y, prefetch=True) for _, w, n, k, x, y in sub])
+            gs = graph_of(torch, lambda sub=sub: [ops.q4_gemv(w, n, k, x, out=y, prefetch=True)
+                                                  for _, w, n, k, x, y in sub])
             t_ms = time_graph(torch, gs, max(20, args.steps // 10), 3)
             per_shape[name] = round(sum(c[1].numel() for c in sub) / (t_ms * 1e-3) / 1e9, 1)
             del gs
-        extras["per_shape_gbs_b1"] = per_shape
-        # batch 8 (config 2's other batch size): same weights, 8-token activations
+        out["per_shape_gbs_b1"] = per_shape
         calls8 = [(n, w, nt, kt, torch.randn(8, kt * 256, device=device, generator=gen).to(torch.bfloat16),
                    torch.empty(8, nt * 32, device=device)) for n, w, nt, kt, _, _ in calls]
         g8 = graph_of(torch, lambda: [ops.q4_gemv(w, n, k, x, out=y, prefetch=True) for _, w, n, k, x, y in calls8])
         t8 = time_graph(torch, g8, max(20, args.steps // 10), 3)
-        extras["batch8_gbs"] = round(step_bytes / (t8 * 1e-3) / 1e9, 1)
+        out["batch8_gbs"] = round(nbytes / (t8 * 1e-3) / 1e9, 1)
         del g8, calls8
-        # q8 lm_head (config 1): 248320 x 1024, batch 1, 270 MB > L2
-        w8 = make_q8_tiles(torch, 7760 * 4, gen, device)
-        x8 = torch.randn(1, 1024, device=device, generator=gen).to(torch.bfloat16)
-        y8 = torch.empty(1, 248320, device=device)
-        gl = graph_of(torch, lambda: ops.q8_gemv(w8, 7760, 4, x8, out=y8))
-        tl = time_graph(torch, gl, max(50, args.steps // 5), 5)
-        extras["q8_lm_head"] = {"us": round(tl * 1e3, 2), "gbs": round(w8.numel() / (tl * 1e-3) / 1e9, 1),
-                                "frac_of_measured_hbm": round(w8.numel() / (tl * 1e-3) / 1e9 / pk["hbm_gbs"], 3)}
-        del gl, w8
-        extras["attention"] = measure_attention(torch, ops, gen, device, pk["hbm_gbs"], args.steps)
-        extras["tc_gemm"] = measure_tc_gemm(torch, ops, gen, device, pk["bf16_tflops"], args.steps)
-        if world == 1:  # config 5's single-GPU layer kernels; the other ranks would wait meanwhile
+        # end to end: every call's x from pinned host memory, every y back, inside the timed region
+        xs_host = torch.cat([c[4].reshape(-1) for c in calls]).cpu().pin_memory()
+        ys_host = torch.empty(sum(c[5].numel() for c in calls), dtype=torch.float32).pin_memory()
+        x_dev = torch.empty_like(xs_host, device=device)
+        y_dev = torch.empty(ys_host.numel(), dtype=torch.float32, device=device)
+        views, off_x, off_y = [], 0, 0
+        for _, w, n_t, k_t, x, y in calls:
+            views.append((w, n_t, k_t, x_dev[off_x:off_x + x.numel()].view(x.shape),
+                          y_dev[off_y:off_y + y.numel()].view(y.shape)))
+            off_x += x.numel()
+            off_y += y.numel()
+        ge = graph_of(torch, lambda: [ops.q4_gemv(w, n, k, x, out=y, prefetch=True) for w, n, k, x, y in views])
+
+        def e2e_step():
+            x_dev.copy_(xs_host, non_blocking=True)
+            ge.replay()
+            ys_host.copy_(y_dev, non_blocking=True)
+
+        for _ in range(3):
+            e2e_step()
+        torch.cuda.synchronize()
+        n_e = max(10, args.steps // 2)
+        a.record()
+        for _ in range(n_e):
+            e2e_step()
+        b.record()
+        b.synchronize()
+        e2e_ms = a.elapsed_time(b) / n_e
+        out["e2e"] = {"gbs": round(nbytes / (e2e_ms * 1e-3) / 1e9, 1), "h2d_bytes_per_step": int(xs_host.numel() * 2),
+                      "d2h_bytes_per_step": int(ys_host.numel() * 4)}
+        del ge
+    del g, calls
+    torch.cuda.empty_cache()
+    return out
+
+
+HEAD_CTX = 4096
+
+
+def run_b200(args, rank: int, world: int) -> dict | None:
+    import torch
+    from llmnputest_b200 import ops
+    from llmnputest_b200.decode import GRANITE_3B
+
+    device = torch.device("cuda", torch.cuda.current_device())
+    gen = torch.Generator(device=device)
+    gen.manual_seed(1000 + rank)
+    pk = peaks()
+    extras = {}
+
+    # ---- N > 1: the tensor-parallel results against one GPU's, before anything is timed
+    if world > 1 and not args.quick:
+        extras["tp_parity"] = tp_parity(torch, world, rank)
+
+    # ---- the value: config 4's decode step, tensor-parallel over the ranks
+    head = measure_headline(torch, world, rank, args.batch, HEAD_CTX, args.steps, args.warmup, pk["hbm_gbs"])
+
+    if not args.quick:
+        extras["decode"] = [measure_decode(torch, world, rank, b, HEAD_CTX, max(10, args.steps // 2), 3)
+                            for b in (1, 8)]
+        if world == 1:
+            extras["decode"] += [measure_decode(torch, world, rank, b, HEAD_CTX, max(10, args.steps // 2), 3,
+                                                program=True) for b in (1, 8)]
+        else:
+            extras["qwen35_tp"] = measure_qwen35_tp(torch, world, rank, args.steps, args.warmup)
+        extras["gemv_sweep"] = gemv_sweep(torch, ops, args, rank, world, gen, device, pk)
+        if world == 1:  # the single-GPU kernel lines (configs 1, 3, 5)
+            w8 = make_q8_tiles(torch, 7760 * 4, gen, device)
+            x8 = torch.randn(1, 1024, device=device, generator=gen).to(torch.bfloat16)
+            y8 = torch.empty(1, 248320, device=device)
+            gl = graph_of(torch, lambda: ops.q8_gemv(w8, 7760, 4, x8, out=y8))
+            tl = time_graph(torch, gl, max(50, args.steps), 5)
+            extras["q8_lm_head"] = {"us": round(tl * 1e3, 2), "gbs": round(w8.numel() / (tl * 1e-3) / 1e9, 1),
+                                    "frac_of_measured_hbm": round(w8.numel() / (tl * 1e-3) / 1e9 / pk["hbm_gbs"], 3)}
+            del gl, w8
+            extras["attention"] = measure_attention(torch, ops, gen, device, pk["hbm_gbs"], args.steps)
+            extras["tc_gemm"] = measure_tc_gemm(torch, ops, gen, device, pk["bf16_tflops"], args.steps)
             extras["deltanet"] = measure_deltanet(torch, ops, gen, device, pk["hbm_gbs"], args.steps)
             extras["deltanet_layers"] = measure_deltanet_layers(torch, device, pk["hbm_gbs"], args.steps)
-            extras["gated_attention"] = measure_gated_attention(torch, ops, gen, device, pk["hbm_gbs"],
-                                                                args.steps)
-
-    # ---- config 4: the full decode step (tensor-parallel across the ranks when N > 1)
-    if not args.quick:
-        del g
-        extras["decode"] = [measure_decode(torch, world, rank, b, 4096, max(10, args.steps // 30), 3)
-                            for b in (1, 8, 32)]
-        if world == 1:
-            extras["decode"] += [measure_decode(torch, world, rank, b, 4096, max(10, args.steps // 30), 3,
-                                                program=True) for b in (1, 8)]
-
-    # ---- e2e: host buffers, copies inside the timed region
-    xs_host = torch.cat([c[4].reshape(-1) for c in calls]).cpu().pin_memory()
-    ys_host = torch.empty(sum(c[5].numel() for c in calls), dtype=torch.float32).pin_memory()
-    x_dev = torch.empty_like(xs_host, device=device)
-    y_dev = torch.empty(ys_host.numel(), dtype=torch.float32, device=device)
-    views, off_x, off_y = [], 0, 0
-    for name, w, n_t, k_t, x, y in calls:
-        views.append((w, n_t, k_t, x_dev[off_x:off_x + x.numel()].view(x.shape),
-                      y_dev[off_y:off_y + y.numel()].view(y.shape)))
-        off_x += x.numel()
-        off_y += y.numel()
-
-    def sweep_e2e():
-        for w, n_t, k_t, x, y in views:
-            ops.q4_gemv(w, n_t, k_t, x, out=y, prefetch=True)
-
-    ge = graph_of(torch, sweep_e2e)
-    e2e_steps = max(10, args.steps // 10)
-
-    def e2e_step():
-        x_dev.copy_(xs_host, non_blocking=True)
-        ge.replay()
-        ys_host.copy_(y_dev, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-
-    for _ in range(args.warmup):
-        e2e_step()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(e2e_steps):
-        e2e_step()
-    b.record()
-    b.synchronize()
-    e2e_ms = a.elapsed_time(b) / e2e_steps
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e_gbs = world * step_bytes / (e2e_ms * 1e-3) / 1e9
+            extras["gated_attention"] = measure_gated_attention(torch, ops, gen, device, pk["hbm_gbs"], args.steps)
+            extras["qwen35_step"] = measure_qwen35_step(torch, device, pk["hbm_gbs"], args.steps)
     assert ops.device_error() == 0, "a kernel recorded a device-side error"
-
     if rank != 0:
         return None
+
+    cfg = GRANITE_3B
+    split = head["split"]
+    dom_name, dom = max(split.items(), key=lambda kv: kv[1]["ms_per_step"])
+    step_gbs = head["bytes_per_step"] / world / (head["ms"] * 1e-3) / 1e9
     out = {
         "metric": METRIC,
-        "value": round(gbs_total, 1),
-        "unit": "GB/s",
+        "value": round(head["tok_s"], 1),
+        "unit": "tok/s",
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": round(ms, 4),
+        "ms_per_step": round(head["ms"], 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic (seeded q4nx tiles with BASELINE distributions, x ~ N(0,1) bf16)",
+        "data": "synthetic (seeded random-init q4nx/q8 weights with BASELINE distributions, KV cache and inputs ~ N(0,1))",
         "config": {
-            "workload": "config 2: q4nx W4A16 GEMV sweep, QKV 2560->3584 / O 2560->2560 / gate+up 2560->16384 / "
-                        "down 8192->2560, 40 layers, batch 1, one CUDA graph per step",
-            "batch": args.batch, "layers": args.layers, "bytes_per_step_per_gpu": step_bytes,
-            "l2": "inputs larger than L2 (1.97 GB of weights streamed per step)",
-            "parallelism": f"replicas x{world} (each rank streams its own weights, no collective)",
+            "workload": f"config 4: full random-init decode step of the dense GQA 3B ({cfg.n_layers} layers, hidden "
+                        f"{cfg.hidden}, {cfg.n_heads}/{cfg.n_kv_heads} heads, intermediate {cfg.intermediate}, vocab "
+                        f"{cfg.vocab}; q4nx projections, q8 lm_head), batch {args.batch}, context {HEAD_CTX}, one CUDA "
+                        "graph per step",
+            "batch": args.batch, "ctx": HEAD_CTX, "layers": cfg.n_layers,
+            "bytes_per_step": head["bytes_per_step"],
+            "l2": f"inputs larger than L2 ({head['bytes_per_step'] / 1e9:.1f} GB of weights and KV cache per step)",
+            "parallelism": "1 GPU" if world == 1 else
+                           f"tp{world}: kv heads, O rows, FFN rows / down K-tiles, vocab rows; peer exchanges over NVLink",
         },
-        "gpu_launches": n_launch * args.steps,
-        "e2e": {"value": round(e2e_gbs, 1), "unit": "GB/s",
-                "h2d_bytes_per_step": int(xs_host.numel() * 2), "d2h_bytes_per_step": int(ys_host.numel() * 4)},
-        "roofline": {"bound": "hbm", "achieved": round(gbs_per_gpu, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(gbs_per_gpu / pk["hbm_gbs"], 4),
-                     "traffic": int(step_bytes / n_launch * GEMV_DRAM_RATIO),
-                     "traffic_unit": "DRAM bytes read+written per launch (mean over the sweep's launches): "
-                                     "algorithmic bytes x the ncu ratio in profiles/q4nx_gemv_b1_one_layer.md",
-                     "kernel": "q4nx_gemv_kernel<q4,NB=1,f32>", "peak_src": pk["src"]},
-        "clocks": clk.summary(),
+        "gpu_launches": head["kernels_per_step"] * args.steps if head["kernels_per_step"] else None,
+        "e2e": {"value": round(head["e2e_tok_s"], 1), "unit": "tok/s", "h2d_bytes_per_step": int(head["h2d"]),
+                "d2h_bytes_per_step": int(head["d2h"])},
+        "roofline": {"bound": "hbm", "achieved": dom["gbs"], "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": dom["frac_of_measured_hbm"], "traffic": None, "kernel": dom_name,
+                     "bytes_per_launch": dom["bytes_per_launch"], "us_per_launch": dom["us_per_launch"],
+                     "peak_src": pk["src"],
+                     "step": {"gbs_per_gpu": round(step_gbs, 1), "frac": round(step_gbs / pk["hbm_gbs"], 4)}},
+        "kernel_split": split,
+        "clocks": head["clocks"],
     }
-    if world == 1 and not args.quick:  # config 5 as one step, last (see measure_qwen35_step)
-        extras["qwen35_step"] = measure_qwen35_step(torch, device, pk["hbm_gbs"], args.steps)
-    out.update(extras)
     if world == 1 and not args.no_cpu_baseline:
-        cb = run_reference_gemv(iters=20)
-        out["cpu_baseline"] = {"value": round(cb["gbs"], 2), "unit": "GB/s", "cores": cb["cores"],
-                               "kind": cb["kind"], "sample": cb["sample"]}
+        gemv = run_reference_gemv(iters=20)
+        cb = cpu_decode_step(args.batch, HEAD_CTX, gemv)
+        out["cpu_baseline"] = {"value": cb["tok_s"], "unit": "tok/s", "cores": cb["cores"], "kind": cb["kind"],
+                               "sample": cb["sample"], "parts_ms": cb["parts_ms"]}
+        if not args.quick:
+            extras["cpu_baselines"] = {
+                "config1_lm_head": cpu_lm_head(),
+                "config2_gemv": {"gbs": round(gemv["gbs"], 2), "cores": gemv["cores"], "kind": gemv["kind"],
+                                 "sample": gemv["sample"]},
+                "config3_attention": [cpu_attention(b, c) for b, c in ((1, 4096), (1, 32768), (16, 4096))],
+                "config4_step_b1": cpu_decode_step(1, HEAD_CTX, gemv),
+            }
+    out.update(extras)
     return out
 
 
 def run_reference(args, rank: int) -> dict | None:
+    """The reference arm: config 4's decode step composed from the reference's own CPU parts
+    (bench.cpu_decode_step: its compiled cpu_baseline.cpp GEMV for the projections, its
+    attention oracle, its --cpu torch lm_head) on all of this host's cores, at the batch and
+    context of the B200 arm.  Rank 0 alone runs; the other ranks exit without work."""
     if rank != 0:
         return None
     t0 = time.time()
-    cb = run_reference_gemv(iters=max(1, args.steps // 10), layers=8)
+    gemv = run_reference_gemv(iters=max(5, args.steps // 2), layers=4)
+    cb = cpu_decode_step(args.batch, HEAD_CTX, gemv)
     sec = time.time() - t0
     return {
-        "impl": "reference", "metric": METRIC, "value": round(cb["gbs"], 2), "unit": "GB/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "fp32 (bf16 codes -> fp32 AVX2 FMA)", "data": "synthetic",
-        "config": {"workload": "config 2: q4nx W4A16 GEMV sweep shapes, batch 1 (reference CPU GEMV)",
-                   "batch": 1},
-        "cpu_baseline": {"value": round(cb["gbs"], 2), "unit": "GB/s", "cores": cb["cores"], "kind": cb["kind"],
+        "impl": "reference", "metric": METRIC, "value": cb["tok_s"], "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "fp32 projections and attention, bf16 lm_head (the reference's CPU paths)",
+        "data": "synthetic",
+        "config": {"workload": f"config 4: decode step of the dense GQA 3B, batch {args.batch}, context {HEAD_CTX} "
+                               "(reference CPU parts, one layer timed x 40 + lm_head)",
+                   "batch": args.batch, "ctx": HEAD_CTX},
+        "cpu_baseline": {"value": cb["tok_s"], "unit": "tok/s", "cores": cb["cores"], "kind": cb["kind"],
                          "sample": cb["sample"]},
-        "e2e": {"value": round(cb["gbs"], 2), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "wall_s": round(sec, 1),
+        "e2e": {"value": cb["tok_s"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "parts_ms": cb["parts_ms"], "wall_s": round(sec, 1),
     }
 
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=3000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--batch", type=int, default=1)
-    ap.add_argument("--layers", type=int, default=LAYERS)
-    ap.add_argument("--quick", action="store_true", help="skip the extra per-shape / q8 / batch-8 lines")
+    ap.add_argument("--batch", type=int, default=32, help="decode batch of the headline step")
+    ap.add_argument("--layers", type=int, default=LAYERS, help="layers of the GEMV sweep")
+    ap.add_argument("--quick", action="store_true", help="the headline step only")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args(argv)
     if args.warmup < 3:
@@ -802,11 +1277,13 @@ def main(argv=None) -> int:
         if world > 1:
             import datetime
             import torch.distributed as dist
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
                                     device_id=torch.device("cuda", local))
         res = run_b200(args, rank, world)
         if world > 1:
             import torch.distributed as dist
+            torch.cuda.synchronize()
+            dist.barrier()
             dist.destroy_process_group()
     if res is not None:
         print(json.dumps(res), flush=True)

@@ -300,13 +300,27 @@ int b2_gated_delta_step(const float* qkv, int ld_qkv, const float* z, int ld_z, 
  *   h   bf16 [batch][ldh] = silu(bf16(G x)) * bf16(U x)        (SwiGLU form)
  *   batch 1..256; x bf16 [batch][ldx], 16-byte aligned, ldx % 8 == 0.
  *   workspace: device memory of b2_q4_gemm_workspace_size bytes, 256-byte
- *   aligned (the staged fp16 x and exponents); not kept between calls. */
+ *   aligned (the staged fp16 x and exponents); not kept between calls.
+ *   flags: B2_GEMV_ACCUMULATE (fp32 form); B2_GEMV_PREFETCH (the weights are not
+ *   written by kernels in flight: their first stages stream, and are dequantised,
+ *   before the wait on the preceding kernel).
+ * Each call is two launches: a pre-pass that stages x (per token, one CTA) and the
+ * GEMM.  The _rmsnorm forms read fp32 rows x [batch][ldx] (16-byte aligned, ldx % 4
+ * == 0) and stage bf16(x * rsqrt(mean(x^2) + eps) * norm_w) in that pre-pass, as
+ * b2_q4_gemv_rmsnorm does for the GEMV (designs/granite_gemv/granite_rmsnorm.h:45-80),
+ * without a separate RMSNorm launch. */
 int b2_q4_gemm_workspace_size(int batch, int k_tiles, size_t* bytes);
 int b2_q4_gemm(const uint8_t* tiles, int n_tile_rows, int k_tiles, const uint16_t* x, int batch, int ldx, float* y,
                int ldy, int flags, void* workspace, size_t workspace_bytes, void* stream);
 int b2_q4_swiglu_gemm(const uint8_t* gate, const uint8_t* up, int n_tile_rows, int k_tiles, const uint16_t* x,
                       int batch, int ldx, uint16_t* h, int ldh, int flags, void* workspace, size_t workspace_bytes,
                       void* stream);
+int b2_q4_gemm_rmsnorm(const uint8_t* tiles, int n_tile_rows, int k_tiles, const float* x, int batch, int ldx,
+                       const uint16_t* norm_w, float eps, float* y, int ldy, int flags, void* workspace,
+                       size_t workspace_bytes, void* stream);
+int b2_q4_swiglu_gemm_rmsnorm(const uint8_t* gate, const uint8_t* up, int n_tile_rows, int k_tiles, const float* x,
+                              int batch, int ldx, const uint16_t* norm_w, float eps, uint16_t* h, int ldh, int flags,
+                              void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
  * Decode program: a whole decode step (or any chain of q4 GEMVs and GQA

@@ -500,19 +500,26 @@ inline size_t tc_ws_bytes(int batch, int k_tiles) {
   return ((img + 255) & ~static_cast<size_t>(255)) + static_cast<size_t>(tc_npad(batch)) * sizeof(int);
 }
 
+// xf (with norm_w, eps): the fused RMSNorm input, fp32 rows [batch][ldx] in place of x
 int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_rows, int k_tiles, const uint16_t* x,
                    int batch, int ldx, void* y, int ldy, int flags, void* workspace, size_t ws_bytes,
-                   void* stream) {
+                   void* stream, const float* xf = nullptr, const uint16_t* norm_w = nullptr, float eps = 0.f) {
   DevInfo di;
   int st = device_info(&di);
   if (st != B2_OK) return st;
+  if (xf) {
+    if (!norm_w) return fail(B2_ERR_ARG, "null norm weight");
+    if (!aligned(xf, 16) || (ldx % 4) || !aligned(norm_w, 16)) return fail(B2_ERR_ALIGN, "x/norm weight alignment");
+    if (!(eps >= 0.f)) return fail(B2_ERR_ARG, "eps must be >= 0");
+    x = reinterpret_cast<const uint16_t*>(xf);  // satisfies the checks below; the pre-pass reads xf
+  }
   if (!w0 || !x || !y || (epi == b2::kTcEpiSwiglu && !w1)) return fail(B2_ERR_ARG, "null pointer argument");
   if (n_tile_rows < 1 || k_tiles < 1) return fail(B2_ERR_ARG, "bad tile shape %d x %d", n_tile_rows, k_tiles);
   if (batch < 1 || batch > b2::kTcMaxN) return fail(B2_ERR_ARG, "batch %d outside 1..%d", batch, b2::kTcMaxN);
-  if (ldx < k_tiles * 256 || ldx % 8) return fail(B2_ERR_ALIGN, "ldx %d: need >= K and a multiple of 8", ldx);
+  if (ldx < k_tiles * 256 || ldx % (xf ? 4 : 8)) return fail(B2_ERR_ALIGN, "ldx %d: need >= K and aligned rows", ldx);
   if (ldy < n_tile_rows * 32) return fail(B2_ERR_ARG, "ldy %d < output rows %d", ldy, n_tile_rows * 32);
   if (!aligned(w0, 16) || (w1 && !aligned(w1, 16)) || !aligned(x, 16)) return fail(B2_ERR_ALIGN, "tiles and x must be 16-byte aligned");
-  if (flags & ~B2_GEMV_ACCUMULATE) return fail(B2_ERR_ARG, "unknown flags 0x%x", flags);
+  if (flags & ~(B2_GEMV_ACCUMULATE | B2_GEMV_PREFETCH)) return fail(B2_ERR_ARG, "unknown flags 0x%x", flags);
   if (epi == b2::kTcEpiSwiglu && (flags & B2_GEMV_ACCUMULATE)) return fail(B2_ERR_ARG, "SwiGLU output cannot accumulate");
   const size_t need = tc_ws_bytes(batch, k_tiles);
   if (!workspace || ws_bytes < need) return fail(B2_ERR_WORKSPACE, "workspace of %zu bytes needed", need);
@@ -571,8 +578,21 @@ int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_row
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = g_pdl ? 1 : 0;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, b2::tc_x_prep_kernel, reinterpret_cast<const __nv_bfloat16*>(x), ldx,
-                                     batch, k_tiles * 256, npad, xsw, xexp, yzero, ldy, n_tile_rows * 32);
+  b2::TcPrep pp = {};
+  pp.x = xf ? nullptr : reinterpret_cast<const __nv_bfloat16*>(x);
+  pp.xf = xf;
+  pp.norm_w = reinterpret_cast<const __nv_bfloat16*>(norm_w);
+  pp.eps = eps;
+  pp.ldx = ldx;
+  pp.batch = batch;
+  pp.k = k_tiles * 256;
+  pp.npad = npad;
+  pp.xsw = xsw;
+  pp.xexp = xexp;
+  pp.yzero = yzero;
+  pp.ldy = ldy;
+  pp.n_out = n_tile_rows * 32;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, b2::tc_x_prep_kernel, pp);
   if (e != cudaSuccess) return cuda_fail(e, "x pre-pass launch");
 
   b2::TcParams p = {};
@@ -595,6 +615,7 @@ int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_row
   p.kt_per_split = kt_per_split;
   p.n_nsplit = n_nsplit;
   p.ncta = ncta;
+  p.prefetch = (flags & B2_GEMV_PREFETCH) ? 1 : 0;
   auto kernel = epi == b2::kTcEpiSwiglu ? b2::q4_gemm_tc_kernel<b2::kTcEpiSwiglu> : b2::q4_gemm_tc_kernel<b2::kTcEpiF32>;
   static int attr_set[64][2] = {};
   int dev = 0;
@@ -1293,6 +1314,20 @@ int b2_q4_swiglu_gemm(const uint8_t* gate, const uint8_t* up, int n_tile_rows, i
                       void* stream) {
   return tc_gemm_common(b2::kTcEpiSwiglu, gate, up, n_tile_rows, k_tiles, x, batch, ldx, h, ldh, flags, workspace,
                         workspace_bytes, stream);
+}
+
+int b2_q4_gemm_rmsnorm(const uint8_t* tiles, int n_tile_rows, int k_tiles, const float* x, int batch, int ldx,
+                       const uint16_t* norm_w, float eps, float* y, int ldy, int flags, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  return tc_gemm_common(b2::kTcEpiF32, tiles, nullptr, n_tile_rows, k_tiles, nullptr, batch, ldx, y, ldy, flags,
+                        workspace, workspace_bytes, stream, x, norm_w, eps);
+}
+
+int b2_q4_swiglu_gemm_rmsnorm(const uint8_t* gate, const uint8_t* up, int n_tile_rows, int k_tiles, const float* x,
+                              int batch, int ldx, const uint16_t* norm_w, float eps, uint16_t* h, int ldh, int flags,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  return tc_gemm_common(b2::kTcEpiSwiglu, gate, up, n_tile_rows, k_tiles, nullptr, batch, ldx, h, ldh, flags,
+                        workspace, workspace_bytes, stream, x, norm_w, eps);
 }
 
 int b2_q4_dequant_tiles(const uint8_t* tiles, int64_t n_tiles, uint16_t* out, void* stream) {

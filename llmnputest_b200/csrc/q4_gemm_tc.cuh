@@ -66,6 +66,8 @@ struct TcParams {
   int kt_per_split;
   int n_nsplit;     // token columns split over CTAs: item = (row tile, K range, column block)
   int ncta;         // token columns per CTA (npad / n_nsplit, a multiple of 16)
+  int prefetch;     // the weights are constant: the first raw stages stream (and are
+                    // dequantised) before the wait on the preceding kernel
 };
 
 struct TcSmem {
@@ -144,34 +146,78 @@ __host__ __device__ __forceinline__ uint32_t sw128_offset(int row, int k) {
 // ------------------------------------------------------------ x pre-pass
 // One CTA per token row n < npad: e = exponent putting max|x| in [2^14, 2^15),
 // x' = fp16(x * 2^e) written into the swizzled slice image; rows >= batch are 0.
-__global__ void __launch_bounds__(256) tc_x_prep_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int batch,
-                                                        int k, int npad, uint8_t* __restrict__ xsw,
-                                                        int* __restrict__ xexp, float* __restrict__ yzero, int ldy,
-                                                        int n_out) {
-  __shared__ float wmax[8];
+// With xf (fused RMSNorm) the row is bf16(xf * rsqrt(mean(xf^2) + eps) * norm_w), the
+// arithmetic of granite_rms_norm (designs/granite_gemv/granite_rmsnorm.h:45-80), from the
+// fp32 row xf [batch][ldx] instead of x.
+struct TcPrep {
+  const __nv_bfloat16* x;
+  const float* xf;
+  const __nv_bfloat16* norm_w;
+  float eps;
+  int ldx, batch, k, npad;
+  uint8_t* xsw;
+  int* xexp;
+  float* yzero;
+  int ldy, n_out;
+};
+
+__global__ void __launch_bounds__(256) tc_x_prep_kernel(const TcPrep a) {
+  __shared__ float wred[8];
   const int n = blockIdx.x;
+  const int k = a.k;
   pdl_wait();
   pdl_launch_dependents();
-  const bool live = n < batch;
+  const bool live = n < a.batch;
+  // 8 values of row n, columns 8c .. 8c+7, as bf16
+  float inv = 0.f;
+  if (live && a.xf) {
+    const float4* xr = reinterpret_cast<const float4*>(a.xf + static_cast<size_t>(n) * a.ldx);
+    float ss = 0.f;
+    for (int c = threadIdx.x; c < k / 4; c += blockDim.x) {
+      const float4 v = xr[c];
+      ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) wred[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tot += wred[i];
+    inv = rsqrtf(tot / static_cast<float>(k) + a.eps);
+    __syncthreads();  // wred is reused for the max below
+  }
+  auto row8 = [&](int c) -> uint4 {
+    if (!a.xf) return *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(n) * a.ldx + c * 8);
+    const float* xr = a.xf + static_cast<size_t>(n) * a.ldx + c * 8;
+    const float4 a0 = *reinterpret_cast<const float4*>(xr), a1 = *reinterpret_cast<const float4*>(xr + 4);
+    const uint4 wv = *reinterpret_cast<const uint4*>(a.norm_w + c * 8);
+    auto nb = [&](float xv, float wf) { return xv * inv * wf; };
+    uint4 o;
+    o.x = pack_bf16x2_rn(nb(a0.x, bf16lo_to_f32(wv.x)), nb(a0.y, bf16hi_to_f32(wv.x)));
+    o.y = pack_bf16x2_rn(nb(a0.z, bf16lo_to_f32(wv.y)), nb(a0.w, bf16hi_to_f32(wv.y)));
+    o.z = pack_bf16x2_rn(nb(a1.x, bf16lo_to_f32(wv.z)), nb(a1.y, bf16hi_to_f32(wv.z)));
+    o.w = pack_bf16x2_rn(nb(a1.z, bf16lo_to_f32(wv.w)), nb(a1.w, bf16hi_to_f32(wv.w)));
+    return o;
+  };
   float m = 0.f;
   if (live)
-    for (int c = threadIdx.x; c < k / 8; c += blockDim.x)
-      m = fmaxf(m, absmax8_bf16(*reinterpret_cast<const uint4*>(x + static_cast<size_t>(n) * ldx + c * 8)));
+    for (int c = threadIdx.x; c < k / 8; c += blockDim.x) m = fmaxf(m, absmax8_bf16(row8(c)));
   m = warp_max(m);
-  if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = m;
+  if ((threadIdx.x & 31) == 0) wred[threadIdx.x >> 5] = m;
   __syncthreads();
   m = 0.f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) m = fmaxf(m, wmax[i]);
+  for (int i = 0; i < 8; ++i) m = fmaxf(m, wred[i]);
   const int e = live ? gemv_scale_exp(__float_as_uint(m)) : 0;
   const float sc = pow2f(e);
-  if (threadIdx.x == 0) xexp[n] = e;
-  if (yzero && live)  // split-K partials are added into y: start it at zero
-    for (int i = threadIdx.x; i < n_out; i += blockDim.x) yzero[static_cast<size_t>(n) * ldy + i] = 0.f;
+  if (threadIdx.x == 0) a.xexp[n] = e;
+  if (a.yzero && live)  // split-K partials are added into y: start it at zero
+    for (int i = threadIdx.x; i < a.n_out; i += blockDim.x) a.yzero[static_cast<size_t>(n) * a.ldy + i] = 0.f;
   for (int c = threadIdx.x; c < k / 8; c += blockDim.x) {
     uint4 o = make_uint4(0u, 0u, 0u, 0u);
     if (live) {
-      const uint4 v = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(n) * ldx + c * 8);
+      const uint4 v = row8(c);
       const uint32_t w[4] = {v.x, v.y, v.z, v.w};
       uint32_t h[4];
 #pragma unroll
@@ -182,7 +228,7 @@ __global__ void __launch_bounds__(256) tc_x_prep_kernel(const __nv_bfloat16* __r
       o = make_uint4(h[0], h[1], h[2], h[3]);
     }
     const int kc = (c * 8) >> 6, kin = (c * 8) & 63;
-    *reinterpret_cast<uint4*>(xsw + static_cast<size_t>(kc) * npad * 128 + sw128_offset(n, kin)) = o;
+    *reinterpret_cast<uint4*>(a.xsw + static_cast<size_t>(kc) * a.npad * 128 + sw128_offset(n, kin)) = o;
   }
 }
 
@@ -253,38 +299,52 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
   if (warp == 0) {
     // ---------------------------------------------------------- producer
     if (lane == 0) {
-      pdl_wait();  // x image comes from the pre-pass
       const uint64_t policy = l2_evict_first_policy();  // weights stream once
       const uint64_t keep = l2_evict_last_policy();     // every CTA reads the same x slices
+      // raw tiles of K-tile kt of row tile `tile` into raw stage rs (no dependency on x)
+      auto issue_raw = [&](int tile, int kt, int rs) {
+        const uint8_t* src[4];
+        uint32_t bytes = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          int tr;
+          const uint8_t* base;
+          if (EPI == kTcEpiSwiglu) {
+            tr = tile * 2 + (j & 1);
+            base = j < 2 ? p.w0 : p.w1;
+          } else {
+            tr = tile * 4 + j;
+            base = p.w0;
+          }
+          src[j] = tr < p.n_tile_rows ? base + (static_cast<size_t>(tr) * KT + kt) * QTraits<kQ4>::kTile : nullptr;
+          bytes += src[j] ? QTraits<kQ4>::kTile : 0;
+        }
+        mbar_arrive_expect_tx(smem_u32(&raw_full[rs]), bytes);
+        const uint32_t dst = smem_u32(smem + L.raw + rs * kTcRawStage);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (src[j]) bulk_g2s(dst + j * kTcRawSlot, src[j], QTraits<kQ4>::kTile, smem_u32(&raw_full[rs]), policy);
+      };
+      // with prefetch, the first RS raw stages go out before the wait on the preceding
+      // kernel (the dequant warps need nothing else), the x slices only after it
+      uint32_t n_pre = 0;
+      if (p.prefetch) {
+        for (int it = blockIdx.x; it < n_items && n_pre < static_cast<uint32_t>(RS); it += gridDim.x)
+          for (int kt = item_k0(it); kt < item_k1(it) && n_pre < static_cast<uint32_t>(RS); ++kt, ++n_pre)
+            issue_raw(item_tile(it), kt, static_cast<int>(n_pre));
+      }
+      pdl_wait();  // x image comes from the pre-pass
       uint32_t rseq = 0, xseq = 0;
       for (int it = blockIdx.x; it < n_items && !*abort_flag; it += gridDim.x) {
         const int tile = item_tile(it);
         for (int kt = item_k0(it); kt < item_k1(it); ++kt, ++rseq) {
           const int rs = rseq % RS;
-          if (rseq >= static_cast<uint32_t>(RS) &&
-              !mbar_wait_bounded(smem_u32(&raw_empty[rs]), ((rseq / RS) & 1) ^ 1, abort_flag, kDevTimeoutEmpty))
-            break;
-          const uint8_t* src[4];
-          uint32_t bytes = 0;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            int tr;
-            const uint8_t* base;
-            if (EPI == kTcEpiSwiglu) {
-              tr = tile * 2 + (j & 1);
-              base = j < 2 ? p.w0 : p.w1;
-            } else {
-              tr = tile * 4 + j;
-              base = p.w0;
-            }
-            src[j] = tr < p.n_tile_rows ? base + (static_cast<size_t>(tr) * KT + kt) * QTraits<kQ4>::kTile : nullptr;
-            bytes += src[j] ? QTraits<kQ4>::kTile : 0;
+          if (rseq >= n_pre) {
+            if (rseq >= static_cast<uint32_t>(RS) &&
+                !mbar_wait_bounded(smem_u32(&raw_empty[rs]), ((rseq / RS) & 1) ^ 1, abort_flag, kDevTimeoutEmpty))
+              break;
+            issue_raw(tile, kt, rs);
           }
-          mbar_arrive_expect_tx(smem_u32(&raw_full[rs]), bytes);
-          const uint32_t dst = smem_u32(smem + L.raw + rs * kTcRawStage);
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            if (src[j]) bulk_g2s(dst + j * kTcRawSlot, src[j], QTraits<kQ4>::kTile, smem_u32(&raw_full[rs]), policy);
           for (int js = 0; js < 4; ++js, ++xseq) {
             const int xs = xseq % XS;
             if (xseq >= static_cast<uint32_t>(XS) &&

@@ -15,8 +15,8 @@ then the final norm fused into the q8 lm_head (b2_q8_gemv_rmsnorm): five
 launches per layer.  The residual stream is
 fp32; GEMV inputs are bf16 as in the reference.  Weights are the raw q4nx tiles,
 resident on the device; the step is captured in one CUDA graph.  Batches of 9
-and more run the projections on the tcgen05 GEMM (b2_q4_gemm / _swiglu_gemm)
-after a separate RMSNorm launch.
+and more run the projections on the tcgen05 GEMM (b2_q4_gemm / _swiglu_gemm, the
+norms fused into their x pre-pass: b2_q4_gemm_rmsnorm / _swiglu_gemm_rmsnorm).
 
 The reference never ran a granite token loop (README.md:299-301); this module
 is the composition its layer design estimates (granite_layer.py:158-164).
@@ -171,22 +171,25 @@ class Q4Decoder:
         return self.logits
 
     def _step_gemm(self) -> torch.Tensor:
-        """Large-batch step: RMSNorm launches + tcgen05 GEMMs for every projection."""
+        """Large-batch step: tcgen05 GEMMs for every projection, RMSNorm fused into their x pre-pass."""
         c = self.cfg
         d = c.head_dim
         qd, kd = c.n_heads * d, c.n_kv_heads * d
         ws = self.gemm_ws
         for li, L in enumerate(self.w["layers"]):
-            ops.rmsnorm(self.resid, L["attn_norm"], c.rms_eps, out=self.xn)
-            ops.q4_gemm(L["qkv"], self.nt_qkv, self.kt_h, self.xn, out=self.qkv, workspace=ws)
+            # RMSNorm fused into the GEMMs' x pre-pass; weights stream before each PDL wait
+            ops.q4_gemm(L["qkv"], self.nt_qkv, self.kt_h, self.resid, out=self.qkv, workspace=ws, prefetch=True,
+                        norm_w=L["attn_norm"], eps=c.rms_eps)
             ops.gqa_decode(self.qkv[:, :qd], self.qkv[:, qd:qd + kd], self.qkv[:, qd + kd:],
                            self.k_cache[li], self.v_cache[li], self.pos, n_q_heads=c.n_heads,
                            n_kv_heads=c.n_kv_heads, theta=c.rope_theta, scale=d ** -0.5, max_len=self.ctx_max,
                            out=self.attn, workspace=self.attn_ws, prefetch_kv=True)
-            ops.q4_gemm(L["o"], self.nt_h, self.kt_q, self.attn, out=self.resid, accumulate=True, workspace=ws)
-            ops.rmsnorm(self.resid, L["mlp_norm"], c.rms_eps, out=self.xn)
-            ops.q4_swiglu_gemm(L["gate"], L["up"], self.nt_i, self.kt_h, self.xn, out=self.h, workspace=ws)
-            ops.q4_gemm(L["down"], self.nt_h, self.kt_i, self.h, out=self.resid, accumulate=True, workspace=ws)
+            ops.q4_gemm(L["o"], self.nt_h, self.kt_q, self.attn, out=self.resid, accumulate=True, workspace=ws,
+                        prefetch=True)
+            ops.q4_swiglu_gemm(L["gate"], L["up"], self.nt_i, self.kt_h, self.resid, out=self.h, workspace=ws,
+                               prefetch=True, norm_w=L["mlp_norm"], eps=c.rms_eps)
+            ops.q4_gemm(L["down"], self.nt_h, self.kt_i, self.h, out=self.resid, accumulate=True, workspace=ws,
+                        prefetch=True)
         ops.gemv_rmsnorm(self.w["lm_head"], self.nt_v, self.kt_h, self.resid, self.w["final_norm"], c.rms_eps,
                          out=self.logits, q8=True)
         return self.logits

@@ -130,38 +130,55 @@ def _aligned_ws(ws: torch.Tensor) -> ctypes.c_void_p:
 
 
 def q4_gemm(tiles: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tensor, out: torch.Tensor | None = None,
-            accumulate: bool = False, workspace: torch.Tensor | None = None) -> torch.Tensor:
-    """fp32 y [B, N] = W x on the tcgen05 tensor cores (batches up to 256)."""
+            accumulate: bool = False, workspace: torch.Tensor | None = None, prefetch: bool = False,
+            norm_w: torch.Tensor | None = None, eps: float = 0.0) -> torch.Tensor:
+    """fp32 y [B, N] = W x on the tcgen05 tensor cores (batches up to 256).
+
+    With norm_w, x is the fp32 residual [B, K] and the GEMM multiplies
+    bf16(rmsnorm(x) * norm_w), the norm done in its x pre-pass (b2_q4_gemm_rmsnorm)."""
     _tiles(tiles, n_tile_rows, k_tiles, Q4_TILE_BYTES, "tiles")
     k, n = k_tiles * TILE_K, n_tile_rows * TILE_ROWS
-    x2 = _x2d(x, k)
+    x2 = _norm_in(x, norm_w, k) if norm_w is not None else _x2d(x, k)
     b = x2.shape[0]
     if out is None:
         out = torch.zeros((b, n), dtype=torch.float32, device=x2.device)
     _need(out, "out", torch.float32)
     ws = _gemm_ws(workspace, b, k_tiles, x2.device)
-    _native.call("b2_q4_gemm", _ptr(tiles), n_tile_rows, k_tiles, _ptr(x2), b, x2.stride(0), _ptr(out),
-                 out.stride(0), GEMV_ACCUMULATE if accumulate else 0,
-                 _aligned_ws(ws) if workspace is None else _ptr(ws), ws.numel() - (256 if workspace is None else 0),
-                 _stream())
+    flags = (GEMV_ACCUMULATE if accumulate else 0) | (GEMV_PREFETCH if prefetch else 0)
+    wsp = _aligned_ws(ws) if workspace is None else _ptr(ws)
+    wsn = ws.numel() - (256 if workspace is None else 0)
+    if norm_w is not None:
+        _native.call("b2_q4_gemm_rmsnorm", _ptr(tiles), n_tile_rows, k_tiles, _ptr(x2), b, x2.stride(0),
+                     _ptr(norm_w), float(eps), _ptr(out), out.stride(0), flags, wsp, wsn, _stream())
+    else:
+        _native.call("b2_q4_gemm", _ptr(tiles), n_tile_rows, k_tiles, _ptr(x2), b, x2.stride(0), _ptr(out),
+                     out.stride(0), flags, wsp, wsn, _stream())
     return out
 
 
 def q4_swiglu_gemm(gate: torch.Tensor, up: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tensor,
-                   out: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
-    """bf16 h = silu(bf16(G x)) * bf16(U x) on the tensor cores (batches up to 256)."""
+                   out: torch.Tensor | None = None, workspace: torch.Tensor | None = None, prefetch: bool = False,
+                   norm_w: torch.Tensor | None = None, eps: float = 0.0) -> torch.Tensor:
+    """bf16 h = silu(bf16(G x)) * bf16(U x) on the tensor cores (batches up to 256); with
+    norm_w, x is the fp32 residual and its RMSNorm is fused (b2_q4_swiglu_gemm_rmsnorm)."""
     _tiles(gate, n_tile_rows, k_tiles, Q4_TILE_BYTES, "gate")
     _tiles(up, n_tile_rows, k_tiles, Q4_TILE_BYTES, "up")
     k, n = k_tiles * TILE_K, n_tile_rows * TILE_ROWS
-    x2 = _x2d(x, k)
+    x2 = _norm_in(x, norm_w, k) if norm_w is not None else _x2d(x, k)
     b = x2.shape[0]
     if out is None:
         out = torch.empty((b, n), dtype=torch.bfloat16, device=x2.device)
     _need(out, "out", torch.bfloat16)
     ws = _gemm_ws(workspace, b, k_tiles, x2.device)
-    _native.call("b2_q4_swiglu_gemm", _ptr(gate), _ptr(up), n_tile_rows, k_tiles, _ptr(x2), b, x2.stride(0),
-                 _ptr(out), out.stride(0), 0, _aligned_ws(ws) if workspace is None else _ptr(ws),
-                 ws.numel() - (256 if workspace is None else 0), _stream())
+    flags = GEMV_PREFETCH if prefetch else 0
+    wsp = _aligned_ws(ws) if workspace is None else _ptr(ws)
+    wsn = ws.numel() - (256 if workspace is None else 0)
+    if norm_w is not None:
+        _native.call("b2_q4_swiglu_gemm_rmsnorm", _ptr(gate), _ptr(up), n_tile_rows, k_tiles, _ptr(x2), b,
+                     x2.stride(0), _ptr(norm_w), float(eps), _ptr(out), out.stride(0), flags, wsp, wsn, _stream())
+    else:
+        _native.call("b2_q4_swiglu_gemm", _ptr(gate), _ptr(up), n_tile_rows, k_tiles, _ptr(x2), b, x2.stride(0),
+                     _ptr(out), out.stride(0), flags, wsp, wsn, _stream())
     return out
 
 

@@ -264,8 +264,8 @@ class TPDecoder:
         self.resid.copy_(self.x_in)
         for li, L in enumerate(self.w["layers"]):
             if self.use_gemm:
-                ops.rmsnorm(self.resid, L["attn_norm"], c.rms_eps, out=self.xn)
-                ops.q4_gemm(L["qkv"], self.nt_qkv_local, self.kt_h, self.xn, out=self.qkv, workspace=ws)
+                ops.q4_gemm(L["qkv"], self.nt_qkv_local, self.kt_h, self.resid, out=self.qkv, workspace=ws,
+                            prefetch=True, norm_w=L["attn_norm"], eps=c.rms_eps)
             else:
                 ops.gemv_rmsnorm(L["qkv"], self.nt_qkv_local, self.kt_h, self.resid, L["attn_norm"], c.rms_eps,
                                  out=self.qkv, prefetch=True)
@@ -275,14 +275,15 @@ class TPDecoder:
                            workspace=self.attn_ws, prefetch_kv=True)
             a = self._gather_heads()
             if self.use_gemm:
-                ops.q4_gemm(L["o"], self.nt_o_local, self.kt_q, a, out=self.o_local, workspace=ws)
+                ops.q4_gemm(L["o"], self.nt_o_local, self.kt_q, a, out=self.o_local, workspace=ws, prefetch=True)
             else:
                 ops.q4_gemv(L["o"], self.nt_o_local, self.kt_q, a, out=self.o_local, prefetch=True)
             self._add_o_rows()
             if self.use_gemm:
-                ops.rmsnorm(self.resid, L["mlp_norm"], c.rms_eps, out=self.xn)
-                ops.q4_swiglu_gemm(L["gate"], L["up"], self.nt_i_local, self.kt_h, self.xn, out=self.h, workspace=ws)
-                ops.q4_gemm(L["down"], c.hidden // TILE_ROWS, self.kt_i_local, self.h, out=self.down, workspace=ws)
+                ops.q4_swiglu_gemm(L["gate"], L["up"], self.nt_i_local, self.kt_h, self.resid, out=self.h,
+                                   workspace=ws, prefetch=True, norm_w=L["mlp_norm"], eps=c.rms_eps)
+                ops.q4_gemm(L["down"], c.hidden // TILE_ROWS, self.kt_i_local, self.h, out=self.down, workspace=ws,
+                            prefetch=True)
             else:
                 ops.swiglu_gemv_rmsnorm(L["gate"], L["up"], self.nt_i_local, self.kt_h, self.resid, L["mlp_norm"],
                                         c.rms_eps, out=self.h, prefetch=True)

@@ -154,3 +154,39 @@ def test_decode_step_gemm_matches_gemv(cuda, bsz, ctx):
         _check(lb.cpu().numpy(), la.cpu().numpy(), 0.9999, 1e-2, ("step", step))
         pos = pos + 1
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("n_t,k_t,bsz,swiglu", [(112, 10, 32, False), (80, 32, 10, False), (256, 10, 32, True),
+                                                (7, 3, 17, False), (14, 4, 256, True)])
+def test_gemm_fused_rmsnorm_and_prefetch(cuda, n_t, k_t, bsz, swiglu):
+    """The GEMM with its RMSNorm fused into the x pre-pass (and the weights streamed before
+    the PDL wait) against b2_rmsnorm followed by the plain GEMM, and against the oracle (the
+    norm in float64).  The two norms sum their squares in different fp32 orders, so a few
+    bf16 inputs may differ by one ulp: the bar is the GEMM's own."""
+    from ml_dtypes import bfloat16
+    from llmnputest_b200 import ops
+    rng = np.random.default_rng(7000 + n_t + k_t + bsz)
+    g = orc.synth_q4_tiles(rng, n_t * k_t)
+    u = orc.synth_q4_tiles(rng, n_t * k_t) if swiglu else None
+    x = (rng.standard_normal((bsz, k_t * 256)) * 3).astype(np.float32)
+    nw = (rng.standard_normal(k_t * 256) * 0.1 + 1).astype(np.float32).astype(bfloat16)
+    xd, nwd = torch.from_numpy(x).to(cuda), dev_bf16(nw.astype(np.float32))
+    xn = ops.rmsnorm(xd, nwd, 1e-6)
+    if swiglu:
+        fused = ops.q4_swiglu_gemm(dev_u8(g), dev_u8(u), n_t, k_t, xd, prefetch=True, norm_w=nwd, eps=1e-6)
+        plain = ops.q4_swiglu_gemm(dev_u8(g), dev_u8(u), n_t, k_t, xn)
+    else:
+        fused = ops.q4_gemm(dev_u8(g), n_t, k_t, xd, prefetch=True, norm_w=nwd, eps=1e-6)
+        plain = ops.q4_gemm(dev_u8(g), n_t, k_t, xn)
+    torch.cuda.synchronize()
+    # SwiGLU outputs are bf16: a one-ulp flip of the largest value is 2^-8 relative; two ulps of bar
+    bar = 8e-3 if swiglu else REL
+    _check(fused.float().cpu().numpy(), plain.float().cpu().numpy(), COS, bar, "fused vs rmsnorm + GEMM")
+    xr = orc.rmsnorm(x, nw, 1e-6).astype(np.float32).astype(bfloat16)
+    if swiglu:
+        ref = np.stack([orc.swiglu_from_accumulators(orc.gemv_q4(g, xr[b], n_t, k_t), orc.gemv_q4(u, xr[b], n_t, k_t))
+                        for b in range(bsz)])
+        _check(fused.float().cpu().numpy(), ref, COS, bar, "swiglu vs oracle")
+    else:
+        _check(fused.cpu().numpy(), orc.gemv_q4(g, xr, n_t, k_t), what="vs oracle")
+    assert ops.device_error() == 0

@@ -112,6 +112,9 @@ def _rank(rank, world, port, out_path, bsz, comm):
                 for b in range(bsz):
                     results.append((step, b, *orc.compare(got[b], ref[b]), *orc.compare(got[b], one[b])))
             pos = pos + 1
+            # rank 0's oracle takes seconds: hold the other rank on the host, not in an
+            # exchange's bounded wait on the GPU
+            dist.barrier()
         from llmnputest_b200 import ops
         assert ops.device_error() == 0
         dist.barrier()
