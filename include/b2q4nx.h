@@ -193,16 +193,19 @@ int b2_gqa_decode_static(const float* q, const float* k_new, const float* v_new,
  * Peer regions: each rank allocates one with b2_peer_alloc (device memory plus a CUDA
  * IPC handle of B2_IPC_HANDLE_BYTES bytes), hands the handle to the other ranks (any
  * host channel), and maps theirs with b2_peer_open.  Plain peer mappings: no multicast
- * object.  The first 4096 bytes of a region are control words (zeroed by the
+ * object.  The first B2_PEER_CTL_BYTES of a region are control words (zeroed by the
  * allocation); exchanged buffers sit at higher offsets, the same on every rank.
- * `peers` below is a DEVICE array of `world` pointers: the regions as mapped in the
- * calling process, peers[rank] being its own.
+ * `peers` below is a DEVICE array of `world` (<= B2_PEER_MAX_RANKS) pointers: the
+ * regions as mapped in the calling process, peers[rank] being its own.
  *
- * Every rank must issue the same exchanges in the same order.  Each exchange waits for
- * the other ranks' data with a bounded spin (b2_set_peer_timeout_ms, default 2000 ms);
- * when it runs out the kernel records device error 6 (b2_read_device_error) and
- * returns without waiting further. */
+ * Every rank must issue the same exchanges in the same order.  An exchange is split
+ * into chunks, one per CTA; each chunk waits only for the same chunk of the other
+ * ranks, with a bounded spin (b2_set_peer_timeout_ms, default 2000 ms); when it runs
+ * out the kernel records device error 6 (b2_read_device_error) and returns without
+ * waiting further. */
 #define B2_IPC_HANDLE_BYTES 64
+#define B2_PEER_CTL_BYTES 65536
+#define B2_PEER_MAX_RANKS 16
 int b2_peer_alloc(size_t bytes, void** ptr, uint8_t* ipc_handle);
 int b2_peer_free(void* ptr);
 int b2_peer_open(const uint8_t* ipc_handle, void** ptr);

@@ -845,12 +845,20 @@ int xchg_check(void* const* peers, int world, int rank, const void* src, int row
     return fail(B2_ERR_ARG, "rank %d of world %d", rank, world);
   if (rows < 1 || cols < 1 || ld_src < cols) return fail(B2_ERR_ARG, "bad block %dx%d (ld %d)", rows, cols, ld_src);
   if (dst_offset < b2::kPeerCtlBytes) return fail(B2_ERR_ARG, "dst_offset inside the control words");
+  static_assert(b2::kPeerCtlBytes == B2_PEER_CTL_BYTES, "control block size");
+  static_assert(b2::kPeerMaxRanks == B2_PEER_MAX_RANKS, "rank limit");
   return B2_OK;
 }
 
-int xchg_chunks(long long bytes_per_peer, int rows) {
-  const long long c = (bytes_per_peer + 16383) / 16384;  // ~16 KB per CTA (to every rank)
-  return static_cast<int>(std::max(1LL, std::min<long long>({c, 64LL, static_cast<long long>(rows)})));
+// Units (16-byte vectors when every row start and the width allow, else elements) and
+// CTAs: one unit per thread up to kPeerMaxChunks CTAs, more units per thread beyond.
+void xchg_plan(b2::XchgParams& p, int elem_bytes, bool vec_ok) {
+  const bool vec = vec_ok && (static_cast<long long>(p.cols) * elem_bytes) % 16 == 0 &&
+                   (static_cast<long long>(p.ld_src) * elem_bytes) % 16 == 0 && aligned(p.src, 16);
+  p.vec = vec ? 1 : 0;
+  const long long units = static_cast<long long>(p.rows) * (vec ? p.cols * elem_bytes / 16 : p.cols);
+  const long long c = (units + b2::kXchgThreads - 1) / b2::kXchgThreads;
+  p.chunks = static_cast<int>(std::max(1LL, std::min<long long>(c, b2::kPeerMaxChunks)));
 }
 
 int xchg_launch(const void* kernel, const b2::XchgParams& p, cudaStream_t s) {
@@ -938,11 +946,14 @@ int b2_tp_gather(void* const* peers, int world, int rank, const void* src, int r
   p.rows = rows;
   p.cols = cols;
   p.ld_src = ld_src;
-  p.elem_bytes = elem_bytes;
   p.dst_offset = dst_offset;
   p.ld_dst = ld_dst;
   p.add_base = add_base;
-  p.chunks = xchg_chunks(static_cast<long long>(rows) * cols * elem_bytes, rows);
+  // 16-byte units need every destination row start aligned too (region bases are
+  // 256-byte aligned allocations), and the add base's rows
+  const bool vec_ok = dst_offset % 16 == 0 && (static_cast<long long>(ld_dst) * elem_bytes) % 16 == 0 &&
+                      (static_cast<long long>(rank) * cols * elem_bytes) % 16 == 0 && (!add_base || aligned(add_base, 16));
+  xchg_plan(p, elem_bytes, vec_ok);
   p.timeout_ns = g_peer_timeout_ns;
   const void* k = elem_bytes == 2 ? reinterpret_cast<const void*>(b2::tp_gather_kernel<uint16_t>)
                                   : reinterpret_cast<const void*>(b2::tp_gather_kernel<uint32_t>);
@@ -966,12 +977,13 @@ int b2_tp_allreduce(void* const* peers, int world, int rank, const float* src, i
   p.rows = rows;
   p.cols = cols;
   p.ld_src = ld_src;
-  p.elem_bytes = 4;
   p.dst_offset = slots_offset;
   p.ld_dst = cols;
   p.y = y;
   p.ldy = ldy;
-  p.chunks = xchg_chunks(static_cast<long long>(rows) * cols * 4, rows);
+  // slots rows are cols floats apart; y rows ldy floats apart
+  const bool vec_ok = (static_cast<long long>(rows) * cols * 4) % 16 == 0 && ldy % 4 == 0 && aligned(y, 16);
+  xchg_plan(p, 4, vec_ok);
   p.timeout_ns = g_peer_timeout_ns;
   return xchg_launch(reinterpret_cast<const void*>(b2::tp_allreduce_kernel), p, static_cast<cudaStream_t>(stream));
 }

@@ -161,63 +161,44 @@ struct TcPrep {
   int ldy, n_out;
 };
 
+// Rows of up to kPrepRegChunks * 256 chunks of 8 (K <= 16384) are read from global
+// memory once into registers; longer rows take three passes over it.
+constexpr int kPrepRegChunks = 8;
+
 __global__ void __launch_bounds__(256) tc_x_prep_kernel(const TcPrep a) {
   __shared__ float wred[8];
   const int n = blockIdx.x;
   const int k = a.k;
-  pdl_wait();
+  const int nc = k / 8;  // chunks of 8 values
+  // the GEMM's CTAs may start (set up, prefetch and dequantise weights) while this runs;
+  // they read the x image only after this grid completed
   pdl_launch_dependents();
+  pdl_wait();
   const bool live = n < a.batch;
-  // 8 values of row n, columns 8c .. 8c+7, as bf16
-  float inv = 0.f;
-  if (live && a.xf) {
-    const float4* xr = reinterpret_cast<const float4*>(a.xf + static_cast<size_t>(n) * a.ldx);
-    float ss = 0.f;
-    for (int c = threadIdx.x; c < k / 4; c += blockDim.x) {
-      const float4 v = xr[c];
-      ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
-    }
+  auto block_sum = [&](float v) {
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if ((threadIdx.x & 31) == 0) wred[threadIdx.x >> 5] = ss;
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if ((threadIdx.x & 31) == 0) wred[threadIdx.x >> 5] = v;
     __syncthreads();
     float tot = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) tot += wred[i];
-    inv = rsqrtf(tot / static_cast<float>(k) + a.eps);
-    __syncthreads();  // wred is reused for the max below
-  }
-  auto row8 = [&](int c) -> uint4 {
-    if (!a.xf) return *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(n) * a.ldx + c * 8);
-    const float* xr = a.xf + static_cast<size_t>(n) * a.ldx + c * 8;
-    const float4 a0 = *reinterpret_cast<const float4*>(xr), a1 = *reinterpret_cast<const float4*>(xr + 4);
-    const uint4 wv = *reinterpret_cast<const uint4*>(a.norm_w + c * 8);
-    auto nb = [&](float xv, float wf) { return xv * inv * wf; };
-    uint4 o;
-    o.x = pack_bf16x2_rn(nb(a0.x, bf16lo_to_f32(wv.x)), nb(a0.y, bf16hi_to_f32(wv.x)));
-    o.y = pack_bf16x2_rn(nb(a0.z, bf16lo_to_f32(wv.y)), nb(a0.w, bf16hi_to_f32(wv.y)));
-    o.z = pack_bf16x2_rn(nb(a1.x, bf16lo_to_f32(wv.z)), nb(a1.y, bf16hi_to_f32(wv.z)));
-    o.w = pack_bf16x2_rn(nb(a1.z, bf16lo_to_f32(wv.w)), nb(a1.w, bf16hi_to_f32(wv.w)));
-    return o;
+    __syncthreads();  // wred is reused
+    return tot;
   };
-  float m = 0.f;
-  if (live)
-    for (int c = threadIdx.x; c < k / 8; c += blockDim.x) m = fmaxf(m, absmax8_bf16(row8(c)));
-  m = warp_max(m);
-  if ((threadIdx.x & 31) == 0) wred[threadIdx.x >> 5] = m;
-  __syncthreads();
-  m = 0.f;
+  auto block_max = [&](float v) {
+    v = warp_max(v);
+    if ((threadIdx.x & 31) == 0) wred[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float m = 0.f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) m = fmaxf(m, wred[i]);
-  const int e = live ? gemv_scale_exp(__float_as_uint(m)) : 0;
-  const float sc = pow2f(e);
-  if (threadIdx.x == 0) a.xexp[n] = e;
-  if (a.yzero && live)  // split-K partials are added into y: start it at zero
-    for (int i = threadIdx.x; i < a.n_out; i += blockDim.x) a.yzero[static_cast<size_t>(n) * a.ldy + i] = 0.f;
-  for (int c = threadIdx.x; c < k / 8; c += blockDim.x) {
+    for (int i = 0; i < 8; ++i) m = fmaxf(m, wred[i]);
+    return m;
+  };
+  // x' = fp16(x * 2^e) of one chunk, stored into the swizzled slice image
+  auto store_chunk = [&](int c, uint4 v, float sc, bool zero) {
     uint4 o = make_uint4(0u, 0u, 0u, 0u);
-    if (live) {
-      const uint4 v = row8(c);
+    if (!zero) {
       const uint32_t w[4] = {v.x, v.y, v.z, v.w};
       uint32_t h[4];
 #pragma unroll
@@ -229,7 +210,99 @@ __global__ void __launch_bounds__(256) tc_x_prep_kernel(const TcPrep a) {
     }
     const int kc = (c * 8) >> 6, kin = (c * 8) & 63;
     *reinterpret_cast<uint4*>(a.xsw + static_cast<size_t>(kc) * a.npad * 128 + sw128_offset(n, kin)) = o;
+  };
+  // bf16(xf * inv * w) of one chunk (fused RMSNorm)
+  auto norm_chunk = [&](int c, float4 a0, float4 a1, float inv) {
+    const uint4 wv = *reinterpret_cast<const uint4*>(a.norm_w + c * 8);
+    auto nb = [&](float xv, float wf) { return xv * inv * wf; };
+    uint4 o;
+    o.x = pack_bf16x2_rn(nb(a0.x, bf16lo_to_f32(wv.x)), nb(a0.y, bf16hi_to_f32(wv.x)));
+    o.y = pack_bf16x2_rn(nb(a0.z, bf16lo_to_f32(wv.y)), nb(a0.w, bf16hi_to_f32(wv.y)));
+    o.z = pack_bf16x2_rn(nb(a1.x, bf16lo_to_f32(wv.z)), nb(a1.y, bf16hi_to_f32(wv.z)));
+    o.w = pack_bf16x2_rn(nb(a1.z, bf16lo_to_f32(wv.w)), nb(a1.w, bf16hi_to_f32(wv.w)));
+    return o;
+  };
+  auto finish_row = [&](float m) {  // exponent, and the zeroed output row for split-K
+    const int e = live ? gemv_scale_exp(__float_as_uint(m)) : 0;
+    if (threadIdx.x == 0) a.xexp[n] = e;
+    if (a.yzero && live)  // split-K partials are added into y: start it at zero
+      for (int i = threadIdx.x; i < a.n_out; i += blockDim.x) a.yzero[static_cast<size_t>(n) * a.ldy + i] = 0.f;
+    return pow2f(e);
+  };
+
+  if (nc <= kPrepRegChunks * 256) {
+    // one read of the row: chunk c = threadIdx.x + 256 i lives in registers
+    uint4 v[kPrepRegChunks];
+#pragma unroll
+    for (int i = 0; i < kPrepRegChunks; ++i) v[i] = make_uint4(0u, 0u, 0u, 0u);
+    if (a.xf) {
+      float4 f[kPrepRegChunks][2];
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < kPrepRegChunks; ++i) {
+        const int c = threadIdx.x + 256 * i;
+        if (live && c < nc) {
+          const float* xr = a.xf + static_cast<size_t>(n) * a.ldx + c * 8;
+          f[i][0] = *reinterpret_cast<const float4*>(xr);
+          f[i][1] = *reinterpret_cast<const float4*>(xr + 4);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kPrepRegChunks; ++i) {
+        const int c = threadIdx.x + 256 * i;
+        if (live && c < nc)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const float4 q = f[i][h];
+            ss = fmaf(q.x, q.x, fmaf(q.y, q.y, fmaf(q.z, q.z, fmaf(q.w, q.w, ss))));
+          }
+      }
+      const float inv = rsqrtf(block_sum(ss) / static_cast<float>(k) + a.eps);
+#pragma unroll
+      for (int i = 0; i < kPrepRegChunks; ++i) {
+        const int c = threadIdx.x + 256 * i;
+        if (live && c < nc) v[i] = norm_chunk(c, f[i][0], f[i][1], inv);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < kPrepRegChunks; ++i) {
+        const int c = threadIdx.x + 256 * i;
+        if (live && c < nc) v[i] = *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(n) * a.ldx + c * 8);
+      }
+    }
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < kPrepRegChunks; ++i) m = fmaxf(m, absmax8_bf16(v[i]));  // zero chunks add nothing
+    const float sc = finish_row(block_max(m));
+#pragma unroll
+    for (int i = 0; i < kPrepRegChunks; ++i) {
+      const int c = threadIdx.x + 256 * i;
+      if (c < nc) store_chunk(c, v[i], sc, !live);
+    }
+    return;
   }
+
+  // long rows: sum of squares, max and conversion as three passes over the row
+  float inv = 0.f;
+  if (live && a.xf) {
+    const float4* xr = reinterpret_cast<const float4*>(a.xf + static_cast<size_t>(n) * a.ldx);
+    float ss = 0.f;
+    for (int c = threadIdx.x; c < k / 4; c += blockDim.x) {
+      const float4 q = xr[c];
+      ss = fmaf(q.x, q.x, fmaf(q.y, q.y, fmaf(q.z, q.z, fmaf(q.w, q.w, ss))));
+    }
+    inv = rsqrtf(block_sum(ss) / static_cast<float>(k) + a.eps);
+  }
+  auto row8 = [&](int c) -> uint4 {
+    if (!a.xf) return *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(n) * a.ldx + c * 8);
+    const float* xr = a.xf + static_cast<size_t>(n) * a.ldx + c * 8;
+    return norm_chunk(c, *reinterpret_cast<const float4*>(xr), *reinterpret_cast<const float4*>(xr + 4), inv);
+  };
+  float m = 0.f;
+  if (live)
+    for (int c = threadIdx.x; c < nc; c += blockDim.x) m = fmaxf(m, absmax8_bf16(row8(c)));
+  const float sc = finish_row(block_max(m));
+  for (int c = threadIdx.x; c < nc; c += blockDim.x) store_chunk(c, live ? row8(c) : make_uint4(0u, 0u, 0u, 0u), sc, !live);
 }
 
 // ------------------------------------------------------------ the GEMM

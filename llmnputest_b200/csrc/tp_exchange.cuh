@@ -1,21 +1,28 @@
 // Tensor-parallel exchanges over NVLink peer memory (one process per GPU).
 //
 // Every rank owns one peer region (cudaMalloc'd, shared with the other ranks by CUDA
-// IPC: plain peer mappings, no multicast object).  Its first 4 KB are control words:
-//   sig[64]  u64  signals received, one monotonic counter per source rank
-//   exp[64]  u64  signals consumed so far, per source rank (this rank's own count)
-//   ticket   u32  last-CTA election of the all-reduce
+// IPC: plain peer mappings, no multicast object).  Its first kPeerCtlBytes are
+// control words:
+//   sig[src][c]  u64  chunk c of an exchange received from rank src (monotonic count)
+//   exp[src][c]  u64  of those, how many this rank has consumed
 // The rest holds the exchanged buffers at offsets the host chooses (the same layout on
 // every rank).  `peers` is a device array of the W region bases as mapped in this
 // process (peers[rank] is the own base).
 //
-// An exchange is one launch of `chunks` CTAs: CTA c reads its rows of this rank's block
-// once and stores them into every rank's region (16-byte stores, over NVLink for the
-// peers), then fences at system scope and adds 1 to every rank's sig[rank].  Every
-// rank runs the same exchanges in the same order, so after an exchange with C chunks each sig[src] has
-// grown by C; a waiter spins (bounded) until sig[src] >= exp[src] + C for all src, then
-// exp[src] += C.  Buffers are reused only after a later exchange that every rank has
-// entered, so a push never overwrites data a peer has yet to read.
+// An exchange is one launch of C CTAs, C from the block size (one 16-byte unit per
+// thread up to kPeerMaxChunks CTAs).  CTA c owns chunk c: a contiguous run of 16-byte
+// units of this rank's block, the same run on every rank.  It
+//   1. loads its units (all loads before any store), stores each to every rank's
+//      region (W stores per unit, over NVLink for the peers);
+//   2. after a CTA barrier, thread q adds 1 to sig[rank][c] of rank q with a
+//      release at system scope (the barrier orders the CTA's stores before it);
+//   3. thread s waits (bounded, acquire at system scope) until sig[s][c] on this rank
+//      exceeds exp[s][c], then advances exp[s][c]: chunk c of every rank has landed;
+//   4. (all-reduce) sums chunk c of the W slots in rank order into y.
+// Waits are per chunk: a CTA depends only on the same chunk of the other ranks, never
+// on the whole exchange.  Every rank runs the same exchanges in the same order, so the
+// counters of each (source, chunk) advance together.  A buffer is rewritten only by a
+// later exchange that every rank has entered after finishing its reads of it.
 //
 // Two kinds, for the seams of tensor-parallel decode (the q4nx tiles' natural cuts:
 // kv heads, output rows, K-tiles, vocab rows):
@@ -32,22 +39,25 @@
 
 namespace b2 {
 
-constexpr int kPeerMaxRanks = 64;
-constexpr int kPeerCtlBytes = 4096;
+constexpr int kPeerMaxRanks = 16;
+constexpr int kPeerMaxChunks = 256;
+constexpr int kPeerCtlBytes = 2 * kPeerMaxRanks * kPeerMaxChunks * 8;  // 64 KB
+constexpr int kXchgThreads = 256;
+constexpr int kXchgUnroll = 4;      // units in flight per thread (loads before stores)
 constexpr int kDevTimeoutPeer = 6;  // device error: a peer's signal never came
 
 struct PeerCtl {
-  unsigned long long sig[kPeerMaxRanks];
-  unsigned long long exp[kPeerMaxRanks];
-  unsigned int ticket;
+  unsigned long long sig[kPeerMaxRanks][kPeerMaxChunks];
+  unsigned long long exp[kPeerMaxRanks][kPeerMaxChunks];
 };
+static_assert(sizeof(PeerCtl) == kPeerCtlBytes, "control block layout");
 
 struct XchgParams {
   void* const* peers;  // [world] region bases
   int world, rank, chunks;
   const void* src;
   int rows, cols, ld_src;  // elements
-  int elem_bytes;          // 2 or 4
+  int vec;                 // 16-byte units (every row start and width aligned), else single elements
   long long dst_offset;    // bytes into every region
   int ld_dst;              // elements (gather: >= cols*world)
   const float* add_base;   // gather: replicated base to add to (fp32), or null
@@ -58,10 +68,8 @@ struct XchgParams {
 
 __device__ __forceinline__ PeerCtl* peer_ctl(void* base) { return reinterpret_cast<PeerCtl*>(base); }
 
-__device__ __forceinline__ void signal_peer(void* peer_base, int rank) {
-  __threadfence_system();
-  unsigned long long* s = &peer_ctl(peer_base)->sig[rank];
-  asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(s) : "memory");
+__device__ __forceinline__ void red_release_sys(unsigned long long* a) {
+  asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(a) : "memory");
 }
 
 __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* a) {
@@ -70,118 +78,167 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
   return v;
 }
 
-// Bounded wait for `chunks` new signals from every rank; true when they all arrived.
-// Called by one thread; does not update exp (the caller does, once per exchange).
-__device__ bool wait_peers(PeerCtl* ctl, int world, int chunks, unsigned long long timeout_ns) {
-  const uint64_t t0 = globaltimer();
-  for (int src = 0; src < world; ++src) {
-    const unsigned long long want = ctl->exp[src] + static_cast<unsigned long long>(chunks);
-    while (ld_acquire_sys(&ctl->sig[src]) < want) {
-      if (globaltimer() - t0 > timeout_ns) {
-        record_error(kDevTimeoutPeer);
-        return false;
-      }
-    }
-  }
-  return true;
+// Units [u0, u1) of chunk c: units are 16-byte vectors (vec) or single elements of the
+// [rows][cols] block in row-major order.
+struct ChunkRange {
+  long long u0, u1;
+  int per_row;  // units per row
+};
+__device__ __forceinline__ ChunkRange chunk_range(const XchgParams& p, int elem_bytes, int c) {
+  ChunkRange r;
+  r.per_row = p.vec ? p.cols * elem_bytes / 16 : p.cols;
+  const long long U = static_cast<long long>(p.rows) * r.per_row;
+  r.u0 = U * c / p.chunks;
+  r.u1 = U * (c + 1) / p.chunks;
+  return r;
 }
 
-// Push this CTA's rows of the rank's block to every rank's region at byte offset
-// `dst_off` (row stride ld_dst elements, this rank's block at column col0).  Each value
-// is read once and stored to all W destinations, so with add_base (which may be this
+// Step 1: this CTA's units of the rank's block to every rank's region at byte offset
+// dst_off (row stride ld_dst elements, the block at column col0).  Each value is read
+// once and the same value stored to all W copies, so with add_base (which may be this
 // rank's own copy of the destination) every copy gets the same base + src.
 template <typename T>
-__device__ void push_rows_all(const XchgParams& p, long long dst_off, int ld_dst, int col0, const float* add_base,
-                              int chunk) {
-  const int r0 = static_cast<int>(static_cast<long long>(chunk) * p.rows / p.chunks);
-  const int r1 = static_cast<int>(static_cast<long long>(chunk + 1) * p.rows / p.chunks);
+__device__ __forceinline__ void push_chunk(const XchgParams& p, long long dst_off, int ld_dst, int col0,
+                                           const float* add_base, const ChunkRange& cr) {
   const T* src = static_cast<const T*>(p.src);
-  constexpr int V = 16 / sizeof(T);
-  const bool vec = (p.cols % V) == 0 && (p.ld_src % V) == 0 && (ld_dst % V) == 0 && (col0 % V) == 0 &&
-                   (dst_off % 16) == 0 && (reinterpret_cast<uintptr_t>(src) % 16) == 0 &&
-                   (!add_base || (reinterpret_cast<uintptr_t>(add_base) % 16) == 0);
-  if (vec) {
-    const int nv = p.cols / V;
-    for (long long e = threadIdx.x; e < static_cast<long long>(r1 - r0) * nv; e += blockDim.x) {
-      const int r = r0 + static_cast<int>(e / nv), v = static_cast<int>(e % nv);
-      const size_t di = static_cast<size_t>(r) * ld_dst + col0 + v * V;
-      uint4 val = *reinterpret_cast<const uint4*>(src + static_cast<size_t>(r) * p.ld_src + v * V);
-      if (sizeof(T) == 4 && add_base) {
-        const float4 b = *reinterpret_cast<const float4*>(add_base + di);
-        float4 f = *reinterpret_cast<float4*>(&val);
-        f.x += b.x; f.y += b.y; f.z += b.z; f.w += b.w;
-        val = *reinterpret_cast<uint4*>(&f);
+  if (p.vec) {
+    constexpr int V = 16 / sizeof(T);
+    for (long long ub = cr.u0; ub < cr.u1; ub += kXchgThreads * kXchgUnroll) {
+      uint4 val[kXchgUnroll];
+      size_t di[kXchgUnroll];
+#pragma unroll
+      for (int j = 0; j < kXchgUnroll; ++j) {
+        const long long u = ub + j * kXchgThreads + threadIdx.x;
+        if (u < cr.u1) {
+          const int r = static_cast<int>(u / cr.per_row), v = static_cast<int>(u % cr.per_row);
+          di[j] = static_cast<size_t>(r) * ld_dst + col0 + v * V;
+          val[j] = *reinterpret_cast<const uint4*>(src + static_cast<size_t>(r) * p.ld_src + v * V);
+          if (sizeof(T) == 4 && add_base) {
+            const float4 b = *reinterpret_cast<const float4*>(add_base + di[j]);
+            float4 f = *reinterpret_cast<float4*>(&val[j]);
+            f.x += b.x;
+            f.y += b.y;
+            f.z += b.z;
+            f.w += b.w;
+            val[j] = *reinterpret_cast<uint4*>(&f);
+          }
+        }
       }
-      for (int q = 0; q < p.world; ++q) {
-        T* dst = reinterpret_cast<T*>(static_cast<uint8_t*>(p.peers[q]) + dst_off);
-        *reinterpret_cast<uint4*>(dst + di) = val;
+#pragma unroll
+      for (int j = 0; j < kXchgUnroll; ++j) {
+        if (ub + j * kXchgThreads + threadIdx.x < cr.u1)
+          for (int q = 0; q < p.world; ++q) {
+            T* dst = reinterpret_cast<T*>(static_cast<uint8_t*>(p.peers[q]) + dst_off);
+            *reinterpret_cast<uint4*>(dst + di[j]) = val[j];
+          }
       }
     }
   } else {
-    for (long long e = threadIdx.x; e < static_cast<long long>(r1 - r0) * p.cols; e += blockDim.x) {
-      const int r = r0 + static_cast<int>(e / p.cols), c = static_cast<int>(e % p.cols);
-      const size_t di = static_cast<size_t>(r) * ld_dst + col0 + c;
-      T val = src[static_cast<size_t>(r) * p.ld_src + c];
-      if (sizeof(T) == 4 && add_base) {
-        const float f = *reinterpret_cast<float*>(&val) + add_base[di];
-        val = *reinterpret_cast<const T*>(&f);
+    for (long long ub = cr.u0; ub < cr.u1; ub += kXchgThreads * kXchgUnroll) {
+      T val[kXchgUnroll];
+      size_t di[kXchgUnroll];
+#pragma unroll
+      for (int j = 0; j < kXchgUnroll; ++j) {
+        const long long u = ub + j * kXchgThreads + threadIdx.x;
+        if (u < cr.u1) {
+          const int r = static_cast<int>(u / cr.per_row), c = static_cast<int>(u % cr.per_row);
+          di[j] = static_cast<size_t>(r) * ld_dst + col0 + c;
+          val[j] = src[static_cast<size_t>(r) * p.ld_src + c];
+          if (sizeof(T) == 4 && add_base) {
+            const float f = *reinterpret_cast<const float*>(&val[j]) + add_base[di[j]];
+            val[j] = *reinterpret_cast<const T*>(&f);
+          }
+        }
       }
-      for (int q = 0; q < p.world; ++q)
-        reinterpret_cast<T*>(static_cast<uint8_t*>(p.peers[q]) + dst_off)[di] = val;
+#pragma unroll
+      for (int j = 0; j < kXchgUnroll; ++j) {
+        if (ub + j * kXchgThreads + threadIdx.x < cr.u1)
+          for (int q = 0; q < p.world; ++q)
+            reinterpret_cast<T*>(static_cast<uint8_t*>(p.peers[q]) + dst_off)[di[j]] = val[j];
+      }
     }
   }
 }
 
-// grid = chunks: CTA c pushes its rows to every rank, then signals every rank
-template <typename T>
-__global__ void __launch_bounds__(256) tp_gather_kernel(const XchgParams p) {
-  pdl_wait();  // the block to send is the preceding kernel's output
-  pdl_launch_dependents();
-  push_rows_all<T>(p, p.dst_offset, p.ld_dst, p.rank * p.cols, p.add_base, blockIdx.x);
+// Steps 2-3 for chunk c; returns (to every thread) whether chunk c of every rank landed.
+__device__ __forceinline__ bool signal_and_wait(const XchgParams& p, int c) {
+  __shared__ int ok;
+  // the CTA barrier orders every thread's stores before thread q's release: a peer
+  // that acquires the signal sees the whole chunk
   __syncthreads();
-  if (threadIdx.x < p.world) signal_peer(p.peers[threadIdx.x], p.rank);
-  // one waiter: the launch completes only when every rank's pushes into this region landed
-  if (blockIdx.x == 0 && threadIdx.x == 0) {
+  if (threadIdx.x == 0) ok = 1;
+  if (threadIdx.x < p.world) red_release_sys(&peer_ctl(p.peers[threadIdx.x])->sig[p.rank][c]);
+  __syncthreads();
+  if (threadIdx.x < p.world) {
     PeerCtl* ctl = peer_ctl(p.peers[p.rank]);
-    if (wait_peers(ctl, p.world, p.chunks, p.timeout_ns))
-      for (int src = 0; src < p.world; ++src) ctl->exp[src] += static_cast<unsigned long long>(p.chunks);
+    const int s = threadIdx.x;
+    const unsigned long long want = ctl->exp[s][c] + 1ull;
+    const uint64_t t0 = globaltimer();
+    bool got = true;
+    while (ld_acquire_sys(&ctl->sig[s][c]) < want) {
+      if (globaltimer() - t0 > p.timeout_ns) {
+        record_error(kDevTimeoutPeer);
+        got = false;
+        break;
+      }
+    }
+    if (got)
+      ctl->exp[s][c] = want;
+    else
+      ok = 0;
   }
+  __syncthreads();
+  return ok != 0;
 }
 
-// slots: W x [rows][cols] fp32 at dst_offset of every region (slot s = rank s's partial)
-__global__ void __launch_bounds__(256) tp_allreduce_kernel(const XchgParams p) {
+// grid = chunks: CTA c pushes chunk c to every rank, signals, and waits for chunk c of
+// every rank; the launch completes once every rank's block has landed here
+template <typename T>
+__global__ void __launch_bounds__(kXchgThreads) tp_gather_kernel(const XchgParams p) {
+  pdl_wait();  // the block to send is the preceding kernel's output
+  pdl_launch_dependents();
+  const ChunkRange cr = chunk_range(p, sizeof(T), blockIdx.x);
+  push_chunk<T>(p, p.dst_offset, p.ld_dst, p.rank * p.cols, p.add_base, cr);
+  signal_and_wait(p, blockIdx.x);
+}
+
+// slots: W x [rows][cols] fp32 at dst_offset of every region (slot s = rank s's
+// partial); CTA c sums chunk c of the slots in rank order into y
+__global__ void __launch_bounds__(kXchgThreads) tp_allreduce_kernel(const XchgParams p) {
   pdl_wait();
   pdl_launch_dependents();
   const size_t slot_elems = static_cast<size_t>(p.rows) * p.cols;
-  push_rows_all<float>(p, p.dst_offset + static_cast<long long>(p.rank) * slot_elems * 4, p.cols, 0, nullptr,
-                       blockIdx.x);
-  __syncthreads();
-  if (threadIdx.x < p.world) signal_peer(p.peers[threadIdx.x], p.rank);
-  // every CTA waits for all partials, then sums its share of the elements in rank order
-  __shared__ int ok;
-  PeerCtl* ctl = peer_ctl(p.peers[p.rank]);
-  if (threadIdx.x == 0) ok = wait_peers(ctl, p.world, p.chunks, p.timeout_ns) ? 1 : 0;
-  __syncthreads();
-  if (ok) {
-    const float* slots = reinterpret_cast<const float*>(static_cast<const uint8_t*>(p.peers[p.rank]) + p.dst_offset);
-    const long long n = static_cast<long long>(slot_elems);
-    const long long e0 = n * blockIdx.x / gridDim.x, e1 = n * (blockIdx.x + 1) / gridDim.x;
-    for (long long e = e0 + threadIdx.x; e < e1; e += blockDim.x) {
-      float s = 0.f;
-      for (int r = 0; r < p.world; ++r) s += slots[static_cast<size_t>(r) * slot_elems + e];
-      const int row = static_cast<int>(e / p.cols), col = static_cast<int>(e % p.cols);
-      p.y[static_cast<size_t>(row) * p.ldy + col] += s;
+  const ChunkRange cr = chunk_range(p, 4, blockIdx.x);
+  push_chunk<float>(p, p.dst_offset + static_cast<long long>(p.rank) * slot_elems * 4, p.cols, 0, nullptr, cr);
+  if (!signal_and_wait(p, blockIdx.x)) return;
+  const float* slots = reinterpret_cast<const float*>(static_cast<const uint8_t*>(p.peers[p.rank]) + p.dst_offset);
+  if (p.vec) {
+    for (long long u = cr.u0 + threadIdx.x; u < cr.u1; u += kXchgThreads) {
+      const int r = static_cast<int>(u / cr.per_row), v = static_cast<int>(u % cr.per_row);
+      const size_t e = static_cast<size_t>(r) * p.cols + v * 4;
+      float4 s = *reinterpret_cast<const float4*>(slots + e);
+      for (int q = 1; q < p.world; ++q) {
+        const float4 t = *reinterpret_cast<const float4*>(slots + q * slot_elems + e);
+        s.x += t.x;
+        s.y += t.y;
+        s.z += t.z;
+        s.w += t.w;
+      }
+      float4* yp = reinterpret_cast<float4*>(p.y + static_cast<size_t>(r) * p.ldy + v * 4);
+      float4 yv = *yp;
+      yv.x += s.x;
+      yv.y += s.y;
+      yv.z += s.z;
+      yv.w += s.w;
+      *yp = yv;
     }
-  }
-  // the last CTA past its wait consumes the signals (every CTA has read exp by then)
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const unsigned int t = atomicAdd(&ctl->ticket, 1u);
-    if (t == gridDim.x - 1) {
-      for (int src = 0; src < p.world; ++src) ctl->exp[src] += static_cast<unsigned long long>(p.chunks);
-      ctl->ticket = 0;
-      __threadfence();
+  } else {
+    for (long long u = cr.u0 + threadIdx.x; u < cr.u1; u += kXchgThreads) {
+      const int r = static_cast<int>(u / cr.per_row), c = static_cast<int>(u % cr.per_row);
+      const size_t e = static_cast<size_t>(r) * p.cols + c;
+      float s = slots[e];
+      for (int q = 1; q < p.world; ++q) s += slots[q * slot_elems + e];
+      p.y[static_cast<size_t>(r) * p.ldy + c] += s;
     }
   }
 }

@@ -20,7 +20,7 @@ import torch
 
 from . import _native
 
-CTL_BYTES = 4096
+CTL_BYTES = 65536  # B2_PEER_CTL_BYTES: the control words at the start of every region
 ALIGN = 256
 IPC_HANDLE_BYTES = 64
 

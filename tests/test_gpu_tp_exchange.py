@@ -15,6 +15,7 @@ import torch
 pytestmark = pytest.mark.gpu
 
 DEV_ERR_PEER_TIMEOUT = 6
+CTL = 65536  # B2_PEER_CTL_BYTES
 
 
 @pytest.fixture(scope="module")
@@ -36,37 +37,39 @@ def _stream():
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
 
-def test_world1_gather_and_allreduce(lib):
+# 16-byte units in several chunks; single elements (width not a multiple of 4 floats);
+# more units than one per thread of 256 CTAs; a block smaller than one unit
+@pytest.mark.parametrize("rows,cols", [(5, 3000), (3, 1001), (64, 8192), (1, 2)])
+def test_world1_gather_and_allreduce(lib, rows, cols):
     from llmnputest_b200.peer import wrap
-    rows, cols = 5, 3000
-    base = _region(lib, 4096 + 3 * rows * cols * 4 + 4096)
+    base = _region(lib, CTL + 3 * rows * cols * 4 + 4096)
     try:
         peers = torch.tensor([base], dtype=torch.int64, device="cuda")
-        dst = wrap(base + 4096, (rows, cols), torch.float32, "cuda")
-        slots = 4096 + rows * cols * 4
+        dst = wrap(base + CTL, (rows, cols), torch.float32, "cuda")
+        slots = CTL + (rows * cols * 4 + 255) // 256 * 256
         g = torch.Generator(device="cuda")
         g.manual_seed(0)
         src = torch.randn(rows, cols, device="cuda", generator=g)
         for _ in range(3):  # repeated exchanges: the signal counters advance together
             assert lib.b2_tp_gather(ctypes.c_void_p(peers.data_ptr()), 1, 0, ctypes.c_void_p(src.data_ptr()), rows,
-                                    cols, cols, 4, 4096, cols, None, _stream()) == 0
+                                    cols, cols, 4, CTL, cols, None, _stream()) == 0
         torch.cuda.synchronize()
         assert torch.equal(dst, src)
         base_before = dst.clone()
         assert lib.b2_tp_gather(ctypes.c_void_p(peers.data_ptr()), 1, 0, ctypes.c_void_p(src.data_ptr()), rows, cols,
-                                cols, 4, 4096, cols, ctypes.c_void_p(dst.data_ptr()), _stream()) == 0  # add mode
+                                cols, 4, CTL, cols, ctypes.c_void_p(dst.data_ptr()), _stream()) == 0  # add mode
         torch.cuda.synchronize()
         assert torch.equal(dst, base_before + src)
-        y = torch.randn(rows, cols + 7, device="cuda", generator=g)
+        y = torch.randn(rows, cols + 8, device="cuda", generator=g)
         y0 = y.clone()
         assert lib.b2_tp_allreduce(ctypes.c_void_p(peers.data_ptr()), 1, 0, ctypes.c_void_p(src.data_ptr()), rows,
                                    cols, cols, slots, ctypes.c_void_p(y.data_ptr()), y.stride(0), _stream()) == 0
         torch.cuda.synchronize()
         assert torch.equal(y[:, :cols], y0[:, :cols] + src) and torch.equal(y[:, cols:], y0[:, cols:])
-        h = torch.randn(rows, 64, device="cuda", generator=g).to(torch.bfloat16)  # 2-byte elements
-        hd = wrap(base + 4096, (rows, 64), torch.bfloat16, "cuda")
-        assert lib.b2_tp_gather(ctypes.c_void_p(peers.data_ptr()), 1, 0, ctypes.c_void_p(h.data_ptr()), rows, 64, 64,
-                                2, 4096, 64, None, _stream()) == 0
+        h = torch.randn(rows, cols, device="cuda", generator=g).to(torch.bfloat16)  # 2-byte elements
+        hd = wrap(base + CTL, (rows, cols), torch.bfloat16, "cuda")
+        assert lib.b2_tp_gather(ctypes.c_void_p(peers.data_ptr()), 1, 0, ctypes.c_void_p(h.data_ptr()), rows, cols,
+                                cols, 2, CTL, cols, None, _stream()) == 0
         torch.cuda.synchronize()
         assert torch.equal(hd, h)
         from llmnputest_b200 import ops
@@ -79,14 +82,14 @@ def test_exchange_wait_runs_out(lib):
     """Rank 0 of a 2-rank exchange whose other rank never runs: device error 6, no hang."""
     from llmnputest_b200 import ops
     rows, cols = 2, 256
-    r0, r1 = _region(lib, 4096 + rows * cols * 4 * 2), _region(lib, 4096 + rows * cols * 4 * 2)
+    r0, r1 = _region(lib, CTL + rows * cols * 4 * 2), _region(lib, CTL + rows * cols * 4 * 2)
     try:
         assert ops.device_error() == 0
         assert lib.b2_set_peer_timeout_ms(50) == 0
         peers = torch.tensor([r0, r1], dtype=torch.int64, device="cuda")
         src = torch.ones(rows, cols, device="cuda")
         assert lib.b2_tp_gather(ctypes.c_void_p(peers.data_ptr()), 2, 0, ctypes.c_void_p(src.data_ptr()), rows, cols,
-                                cols, 4, 4096, 2 * cols, None, _stream()) == 0
+                                cols, 4, CTL, 2 * cols, None, _stream()) == 0
         torch.cuda.synchronize()  # returns: the wait gave up after 50 ms
         assert ops.device_error() == DEV_ERR_PEER_TIMEOUT
         assert ops.device_error() == 0  # read and cleared
@@ -104,10 +107,11 @@ def test_exchange_argument_errors(lib):
     s = _stream()
     p = ctypes.c_void_p(peers.data_ptr())
     sp = ctypes.c_void_p(src.data_ptr())
-    assert lib.b2_tp_gather(p, 2, 2, sp, 4, 4, 4, 4, 4096, 8, None, s) != 0         # rank out of range
-    assert lib.b2_tp_gather(p, 2, 0, sp, 4, 4, 4, 4, 1024, 8, None, s) != 0         # inside the control words
-    assert lib.b2_tp_gather(p, 2, 0, sp, 4, 4, 4, 4, 4096, 7, None, s) != 0         # ld_dst < cols*world
-    assert lib.b2_tp_gather(p, 2, 0, sp, 4, 4, 4, 3, 4096, 8, None, s) != 0         # element size
-    assert lib.b2_tp_gather(p, 2, 0, sp, 4, 4, 4, 2, 4096, 8, sp, s) != 0           # add needs fp32
-    assert lib.b2_tp_allreduce(p, 2, 0, sp, 4, 4, 4, 4100, sp, 4, s) != 0           # slots misaligned
+    assert lib.b2_tp_gather(p, 2, 2, sp, 4, 4, 4, 4, CTL, 8, None, s) != 0          # rank out of range
+    assert lib.b2_tp_gather(p, 17, 0, sp, 4, 4, 4, 4, CTL, 68, None, s) != 0        # more ranks than the limit
+    assert lib.b2_tp_gather(p, 2, 0, sp, 4, 4, 4, 4, CTL - 16, 8, None, s) != 0     # inside the control words
+    assert lib.b2_tp_gather(p, 2, 0, sp, 4, 4, 4, 4, CTL, 7, None, s) != 0          # ld_dst < cols*world
+    assert lib.b2_tp_gather(p, 2, 0, sp, 4, 4, 4, 3, CTL, 8, None, s) != 0          # element size
+    assert lib.b2_tp_gather(p, 2, 0, sp, 4, 4, 4, 2, CTL, 8, sp, s) != 0            # add needs fp32
+    assert lib.b2_tp_allreduce(p, 2, 0, sp, 4, 4, 4, CTL + 4, sp, 4, s) != 0        # slots misaligned
     assert lib.b2_set_peer_timeout_ms(0) != 0
