@@ -340,10 +340,12 @@ def time_graph(torch, g, steps: int, warmup: int) -> float:
     return a.elapsed_time(b) / steps  # ms per replay
 
 
-def measure_tc_gemm(torch, ops, gen, device, tensor_peak: float, steps: int) -> list:
+def measure_tc_gemm(torch, ops, gen, device, tensor_peak: float, steps: int, hbm_peak: float) -> list:
     """Tensor-core GEMM (b2_q4_gemm / b2_q4_swiglu_gemm): config-5 MLP shapes at batch 256
-    (hidden 1024, intermediate 3584) and config-4 projections at batch 32.  A weight
-    pool above L2 is rotated; algorithmic bytes = the q4 tiles, flops = 2*B*N*K."""
+    (hidden 1024, intermediate 3584) and config-4 projections at batch 32, on packed tiles
+    (A dequantised into TMEM, the decoders' form) and on the tiles as stored (A through
+    shared memory).  A weight pool above L2 is rotated; algorithmic bytes = the q4 tiles,
+    flops = 2*B*N*K."""
     cases = [("c5_gate_up_swiglu", 112, 4, 256, True), ("c5_down", 32, 14, 256, False),
              ("c4_qkv", 112, 10, 32, False), ("c4_gate_up_swiglu", 256, 10, 32, True), ("c4_down", 80, 32, 32, False)]
     out = []
@@ -358,20 +360,27 @@ def measure_tc_gemm(torch, ops, gen, device, tensor_peak: float, steps: int) -> 
         raw = torch.empty(nb + 256, dtype=torch.uint8, device=device)
         wsb = raw[(256 - raw.data_ptr() % 256) % 256:][:nb]
 
-        def calls(ws_=ws_, x=x, y=y, wsb=wsb, n_t=n_t, k_t=k_t, swiglu=swiglu):
-            for g_, u_ in ws_:
+        def calls(pool_=ws_, packed=False, x=x, y=y, wsb=wsb, n_t=n_t, k_t=k_t, swiglu=swiglu):
+            for g_, u_ in pool_:
                 if swiglu:
-                    ops.q4_swiglu_gemm(g_, u_, n_t, k_t, x, out=y, workspace=wsb)
+                    ops.q4_swiglu_gemm(g_, u_, n_t, k_t, x, out=y, workspace=wsb, prefetch=True, packed=packed)
                 else:
-                    ops.q4_gemm(g_, n_t, k_t, x, out=y, workspace=wsb)
+                    ops.q4_gemm(g_, n_t, k_t, x, out=y, workspace=wsb, prefetch=True, packed=packed)
 
-        g = graph_of(torch, calls)
-        t_ms = time_graph(torch, g, max(5, steps // 50), 3) / pool
         flops = 2 * bsz * n_t * 32 * k_t * 256 * (2 if swiglu else 1)
+        g = graph_of(torch, calls)
+        t_smem = time_graph(torch, g, max(5, steps // 50), 3) / pool
+        del g
+        pk = [(ops.q4_gemm_pack(g_, n_t, k_t), ops.q4_gemm_pack(u_, n_t, k_t) if u_ is not None else None)
+              for g_, u_ in ws_]
+        g = graph_of(torch, lambda: calls(pk, True))
+        t_ms = time_graph(torch, g, max(5, steps // 50), 3) / pool
         out.append({"case": name, "batch": bsz, "us": round(t_ms * 1e3, 2), "gbs": round(per / (t_ms * 1e-3) / 1e9, 1),
+                    "frac_of_measured_hbm": round(per / (t_ms * 1e-3) / 1e9 / hbm_peak, 3),
                     "tflops": round(flops / (t_ms * 1e-3) / 1e12, 1),
-                    "frac_of_measured_tensor": round(flops / (t_ms * 1e-3) / 1e12 / tensor_peak, 3)})
-        del g, ws_
+                    "frac_of_measured_tensor": round(flops / (t_ms * 1e-3) / 1e12 / tensor_peak, 3),
+                    "form": "packed tiles, A in TMEM", "us_tiles_as_stored": round(t_smem * 1e3, 2)})
+        del g, ws_, pk
         torch.cuda.empty_cache()
     return out
 
@@ -514,18 +523,24 @@ def decode_kernel_split(torch, dec, hbm_peak: float, reps: int = 10) -> dict:
         nt_i = getattr(dec, "nt_i_local", getattr(dec, "nt_i", None))
         o_out = getattr(dec, "o_local", None)
         down_out = getattr(dec, "down", None)
-        L = dec.w["layers"]
-        qkv_b = sum(l["qkv"].numel() for l in L)
-        timed(lambda: [ops.q4_gemm(l["qkv"], nt_qkv, dec.kt_h, dec.xn, out=dec.qkv, workspace=ws) for l in L],
+        # the step's own calls: packed weights (A in TMEM), RMSNorm fused, weights prefetched
+        L, G = dec.w["layers"], dec.wg
+        pk = getattr(dec, "packed", True)
+        qkv_b = sum(g["qkv"].numel() for g in G)
+        timed(lambda: [ops.q4_gemm(g["qkv"], nt_qkv, dec.kt_h, dec.resid, out=dec.qkv, workspace=ws, prefetch=True,
+                                   norm_w=l["attn_norm"], eps=c.rms_eps, packed=pk) for g, l in zip(G, L)],
               qkv_b, n_l, "q4_gemm_qkv")
-        timed(lambda: [ops.q4_gemm(l["o"], nt_o, dec.kt_q, dec.attn, out=o_out if o_out is not None else dec.resid,
-                                   accumulate=o_out is None, workspace=ws) for l in L],
-              sum(l["o"].numel() for l in L), n_l, "q4_gemm_o")
-        timed(lambda: [ops.q4_swiglu_gemm(l["gate"], l["up"], nt_i, dec.kt_h, dec.xn, out=dec.h, workspace=ws)
-                       for l in L], sum(l["gate"].numel() + l["up"].numel() for l in L), n_l, "q4_swiglu_gemm")
-        timed(lambda: [ops.q4_gemm(l["down"], c.hidden // 32, kt_i, dec.h,
+        timed(lambda: [ops.q4_gemm(g["o"], nt_o, dec.kt_q, dec.attn, out=o_out if o_out is not None else dec.resid,
+                                   accumulate=o_out is None, workspace=ws, prefetch=True, packed=pk) for g in G],
+              sum(g["o"].numel() for g in G), n_l, "q4_gemm_o")
+        timed(lambda: [ops.q4_swiglu_gemm(g["gate"], g["up"], nt_i, dec.kt_h, dec.resid, out=dec.h, workspace=ws,
+                                          prefetch=True, norm_w=l["mlp_norm"], eps=c.rms_eps, packed=pk)
+                       for g, l in zip(G, L)], sum(g["gate"].numel() + g["up"].numel() for g in G), n_l,
+              "q4_swiglu_gemm")
+        timed(lambda: [ops.q4_gemm(g["down"], c.hidden // 32, kt_i, dec.h,
                                    out=down_out if down_out is not None else dec.resid, accumulate=down_out is None,
-                                   workspace=ws) for l in L], sum(l["down"].numel() for l in L), n_l, "q4_gemm_down")
+                                   workspace=ws, prefetch=True, packed=pk) for g in G],
+              sum(g["down"].numel() for g in G), n_l, "q4_gemm_down")
     return out
 
 
@@ -1160,7 +1175,7 @@ def run_b200(args, rank: int, world: int) -> dict | None:
                                     "frac_of_measured_hbm": round(w8.numel() / (tl * 1e-3) / 1e9 / pk["hbm_gbs"], 3)}
             del gl, w8
             extras["attention"] = measure_attention(torch, ops, gen, device, pk["hbm_gbs"], args.steps)
-            extras["tc_gemm"] = measure_tc_gemm(torch, ops, gen, device, pk["bf16_tflops"], args.steps)
+            extras["tc_gemm"] = measure_tc_gemm(torch, ops, gen, device, pk["bf16_tflops"], args.steps, pk["hbm_gbs"])
             extras["deltanet"] = measure_deltanet(torch, ops, gen, device, pk["hbm_gbs"], args.steps)
             extras["deltanet_layers"] = measure_deltanet_layers(torch, device, pk["hbm_gbs"], args.steps)
             extras["gated_attention"] = measure_gated_attention(torch, ops, gen, device, pk["hbm_gbs"], args.steps)

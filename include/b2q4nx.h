@@ -72,6 +72,8 @@ int b2_read_device_error(int* code, void* stream);
 #define B2_GEMV_ACCUMULATE 1 /* y += W x (residual add) instead of y = W x */
 #define B2_GEMV_PREFETCH 2   /* weights are not written by earlier kernels in the
                                 stream: they may be streamed before the PDL wait */
+#define B2_GEMM_PACKED 4     /* tensor-core GEMM only: the tiles are in the packed
+                                layout of b2_q4_gemm_pack */
 
 /* y[b][n] = sum_k W[n][k] x[b][k] for a q4nx q4 (W4A16) weight.
  *   tiles     [n_tile_rows][k_tiles][5120] bytes
@@ -306,13 +308,26 @@ int b2_gated_delta_step(const float* qkv, int ld_qkv, const float* z, int ld_z, 
  *   aligned (the staged fp16 x and exponents); not kept between calls.
  *   flags: B2_GEMV_ACCUMULATE (fp32 form); B2_GEMV_PREFETCH (the weights are not
  *   written by kernels in flight: their first stages stream, and are dequantised,
- *   before the wait on the preceding kernel).
+ *   before the wait on the preceding kernel); B2_GEMM_PACKED (tiles from
+ *   b2_q4_gemm_pack; A is dequantised into tensor memory).
  * Each call is two launches: a pre-pass that stages x (per token, one CTA) and the
  * GEMM.  The _rmsnorm forms read fp32 rows x [batch][ldx] (16-byte aligned, ldx % 4
  * == 0) and stage bf16(x * rsqrt(mean(x^2) + eps) * norm_w) in that pre-pass, as
  * b2_q4_gemv_rmsnorm does for the GEMV (designs/granite_gemv/granite_rmsnorm.h:45-80),
  * without a separate RMSNorm launch. */
 int b2_q4_gemm_workspace_size(int batch, int k_tiles, size_t* bytes);
+
+/* Packed layout for the tensor-core GEMM: the same codes and scales of a q4nx weight
+ * [n_tile_rows][k_tiles] (5120 bytes per tile in and out), reordered so that each
+ * weight row's codes for 32 consecutive k sit in 16 contiguous bytes (with that
+ * block's d and m beside them) and the two tile-rows of each pair are contiguous at
+ * every K-tile (one copy per pair).
+ * With B2_GEMM_PACKED the GEMM dequantises every row in one thread and writes A
+ * straight into tensor memory, where the tensor cores read it (no shared-memory pass
+ * for the dequantised weights).  Repack once per weight (a load-time step); a pure
+ * byte permutation, so results equal the GEMM on the original tiles.  Not in place.
+ * No reference counterpart: the reference reads the tiles as stored. */
+int b2_q4_gemm_pack(const uint8_t* tiles, int n_tile_rows, int k_tiles, uint8_t* packed, void* stream);
 int b2_q4_gemm(const uint8_t* tiles, int n_tile_rows, int k_tiles, const uint16_t* x, int batch, int ldx, float* y,
                int ldy, int flags, void* workspace, size_t workspace_bytes, void* stream);
 int b2_q4_swiglu_gemm(const uint8_t* gate, const uint8_t* up, int n_tile_rows, int k_tiles, const uint16_t* x,

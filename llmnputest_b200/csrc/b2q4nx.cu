@@ -519,8 +519,10 @@ int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_row
   if (ldx < k_tiles * 256 || ldx % (xf ? 4 : 8)) return fail(B2_ERR_ALIGN, "ldx %d: need >= K and aligned rows", ldx);
   if (ldy < n_tile_rows * 32) return fail(B2_ERR_ARG, "ldy %d < output rows %d", ldy, n_tile_rows * 32);
   if (!aligned(w0, 16) || (w1 && !aligned(w1, 16)) || !aligned(x, 16)) return fail(B2_ERR_ALIGN, "tiles and x must be 16-byte aligned");
-  if (flags & ~(B2_GEMV_ACCUMULATE | B2_GEMV_PREFETCH)) return fail(B2_ERR_ARG, "unknown flags 0x%x", flags);
+  if (flags & ~(B2_GEMV_ACCUMULATE | B2_GEMV_PREFETCH | B2_GEMM_PACKED))
+    return fail(B2_ERR_ARG, "unknown flags 0x%x", flags);
   if (epi == b2::kTcEpiSwiglu && (flags & B2_GEMV_ACCUMULATE)) return fail(B2_ERR_ARG, "SwiGLU output cannot accumulate");
+  const bool packed = (flags & B2_GEMM_PACKED) != 0;
   const size_t need = tc_ws_bytes(batch, k_tiles);
   if (!workspace || ws_bytes < need) return fail(B2_ERR_WORKSPACE, "workspace of %zu bytes needed", need);
   if (!aligned(workspace, 256)) return fail(B2_ERR_ALIGN, "workspace must be 256-byte aligned");
@@ -536,21 +538,40 @@ int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_row
       n_nsplit *= 2;  // columns per CTA stay a multiple of 16 (MMA N) and >= 64
   const int ncta = npad / n_nsplit;
   const int budget = di.smem_optin - 1024;  // alignment slack for the 1024-byte operand atoms
-  // pipeline: double-buffered A slices when they fit beside >= 2 raw and >= 2 x stages
   int raw_stages = 0, x_stages = 0, a_bufs = tuning().tc_abufs > 0 ? tuning().tc_abufs : 2;
-  const int max_raw = tuning().tc_raw > 0 ? tuning().tc_raw : 3;
   const int max_x = tuning().tc_xst > 0 ? tuning().tc_xst : 8;
-  for (; a_bufs >= 1 && x_stages < 2; --a_bufs) {
-    for (raw_stages = max_raw; raw_stages >= 2; --raw_stages) {
-      const b2::TcSmem base(ncta, raw_stages, 0, a_bufs);
-      x_stages = std::min(max_x, (budget - base.total) / (ncta * 128 + 16));
-      if (x_stages >= 2) break;
+  int smem = 0;
+  if (packed) {
+    // A lives in TMEM (two K-tile buffers): shared memory holds only the raw and x rings,
+    // so the raw ring can run deeper
+    // x stages are whole K-tiles: the deepest raw ring that leaves two of them
+    a_bufs = 2;
+    const int max_raw = tuning().tc_raw > 0 ? tuning().tc_raw : 6;
+    const int max_xp = tuning().tc_xst > 0 ? tuning().tc_xst : 4;
+    auto x_fit = [&](int rs) {
+      return std::min(max_xp, (budget - b2::TcSmem(ncta, rs, 0, 0, 4).total) / (4 * ncta * 128 + 16));
+    };
+    raw_stages = max_raw;
+    while (raw_stages > 2 && x_fit(raw_stages) < std::min(2, max_xp)) --raw_stages;
+    x_stages = x_fit(raw_stages);
+    if (x_stages < 1) return fail(B2_ERR_UNSUPPORTED, "shared memory too small for the tensor-core GEMM");
+    // more than half of an SM's shared memory: two of these CTAs (each allocating all
+    // 512 TMEM columns) are never resident on one SM
+    smem = std::max(b2::TcSmem(ncta, raw_stages, x_stages, 0, 4).total + 1024, di.smem_per_sm / 2 + 1024);
+  } else {
+    // pipeline: double-buffered A slices when they fit beside >= 2 raw and >= 2 x stages
+    const int max_raw = tuning().tc_raw > 0 ? tuning().tc_raw : 3;
+    for (; a_bufs >= 1 && x_stages < 2; --a_bufs) {
+      for (raw_stages = max_raw; raw_stages >= 2; --raw_stages) {
+        const b2::TcSmem base(ncta, raw_stages, 0, a_bufs);
+        x_stages = std::min(max_x, (budget - base.total) / (ncta * 128 + 16));
+        if (x_stages >= 2) break;
+      }
     }
+    ++a_bufs;  // undo the loop's last decrement
+    if (x_stages < 2) return fail(B2_ERR_UNSUPPORTED, "shared memory too small for the tensor-core GEMM");
+    smem = b2::TcSmem(ncta, raw_stages, x_stages, a_bufs).total + 1024;
   }
-  ++a_bufs;  // undo the loop's last decrement
-  if (x_stages < 2) return fail(B2_ERR_UNSUPPORTED, "shared memory too small for the tensor-core GEMM");
-  const int smem = b2::TcSmem(ncta, raw_stages, x_stages, a_bufs).total + 1024;
-  // split-K (fp32 form only) so that small projections still occupy every SM
   // split-K (fp32 form only) so that small projections still occupy every SM, in
   // one wave: row tiles x splits <= SMs
   int n_splits = 1, kt_per_split = k_tiles;
@@ -616,14 +637,21 @@ int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_row
   p.n_nsplit = n_nsplit;
   p.ncta = ncta;
   p.prefetch = (flags & B2_GEMV_PREFETCH) ? 1 : 0;
-  auto kernel = epi == b2::kTcEpiSwiglu ? b2::q4_gemm_tc_kernel<b2::kTcEpiSwiglu> : b2::q4_gemm_tc_kernel<b2::kTcEpiF32>;
-  static int attr_set[64][2] = {};
+  {
+    const int nc = ncta <= 32 ? 32 : (ncta <= 64 ? 64 : (ncta <= 128 ? 128 : 256));
+    p.d_bufs = (packed && 2 * nc > b2::kTcTmemACol) ? 1 : 2;
+  }
+  auto kernel = epi == b2::kTcEpiSwiglu
+                    ? (packed ? b2::q4_gemm_tc_kernel<b2::kTcEpiSwiglu, true> : b2::q4_gemm_tc_kernel<b2::kTcEpiSwiglu, false>)
+                    : (packed ? b2::q4_gemm_tc_kernel<b2::kTcEpiF32, true> : b2::q4_gemm_tc_kernel<b2::kTcEpiF32, false>);
+  static int attr_set[64][4] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!attr_set[dev][epi]) {
+  const int variant = epi * 2 + (packed ? 1 : 0);
+  if (!attr_set[dev][variant]) {
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, di.smem_optin);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tensor-core GEMM)");
-    attr_set[dev][epi] = 1;
+    attr_set[dev][variant] = 1;
   }
   cfg.gridDim = dim3(std::min(n_row_tiles * n_splits * n_nsplit, di.sms), 1, 1);
   cfg.blockDim = dim3(b2::kTcThreads, 1, 1);
@@ -1340,6 +1368,22 @@ int b2_q4_swiglu_gemm_rmsnorm(const uint8_t* gate, const uint8_t* up, int n_tile
                               void* workspace, size_t workspace_bytes, void* stream) {
   return tc_gemm_common(b2::kTcEpiSwiglu, gate, up, n_tile_rows, k_tiles, nullptr, batch, ldx, h, ldh, flags,
                         workspace, workspace_bytes, stream, x, norm_w, eps);
+}
+
+int b2_q4_gemm_pack(const uint8_t* tiles, int n_tile_rows, int k_tiles, uint8_t* packed, void* stream) {
+  DevInfo di;
+  int st = device_info(&di);
+  if (st != B2_OK) return st;
+  if (!tiles || !packed || n_tile_rows < 1 || k_tiles < 1) return fail(B2_ERR_ARG, "bad pack arguments");
+  const int64_t n_tiles = static_cast<int64_t>(n_tile_rows) * k_tiles;
+  if (!aligned(tiles, 16) || !aligned(packed, 16)) return fail(B2_ERR_ALIGN, "tiles and packed must be 16-byte aligned");
+  const uint8_t* in_end = tiles + n_tiles * b2::QTraits<b2::kQ4>::kTile;
+  const uint8_t* out_end = packed + n_tiles * b2::QTraits<b2::kQ4>::kTile;
+  if (tiles < out_end && packed < in_end) return fail(B2_ERR_ARG, "packing cannot run in place");
+  const int grid = static_cast<int>(std::min<int64_t>(n_tiles, 16LL * di.sms));
+  b2::tc_pack_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(tiles, packed, n_tile_rows, k_tiles);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? B2_OK : cuda_fail(e, "pack launch");
 }
 
 int b2_q4_dequant_tiles(const uint8_t* tiles, int64_t n_tiles, uint16_t* out, void* stream) {

@@ -26,6 +26,16 @@
 //                K-tile (raw ring -> A ring slot j)
 // Every mbarrier wait is bounded; on a timeout the kernel records an error,
 // stops issuing, waits (bounded) for the MMAs it issued, frees TMEM and exits.
+//
+// Packed form (TA): the same arithmetic from tiles repacked once per weight into a
+// lane-per-row layout (tc_pack_kernel below).  The dequant warps then decode their
+// own row with one conflict-free 16-byte load per 32 k and write A straight into
+// tensor memory (tcgen05.st, 32x32b: TMEM lane = weight row); tcgen05.mma reads A
+// from TMEM and only x from shared memory.  TMEM: columns 0-255 hold D (two
+// buffers of up to 128 columns, or one of 256), columns 256-511 two K-tile A
+// buffers of 128 columns (256 k as fp16 pairs).  Warp w (w % 4 = its TMEM lane
+// quarter = tile-row slot q) decodes k 128*h .. 128*h + 127 of each K-tile, h = 0
+// for warps 6-9 and 1 for warps 10-13.
 #pragma once
 
 #include "b2_common.cuh"
@@ -41,10 +51,33 @@ constexpr int kTcDqWarp0 = 6;
 constexpr int kTcMaxASlots = 8;              // per 64-k slice of a K-tile: 1 or 2 (double-buffered)
 constexpr int kTcASlotBytes = kTcM * 128;    // 128 rows x 64 fp16
 constexpr int kTcRawSlot = QTraits<kQ4>::kSlot;
+// packed form: tiles sit back to back in a raw stage (a tile-row pair is one copy; the
+// lane-per-row loads need no padding against bank conflicts)
+constexpr int kTcRawSlotPacked = QTraits<kQ4>::kTile;
 constexpr int kTcRawStage = 4 * kTcRawSlot;
 constexpr int kTcMaxN = 256;
 constexpr int kTcXchgStride = 33;            // SwiGLU exchange row stride in floats (bank spread)
 constexpr int kTcXchgBytes = 64 * kTcXchgStride * 4 + 256 * 4;  // 64 rows x 32 tokens, then 2^-e per token
+constexpr int kTcTmemACol = 256;             // packed form: first A column in TMEM
+constexpr int kTcTmemABuf = 128;             // packed form: columns per A buffer (one K-tile)
+
+// Packed weight: the tiles of a [n_tile_rows][k_tiles] weight reordered pair-major,
+// tile (tr, kt) at position (tr/2)*2*k_tiles + kt*np + tr%2 (np = tiles in tr's pair,
+// 2 or, for a last odd tile-row, 1), so that both tile-rows of a pair at one K-tile are
+// one contiguous copy; inside each tile (5120 bytes, same size as a q4nx tile), for 32
+// rows x 256 k:
+//   bytes    0..1023  scales: entry s*32 + l = bf16 d | bf16 m << 16 of row l, 32-k block s
+//   bytes 1024..5119  codes:  16 bytes at 1024 + (s*32 + l)*16 = row l, k 32s .. 32s+31 as
+//                     four words w; nibble i of word w is k = 32s + 8w + 2i (i < 4) or
+//                     32s + 8w + 2(i-4) + 1 (i >= 4), so (word >> 4p) & 0x000F000F holds
+//                     the codes of k = 32s + 8w + 2p and k + 1.
+__host__ __device__ constexpr int tc_packed_scale_off(int s, int l) { return (s * 32 + l) * 4; }
+__host__ __device__ inline long long tc_packed_tile(int tr, int kt, int n_tile_rows, int k_tiles) {
+  const int pr = tr >> 1;
+  const int np = (n_tile_rows - 2 * pr) >= 2 ? 2 : 1;
+  return static_cast<long long>(pr) * 2 * k_tiles + static_cast<long long>(kt) * np + (tr & 1);
+}
+__host__ __device__ constexpr int tc_packed_code_off(int s, int l) { return 1024 + (s * 32 + l) * 16; }
 
 enum TcEpi : int { kTcEpiF32 = 0, kTcEpiSwiglu = 1 };
 
@@ -68,14 +101,16 @@ struct TcParams {
   int ncta;         // token columns per CTA (npad / n_nsplit, a multiple of 16)
   int prefetch;     // the weights are constant: the first raw stages stream (and are
                     // dequantised) before the wait on the preceding kernel
+  int d_bufs;       // accumulator buffers in TMEM (2, or 1 for 256 columns in the packed form)
 };
 
 struct TcSmem {
   int a, x, raw, xchg, bar, total;
-  __host__ __device__ TcSmem(int npad, int raw_stages, int x_stages, int a_bufs) {
+  // x_slices: 64-k slices per x stage (1; packed form 4, a whole K-tile)
+  __host__ __device__ TcSmem(int npad, int raw_stages, int x_stages, int a_bufs, int x_slices = 1) {
     a = 0;  // 1024-aligned base (the kernel aligns the dynamic smem pointer)
     x = a + 4 * a_bufs * kTcASlotBytes;
-    raw = x + x_stages * npad * 128;
+    raw = x + x_stages * x_slices * npad * 128;
     xchg = raw + raw_stages * kTcRawStage;
     bar = (xchg + kTcXchgBytes + 15) & ~15;
     // raw full/empty, a full/empty, x full/empty, acc full/empty x2, done, tmem addr
@@ -107,6 +142,25 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uin
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D[tmem] (+)= A[tmem] * B[smem]^T, fp16 x fp16 -> fp32 (A: M lanes x 16 k as 8 columns)
+__device__ __forceinline__ void tc_mma_f16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// 16 consecutive columns of this thread's TMEM lane (32x32b shape: lane = thread of the warp)
+__device__ __forceinline__ void tmem_st32x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // arrive on `bar` once every MMA this thread issued so far has completed
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
@@ -306,12 +360,12 @@ __global__ void __launch_bounds__(256) tc_x_prep_kernel(const TcPrep a) {
 }
 
 // ------------------------------------------------------------ the GEMM
-template <int EPI>
+template <int EPI, bool TA>
 __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled operand slices
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  const TcSmem L(p.ncta, p.raw_stages, p.x_stages, p.a_bufs);
+  const TcSmem L(p.ncta, p.raw_stages, p.x_stages, TA ? 0 : p.a_bufs, TA ? 4 : 1);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar);
   const int RS = p.raw_stages, XS = p.x_stages;
   uint64_t* raw_full = bars;
@@ -329,6 +383,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int npad = p.npad, ncta = p.ncta;
   const uint32_t ncols = ncta <= 32 ? 32u : (ncta <= 64 ? 64u : (ncta <= 128 ? 128u : 256u));  // per buffer
+  const uint32_t tcols = TA ? 512u : 2 * ncols;  // TMEM columns allocated
+  const int DB = p.d_bufs;                       // accumulator buffers (1 or 2)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < RS; ++s) {
@@ -336,7 +392,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
       mbar_init(smem_u32(&raw_empty[s]), 8);  // the 8 dequant warps
     }
     for (int s = 0; s < kTcMaxASlots; ++s) {
-      mbar_init(smem_u32(&a_full[s]), 2);   // the dequant pair of slice s % 4, buffer s / 4
+      // the dequant pair of slice s % 4, buffer s / 4; packed form: all 8 dequant warps, buffer s
+      mbar_init(smem_u32(&a_full[s]), TA ? 8 : 2);
       mbar_init(smem_u32(&a_empty[s]), 1);  // [0..1]: buffer free again (tcgen05.commit per K-tile)
     }
     for (int s = 0; s < XS; ++s) {
@@ -352,7 +409,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), 2 * ncols);
+    tmem_alloc(smem_u32(tmem_slot), tcols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -392,45 +449,99 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
           src[j] = tr < p.n_tile_rows ? base + (static_cast<size_t>(tr) * KT + kt) * QTraits<kQ4>::kTile : nullptr;
           bytes += src[j] ? QTraits<kQ4>::kTile : 0;
         }
-        mbar_arrive_expect_tx(smem_u32(&raw_full[rs]), bytes);
         const uint32_t dst = smem_u32(smem + L.raw + rs * kTcRawStage);
+        if constexpr (TA) {
+          // packed: slots 0-1 and 2-3 are each one tile-row pair, contiguous at this K-tile
+          mbar_arrive_expect_tx(smem_u32(&raw_full[rs]), bytes);
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          if (src[j]) bulk_g2s(dst + j * kTcRawSlot, src[j], QTraits<kQ4>::kTile, smem_u32(&raw_full[rs]), policy);
+          for (int h = 0; h < 2; ++h) {
+            const uint8_t* b = EPI == kTcEpiSwiglu ? (h ? p.w1 : p.w0) : p.w0;
+            const int tr0 = EPI == kTcEpiSwiglu ? tile * 2 : tile * 4 + 2 * h;
+            if (tr0 >= p.n_tile_rows) continue;
+            const int np = p.n_tile_rows - tr0 >= 2 ? 2 : 1;
+            bulk_g2s(dst + 2 * h * kTcRawSlotPacked, b + tc_packed_tile(tr0, kt, p.n_tile_rows, KT) * QTraits<kQ4>::kTile,
+                     np * QTraits<kQ4>::kTile, smem_u32(&raw_full[rs]), policy);
+          }
+        } else {
+          mbar_arrive_expect_tx(smem_u32(&raw_full[rs]), bytes);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (src[j]) bulk_g2s(dst + j * kTcRawSlot, src[j], QTraits<kQ4>::kTile, smem_u32(&raw_full[rs]), policy);
+        }
       };
-      // with prefetch, the first RS raw stages go out before the wait on the preceding
-      // kernel (the dequant warps need nothing else), the x slices only after it
-      uint32_t n_pre = 0;
-      if (p.prefetch) {
-        for (int it = blockIdx.x; it < n_items && n_pre < static_cast<uint32_t>(RS); it += gridDim.x)
-          for (int kt = item_k0(it); kt < item_k1(it) && n_pre < static_cast<uint32_t>(RS); ++kt, ++n_pre)
-            issue_raw(item_tile(it), kt, static_cast<int>(n_pre));
-      }
+      // The raw ring (per K-tile) and the x ring (per 64-k slice) advance independently:
+      // each is refilled as soon as its consumers free a slot, so the raw prefetch runs
+      // the full ring ahead of the MMAs instead of waiting behind x slots.  With prefetch
+      // the first RS raw stages go out before the wait on the preceding kernel (the
+      // dequant warps need nothing else), the x slices only after it.
+      int it_r = blockIdx.x, kt_r = it_r < n_items ? item_k0(it_r) : 0;  // raw cursor
+      uint32_t r_next = 0, n_k = 0;
+      for (int it = blockIdx.x; it < n_items; it += gridDim.x) n_k += static_cast<uint32_t>(item_k1(it) - item_k0(it));
+      auto advance_r = [&]() {
+        if (++kt_r == item_k1(it_r)) {
+          it_r += gridDim.x;
+          if (it_r < n_items) kt_r = item_k0(it_r);
+        }
+        ++r_next;
+      };
+      if (p.prefetch)
+        while (r_next < n_k && r_next < static_cast<uint32_t>(RS)) {
+          issue_raw(item_tile(it_r), kt_r, static_cast<int>(r_next));
+          advance_r();
+        }
       pdl_wait();  // x image comes from the pre-pass
-      uint32_t rseq = 0, xseq = 0;
-      for (int it = blockIdx.x; it < n_items && !*abort_flag; it += gridDim.x) {
-        const int tile = item_tile(it);
-        for (int kt = item_k0(it); kt < item_k1(it); ++kt, ++rseq) {
-          const int rs = rseq % RS;
-          if (rseq >= n_pre) {
-            if (rseq >= static_cast<uint32_t>(RS) &&
-                !mbar_wait_bounded(smem_u32(&raw_empty[rs]), ((rseq / RS) & 1) ^ 1, abort_flag, kDevTimeoutEmpty))
-              break;
-            issue_raw(tile, kt, rs);
-          }
-          for (int js = 0; js < 4; ++js, ++xseq) {
-            const int xs = xseq % XS;
-            if (xseq >= static_cast<uint32_t>(XS) &&
-                !mbar_wait_bounded(smem_u32(&x_empty[xs]), ((xseq / XS) & 1) ^ 1, abort_flag, kDevTimeoutEmpty))
-              break;
-            // this CTA's token rows n0.. of the slice: contiguous, and their swizzle
-            // pattern is the slice's (n0 is a multiple of 8 rows)
-            const uint32_t xbytes = static_cast<uint32_t>(ncta) * 128;
-            mbar_arrive_expect_tx(smem_u32(&x_full[xs]), xbytes);
-            bulk_g2s(smem_u32(smem + L.x + xs * xbytes),
-                     p.xsw + (static_cast<size_t>(kt * 4 + js) * npad + item_n0(it)) * 128, xbytes,
+      int it_x = blockIdx.x, kt_x = it_x < n_items ? item_k0(it_x) : 0, js_x = 0;  // x cursor
+      uint32_t x_next = 0;
+      // stages: one 64-k slice, or (packed form) the four slices of a K-tile
+      const uint32_t n_x = TA ? n_k : 4 * n_k;
+      const uint32_t xbytes = static_cast<uint32_t>(ncta) * 128;
+      const uint32_t xstage = TA ? 4 * xbytes : xbytes;
+      uint64_t t_prog = globaltimer();
+      while ((r_next < n_k || x_next < n_x) && !*abort_flag) {
+        bool progressed = false;
+        while (r_next < n_k) {
+          const int rs = static_cast<int>(r_next % RS);
+          if (r_next >= static_cast<uint32_t>(RS) && !mbar_test_wait(smem_u32(&raw_empty[rs]), ((r_next / RS) & 1) ^ 1))
+            break;
+          issue_raw(item_tile(it_r), kt_r, rs);
+          advance_r();
+          progressed = true;
+        }
+        while (x_next < n_x) {
+          const int xs = static_cast<int>(x_next % XS);
+          if (x_next >= static_cast<uint32_t>(XS) && !mbar_test_wait(smem_u32(&x_empty[xs]), ((x_next / XS) & 1) ^ 1))
+            break;
+          // this CTA's token rows n0.. of the slice: contiguous, and their swizzle
+          // pattern is the slice's (n0 is a multiple of 8 rows)
+          mbar_arrive_expect_tx(smem_u32(&x_full[xs]), xstage);
+          if (TA && ncta == npad) {  // the K-tile's four slices are contiguous in the image
+            bulk_g2s(smem_u32(smem + L.x + xs * xstage), p.xsw + static_cast<size_t>(kt_x) * 4 * npad * 128, xstage,
                      smem_u32(&x_full[xs]), keep);
+          } else {
+            const int nsl = TA ? 4 : 1;
+            for (int j = 0; j < nsl; ++j)
+              bulk_g2s(smem_u32(smem + L.x + xs * xstage + j * xbytes),
+                       p.xsw + (static_cast<size_t>(kt_x * 4 + js_x + j) * npad + item_n0(it_x)) * 128, xbytes,
+                       smem_u32(&x_full[xs]), keep);
           }
+          if (TA) js_x = 3;  // a whole K-tile per stage
+          if (++js_x == 4) {
+            js_x = 0;
+            if (++kt_x == item_k1(it_x)) {
+              it_x += gridDim.x;
+              if (it_x < n_items) kt_x = item_k0(it_x);
+            }
+          }
+          ++x_next;
+          progressed = true;
+        }
+        if (progressed) {
+          t_prog = globaltimer();
+        } else if (globaltimer() - t_prog > B2_WAIT_TIMEOUT_NS) {
+          *abort_flag = 1;
+          record_error(kDevTimeoutEmpty);
+        } else {
+          __nanosleep(64);  // leave the issue slots to the dequant warps between probes
         }
       }
     }
@@ -447,12 +558,35 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
       const uint32_t xbytes = static_cast<uint32_t>(ncta) * 128;
       bool issued_any = false;
       for (int it = blockIdx.x; it < n_items && !*abort_flag; it += gridDim.x, ++t_it) {
-        const int buf = t_it & 1;
-        if (t_it >= 2)
-          mbar_wait_bounded(smem_u32(&acc_empty[buf]), ((t_it >> 1) & 1) ^ 1, abort_flag, kDevTimeoutEmpty);
+        const int buf = DB == 2 ? static_cast<int>(t_it & 1) : 0;
+        const uint32_t uses = DB == 2 ? t_it >> 1 : t_it;  // earlier items on this buffer
+        if (t_it >= static_cast<uint32_t>(DB))
+          mbar_wait_bounded(smem_u32(&acc_empty[buf]), (uses & 1) ^ 1, abort_flag, kDevTimeoutEmpty);
         const uint32_t d_tmem = tmem_base + buf * ncols;
         const int k0 = item_k0(it), k1 = item_k1(it);
         for (int kt = k0; kt < k1; ++kt) {
+          if constexpr (TA) {
+            // A of this K-tile in TMEM (all 8 dequant warps), then the x slices; a
+            // failed wait has set the abort flag, checked below
+            if (mbar_wait_bounded(smem_u32(&a_full[ab]), aph, abort_flag, kDevTimeoutFull) &&
+                mbar_wait_bounded(smem_u32(&x_full[xs]), xph, abort_flag, kDevTimeoutFull)) {
+              tc_fence_after();
+              const uint32_t a_tmem = tmem_base + kTcTmemACol + ab * kTcTmemABuf;
+#pragma unroll
+              for (int js = 0; js < 4; ++js) {
+                const uint64_t bd = umma_desc_sw128(x0 + (4 * xs + js) * xbytes);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)  // 16 k = 8 TMEM columns of A; +32 bytes along K of x
+                  tc_mma_f16_ta(d_tmem, a_tmem + js * 32 + kk * 8, bd + 2 * kk, idesc, ((kt - k0) | js | kk) != 0);
+              }
+              issued_any = true;
+              tc_commit(smem_u32(&x_empty[xs]));
+              if (++xs == XS) {
+                xs = 0;
+                xph ^= 1;
+              }
+            }
+          } else {
           for (int js = 0; js < 4; ++js) {
             const bool ok_a = mbar_wait_bounded(smem_u32(&a_full[4 * ab + js]), aph, abort_flag, kDevTimeoutFull);
             const bool ok_x = mbar_wait_bounded(smem_u32(&x_full[xs]), xph, abort_flag, kDevTimeoutFull);
@@ -469,6 +603,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
               xs = 0;
               xph ^= 1;
             }
+          }
           }
           if (*abort_flag) break;
           tc_commit(smem_u32(&a_empty[ab]));
@@ -505,29 +640,30 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
     for (int it = blockIdx.x; it < n_items; it += gridDim.x, ++t_it) {
       const int tile = item_tile(it);
       const int n0 = item_n0(it);
-      const int buf = t_it & 1;
-      const bool ok = mbar_wait_bounded(smem_u32(&acc_full[buf]), (t_it >> 1) & 1, abort_flag, kDevTimeoutFull);
+      const int buf = DB == 2 ? static_cast<int>(t_it & 1) : 0;
+      const uint32_t uses = DB == 2 ? t_it >> 1 : t_it;
+      const bool ok = mbar_wait_bounded(smem_u32(&acc_full[buf]), uses & 1, abort_flag, kDevTimeoutFull);
       tc_fence_after();
       const uint32_t t_row = tmem_base + buf * ncols + (static_cast<uint32_t>(q * 32) << 16);
       for (int c0 = n0; c0 < n0 + ncta; c0 += 32) {  // c0: global token column
         uint32_t r[32];
         tmem_ld32(t_row + (c0 - n0), r);
-        // the 32 columns' x scales (shared table), read before any store below
-        float u2v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) u2v[j] = inv_sc[c0 + j];
         if (EPI == kTcEpiF32) {
           const int tr = tile * 4 + (row_local >> 5);
           const int grow = tile * kTcM + row_local;
           if (ok && !*abort_flag && tr < p.n_tile_rows) {
             float* y = static_cast<float*>(p.y) + grow;
-            if (p.n_splits > 1) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j)  // zeroed by the pre-pass unless accumulating
-                if (c0 + j < p.batch) atomicAdd(y + static_cast<size_t>(c0 + j) * p.ldy, __uint_as_float(r[j]) * u2v[j]);
-            } else {
+            for (int hh = 0; hh < 32; hh += 16) {
+              float u2v[16];  // the half's x scales (shared table)
 #pragma unroll
-              for (int hh = 0; hh < 32; hh += 16) {
+              for (int j = 0; j < 16; ++j) u2v[j] = inv_sc[c0 + hh + j];
+              if (p.n_splits > 1) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j)  // zeroed by the pre-pass unless accumulating
+                  if (c0 + hh + j < p.batch)
+                    atomicAdd(y + static_cast<size_t>(c0 + hh + j) * p.ldy, __uint_as_float(r[hh + j]) * u2v[j]);
+              } else {
                 float old[16];  // the half's loads before its first store (no load waits behind a store)
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
@@ -535,11 +671,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
 #pragma unroll
                 for (int j = 0; j < 16; ++j)
                   if (c0 + hh + j < p.batch)
-                    y[static_cast<size_t>(c0 + hh + j) * p.ldy] = old[j] + __uint_as_float(r[hh + j]) * u2v[hh + j];
+                    y[static_cast<size_t>(c0 + hh + j) * p.ldy] = old[j] + __uint_as_float(r[hh + j]) * u2v[j];
               }
             }
           }
         } else {
+          // the 32 columns' x scales (shared table), read before any store below
+          float u2v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) u2v[j] = inv_sc[c0 + j];
           // rows 0-63 gate, 64-127 the matching up rows.  Gate warps finish columns
           // 0-15 of the chunk and up warps columns 16-31: each hands the other half
           // of its values over (disjoint columns of the exchange rows).  Indices stay
@@ -589,6 +729,57 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&acc_empty[buf]));
+    }
+  } else if constexpr (TA) {
+    // ------------------------------------------------- dequant, packed form
+    // warp w: TMEM lane quarter q = w % 4 = tile-row slot q of the raw stage, row = lane;
+    // half hh of each K-tile: 32-k blocks 4 hh .. 4 hh + 3 (TMEM columns 64 hh ..)
+    const int q = warp & 3;
+    const int hh = (warp - kTcDqWarp0) >> 2;
+    const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
+    uint32_t rseq = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+      for (int kt = item_k0(it); kt < item_k1(it); ++kt, ++rseq) {
+        const int rs = rseq % RS;
+        const int abuf = static_cast<int>(rseq % AB);
+        ok = ok && mbar_wait_bounded(smem_u32(&raw_full[rs]), (rseq / RS) & 1, abort_flag, kDevTimeoutFull);
+        if (rseq >= static_cast<uint32_t>(AB))
+          ok = ok && mbar_wait_bounded(smem_u32(&a_empty[abuf]), ((rseq / AB) & 1) ^ 1, abort_flag,
+                                       kDevTimeoutEmpty);
+        ok = __all_sync(0xffffffffu, ok);  // the TMEM stores below are warp-collective
+        if (ok) {
+          tc_fence_after();  // the MMAs that read this A buffer have completed
+          const uint8_t* tl = smem + L.raw + rs * kTcRawStage + q * kTcRawSlotPacked;
+          const uint32_t a_col = tmem_base + t_lane + kTcTmemACol + abuf * kTcTmemABuf;
+#pragma unroll
+          for (int sb = 0; sb < 4; ++sb) {
+            const int s = 4 * hh + sb;  // 32-k block of the K-tile
+            const uint32_t sc = *reinterpret_cast<const uint32_t*>(tl + tc_packed_scale_off(s, lane));
+            const uint4 nv = *reinterpret_cast<const uint4*>(tl + tc_packed_code_off(s, lane));
+            const float dv = bf16lo_to_f32(sc), mv = bf16hi_to_f32(sc);
+            const __half2 d2 = __floats2half2_rn(dv, dv), m2 = __floats2half2_rn(mv, mv);
+            const uint32_t wv[4] = {nv.x, nv.y, nv.z, nv.w};
+            uint32_t a[16];
+#pragma unroll
+            for (int w = 0; w < 4; ++w)
+#pragma unroll
+              for (int pp = 0; pp < 4; ++pp) {
+                const uint32_t code = f16x2_sub(lop3<kLutAndOr>(wv[w] >> (4 * pp), 0x000F000Fu, 0x64006400u), 0x64006400u);
+                const __half2 wh = __hfma2(*reinterpret_cast<const __half2*>(&code), d2, m2);
+                a[4 * w + pp] = *reinterpret_cast<const uint32_t*>(&wh);
+              }
+            tmem_st32x16(a_col + s * 16, a);
+          }
+          tmem_wait_st();
+          tc_fence_before();
+        }
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(smem_u32(&a_full[abuf]));
+          mbar_arrive(smem_u32(&raw_empty[rs]));
+        }
+      }
     }
   } else {
     // ------------------------------------------------------------ dequant
@@ -664,7 +855,37 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 2 * ncols);
+    tmem_dealloc(tmem_base, tcols);
+  }
+}
+
+// ------------------------------------------------------------ packing
+// q4nx weight -> packed weight (the layout above): one CTA of 256 threads per tile,
+// thread (s, l) = (threadIdx.x / 32, threadIdx.x % 32) writes row l's 32-k block s.
+// A pure byte permutation: every code, d and m keeps its bits.
+__global__ void __launch_bounds__(256) tc_pack_kernel(const uint8_t* __restrict__ in, uint8_t* __restrict__ out,
+                                                      int n_tile_rows, int k_tiles) {
+  const int s = threadIdx.x >> 5, l = threadIdx.x & 31;
+  const int rb = l >> 4, r = l & 15;
+  const long long n_tiles = static_cast<long long>(n_tile_rows) * k_tiles;
+  for (long long t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+    const int tr = static_cast<int>(t / k_tiles), kt = static_cast<int>(t % k_tiles);
+    const uint8_t* ti = in + t * QTraits<kQ4>::kTile;
+    uint8_t* to = out + tc_packed_tile(tr, kt, n_tile_rows, k_tiles) * QTraits<kQ4>::kTile;
+    const uint16_t* dm = reinterpret_cast<const uint16_t*>(ti);
+    const uint32_t d = dm[s * 32 + l], m = dm[256 + s * 32 + l];  // entry (k/32)*32 + row
+    *reinterpret_cast<uint32_t*>(to + tc_packed_scale_off(s, l)) = d | (m << 16);
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {  // k = 32 s + j
+      const int k = 32 * s + j;
+      const int i = rb * 4096 + k * 16 + r;  // nibble index in the q4nx tile
+      const uint32_t code = (ti[1024 + (i >> 1)] >> ((i & 1) * 4)) & 0xFu;
+      const int wi = j >> 3, jj = j & 7;
+      const int pos = (jj & 1) ? 4 + (jj >> 1) : (jj >> 1);
+      w[wi] |= code << (4 * pos);
+    }
+    *reinterpret_cast<uint4*>(to + tc_packed_code_off(s, l)) = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 

@@ -76,11 +76,17 @@ def synth_q8(n_tiles: int, gen: torch.Generator, device) -> torch.Tensor:
     return w.reshape(-1)
 
 
+def pack_projections(layer: dict, shapes: dict) -> dict:
+    """One layer's q4 projections in the tensor-core GEMM's packed layout (a load-time
+    step); shapes maps each projection to its (n_tile_rows, k_tiles)."""
+    return {k: ops.q4_gemm_pack(layer[k], *shape) for k, shape in shapes.items()}
+
+
 class Q4Decoder:
     """Resident weights, KV cache and buffers for batched decode; `step()` is graph-capturable."""
 
     def __init__(self, cfg: DecoderConfig, batch: int, ctx_max: int, device=None, seed: int = 0,
-                 weights: dict | None = None, gemm_min_batch: int = 9):
+                 weights: dict | None = None, gemm_min_batch: int = 9, pack_gemm: bool = True):
         self.cfg = cfg
         self.batch = batch
         self.ctx_max = ctx_max
@@ -119,6 +125,12 @@ class Q4Decoder:
             self.gemm_ws_raw = torch.empty(nbytes + 256, dtype=torch.uint8, device=dev)
             off = (256 - self.gemm_ws_raw.data_ptr() % 256) % 256
             self.gemm_ws = self.gemm_ws_raw[off:off + nbytes]
+        # the GEMM's projections repacked once (b2_q4_gemm_pack): A is dequantised into TMEM
+        self.packed = self.use_gemm and pack_gemm
+        shapes = {"qkv": (self.nt_qkv, self.kt_h), "o": (self.nt_h, self.kt_q), "gate": (self.nt_i, self.kt_h),
+                  "up": (self.nt_i, self.kt_h), "down": (self.nt_h, self.kt_i)}
+        self.wg = ([pack_projections(L, shapes) if self.packed else L for L in self.w["layers"]]
+                   if self.use_gemm else None)
 
     def _synthetic(self, seed: int) -> dict:
         c, dev = self.cfg, self.device
@@ -171,25 +183,28 @@ class Q4Decoder:
         return self.logits
 
     def _step_gemm(self) -> torch.Tensor:
-        """Large-batch step: tcgen05 GEMMs for every projection, RMSNorm fused into their x pre-pass."""
+        """Large-batch step: tcgen05 GEMMs for every projection (packed weights, A in TMEM),
+        RMSNorm fused into their x pre-pass."""
         c = self.cfg
         d = c.head_dim
         qd, kd = c.n_heads * d, c.n_kv_heads * d
         ws = self.gemm_ws
+        pk = self.packed
         for li, L in enumerate(self.w["layers"]):
+            G = self.wg[li]
             # RMSNorm fused into the GEMMs' x pre-pass; weights stream before each PDL wait
-            ops.q4_gemm(L["qkv"], self.nt_qkv, self.kt_h, self.resid, out=self.qkv, workspace=ws, prefetch=True,
-                        norm_w=L["attn_norm"], eps=c.rms_eps)
+            ops.q4_gemm(G["qkv"], self.nt_qkv, self.kt_h, self.resid, out=self.qkv, workspace=ws, prefetch=True,
+                        norm_w=L["attn_norm"], eps=c.rms_eps, packed=pk)
             ops.gqa_decode(self.qkv[:, :qd], self.qkv[:, qd:qd + kd], self.qkv[:, qd + kd:],
                            self.k_cache[li], self.v_cache[li], self.pos, n_q_heads=c.n_heads,
                            n_kv_heads=c.n_kv_heads, theta=c.rope_theta, scale=d ** -0.5, max_len=self.ctx_max,
                            out=self.attn, workspace=self.attn_ws, prefetch_kv=True)
-            ops.q4_gemm(L["o"], self.nt_h, self.kt_q, self.attn, out=self.resid, accumulate=True, workspace=ws,
-                        prefetch=True)
-            ops.q4_swiglu_gemm(L["gate"], L["up"], self.nt_i, self.kt_h, self.resid, out=self.h, workspace=ws,
-                               prefetch=True, norm_w=L["mlp_norm"], eps=c.rms_eps)
-            ops.q4_gemm(L["down"], self.nt_h, self.kt_i, self.h, out=self.resid, accumulate=True, workspace=ws,
-                        prefetch=True)
+            ops.q4_gemm(G["o"], self.nt_h, self.kt_q, self.attn, out=self.resid, accumulate=True, workspace=ws,
+                        prefetch=True, packed=pk)
+            ops.q4_swiglu_gemm(G["gate"], G["up"], self.nt_i, self.kt_h, self.resid, out=self.h, workspace=ws,
+                               prefetch=True, norm_w=L["mlp_norm"], eps=c.rms_eps, packed=pk)
+            ops.q4_gemm(G["down"], self.nt_h, self.kt_i, self.h, out=self.resid, accumulate=True, workspace=ws,
+                        prefetch=True, packed=pk)
         ops.gemv_rmsnorm(self.w["lm_head"], self.nt_v, self.kt_h, self.resid, self.w["final_norm"], c.rms_eps,
                          out=self.logits, q8=True)
         return self.logits

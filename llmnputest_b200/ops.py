@@ -15,6 +15,7 @@ from .format import Q4_TILE_BYTES, Q8_TILE_BYTES, TILE_K, TILE_ROWS
 
 GEMV_ACCUMULATE = 1
 GEMV_PREFETCH = 2
+GEMM_PACKED = 4
 
 
 def _stream() -> ctypes.c_void_p:
@@ -129,13 +130,27 @@ def _aligned_ws(ws: torch.Tensor) -> ctypes.c_void_p:
     return ctypes.c_void_p((ws.data_ptr() + 255) // 256 * 256)
 
 
+def q4_gemm_pack(tiles: torch.Tensor, n_tile_rows: int, k_tiles: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """The packed layout of a q4nx weight [n_tile_rows][k_tiles] for the tensor-core GEMM
+    (b2_q4_gemm_pack): same size, every code and scale kept, reordered lane-per-row and
+    tile-row-pair-major.  A load-time step."""
+    _tiles(tiles, n_tile_rows, k_tiles, Q4_TILE_BYTES, "tiles")
+    if out is None:
+        out = torch.empty_like(tiles)
+    if out.shape != tiles.shape or out.dtype != torch.uint8:
+        raise ValueError("out must match tiles")
+    _native.call("b2_q4_gemm_pack", _ptr(tiles), n_tile_rows, k_tiles, _ptr(out), _stream())
+    return out
+
+
 def q4_gemm(tiles: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tensor, out: torch.Tensor | None = None,
             accumulate: bool = False, workspace: torch.Tensor | None = None, prefetch: bool = False,
-            norm_w: torch.Tensor | None = None, eps: float = 0.0) -> torch.Tensor:
+            norm_w: torch.Tensor | None = None, eps: float = 0.0, packed: bool = False) -> torch.Tensor:
     """fp32 y [B, N] = W x on the tcgen05 tensor cores (batches up to 256).
 
     With norm_w, x is the fp32 residual [B, K] and the GEMM multiplies
-    bf16(rmsnorm(x) * norm_w), the norm done in its x pre-pass (b2_q4_gemm_rmsnorm)."""
+    bf16(rmsnorm(x) * norm_w), the norm done in its x pre-pass (b2_q4_gemm_rmsnorm).
+    packed: the tiles come from q4_gemm_pack (A is dequantised into tensor memory)."""
     _tiles(tiles, n_tile_rows, k_tiles, Q4_TILE_BYTES, "tiles")
     k, n = k_tiles * TILE_K, n_tile_rows * TILE_ROWS
     x2 = _norm_in(x, norm_w, k) if norm_w is not None else _x2d(x, k)
@@ -144,7 +159,7 @@ def q4_gemm(tiles: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tensor
         out = torch.zeros((b, n), dtype=torch.float32, device=x2.device)
     _need(out, "out", torch.float32)
     ws = _gemm_ws(workspace, b, k_tiles, x2.device)
-    flags = (GEMV_ACCUMULATE if accumulate else 0) | (GEMV_PREFETCH if prefetch else 0)
+    flags = (GEMV_ACCUMULATE if accumulate else 0) | (GEMV_PREFETCH if prefetch else 0) | (GEMM_PACKED if packed else 0)
     wsp = _aligned_ws(ws) if workspace is None else _ptr(ws)
     wsn = ws.numel() - (256 if workspace is None else 0)
     if norm_w is not None:
@@ -158,9 +173,10 @@ def q4_gemm(tiles: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tensor
 
 def q4_swiglu_gemm(gate: torch.Tensor, up: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tensor,
                    out: torch.Tensor | None = None, workspace: torch.Tensor | None = None, prefetch: bool = False,
-                   norm_w: torch.Tensor | None = None, eps: float = 0.0) -> torch.Tensor:
+                   norm_w: torch.Tensor | None = None, eps: float = 0.0, packed: bool = False) -> torch.Tensor:
     """bf16 h = silu(bf16(G x)) * bf16(U x) on the tensor cores (batches up to 256); with
-    norm_w, x is the fp32 residual and its RMSNorm is fused (b2_q4_swiglu_gemm_rmsnorm)."""
+    norm_w, x is the fp32 residual and its RMSNorm is fused (b2_q4_swiglu_gemm_rmsnorm).
+    packed: gate and up come from q4_gemm_pack."""
     _tiles(gate, n_tile_rows, k_tiles, Q4_TILE_BYTES, "gate")
     _tiles(up, n_tile_rows, k_tiles, Q4_TILE_BYTES, "up")
     k, n = k_tiles * TILE_K, n_tile_rows * TILE_ROWS
@@ -170,7 +186,7 @@ def q4_swiglu_gemm(gate: torch.Tensor, up: torch.Tensor, n_tile_rows: int, k_til
         out = torch.empty((b, n), dtype=torch.bfloat16, device=x2.device)
     _need(out, "out", torch.bfloat16)
     ws = _gemm_ws(workspace, b, k_tiles, x2.device)
-    flags = GEMV_PREFETCH if prefetch else 0
+    flags = (GEMV_PREFETCH if prefetch else 0) | (GEMM_PACKED if packed else 0)
     wsp = _aligned_ws(ws) if workspace is None else _ptr(ws)
     wsn = ws.numel() - (256 if workspace is None else 0)
     if norm_w is not None:

@@ -207,6 +207,11 @@ class TPDecoder:
             self.gemm_ws_raw = torch.empty(nbytes + 256, dtype=torch.uint8, device=dev)
             off = (256 - self.gemm_ws_raw.data_ptr() % 256) % 256
             self.gemm_ws = self.gemm_ws_raw[off:off + nbytes]
+            # this rank's projection shards repacked once for the GEMM (A dequantised into TMEM)
+            shapes = {"qkv": (self.nt_qkv_local, self.kt_h), "o": (self.nt_o_local, self.kt_q),
+                      "gate": (self.nt_i_local, self.kt_h), "up": (self.nt_i_local, self.kt_h),
+                      "down": (cfg.hidden // TILE_ROWS, self.kt_i_local)}
+            self.wg = [{k: self.ops.q4_gemm_pack(L[k], *shp) for k, shp in shapes.items()} for L in self.w["layers"]]
 
     def close(self) -> None:
         """Release the peer mappings (every rank, after its last step)."""
@@ -263,9 +268,10 @@ class TPDecoder:
         ws = self.gemm_ws if self.use_gemm else None
         self.resid.copy_(self.x_in)
         for li, L in enumerate(self.w["layers"]):
+            G = self.wg[li] if self.use_gemm else None
             if self.use_gemm:
-                ops.q4_gemm(L["qkv"], self.nt_qkv_local, self.kt_h, self.resid, out=self.qkv, workspace=ws,
-                            prefetch=True, norm_w=L["attn_norm"], eps=c.rms_eps)
+                ops.q4_gemm(G["qkv"], self.nt_qkv_local, self.kt_h, self.resid, out=self.qkv, workspace=ws,
+                            prefetch=True, norm_w=L["attn_norm"], eps=c.rms_eps, packed=True)
             else:
                 ops.gemv_rmsnorm(L["qkv"], self.nt_qkv_local, self.kt_h, self.resid, L["attn_norm"], c.rms_eps,
                                  out=self.qkv, prefetch=True)
@@ -275,15 +281,16 @@ class TPDecoder:
                            workspace=self.attn_ws, prefetch_kv=True)
             a = self._gather_heads()
             if self.use_gemm:
-                ops.q4_gemm(L["o"], self.nt_o_local, self.kt_q, a, out=self.o_local, workspace=ws, prefetch=True)
+                ops.q4_gemm(G["o"], self.nt_o_local, self.kt_q, a, out=self.o_local, workspace=ws, prefetch=True,
+                            packed=True)
             else:
                 ops.q4_gemv(L["o"], self.nt_o_local, self.kt_q, a, out=self.o_local, prefetch=True)
             self._add_o_rows()
             if self.use_gemm:
-                ops.q4_swiglu_gemm(L["gate"], L["up"], self.nt_i_local, self.kt_h, self.resid, out=self.h,
-                                   workspace=ws, prefetch=True, norm_w=L["mlp_norm"], eps=c.rms_eps)
-                ops.q4_gemm(L["down"], c.hidden // TILE_ROWS, self.kt_i_local, self.h, out=self.down, workspace=ws,
-                            prefetch=True)
+                ops.q4_swiglu_gemm(G["gate"], G["up"], self.nt_i_local, self.kt_h, self.resid, out=self.h,
+                                   workspace=ws, prefetch=True, norm_w=L["mlp_norm"], eps=c.rms_eps, packed=True)
+                ops.q4_gemm(G["down"], c.hidden // TILE_ROWS, self.kt_i_local, self.h, out=self.down, workspace=ws,
+                            prefetch=True, packed=True)
             else:
                 ops.swiglu_gemv_rmsnorm(L["gate"], L["up"], self.nt_i_local, self.kt_h, self.resid, L["mlp_norm"],
                                         c.rms_eps, out=self.h, prefetch=True)

@@ -191,3 +191,64 @@ def test_gemm_fused_rmsnorm_and_prefetch(cuda, n_t, k_t, bsz, swiglu):
     else:
         _check(fused.cpu().numpy(), orc.gemv_q4(g, xr, n_t, k_t), what="vs oracle")
     assert ops.device_error() == 0
+
+
+# ------------------------------------------------------------ packed form
+def test_device_pack_matches_layout(cuda):
+    """b2_q4_gemm_pack against the numpy statement of the packed layout, byte for byte."""
+    from llmnputest_b200 import ops
+    from tests import gemm_pack_layout as gpl
+    rng = np.random.default_rng(5)
+    for n_t, k_t in ((7, 5), (4, 1), (1, 3)):
+        tiles = orc.synth_q4_tiles(rng, n_t * k_t)
+        got = ops.q4_gemm_pack(dev_u8(tiles), n_t, k_t)
+        torch.cuda.synchronize()
+        assert np.array_equal(got.cpu().numpy().reshape(tiles.shape), gpl.pack(tiles, n_t, k_t)), (n_t, k_t)
+
+
+# (n_t, k_t, batch, form): split-K, odd shapes, one token, 256 tokens (one accumulator
+# buffer of 256 TMEM columns), accumulate, fused norm, SwiGLU with and without the
+# column split
+@pytest.mark.parametrize("n_t,k_t,bsz,form", [
+    (112, 10, 32, "f32"), (80, 32, 32, "acc"), (7, 3, 17, "f32"), (4, 4, 1, "f32"), (12, 10, 256, "f32"),
+    (112, 10, 32, "norm"), (256, 10, 32, "swiglu"), (14, 4, 256, "swiglu"), (30, 10, 9, "swiglu_norm")])
+def test_packed_gemm_equals_gemm(cuda, n_t, k_t, bsz, form):
+    """The packed form (A dequantised into tensor memory) multiplies the same fp16 weights
+    and x as the shared-memory form in the same K order: the outputs agree to fp32
+    rounding; and both against the oracle."""
+    from llmnputest_b200 import ops
+    rng = np.random.default_rng(9000 + n_t + k_t + bsz)
+    swiglu = form.startswith("swiglu")
+    g = orc.synth_q4_tiles(rng, n_t * k_t)
+    u = orc.synth_q4_tiles(rng, n_t * k_t) if swiglu else None
+    norm = form.endswith("norm")
+    if norm:
+        x = (rng.standard_normal((bsz, k_t * 256)) * 3).astype(np.float32)
+        xd = torch.from_numpy(x).to(cuda)
+        nw = (rng.standard_normal(k_t * 256) * 0.1 + 1).astype(np.float32)
+        kw = dict(norm_w=dev_bf16(nw), eps=1e-6)
+    else:
+        x = orc.synth_bf16(rng, (bsz, k_t * 256)).astype(np.float32)
+        xd = dev_bf16(x)
+        kw = {}
+    gd = dev_u8(g)
+    gp = ops.q4_gemm_pack(gd, n_t, k_t)
+    if swiglu:
+        ud = dev_u8(u)
+        up = ops.q4_gemm_pack(ud, n_t, k_t)
+        plain = ops.q4_swiglu_gemm(gd, ud, n_t, k_t, xd, **kw)
+        packed = ops.q4_swiglu_gemm(gp, up, n_t, k_t, xd, packed=True, prefetch=True, **kw)
+    else:
+        acc = form == "acc"
+        y0 = torch.from_numpy(rng.standard_normal((bsz, n_t * 32)).astype(np.float32)).to(cuda)
+        plain = ops.q4_gemm(gd, n_t, k_t, xd, out=y0.clone(), accumulate=acc, **kw)
+        packed = ops.q4_gemm(gp, n_t, k_t, xd, out=y0.clone(), accumulate=acc, packed=True, prefetch=True, **kw)
+    torch.cuda.synchronize()
+    a, b = packed.float().cpu().numpy(), plain.float().cpu().numpy()
+    if swiglu:  # bf16 outputs
+        assert np.array_equal(a, b), float(np.abs(a - b).max())
+    else:  # split-K partials meet in fp32 atomics of either order
+        assert np.abs(a - b).max() <= 1e-5 * max(1.0, float(np.abs(b).max())), float(np.abs(a - b).max())
+    if not norm and not swiglu and form != "acc":
+        _check(a, np.stack([orc.gemv_q4(g, x[i], n_t, k_t) for i in range(bsz)]), what=("packed", n_t, k_t, bsz))
+    assert ops.device_error() == 0
