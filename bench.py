@@ -541,6 +541,11 @@ def decode_kernel_split(torch, dec, hbm_peak: float, reps: int = 10) -> dict:
                                    out=down_out if down_out is not None else dec.resid, accumulate=down_out is None,
                                    workspace=ws, prefetch=True, packed=pk) for g in G],
               sum(g["down"].numel() for g in G), n_l, "q4_gemm_down")
+    # the lm_head (q8, RMSNorm fused) once per step
+    nt_v = getattr(dec, "nt_v_local", getattr(dec, "nt_v", None))
+    lg = getattr(dec, "logits_local", dec.logits)
+    timed(lambda: ops.gemv_rmsnorm(dec.w["lm_head"], nt_v, dec.kt_h, dec.resid, dec.w["final_norm"], c.rms_eps,
+                                   out=lg, q8=True), dec.w["lm_head"].numel(), 1, "lm_head_q8")
     return out
 
 

@@ -639,7 +639,10 @@ int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_row
   p.prefetch = (flags & B2_GEMV_PREFETCH) ? 1 : 0;
   {
     const int nc = ncta <= 32 ? 32 : (ncta <= 64 ? 64 : (ncta <= 128 ? 128 : 256));
-    p.d_bufs = (packed && 2 * nc > b2::kTcTmemACol) ? 1 : 2;
+    // packed: two MMA issuers (two partials) while 2 x N columns fit the D region, and two
+    // accumulator buffers while those fit too
+    p.n_issuers = (packed && 2 * nc <= b2::kTcTmemACol) ? 2 : 1;
+    p.d_bufs = (!packed || 2 * p.n_issuers * nc <= b2::kTcTmemACol) ? 2 : 1;
   }
   auto kernel = epi == b2::kTcEpiSwiglu
                     ? (packed ? b2::q4_gemm_tc_kernel<b2::kTcEpiSwiglu, true> : b2::q4_gemm_tc_kernel<b2::kTcEpiSwiglu, false>)

@@ -15,7 +15,7 @@
 //       tensor map) lands each 64-k slice ready for the tensor core.
 //   D = fp32 in TMEM, 2 x N columns (double-buffered across row tiles).
 //
-// Warp roles (14 warps):
+// Warp roles (15 warps):
 //   warp 0       producer: bulk copies of the raw tiles (one K-tile stage) and
 //                of the x slices, mbarrier complete_tx
 //   warp 1       TMEM allocation; lane 0 issues tcgen05.mma (4 per 64-k slice)
@@ -24,6 +24,7 @@
 //                32*(w%4) ..), scale by 2^-e, store y / SwiGLU through smem
 //   warps 6-13   dequant: four pairs, pair j converts 64-k slice j of every
 //                K-tile (raw ring -> A ring slot j)
+//   warp 14      packed form: lane 0 is the second MMA issuer (below); idle otherwise
 // Every mbarrier wait is bounded; on a timeout the kernel records an error,
 // stops issuing, waits (bounded) for the MMAs it issued, frees TMEM and exits.
 //
@@ -35,7 +36,11 @@
 // buffers of up to 128 columns, or one of 256), columns 256-511 two K-tile A
 // buffers of 128 columns (256 k as fp16 pairs).  Warp w (w % 4 = its TMEM lane
 // quarter = tile-row slot q) decodes k 128*h .. 128*h + 127 of each K-tile, h = 0
-// for warps 6-9 and 1 for warps 10-13.
+// for warps 6-9 and 1 for warps 10-13.  A single issuing thread sustains one
+// tcgen05.mma (M=128, K=16) per ~53 cycles whatever N <= 64, well below the tensor
+// pipe's rate at small N; two issuers (warp 1 lane 0 and warp 14 lane 0) take the
+// odd and even K-tiles of each item into two partial accumulators, which the
+// epilogue adds (TMEM columns allowing: 2 x N <= 256).
 #pragma once
 
 #include "b2_common.cuh"
@@ -44,7 +49,8 @@
 namespace b2 {
 
 constexpr int kTcM = 128;
-constexpr int kTcWarps = 14;
+constexpr int kTcWarps = 15;
+constexpr int kTcMma2Warp = 14;             // packed form: the second MMA issuer
 constexpr int kTcThreads = kTcWarps * 32;
 constexpr int kTcEpiWarp0 = 2;
 constexpr int kTcDqWarp0 = 6;
@@ -102,6 +108,7 @@ struct TcParams {
   int prefetch;     // the weights are constant: the first raw stages stream (and are
                     // dequantised) before the wait on the preceding kernel
   int d_bufs;       // accumulator buffers in TMEM (2, or 1 for 256 columns in the packed form)
+  int n_issuers;    // packed form: MMA issuing threads (1 or 2), each with its own partial
 };
 
 struct TcSmem {
@@ -114,7 +121,7 @@ struct TcSmem {
     xchg = raw + raw_stages * kTcRawStage;
     bar = (xchg + kTcXchgBytes + 15) & ~15;
     // raw full/empty, a full/empty, x full/empty, acc full/empty x2, done, tmem addr
-    total = bar + (2 * raw_stages + 2 * kTcMaxASlots + 2 * x_stages + 4 + 1) * 8 + 16;
+    total = bar + (2 * raw_stages + 2 * kTcMaxASlots + 2 * x_stages + 4 + 2) * 8 + 16;
   }
 };
 
@@ -376,8 +383,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
   uint64_t* x_empty = x_full + XS;
   uint64_t* acc_full = x_empty + XS;  // [2]
   uint64_t* acc_empty = acc_full + 2;  // [2]
-  uint64_t* mma_done = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* mma_done = acc_empty + 2;  // [2]: one per MMA issuer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -385,6 +392,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
   const uint32_t ncols = ncta <= 32 ? 32u : (ncta <= 64 ? 64u : (ncta <= 128 ? 128u : 256u));  // per buffer
   const uint32_t tcols = TA ? 512u : 2 * ncols;  // TMEM columns allocated
   const int DB = p.d_bufs;                       // accumulator buffers (1 or 2)
+  const int NI = TA ? p.n_issuers : 1;           // MMA issuers = partial accumulators per buffer
+  const uint32_t dstride = NI * ncols;           // TMEM columns per accumulator buffer
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < RS; ++s) {
@@ -401,10 +410,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
       mbar_init(smem_u32(&x_empty[s]), 1);
     }
     for (int s = 0; s < 2; ++s) {
-      mbar_init(smem_u32(&acc_full[s]), 1);
+      mbar_init(smem_u32(&acc_full[s]), NI);  // each MMA issuer's commit
       mbar_init(smem_u32(&acc_empty[s]), 4);  // the 4 epilogue warps
+      mbar_init(smem_u32(&mma_done[s]), 1);
     }
-    mbar_init(smem_u32(mma_done), 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -545,6 +554,69 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
         }
       }
     }
+  } else if (TA && (warp == 1 || warp == kTcMma2Warp)) {
+    // --------------------------------------------- MMA, packed form (A in TMEM)
+    // issuer e takes the K-tiles kt of each item with (kt - k0) % NI == e into partial e;
+    // A buffer and x stage follow the CTA's K-tile sequence rseq (shared with the
+    // producer and the dequant warps)
+    const int e = warp == 1 ? 0 : 1;
+    if (lane == 0 && e < NI) {
+      pdl_wait();
+      const uint32_t idesc = umma_idesc_f16(kTcM, ncta);
+      const uint32_t x0 = smem_u32(smem + L.x);
+      const uint32_t xbytes = static_cast<uint32_t>(ncta) * 128;
+      bool issued_any = false;
+      uint32_t rseq = 0, t_it = 0;
+      for (int it = blockIdx.x; it < n_items && !*abort_flag; it += gridDim.x, ++t_it) {
+        const int buf = DB == 2 ? static_cast<int>(t_it & 1) : 0;
+        const uint32_t uses = DB == 2 ? t_it >> 1 : t_it;  // earlier items on this buffer
+        if (t_it >= static_cast<uint32_t>(DB))
+          mbar_wait_bounded(smem_u32(&acc_empty[buf]), (uses & 1) ^ 1, abort_flag, kDevTimeoutEmpty);
+        const uint32_t d_tmem = tmem_base + buf * dstride + e * ncols;
+        const int k0 = item_k0(it), k1 = item_k1(it);
+        uint32_t acc = 0;  // the partial's first MMA of the item starts it
+        for (int kt = k0; kt < k1; ++kt, ++rseq) {
+          if ((kt - k0) % NI != e) continue;
+          const int ab = static_cast<int>(rseq & 1);  // AB == 2 in the packed form
+          const uint32_t aph = (rseq >> 1) & 1;
+          const int xs = static_cast<int>(rseq % XS);
+          const uint32_t xph = (rseq / XS) & 1;
+          // a failed wait has set the abort flag, checked below
+          if (!mbar_wait_bounded(smem_u32(&a_full[ab]), aph, abort_flag, kDevTimeoutFull) ||
+              !mbar_wait_bounded(smem_u32(&x_full[xs]), xph, abort_flag, kDevTimeoutFull))
+            break;
+          tc_fence_after();
+          const uint32_t a_tmem = tmem_base + kTcTmemACol + ab * kTcTmemABuf;
+#pragma unroll
+          for (int js = 0; js < 4; ++js) {
+            const uint64_t bd = umma_desc_sw128(x0 + (4 * xs + js) * xbytes);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {  // 16 k = 8 TMEM columns of A; +32 bytes along K of x
+              tc_mma_f16_ta(d_tmem, a_tmem + js * 32 + kk * 8, bd + 2 * kk, idesc, acc);
+              acc = 1;
+            }
+          }
+          issued_any = true;
+          tc_commit(smem_u32(&x_empty[xs]));
+          tc_commit(smem_u32(&a_empty[ab]));
+        }
+        if (*abort_flag) break;
+        tc_commit(smem_u32(&acc_full[buf]));
+      }
+      // every MMA issued here has completed before TMEM is released
+      if (issued_any) {
+        tc_commit(smem_u32(&mma_done[e]));
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(smem_u32(&mma_done[e]), 0)) {
+          if (globaltimer() - t0 > B2_WAIT_TIMEOUT_NS) {
+            record_error(kDevTimeoutDrain);
+            break;
+          }
+        }
+      }
+    }
+  } else if (warp == kTcMma2Warp) {
+    // shared-memory form: no second issuer
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA
     if (lane == 0) {
@@ -565,28 +637,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
         const uint32_t d_tmem = tmem_base + buf * ncols;
         const int k0 = item_k0(it), k1 = item_k1(it);
         for (int kt = k0; kt < k1; ++kt) {
-          if constexpr (TA) {
-            // A of this K-tile in TMEM (all 8 dequant warps), then the x slices; a
-            // failed wait has set the abort flag, checked below
-            if (mbar_wait_bounded(smem_u32(&a_full[ab]), aph, abort_flag, kDevTimeoutFull) &&
-                mbar_wait_bounded(smem_u32(&x_full[xs]), xph, abort_flag, kDevTimeoutFull)) {
-              tc_fence_after();
-              const uint32_t a_tmem = tmem_base + kTcTmemACol + ab * kTcTmemABuf;
-#pragma unroll
-              for (int js = 0; js < 4; ++js) {
-                const uint64_t bd = umma_desc_sw128(x0 + (4 * xs + js) * xbytes);
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)  // 16 k = 8 TMEM columns of A; +32 bytes along K of x
-                  tc_mma_f16_ta(d_tmem, a_tmem + js * 32 + kk * 8, bd + 2 * kk, idesc, ((kt - k0) | js | kk) != 0);
-              }
-              issued_any = true;
-              tc_commit(smem_u32(&x_empty[xs]));
-              if (++xs == XS) {
-                xs = 0;
-                xph ^= 1;
-              }
-            }
-          } else {
           for (int js = 0; js < 4; ++js) {
             const bool ok_a = mbar_wait_bounded(smem_u32(&a_full[4 * ab + js]), aph, abort_flag, kDevTimeoutFull);
             const bool ok_x = mbar_wait_bounded(smem_u32(&x_full[xs]), xph, abort_flag, kDevTimeoutFull);
@@ -604,7 +654,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
               xph ^= 1;
             }
           }
-          }
           if (*abort_flag) break;
           tc_commit(smem_u32(&a_empty[ab]));
           if (++ab == AB) {
@@ -617,9 +666,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
       }
       // every MMA issued here has completed before TMEM is released
       if (issued_any) {
-        tc_commit(smem_u32(mma_done));
+        tc_commit(smem_u32(&mma_done[0]));
         const uint64_t t0 = globaltimer();
-        while (!mbar_try_wait(smem_u32(mma_done), 0)) {
+        while (!mbar_try_wait(smem_u32(&mma_done[0]), 0)) {
           if (globaltimer() - t0 > B2_WAIT_TIMEOUT_NS) {
             record_error(kDevTimeoutDrain);
             break;
@@ -644,10 +693,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
       const uint32_t uses = DB == 2 ? t_it >> 1 : t_it;
       const bool ok = mbar_wait_bounded(smem_u32(&acc_full[buf]), uses & 1, abort_flag, kDevTimeoutFull);
       tc_fence_after();
-      const uint32_t t_row = tmem_base + buf * ncols + (static_cast<uint32_t>(q * 32) << 16);
+      const uint32_t t_row = tmem_base + buf * dstride + (static_cast<uint32_t>(q * 32) << 16);
+      const bool two = NI == 2 && item_k1(it) - item_k0(it) >= 2;  // partial 1 was written
       for (int c0 = n0; c0 < n0 + ncta; c0 += 32) {  // c0: global token column
         uint32_t r[32];
         tmem_ld32(t_row + (c0 - n0), r);
+        if (two) {
+          uint32_t r1[32];
+          tmem_ld32(t_row + ncols + (c0 - n0), r1);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(r1[j]));
+        }
         if (EPI == kTcEpiF32) {
           const int tr = tile * 4 + (row_local >> 5);
           const int grow = tile * kTcM + row_local;

@@ -214,8 +214,9 @@ def test_device_pack_matches_layout(cuda):
     (112, 10, 32, "norm"), (256, 10, 32, "swiglu"), (14, 4, 256, "swiglu"), (30, 10, 9, "swiglu_norm")])
 def test_packed_gemm_equals_gemm(cuda, n_t, k_t, bsz, form):
     """The packed form (A dequantised into tensor memory) multiplies the same fp16 weights
-    and x as the shared-memory form in the same K order: the outputs agree to fp32
-    rounding; and both against the oracle."""
+    and x as the shared-memory form; it sums the K-tile's MMAs in up to four partial
+    accumulators, so the fp32 sums differ only in grouping (bf16 SwiGLU outputs then by a
+    rounding flip at most); and both against the oracle."""
     from llmnputest_b200 import ops
     rng = np.random.default_rng(9000 + n_t + k_t + bsz)
     swiglu = form.startswith("swiglu")
@@ -245,9 +246,9 @@ def test_packed_gemm_equals_gemm(cuda, n_t, k_t, bsz, form):
         packed = ops.q4_gemm(gp, n_t, k_t, xd, out=y0.clone(), accumulate=acc, packed=True, prefetch=True, **kw)
     torch.cuda.synchronize()
     a, b = packed.float().cpu().numpy(), plain.float().cpu().numpy()
-    if swiglu:  # bf16 outputs
-        assert np.array_equal(a, b), float(np.abs(a - b).max())
-    else:  # split-K partials meet in fp32 atomics of either order
+    if swiglu:  # bf16 outputs: the other SwiGLU checks' bar
+        _check(a, b, 0.9999, 1e-2, ("packed swiglu", n_t, k_t, bsz))
+    else:  # fp32 sums of other grouping (and split-K partials meeting in atomics of either order)
         assert np.abs(a - b).max() <= 1e-5 * max(1.0, float(np.abs(b).max())), float(np.abs(a - b).max())
     if not norm and not swiglu and form != "acc":
         _check(a, np.stack([orc.gemv_q4(g, x[i], n_t, k_t) for i in range(bsz)]), what=("packed", n_t, k_t, bsz))
