@@ -90,6 +90,9 @@ inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_
 //   B2Q4NX_MAX_STAGES    cap on the shared-memory pipeline depth (1..8)
 //   B2Q4NX_TC_SPLITS / _TC_RAW / _TC_XSTAGES / _TC_ABUFS   tensor-core GEMM split-K
 //                        count, raw and x pipeline depths, A buffers per slice
+//   B2Q4NX_TC_PREP_EARLY 1: the GEMM's x pre-pass releases the GEMM before its own wait
+//   B2Q4NX_PDL_MASK      launch kinds that use PDL: 1 GEMV, 2 GEMM pre-pass, 4 GEMM,
+//                        8 attention, 16 exchange, 32 other (default 0x37)
 //   B2Q4NX_ATTN_WAVE     0: attention splits as many as the 4-CTAs-per-SM target asks
 //                        (default 1: unclustered launches capped at one wave of
 //                        resident CTAs)
@@ -98,12 +101,28 @@ struct Tuning {
   int ctas_per_sm = 0;
   int max_stages = b2::kMaxStages;
   int tc_splits = 0, tc_raw = 0, tc_xst = 0, tc_abufs = 0;  // tensor-core GEMM overrides (0 = plan)
+  // GEMM x pre-pass releases the GEMM before its own PDL wait (off: after an attention
+  // call the GEMM's CTAs, over half an SM's shared memory each, would take SMs from it)
+  int tc_prep_early = 0;
+  // launch kinds that use PDL (PdlKind bits).  Not attention: launched early behind a
+  // tensor-core GEMM its CTAs contend with the GEMM's, and a batch-32 decode step of
+  // config 4 measured 4.78 ms without it against 5.45 ms with it (batch 1: equal,
+  // batch 8: 2.87 against 2.93 ms)
+  int pdl_mask = 0x37;
   int attn_wave = 1;  // attention: cap unclustered splits at one wave of resident CTAs
   // attention warps per CTA: 1 always 8 (measured equal or faster on every bench
   // shape), 2 always 4, 0 by launch shape (8 for <= one CTA per SM or long splits)
   int attn_wide = 1;
   int gated_min_split = 256;  // gated attention: fewest keys per split
 };
+// PDL per launch kind (B2Q4NX_PDL_MASK, default all but attention): a kind's launches
+// may start before the preceding kernel completes
+enum PdlKind : int {
+  kPdlGemv = 1, kPdlGemmPrep = 2, kPdlGemm = 4, kPdlAttention = 8, kPdlExchange = 16, kPdlOther = 32
+};
+const Tuning& tuning();
+bool pdl_for(int kind) { return g_pdl && (tuning().pdl_mask & kind) != 0; }
+
 const Tuning& tuning() {
   static const Tuning t = [] {
     Tuning v;
@@ -114,6 +133,8 @@ const Tuning& tuning() {
     if (const char* e = getenv("B2Q4NX_TC_RAW")) v.tc_raw = std::max(0, std::min(4, atoi(e)));
     if (const char* e = getenv("B2Q4NX_TC_XSTAGES")) v.tc_xst = std::max(0, std::min(8, atoi(e)));
     if (const char* e = getenv("B2Q4NX_TC_ABUFS")) v.tc_abufs = std::max(0, std::min(2, atoi(e)));
+    if (const char* e = getenv("B2Q4NX_TC_PREP_EARLY")) v.tc_prep_early = atoi(e) != 0;
+    if (const char* e = getenv("B2Q4NX_PDL_MASK")) v.pdl_mask = static_cast<int>(strtol(e, nullptr, 0)) & 0x3F;
     if (const char* e = getenv("B2Q4NX_ATTN_WAVE")) v.attn_wave = atoi(e) != 0;
     if (const char* e = getenv("B2Q4NX_ATTN_WIDE")) v.attn_wide = std::max(0, std::min(2, atoi(e)));
     if (const char* e = getenv("B2Q4NX_GATED_MIN_SPLIT")) v.gated_min_split = std::max(64, std::min(4096, atoi(e)));
@@ -222,7 +243,7 @@ int launch_gemv_t(b2::GemvParams p, const DevInfo& di, cudaStream_t stream) {
     attrs[na].val.clusterDim.z = 1;
     ++na;
   }
-  if (g_pdl) {
+  if (pdl_for(kPdlGemv)) {
     attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attrs[na].val.programmaticStreamSerializationAllowed = 1;
     ++na;
@@ -598,7 +619,7 @@ int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_row
   cfg.blockDim = dim3(256, 1, 1);
   cfg.stream = s;
   cfg.attrs = attr;
-  cfg.numAttrs = g_pdl ? 1 : 0;
+  cfg.numAttrs = pdl_for(kPdlGemmPrep) ? 1 : 0;
   b2::TcPrep pp = {};
   pp.x = xf ? nullptr : reinterpret_cast<const __nv_bfloat16*>(x);
   pp.xf = xf;
@@ -613,6 +634,7 @@ int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_row
   pp.yzero = yzero;
   pp.ldy = ldy;
   pp.n_out = n_tile_rows * 32;
+  pp.early = tuning().tc_prep_early;
   cudaError_t e = cudaLaunchKernelEx(&cfg, b2::tc_x_prep_kernel, pp);
   if (e != cudaSuccess) return cuda_fail(e, "x pre-pass launch");
 
@@ -659,6 +681,7 @@ int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_row
   cfg.gridDim = dim3(std::min(n_row_tiles * n_splits * n_nsplit, di.sms), 1, 1);
   cfg.blockDim = dim3(b2::kTcThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
+  cfg.numAttrs = pdl_for(kPdlGemm) ? 1 : 0;
   e = cudaLaunchKernelEx(&cfg, kernel, p);
   if (e != cudaSuccess) return cuda_fail(e, "tensor-core GEMM launch");
   return B2_OK;
@@ -800,7 +823,7 @@ static int gqa_decode_impl(const float* q, const float* k_new, const float* v_ne
   }
   cudaLaunchAttribute attr[2];
   int na = 0;
-  if (g_pdl) {
+  if (pdl_for(kPdlAttention)) {
     attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[na].val.programmaticStreamSerializationAllowed = 1;
     ++na;
@@ -821,7 +844,7 @@ static int gqa_decode_impl(const float* q, const float* k_new, const float* v_ne
   cfg.numAttrs = na;  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p);
   if (e != cudaSuccess) return cuda_fail(e, "attention launch");
   if (pl.n_splits > 1 && !pl.clustered) {
-    cfg.numAttrs = g_pdl ? 1 : 0;  // the combine kernel is not clustered
+    cfg.numAttrs = pdl_for(kPdlAttention) ? 1 : 0;  // the combine kernel is not clustered
     cfg.gridDim = dim3(n_q_heads, batch, 1);
     cfg.blockDim = dim3(64, 1, 1);
     e = cudaLaunchKernelEx(&cfg, b2::gqa_combine_kernel<64>, p);
@@ -901,7 +924,7 @@ int xchg_launch(const void* kernel, const b2::XchgParams& p, cudaStream_t s) {
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = g_pdl ? 1 : 0;
+  cfg.numAttrs = pdl_for(kPdlExchange) ? 1 : 0;
   void* args[] = {const_cast<b2::XchgParams*>(&p)};
   cudaError_t e = cudaLaunchKernelExC(&cfg, kernel, args);
   if (e != cudaSuccess) return cuda_fail(e, "exchange launch");
@@ -1035,7 +1058,7 @@ int b2_rmsnorm(const void* x, int x_is_f32, int ldx, const uint16_t* w, float ep
   cfg.blockDim = dim3(b2::kNormThreads, 1, 1);
   cfg.stream = static_cast<cudaStream_t>(stream);
   cfg.attrs = attr;
-  cfg.numAttrs = g_pdl ? 1 : 0;
+  cfg.numAttrs = pdl_for(kPdlOther) ? 1 : 0;
   const __nv_bfloat16* wb = reinterpret_cast<const __nv_bfloat16*>(w);
   __nv_bfloat16* yb = reinterpret_cast<__nv_bfloat16*>(y);
   cudaError_t e = x_is_f32 ? cudaLaunchKernelEx(&cfg, b2::rmsnorm_kernel<true>, x, ldx, wb, eps, n, yb, ldy)
@@ -1134,7 +1157,7 @@ int b2_gated_attn_decode(const float* qg, int ld_qg, const float* k_new, const f
   cfg.blockDim = dim3(b2::kGaThreads, 1, 1);
   cfg.stream = static_cast<cudaStream_t>(stream);
   cfg.attrs = attr;
-  cfg.numAttrs = g_pdl ? 1 : 0;
+  cfg.numAttrs = pdl_for(kPdlOther) ? 1 : 0;
   cudaError_t e = G == 4   ? cudaLaunchKernelEx(&cfg, b2::gated_attn_kernel<4>, p)
                   : G == 2 ? cudaLaunchKernelEx(&cfg, b2::gated_attn_kernel<2>, p)
                            : cudaLaunchKernelEx(&cfg, b2::gated_attn_kernel<1>, p);
@@ -1192,7 +1215,7 @@ int b2_gated_delta_step(const float* qkv, int ld_qkv, const float* z, int ld_z, 
   p.prefetch_state = (flags & B2_DELTA_PREFETCH_STATE) ? 1 : 0;
   cudaLaunchAttribute attr[2];
   int na = 0;
-  if (g_pdl) {
+  if (pdl_for(kPdlOther)) {
     attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[na].val.programmaticStreamSerializationAllowed = 1;
     ++na;

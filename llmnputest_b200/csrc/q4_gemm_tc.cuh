@@ -220,6 +220,7 @@ struct TcPrep {
   int* xexp;
   float* yzero;
   int ldy, n_out;
+  int early;  // release the GEMM before this pass's own wait (see the kernel)
 };
 
 // Rows of up to kPrepRegChunks * 256 chunks of 8 (K <= 16384) are read from global
@@ -231,10 +232,13 @@ __global__ void __launch_bounds__(256) tc_x_prep_kernel(const TcPrep a) {
   const int n = blockIdx.x;
   const int k = a.k;
   const int nc = k / 8;  // chunks of 8 values
-  // the GEMM's CTAs may start (set up, prefetch and dequantise weights) while this runs;
-  // they read the x image only after this grid completed
-  pdl_launch_dependents();
+  // early: the GEMM's CTAs may start (set up, prefetch and dequantise weights) while
+  // this runs, they read the x image only after this grid completed.  Not after a
+  // kernel whose CTAs still wait for SMs: the GEMM's (over half an SM's shared memory
+  // each) would hold SMs that kernel needs.
+  if (a.early) pdl_launch_dependents();
   pdl_wait();
+  if (!a.early) pdl_launch_dependents();
   const bool live = n < a.batch;
   auto block_sum = [&](float v) {
 #pragma unroll
