@@ -541,11 +541,17 @@ def decode_kernel_split(torch, dec, hbm_peak: float, reps: int = 10) -> dict:
                                    out=down_out if down_out is not None else dec.resid, accumulate=down_out is None,
                                    workspace=ws, prefetch=True, packed=pk) for g in G],
               sum(g["down"].numel() for g in G), n_l, "q4_gemm_down")
-    # the lm_head (q8, RMSNorm fused) once per step
+    # the lm_head (q8, RMSNorm fused) once per step: the q8 GEMM on the packed head at GEMM
+    # batches, else the GEMV
     nt_v = getattr(dec, "nt_v_local", getattr(dec, "nt_v", None))
     lg = getattr(dec, "logits_local", dec.logits)
-    timed(lambda: ops.gemv_rmsnorm(dec.w["lm_head"], nt_v, dec.kt_h, dec.resid, dec.w["final_norm"], c.rms_eps,
-                                   out=lg, q8=True), dec.w["lm_head"].numel(), 1, "lm_head_q8")
+    lmp = getattr(dec, "lm_packed", None)
+    if lmp is not None:
+        timed(lambda: ops.q8_gemm(lmp, nt_v, dec.kt_h, dec.resid, out=lg, workspace=dec.gemm_ws, prefetch=True,
+                                  norm_w=dec.w["final_norm"], eps=c.rms_eps), lmp.numel(), 1, "lm_head_q8_gemm")
+    else:
+        timed(lambda: ops.gemv_rmsnorm(dec.w["lm_head"], nt_v, dec.kt_h, dec.resid, dec.w["final_norm"], c.rms_eps,
+                                       out=lg, q8=True), dec.w["lm_head"].numel(), 1, "lm_head_q8")
     return out
 
 

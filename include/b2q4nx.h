@@ -328,6 +328,19 @@ int b2_q4_gemm_workspace_size(int batch, int k_tiles, size_t* bytes);
  * byte permutation, so results equal the GEMM on the original tiles.  Not in place.
  * No reference counterpart: the reference reads the tiles as stored. */
 int b2_q4_gemm_pack(const uint8_t* tiles, int n_tile_rows, int k_tiles, uint8_t* packed, void* stream);
+
+/* The q8 form (the lm_head): b2_q8_gemm_pack packs a q8 weight (8704-byte tiles: each
+ * row's bf16 scale and 32 int8 codes of a 32-k block contiguous, tile-row pairs
+ * contiguous per K-tile); b2_q8_gemm / b2_q8_gemm_rmsnorm are the fp32 form of the
+ * GEMM above on those tiles, w = fp16(code * scale) rounded once (the q8 GEMV's
+ * arithmetic, b2_q8_gemv), flags must include B2_GEMM_PACKED.  Replaces the reference's
+ * batched lm_head GEMV (designs/lm_head/lm_head.py:129-144) for large decode batches. */
+int b2_q8_gemm_pack(const uint8_t* tiles, int n_tile_rows, int k_tiles, uint8_t* packed, void* stream);
+int b2_q8_gemm(const uint8_t* tiles, int n_tile_rows, int k_tiles, const uint16_t* x, int batch, int ldx, float* y,
+               int ldy, int flags, void* workspace, size_t workspace_bytes, void* stream);
+int b2_q8_gemm_rmsnorm(const uint8_t* tiles, int n_tile_rows, int k_tiles, const float* x, int batch, int ldx,
+                       const uint16_t* norm_w, float eps, float* y, int ldy, int flags, void* workspace,
+                       size_t workspace_bytes, void* stream);
 int b2_q4_gemm(const uint8_t* tiles, int n_tile_rows, int k_tiles, const uint16_t* x, int batch, int ldx, float* y,
                int ldy, int flags, void* workspace, size_t workspace_bytes, void* stream);
 int b2_q4_swiglu_gemm(const uint8_t* gate, const uint8_t* up, int n_tile_rows, int k_tiles, const uint16_t* x,

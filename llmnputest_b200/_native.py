@@ -62,6 +62,10 @@ SIGNATURES: dict[str, tuple] = {
     "b2_program_upload": (_i32, [_vp, _i32, _i32, _vp, _c.c_size_t, _vp]),
     "b2_program_launch": (_i32, [_vp, _i32, _i32, _vp, _f32, _vp, _c.c_size_t, _vp]),
     "b2_q4_gemm_pack": (_i32, [_vp, _i32, _i32, _vp, _vp]),
+    "b2_q8_gemm_pack": (_i32, [_vp, _i32, _i32, _vp, _vp]),
+    "b2_q8_gemm": (_i32, [_vp, _i32, _i32, _vp, _i32, _i32, _vp, _i32, _i32, _vp, _c.c_size_t, _vp]),
+    "b2_q8_gemm_rmsnorm": (_i32, [_vp, _i32, _i32, _vp, _i32, _i32, _vp, _f32, _vp, _i32, _i32, _vp, _c.c_size_t,
+                                  _vp]),
     "b2_q4_dequant_tiles": (_i32, [_vp, _i64, _vp, _vp]),
     "b2_q8_dequant_tiles": (_i32, [_vp, _i64, _vp, _vp]),
     "b2_q4_dequant_matrix": (_i32, [_vp, _i32, _i32, _vp, _i64, _vp]),

@@ -522,9 +522,11 @@ inline size_t tc_ws_bytes(int batch, int k_tiles) {
 }
 
 // xf (with norm_w, eps): the fused RMSNorm input, fp32 rows [batch][ldx] in place of x
+// qt: b2::kQ4, or b2::kQ8 (packed tiles and the fp32 form only)
 int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_rows, int k_tiles, const uint16_t* x,
                    int batch, int ldx, void* y, int ldy, int flags, void* workspace, size_t ws_bytes,
-                   void* stream, const float* xf = nullptr, const uint16_t* norm_w = nullptr, float eps = 0.f) {
+                   void* stream, const float* xf = nullptr, const uint16_t* norm_w = nullptr, float eps = 0.f,
+                   int qt = b2::kQ4) {
   DevInfo di;
   int st = device_info(&di);
   if (st != B2_OK) return st;
@@ -544,6 +546,9 @@ int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_row
     return fail(B2_ERR_ARG, "unknown flags 0x%x", flags);
   if (epi == b2::kTcEpiSwiglu && (flags & B2_GEMV_ACCUMULATE)) return fail(B2_ERR_ARG, "SwiGLU output cannot accumulate");
   const bool packed = (flags & B2_GEMM_PACKED) != 0;
+  if (qt == b2::kQ8 && (!packed || epi != b2::kTcEpiF32))
+    return fail(B2_ERR_ARG, "the q8 tensor-core GEMM takes packed tiles (B2_GEMM_PACKED), fp32 form");
+  const int tile_bytes = qt == b2::kQ8 ? b2::QTraits<b2::kQ8>::kTile : b2::QTraits<b2::kQ4>::kTile;
   const size_t need = tc_ws_bytes(batch, k_tiles);
   if (!workspace || ws_bytes < need) return fail(B2_ERR_WORKSPACE, "workspace of %zu bytes needed", need);
   if (!aligned(workspace, 256)) return fail(B2_ERR_ALIGN, "workspace must be 256-byte aligned");
@@ -570,7 +575,7 @@ int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_row
     const int max_raw = tuning().tc_raw > 0 ? tuning().tc_raw : 6;
     const int max_xp = tuning().tc_xst > 0 ? tuning().tc_xst : 4;
     auto x_fit = [&](int rs) {
-      return std::min(max_xp, (budget - b2::TcSmem(ncta, rs, 0, 0, 4).total) / (4 * ncta * 128 + 16));
+      return std::min(max_xp, (budget - b2::TcSmem(ncta, rs, 0, 0, 4, 4 * tile_bytes).total) / (4 * ncta * 128 + 16));
     };
     raw_stages = max_raw;
     while (raw_stages > 2 && x_fit(raw_stages) < std::min(2, max_xp)) --raw_stages;
@@ -578,7 +583,8 @@ int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_row
     if (x_stages < 1) return fail(B2_ERR_UNSUPPORTED, "shared memory too small for the tensor-core GEMM");
     // more than half of an SM's shared memory: two of these CTAs (each allocating all
     // 512 TMEM columns) are never resident on one SM
-    smem = std::max(b2::TcSmem(ncta, raw_stages, x_stages, 0, 4).total + 1024, di.smem_per_sm / 2 + 1024);
+    smem = std::max(b2::TcSmem(ncta, raw_stages, x_stages, 0, 4, 4 * tile_bytes).total + 1024,
+                    di.smem_per_sm / 2 + 1024);
   } else {
     // pipeline: double-buffered A slices when they fit beside >= 2 raw and >= 2 x stages
     const int max_raw = tuning().tc_raw > 0 ? tuning().tc_raw : 3;
@@ -666,13 +672,14 @@ int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_row
     p.n_issuers = (packed && 2 * nc <= b2::kTcTmemACol) ? 2 : 1;
     p.d_bufs = (!packed || 2 * p.n_issuers * nc <= b2::kTcTmemACol) ? 2 : 1;
   }
-  auto kernel = epi == b2::kTcEpiSwiglu
+  auto kernel = qt == b2::kQ8 ? b2::q4_gemm_tc_kernel<b2::kTcEpiF32, true, b2::kQ8>
+                : epi == b2::kTcEpiSwiglu
                     ? (packed ? b2::q4_gemm_tc_kernel<b2::kTcEpiSwiglu, true> : b2::q4_gemm_tc_kernel<b2::kTcEpiSwiglu, false>)
                     : (packed ? b2::q4_gemm_tc_kernel<b2::kTcEpiF32, true> : b2::q4_gemm_tc_kernel<b2::kTcEpiF32, false>);
-  static int attr_set[64][4] = {};
+  static int attr_set[64][5] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  const int variant = epi * 2 + (packed ? 1 : 0);
+  const int variant = qt == b2::kQ8 ? 4 : epi * 2 + (packed ? 1 : 0);
   if (!attr_set[dev][variant]) {
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, di.smem_optin);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(tensor-core GEMM)");
@@ -1396,20 +1403,45 @@ int b2_q4_swiglu_gemm_rmsnorm(const uint8_t* gate, const uint8_t* up, int n_tile
                         workspace, workspace_bytes, stream, x, norm_w, eps);
 }
 
-int b2_q4_gemm_pack(const uint8_t* tiles, int n_tile_rows, int k_tiles, uint8_t* packed, void* stream) {
+namespace {
+int gemm_pack(int qt, const uint8_t* tiles, int n_tile_rows, int k_tiles, uint8_t* packed, void* stream) {
   DevInfo di;
   int st = device_info(&di);
   if (st != B2_OK) return st;
   if (!tiles || !packed || n_tile_rows < 1 || k_tiles < 1) return fail(B2_ERR_ARG, "bad pack arguments");
   const int64_t n_tiles = static_cast<int64_t>(n_tile_rows) * k_tiles;
   if (!aligned(tiles, 16) || !aligned(packed, 16)) return fail(B2_ERR_ALIGN, "tiles and packed must be 16-byte aligned");
-  const uint8_t* in_end = tiles + n_tiles * b2::QTraits<b2::kQ4>::kTile;
-  const uint8_t* out_end = packed + n_tiles * b2::QTraits<b2::kQ4>::kTile;
-  if (tiles < out_end && packed < in_end) return fail(B2_ERR_ARG, "packing cannot run in place");
+  const int64_t tb = qt == b2::kQ8 ? b2::QTraits<b2::kQ8>::kTile : b2::QTraits<b2::kQ4>::kTile;
+  if (tiles < packed + n_tiles * tb && packed < tiles + n_tiles * tb) return fail(B2_ERR_ARG, "packing cannot run in place");
   const int grid = static_cast<int>(std::min<int64_t>(n_tiles, 16LL * di.sms));
-  b2::tc_pack_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(tiles, packed, n_tile_rows, k_tiles);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (qt == b2::kQ8)
+    b2::tc_pack8_kernel<<<grid, 256, 0, s>>>(tiles, packed, n_tile_rows, k_tiles);
+  else
+    b2::tc_pack_kernel<<<grid, 256, 0, s>>>(tiles, packed, n_tile_rows, k_tiles);
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? B2_OK : cuda_fail(e, "pack launch");
+}
+}  // namespace
+
+int b2_q4_gemm_pack(const uint8_t* tiles, int n_tile_rows, int k_tiles, uint8_t* packed, void* stream) {
+  return gemm_pack(b2::kQ4, tiles, n_tile_rows, k_tiles, packed, stream);
+}
+int b2_q8_gemm_pack(const uint8_t* tiles, int n_tile_rows, int k_tiles, uint8_t* packed, void* stream) {
+  return gemm_pack(b2::kQ8, tiles, n_tile_rows, k_tiles, packed, stream);
+}
+
+int b2_q8_gemm(const uint8_t* tiles, int n_tile_rows, int k_tiles, const uint16_t* x, int batch, int ldx, float* y,
+               int ldy, int flags, void* workspace, size_t workspace_bytes, void* stream) {
+  return tc_gemm_common(b2::kTcEpiF32, tiles, nullptr, n_tile_rows, k_tiles, x, batch, ldx, y, ldy, flags, workspace,
+                        workspace_bytes, stream, nullptr, nullptr, 0.f, b2::kQ8);
+}
+
+int b2_q8_gemm_rmsnorm(const uint8_t* tiles, int n_tile_rows, int k_tiles, const float* x, int batch, int ldx,
+                       const uint16_t* norm_w, float eps, float* y, int ldy, int flags, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  return tc_gemm_common(b2::kTcEpiF32, tiles, nullptr, n_tile_rows, k_tiles, nullptr, batch, ldx, y, ldy, flags,
+                        workspace, workspace_bytes, stream, x, norm_w, eps, b2::kQ8);
 }
 
 int b2_q4_dequant_tiles(const uint8_t* tiles, int64_t n_tiles, uint16_t* out, void* stream) {

@@ -57,9 +57,6 @@ constexpr int kTcDqWarp0 = 6;
 constexpr int kTcMaxASlots = 8;              // per 64-k slice of a K-tile: 1 or 2 (double-buffered)
 constexpr int kTcASlotBytes = kTcM * 128;    // 128 rows x 64 fp16
 constexpr int kTcRawSlot = QTraits<kQ4>::kSlot;
-// packed form: tiles sit back to back in a raw stage (a tile-row pair is one copy; the
-// lane-per-row loads need no padding against bank conflicts)
-constexpr int kTcRawSlotPacked = QTraits<kQ4>::kTile;
 constexpr int kTcRawStage = 4 * kTcRawSlot;
 constexpr int kTcMaxN = 256;
 constexpr int kTcXchgStride = 33;            // SwiGLU exchange row stride in floats (bank spread)
@@ -77,7 +74,12 @@ constexpr int kTcTmemABuf = 128;             // packed form: columns per A buffe
 //                     four words w; nibble i of word w is k = 32s + 8w + 2i (i < 4) or
 //                     32s + 8w + 2(i-4) + 1 (i >= 4), so (word >> 4p) & 0x000F000F holds
 //                     the codes of k = 32s + 8w + 2p and k + 1.
+// q8 packed tile (8704 bytes): bytes 0..511 the bf16 scale of row l, block s at
+// (s*32 + l)*2; bytes 512..8703 row l's 32 int8 codes of block s (k = 32s + j at byte j)
+// at 512 + (s*32 + l)*32.
 __host__ __device__ constexpr int tc_packed_scale_off(int s, int l) { return (s * 32 + l) * 4; }
+__host__ __device__ constexpr int tc_packed8_scale_off(int s, int l) { return (s * 32 + l) * 2; }
+__host__ __device__ constexpr int tc_packed8_code_off(int s, int l) { return 512 + (s * 32 + l) * 32; }
 __host__ __device__ inline long long tc_packed_tile(int tr, int kt, int n_tile_rows, int k_tiles) {
   const int pr = tr >> 1;
   const int np = (n_tile_rows - 2 * pr) >= 2 ? 2 : 1;
@@ -114,11 +116,12 @@ struct TcParams {
 struct TcSmem {
   int a, x, raw, xchg, bar, total;
   // x_slices: 64-k slices per x stage (1; packed form 4, a whole K-tile)
-  __host__ __device__ TcSmem(int npad, int raw_stages, int x_stages, int a_bufs, int x_slices = 1) {
+  __host__ __device__ TcSmem(int npad, int raw_stages, int x_stages, int a_bufs, int x_slices = 1,
+                             int raw_stage_bytes = kTcRawStage) {
     a = 0;  // 1024-aligned base (the kernel aligns the dynamic smem pointer)
     x = a + 4 * a_bufs * kTcASlotBytes;
     raw = x + x_stages * x_slices * npad * 128;
-    xchg = raw + raw_stages * kTcRawStage;
+    xchg = raw + raw_stages * raw_stage_bytes;
     bar = (xchg + kTcXchgBytes + 15) & ~15;
     // raw full/empty, a full/empty, x full/empty, acc full/empty x2, done, tmem addr
     total = bar + (2 * raw_stages + 2 * kTcMaxASlots + 2 * x_stages + 4 + 2) * 8 + 16;
@@ -371,12 +374,15 @@ __global__ void __launch_bounds__(256) tc_x_prep_kernel(const TcPrep a) {
 }
 
 // ------------------------------------------------------------ the GEMM
-template <int EPI, bool TA>
+// QT: kQ4, or kQ8 (packed form, fp32 epilogue only)
+template <int EPI, bool TA, int QT = kQ4>
 __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParams p) {
+  constexpr int TILE = QTraits<QT>::kTile;
+  constexpr int RAW_STAGE = TA ? 4 * TILE : kTcRawStage;  // packed: tiles back to back
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled operand slices
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  const TcSmem L(p.ncta, p.raw_stages, p.x_stages, TA ? 0 : p.a_bufs, TA ? 4 : 1);
+  const TcSmem L(p.ncta, p.raw_stages, p.x_stages, TA ? 0 : p.a_bufs, TA ? 4 : 1, RAW_STAGE);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar);
   const int RS = p.raw_stages, XS = p.x_stages;
   uint64_t* raw_full = bars;
@@ -459,10 +465,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
             tr = tile * 4 + j;
             base = p.w0;
           }
-          src[j] = tr < p.n_tile_rows ? base + (static_cast<size_t>(tr) * KT + kt) * QTraits<kQ4>::kTile : nullptr;
-          bytes += src[j] ? QTraits<kQ4>::kTile : 0;
+          src[j] = tr < p.n_tile_rows ? base + (static_cast<size_t>(tr) * KT + kt) * TILE : nullptr;
+          bytes += src[j] ? TILE : 0;
         }
-        const uint32_t dst = smem_u32(smem + L.raw + rs * kTcRawStage);
+        const uint32_t dst = smem_u32(smem + L.raw + rs * RAW_STAGE);
         if constexpr (TA) {
           // packed: slots 0-1 and 2-3 are each one tile-row pair, contiguous at this K-tile
           mbar_arrive_expect_tx(smem_u32(&raw_full[rs]), bytes);
@@ -472,14 +478,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
             const int tr0 = EPI == kTcEpiSwiglu ? tile * 2 : tile * 4 + 2 * h;
             if (tr0 >= p.n_tile_rows) continue;
             const int np = p.n_tile_rows - tr0 >= 2 ? 2 : 1;
-            bulk_g2s(dst + 2 * h * kTcRawSlotPacked, b + tc_packed_tile(tr0, kt, p.n_tile_rows, KT) * QTraits<kQ4>::kTile,
-                     np * QTraits<kQ4>::kTile, smem_u32(&raw_full[rs]), policy);
+            bulk_g2s(dst + 2 * h * TILE, b + tc_packed_tile(tr0, kt, p.n_tile_rows, KT) * TILE, np * TILE,
+                     smem_u32(&raw_full[rs]), policy);
           }
         } else {
           mbar_arrive_expect_tx(smem_u32(&raw_full[rs]), bytes);
 #pragma unroll
           for (int j = 0; j < 4; ++j)
-            if (src[j]) bulk_g2s(dst + j * kTcRawSlot, src[j], QTraits<kQ4>::kTile, smem_u32(&raw_full[rs]), policy);
+            if (src[j]) bulk_g2s(dst + j * kTcRawSlot, src[j], TILE, smem_u32(&raw_full[rs]), policy);
         }
       };
       // The raw ring (per K-tile) and the x ring (per 64-k slice) advance independently:
@@ -810,11 +816,35 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
         ok = __all_sync(0xffffffffu, ok);  // the TMEM stores below are warp-collective
         if (ok) {
           tc_fence_after();  // the MMAs that read this A buffer have completed
-          const uint8_t* tl = smem + L.raw + rs * kTcRawStage + q * kTcRawSlotPacked;
+          const uint8_t* tl = smem + L.raw + rs * RAW_STAGE + q * TILE;
           const uint32_t a_col = tmem_base + t_lane + kTcTmemACol + abuf * kTcTmemABuf;
 #pragma unroll
           for (int sb = 0; sb < 4; ++sb) {
             const int s = 4 * hh + sb;  // 32-k block of the K-tile
+            if constexpr (QT == kQ8) {
+              // int8 code c: byte ^ 0x80 = c + 128 placed under 0x64 is fp16 1024 + c + 128,
+              // less 1152 is c exactly; times the block scale, rounded once
+              const float sv = __uint_as_float(static_cast<uint32_t>(
+                                   *reinterpret_cast<const uint16_t*>(tl + tc_packed8_scale_off(s, lane))) << 16);
+              const __half2 s2 = __floats2half2_rn(sv, sv);
+              const uint4 c0 = *reinterpret_cast<const uint4*>(tl + tc_packed8_code_off(s, lane));
+              const uint4 c1 = *reinterpret_cast<const uint4*>(tl + tc_packed8_code_off(s, lane) + 16);
+              const uint32_t wv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+              uint32_t a[16];
+#pragma unroll
+              for (int w = 0; w < 8; ++w) {
+                const uint32_t u = wv[w] ^ 0x80808080u;
+#pragma unroll
+                for (int hp = 0; hp < 2; ++hp) {  // bytes (0, 1) and (2, 3): k = 4w + 2hp, +1
+                  const uint32_t h = prmt(u, 0x64646464u, hp ? 0x4342u : 0x4140u);
+                  const uint32_t cc = f16x2_sub(h, 0x64806480u);
+                  const __half2 wh = __hmul2(*reinterpret_cast<const __half2*>(&cc), s2);
+                  a[2 * w + hp] = *reinterpret_cast<const uint32_t*>(&wh);
+                }
+              }
+              tmem_st32x16(a_col + s * 16, a);
+              continue;
+            }
             const uint32_t sc = *reinterpret_cast<const uint32_t*>(tl + tc_packed_scale_off(s, lane));
             const uint4 nv = *reinterpret_cast<const uint4*>(tl + tc_packed_code_off(s, lane));
             const float dv = bf16lo_to_f32(sc), mv = bf16hi_to_f32(sc);
@@ -864,7 +894,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
           ok = ok && mbar_wait_bounded(smem_u32(&a_empty[abuf]), ((rseq / AB) & 1) ^ 1, abort_flag,
                                        kDevTimeoutEmpty);
         if (ok) {
-          const uint8_t* tl = smem + L.raw + rs * kTcRawStage + t * kTcRawSlot;
+          const uint8_t* tl = smem + L.raw + rs * RAW_STAGE + t * kTcRawSlot;
           // scales of the 16 rows at block kb: d, m bf16 -> fp16 pairs (d, d), (m, m)
           const uint4* dp = reinterpret_cast<const uint4*>(tl + (kb * 32 + rb * 16) * 2);
           const uint4 d0 = dp[0], d1 = dp[1], m0 = dp[32], m1 = dp[33];
@@ -946,6 +976,36 @@ __global__ void __launch_bounds__(256) tc_pack_kernel(const uint8_t* __restrict_
       w[wi] |= code << (4 * pos);
     }
     *reinterpret_cast<uint4*>(to + tc_packed_code_off(s, l)) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+
+// q8 weight -> packed q8 weight: thread (s, l) writes row l's scale and 32 codes of block s
+__global__ void __launch_bounds__(256) tc_pack8_kernel(const uint8_t* __restrict__ in, uint8_t* __restrict__ out,
+                                                       int n_tile_rows, int k_tiles) {
+  constexpr int T8 = QTraits<kQ8>::kTile;
+  const int s = threadIdx.x >> 5, l = threadIdx.x & 31;
+  const int rb = l >> 4, r = l & 15;
+  const long long n_tiles = static_cast<long long>(n_tile_rows) * k_tiles;
+  for (long long t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+    const int tr = static_cast<int>(t / k_tiles), kt = static_cast<int>(t % k_tiles);
+    const uint8_t* ti = in + t * T8;
+    uint8_t* to = out + tc_packed_tile(tr, kt, n_tile_rows, k_tiles) * T8;
+    *reinterpret_cast<uint16_t*>(to + tc_packed8_scale_off(s, l)) =
+        reinterpret_cast<const uint16_t*>(ti)[s * 32 + l];  // entry (k/32)*32 + row
+    uint32_t w[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      uint32_t v = 0u;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const int k = 32 * s + 4 * q + b;
+        v |= static_cast<uint32_t>(ti[512 + rb * 4096 + k * 16 + r]) << (8 * b);  // code index rb*4096 + k*16 + r
+      }
+      w[q] = v;
+    }
+    *reinterpret_cast<uint4*>(to + tc_packed8_code_off(s, l)) = make_uint4(w[0], w[1], w[2], w[3]);
+    *reinterpret_cast<uint4*>(to + tc_packed8_code_off(s, l) + 16) = make_uint4(w[4], w[5], w[6], w[7]);
   }
 }
 

@@ -131,6 +131,8 @@ class Q4Decoder:
                   "up": (self.nt_i, self.kt_h), "down": (self.nt_h, self.kt_i)}
         self.wg = ([pack_projections(L, shapes) if self.packed else L for L in self.w["layers"]]
                    if self.use_gemm else None)
+        # the q8 lm_head on the tensor cores too (one pass for the whole batch)
+        self.lm_packed = ops.q8_gemm_pack(self.w["lm_head"], self.nt_v, self.kt_h) if self.packed else None
 
     def _synthetic(self, seed: int) -> dict:
         c, dev = self.cfg, self.device
@@ -205,9 +207,18 @@ class Q4Decoder:
                                prefetch=True, norm_w=L["mlp_norm"], eps=c.rms_eps, packed=pk)
             ops.q4_gemm(G["down"], self.nt_h, self.kt_i, self.h, out=self.resid, accumulate=True, workspace=ws,
                         prefetch=True, packed=pk)
-        ops.gemv_rmsnorm(self.w["lm_head"], self.nt_v, self.kt_h, self.resid, self.w["final_norm"], c.rms_eps,
-                         out=self.logits, q8=True)
+        self.lm_head()
         return self.logits
+
+    def lm_head(self) -> torch.Tensor:
+        """logits = lm_head(rmsnorm(resid)): the q8 tensor-core GEMM on the packed head at
+        GEMM batches, else the q8 GEMV (RMSNorm fused either way)."""
+        c = self.cfg
+        if self.lm_packed is not None:
+            return ops.q8_gemm(self.lm_packed, self.nt_v, self.kt_h, self.resid, out=self.logits,
+                               workspace=self.gemm_ws, prefetch=True, norm_w=self.w["final_norm"], eps=c.rms_eps)
+        return ops.gemv_rmsnorm(self.w["lm_head"], self.nt_v, self.kt_h, self.resid, self.w["final_norm"],
+                                c.rms_eps, out=self.logits, q8=True)
 
     # ------------------------------------------------------ persistent program
     def build_program(self):

@@ -82,6 +82,9 @@ class DeltaNetLayer:
             self._ws_raw = torch.empty(nbytes + 256, dtype=torch.uint8, device=dev)
             off = (256 - self._ws_raw.data_ptr() % 256) % 256
             self.gemm_ws = self._ws_raw[off:off + nbytes]
+            # the projections repacked once for the tensor-core GEMM (A dequantised into TMEM)
+            self.wg = {"in_proj": self.ops.q4_gemm_pack(self.w["in_proj"], self.nt_in, self.kt_h),
+                       "out_proj": self.ops.q4_gemm_pack(self.w["out_proj"], self.nt_h, self.kt_v)}
 
     def _synthetic(self, seed: int) -> dict:
         dev, d = self.device, HEAD_DIM
@@ -124,23 +127,22 @@ class DeltaNetLayer:
         """out (fp32 [B, hidden]) = (or +=) out_proj h."""
         ops, w = self.ops, self.w
         if self.use_gemm:
-            return ops.q4_gemm(w["out_proj"], self.nt_h, self.kt_v, h, out=out, accumulate=accumulate,
-                               workspace=self.gemm_ws)
+            return ops.q4_gemm(self.wg["out_proj"], self.nt_h, self.kt_v, h, out=out, accumulate=accumulate,
+                               workspace=self.gemm_ws, prefetch=True, packed=True)
         return ops.q4_gemv(w["out_proj"], self.nt_h, self.kt_v, h, out=out, accumulate=accumulate, prefetch=True)
 
     def mix(self, resid: torch.Tensor, prefetch_state: bool = False) -> torch.Tensor:
         """Input RMSNorm, in_proj and the gated delta step; returns the bf16 [B, nv*128] step output."""
         ops, w, nv = self.ops, self.w, self.nv
         q4_out = self.proj[:, :self.nt_in * TILE_ROWS]  # the whole buffer unless b|a follow the q4 rows
-        if self.use_gemm:
-            ops.rmsnorm(resid, w["input_norm"], self.eps, out=self.xn)
-            ops.q4_gemm(w["in_proj"], self.nt_in, self.kt_h, self.xn, out=q4_out, workspace=self.gemm_ws)
+        if self.use_gemm:  # RMSNorm fused into the GEMM's x pre-pass
+            ops.q4_gemm(self.wg["in_proj"], self.nt_in, self.kt_h, resid, out=q4_out, workspace=self.gemm_ws,
+                        prefetch=True, norm_w=w["input_norm"], eps=self.eps, packed=True)
         else:
             ops.gemv_rmsnorm(w["in_proj"], self.nt_in, self.kt_h, resid, w["input_norm"], self.eps, out=q4_out,
                              prefetch=True)
         if self.ba_dense:  # b|a = bf16(rmsnorm(x)) W_ba^T in fp32 (a plain library GEMM of 2*nv columns)
-            if not self.use_gemm:
-                ops.rmsnorm(resid, w["input_norm"], self.eps, out=self.xn)
+            ops.rmsnorm(resid, w["input_norm"], self.eps, out=self.xn)
             self.xn_f.copy_(self.xn)
             torch.mm(self.xn_f, self.w_ba_t, out=self.ba_out)
             self.proj[:, self.c_b:self.c_a + nv].copy_(self.ba_out)

@@ -67,6 +67,9 @@ class GatedAttentionLayer:
             self._ws_raw = torch.empty(nbytes + 256, dtype=torch.uint8, device=dev)
             off = (256 - self._ws_raw.data_ptr() % 256) % 256
             self.gemm_ws = self._ws_raw[off:off + nbytes]
+            # the projections repacked once for the tensor-core GEMM (A dequantised into TMEM)
+            self.wg = {"in_proj": self.ops.q4_gemm_pack(self.w["in_proj"], self.nt_in, self.kt_h),
+                       "o_proj": self.ops.q4_gemm_pack(self.w["o_proj"], self.nt_h, self.kt_o)}
 
     def _synthetic(self, seed: int) -> dict:
         dev, d = self.device, HEAD_DIM
@@ -91,16 +94,16 @@ class GatedAttentionLayer:
     def o_proj(self, a: torch.Tensor, out: torch.Tensor, accumulate: bool) -> torch.Tensor:
         ops, w = self.ops, self.w
         if self.use_gemm:
-            return ops.q4_gemm(w["o_proj"], self.nt_h, self.kt_o, a, out=out, accumulate=accumulate,
-                               workspace=self.gemm_ws)
+            return ops.q4_gemm(self.wg["o_proj"], self.nt_h, self.kt_o, a, out=out, accumulate=accumulate,
+                               workspace=self.gemm_ws, prefetch=True, packed=True)
         return ops.q4_gemv(w["o_proj"], self.nt_h, self.kt_o, a, out=out, accumulate=accumulate, prefetch=True)
 
     def mix(self, resid: torch.Tensor) -> torch.Tensor:
         """Input RMSNorm, in_proj and the gated attention; returns the bf16 [B, nq*256] output."""
         ops, w = self.ops, self.w
-        if self.use_gemm:
-            ops.rmsnorm(resid, w["input_norm"], self.eps, out=self.xn)
-            ops.q4_gemm(w["in_proj"], self.nt_in, self.kt_h, self.xn, out=self.proj, workspace=self.gemm_ws)
+        if self.use_gemm:  # RMSNorm fused into the GEMM's x pre-pass
+            ops.q4_gemm(self.wg["in_proj"], self.nt_in, self.kt_h, resid, out=self.proj, workspace=self.gemm_ws,
+                        prefetch=True, norm_w=w["input_norm"], eps=self.eps, packed=True)
         else:
             ops.gemv_rmsnorm(w["in_proj"], self.nt_in, self.kt_h, resid, w["input_norm"], self.eps, out=self.proj,
                              prefetch=True)

@@ -143,6 +143,43 @@ def q4_gemm_pack(tiles: torch.Tensor, n_tile_rows: int, k_tiles: int, out: torch
     return out
 
 
+def q8_gemm_pack(tiles: torch.Tensor, n_tile_rows: int, k_tiles: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """The packed layout of a q8 weight [n_tile_rows][k_tiles] for the tensor-core GEMM
+    (b2_q8_gemm_pack).  A load-time step."""
+    _tiles(tiles, n_tile_rows, k_tiles, Q8_TILE_BYTES, "tiles")
+    if out is None:
+        out = torch.empty_like(tiles)
+    if out.shape != tiles.shape or out.dtype != torch.uint8:
+        raise ValueError("out must match tiles")
+    _native.call("b2_q8_gemm_pack", _ptr(tiles), n_tile_rows, k_tiles, _ptr(out), _stream())
+    return out
+
+
+def q8_gemm(packed: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tensor, out: torch.Tensor | None = None,
+            accumulate: bool = False, workspace: torch.Tensor | None = None, prefetch: bool = False,
+            norm_w: torch.Tensor | None = None, eps: float = 0.0) -> torch.Tensor:
+    """fp32 y [B, N] = W x for a packed q8 weight (q8_gemm_pack) on the tensor cores; with
+    norm_w, x is the fp32 residual and its RMSNorm is fused (b2_q8_gemm_rmsnorm)."""
+    _tiles(packed, n_tile_rows, k_tiles, Q8_TILE_BYTES, "packed")
+    k, n = k_tiles * TILE_K, n_tile_rows * TILE_ROWS
+    x2 = _norm_in(x, norm_w, k) if norm_w is not None else _x2d(x, k)
+    b = x2.shape[0]
+    if out is None:
+        out = torch.zeros((b, n), dtype=torch.float32, device=x2.device)
+    _need(out, "out", torch.float32)
+    ws = _gemm_ws(workspace, b, k_tiles, x2.device)
+    flags = GEMM_PACKED | (GEMV_ACCUMULATE if accumulate else 0) | (GEMV_PREFETCH if prefetch else 0)
+    wsp = _aligned_ws(ws) if workspace is None else _ptr(ws)
+    wsn = ws.numel() - (256 if workspace is None else 0)
+    if norm_w is not None:
+        _native.call("b2_q8_gemm_rmsnorm", _ptr(packed), n_tile_rows, k_tiles, _ptr(x2), b, x2.stride(0),
+                     _ptr(norm_w), float(eps), _ptr(out), out.stride(0), flags, wsp, wsn, _stream())
+    else:
+        _native.call("b2_q8_gemm", _ptr(packed), n_tile_rows, k_tiles, _ptr(x2), b, x2.stride(0), _ptr(out),
+                     out.stride(0), flags, wsp, wsn, _stream())
+    return out
+
+
 def q4_gemm(tiles: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tensor, out: torch.Tensor | None = None,
             accumulate: bool = False, workspace: torch.Tensor | None = None, prefetch: bool = False,
             norm_w: torch.Tensor | None = None, eps: float = 0.0, packed: bool = False) -> torch.Tensor:

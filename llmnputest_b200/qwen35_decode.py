@@ -87,6 +87,11 @@ class Qwen35Decoder:
             self._ws_raw = torch.empty(nbytes + 256, dtype=torch.uint8, device=dev)
             off = (256 - self._ws_raw.data_ptr() % 256) % 256
             self.gemm_ws = self._ws_raw[off:off + nbytes]
+            # the MLP projections repacked once for the tensor-core GEMM (A dequantised into TMEM)
+            pk = self.ops.q4_gemm_pack
+            self.wg = [{"gate": pk(L["gate"], self.nt_i, self.kt_h), "up": pk(L["up"], self.nt_i, self.kt_h),
+                        "down": pk(L["down"], self.nt_h, self.kt_i)} for L in self.w["layers"]]
+            self.lm_packed = self.ops.q8_gemm_pack(self.w["lm_head"], self.nt_v, self.kt_h)
 
     def _synthetic(self, seed: int) -> dict:
         c, dev = self.cfg, self.device
@@ -115,19 +120,24 @@ class Qwen35Decoder:
         steps with an ordinary stream operation."""
         ops, c = self.ops, self.cfg
         self.resid.copy_(self.x_in)
-        for m, L in zip(self.mixers, self.w["layers"]):
+        for li, (m, L) in enumerate(zip(self.mixers, self.w["layers"])):
             m.step(self.resid)
-            if self.use_gemm:
-                ops.rmsnorm(self.resid, L["post_norm"], c.eps, out=self.xn)
-                ops.q4_swiglu_gemm(L["gate"], L["up"], self.nt_i, self.kt_h, self.xn, out=self.h,
-                                   workspace=self.gemm_ws)
-                ops.q4_gemm(L["down"], self.nt_h, self.kt_i, self.h, out=self.resid, accumulate=True,
-                            workspace=self.gemm_ws)
+            if self.use_gemm:  # RMSNorm fused into the SwiGLU GEMM's x pre-pass
+                G = self.wg[li]
+                ops.q4_swiglu_gemm(G["gate"], G["up"], self.nt_i, self.kt_h, self.resid, out=self.h,
+                                   workspace=self.gemm_ws, prefetch=True, norm_w=L["post_norm"], eps=c.eps,
+                                   packed=True)
+                ops.q4_gemm(G["down"], self.nt_h, self.kt_i, self.h, out=self.resid, accumulate=True,
+                            workspace=self.gemm_ws, prefetch=True, packed=True)
             else:
                 ops.swiglu_gemv_rmsnorm(L["gate"], L["up"], self.nt_i, self.kt_h, self.resid, L["post_norm"],
                                         c.eps, out=self.h, prefetch=True)
                 ops.q4_gemv(L["down"], self.nt_h, self.kt_i, self.h, out=self.resid, accumulate=True,
                             prefetch=True)
-        ops.gemv_rmsnorm(self.w["lm_head"], self.nt_v, self.kt_h, self.resid, self.w["final_norm"], c.eps,
-                         out=self.logits, prefetch=True, q8=True)
+        if self.use_gemm:  # the q8 lm_head on the tensor cores, the whole batch in one pass
+            ops.q8_gemm(self.lm_packed, self.nt_v, self.kt_h, self.resid, out=self.logits, workspace=self.gemm_ws,
+                        prefetch=True, norm_w=self.w["final_norm"], eps=c.eps)
+        else:
+            ops.gemv_rmsnorm(self.w["lm_head"], self.nt_v, self.kt_h, self.resid, self.w["final_norm"], c.eps,
+                             out=self.logits, prefetch=True, q8=True)
         return self.logits

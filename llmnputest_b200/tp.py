@@ -212,6 +212,7 @@ class TPDecoder:
                       "gate": (self.nt_i_local, self.kt_h), "up": (self.nt_i_local, self.kt_h),
                       "down": (cfg.hidden // TILE_ROWS, self.kt_i_local)}
             self.wg = [{k: self.ops.q4_gemm_pack(L[k], *shp) for k, shp in shapes.items()} for L in self.w["layers"]]
+            self.lm_packed = self.ops.q8_gemm_pack(self.w["lm_head"], self.nt_v_local, self.kt_h)
 
     def close(self) -> None:
         """Release the peer mappings (every rank, after its last step)."""
@@ -296,8 +297,12 @@ class TPDecoder:
                                         c.rms_eps, out=self.h, prefetch=True)
                 ops.q4_gemv(L["down"], c.hidden // TILE_ROWS, self.kt_i_local, self.h, out=self.down, prefetch=True)
             self._reduce_down()
-        ops.gemv_rmsnorm(self.w["lm_head"], self.nt_v_local, self.kt_h, self.resid, self.w["final_norm"], c.rms_eps,
-                         out=self.logits_local, prefetch=True, q8=True)
+        if self.use_gemm:
+            ops.q8_gemm(self.lm_packed, self.nt_v_local, self.kt_h, self.resid, out=self.logits_local, workspace=ws,
+                        prefetch=True, norm_w=self.w["final_norm"], eps=c.rms_eps)
+        else:
+            ops.gemv_rmsnorm(self.w["lm_head"], self.nt_v_local, self.kt_h, self.resid, self.w["final_norm"],
+                             c.rms_eps, out=self.logits_local, prefetch=True, q8=True)
         self._gather_logits()
         return self.logits
 

@@ -132,6 +132,11 @@ class TPQwen35Decoder:
             self._ws_raw = torch.empty(nbytes + 256, dtype=torch.uint8, device=dev)
             off = (256 - self._ws_raw.data_ptr() % 256) % 256
             self.gemm_ws = self._ws_raw[off:off + nbytes]
+            # this rank's MLP shards repacked once for the tensor-core GEMM (A dequantised into TMEM)
+            self.wg = [{"gate": ops.q4_gemm_pack(L["gate"], self.nt_i_local, self.kt_h),
+                        "up": ops.q4_gemm_pack(L["up"], self.nt_i_local, self.kt_h),
+                        "down": ops.q4_gemm_pack(L["down"], self.nt_h, self.kt_i_local)} for L in self.w["layers"]]
+            self.lm_packed = ops.q8_gemm_pack(self.w["lm_head"], self.nt_v_local, self.kt_h)
         self.down = torch.zeros(batch, c.hidden, dtype=torch.float32, device=dev)
         self.logits_local = torch.zeros(batch, self.nt_v_local * TILE_ROWS, dtype=torch.float32, device=dev)
         self.logits_all = torch.zeros(W * batch, self.nt_v_local * TILE_ROWS, dtype=torch.float32, device=dev)
@@ -139,16 +144,18 @@ class TPQwen35Decoder:
 
     def step(self) -> torch.Tensor:
         """One decode step: x_in at positions `pos` -> logits [B, vocab] on every rank (GEMVs
-        below gemm_min_batch, tcgen05 GEMMs from it; the lm_head GEMV in passes of 16 tokens)."""
+        below gemm_min_batch, tcgen05 GEMMs from it, the lm_head included)."""
         ops, c, W = self.ops, self.cfg, self.plan.world
         self.resid.copy_(self.x_in)
-        for m, L in zip(self.mixers, self.w["layers"]):
+        for li, (m, L) in enumerate(zip(self.mixers, self.w["layers"])):
             m.step(self.resid)
-            if self.use_gemm:
-                ops.rmsnorm(self.resid, L["post_norm"], c.eps, out=self.xn)
-                ops.q4_swiglu_gemm(L["gate"], L["up"], self.nt_i_local, self.kt_h, self.xn, out=self.h,
-                                   workspace=self.gemm_ws)
-                ops.q4_gemm(L["down"], self.nt_h, self.kt_i_local, self.h, out=self.down, workspace=self.gemm_ws)
+            if self.use_gemm:  # RMSNorm fused into the SwiGLU GEMM's x pre-pass
+                G = self.wg[li]
+                ops.q4_swiglu_gemm(G["gate"], G["up"], self.nt_i_local, self.kt_h, self.resid, out=self.h,
+                                   workspace=self.gemm_ws, prefetch=True, norm_w=L["post_norm"], eps=c.eps,
+                                   packed=True)
+                ops.q4_gemm(G["down"], self.nt_h, self.kt_i_local, self.h, out=self.down, workspace=self.gemm_ws,
+                            prefetch=True, packed=True)
             else:
                 ops.swiglu_gemv_rmsnorm(L["gate"], L["up"], self.nt_i_local, self.kt_h, self.resid, L["post_norm"],
                                         c.eps, out=self.h, prefetch=True)
@@ -156,8 +163,12 @@ class TPQwen35Decoder:
             if W > 1:
                 dist.all_reduce(self.down)
             self.resid.add_(self.down)
-        ops.gemv_rmsnorm(self.w["lm_head"], self.nt_v_local, self.kt_h, self.resid, self.w["final_norm"], c.eps,
-                         out=self.logits_local, prefetch=True, q8=True)
+        if self.use_gemm:  # the q8 lm_head shard on the tensor cores
+            ops.q8_gemm(self.lm_packed, self.nt_v_local, self.kt_h, self.resid, out=self.logits_local,
+                        workspace=self.gemm_ws, prefetch=True, norm_w=self.w["final_norm"], eps=c.eps)
+        else:
+            ops.gemv_rmsnorm(self.w["lm_head"], self.nt_v_local, self.kt_h, self.resid, self.w["final_norm"], c.eps,
+                             out=self.logits_local, prefetch=True, q8=True)
         if W > 1:
             dist.all_gather_into_tensor(self.logits_all, self.logits_local)
             self.logits.view(self.batch, W, -1).copy_(self.logits_all.view(W, self.batch, -1).permute(1, 0, 2))

@@ -78,3 +78,35 @@ def dequant_packed(packed: np.ndarray) -> np.ndarray:
                 code = ((words[:, s, :, w] >> np.uint32(4 * i)) & 0xF).astype(np.float32)  # [n][l]
                 out[:, :, 32 * s + ks[8 * w + i]] = code * d[:, s, :] + m[:, s, :]
     return out
+
+
+def pack8_tiles(tiles: np.ndarray) -> np.ndarray:
+    """Each q8 tile [n, 8704] -> its packed tile: scales (s*32 + l)*2, then row l's 32 codes
+    of block s at 512 + (s*32 + l)*32 in k order."""
+    t = np.ascontiguousarray(tiles, dtype=np.uint8).reshape(-1, orc.Q8_TILE_BYTES)
+    n = t.shape[0]
+    out = np.empty_like(t)
+    out[:, :512] = t[:, :512]  # entry (k/32)*32 + row is already [s][l]
+    codes = t[:, 512:].reshape(n, 2, 256, 16).transpose(0, 1, 3, 2).reshape(n, 32, 256)  # [row][k]
+    out[:, 512:] = codes.reshape(n, 32, 8, 32).transpose(0, 2, 1, 3).reshape(n, 8192)  # [s][l][j]
+    return out.reshape(np.asarray(tiles).shape)
+
+
+def pack8(weight: np.ndarray, n_tile_rows: int, k_tiles: int) -> np.ndarray:
+    """q8 weight [n_tile_rows * k_tiles, 8704] -> the packed q8 weight (pair-major tiles)."""
+    t = pack8_tiles(weight).reshape(-1, orc.Q8_TILE_BYTES)
+    out = np.empty_like(t)
+    for tr in range(n_tile_rows):
+        for kt in range(k_tiles):
+            out[packed_position(tr, kt, n_tile_rows, k_tiles)] = t[tr * k_tiles + kt]
+    return out.reshape(np.asarray(weight).shape)
+
+
+def dequant_packed8(packed: np.ndarray) -> np.ndarray:
+    """Packed q8 tiles -> float32 [n, 32 rows, 256 k], code*scale (tools/q4nx.py:140-143)."""
+    p = np.ascontiguousarray(packed, dtype=np.uint8).reshape(-1, orc.Q8_TILE_BYTES)
+    n = p.shape[0]
+    sc = p[:, :512].view(np.uint16).view(orc.bfloat16).astype(np.float32).reshape(n, 8, 32)  # [s][l]
+    codes = p[:, 512:].view(np.int8).astype(np.float32).reshape(n, 8, 32, 32)  # [s][l][j]
+    w = codes * sc[..., None]
+    return w.transpose(0, 2, 1, 3).reshape(n, 32, 256)

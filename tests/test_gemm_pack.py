@@ -44,3 +44,17 @@ def test_pack_orders_tiles_pair_major():
     assert sorted(want) == list(range(n_t * k_t))
     assert all(tags[pos] == src for pos, src in want.items())
     assert want[12] == 12 and want[13] == 13 and want[14] == 14  # the odd last tile-row keeps its K order
+
+
+def test_pack8_is_a_permutation_with_the_oracle_values():
+    rng = np.random.default_rng(12)
+    tiles = orc.synth_q8_tiles(rng, 5)
+    packed = gpl.pack8_tiles(tiles)
+    assert np.array_equal(np.sort(packed, axis=1), np.sort(tiles, axis=1))
+    ref = orc.q8_tiles_f32(tiles).reshape(5, 2, 256, 16).transpose(0, 1, 3, 2).reshape(5, 32, 256)
+    assert np.array_equal(gpl.dequant_packed8(packed), ref)
+    # one hand-placed code: row 21 (row-block 1, r 5), k 70 (block 2, byte 6)
+    t = np.zeros((1, orc.Q8_TILE_BYTES), np.uint8)
+    t[0, 512 + 1 * 4096 + 70 * 16 + 5] = 0x7B
+    p = gpl.pack8_tiles(t)
+    assert p[0, 512 + (2 * 32 + 21) * 32 + 6] == 0x7B and np.count_nonzero(p) == 1

@@ -253,3 +253,39 @@ def test_packed_gemm_equals_gemm(cuda, n_t, k_t, bsz, form):
     if not norm and not swiglu and form != "acc":
         _check(a, np.stack([orc.gemv_q4(g, x[i], n_t, k_t) for i in range(bsz)]), what=("packed", n_t, k_t, bsz))
     assert ops.device_error() == 0
+
+
+def test_device_pack8_matches_layout(cuda):
+    from llmnputest_b200 import ops
+    from tests import gemm_pack_layout as gpl
+    rng = np.random.default_rng(6)
+    for n_t, k_t in ((5, 3), (2, 1)):
+        tiles = orc.synth_q8_tiles(rng, n_t * k_t)
+        got = ops.q8_gemm_pack(dev_u8(tiles), n_t, k_t)
+        torch.cuda.synchronize()
+        assert np.array_equal(got.cpu().numpy().reshape(tiles.shape), gpl.pack8(tiles, n_t, k_t)), (n_t, k_t)
+
+
+# q8 (the lm_head): decode batches, 256 tokens, odd shapes, the fused RMSNorm
+@pytest.mark.parametrize("n_t,k_t,bsz,norm", [(40, 10, 32, False), (9, 4, 256, False), (7, 3, 17, False),
+                                              (40, 10, 32, True), (3, 2, 1, False)])
+def test_q8_gemm_vs_oracle(cuda, n_t, k_t, bsz, norm):
+    """q8 GEMM on packed tiles: w = fp16(code * scale) rounded once (relative 2^-11), fp32
+    accumulation: the north-star bar against the oracle's float32 GEMV."""
+    from llmnputest_b200 import ops
+    rng = np.random.default_rng(8000 + n_t + k_t + bsz)
+    w = orc.synth_q8_tiles(rng, n_t * k_t)
+    pk = ops.q8_gemm_pack(dev_u8(w), n_t, k_t)
+    if norm:
+        from ml_dtypes import bfloat16
+        x = (rng.standard_normal((bsz, k_t * 256)) * 3).astype(np.float32)
+        nw = (rng.standard_normal(k_t * 256) * 0.1 + 1).astype(np.float32)
+        y = ops.q8_gemm(pk, n_t, k_t, torch.from_numpy(x).to(cuda), prefetch=True, norm_w=dev_bf16(nw), eps=1e-6)
+        xr = orc.rmsnorm(x, nw.astype(bfloat16), 1e-6).astype(np.float32).astype(bfloat16).astype(np.float32)
+    else:
+        xr = orc.synth_bf16(rng, (bsz, k_t * 256)).astype(np.float32)
+        y = ops.q8_gemm(pk, n_t, k_t, dev_bf16(xr), prefetch=True)
+    torch.cuda.synchronize()
+    ref = np.stack([orc.gemv_q8(w, xr[b], n_t, k_t) for b in range(bsz)])
+    _check(y.cpu().numpy(), ref, what=("q8", n_t, k_t, bsz, norm))
+    assert ops.device_error() == 0

@@ -23,15 +23,34 @@ CFG = Qwen35Config(hidden=256, n_layers=4, layer_types=("linear_attention",) * 3
 
 
 class Q35Ops(DeltaOracleOps, GatedOracleOps):
-    """Adds the tensor-core GEMM entry points (same arithmetic as the GEMV shim)."""
+    """Adds the tensor-core GEMM entry points (same arithmetic as the GEMV shim; the
+    packing is the identity here: the shims compute on the tiles as stored)."""
 
     def gemm_workspace_bytes(self, *a):
         return 0
 
-    def q4_gemm(self, tiles, n_t, k_t, x, out=None, accumulate=False, workspace=None):
+    def q4_gemm_pack(self, tiles, n_t, k_t):
+        return tiles
+
+    def q8_gemm_pack(self, tiles, n_t, k_t):
+        return tiles
+
+    def q8_gemm(self, tiles, n_t, k_t, x, out=None, accumulate=False, workspace=None, prefetch=False, norm_w=None,
+                eps=0.0):
+        if norm_w is not None:
+            return self.gemv_rmsnorm(tiles, n_t, k_t, x, norm_w, eps, out=out, accumulate=accumulate, q8=True)
+        return self.q8_gemv(tiles, n_t, k_t, x, out=out, accumulate=accumulate)
+
+    def q4_gemm(self, tiles, n_t, k_t, x, out=None, accumulate=False, workspace=None, prefetch=False, norm_w=None,
+                eps=0.0, packed=False):
+        if norm_w is not None:
+            return self.gemv_rmsnorm(tiles, n_t, k_t, x, norm_w, eps, out=out, accumulate=accumulate)
         return self.q4_gemv(tiles, n_t, k_t, x, out=out, accumulate=accumulate)
 
-    def q4_swiglu_gemm(self, gate, up, n_t, k_t, x, out=None, workspace=None):
+    def q4_swiglu_gemm(self, gate, up, n_t, k_t, x, out=None, workspace=None, prefetch=False, norm_w=None, eps=0.0,
+                       packed=False):
+        if norm_w is not None:
+            return self.swiglu_gemv_rmsnorm(gate, up, n_t, k_t, x, norm_w, eps, out=out)
         return self.q4_swiglu_gemv(gate, up, n_t, k_t, x, out=out)
 
 
@@ -39,7 +58,7 @@ def _bf(x):
     return np.asarray(x, np.float32).astype(bfloat16).astype(np.float32)
 
 
-@pytest.mark.parametrize("bsz", [2, 10])  # GEMV path, tensor-core GEMM path (norm launches apart)
+@pytest.mark.parametrize("bsz", [2, 10])  # GEMV path, tensor-core GEMM path
 def test_qwen35_decoder_matches_oracle_composition(bsz):
     ctx = 8
     dec = Qwen35Decoder(CFG, bsz, ctx, device="cpu", seed=1, ops_impl=Q35Ops())
