@@ -415,15 +415,13 @@ def build_decoder(torch, world: int, rank: int, batch: int, ctx: int, seed: int 
     return dec
 
 
-def capture_step(torch, dec, program: bool = False):
+def capture_step(torch, dec):
     """The decoder's step in one CUDA graph (kept, so its kernel nodes can be counted)."""
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
-        dec.step_program() if program else dec.step()
+        dec.step()
     torch.cuda.current_stream().wait_stream(s)
-    if program:
-        return dec.capture(program=True)
     g = torch.cuda.CUDAGraph(keep_graph=True)
     with torch.cuda.graph(g):
         dec.step()
@@ -445,18 +443,15 @@ def _max_over_ranks(torch, world: int, v: float) -> float:
     return float(t.item())
 
 
-def measure_decode(torch, world: int, rank: int, batch: int, ctx: int, steps: int, warmup: int,
-                   program: bool = False) -> dict:
-    """Config 4: the full 40-layer decode step at `batch` tokens, context `ctx`, TP over `world`
-    ranks (the persistent program instead of one launch per op with program=True, one GPU)."""
+def measure_decode(torch, world: int, rank: int, batch: int, ctx: int, steps: int, warmup: int) -> dict:
+    """Config 4: the full 40-layer decode step at `batch` tokens, context `ctx`, TP over `world` ranks."""
     import torch.distributed as dist
     from llmnputest_b200.decode import GRANITE_3B as cfg
     dec = build_decoder(torch, world, rank, batch, ctx)
     dec.pos.fill_(ctx - 1)  # attend over the full context
     dec.x_in.normal_()
-    g = capture_step(torch, dec, program)
-    how = ("persistent program, cuda graph" if program else
-           ("tcgen05 GEMM, cuda graph" if getattr(dec, "use_gemm", False) else "GEMV, cuda graph"))
+    g = capture_step(torch, dec)
+    how = "tcgen05 GEMM, cuda graph" if getattr(dec, "use_gemm", False) else "GEMV, cuda graph"
     if world > 1:
         how += ", peer exchanges"
     for _ in range(warmup):
@@ -472,7 +467,7 @@ def measure_decode(torch, world: int, rank: int, batch: int, ctx: int, steps: in
     b.synchronize()
     ms = _max_over_ranks(torch, world, a.elapsed_time(b) / steps)
     nbytes = step_bytes(cfg, batch, ctx)
-    out = {"batch": batch, "ctx": ctx, "tp": world, "ms_per_step": round(ms, 4), "program": program,
+    out = {"batch": batch, "ctx": ctx, "tp": world, "ms_per_step": round(ms, 4),
            "tok_s": round(batch / (ms * 1e-3), 1), "how": how,
            "hbm_gbs_per_gpu": round(nbytes / world / (ms * 1e-3) / 1e9, 1)}
     torch.cuda.synchronize()
@@ -1170,10 +1165,7 @@ def run_b200(args, rank: int, world: int) -> dict | None:
     if not args.quick:
         extras["decode"] = [measure_decode(torch, world, rank, b, HEAD_CTX, max(10, args.steps // 2), 3)
                             for b in (1, 8)]
-        if world == 1:
-            extras["decode"] += [measure_decode(torch, world, rank, b, HEAD_CTX, max(10, args.steps // 2), 3,
-                                                program=True) for b in (1, 8)]
-        else:
+        if world > 1:
             extras["qwen35_tp"] = measure_qwen35_tp(torch, world, rank, args.steps, args.warmup)
         extras["gemv_sweep"] = gemv_sweep(torch, ops, args, rank, world, gen, device, pk)
         if world == 1:  # the single-GPU kernel lines (configs 1, 3, 5)

@@ -62,7 +62,7 @@ const char* b2_last_error_message(void);
 int b2_set_launch_options(int pdl);
 
 /* Read and clear the device error word (0 = none; the first error wins): 1-4 a
- * bounded wait gave up (1 full-wait, 2 empty-wait, 3 drain, 4 grid barrier), 5 an
+ * bounded wait gave up (1 full-wait, 2 empty-wait, 3 drain; 4 unused), 5 an
  * attention call met a sequence position outside its cache or planned length, 6 a
  * tensor-parallel exchange waited too long for another rank (b2_tp_*).
  * Synchronises `stream`.  Returns B2_OK or B2_ERR_CUDA. */
@@ -352,92 +352,6 @@ int b2_q4_gemm_rmsnorm(const uint8_t* tiles, int n_tile_rows, int k_tiles, const
 int b2_q4_swiglu_gemm_rmsnorm(const uint8_t* gate, const uint8_t* up, int n_tile_rows, int k_tiles, const float* x,
                               int batch, int ldx, const uint16_t* norm_w, float eps, uint16_t* h, int ldh, int flags,
                               void* workspace, size_t workspace_bytes, void* stream);
-
-/* ------------------------------------------------------------------------
- * Decode program: a whole decode step (or any chain of q4 GEMVs and GQA
- * attention) as ONE persistent launch.  Replaces the per-op token loop that
- * chat.py:74-78 drives through model.generate (one call per projection,
- * designs/granite_gemv/granite_layer.py:54-59 groups) -- the reference's own
- * finding is that per-call issue cost dominates small matmuls
- * (README.md:117-137, granite_layer.py:1-28).
- *
- * The caller describes the step as an array of phases, uploads it once with
- * b2_program_upload (validated there), and launches it every step.
- *
- *   B2_PHASE_PREP       resid copy / zeroing side tasks, RoPE cos/sin table
- *   B2_PHASE_GEMV_Q4    y[b][n] += sum_k W[n][k] x[b][k], W q4 tiles
- *                       [n_tile_rows][k_tiles][5120]; y fp32, ALWAYS added to
- *                       with atomics (zero it in an earlier phase's side task
- *                       or pass a residual).  x from x_source:
- *         B2_X_BF16      bf16 [batch][ldx]
- *         B2_X_RMSNORM   fp32 [batch][ldx], bf16(x*rsqrt(mean(x^2)+eps)*norm_w)
- *         B2_X_ATTENTION the log-sum-exp merge of an attention phase's split
- *                        partials (part, n_q_heads, n_kv_heads, n_splits of
- *                        that phase), rounded to bf16
- *         B2_X_SWIGLU    fp32 [batch][ldx] gate at column k, up at k + half:
- *                        bf16(silu(bf16 g) * bf16 u)
- *   B2_PHASE_ATTENTION  GQA decode attention of the new token (head_dim 64):
- *                       q/k/v fp32 rows of qkv ([batch][ld_qkv]: q heads, k
- *                       heads, v heads), RoPE on q and k, k/v appended to the
- *                       caches at pos, split partials to part (size from
- *                       b2_program_attention_plan)
- *   Side tasks of every phase (run first, spread over all CTAs): zero0[0..n),
- *   zero1[0..n) set to 0.0f; copy_dst[i] = copy_src[i] for i < copy_n.
- *   barrier_after != 0: every later phase sees this phase's writes.  Phases
- *   without it may run concurrently with the next one on other SMs.
- *
- * All GEMV outputs are fp32 sums in an unspecified order (atomics): results
- * match the per-op entry points to fp32 rounding, not bit for bit. */
-typedef enum b2_phase_kind { B2_PHASE_GEMV_Q4 = 0, B2_PHASE_ATTENTION = 1, B2_PHASE_PREP = 2 } b2_phase_kind;
-typedef enum b2_x_source { B2_X_BF16 = 0, B2_X_RMSNORM = 1, B2_X_ATTENTION = 2, B2_X_SWIGLU = 3 } b2_x_source;
-
-typedef struct b2_phase {
-  int32_t kind, x_source, barrier_after, n_tile_rows;
-  int32_t k_tiles, ldx, half, ldy;
-  int32_t n_q_heads, n_kv_heads, n_splits, split_len;
-  int32_t ld_qkv, ctx_max, zero0_n, zero1_n;
-  int32_t copy_n;
-  float eps;
-  float scale; /* attention softmax scale (b2_program_upload converts it to log2 units) */
-  int32_t reserved;
-  const uint8_t* w;
-  const void* x;
-  const uint16_t* norm_w;
-  float* y;
-  float* part;
-  const float* qkv;
-  uint16_t* k_cache;
-  uint16_t* v_cache;
-  float* zero0;
-  float* zero1;
-  const float* copy_src;
-  float* copy_dst;
-} b2_phase;
-
-/* sizeof(b2_phase) as compiled into the library (binding check). */
-size_t b2_phase_struct_bytes(void);
-
-/* Context splits of a B2_PHASE_ATTENTION phase and the bytes of its `part`
- * buffer, for `batch` sequences attending over at most max_len positions. */
-int b2_program_attention_plan(int batch, int n_q_heads, int n_kv_heads, int head_dim, int max_len, int* n_splits,
-                              int* split_len, size_t* part_bytes);
-
-/* Bytes of the per-launch scratch (barrier words + RoPE table) for `batch`. */
-int b2_program_scratch_size(int batch, size_t* bytes);
-
-/* Validate n_phases host-side phases for `batch` (1..8) sequences and copy
- * them into the caller's device buffer dev_phases (>= n_phases *
- * sizeof(b2_phase) bytes, 16-byte aligned).  Blocks until the copy is done. */
-int b2_program_upload(const b2_phase* phases, int n_phases, int batch, void* dev_phases, size_t dev_bytes,
-                      void* stream);
-
-/* Run an uploaded program: one cooperative launch with one CTA per SM.
- * pos: int32 [batch] positions of the new tokens (device).  scratch: device
- * buffer of b2_program_scratch_size bytes, 16-byte aligned; its first 16 bytes
- * are cleared on the stream before the launch (so concurrent launches need
- * separate scratch).  Stream-capturable. */
-int b2_program_launch(const void* dev_phases, int n_phases, int batch, const int32_t* pos, float theta,
-                      void* scratch, size_t scratch_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -55,12 +55,6 @@ SIGNATURES: dict[str, tuple] = {
                                   _vp]),
     "b2_q4_swiglu_gemm_rmsnorm": (_i32, [_vp, _vp, _i32, _i32, _vp, _i32, _i32, _vp, _f32, _vp, _i32, _i32, _vp,
                                          _c.c_size_t, _vp]),
-    "b2_phase_struct_bytes": (_c.c_size_t, []),
-    "b2_program_attention_plan": (_i32, [_i32, _i32, _i32, _i32, _i32, _c.POINTER(_i32), _c.POINTER(_i32),
-                                         _c.POINTER(_c.c_size_t)]),
-    "b2_program_scratch_size": (_i32, [_i32, _c.POINTER(_c.c_size_t)]),
-    "b2_program_upload": (_i32, [_vp, _i32, _i32, _vp, _c.c_size_t, _vp]),
-    "b2_program_launch": (_i32, [_vp, _i32, _i32, _vp, _f32, _vp, _c.c_size_t, _vp]),
     "b2_q4_gemm_pack": (_i32, [_vp, _i32, _i32, _vp, _vp]),
     "b2_q8_gemm_pack": (_i32, [_vp, _i32, _i32, _vp, _vp]),
     "b2_q8_gemm": (_i32, [_vp, _i32, _i32, _vp, _i32, _i32, _vp, _i32, _i32, _vp, _c.c_size_t, _vp]),

@@ -26,7 +26,7 @@ enum DeviceError : int {
   kDevTimeoutFull = 1,   // consumer waited too long for a bulk copy to land
   kDevTimeoutEmpty = 2,  // producer waited too long for consumers to free a slot
   kDevTimeoutDrain = 3,  // abort path: an in-flight copy never completed
-  kDevTimeoutGrid = 4,   // a grid-wide barrier of the decode program timed out
+  // 4 is not used (it was a grid-wide barrier of a persistent launch, since removed)
 };
 
 __device__ int g_device_error;  // first error wins; cleared by the host

@@ -17,7 +17,6 @@
 
 #include "../../include/b2q4nx.h"
 #include "b2_common.cuh"
-#include "decode_program.cuh"
 #include "q4_gemm_tc.cuh"
 #include "q4nx_dequant.cuh"
 #include "gated_attention.cuh"
@@ -434,84 +433,6 @@ int attn_static_scratch(void** out) {
   }
   *out = g_attn_static_ptr[d];
   return B2_OK;
-}
-
-// ------------------------------------------------------------ decode program
-static_assert(sizeof(b2_phase) == sizeof(b2::ProgPhase), "b2_phase and its device mirror differ");
-constexpr size_t kProgRopeOffset = 256;  // scratch: [0,16) barrier words, then the RoPE table
-
-// Splits of an attention phase: about one (sequence, kv head, split) unit per
-// SM, at least one 16-position chunk per consumer warp in each split.
-void prog_attn_plan(int batch, int hkv, int max_len, int sms, int* n_splits, int* split_len) {
-  const int bh = batch * hkv;
-  int S = std::max(1, sms / bh);
-  int len = (max_len + S - 1) / S;
-  len = std::max(b2::kProgWarps * b2::kAttnChunk, (len + 15) / 16 * 16);
-  S = (max_len + len - 1) / len;
-  *n_splits = S;
-  *split_len = len;
-}
-
-// Deepest weight ring that fits one CTA per SM.
-int prog_stages(int batch, const DevInfo& di) {
-  for (int s = b2::kProgMaxStages; s >= 2; --s)
-    if (b2::ProgSmem(s, batch).total <= di.smem_optin) return s;
-  return 0;
-}
-
-int prog_check_phase(const b2_phase& P, int i) {
-  auto bad = [&](const char* what) { return fail(B2_ERR_ARG, "phase %d: %s", i, what); };
-  auto mis = [&](const char* what) { return fail(B2_ERR_ALIGN, "phase %d: %s", i, what); };
-  if (P.zero0_n < 0 || P.zero1_n < 0 || P.copy_n < 0) return bad("negative side-task count");
-  if ((P.zero0_n && !P.zero0) || (P.zero1_n && !P.zero1) || (P.copy_n && (!P.copy_src || !P.copy_dst)))
-    return bad("side task without a pointer");
-  auto heads_ok = [&]() {
-    return P.n_q_heads >= 1 && P.n_kv_heads >= 1 && P.n_q_heads % P.n_kv_heads == 0 &&
-           P.n_q_heads / P.n_kv_heads <= 8 && P.n_splits >= 1;
-  };
-  switch (P.kind) {
-    case B2_PHASE_PREP:
-      return B2_OK;
-    case B2_PHASE_ATTENTION: {
-      if (!heads_ok()) return bad("attention head counts (hq % hkv == 0, group <= 8, n_splits >= 1)");
-      if (!P.qkv || !P.k_cache || !P.v_cache || !P.part) return bad("attention pointer is null");
-      if (P.ld_qkv < (P.n_q_heads + 2 * P.n_kv_heads) * 64) return bad("ld_qkv < (hq + 2 hkv) * 64");
-      if (P.ctx_max < 1 || P.split_len < 16 || P.split_len % 16) return bad("ctx_max / split_len");
-      if (static_cast<long long>(P.n_splits) * P.split_len < P.ctx_max) return bad("splits do not cover ctx_max");
-      if (!aligned(P.k_cache, 16) || !aligned(P.v_cache, 16) || !aligned(P.part, 8)) return mis("cache or part");
-      return B2_OK;
-    }
-    case B2_PHASE_GEMV_Q4: {
-      const int K = P.k_tiles * 256;
-      if (P.n_tile_rows < 1 || P.k_tiles < 1) return bad("GEMV shape");
-      if (!P.w || !P.y) return bad("GEMV pointer is null");
-      if (!aligned(P.w, 16)) return mis("tiles must be 16-byte aligned");
-      if (P.ldy < P.n_tile_rows * 32) return bad("ldy < n_tile_rows * 32");
-      switch (P.x_source) {
-        case B2_X_BF16:
-          if (!P.x || P.ldx < K) return bad("bf16 x");
-          if (!aligned(P.x, 16) || P.ldx % 8) return mis("bf16 x (16-byte rows)");
-          return B2_OK;
-        case B2_X_RMSNORM:
-          if (!P.x || !P.norm_w || P.ldx < K || !(P.eps >= 0.f)) return bad("rmsnorm x");
-          if (!aligned(P.x, 16) || !aligned(P.norm_w, 16) || P.ldx % 4) return mis("rmsnorm x / norm_w");
-          return B2_OK;
-        case B2_X_SWIGLU:
-          if (!P.x || P.half < K || P.ldx < P.half + K) return bad("swiglu x (half >= K, ldx >= half + K)");
-          if (!aligned(P.x, 16) || P.ldx % 4 || P.half % 4) return mis("swiglu x");
-          return B2_OK;
-        case B2_X_ATTENTION:
-          if (!heads_ok() || !P.part) return bad("attention source");
-          if (P.n_q_heads * 64 != K) return bad("attention source: K != n_q_heads * 64");
-          if (!aligned(P.part, 8)) return mis("part");
-          return B2_OK;
-        default:
-          return bad("unknown x_source");
-      }
-    }
-    default:
-      return bad("unknown kind");
-  }
 }
 
 // ------------------------------------------------- tcgen05 GEMM (large batch)
@@ -1262,111 +1183,6 @@ int b2_q4_swiglu_gemv_rmsnorm(const uint8_t* gate, const uint8_t* up, int n_tile
                               int flags, void* stream) {
   return gemv_common(b2::kQ4, b2::kEpiSwiglu, gate, up, n_tile_rows, k_tiles, nullptr, batch, ldx, h, ldh, flags,
                      stream, x, norm_w, eps);
-}
-
-size_t b2_phase_struct_bytes(void) { return sizeof(b2_phase); }
-
-int b2_program_attention_plan(int batch, int n_q_heads, int n_kv_heads, int head_dim, int max_len, int* n_splits,
-                              int* split_len, size_t* part_bytes) {
-  DevInfo di;
-  int st = device_info(&di);
-  if (st != B2_OK) return st;
-  if (!n_splits || !split_len || !part_bytes) return fail(B2_ERR_ARG, "null output pointer");
-  if (batch < 1 || batch > b2::kProgMaxBatch) return fail(B2_ERR_ARG, "batch %d outside 1..%d", batch, b2::kProgMaxBatch);
-  st = attn_check(batch, n_q_heads, n_kv_heads, head_dim, max_len, max_len);
-  if (st != B2_OK) return st;
-  prog_attn_plan(batch, n_kv_heads, max_len, di.sms, n_splits, split_len);
-  *part_bytes = static_cast<size_t>(batch) * n_kv_heads * *n_splits * (n_q_heads / n_kv_heads) * b2::kPartStride *
-                sizeof(float);
-  return B2_OK;
-}
-
-int b2_program_scratch_size(int batch, size_t* bytes) {
-  if (!bytes) return fail(B2_ERR_ARG, "null bytes pointer");
-  if (batch < 1 || batch > b2::kProgMaxBatch) return fail(B2_ERR_ARG, "batch %d outside 1..%d", batch, b2::kProgMaxBatch);
-  *bytes = kProgRopeOffset + static_cast<size_t>(batch) * 32 * 2 * sizeof(float);
-  return B2_OK;
-}
-
-int b2_program_upload(const b2_phase* phases, int n_phases, int batch, void* dev_phases, size_t dev_bytes,
-                      void* stream) {
-  DevInfo di;
-  int st = device_info(&di);
-  if (st != B2_OK) return st;
-  if (!phases || n_phases < 1 || !dev_phases) return fail(B2_ERR_ARG, "null phases or n_phases < 1");
-  if (batch < 1 || batch > b2::kProgMaxBatch) return fail(B2_ERR_ARG, "batch %d outside 1..%d", batch, b2::kProgMaxBatch);
-  if (dev_bytes < static_cast<size_t>(n_phases) * sizeof(b2_phase)) return fail(B2_ERR_WORKSPACE, "dev_phases too small");
-  if (!aligned(dev_phases, 16)) return fail(B2_ERR_ALIGN, "dev_phases must be 16-byte aligned");
-  std::vector<b2::ProgPhase> dev(n_phases);
-  for (int i = 0; i < n_phases; ++i) {
-    st = prog_check_phase(phases[i], i);
-    if (st != B2_OK) return st;
-    std::memcpy(&dev[i], &phases[i], sizeof(b2_phase));
-    dev[i].scale_log2 = phases[i].scale * 1.4426950408889634f;
-  }
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaMemcpyAsync(dev_phases, dev.data(), dev.size() * sizeof(b2::ProgPhase), cudaMemcpyHostToDevice, s);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-  if (e != cudaSuccess) return cuda_fail(e, "uploading the program");
-  return B2_OK;
-}
-
-int b2_program_launch(const void* dev_phases, int n_phases, int batch, const int32_t* pos, float theta,
-                      void* scratch, size_t scratch_bytes, void* stream) {
-  DevInfo di;
-  int st = device_info(&di);
-  if (st != B2_OK) return st;
-  if (!dev_phases || n_phases < 1 || !pos) return fail(B2_ERR_ARG, "null program, n_phases < 1 or null pos");
-  if (batch < 1 || batch > b2::kProgMaxBatch) return fail(B2_ERR_ARG, "batch %d outside 1..%d", batch, b2::kProgMaxBatch);
-  size_t need = 0;
-  b2_program_scratch_size(batch, &need);
-  if (!scratch || scratch_bytes < need) return fail(B2_ERR_WORKSPACE, "scratch of %zu bytes needed", need);
-  if (!aligned(scratch, 16) || !aligned(dev_phases, 16)) return fail(B2_ERR_ALIGN, "scratch / program alignment");
-  const int stages = prog_stages(batch, di);
-  if (stages < 2) return fail(B2_ERR_UNSUPPORTED, "shared memory too small for the decode program");
-  const int smem = b2::ProgSmem(stages, batch).total;
-  static int attr_set[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(b2::decode_program_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         di.smem_optin);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(decode program)");
-    int nb = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, b2::decode_program_kernel, b2::kProgThreads, smem);
-    if (e != cudaSuccess) return cuda_fail(e, "occupancy of the decode program");
-    if (nb < 1) return fail(B2_ERR_UNSUPPORTED, "decode program does not fit one CTA per SM");
-    attr_set[dev] = 1;
-  }
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaMemsetAsync(scratch, 0, 16, s);
-  if (e != cudaSuccess) return cuda_fail(e, "clearing the program barrier");
-  float* rope = reinterpret_cast<float*>(static_cast<char*>(scratch) + kProgRopeOffset);
-  b2::prog_rope_kernel<<<batch, 32, 0, s>>>(pos, theta, rope);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "RoPE table launch");
-  b2::ProgParams p = {};
-  p.phases = static_cast<const b2::ProgPhase*>(dev_phases);
-  p.n_phases = n_phases;
-  p.batch = batch;
-  p.stages = stages;
-  p.theta = theta;
-  p.pos = pos;
-  p.rope = rope;
-  p.barrier = static_cast<unsigned int*>(scratch);
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(di.sms, 1, 1);
-  cfg.blockDim = dim3(b2::kProgThreads, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, b2::decode_program_kernel, p);
-  if (e != cudaSuccess) return cuda_fail(e, "decode program launch");
-  return B2_OK;
 }
 
 int b2_q4_gemm_workspace_size(int batch, int k_tiles, size_t* bytes) {

@@ -220,63 +220,9 @@ class Q4Decoder:
         return ops.gemv_rmsnorm(self.w["lm_head"], self.nt_v, self.kt_h, self.resid, self.w["final_norm"],
                                 c.rms_eps, out=self.logits, q8=True)
 
-    # ------------------------------------------------------ persistent program
-    def build_program(self):
-        """The layers as one b2_program launch (the lm_head stays a second launch).
-
-        Split-K targets are double-buffered by layer parity: layer l accumulates into
-        qkv2[l&1] / gu2[l&1] while its attention phase zeroes the other pair for l+1.
-        """
-        from . import program as pg
-        c, B, dev = self.cfg, self.batch, self.device
-        d = c.head_dim
-        inter = c.intermediate
-        self.qkv2 = torch.zeros(2, B, c.qkv_rows, dtype=torch.float32, device=dev)
-        self.gu2 = torch.zeros(2, B, 2 * inter, dtype=torch.float32, device=dev)
-        n_splits, split_len, part_bytes = pg.attention_plan(B, c.n_heads, c.n_kv_heads, self.ctx_max, d)
-        self.part = torch.empty(max(1, part_bytes // 4), dtype=torch.float32, device=dev)
-        ph = [pg.prep_phase(copy_src=self.x_in, copy_dst=self.resid, copy_n=B * c.hidden,
-                            zero0=self.qkv2[0], zero0_n=B * c.qkv_rows, zero1=self.gu2[0], zero1_n=B * 2 * inter)]
-        for li, L in enumerate(self.w["layers"]):
-            cur, nxt = li & 1, (li + 1) & 1
-            qkv, gu = self.qkv2[cur], self.gu2[cur]
-            ph.append(pg.gemv_phase(L["qkv"], self.nt_qkv, self.kt_h, pg.X_RMSNORM, self.resid, c.hidden, qkv,
-                                    c.qkv_rows, norm_w=L["attn_norm"], eps=c.rms_eps))
-            at = pg.attention_phase(qkv, c.qkv_rows, self.k_cache[li], self.v_cache[li], c.n_heads, c.n_kv_heads,
-                                    self.ctx_max, n_splits, split_len, self.part, d ** -0.5,
-                                    zero0=self.qkv2[nxt], zero0_n=B * c.qkv_rows,
-                                    zero1=self.gu2[nxt], zero1_n=B * 2 * inter)
-            ph.append(at)
-            ph.append(pg.gemv_phase(L["o"], self.nt_h, self.kt_q, pg.X_ATTENTION, None, 0, self.resid, c.hidden,
-                                    attn=at))
-            ph.append(pg.gemv_phase(L["gate"], self.nt_i, self.kt_h, pg.X_RMSNORM, self.resid, c.hidden, gu,
-                                    2 * inter, norm_w=L["mlp_norm"], eps=c.rms_eps, barrier=False))
-            ph.append(pg.gemv_phase(L["up"], self.nt_i, self.kt_h, pg.X_RMSNORM, self.resid, c.hidden,
-                                    gu.data_ptr() + inter * 4, 2 * inter, norm_w=L["mlp_norm"], eps=c.rms_eps))
-            ph.append(pg.gemv_phase(L["down"], self.nt_h, self.kt_i, pg.X_SWIGLU, gu, 2 * inter, self.resid,
-                                    c.hidden, half=inter))
-        ph[-1].barrier_after = 0  # the launch boundary orders it before the lm_head
-        self.program = pg.Program(ph, B, dev)
-        return self.program
-
-    def step_program(self) -> torch.Tensor:
-        """One decode step as two launches: the persistent program, then the q8 lm_head."""
-        c = self.cfg
-        if getattr(self, "program", None) is None:
-            self.build_program()
-        self.program.launch(self.pos, c.rope_theta)
-        ops.gemv_rmsnorm(self.w["lm_head"], self.nt_v, self.kt_h, self.resid, self.w["final_norm"], c.rms_eps,
-                         out=self.logits, prefetch=False, q8=True)
-        return self.logits
-
-    def capture(self, program: bool = False) -> torch.cuda.CUDAGraph:
-        """The step as one CUDA graph (warm once outside the capture first).
-
-        program=True captures step_program (persistent launch + lm_head) instead of
-        the one-launch-per-op step."""
-        fn = self.step_program if program else self.step
-        if program and getattr(self, "program", None) is None:
-            self.build_program()  # uploads synchronously: before the capture
+    def capture(self) -> torch.cuda.CUDAGraph:
+        """The step as one CUDA graph (warm once outside the capture first)."""
+        fn = self.step
         s = torch.cuda.Stream(self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
