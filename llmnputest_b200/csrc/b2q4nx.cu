@@ -109,8 +109,9 @@ struct Tuning {
   // batch 8: 2.87 against 2.93 ms)
   int pdl_mask = 0x37;
   int attn_wave = 1;  // attention: cap unclustered splits at one wave of resident CTAs
-  // attention warps per CTA: 1 always 8 (measured equal or faster on every bench
-  // shape), 2 always 4, 0 by launch shape (8 for <= one CTA per SM or long splits)
+  // attention warps per CTA: 1 always 8 (default: measured equal or faster at every
+  // bench shape), 2 always 4, 0 by launch shape (8 when the launch has at most one CTA
+  // per SM, else 4)
   int attn_wide = 1;
   int gated_min_split = 256;  // gated attention: fewest keys per split
 };
@@ -355,11 +356,12 @@ struct AttnPlan {
 // (decode-sized, < 64 MB) the splits of a (sequence, kv head) are capped at 16
 // and merged inside a cluster -- one launch; larger contexts take more splits
 // and merge in a second kernel through the caller's workspace.
-// warps per attention CTA: 8, or under attn_wide 0, 4 for short splits over
-// more CTAs than SMs (more, smaller CTAs resident)
+// warps per attention CTA: 8 when the launch has at most one CTA per SM, else 4
+// (three resident per SM; the tuning switch forces either)
 bool attn_wide(long long n_cta, int split_len, int sms) {
+  (void)split_len;
   if (tuning().attn_wide) return tuning().attn_wide == 1;
-  return n_cta <= sms || split_len >= 1024;
+  return n_cta <= sms;
 }
 
 // wave_cap: unclustered launches use at most one wave of resident CTAs (fewer,
@@ -743,8 +745,8 @@ static int gqa_decode_impl(const float* q, const float* k_new, const float* v_ne
   if (!attr_set[dev]) {
     for (auto kf : {b2::gqa_decode_kernel<64, 8>, b2::gqa_decode_kernel<64, 4>}) {
       cudaError_t e = cudaFuncSetAttribute(kf, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-      // the cluster merge buffer (<= 16 splits x 8 heads x 66 floats) beside up to ~37 KB of static smem
-      if (e == cudaSuccess) e = cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+      // the cluster merge buffer (<= 16 splits x 8 heads x 66 floats) and the 64 KB of K/V rings
+      if (e == cudaSuccess) e = cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 1024);
       if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attention)");
     }
     attr_set[dev] = 1;
@@ -766,7 +768,10 @@ static int gqa_decode_impl(const float* q, const float* k_new, const float* v_ne
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.n_splits, n_kv_heads, batch);
   cfg.blockDim = dim3(wide ? 256 : 128, 1, 1);
-  cfg.dynamicSmemBytes = pl.clustered ? pl.n_splits * (n_q_heads / n_kv_heads) * (head_dim + 2) * sizeof(float) : 0;
+  {
+    const size_t gather = pl.clustered ? pl.n_splits * (n_q_heads / n_kv_heads) * (head_dim + 2) * sizeof(float) : 0;
+    cfg.dynamicSmemBytes = ((gather + 127) & ~static_cast<size_t>(127)) + b2::attn_ring_bytes(wide ? 8 : 4);
+  }
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = na;  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p);
@@ -775,6 +780,7 @@ static int gqa_decode_impl(const float* q, const float* k_new, const float* v_ne
     cfg.numAttrs = pdl_for(kPdlAttention) ? 1 : 0;  // the combine kernel is not clustered
     cfg.gridDim = dim3(n_q_heads, batch, 1);
     cfg.blockDim = dim3(64, 1, 1);
+    cfg.dynamicSmemBytes = 0;
     e = cudaLaunchKernelEx(&cfg, b2::gqa_combine_kernel<64>, p);
     if (e != cudaSuccess) return cuda_fail(e, "attention combine launch");
   }

@@ -23,18 +23,18 @@
 // online softmax on the accumulator fragments (scores pre-scaled by log2 e,
 // exp2), P reused from the accumulator layout as the A operand of O += P V
 // (8 n-tiles of d), P split as bf16 hi + lo so the product keeps ~2^-17 of P.
-// K/V come straight from global memory with 16-byte loads (row-contiguous,
-// coalesced; the next chunk's loads are issued before the current chunk's
-// math).  Warps merge in shared memory; splits merge in a second kernel from a
-// caller-provided workspace (log-sum-exp).
+// K/V stream through a ring of shared-memory stages per warp, filled with
+// 16-byte asynchronous copies (cp.async, coalesced rows) several chunks ahead of
+// the math, so the loads in flight do not cost registers.  Warps merge in shared
+// memory; splits merge in a cluster or in a second kernel from a caller-provided
+// workspace (log-sum-exp).
 #pragma once
 
 #include "b2_common.cuh"
 
 namespace b2 {
 
-// Warps per CTA (template W): 8 when a launch has few CTAs or long splits (more
-// K/V bytes in flight per SM, shorter chunk chains per warp), else 4.
+// Warps per CTA (template W): 8 when a launch has at most one CTA per SM, else 4.
 constexpr int kAttnMaxWarps = 8;
 constexpr int kAttnChunk = 16;  // positions per inner step
 
@@ -88,15 +88,38 @@ __device__ __forceinline__ void rope_apply_bf16(const float* src, __nv_bfloat16*
 }
 
 
+// 16-byte asynchronous copy global -> shared (bypassing L1), and its group fences
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// K/V ring of one warp: kAttnStages(W) stages of one 16-position chunk, K rows then V
+// rows (128 bytes each); 16-byte piece c of row r sits at piece c ^ (r % 8), so the
+// fragment reads below (8 rows x 4 pieces, or 4 rows x 8 pieces per load) hit every
+// bank once per wavefront.  Every warp has the same ring bytes: 2 stages at 8 warps,
+// 4 at 4 warps (64 KB per CTA), the loads in flight per warp that a 4-warp CTA, three
+// per SM, can keep deeper.
+constexpr int kAttnStageBytes = 2 * kAttnChunk * 128;
+__host__ __device__ constexpr int attn_stages(int w) { return w == 8 ? 2 : 4; }
+__host__ __device__ constexpr int attn_ring_bytes(int w) { return w * attn_stages(w) * kAttnStageBytes; }
+__device__ __forceinline__ uint32_t attn_swz(int row, int piece) {
+  return static_cast<uint32_t>(row * 128 + ((piece ^ (row & 7)) << 4));
+}
+
 template <int D, int W>
-__global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) gqa_decode_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 3) gqa_decode_kernel(const AttnParams p) {
   constexpr int kAttnWarps = W, kAttnThreads = W * 32;
+  constexpr int NS = attn_stages(W);
   static_assert(D == 64, "this kernel is written for head_dim 64");
-  extern __shared__ __align__(16) float gather[];  // clustered: [n_splits][grp][D + 2] on rank 0
+  // dynamic: the cluster merge buffer (clustered: [n_splits][grp][D + 2] floats on rank
+  // 0), then at a 128-byte boundary the warps' K/V rings, reused for the warp merge
+  extern __shared__ __align__(128) float gather[];
   constexpr int QW = D / 2 + 4;  // q_s row stride in 32-bit words (bank spread)
   __shared__ __align__(16) uint32_t q_s[16 * QW];        // bf16x2, 16 head rows (rows >= grp zero)
   __shared__ float wm[kAttnWarps][16], wl[kAttnWarps][16];
-  __shared__ float wo[kAttnWarps][16][D + 1];
   __shared__ float rope_cs[2][D / 2];  // cos, sin of each pair's angle at pos
 
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
@@ -124,31 +147,35 @@ __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) gqa_decode_kernel(cons
   const __nv_bfloat16* kbase = p.k_cache + (static_cast<size_t>(b) * p.hkv + kvh) * p.ctx_max * D;
   const __nv_bfloat16* vbase = p.v_cache + (static_cast<size_t>(b) * p.hkv + kvh) * p.ctx_max * D;
 
-  auto load_chunk = [&](int c0, uint4 (&kr)[4], uint4 (&vr)[4]) {
-    // K rows c0+g and c0+8+g at d 16t..16t+15; V rows c0+{2t,2t+1,8+2t,9+2t} at d 8g..8g+7.
-    // Rows past the end are clamped to the last valid row (their scores are masked).
-    const int last = w_hi - 1;
-    const int r0 = min(c0 + g, last), r1 = min(c0 + 8 + g, last);
-    kr[0] = *reinterpret_cast<const uint4*>(kbase + static_cast<size_t>(r0) * D + 16 * t);
-    kr[1] = *reinterpret_cast<const uint4*>(kbase + static_cast<size_t>(r0) * D + 16 * t + 8);
-    kr[2] = *reinterpret_cast<const uint4*>(kbase + static_cast<size_t>(r1) * D + 16 * t);
-    kr[3] = *reinterpret_cast<const uint4*>(kbase + static_cast<size_t>(r1) * D + 16 * t + 8);
-    const int v0 = min(c0 + 2 * t, last), v1 = min(c0 + 2 * t + 1, last);
-    const int v2 = min(c0 + 8 + 2 * t, last), v3 = min(c0 + 9 + 2 * t, last);
-    vr[0] = *reinterpret_cast<const uint4*>(vbase + static_cast<size_t>(v0) * D + 8 * g);
-    vr[1] = *reinterpret_cast<const uint4*>(vbase + static_cast<size_t>(v1) * D + 8 * g);
-    vr[2] = *reinterpret_cast<const uint4*>(vbase + static_cast<size_t>(v2) * D + 8 * g);
-    vr[3] = *reinterpret_cast<const uint4*>(vbase + static_cast<size_t>(v3) * D + 8 * g);
+  // this warp's ring; stage ci % NS holds chunk ci (positions w_lo + 16 ci ..)
+  const int gbytes = p.clustered ? ((p.n_splits * grp * (D + 2) * 4 + 127) & ~127) : 0;
+  uint8_t* rings = reinterpret_cast<uint8_t*>(gather) + gbytes;
+  const uint32_t ring_s = smem_u32(rings) + warp * NS * kAttnStageBytes;
+  const int n_chunks = w_hi > w_lo ? (w_hi - w_lo + kAttnChunk - 1) / kAttnChunk : 0;
+  // chunk ci: 16 K rows then 16 V rows, 8 pieces each, 8 pieces per lane.  Rows past the
+  // end are the last valid row (their scores are masked).  One commit group per chunk
+  // index, empty past the end, so the group count stays in step with the chunks.
+  auto issue_chunk = [&](int ci) {
+    if (ci < n_chunks) {
+      const int c0 = w_lo + ci * kAttnChunk, last = w_hi - 1;
+      const uint32_t st = ring_s + (ci % NS) * kAttnStageBytes;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int pc = lane + 32 * j;
+        const int kv = pc >> 7, row = (pc >> 3) & 15, pce = pc & 7;
+        const int r = min(c0 + row, last);
+        cp_async16(st + kv * (kAttnChunk * 128) + attn_swz(row, pce),
+                   (kv ? vbase : kbase) + static_cast<size_t>(r) * D + pce * 8);
+      }
+    }
+    cp_async_commit();
   };
-  // With prefetch_kv the warp's first two chunks are loaded before the PDL wait,
-  // unless a chunk reaches row pos (appended below, after the wait): rows read
-  // are min(c0 + r, w_hi - 1), which include pos only when w_hi == len.
+  // With prefetch_kv the warp's first chunks are issued before the PDL wait, unless a
+  // chunk reaches row pos (appended below, after the wait): rows read are
+  // min(c0 + r, w_hi - 1), which include pos only when w_hi == len.
   auto early_ok = [&](int c0) { return p.prefetch_kv && (w_hi != len || c0 + kAttnChunk - 1 < pos); };
-  uint4 kr[4], vr[4], kn[4], vn[4];
-  const bool pre0 = w_lo < w_hi && early_ok(w_lo);
-  const bool pre1 = pre0 && w_lo + kAttnChunk < w_hi && early_ok(w_lo + kAttnChunk);
-  if (pre0) load_chunk(w_lo, kr, vr);
-  if (pre1) load_chunk(w_lo + kAttnChunk, kn, vn);
+  int n_pre = 0;
+  while (n_pre < NS - 1 && n_pre < n_chunks && early_ok(w_lo + n_pre * kAttnChunk)) issue_chunk(n_pre++);
   // the rotation angles depend on pos only: with prefetch_kv (pos final at launch)
   // their fp64 evaluation runs before the wait, off the dependent path
   if (p.prefetch_kv && threadIdx.x < D / 2 && p.rope) rope_angle<D>(pos, p.theta, threadIdx.x, rope_cs[0][threadIdx.x], rope_cs[1][threadIdx.x]);
@@ -191,11 +218,27 @@ __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) gqa_decode_kernel(cons
 #pragma unroll
   for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
 
-  if (w_lo < w_hi) {
-    if (!pre0) load_chunk(w_lo, kr, vr);
+  if (n_chunks > 0) {
+    for (int ci = n_pre; ci < NS - 1; ++ci) issue_chunk(ci);  // the rest of the first NS - 1 chunks
     for (int c0 = w_lo; c0 < w_hi; c0 += kAttnChunk) {
-      const bool more = c0 + kAttnChunk < w_hi;
-      if (more && !(pre1 && c0 == w_lo)) load_chunk(c0 + kAttnChunk, kn, vn);
+      const int ci = (c0 - w_lo) / kAttnChunk;
+      __syncwarp();  // every lane is done with stage (ci - 1) % NS, refilled next
+      issue_chunk(ci + NS - 1);
+      cp_async_wait<NS - 1>();
+      __syncwarp();  // every lane's copies of chunk ci are visible to the warp
+      uint4 kr[4], vr[4];
+      {
+        const uint8_t* st = rings + warp * NS * kAttnStageBytes + (ci % NS) * kAttnStageBytes;
+        kr[0] = *reinterpret_cast<const uint4*>(st + attn_swz(g, 2 * t));
+        kr[1] = *reinterpret_cast<const uint4*>(st + attn_swz(g, 2 * t + 1));
+        kr[2] = *reinterpret_cast<const uint4*>(st + attn_swz(8 + g, 2 * t));
+        kr[3] = *reinterpret_cast<const uint4*>(st + attn_swz(8 + g, 2 * t + 1));
+        const uint8_t* sv = st + kAttnChunk * 128;
+        vr[0] = *reinterpret_cast<const uint4*>(sv + attn_swz(2 * t, g));
+        vr[1] = *reinterpret_cast<const uint4*>(sv + attn_swz(2 * t + 1, g));
+        vr[2] = *reinterpret_cast<const uint4*>(sv + attn_swz(8 + 2 * t, g));
+        vr[3] = *reinterpret_cast<const uint4*>(sv + attn_swz(9 + 2 * t, g));
+      }
       // S = Q K^T for positions c0..c0+7 (n-tile 0) and c0+8..c0+15 (n-tile 1)
       float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
@@ -246,19 +289,17 @@ __global__ void __launch_bounds__(W * 32, W == 8 ? 2 : 1) gqa_decode_kernel(cons
         mma_bf16_m16n8k16(o[i][0], o[i][1], o[i][2], o[i][3], ph0, 0u, ph1, 0u, b0, b1);
         mma_bf16_m16n8k16(o[i][0], o[i][1], o[i][2], o[i][3], pl0, 0u, pl1, 0u, b0, b1);
       }
-      if (more) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          kr[i] = kn[i];
-          vr[i] = vn[i];
-        }
-      }
     }
+    cp_async_wait<0>();  // no copy into the rings is left in flight (the merge reuses them)
   }
   l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
   l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
 
-  // ---- merge the 4 warps (head g rows; lane t holds d = 16t + i and 16t + 8 + i)
+  // ---- merge the warps (head g rows; lane t holds d = 16t + i and 16t + 8 + i) through
+  // the ring bytes, once every warp is done with its ring
+  float (*wo)[16][D + 1] = reinterpret_cast<float (*)[16][D + 1]>(rings);
+  static_assert(kAttnWarps * 16 * (D + 1) * 4 <= attn_ring_bytes(kAttnWarps), "merge buffer fits the rings");
+  __syncthreads();
   if (t == 0) {
     wm[warp][g] = m_run;
     wl[warp][g] = l_run;

@@ -22,6 +22,18 @@ pytestmark = pytest.mark.gpu
 MAX_NEW = 16
 
 
+@pytest.fixture
+def cpu_torch_qwen35(monkeypatch):
+    """transformers' Qwen3.5 modules on their torch path: with a GPU present they bind
+    flash-linear-attention's and causal-conv1d's Triton kernels, which cannot take the CPU
+    tensors of chat.py's model (the model stays on the CPU, as in the reference)."""
+    from transformers.models.qwen3_5 import modeling_qwen3_5 as mq
+    for name in ("FusedRMSNormGated", "chunk_gated_delta_rule", "fused_recurrent_gated_delta_rule",
+                 "causal_conv1d_fn", "causal_conv1d_update"):
+        if hasattr(mq, name):
+            monkeypatch.setattr(mq, name, None)
+
+
 def _model():
     from transformers.models.qwen3_5 import configuration_qwen3_5 as conf
     from transformers.models.qwen3_5 import modeling_qwen3_5 as mq
@@ -53,7 +65,7 @@ def _turn(model, ids, head):
     return new, torch.stack(out.scores, 0)[:, 0].float().numpy(), line + "]"
 
 
-def test_chat_turn_with_gpu_lm_head(container_path, golden):
+def test_chat_turn_with_gpu_lm_head(container_path, golden, cpu_torch_qwen35):
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     from llmnputest_b200 import format as fmt
