@@ -726,7 +726,7 @@ def measure_qwen35_tp(torch, world: int, rank: int, steps: int, warmup: int) -> 
     """Config 5 on `world` GPUs (tp_qwen35.TPQwen35Decoder: DeltaNet by k head, attention by kv
     head or replicated, MLP by down K-tiles, the q8 lm_head by vocab rows with the fp32 logits
     all-gathered), ctx 2048, batch 1 and 256, one CUDA graph per step, max over ranks.  The
-    lm_head GEMV and the logits all-gather are also timed alone, each in its own graph."""
+    lm_head and the logits all-gather are also timed alone, each in its own graph."""
     import torch.distributed as dist
     from llmnputest_b200 import ops
     from llmnputest_b200.qwen35_decode import Qwen35Config, Qwen35Decoder
@@ -757,10 +757,16 @@ def measure_qwen35_tp(torch, world: int, rank: int, steps: int, warmup: int) -> 
             b.synchronize()
             ms = _max_over_ranks(torch, world, a.elapsed_time(b) / n)
             del g
-            # the lm_head GEMV alone, and the logits all-gather alone
-            gl = graph_of(torch, lambda: ops.gemv_rmsnorm(dec.w["lm_head"], dec.nt_v_local, dec.kt_h, dec.resid,
-                                                           dec.w["final_norm"], cfg.eps, out=dec.logits_local,
-                                                           prefetch=True, q8=True))
+            # the lm_head alone (the q8 GEMM on the packed shard at GEMM batches, else the
+            # GEMV), and the logits all-gather alone
+            if dec.use_gemm:
+                gl = graph_of(torch, lambda: ops.q8_gemm(dec.lm_packed, dec.nt_v_local, dec.kt_h, dec.resid,
+                                                          out=dec.logits_local, workspace=dec.gemm_ws, prefetch=True,
+                                                          norm_w=dec.w["final_norm"], eps=cfg.eps))
+            else:
+                gl = graph_of(torch, lambda: ops.gemv_rmsnorm(dec.w["lm_head"], dec.nt_v_local, dec.kt_h, dec.resid,
+                                                               dec.w["final_norm"], cfg.eps, out=dec.logits_local,
+                                                               prefetch=True, q8=True))
             dist.barrier()
             t_lm = _max_over_ranks(torch, world, time_graph(torch, gl, 10, 2))
             del gl
@@ -771,7 +777,8 @@ def measure_qwen35_tp(torch, world: int, rank: int, steps: int, warmup: int) -> 
             torch.cuda.synchronize()
             dist.barrier()
             out.append({"batch": bsz, "ctx": GATED_CTX, "tp": world, "ms_per_step": round(ms, 4),
-                        "tok_s": round(bsz / (ms * 1e-3), 1), "lm_head_gemv_ms": round(t_lm, 4),
+                        "tok_s": round(bsz / (ms * 1e-3), 1), "lm_head_ms": round(t_lm, 4),
+                        "lm_head_how": "q8 tcgen05 GEMM" if dec.use_gemm else "q8 GEMV",
                         "logits_all_gather_ms": round(t_ag, 4),
                         "logits_all_gather_mb": round(bsz * cfg.vocab * 4 / 1e6, 1),
                         "how": ("tcgen05 GEMM" if dec.use_gemm else "GEMV") + ", cuda graph, NCCL collectives",

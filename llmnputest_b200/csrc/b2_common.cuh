@@ -127,6 +127,14 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       : "memory");
 }
 
+// 16-byte asynchronous copy global -> shared (bypassing L1), and its group fences
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 // Hint that [src, src + bytes) will be read soon: brings the lines into L2 only
 // (no data returned, so it is safe on memory another grid may still write).
 // src 16-byte aligned, bytes a multiple of 16.

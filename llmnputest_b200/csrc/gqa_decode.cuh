@@ -88,14 +88,6 @@ __device__ __forceinline__ void rope_apply_bf16(const float* src, __nv_bfloat16*
 }
 
 
-// 16-byte asynchronous copy global -> shared (bypassing L1), and its group fences
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
 // K/V ring of one warp: kAttnStages(W) stages of one 16-position chunk, K rows then V
 // rows (128 bytes each); 16-byte piece c of row r sits at piece c ^ (r % 8), so the
 // fragment reads below (8 rows x 4 pieces, or 4 rows x 8 pieces per load) hit every
