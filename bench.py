@@ -47,6 +47,11 @@ Q4_TILE, Q8_TILE = 5120, 8704
 # dram__bytes_read.sum + dram__bytes_write.sum over tile bytes for the GEMV launches
 # that stream from DRAM (one ncu capture of a layer's four GEMVs)
 GEMV_DRAM_RATIO = 1.003
+# the same ratio for the step's kernels (one ncu capture each, bench.py --profile-case,
+# summaries under profiles/): attention at B=32 ctx 4096 (268.94 MB read + 4.18 MB written
+# over 268.44 MB of K/V), the packed SwiGLU GEMM (26.44 over 26.21 MB of tiles), the q8
+# lm_head GEMM (273.19 + 9.50 over 273.11 MB of tiles; the logits are written)
+DRAM_RATIO = {"gqa_decode": 1.0175, "q4_swiglu_gemm": 1.009, "lm_head_q8_gemm": 1.035}
 LAYERS = 40
 
 
@@ -548,6 +553,68 @@ def decode_kernel_split(torch, dec, hbm_peak: float, reps: int = 10) -> dict:
         timed(lambda: ops.gemv_rmsnorm(dec.w["lm_head"], nt_v, dec.kt_h, dec.resid, dec.w["final_norm"], c.rms_eps,
                                        out=lg, q8=True), dec.w["lm_head"].numel(), 1, "lm_head_q8")
     return out
+
+
+PROFILE_CASES = ("attention_b32", "swiglu_b32", "lm_head_b32", "step_b32")
+
+
+def profile_case(torch, name: str) -> None:
+    """One small workload for an ncu capture (`--profile-case`), a few launches of it:
+      attention_b32  one config-4 layer's GQA attention, batch 32, ctx 4096 (268 MB of K/V), 4 calls
+      swiglu_b32     config-4 gate+up SwiGLU then down GEMMs, batch 32, packed, 8 layers' weights, x2
+      lm_head_b32    config-4 q8 lm_head GEMM (100352 x 2560, packed), batch 32, 4 calls
+      step_b32       the config-4 batch-32 decode step (one CUDA graph), 3 replays
+    Prints "ok" after checking the device error word."""
+    from llmnputest_b200 import ops
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3)
+    if name == "attention_b32":
+        B, H, HKV, D, CTX = 32, 40, 8, 64, HEAD_CTX
+        qkv = torch.randn(B, (H + 2 * HKV) * D, device=dev, generator=gen)
+        kc = torch.randn(B, HKV, CTX, D, device=dev, generator=gen).to(torch.bfloat16)
+        vc = torch.randn(B, HKV, CTX, D, device=dev, generator=gen).to(torch.bfloat16)
+        pos = torch.full((B,), CTX - 1, dtype=torch.int32, device=dev)
+        out = torch.empty(B, H * D, device=dev, dtype=torch.bfloat16)
+        ws = torch.empty(max(ops.gqa_decode_workspace_bytes(B, H, HKV, D, CTX), 16), dtype=torch.uint8, device=dev)
+        qd, kd = H * D, HKV * D
+        for _ in range(4):
+            ops.gqa_decode(qkv[:, :qd], qkv[:, qd:qd + kd], qkv[:, qd + kd:], kc, vc, pos, n_q_heads=H,
+                           n_kv_heads=HKV, theta=10000.0, scale=D ** -0.5, max_len=CTX, out=out, workspace=ws,
+                           prefetch_kv=True)
+    elif name == "swiglu_b32":
+        B = 32
+        resid = torch.randn(B, 2560, device=dev, generator=gen)
+        norm = (torch.randn(2560, device=dev, generator=gen) * 0.1 + 1).to(torch.bfloat16)
+        h = torch.randn(B, 8192, device=dev, generator=gen).to(torch.bfloat16)
+        ws = torch.empty(64 << 20, device=dev, dtype=torch.uint8)
+        W = [{k: ops.q4_gemm_pack(make_q4_tiles(torch, n * kt, gen, dev), n, kt)
+              for k, n, kt in (("gate", 256, 10), ("up", 256, 10), ("down", 80, 32))} for _ in range(8)]
+        for _ in range(2):
+            for L in W:
+                ops.q4_swiglu_gemm(L["gate"], L["up"], 256, 10, resid, out=h, workspace=ws, norm_w=norm, eps=1e-5,
+                                   prefetch=True, packed=True)
+                ops.q4_gemm(L["down"], 80, 32, h, out=resid, accumulate=True, workspace=ws, prefetch=True,
+                            packed=True)
+    elif name == "lm_head_b32":
+        pk = ops.q8_gemm_pack(make_q8_tiles(torch, 3136 * 10, gen, dev), 3136, 10)
+        resid = torch.randn(32, 2560, device=dev, generator=gen)
+        norm = (torch.randn(2560, device=dev, generator=gen) * 0.1 + 1).to(torch.bfloat16)
+        out = torch.empty(32, 100352, device=dev)
+        for _ in range(4):
+            ops.q8_gemm(pk, 3136, 10, resid, out=out, prefetch=True, norm_w=norm, eps=1e-5)
+    elif name == "step_b32":
+        dec = build_decoder(torch, 1, 0, 32, HEAD_CTX)
+        dec.pos.fill_(HEAD_CTX - 1)
+        dec.x_in.normal_()
+        g = capture_step(torch, dec)
+        for _ in range(3):
+            g.replay()
+    else:
+        raise ValueError(f"unknown profile case {name!r}: {PROFILE_CASES}")
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0, "a kernel recorded a device-side error"
+    print("ok")
 
 
 def measure_headline(torch, world: int, rank: int, batch: int, ctx: int, steps: int, warmup: int,
@@ -1226,7 +1293,10 @@ def run_b200(args, rank: int, world: int) -> dict | None:
         "e2e": {"value": round(head["e2e_tok_s"], 1), "unit": "tok/s", "h2d_bytes_per_step": int(head["h2d"]),
                 "d2h_bytes_per_step": int(head["d2h"])},
         "roofline": {"bound": "hbm", "achieved": dom["gbs"], "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": dom["frac_of_measured_hbm"], "traffic": None, "kernel": dom_name,
+                     "frac": dom["frac_of_measured_hbm"],
+                     "traffic": (int(dom["bytes_per_launch"] * DRAM_RATIO[dom_name]) if dom_name in DRAM_RATIO
+                                 else None),
+                     "kernel": dom_name,
                      "bytes_per_launch": dom["bytes_per_launch"], "us_per_launch": dom["us_per_launch"],
                      "peak_src": pk["src"],
                      "step": {"gbs_per_gpu": round(step_gbs, 1), "frac": round(step_gbs / pk["hbm_gbs"], 4)}},
@@ -1286,6 +1356,8 @@ def main(argv=None) -> int:
     ap.add_argument("--layers", type=int, default=LAYERS, help="layers of the GEMV sweep")
     ap.add_argument("--quick", action="store_true", help="the headline step only")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-case", choices=PROFILE_CASES,
+                    help="run one small workload for an ncu capture and exit (no timing, no JSON line)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -1294,6 +1366,11 @@ def main(argv=None) -> int:
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
 
+    if args.profile_case:
+        import torch
+        torch.cuda.set_device(local)
+        profile_case(torch, args.profile_case)
+        return 0
     if args.impl == "reference":
         res = run_reference(args, rank)
     else:
