@@ -497,6 +497,7 @@ def decode_kernel_split(torch, dec, hbm_peak: float, reps: int = 10) -> dict:
     hkv = p.kv_local if p else c.n_kv_heads
     qd, kd = hq * d, hkv * d
     n_l = len(dec.w["layers"])
+    attn_out = dec.attn_local[:, :qd] if hasattr(dec, "attn_local") else dec.attn
     out = {}
 
     def timed(fn, nbytes, launches, name):
@@ -512,16 +513,17 @@ def decode_kernel_split(torch, dec, hbm_peak: float, reps: int = 10) -> dict:
     kv = dec.batch * dec.ctx_max * hkv * d * 4 * n_l
     timed(lambda: [ops.gqa_decode(dec.qkv[:, :qd], dec.qkv[:, qd:qd + kd], dec.qkv[:, qd + kd:], dec.k_cache[li],
                                   dec.v_cache[li], dec.pos, n_q_heads=hq, n_kv_heads=hkv, theta=c.rope_theta,
-                                  scale=d ** -0.5, max_len=dec.ctx_max, out=getattr(dec, "attn_local", dec.attn),
+                                  scale=d ** -0.5, max_len=dec.ctx_max, out=attn_out,
                                   workspace=dec.attn_ws, prefetch_kv=True) for li in range(n_l)],
           kv, n_l, "gqa_decode")
     if getattr(dec, "use_gemm", False):
         ws = dec.gemm_ws
         kt_i = getattr(dec, "kt_i_local", dec.kt_i)
         nt_qkv = getattr(dec, "nt_qkv_local", getattr(dec, "nt_qkv", None))
-        nt_o = getattr(dec, "nt_o_local", getattr(dec, "nt_h", None))
         nt_i = getattr(dec, "nt_i_local", getattr(dec, "nt_i", None))
-        o_out = getattr(dec, "o_local", None)
+        tp = hasattr(dec, "o_part")  # tensor-parallel: O by input columns into fp32 partials
+        kt_o = dec.kt_o_local if tp else dec.kt_q
+        o_in = dec.attn_local if tp else dec.attn
         down_out = getattr(dec, "down", None)
         # the step's own calls: packed weights (A in TMEM), RMSNorm fused, weights prefetched
         L, G = dec.w["layers"], dec.wg
@@ -530,17 +532,26 @@ def decode_kernel_split(torch, dec, hbm_peak: float, reps: int = 10) -> dict:
         timed(lambda: [ops.q4_gemm(g["qkv"], nt_qkv, dec.kt_h, dec.resid, out=dec.qkv, workspace=ws, prefetch=True,
                                    norm_w=l["attn_norm"], eps=c.rms_eps, packed=pk) for g, l in zip(G, L)],
               qkv_b, n_l, "q4_gemm_qkv")
-        timed(lambda: [ops.q4_gemm(g["o"], nt_o, dec.kt_q, dec.attn, out=o_out if o_out is not None else dec.resid,
-                                   accumulate=o_out is None, workspace=ws, prefetch=True, packed=pk) for g in G],
+        timed(lambda: [ops.q4_gemm(g["o"], c.hidden // 32, kt_o, o_in, out=dec.o_part if tp else dec.resid,
+                                   accumulate=not tp, workspace=ws, prefetch=True, packed=pk) for g in G],
               sum(g["o"].numel() for g in G), n_l, "q4_gemm_o")
-        timed(lambda: [ops.q4_swiglu_gemm(g["gate"], g["up"], nt_i, dec.kt_h, dec.resid, out=dec.h, workspace=ws,
-                                          prefetch=True, norm_w=l["mlp_norm"], eps=c.rms_eps, packed=pk)
-                       for g, l in zip(G, L)], sum(g["gate"].numel() + g["up"].numel() for g in G), n_l,
-              "q4_swiglu_gemm")
-        timed(lambda: [ops.q4_gemm(g["down"], c.hidden // 32, kt_i, dec.h,
-                                   out=down_out if down_out is not None else dec.resid, accumulate=down_out is None,
-                                   workspace=ws, prefetch=True, packed=pk) for g in G],
-              sum(g["down"].numel() for g in G), n_l, "q4_gemm_down")
+        if getattr(dec, "swiglu_split", False):
+            # gate+up as one split-K GEMM, the SwiGLU in the down GEMM's x pre-pass
+            timed(lambda: [ops.q4_gemm(g["gu"], 2 * nt_i, dec.kt_h, dec.resid, out=dec.gu, workspace=ws,
+                                       prefetch=True, norm_w=l["mlp_norm"], eps=c.rms_eps, packed=pk)
+                           for g, l in zip(G, L)], sum(g["gu"].numel() for g in G), n_l, "q4_gemm_gate_up")
+            timed(lambda: [ops.q4_gemm(g["down"], c.hidden // 32, kt_i, dec.gu, out=down_out, workspace=ws,
+                                       prefetch=True, packed=pk, swiglu_in=True) for g in G],
+                  sum(g["down"].numel() for g in G), n_l, "q4_gemm_down_swiglu_in")
+        else:
+            timed(lambda: [ops.q4_swiglu_gemm(g["gate"], g["up"], nt_i, dec.kt_h, dec.resid, out=dec.h, workspace=ws,
+                                              prefetch=True, norm_w=l["mlp_norm"], eps=c.rms_eps, packed=pk)
+                           for g, l in zip(G, L)], sum(g["gate"].numel() + g["up"].numel() for g in G), n_l,
+                  "q4_swiglu_gemm")
+            timed(lambda: [ops.q4_gemm(g["down"], c.hidden // 32, kt_i, dec.h,
+                                       out=down_out if down_out is not None else dec.resid,
+                                       accumulate=down_out is None, workspace=ws, prefetch=True, packed=pk)
+                           for g in G], sum(g["down"].numel() for g in G), n_l, "q4_gemm_down")
     # the lm_head (q8, RMSNorm fused) once per step: the q8 GEMM on the packed head at GEMM
     # batches, else the GEMV
     nt_v = getattr(dec, "nt_v_local", getattr(dec, "nt_v", None))
@@ -751,7 +762,9 @@ def tp_parity(torch, world: int, rank: int) -> dict:
             del g
             tp.close()
             out["config4"][f"b{bsz}"] = {"cos": round(worst[0], 9), "rel": float(f"{worst[1]:.3e}"),
-                                         "how": "tcgen05 GEMM" if tp.use_gemm else "GEMV"} if rank == 0 else None
+                                         "how": "tcgen05 GEMM" if tp.use_gemm else "GEMV",
+                                         "mlp": "split (gate+up GEMM, SwiGLU in the down pre-pass)"
+                                         if tp.swiglu_split else "fused SwiGLU"} if rank == 0 else None
             del tp, one, full
             torch.cuda.empty_cache()
         except Exception as e:  # recorded in the line; every rank raises alike or the barrier times out

@@ -353,6 +353,17 @@ int b2_q4_swiglu_gemm_rmsnorm(const uint8_t* gate, const uint8_t* up, int n_tile
                               int batch, int ldx, const uint16_t* norm_w, float eps, uint16_t* h, int ldh, int flags,
                               void* workspace, size_t workspace_bytes, void* stream);
 
+/* The down projection with the SwiGLU in its x pre-pass: y = W h (fp32 form, flags as
+ * b2_q4_gemm) with h[b][k] = bf16(silu(bf16 g) * bf16 u), g = gu[b][k] and
+ * u = gu[b][K + k] (K = k_tiles*256): the SwiGLU epilogue's arithmetic
+ * (designs/granite_gemv/granite_mlp.py:172-181) applied to the fp32 outputs of a plain
+ * GEMM over the gate and up tile-rows stacked as one weight.  That GEMM can split K
+ * across CTAs (the fused SwiGLU form cannot: its epilogue needs whole sums), which
+ * fills the SMs when a tensor-parallel shard leaves few row tiles.
+ *   gu fp32 [batch][ldgu], 16-byte aligned, ldgu % 4 == 0, ldgu >= 2K. */
+int b2_q4_gemm_swiglu_in(const uint8_t* tiles, int n_tile_rows, int k_tiles, const float* gu, int batch, int ldgu,
+                          float* y, int ldy, int flags, void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

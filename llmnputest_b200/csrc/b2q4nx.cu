@@ -449,7 +449,7 @@ inline size_t tc_ws_bytes(int batch, int k_tiles) {
 int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_rows, int k_tiles, const uint16_t* x,
                    int batch, int ldx, void* y, int ldy, int flags, void* workspace, size_t ws_bytes,
                    void* stream, const float* xf = nullptr, const uint16_t* norm_w = nullptr, float eps = 0.f,
-                   int qt = b2::kQ4) {
+                   int qt = b2::kQ4, const float* gu = nullptr) {
   DevInfo di;
   int st = device_info(&di);
   if (st != B2_OK) return st;
@@ -459,10 +459,16 @@ int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_row
     if (!(eps >= 0.f)) return fail(B2_ERR_ARG, "eps must be >= 0");
     x = reinterpret_cast<const uint16_t*>(xf);  // satisfies the checks below; the pre-pass reads xf
   }
+  if (gu) {  // SwiGLU input: fp32 rows [batch][ldx] holding g at column k and u at K + k
+    if (xf || epi != b2::kTcEpiF32 || qt != b2::kQ4) return fail(B2_ERR_ARG, "SwiGLU input is for the plain q4 GEMM");
+    if (!aligned(gu, 16) || (ldx % 4)) return fail(B2_ERR_ALIGN, "gu must be 16-byte aligned with ldx %% 4 == 0");
+    if (ldx < 2 * k_tiles * 256) return fail(B2_ERR_ARG, "ldx %d < 2K %d (gate and up halves)", ldx, 2 * k_tiles * 256);
+    x = reinterpret_cast<const uint16_t*>(gu);  // satisfies the checks below; the pre-pass reads gu
+  }
   if (!w0 || !x || !y || (epi == b2::kTcEpiSwiglu && !w1)) return fail(B2_ERR_ARG, "null pointer argument");
   if (n_tile_rows < 1 || k_tiles < 1) return fail(B2_ERR_ARG, "bad tile shape %d x %d", n_tile_rows, k_tiles);
   if (batch < 1 || batch > b2::kTcMaxN) return fail(B2_ERR_ARG, "batch %d outside 1..%d", batch, b2::kTcMaxN);
-  if (ldx < k_tiles * 256 || ldx % (xf ? 4 : 8)) return fail(B2_ERR_ALIGN, "ldx %d: need >= K and aligned rows", ldx);
+  if (ldx < k_tiles * 256 || ldx % ((xf || gu) ? 4 : 8)) return fail(B2_ERR_ALIGN, "ldx %d: need >= K and aligned rows", ldx);
   if (ldy < n_tile_rows * 32) return fail(B2_ERR_ARG, "ldy %d < output rows %d", ldy, n_tile_rows * 32);
   if (!aligned(w0, 16) || (w1 && !aligned(w1, 16)) || !aligned(x, 16)) return fail(B2_ERR_ALIGN, "tiles and x must be 16-byte aligned");
   if (flags & ~(B2_GEMV_ACCUMULATE | B2_GEMV_PREFETCH | B2_GEMM_PACKED))
@@ -550,8 +556,10 @@ int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_row
   cfg.attrs = attr;
   cfg.numAttrs = pdl_for(kPdlGemmPrep) ? 1 : 0;
   b2::TcPrep pp = {};
-  pp.x = xf ? nullptr : reinterpret_cast<const __nv_bfloat16*>(x);
+  pp.x = (xf || gu) ? nullptr : reinterpret_cast<const __nv_bfloat16*>(x);
   pp.xf = xf;
+  pp.gu = gu;
+  pp.gu_half = k_tiles * 256;
   pp.norm_w = reinterpret_cast<const __nv_bfloat16*>(norm_w);
   pp.eps = eps;
   pp.ldx = ldx;
@@ -1209,6 +1217,12 @@ int b2_q4_swiglu_gemm(const uint8_t* gate, const uint8_t* up, int n_tile_rows, i
                       void* stream) {
   return tc_gemm_common(b2::kTcEpiSwiglu, gate, up, n_tile_rows, k_tiles, x, batch, ldx, h, ldh, flags, workspace,
                         workspace_bytes, stream);
+}
+
+int b2_q4_gemm_swiglu_in(const uint8_t* tiles, int n_tile_rows, int k_tiles, const float* gu, int batch, int ldgu,
+                          float* y, int ldy, int flags, void* workspace, size_t workspace_bytes, void* stream) {
+  return tc_gemm_common(b2::kTcEpiF32, tiles, nullptr, n_tile_rows, k_tiles, nullptr, batch, ldgu, y, ldy, flags,
+                        workspace, workspace_bytes, stream, nullptr, nullptr, 0.f, b2::kQ4, gu);
 }
 
 int b2_q4_gemm_rmsnorm(const uint8_t* tiles, int n_tile_rows, int k_tiles, const float* x, int batch, int ldx,

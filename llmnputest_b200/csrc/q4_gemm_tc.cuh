@@ -212,10 +212,15 @@ __host__ __device__ __forceinline__ uint32_t sw128_offset(int row, int k) {
 // x' = fp16(x * 2^e) written into the swizzled slice image; rows >= batch are 0.
 // With xf (fused RMSNorm) the row is bf16(xf * rsqrt(mean(xf^2) + eps) * norm_w), the
 // arithmetic of granite_rms_norm (designs/granite_gemv/granite_rmsnorm.h:45-80), from the
-// fp32 row xf [batch][ldx] instead of x.
+// fp32 row xf [batch][ldx] instead of x.  With gu (SwiGLU input) the row is
+// bf16(silu(bf16 g) * bf16 u) of the fp32 gate/up projections g = gu[n][k] and
+// u = gu[n][gu_half + k]: the SwiGLU epilogue's arithmetic (granite_mlp.py:172-181), here
+// run on the outputs of a plain split-K gate+up GEMM.
 struct TcPrep {
   const __nv_bfloat16* x;
   const float* xf;
+  const float* gu;
+  int gu_half;
   const __nv_bfloat16* norm_w;
   float eps;
   int ldx, batch, k, npad;
@@ -290,6 +295,24 @@ __global__ void __launch_bounds__(256) tc_x_prep_kernel(const TcPrep a) {
     o.w = pack_bf16x2_rn(nb(a1.z, bf16lo_to_f32(wv.w)), nb(a1.w, bf16hi_to_f32(wv.w)));
     return o;
   };
+  // bf16(silu(bf16 g) * bf16 u) of one chunk (SwiGLU input), as the fused epilogue
+  auto swiglu_chunk = [&](int c) {
+    const float* gr = a.gu + static_cast<size_t>(n) * a.ldx + c * 8;
+    const float4 g0 = *reinterpret_cast<const float4*>(gr), g1 = *reinterpret_cast<const float4*>(gr + 4);
+    const float4 u0 = *reinterpret_cast<const float4*>(gr + a.gu_half);
+    const float4 u1 = *reinterpret_cast<const float4*>(gr + a.gu_half + 4);
+    auto h = [](float g, float u) {
+      const float gb = __bfloat162float(__float2bfloat16_rn(g));
+      const float ub = __bfloat162float(__float2bfloat16_rn(u));
+      return __fdividef(gb, 1.f + __expf(-gb)) * ub;
+    };
+    uint4 o;
+    o.x = pack_bf16x2_rn(h(g0.x, u0.x), h(g0.y, u0.y));
+    o.y = pack_bf16x2_rn(h(g0.z, u0.z), h(g0.w, u0.w));
+    o.z = pack_bf16x2_rn(h(g1.x, u1.x), h(g1.y, u1.y));
+    o.w = pack_bf16x2_rn(h(g1.z, u1.z), h(g1.w, u1.w));
+    return o;
+  };
   auto finish_row = [&](float m) {  // exponent, and the zeroed output row for split-K
     const int e = live ? gemv_scale_exp(__float_as_uint(m)) : 0;
     if (threadIdx.x == 0) a.xexp[n] = e;
@@ -303,7 +326,13 @@ __global__ void __launch_bounds__(256) tc_x_prep_kernel(const TcPrep a) {
     uint4 v[kPrepRegChunks];
 #pragma unroll
     for (int i = 0; i < kPrepRegChunks; ++i) v[i] = make_uint4(0u, 0u, 0u, 0u);
-    if (a.xf) {
+    if (a.gu) {
+#pragma unroll
+      for (int i = 0; i < kPrepRegChunks; ++i) {
+        const int c = threadIdx.x + 256 * i;
+        if (live && c < nc) v[i] = swiglu_chunk(c);
+      }
+    } else if (a.xf) {
       float4 f[kPrepRegChunks][2];
       float ss = 0.f;
 #pragma unroll
@@ -362,6 +391,7 @@ __global__ void __launch_bounds__(256) tc_x_prep_kernel(const TcPrep a) {
     inv = rsqrtf(block_sum(ss) / static_cast<float>(k) + a.eps);
   }
   auto row8 = [&](int c) -> uint4 {
+    if (a.gu) return swiglu_chunk(c);
     if (!a.xf) return *reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(n) * a.ldx + c * 8);
     const float* xr = a.xf + static_cast<size_t>(n) * a.ldx + c * 8;
     return norm_chunk(c, *reinterpret_cast<const float4*>(xr), *reinterpret_cast<const float4*>(xr + 4), inv);

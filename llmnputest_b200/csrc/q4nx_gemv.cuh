@@ -40,11 +40,13 @@
 //                  8 row-block halves), x' as the B operand (N = batch);
 //                  after each 32-k block the d/m scaling into fp32 totals;
 //   epilogue:      warp totals -> shared memory -> CTA sum (fixed order) ->
-//                  split-K sum across a thread-block cluster through
-//                  distributed shared memory (fixed order) -> store.
-// Split-K across CTAs uses a cluster (no global workspace, deterministic);
-// when the groups outnumber the SMs the grid is persistent and the producer
-// runs ahead across group boundaries.
+//                  split-K: SwiGLU sums the cluster's partials through
+//                  distributed shared memory (fixed order, deterministic);
+//                  f32 adds them into y with global reductions (the order of
+//                  those fp32 adds, and so the last bits, vary between runs).
+// Split-K across CTAs uses a cluster (no global workspace); when the groups
+// outnumber the SMs the grid is persistent and the producer runs ahead across
+// group boundaries.
 #pragma once
 
 #include "b2_common.cuh"

@@ -182,15 +182,29 @@ def q8_gemm(packed: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tenso
 
 def q4_gemm(tiles: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tensor, out: torch.Tensor | None = None,
             accumulate: bool = False, workspace: torch.Tensor | None = None, prefetch: bool = False,
-            norm_w: torch.Tensor | None = None, eps: float = 0.0, packed: bool = False) -> torch.Tensor:
+            norm_w: torch.Tensor | None = None, eps: float = 0.0, packed: bool = False,
+            swiglu_in: bool = False) -> torch.Tensor:
     """fp32 y [B, N] = W x on the tcgen05 tensor cores (batches up to 256).
 
     With norm_w, x is the fp32 residual [B, K] and the GEMM multiplies
     bf16(rmsnorm(x) * norm_w), the norm done in its x pre-pass (b2_q4_gemm_rmsnorm).
+    With swiglu_in, x is the fp32 output [B, 2K] of a gate+up GEMM (gate columns first)
+    and the GEMM multiplies bf16(silu(bf16 g) * bf16 u), formed in its x pre-pass
+    (b2_q4_gemm_swiglu_in).
     packed: the tiles come from q4_gemm_pack (A is dequantised into tensor memory)."""
     _tiles(tiles, n_tile_rows, k_tiles, Q4_TILE_BYTES, "tiles")
     k, n = k_tiles * TILE_K, n_tile_rows * TILE_ROWS
-    x2 = _norm_in(x, norm_w, k) if norm_w is not None else _x2d(x, k)
+    if swiglu_in:
+        if norm_w is not None:
+            raise ValueError("swiglu_in and norm_w are exclusive")
+        _need(x, "x", torch.float32)
+        x2 = x.reshape(1, -1) if x.dim() == 1 else x
+        if x2.dim() != 2 or x2.shape[1] != 2 * k:
+            raise ValueError(f"swiglu_in wants x [B, {2 * k}] fp32 (gate columns, then up)")
+        if x2.stride(1) != 1 or x2.stride(0) % 4 or x2.data_ptr() % 16:
+            x2 = x2.contiguous()
+    else:
+        x2 = _norm_in(x, norm_w, k) if norm_w is not None else _x2d(x, k)
     b = x2.shape[0]
     if out is None:
         out = torch.zeros((b, n), dtype=torch.float32, device=x2.device)
@@ -199,7 +213,10 @@ def q4_gemm(tiles: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tensor
     flags = (GEMV_ACCUMULATE if accumulate else 0) | (GEMV_PREFETCH if prefetch else 0) | (GEMM_PACKED if packed else 0)
     wsp = _aligned_ws(ws) if workspace is None else _ptr(ws)
     wsn = ws.numel() - (256 if workspace is None else 0)
-    if norm_w is not None:
+    if swiglu_in:
+        _native.call("b2_q4_gemm_swiglu_in", _ptr(tiles), n_tile_rows, k_tiles, _ptr(x2), b, x2.stride(0),
+                     _ptr(out), out.stride(0), flags, wsp, wsn, _stream())
+    elif norm_w is not None:
         _native.call("b2_q4_gemm_rmsnorm", _ptr(tiles), n_tile_rows, k_tiles, _ptr(x2), b, x2.stride(0),
                      _ptr(norm_w), float(eps), _ptr(out), out.stride(0), flags, wsp, wsn, _stream())
     else:

@@ -7,11 +7,13 @@ tile bytes are never modified):
                    their q heads; its QKV weight is those heads' whole tile-rows
                    (q: grp*D rows per kv head, k and v: D rows each), and its KV
                    cache holds only its heads.  No collective.
-  O                the attention outputs are all-gathered (bf16), O is sharded by
-                   output rows (hidden/W rows = whole tile-rows) and its outputs
-                   all-gathered into every rank's replicated residual stream.
-                   (Sharding O by input columns would cut 256-wide K-tiles at
-                   W = 4 and 8: 640 or 320 columns per rank.)
+  O                by input columns: rank r owns the columns of its own q heads, so
+                   its attention output is its O input with no exchange.  Those
+                   columns (640 or 320 at W = 4 or 8) cut 256-wide K-tiles, so the
+                   shard is re-tiled by whole 32-column quantisation blocks (every
+                   code and scale kept, the last K-tile zero-padded) and the input
+                   row padded with zeros to match; the fp32 partial outputs are
+                   all-reduced (sum) into the residual.
   FFN              gate/up by intermediate rows (I/W rows each), SwiGLU local;
                    down by whole K-tiles of the intermediate axis (I/W/256 per
                    rank), its fp32 partials all-reduced (sum) into the residual.
@@ -80,8 +82,15 @@ class ShardPlan:
         per = n_rows // self.world
         return self.rank * per, (self.rank + 1) * per
 
-    def o_tile_rows(self) -> range:
-        return range(*self.row_range(self.hidden // TILE_ROWS))
+    def o_k_range(self) -> tuple[int, int]:
+        """Input columns of O this rank owns: its q heads' attention outputs."""
+        w = self.q_local * self.head_dim
+        return self.rank * w, (self.rank + 1) * w
+
+    @property
+    def o_k_tiles(self) -> int:
+        """K-tiles of this rank's O shard (its columns re-tiled from column 0, zero-padded)."""
+        return -(-self.q_local * self.head_dim // TILE_K)
 
     def ffn_tile_rows(self) -> range:
         return range(*self.row_range(self.intermediate // TILE_ROWS))
@@ -107,6 +116,37 @@ def take_k_tiles(tiles: torch.Tensor, n_tile_rows: int, k_tiles: int, tile_bytes
     return t.index_select(1, idx).reshape(-1).contiguous()
 
 
+def take_k_blocks(tiles: torch.Tensor, n_tile_rows: int, k_tiles: int, k0: int, k1: int) -> torch.Tensor:
+    """q4 columns [k0, k1) of every tile-row, re-tiled from column 0: [n_t][ceil((k1-k0)/256)][tile].
+
+    k0 and k1 are multiples of the 32-wide quantisation block, so every block moves whole
+    (its 32 d and 32 m entries and, per row block, its 256 nibble bytes) and every
+    weight keeps its exact codes and scales; blocks past k1 in the last K-tile are zero
+    (d = m = 0, codes 0: weight 0).  In a q4 tile (tools/q4nx.py:89-94) block kb owns scale
+    entries [32kb, 32kb+32) of each plane and nibble bytes rb*2048 + [256kb, 256kb+256).
+    """
+    blk = 32
+    if k0 % blk or k1 % blk or not 0 <= k0 < k1 <= k_tiles * TILE_K:
+        raise ValueError(f"columns [{k0}, {k1}) are not whole 32-blocks inside K = {k_tiles * TILE_K}")
+    t = tiles.view(n_tile_rows, k_tiles, Q4_TILE_BYTES)
+    per_tile = TILE_K // blk  # 8 blocks
+    # the four byte runs of every block: d, m, nibbles of row block 0, of row block 1
+    runs = [t[:, :, 0:512].reshape(n_tile_rows, k_tiles * per_tile, 64),
+            t[:, :, 512:1024].reshape(n_tile_rows, k_tiles * per_tile, 64),
+            t[:, :, 1024:3072].reshape(n_tile_rows, k_tiles * per_tile, 256),
+            t[:, :, 3072:5120].reshape(n_tile_rows, k_tiles * per_tile, 256)]
+    nb = (k1 - k0) // blk
+    kt_out = -(-nb // per_tile)
+    out = torch.zeros(n_tile_rows, kt_out, Q4_TILE_BYTES, dtype=torch.uint8, device=tiles.device)
+    offs = (0, 512, 1024, 3072)
+    for run, off in zip(runs, offs):
+        w = run.shape[2]
+        sel = torch.zeros(n_tile_rows, kt_out * per_tile, w, dtype=torch.uint8, device=tiles.device)
+        sel[:, :nb] = run[:, k0 // blk:k1 // blk]
+        out[:, :, off:off + per_tile * w] = sel.view(n_tile_rows, kt_out, per_tile * w)
+    return out.reshape(-1)
+
+
 def shard_weights(full: dict, plan: ShardPlan) -> dict:
     """One rank's slice of a full (unsharded) weight dict in the layout of decode.Q4Decoder."""
     kt_h = plan.hidden // TILE_K
@@ -117,7 +157,7 @@ def shard_weights(full: dict, plan: ShardPlan) -> dict:
     for L in full["layers"]:
         out["layers"].append({
             "qkv": take_tile_rows(L["qkv"], kt_h, Q4_TILE_BYTES, plan.qkv_tile_rows()),
-            "o": take_tile_rows(L["o"], kt_q, Q4_TILE_BYTES, plan.o_tile_rows()),
+            "o": take_k_blocks(L["o"], nt_h, kt_q, *plan.o_k_range()),
             "gate": take_tile_rows(L["gate"], kt_h, Q4_TILE_BYTES, plan.ffn_tile_rows()),
             "up": take_tile_rows(L["up"], kt_h, Q4_TILE_BYTES, plan.ffn_tile_rows()),
             "down": take_k_tiles(L["down"], nt_h, kt_i, Q4_TILE_BYTES, plan.down_k_tiles()),
@@ -129,25 +169,39 @@ def shard_weights(full: dict, plan: ShardPlan) -> dict:
     return out
 
 
+def tp_exchange_layout(cfg, batch: int, world: int) -> list:
+    """The peer buffers of TPDecoder: the replicated residual, one slot array per all-reduce
+    seam (O and down alternate, so a rank never rewrites a slot another rank may still be
+    summing: between two uses of one array every rank has entered the other seam's
+    exchange), and the gathered logits."""
+    return [("resid", (batch, cfg.hidden), torch.float32),
+            ("slots_o", (world, batch, cfg.hidden), torch.float32),
+            ("slots", (world, batch, cfg.hidden), torch.float32),
+            ("logits", (batch, cfg.vocab), torch.float32)]
+
+
 class TPDecoder:
     """Tensor-parallel decode step on this rank's shard.
 
     comm selects how the ranks meet at the seams of a layer:
-      "peer"        (GPU default) the exchanges of peer.py: the attention heads are
-                    gathered into every rank's copy of the attention output, each rank
-                    adds its O rows into every rank's copy of the residual stream, and
-                    the down projection's partials are all-reduced into it (in rank order,
-                    so every copy is bit-identical): three small kernels per layer that
-                    store straight into the other GPUs' memory, captured in the step's
-                    CUDA graph.
+      "peer"        (GPU default) the exchanges of peer.py: the O and down projections'
+                    fp32 partials are all-reduced into every rank's copy of the residual
+                    stream (summed in rank order, so every copy is bit-identical): two
+                    small kernels per layer that store straight into the other GPUs'
+                    memory, captured in the step's CUDA graph; the logits are gathered
+                    once per step.
       "collective"  torch.distributed all_gather / all_reduce (NCCL on GPUs, gloo on CPU).
     `xchg` (comm="peer"): an exchange object with .buffers, .gather(src, name, add_base)
     and .allreduce_add(src, name, y); built from peer.PeerRegion when not given.
     Batches of gemm_min_batch and more run the projections on the tcgen05 GEMM, as
-    decode.Q4Decoder does."""
+    decode.Q4Decoder does.  swiglu_split (GEMM batches): gate and up as one plain GEMM
+    over their stacked tile-rows, which splits K over CTAs, with the SwiGLU formed in the
+    down GEMM's x pre-pass -- instead of the fused SwiGLU GEMM, whose one CTA per 64
+    gate + 64 up rows leaves most SMs idle on a shard; None: split when those row tiles
+    would fill at most half the SMs."""
 
     def __init__(self, cfg, batch: int, ctx_max: int, shard: dict, plan: ShardPlan, device=None, ops=None,
-                 comm: str | None = None, xchg=None, gemm_min_batch: int = 9):
+                 comm: str | None = None, xchg=None, gemm_min_batch: int = 9, swiglu_split: bool | None = None):
         if ops is None:
             from . import ops  # the GPU path; tests of the host logic may pass another implementation
         self.ops = ops
@@ -163,7 +217,7 @@ class TPDecoder:
         self.kt_h, self.kt_q, self.kt_i = c.hidden // TILE_K, c.n_heads * c.head_dim // TILE_K, c.intermediate // TILE_K
         self.kt_i_local = self.kt_i // W
         self.nt_qkv_local = len(p.qkv_tile_rows())
-        self.nt_o_local = c.hidden // TILE_ROWS // W
+        self.kt_o_local = p.o_k_tiles
         self.nt_i_local = c.intermediate // TILE_ROWS // W
         self.nt_v_local = c.vocab // TILE_ROWS // W
         d = c.head_dim
@@ -173,8 +227,10 @@ class TPDecoder:
         self.x_in = torch.zeros(batch, c.hidden, dtype=torch.float32, device=dev)
         self.xn = torch.zeros(batch, c.hidden, dtype=torch.bfloat16, device=dev)
         self.qkv = torch.zeros(batch, self.nt_qkv_local * TILE_ROWS, dtype=torch.float32, device=dev)
-        self.attn_local = torch.zeros(batch, p.q_local * d, dtype=torch.bfloat16, device=dev)
-        self.o_local = torch.zeros(batch, c.hidden // W, dtype=torch.float32, device=dev)
+        # this rank's heads' attention output = its O input, zero past q_local*d (the padding
+        # columns of the re-tiled O shard; the attention writes only the first q_local*d)
+        self.attn_local = torch.zeros(batch, self.kt_o_local * TILE_K, dtype=torch.bfloat16, device=dev)
+        self.o_part = torch.zeros(batch, c.hidden, dtype=torch.float32, device=dev)
         self.h = torch.zeros(batch, c.intermediate // W, dtype=torch.bfloat16, device=dev)
         self.down = torch.zeros(batch, c.hidden, dtype=torch.float32, device=dev)
         self.logits_local = torch.zeros(batch, c.vocab // W, dtype=torch.float32, device=dev)
@@ -182,36 +238,40 @@ class TPDecoder:
         if comm == "peer":
             if xchg is None:
                 from .peer import PeerExchange
-                xchg = PeerExchange([("attn", (batch, c.n_heads * d), torch.bfloat16),
-                                     ("resid", (batch, c.hidden), torch.float32),
-                                     ("slots", (W, batch, c.hidden), torch.float32),
-                                     ("logits", (batch, c.vocab), torch.float32)], device=dev)
+                xchg = PeerExchange(tp_exchange_layout(cfg, batch, W), device=dev)
             self.xchg = xchg
-            self.attn = xchg.buffers["attn"]
             self.resid = xchg.buffers["resid"]
             self.logits = xchg.buffers["logits"]
         else:
             self.xchg = None
             # gathered buffers are [W*B, n] (rank-major), viewed as [W, B, n] when merged
-            self.attn_all = torch.zeros(W * batch, p.q_local * d, dtype=torch.bfloat16, device=dev)
-            self.attn = torch.zeros(batch, c.n_heads * d, dtype=torch.bfloat16, device=dev)
-            self.o_all = torch.zeros(W * batch, c.hidden // W, dtype=torch.float32, device=dev)
             self.logits_all = torch.zeros(W * batch, c.vocab // W, dtype=torch.float32, device=dev)
             self.resid = torch.zeros(batch, c.hidden, dtype=torch.float32, device=dev)
             self.logits = torch.zeros(batch, c.vocab, dtype=torch.float32, device=dev)
         ws = ops.gqa_decode_workspace_bytes(batch, p.q_local, p.kv_local, d, ctx_max)
         self.attn_ws = torch.empty(max(ws, 1), dtype=torch.uint8, device=dev)
         self.use_gemm = batch >= gemm_min_batch
+        self.swiglu_split = False
         if self.use_gemm:
-            nbytes = ops.gemm_workspace_bytes(batch, max(self.kt_h, self.kt_q, self.kt_i_local))
+            nbytes = ops.gemm_workspace_bytes(batch, max(self.kt_h, self.kt_o_local, self.kt_i_local))
             self.gemm_ws_raw = torch.empty(nbytes + 256, dtype=torch.uint8, device=dev)
             off = (256 - self.gemm_ws_raw.data_ptr() % 256) % 256
             self.gemm_ws = self.gemm_ws_raw[off:off + nbytes]
             # this rank's projection shards repacked once for the GEMM (A dequantised into TMEM)
-            shapes = {"qkv": (self.nt_qkv_local, self.kt_h), "o": (self.nt_o_local, self.kt_q),
-                      "gate": (self.nt_i_local, self.kt_h), "up": (self.nt_i_local, self.kt_h),
+            if swiglu_split is None:
+                sms = torch.cuda.get_device_properties(dev).multi_processor_count if dev.type == "cuda" else 148
+                swiglu_split = self.nt_i_local // 2 <= sms // 2
+            self.swiglu_split = bool(swiglu_split)
+            shapes = {"qkv": (self.nt_qkv_local, self.kt_h), "o": (c.hidden // TILE_ROWS, self.kt_o_local),
                       "down": (cfg.hidden // TILE_ROWS, self.kt_i_local)}
+            if not swiglu_split:
+                shapes.update(gate=(self.nt_i_local, self.kt_h), up=(self.nt_i_local, self.kt_h))
             self.wg = [{k: self.ops.q4_gemm_pack(L[k], *shp) for k, shp in shapes.items()} for L in self.w["layers"]]
+            if swiglu_split:
+                for G, L in zip(self.wg, self.w["layers"]):
+                    G["gu"] = self.ops.q4_gemm_pack(torch.cat([L["gate"], L["up"]]), 2 * self.nt_i_local, self.kt_h)
+                # gate outputs in columns [0, I/W), up outputs in [I/W, 2I/W)
+                self.gu = torch.zeros(batch, 2 * c.intermediate // W, dtype=torch.float32, device=dev)
             self.lm_packed = self.ops.q8_gemm_pack(self.w["lm_head"], self.nt_v_local, self.kt_h)
 
     def close(self) -> None:
@@ -221,27 +281,13 @@ class TPDecoder:
         self.xchg = None
 
     # ---------------------------------------------------------------- seams
-    def _gather_heads(self) -> torch.Tensor:
-        W, B, qd = self.plan.world, self.batch, self.attn_local.shape[1]
-        if W == 1:
-            return self.attn_local
+    def _reduce_o(self) -> None:
         if self.comm == "peer":
-            self.xchg.gather(self.attn_local, "attn")
+            self.xchg.allreduce_add(self.o_part, "slots_o", self.resid)
         else:
-            dist.all_gather_into_tensor(self.attn_all, self.attn_local)
-            # rank-major [W][B][q_local*D] -> [B][Hq*D] (head order = rank order)
-            self.attn.view(B, W, qd).copy_(self.attn_all.view(W, B, qd).permute(1, 0, 2))
-        return self.attn
-
-    def _add_o_rows(self) -> None:
-        W, B = self.plan.world, self.batch
-        if self.comm == "peer":
-            self.xchg.gather(self.o_local, "resid", add_base=self.resid)
-        elif W > 1:
-            dist.all_gather_into_tensor(self.o_all, self.o_local)
-            self.resid.view(B, W, -1).add_(self.o_all.view(W, B, -1).permute(1, 0, 2))
-        else:
-            self.resid.add_(self.o_local)
+            if self.plan.world > 1:
+                dist.all_reduce(self.o_part)
+            self.resid.add_(self.o_part)
 
     def _reduce_down(self) -> None:
         if self.comm == "peer":
@@ -278,16 +324,21 @@ class TPDecoder:
                                  out=self.qkv, prefetch=True)
             ops.gqa_decode(self.qkv[:, :qd], self.qkv[:, qd:qd + kd], self.qkv[:, qd + kd:], self.k_cache[li],
                            self.v_cache[li], self.pos, n_q_heads=p.q_local, n_kv_heads=p.kv_local,
-                           theta=c.rope_theta, scale=d ** -0.5, max_len=self.ctx_max, out=self.attn_local,
+                           theta=c.rope_theta, scale=d ** -0.5, max_len=self.ctx_max, out=self.attn_local[:, :qd],
                            workspace=self.attn_ws, prefetch_kv=True)
-            a = self._gather_heads()
             if self.use_gemm:
-                ops.q4_gemm(G["o"], self.nt_o_local, self.kt_q, a, out=self.o_local, workspace=ws, prefetch=True,
-                            packed=True)
+                ops.q4_gemm(G["o"], c.hidden // TILE_ROWS, self.kt_o_local, self.attn_local, out=self.o_part,
+                            workspace=ws, prefetch=True, packed=True)
             else:
-                ops.q4_gemv(L["o"], self.nt_o_local, self.kt_q, a, out=self.o_local, prefetch=True)
-            self._add_o_rows()
-            if self.use_gemm:
+                ops.q4_gemv(L["o"], c.hidden // TILE_ROWS, self.kt_o_local, self.attn_local, out=self.o_part,
+                            prefetch=True)
+            self._reduce_o()
+            if self.swiglu_split:
+                ops.q4_gemm(G["gu"], 2 * self.nt_i_local, self.kt_h, self.resid, out=self.gu, workspace=ws,
+                            prefetch=True, norm_w=L["mlp_norm"], eps=c.rms_eps, packed=True)
+                ops.q4_gemm(G["down"], c.hidden // TILE_ROWS, self.kt_i_local, self.gu, out=self.down, workspace=ws,
+                            prefetch=True, packed=True, swiglu_in=True)
+            elif self.use_gemm:
                 ops.q4_swiglu_gemm(G["gate"], G["up"], self.nt_i_local, self.kt_h, self.resid, out=self.h,
                                    workspace=ws, prefetch=True, norm_w=L["mlp_norm"], eps=c.rms_eps, packed=True)
                 ops.q4_gemm(G["down"], c.hidden // TILE_ROWS, self.kt_i_local, self.h, out=self.down, workspace=ws,

@@ -9,6 +9,7 @@ token, fp32 accumulation."""
 import numpy as np
 import pytest
 import torch
+from ml_dtypes import bfloat16
 
 from oracle import q4nx_oracle as orc
 from tests.test_gpu_gemv import dev_bf16, dev_u8
@@ -289,3 +290,51 @@ def test_q8_gemm_vs_oracle(cuda, n_t, k_t, bsz, norm):
     ref = np.stack([orc.gemv_q8(w, xr[b], n_t, k_t) for b in range(bsz)])
     _check(y.cpu().numpy(), ref, what=("q8", n_t, k_t, bsz, norm))
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("nt_i,kt_h,nt_h,bsz", [(16, 2, 4, 32), (64, 3, 8, 100), (32, 10, 20, 256)])
+def test_swiglu_in_gemm_vs_oracle(cuda, nt_i, kt_h, nt_h, bsz):
+    """The split MLP: gate and up as one split-K GEMM over their stacked tile-rows (fp32
+    outputs), then the down GEMM whose x pre-pass forms bf16(silu(bf16 g) * bf16 u)
+    (granite_mlp.py:172-181).  Against the numpy oracle and against the fused SwiGLU GEMM
+    feeding the plain down GEMM; the bars are the SwiGLU bars (a token may move a bf16 ulp
+    on g and u before SiLU)."""
+    from llmnputest_b200 import ops
+    rng = np.random.default_rng(9100 + nt_i + kt_h + bsz)
+    kt_i = nt_i * 32 // 256
+    gate = orc.synth_q4_tiles(rng, nt_i * kt_h)
+    up = orc.synth_q4_tiles(rng, nt_i * kt_h)
+    down = orc.synth_q4_tiles(rng, nt_h * kt_i)
+    x = orc.synth_bf16(rng, (bsz, kt_h * 256)).astype(np.float32)
+    gu_w = ops.q4_gemm_pack(dev_u8(np.concatenate([gate.reshape(-1), up.reshape(-1)])), 2 * nt_i, kt_h)
+    down_p = ops.q4_gemm_pack(dev_u8(down), nt_h, kt_i)
+    gu = ops.q4_gemm(gu_w, 2 * nt_i, kt_h, dev_bf16(x), packed=True, prefetch=True)
+    y = ops.q4_gemm(down_p, nt_h, kt_i, gu, packed=True, prefetch=True, swiglu_in=True)
+    h = ops.q4_swiglu_gemm(ops.q4_gemm_pack(dev_u8(gate), nt_i, kt_h), ops.q4_gemm_pack(dev_u8(up), nt_i, kt_h),
+                           nt_i, kt_h, dev_bf16(x), packed=True)
+    y_fused = ops.q4_gemm(down_p, nt_h, kt_i, h, packed=True)
+    torch.cuda.synchronize()
+    bf = lambda a: np.asarray(a, np.float32).astype(bfloat16).astype(np.float32)
+    g = bf(np.stack([orc.gemv_q4(gate, x[b], nt_i, kt_h) for b in range(bsz)]))
+    u = bf(np.stack([orc.gemv_q4(up, x[b], nt_i, kt_h) for b in range(bsz)]))
+    hb = bf(g / (1.0 + np.exp(-g.astype(np.float64))) * u)
+    ref = np.stack([orc.gemv_q4(down, hb[b], nt_h, kt_i) for b in range(bsz)])
+    _check(y.cpu().numpy(), ref, 0.9999, 2e-2, ("swiglu_in", nt_i, kt_h, bsz))
+    _check(y.cpu().numpy(), y_fused.cpu().numpy(), 0.9999, 2e-2, ("swiglu_in vs fused", nt_i, kt_h, bsz))
+    # the gate/up GEMM alone is the plain GEMM on the stacked rows
+    _check(gu[:, :nt_i * 32].cpu().numpy(), np.stack([orc.gemv_q4(gate, x[b], nt_i, kt_h) for b in range(bsz)]),
+           what="gate half")
+    assert ops.device_error() == 0
+
+
+def test_swiglu_in_argument_errors(cuda):
+    from llmnputest_b200 import _native, ops
+    w = torch.zeros(4 * 2 * 5120, dtype=torch.uint8, device=cuda)
+    with pytest.raises(ValueError):
+        ops.q4_gemm(w, 4, 2, torch.zeros(32, 512, device=cuda), swiglu_in=True)  # needs [B, 2K]
+    ws = torch.empty(ops.gemm_workspace_bytes(32, 2), dtype=torch.uint8, device=cuda)
+    y = torch.zeros(32, 128, device=cuda)
+    gu = torch.zeros(32, 1024, device=cuda)
+    with pytest.raises(_native.B2Error):  # ldgu below 2K
+        _native.call("b2_q4_gemm_swiglu_in", w.data_ptr(), 4, 2, gu.data_ptr(), 32, 512, y.data_ptr(), 128, 0,
+                     ws.data_ptr(), ws.numel(), None)

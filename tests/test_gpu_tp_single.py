@@ -1,0 +1,64 @@
+"""The tensor-parallel decoder's own code paths on one GPU (world 1): O as fp32 partials
+over the rank's input columns added into the residual, and the split MLP (gate and up as
+one split-K GEMM over their stacked tile-rows, the SwiGLU in the down GEMM's x pre-pass)
+against the fused SwiGLU GEMM and against decode.Q4Decoder on the same weights and cache
+history.  The multi-GPU runs (tests/test_multigpu_tp.py) need two GPUs; this file keeps
+the sharded step's host logic and kernels checked on a one-GPU box."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import q4nx_oracle as orc
+from tests.test_multigpu_tp import NS_COS, NS_REL, SPLIT_COS, SPLIT_REL, _weights
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("bsz,split", [(2, None), (10, False), (10, True), (40, True)])
+def test_tp_world1_matches_single_gpu_step(bsz, split):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from llmnputest_b200 import ops
+    from llmnputest_b200.decode import DecoderConfig, Q4Decoder
+    from llmnputest_b200.tp import ShardPlan, TPDecoder, shard_weights
+    from tests.test_gpu_gemv import dev_bf16, dev_u8
+
+    cfg = DecoderConfig(n_layers=2, vocab=4096)
+    ctx = 128
+    rng = np.random.default_rng(31 + bsz)
+    W = _weights(cfg, rng)
+    dev_w = {"layers": [{k: (dev_u8(v) if v.dtype == np.uint8 else dev_bf16(v.astype(np.float32)))
+                         for k, v in L.items()} for L in W["layers"]],
+             "final_norm": dev_bf16(W["final_norm"].astype(np.float32)), "lm_head": dev_u8(W["lm_head"])}
+    plan = ShardPlan(cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.hidden, cfg.intermediate, cfg.vocab, 1, 0)
+    tp = TPDecoder(cfg, bsz, ctx, shard_weights(dev_w, plan), plan, swiglu_split=split)
+    if split is not None:
+        assert tp.swiglu_split == split
+    one = Q4Decoder(cfg, bsz, ctx, weights=dev_w)
+    for li in range(2):
+        kc = orc.synth_bf16(rng, (bsz, cfg.n_kv_heads, ctx, cfg.head_dim)).astype(np.float32)
+        vc = orc.synth_bf16(rng, (bsz, cfg.n_kv_heads, ctx, cfg.head_dim)).astype(np.float32)
+        for d in (tp, one):
+            d.k_cache[li].copy_(dev_bf16(kc))
+            d.v_cache[li].copy_(dev_bf16(vc))
+    g = tp.capture()
+    pos = (np.arange(bsz, dtype=np.int32) * 7 + 17) % (ctx - 4)
+    for step in range(2):
+        x = rng.standard_normal((bsz, cfg.hidden)).astype(np.float32)
+        for d in (tp, one):
+            d.x_in.copy_(torch.from_numpy(x))
+            d.pos.copy_(torch.from_numpy(pos))
+        g.replay()
+        ref = one.step()
+        torch.cuda.synchronize()
+        got, ref = tp.logits.cpu().numpy(), ref.cpu().numpy()
+        # the fused SwiGLU on both sides: only the O seam's fp32 order differs, the
+        # north-star bar; the split MLP: the SwiGLU step-composition bar
+        c_min, r_max = (SPLIT_COS, SPLIT_REL) if tp.swiglu_split else (NS_COS, NS_REL)
+        for b in range(bsz):
+            cos, rel = orc.compare(got[b], ref[b])
+            assert cos >= c_min and rel <= r_max, (step, b, cos, rel)
+        pos = pos + 1
+    assert ops.device_error() == 0
+    del g

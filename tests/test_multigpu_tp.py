@@ -1,7 +1,7 @@
 """Tensor-parallel decode on 2 GPUs against the oracle composition and the single-GPU step.
 
-Each rank holds its shard of the same seeded weights (kv heads, O rows, FFN rows and
-down K-tiles, vocab rows) and its kv heads' cache history.  Two steps run at advancing
+Each rank holds its shard of the same seeded weights (kv heads, O input columns, FFN
+rows and down K-tiles, vocab rows) and its kv heads' cache history.  Two steps run at advancing
 positions; rank 0 checks the logits against
 
   * the numpy composition of the reference's per-op oracles (tests/test_gpu_decode.py
@@ -28,6 +28,11 @@ pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 # re-rounding on either side), and the north-star bar for TP against the 1-GPU step
 ORACLE_COS, ORACLE_REL = 0.9999, 1e-2
 NS_COS, NS_REL = 0.99999, 1e-3
+# TP with the split MLP against the 1-GPU step's fused SwiGLU: the two forms sum g and u
+# in another fp32 order before narrowing them to bf16, so an h element on a rounding
+# boundary moves a bf16 ulp; over a two-layer step that is the bar of the tensor-core
+# step against the GEMV step (tests/test_gpu_gemm_tc.py::test_decode_step_gemm_matches_gemv)
+SPLIT_COS, SPLIT_REL = 0.9999, 1e-2
 
 
 def _port():
@@ -110,7 +115,8 @@ def _rank(rank, world, port, out_path, bsz, comm):
                 one = single.step().cpu().numpy()
                 ref = _oracle_step(cfg, W, kc, vc, x, pos)
                 for b in range(bsz):
-                    results.append((step, b, *orc.compare(got[b], ref[b]), *orc.compare(got[b], one[b])))
+                    results.append((step, b, *orc.compare(got[b], ref[b]), *orc.compare(got[b], one[b]),
+                                    tp.swiglu_split))
             pos = pos + 1
             # rank 0's oracle takes seconds: hold the other rank on the host, not in an
             # exchange's bounded wait on the GPU
@@ -140,6 +146,7 @@ def test_tp2_matches_oracle_and_single_gpu(tmp_path, bsz, comm):
     for p in procs:
         p.join(timeout=300)
         assert p.exitcode == 0
-    for step, b, cos_o, rel_o, cos_1, rel_1 in torch.load(out):
+    for step, b, cos_o, rel_o, cos_1, rel_1, split in torch.load(out):
         assert cos_o >= ORACLE_COS and rel_o <= ORACLE_REL, ("oracle", step, b, cos_o, rel_o)
-        assert cos_1 >= NS_COS and rel_1 <= NS_REL, ("single gpu", step, b, cos_1, rel_1)
+        c_min, r_max = (SPLIT_COS, SPLIT_REL) if split else (NS_COS, NS_REL)
+        assert cos_1 >= c_min and rel_1 <= r_max, ("single gpu", step, b, cos_1, rel_1, split)

@@ -16,7 +16,7 @@ from ml_dtypes import bfloat16
 
 from oracle import q4nx_oracle as orc
 from llmnputest_b200.decode import DecoderConfig
-from llmnputest_b200.tp import ShardPlan, TPDecoder, shard_weights
+from llmnputest_b200.tp import ShardPlan, TPDecoder, shard_weights, take_k_blocks, tp_exchange_layout
 
 CFG = DecoderConfig(n_layers=2, hidden=512, n_heads=8, n_kv_heads=2, head_dim=64, intermediate=1024, vocab=512)
 
@@ -103,6 +103,9 @@ def test_shards_reassemble_full_projections(world):
     h = orc.synth_bf16(rng, cfg.intermediate)
     full_down = orc.gemv_q4(L["down"].numpy(), h, cfg.hidden // 32, kt_i)
     down_sum = np.zeros(cfg.hidden)
+    a = orc.synth_bf16(rng, cfg.n_heads * 64)  # attention output, all heads
+    full_o = orc.gemv_q4(L["o"].numpy(), a, cfg.hidden // 32, cfg.n_heads * 64 // 256)
+    o_sum = np.zeros(cfg.hidden)
     heads = []
     for r in range(world):
         plan = ShardPlan(cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.hidden, cfg.intermediate, cfg.vocab, world, r)
@@ -113,8 +116,36 @@ def test_shards_reassemble_full_projections(world):
         heads.append(qkv[:plan.q_local * 64])
         ks = list(plan.down_k_tiles())
         down_sum += orc.gemv_q4(S["down"].numpy(), h[ks[0] * 256:(ks[-1] + 1) * 256], cfg.hidden // 32, len(ks))
+        k0, k1 = plan.o_k_range()
+        a_loc = np.zeros(plan.o_k_tiles * 256, dtype=a.dtype)  # the rank's heads, zero-padded
+        a_loc[:k1 - k0] = a[k0:k1]
+        o_sum += orc.gemv_q4(S["o"].numpy(), a_loc, cfg.hidden // 32, plan.o_k_tiles)
     assert np.array_equal(np.concatenate(heads), full_qkv[:cfg.n_heads * 64])  # q heads in rank order
     np.testing.assert_allclose(down_sum, full_down, rtol=1e-4, atol=1e-3 * np.abs(full_down).max())
+    np.testing.assert_allclose(o_sum, full_o, rtol=1e-4, atol=1e-3 * np.abs(full_o).max())
+
+
+@pytest.mark.parametrize("k0,k1", [(0, 256), (64, 320), (640, 1280), (320, 640), (2048 - 32, 2048), (96, 1056)])
+def test_take_k_blocks_moves_whole_blocks(k0, k1):
+    """Re-tiling by 32-column blocks keeps every dequantised weight bit-identical and pads
+    the last K-tile with exact zeros."""
+    rng = np.random.default_rng(k0 + 7 * k1)
+    n_t, k_t = 3, 8
+    tiles = orc.synth_q4_tiles(rng, n_t * k_t)
+    out = take_k_blocks(torch.from_numpy(tiles.reshape(-1)), n_t, k_t, k0, k1).numpy()
+    kt_out = -(-(k1 - k0) // 256)
+    assert out.size == n_t * kt_out * 5120
+    full = orc.q4_matrix(tiles.reshape(-1), n_t, k_t)
+    got = orc.q4_matrix(out, n_t, kt_out)
+    assert np.array_equal(got[:, :k1 - k0], full[:, k0:k1])
+    assert not got[:, k1 - k0:].any()
+
+
+@pytest.mark.parametrize("k0,k1", [(16, 256), (0, 300), (256, 256), (0, 2304)])
+def test_take_k_blocks_rejects_partial_blocks(k0, k1):
+    tiles = torch.zeros(2 * 8 * 5120, dtype=torch.uint8)
+    with pytest.raises(ValueError):
+        take_k_blocks(tiles, 2, 8, k0, k1)
 
 
 def _free_port():
@@ -167,9 +198,7 @@ def _run_rank(rank, world, port, x, pos, ctx, result_path, comm="collective"):
         xchg = None
         if comm == "peer":
             b, d = x.shape[1], CFG.head_dim
-            xchg = GlooExchange([("attn", (b, CFG.n_heads * d), torch.bfloat16), ("resid", (b, CFG.hidden), torch.float32),
-                                 ("slots", (world, b, CFG.hidden), torch.float32),
-                                 ("logits", (b, CFG.vocab), torch.float32)])
+            xchg = GlooExchange(tp_exchange_layout(CFG, b, world))
         dec = TPDecoder(CFG, x.shape[1], ctx, shard_weights(W, plan), plan, device="cpu", ops=OracleOps(), comm=comm,
                         xchg=xchg)
         for step in range(2):
