@@ -89,6 +89,8 @@ inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_
 //   B2Q4NX_MAX_STAGES    cap on the shared-memory pipeline depth (1..8)
 //   B2Q4NX_TC_SPLITS / _TC_RAW / _TC_XSTAGES / _TC_ABUFS   tensor-core GEMM split-K
 //                        count, raw and x pipeline depths, A buffers per slice
+//   B2Q4NX_TC_PRE_RAW    raw stages the GEMM issues before its PDL wait (default: its
+//                        whole raw ring; 2-4 measured the same, 1 slower)
 //   B2Q4NX_TC_PREP_EARLY 1: the GEMM's x pre-pass releases the GEMM before its own wait
 //   B2Q4NX_PDL_MASK      launch kinds that use PDL: 1 GEMV, 2 GEMM pre-pass, 4 GEMM,
 //                        8 attention, 16 exchange, 32 other (default 0x37)
@@ -100,6 +102,7 @@ struct Tuning {
   int ctas_per_sm = 0;
   int max_stages = b2::kMaxStages;
   int tc_splits = 0, tc_raw = 0, tc_xst = 0, tc_abufs = 0;  // tensor-core GEMM overrides (0 = plan)
+  int tc_pre_raw = 0;  // raw stages the GEMM issues before its PDL wait (0 = all of its ring)
   // GEMM x pre-pass releases the GEMM before its own PDL wait (off: after an attention
   // call the GEMM's CTAs, over half an SM's shared memory each, would take SMs from it)
   int tc_prep_early = 0;
@@ -133,6 +136,7 @@ const Tuning& tuning() {
     if (const char* e = getenv("B2Q4NX_TC_RAW")) v.tc_raw = std::max(0, std::min(4, atoi(e)));
     if (const char* e = getenv("B2Q4NX_TC_XSTAGES")) v.tc_xst = std::max(0, std::min(8, atoi(e)));
     if (const char* e = getenv("B2Q4NX_TC_ABUFS")) v.tc_abufs = std::max(0, std::min(2, atoi(e)));
+    if (const char* e = getenv("B2Q4NX_TC_PRE_RAW")) v.tc_pre_raw = std::max(0, std::min(8, atoi(e)));
     if (const char* e = getenv("B2Q4NX_TC_PREP_EARLY")) v.tc_prep_early = atoi(e) != 0;
     if (const char* e = getenv("B2Q4NX_PDL_MASK")) v.pdl_mask = static_cast<int>(strtol(e, nullptr, 0)) & 0x3F;
     if (const char* e = getenv("B2Q4NX_ATTN_WAVE")) v.attn_wave = atoi(e) != 0;
@@ -585,6 +589,7 @@ int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_row
   p.batch = batch;
   p.npad = npad;
   p.raw_stages = raw_stages;
+  p.pre_raw = tuning().tc_pre_raw > 0 ? std::min(raw_stages, tuning().tc_pre_raw) : raw_stages;
   p.x_stages = x_stages;
   p.a_bufs = a_bufs;
   p.y = y;

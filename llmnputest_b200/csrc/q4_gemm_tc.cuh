@@ -98,6 +98,7 @@ struct TcParams {
   const int* xexp;     // [npad] exponents e (x' = x * 2^e)
   int batch, npad;
   int raw_stages, x_stages;
+  int pre_raw;  // raw stages issued before the wait on the preceding kernel (<= raw_stages)
   int a_bufs;  // A slots per 64-k slice (1 or 2)
   void* y;     // fp32 [batch][ldy], or SwiGLU bf16 [batch][ldy]
   int ldy;
@@ -284,9 +285,8 @@ __global__ void __launch_bounds__(256) tc_x_prep_kernel(const TcPrep a) {
     const int kc = (c * 8) >> 6, kin = (c * 8) & 63;
     *reinterpret_cast<uint4*>(a.xsw + static_cast<size_t>(kc) * a.npad * 128 + sw128_offset(n, kin)) = o;
   };
-  // bf16(xf * inv * w) of one chunk (fused RMSNorm)
-  auto norm_chunk = [&](int c, float4 a0, float4 a1, float inv) {
-    const uint4 wv = *reinterpret_cast<const uint4*>(a.norm_w + c * 8);
+  // bf16(xf * inv * w) of one chunk (fused RMSNorm), with the chunk's 8 norm weights wv
+  auto norm_chunk_w = [&](uint4 wv, float4 a0, float4 a1, float inv) {
     auto nb = [&](float xv, float wf) { return xv * inv * wf; };
     uint4 o;
     o.x = pack_bf16x2_rn(nb(a0.x, bf16lo_to_f32(wv.x)), nb(a0.y, bf16hi_to_f32(wv.x)));
@@ -294,6 +294,9 @@ __global__ void __launch_bounds__(256) tc_x_prep_kernel(const TcPrep a) {
     o.z = pack_bf16x2_rn(nb(a1.x, bf16lo_to_f32(wv.z)), nb(a1.y, bf16hi_to_f32(wv.z)));
     o.w = pack_bf16x2_rn(nb(a1.z, bf16lo_to_f32(wv.w)), nb(a1.w, bf16hi_to_f32(wv.w)));
     return o;
+  };
+  auto norm_chunk = [&](int c, float4 a0, float4 a1, float inv) {
+    return norm_chunk_w(*reinterpret_cast<const uint4*>(a.norm_w + c * 8), a0, a1, inv);
   };
   // bf16(silu(bf16 g) * bf16 u) of one chunk (SwiGLU input), as the fused epilogue
   auto swiglu_chunk = [&](int c) {
@@ -334,6 +337,7 @@ __global__ void __launch_bounds__(256) tc_x_prep_kernel(const TcPrep a) {
       }
     } else if (a.xf) {
       float4 f[kPrepRegChunks][2];
+      uint4 wv[kPrepRegChunks];  // the norm weights, loaded with the row (not after its reduction)
       float ss = 0.f;
 #pragma unroll
       for (int i = 0; i < kPrepRegChunks; ++i) {
@@ -342,6 +346,7 @@ __global__ void __launch_bounds__(256) tc_x_prep_kernel(const TcPrep a) {
           const float* xr = a.xf + static_cast<size_t>(n) * a.ldx + c * 8;
           f[i][0] = *reinterpret_cast<const float4*>(xr);
           f[i][1] = *reinterpret_cast<const float4*>(xr + 4);
+          wv[i] = *reinterpret_cast<const uint4*>(a.norm_w + c * 8);
         }
       }
 #pragma unroll
@@ -358,7 +363,7 @@ __global__ void __launch_bounds__(256) tc_x_prep_kernel(const TcPrep a) {
 #pragma unroll
       for (int i = 0; i < kPrepRegChunks; ++i) {
         const int c = threadIdx.x + 256 * i;
-        if (live && c < nc) v[i] = norm_chunk(c, f[i][0], f[i][1], inv);
+        if (live && c < nc) v[i] = norm_chunk_w(wv[i], f[i][0], f[i][1], inv);
       }
     } else {
 #pragma unroll
@@ -534,7 +539,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
         ++r_next;
       };
       if (p.prefetch)
-        while (r_next < n_k && r_next < static_cast<uint32_t>(RS)) {
+        while (r_next < n_k && r_next < static_cast<uint32_t>(p.pre_raw)) {
           issue_raw(item_tile(it_r), kt_r, static_cast<int>(r_next));
           advance_r();
         }
@@ -548,41 +553,43 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
       uint64_t t_prog = globaltimer();
       while ((r_next < n_k || x_next < n_x) && !*abort_flag) {
         bool progressed = false;
-        while (r_next < n_k) {
-          const int rs = static_cast<int>(r_next % RS);
-          if (r_next >= static_cast<uint32_t>(RS) && !mbar_test_wait(smem_u32(&raw_empty[rs]), ((r_next / RS) & 1) ^ 1))
-            break;
-          issue_raw(item_tile(it_r), kt_r, rs);
-          advance_r();
-          progressed = true;
-        }
-        while (x_next < n_x) {
+        // one x stage, then one raw stage, per pass: the MMAs wait on x while the raw ring
+        // already runs up to RS K-tiles ahead (prefetched before the wait), so x goes first
+        if (x_next < n_x) {
           const int xs = static_cast<int>(x_next % XS);
-          if (x_next >= static_cast<uint32_t>(XS) && !mbar_test_wait(smem_u32(&x_empty[xs]), ((x_next / XS) & 1) ^ 1))
-            break;
-          // this CTA's token rows n0.. of the slice: contiguous, and their swizzle
-          // pattern is the slice's (n0 is a multiple of 8 rows)
-          mbar_arrive_expect_tx(smem_u32(&x_full[xs]), xstage);
-          if (TA && ncta == npad) {  // the K-tile's four slices are contiguous in the image
-            bulk_g2s(smem_u32(smem + L.x + xs * xstage), p.xsw + static_cast<size_t>(kt_x) * 4 * npad * 128, xstage,
-                     smem_u32(&x_full[xs]), keep);
-          } else {
-            const int nsl = TA ? 4 : 1;
-            for (int j = 0; j < nsl; ++j)
-              bulk_g2s(smem_u32(smem + L.x + xs * xstage + j * xbytes),
-                       p.xsw + (static_cast<size_t>(kt_x * 4 + js_x + j) * npad + item_n0(it_x)) * 128, xbytes,
+          if (x_next < static_cast<uint32_t>(XS) || mbar_test_wait(smem_u32(&x_empty[xs]), ((x_next / XS) & 1) ^ 1)) {
+            // this CTA's token rows n0.. of the slice: contiguous, and their swizzle
+            // pattern is the slice's (n0 is a multiple of 8 rows)
+            mbar_arrive_expect_tx(smem_u32(&x_full[xs]), xstage);
+            if (TA && ncta == npad) {  // the K-tile's four slices are contiguous in the image
+              bulk_g2s(smem_u32(smem + L.x + xs * xstage), p.xsw + static_cast<size_t>(kt_x) * 4 * npad * 128, xstage,
                        smem_u32(&x_full[xs]), keep);
-          }
-          if (TA) js_x = 3;  // a whole K-tile per stage
-          if (++js_x == 4) {
-            js_x = 0;
-            if (++kt_x == item_k1(it_x)) {
-              it_x += gridDim.x;
-              if (it_x < n_items) kt_x = item_k0(it_x);
+            } else {
+              const int nsl = TA ? 4 : 1;
+              for (int j = 0; j < nsl; ++j)
+                bulk_g2s(smem_u32(smem + L.x + xs * xstage + j * xbytes),
+                         p.xsw + (static_cast<size_t>(kt_x * 4 + js_x + j) * npad + item_n0(it_x)) * 128, xbytes,
+                         smem_u32(&x_full[xs]), keep);
             }
+            if (TA) js_x = 3;  // a whole K-tile per stage
+            if (++js_x == 4) {
+              js_x = 0;
+              if (++kt_x == item_k1(it_x)) {
+                it_x += gridDim.x;
+                if (it_x < n_items) kt_x = item_k0(it_x);
+              }
+            }
+            ++x_next;
+            progressed = true;
           }
-          ++x_next;
-          progressed = true;
+        }
+        if (r_next < n_k) {
+          const int rs = static_cast<int>(r_next % RS);
+          if (r_next < static_cast<uint32_t>(RS) || mbar_test_wait(smem_u32(&raw_empty[rs]), ((r_next / RS) & 1) ^ 1)) {
+            issue_raw(item_tile(it_r), kt_r, rs);
+            advance_r();
+            progressed = true;
+          }
         }
         if (progressed) {
           t_prog = globaltimer();
