@@ -231,6 +231,30 @@ int b2_tp_gather(void* const* peers, int world, int rank, const void* src, int r
 int b2_tp_allreduce(void* const* peers, int world, int rank, const float* src, int rows, int cols, int ld_src,
                     long long slots_offset, float* y, int ldy, void* stream);
 
+/* The all-reduce fused into the tensor-core GEMM that consumes it (a "pulled seam"):
+ * the _rmsnorm GEMM of `form` (B2_SEAM_Q4_F32: b2_q4_gemm_rmsnorm, y fp32;
+ * B2_SEAM_Q4_SWIGLU: b2_q4_swiglu_gemm_rmsnorm with w0 = gate, w1 = up, y = h bf16;
+ * B2_SEAM_Q8_F32: b2_q8_gemm_rmsnorm) whose x pre-pass first makes every residual row
+ *   x[b] += sum over ranks r, in rank order, of r's fp32 partial [batch][ld_part] at byte
+ *   part_offset of r's region
+ * (read over NVLink through `peers`) and writes it back to x -- bit-identical on every
+ * rank -- then normalises it.  The partial is the output of the kernel just before, on
+ * every rank (the K-sharded O or down projection); the pre-pass signals that its own is
+ * final and waits (bounded: device error 6) for the others', per `seam` (0 ..
+ * B2_PEER_MAX_SEAMS - 1, its own counters in the control words).  A rank rewrites a
+ * partial only after every rank has read it: alternate two seams (O, then down) per
+ * layer, each in its own buffer.  x: K <= 16384, the region offset 16-byte aligned and
+ * past the control words, ld_part >= K and a multiple of 4.  Replaces the reference's
+ * single-device residual add, as b2_tp_allreduce does, with no launch of its own. */
+#define B2_PEER_MAX_SEAMS 8
+#define B2_SEAM_Q4_F32 0
+#define B2_SEAM_Q4_SWIGLU 1
+#define B2_SEAM_Q8_F32 2
+int b2_gemm_rmsnorm_seam(int form, const uint8_t* w0, const uint8_t* w1, int n_tile_rows, int k_tiles, float* x,
+                         int batch, int ldx, const uint16_t* norm_w, float eps, void* y, int ldy, int flags,
+                         void* workspace, size_t workspace_bytes, void* const* peers, int world, int rank,
+                         long long part_offset, int ld_part, int seam, void* stream);
+
 /* RMSNorm y = x * rsqrt(mean(x^2) + eps) * w over rows of n, bf16 out.
  *   x  bf16 (x_is_f32 = 0) or fp32 (x_is_f32 = 1), [batch][ldx];  w bf16 [n]
  * Replaces granite_rms_norm (designs/granite_gemv/granite_rmsnorm.h:45-80). */

@@ -56,6 +56,8 @@ SIGNATURES: dict[str, tuple] = {
     "b2_q4_swiglu_gemm_rmsnorm": (_i32, [_vp, _vp, _i32, _i32, _vp, _i32, _i32, _vp, _f32, _vp, _i32, _i32, _vp,
                                          _c.c_size_t, _vp]),
     "b2_q4_gemm_swiglu_in": (_i32, [_vp, _i32, _i32, _vp, _i32, _i32, _vp, _i32, _i32, _vp, _c.c_size_t, _vp]),
+    "b2_gemm_rmsnorm_seam": (_i32, [_i32, _vp, _vp, _i32, _i32, _vp, _i32, _i32, _vp, _f32, _vp, _i32, _i32, _vp,
+                                     _c.c_size_t, _vp, _i32, _i32, _c.c_longlong, _i32, _i32, _vp]),
     "b2_q4_gemm_pack": (_i32, [_vp, _i32, _i32, _vp, _vp]),
     "b2_q8_gemm_pack": (_i32, [_vp, _i32, _i32, _vp, _vp]),
     "b2_q8_gemm": (_i32, [_vp, _i32, _i32, _vp, _i32, _i32, _vp, _i32, _i32, _vp, _c.c_size_t, _vp]),

@@ -30,6 +30,15 @@ namespace {
 
 thread_local char g_msg[512] = "";
 int g_pdl = 1;
+unsigned long long g_peer_timeout_ns = B2_WAIT_TIMEOUT_NS;  // bounded waits on other ranks (b2_set_peer_timeout_ms)
+
+// A pulled seam for the _rmsnorm GEMMs' x pre-pass (tensor-parallel decode): the residual
+// rows gain the sum over ranks of the fp32 partials at part_off of every peer region.
+struct SeamArgs {
+  void* const* peers;
+  int world, rank, seam, ld_part;
+  long long part_off;
+};
 
 int fail(int status, const char* fmt, ...) {
   va_list ap;
@@ -453,7 +462,7 @@ inline size_t tc_ws_bytes(int batch, int k_tiles) {
 int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_rows, int k_tiles, const uint16_t* x,
                    int batch, int ldx, void* y, int ldy, int flags, void* workspace, size_t ws_bytes,
                    void* stream, const float* xf = nullptr, const uint16_t* norm_w = nullptr, float eps = 0.f,
-                   int qt = b2::kQ4, const float* gu = nullptr) {
+                   int qt = b2::kQ4, const float* gu = nullptr, const SeamArgs* seam = nullptr) {
   DevInfo di;
   int st = device_info(&di);
   if (st != B2_OK) return st;
@@ -462,6 +471,16 @@ int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_row
     if (!aligned(xf, 16) || (ldx % 4) || !aligned(norm_w, 16)) return fail(B2_ERR_ALIGN, "x/norm weight alignment");
     if (!(eps >= 0.f)) return fail(B2_ERR_ARG, "eps must be >= 0");
     x = reinterpret_cast<const uint16_t*>(xf);  // satisfies the checks below; the pre-pass reads xf
+  }
+  if (seam) {
+    if (!xf) return fail(B2_ERR_ARG, "a pulled seam needs the _rmsnorm form");
+    if (!seam->peers) return fail(B2_ERR_ARG, "null peers");
+    if (seam->world < 1 || seam->world > b2::kPeerMaxRanks || seam->rank < 0 || seam->rank >= seam->world)
+      return fail(B2_ERR_ARG, "rank %d of world %d", seam->rank, seam->world);
+    if (seam->seam < 0 || seam->seam >= b2::kPeerMaxSeams) return fail(B2_ERR_ARG, "seam %d outside 0..%d", seam->seam, b2::kPeerMaxSeams - 1);
+    if (seam->part_off < b2::kPeerCtlBytes || seam->part_off % 16) return fail(B2_ERR_ALIGN, "partial offset %lld", seam->part_off);
+    if (seam->ld_part < k_tiles * 256 || seam->ld_part % 4) return fail(B2_ERR_ARG, "ld_part %d (K %d)", seam->ld_part, k_tiles * 256);
+    if (k_tiles * 256 > b2::kPrepRegChunks * 256 * 8) return fail(B2_ERR_ARG, "a pulled seam takes K <= %d", b2::kPrepRegChunks * 2048);
   }
   if (gu) {  // SwiGLU input: fp32 rows [batch][ldx] holding g at column k and u at K + k
     if (xf || epi != b2::kTcEpiF32 || qt != b2::kQ4) return fail(B2_ERR_ARG, "SwiGLU input is for the plain q4 GEMM");
@@ -564,6 +583,16 @@ int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_row
   pp.xf = xf;
   pp.gu = gu;
   pp.gu_half = k_tiles * 256;
+  if (seam) {
+    pp.peers = seam->peers;
+    pp.world = seam->world;
+    pp.rank = seam->rank;
+    pp.seam = seam->seam;
+    pp.ld_part = seam->ld_part;
+    pp.part_off = seam->part_off;
+    pp.xf_out = const_cast<float*>(xf);
+    pp.timeout_ns = g_peer_timeout_ns;
+  }
   pp.norm_w = reinterpret_cast<const __nv_bfloat16*>(norm_w);
   pp.eps = eps;
   pp.ldx = ldx;
@@ -837,8 +866,6 @@ int b2_gqa_decode_static(const float* q, const float* k_new, const float* v_new,
 
 // ------------------------------------------------- tensor-parallel exchanges
 namespace {
-unsigned long long g_peer_timeout_ns = B2_WAIT_TIMEOUT_NS;
-
 int xchg_check(void* const* peers, int world, int rank, const void* src, int rows, int cols, int ld_src,
                long long dst_offset) {
   if (!peers || !src) return fail(B2_ERR_ARG, "null pointer argument");
@@ -1283,6 +1310,26 @@ int b2_q8_gemm_rmsnorm(const uint8_t* tiles, int n_tile_rows, int k_tiles, const
                        size_t workspace_bytes, void* stream) {
   return tc_gemm_common(b2::kTcEpiF32, tiles, nullptr, n_tile_rows, k_tiles, nullptr, batch, ldx, y, ldy, flags,
                         workspace, workspace_bytes, stream, x, norm_w, eps, b2::kQ8);
+}
+
+int b2_gemm_rmsnorm_seam(int form, const uint8_t* w0, const uint8_t* w1, int n_tile_rows, int k_tiles, float* x,
+                         int batch, int ldx, const uint16_t* norm_w, float eps, void* y, int ldy, int flags,
+                         void* workspace, size_t workspace_bytes, void* const* peers, int world, int rank,
+                         long long part_offset, int ld_part, int seam, void* stream) {
+  const SeamArgs sa = {peers, world, rank, seam, ld_part, part_offset};
+  switch (form) {
+    case B2_SEAM_Q4_F32:
+      return tc_gemm_common(b2::kTcEpiF32, w0, nullptr, n_tile_rows, k_tiles, nullptr, batch, ldx, y, ldy, flags,
+                            workspace, workspace_bytes, stream, x, norm_w, eps, b2::kQ4, nullptr, &sa);
+    case B2_SEAM_Q4_SWIGLU:
+      return tc_gemm_common(b2::kTcEpiSwiglu, w0, w1, n_tile_rows, k_tiles, nullptr, batch, ldx, y, ldy, flags,
+                            workspace, workspace_bytes, stream, x, norm_w, eps, b2::kQ4, nullptr, &sa);
+    case B2_SEAM_Q8_F32:
+      return tc_gemm_common(b2::kTcEpiF32, w0, nullptr, n_tile_rows, k_tiles, nullptr, batch, ldx, y, ldy, flags,
+                            workspace, workspace_bytes, stream, x, norm_w, eps, b2::kQ8, nullptr, &sa);
+    default:
+      return fail(B2_ERR_ARG, "unknown form %d", form);
+  }
 }
 
 int b2_q4_dequant_tiles(const uint8_t* tiles, int64_t n_tiles, uint16_t* out, void* stream) {

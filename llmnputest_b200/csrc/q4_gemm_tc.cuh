@@ -45,6 +45,7 @@
 
 #include "b2_common.cuh"
 #include "q4nx_gemv.cuh"
+#include "tp_exchange.cuh"
 
 namespace b2 {
 
@@ -230,6 +231,14 @@ struct TcPrep {
   float* yzero;
   int ldy, n_out;
   int early;  // release the GEMM before this pass's own wait (see the kernel)
+  // pulled seam (tensor-parallel decode; with xf only): before the norm, the fp32 row
+  // becomes xf + sum over ranks r (in rank order) of r's partial at byte `part_off` of
+  // its peer region ([batch][ld_part] fp32) and is written back to xf_out (= xf)
+  void* const* peers;  // null: no seam
+  int world, rank, seam, ld_part;
+  long long part_off;
+  float* xf_out;
+  unsigned long long timeout_ns;
 };
 
 // Rows of up to kPrepRegChunks * 256 chunks of 8 (K <= 16384) are read from global
@@ -249,6 +258,27 @@ __global__ void __launch_bounds__(256) tc_x_prep_kernel(const TcPrep a) {
   pdl_wait();
   if (!a.early) pdl_launch_dependents();
   const bool live = n < a.batch;
+  if (a.peers) {
+    // this rank's partial is final (its producer grid completed before our wait): post
+    // it, then wait until every rank's has landed
+    if (blockIdx.x == 0) tp_seam_post(a.peers, a.world, a.rank, a.seam);
+    tp_seam_wait(a.peers, a.world, a.rank, a.seam, a.timeout_ns);
+  }
+  // chunk c (8 values) of the seam's sum over ranks, in rank order
+  auto seam_sum = [&](int c, float4& s0, float4& s1) {
+    const size_t e = static_cast<size_t>(n) * a.ld_part + c * 8;
+    for (int q = 0; q < a.world; ++q) {
+      const float* pr = reinterpret_cast<const float*>(static_cast<const uint8_t*>(a.peers[q]) + a.part_off) + e;
+      const float4 t0 = *reinterpret_cast<const float4*>(pr), t1 = *reinterpret_cast<const float4*>(pr + 4);
+      if (q == 0) {
+        s0 = t0;
+        s1 = t1;
+      } else {
+        s0.x += t0.x; s0.y += t0.y; s0.z += t0.z; s0.w += t0.w;
+        s1.x += t1.x; s1.y += t1.y; s1.z += t1.z; s1.w += t1.w;
+      }
+    }
+  };
   auto block_sum = [&](float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -347,6 +377,21 @@ __global__ void __launch_bounds__(256) tc_x_prep_kernel(const TcPrep a) {
           f[i][0] = *reinterpret_cast<const float4*>(xr);
           f[i][1] = *reinterpret_cast<const float4*>(xr + 4);
           wv[i] = *reinterpret_cast<const uint4*>(a.norm_w + c * 8);
+        }
+      }
+      if (a.peers) {  // the residual plus the seam's sum, kept for the next seam
+#pragma unroll
+        for (int i = 0; i < kPrepRegChunks; ++i) {
+          const int c = threadIdx.x + 256 * i;
+          if (live && c < nc) {
+            float4 s0, s1;
+            seam_sum(c, s0, s1);
+            f[i][0].x += s0.x; f[i][0].y += s0.y; f[i][0].z += s0.z; f[i][0].w += s0.w;
+            f[i][1].x += s1.x; f[i][1].y += s1.y; f[i][1].z += s1.z; f[i][1].w += s1.w;
+            float* xo = a.xf_out + static_cast<size_t>(n) * a.ldx + c * 8;
+            *reinterpret_cast<float4*>(xo) = f[i][0];
+            *reinterpret_cast<float4*>(xo + 4) = f[i][1];
+          }
         }
       }
 #pragma unroll

@@ -5,6 +5,8 @@
 // control words:
 //   sig[src][c]  u64  chunk c of an exchange received from rank src (monotonic count)
 //   exp[src][c]  u64  of those, how many this rank has consumed
+//   seam_sig[src][z], seam_exp[src][z], seam_done[z]   the same for a seam z whose sum
+//                is pulled by a consumer kernel (tp_seam_* below)
 // The rest holds the exchanged buffers at offsets the host chooses (the same layout on
 // every rank).  `peers` is a device array of the W region bases as mapped in this
 // process (peers[rank] is the own base).
@@ -40,8 +42,9 @@
 namespace b2 {
 
 constexpr int kPeerMaxRanks = 16;
-constexpr int kPeerMaxChunks = 256;
-constexpr int kPeerCtlBytes = 2 * kPeerMaxRanks * kPeerMaxChunks * 8;  // 64 KB
+constexpr int kPeerMaxChunks = 240;
+constexpr int kPeerMaxSeams = 8;
+constexpr int kPeerCtlBytes = 65536;
 constexpr int kXchgThreads = 256;
 constexpr int kXchgUnroll = 4;      // units in flight per thread (loads before stores)
 constexpr int kDevTimeoutPeer = 6;  // device error: a peer's signal never came
@@ -49,6 +52,11 @@ constexpr int kDevTimeoutPeer = 6;  // device error: a peer's signal never came
 struct PeerCtl {
   unsigned long long sig[kPeerMaxRanks][kPeerMaxChunks];
   unsigned long long exp[kPeerMaxRanks][kPeerMaxChunks];
+  unsigned long long seam_sig[kPeerMaxRanks][kPeerMaxSeams];
+  unsigned long long seam_exp[kPeerMaxRanks][kPeerMaxSeams];
+  unsigned long long seam_done[kPeerMaxSeams];
+  unsigned long long pad[(kPeerCtlBytes - (2 * kPeerMaxRanks * kPeerMaxChunks + 2 * kPeerMaxRanks * kPeerMaxSeams +
+                                           kPeerMaxSeams) * 8) / 8];
 };
 static_assert(sizeof(PeerCtl) == kPeerCtlBytes, "control block layout");
 
@@ -241,6 +249,60 @@ __global__ void __launch_bounds__(kXchgThreads) tp_allreduce_kernel(const XchgPa
       p.y[static_cast<size_t>(r) * p.ldy + c] += s;
     }
   }
+}
+
+
+// ------------------------------------------------------------------ pulled seams
+// A seam whose fp32 partials [rows][ld] sit in every rank's region at one offset and
+// are summed by the kernel that consumes them (the tensor-core GEMM's x pre-pass), so
+// the all-reduce costs no kernel of its own.  Per use of seam z:
+//   post  (one thread per rank q, in the consumer, once the producer grid has
+//         completed): a system-scope fence, then seam_sig[rank][z] += 1 on rank q;
+//   wait  (thread s of every consumer CTA): until seam_sig[s][z] here exceeds
+//         seam_exp[s][z] (bounded; device error kDevTimeoutPeer);
+//   done  (every consumer CTA after its waits): the last CTA advances seam_exp[.][z].
+// A rank rewrites its partial only in a later use of the same seam, after it has
+// waited in another seam that every rank posts only after finishing this one's reads:
+// decoders alternate two seams (O and down) per layer.
+__device__ __forceinline__ void tp_seam_post(void* const* peers, int world, int rank, int z) {
+  if (threadIdx.x < world) {
+    __threadfence_system();  // the producer grid's partial (complete at our PDL wait) before the signal
+    red_release_sys(&peer_ctl(peers[threadIdx.x])->seam_sig[rank][z]);
+  }
+}
+
+// Every thread of the CTA calls it; true when every rank's partial has landed.
+__device__ __forceinline__ bool tp_seam_wait(void* const* peers, int world, int rank, int z,
+                                             unsigned long long timeout_ns) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = 1;
+  __syncthreads();
+  if (threadIdx.x < world) {
+    PeerCtl* ctl = peer_ctl(peers[rank]);
+    const int s = threadIdx.x;
+    const unsigned long long want = ctl->seam_exp[s][z] + 1ull;
+    const uint64_t t0 = globaltimer();
+    while (ld_acquire_sys(&ctl->seam_sig[s][z]) < want) {
+      if (globaltimer() - t0 > timeout_ns) {
+        record_error(kDevTimeoutPeer);
+        ok = 0;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  const bool r = ok != 0;
+  if (threadIdx.x == 0) {
+    // the last CTA past its waits advances the consumed counts for the next use
+    PeerCtl* ctl = peer_ctl(peers[rank]);
+    __threadfence();
+    if (atomicAdd(&ctl->seam_done[z], 1ull) == gridDim.x - 1ull) {
+      __threadfence();
+      for (int q = 0; q < world; ++q) ctl->seam_exp[q][z] += 1ull;
+      ctl->seam_done[z] = 0ull;
+    }
+  }
+  return r;
 }
 
 }  // namespace b2

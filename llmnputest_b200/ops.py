@@ -157,9 +157,12 @@ def q8_gemm_pack(tiles: torch.Tensor, n_tile_rows: int, k_tiles: int, out: torch
 
 def q8_gemm(packed: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tensor, out: torch.Tensor | None = None,
             accumulate: bool = False, workspace: torch.Tensor | None = None, prefetch: bool = False,
-            norm_w: torch.Tensor | None = None, eps: float = 0.0) -> torch.Tensor:
+            norm_w: torch.Tensor | None = None, eps: float = 0.0, peer_sum: PeerSum | None = None) -> torch.Tensor:
     """fp32 y [B, N] = W x for a packed q8 weight (q8_gemm_pack) on the tensor cores; with
-    norm_w, x is the fp32 residual and its RMSNorm is fused (b2_q8_gemm_rmsnorm)."""
+    norm_w, x is the fp32 residual and its RMSNorm is fused (b2_q8_gemm_rmsnorm); peer_sum
+    (with norm_w): x += the seam's sum over ranks first, in place (b2_gemm_rmsnorm_seam)."""
+    if peer_sum is not None and norm_w is None:
+        raise ValueError("peer_sum needs norm_w (the _rmsnorm form)")
     _tiles(packed, n_tile_rows, k_tiles, Q8_TILE_BYTES, "packed")
     k, n = k_tiles * TILE_K, n_tile_rows * TILE_ROWS
     x2 = _norm_in(x, norm_w, k) if norm_w is not None else _x2d(x, k)
@@ -171,7 +174,11 @@ def q8_gemm(packed: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tenso
     flags = GEMM_PACKED | (GEMV_ACCUMULATE if accumulate else 0) | (GEMV_PREFETCH if prefetch else 0)
     wsp = _aligned_ws(ws) if workspace is None else _ptr(ws)
     wsn = ws.numel() - (256 if workspace is None else 0)
-    if norm_w is not None:
+    if peer_sum is not None:
+        if x2.data_ptr() != x.data_ptr():
+            raise ValueError("peer_sum updates x in place: x must be fp32 row-major and 16-byte aligned")
+        _seam_call(SEAM_Q8_F32, packed, None, n_tile_rows, k_tiles, x2, norm_w, eps, out, flags, wsp, wsn, peer_sum)
+    elif norm_w is not None:
         _native.call("b2_q8_gemm_rmsnorm", _ptr(packed), n_tile_rows, k_tiles, _ptr(x2), b, x2.stride(0),
                      _ptr(norm_w), float(eps), _ptr(out), out.stride(0), flags, wsp, wsn, _stream())
     else:
@@ -180,10 +187,35 @@ def q8_gemm(packed: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tenso
     return out
 
 
+SEAM_Q4_F32, SEAM_Q4_SWIGLU, SEAM_Q8_F32 = 0, 1, 2  # B2_SEAM_* forms
+
+
+class PeerSum:
+    """A pulled seam (b2_gemm_rmsnorm_seam) for an _rmsnorm GEMM: before the norm, the fp32
+    residual x gains, in place, the sum over ranks of the partials in `buffer` of the peer
+    region `region` (a peer.PeerRegion), with counters `seam`."""
+
+    def __init__(self, region, buffer: str, seam: int):
+        off, shape, dtype = region.offsets[buffer]
+        if dtype != torch.float32 or len(shape) != 2:
+            raise ValueError(f"seam buffer {buffer} must be fp32 [rows, cols]")
+        self.region, self.offset, self.ld, self.rows, self.seam = region, off, shape[1], shape[0], seam
+
+
+def _seam_call(form: int, w0, w1, n_tile_rows: int, k_tiles: int, x2: torch.Tensor, norm_w, eps: float,
+               out: torch.Tensor, flags: int, wsp, wsn: int, ps: PeerSum) -> None:
+    if x2.shape[0] > ps.rows:
+        raise ValueError("more rows than the seam buffer holds")
+    r = ps.region
+    _native.call("b2_gemm_rmsnorm_seam", form, _ptr(w0), _ptr(w1) if w1 is not None else None, n_tile_rows, k_tiles,
+                 _ptr(x2), x2.shape[0], x2.stride(0), _ptr(norm_w), float(eps), _ptr(out), out.stride(0), flags, wsp,
+                 wsn, ctypes.c_void_p(r.peers_dev.data_ptr()), r.world, r.rank, ps.offset, ps.ld, ps.seam, _stream())
+
+
 def q4_gemm(tiles: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tensor, out: torch.Tensor | None = None,
             accumulate: bool = False, workspace: torch.Tensor | None = None, prefetch: bool = False,
             norm_w: torch.Tensor | None = None, eps: float = 0.0, packed: bool = False,
-            swiglu_in: bool = False) -> torch.Tensor:
+            swiglu_in: bool = False, peer_sum: PeerSum | None = None) -> torch.Tensor:
     """fp32 y [B, N] = W x on the tcgen05 tensor cores (batches up to 256).
 
     With norm_w, x is the fp32 residual [B, K] and the GEMM multiplies
@@ -191,9 +223,12 @@ def q4_gemm(tiles: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tensor
     With swiglu_in, x is the fp32 output [B, 2K] of a gate+up GEMM (gate columns first)
     and the GEMM multiplies bf16(silu(bf16 g) * bf16 u), formed in its x pre-pass
     (b2_q4_gemm_swiglu_in).
-    packed: the tiles come from q4_gemm_pack (A is dequantised into tensor memory)."""
+    packed: the tiles come from q4_gemm_pack (A is dequantised into tensor memory).
+    peer_sum (with norm_w): x += the seam's sum over ranks first, in place (b2_gemm_rmsnorm_seam)."""
     _tiles(tiles, n_tile_rows, k_tiles, Q4_TILE_BYTES, "tiles")
     k, n = k_tiles * TILE_K, n_tile_rows * TILE_ROWS
+    if peer_sum is not None and norm_w is None:
+        raise ValueError("peer_sum needs norm_w (the _rmsnorm form)")
     if swiglu_in:
         if norm_w is not None:
             raise ValueError("swiglu_in and norm_w are exclusive")
@@ -213,7 +248,11 @@ def q4_gemm(tiles: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tensor
     flags = (GEMV_ACCUMULATE if accumulate else 0) | (GEMV_PREFETCH if prefetch else 0) | (GEMM_PACKED if packed else 0)
     wsp = _aligned_ws(ws) if workspace is None else _ptr(ws)
     wsn = ws.numel() - (256 if workspace is None else 0)
-    if swiglu_in:
+    if peer_sum is not None:
+        if x2.data_ptr() != x.data_ptr():
+            raise ValueError("peer_sum updates x in place: x must be fp32 row-major and 16-byte aligned")
+        _seam_call(SEAM_Q4_F32, tiles, None, n_tile_rows, k_tiles, x2, norm_w, eps, out, flags, wsp, wsn, peer_sum)
+    elif swiglu_in:
         _native.call("b2_q4_gemm_swiglu_in", _ptr(tiles), n_tile_rows, k_tiles, _ptr(x2), b, x2.stride(0),
                      _ptr(out), out.stride(0), flags, wsp, wsn, _stream())
     elif norm_w is not None:
@@ -227,9 +266,11 @@ def q4_gemm(tiles: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tensor
 
 def q4_swiglu_gemm(gate: torch.Tensor, up: torch.Tensor, n_tile_rows: int, k_tiles: int, x: torch.Tensor,
                    out: torch.Tensor | None = None, workspace: torch.Tensor | None = None, prefetch: bool = False,
-                   norm_w: torch.Tensor | None = None, eps: float = 0.0, packed: bool = False) -> torch.Tensor:
+                   norm_w: torch.Tensor | None = None, eps: float = 0.0, packed: bool = False,
+                   peer_sum: PeerSum | None = None) -> torch.Tensor:
     """bf16 h = silu(bf16(G x)) * bf16(U x) on the tensor cores (batches up to 256); with
-    norm_w, x is the fp32 residual and its RMSNorm is fused (b2_q4_swiglu_gemm_rmsnorm).
+    norm_w, x is the fp32 residual and its RMSNorm is fused (b2_q4_swiglu_gemm_rmsnorm);
+    peer_sum (with norm_w): x += the seam's sum over ranks first, in place.
     packed: gate and up come from q4_gemm_pack."""
     _tiles(gate, n_tile_rows, k_tiles, Q4_TILE_BYTES, "gate")
     _tiles(up, n_tile_rows, k_tiles, Q4_TILE_BYTES, "up")
@@ -243,7 +284,11 @@ def q4_swiglu_gemm(gate: torch.Tensor, up: torch.Tensor, n_tile_rows: int, k_til
     flags = (GEMV_PREFETCH if prefetch else 0) | (GEMM_PACKED if packed else 0)
     wsp = _aligned_ws(ws) if workspace is None else _ptr(ws)
     wsn = ws.numel() - (256 if workspace is None else 0)
-    if norm_w is not None:
+    if peer_sum is not None:
+        if norm_w is None or x2.data_ptr() != x.data_ptr():
+            raise ValueError("peer_sum needs norm_w and an fp32 row-major, 16-byte aligned x (updated in place)")
+        _seam_call(SEAM_Q4_SWIGLU, gate, up, n_tile_rows, k_tiles, x2, norm_w, eps, out, flags, wsp, wsn, peer_sum)
+    elif norm_w is not None:
         _native.call("b2_q4_swiglu_gemm_rmsnorm", _ptr(gate), _ptr(up), n_tile_rows, k_tiles, _ptr(x2), b,
                      x2.stride(0), _ptr(norm_w), float(eps), _ptr(out), out.stride(0), flags, wsp, wsn, _stream())
     else:

@@ -169,15 +169,18 @@ def shard_weights(full: dict, plan: ShardPlan) -> dict:
     return out
 
 
-def tp_exchange_layout(cfg, batch: int, world: int) -> list:
-    """The peer buffers of TPDecoder: the replicated residual, one slot array per all-reduce
-    seam (O and down alternate, so a rank never rewrites a slot another rank may still be
-    summing: between two uses of one array every rank has entered the other seam's
-    exchange), and the gathered logits."""
-    return [("resid", (batch, cfg.hidden), torch.float32),
-            ("slots_o", (world, batch, cfg.hidden), torch.float32),
-            ("slots", (world, batch, cfg.hidden), torch.float32),
-            ("logits", (batch, cfg.vocab), torch.float32)]
+def tp_exchange_layout(cfg, batch: int, world: int, pulled: bool = False) -> list:
+    """The peer buffers of TPDecoder: the replicated residual, the gathered logits, and per
+    all-reduce seam either a slot array for its exchange kernel or (pulled) the partial
+    itself, which the consuming GEMM's pre-pass reads from every rank.  The O and down
+    seams alternate, each with its own buffer, so a rank never rewrites one that another
+    rank may still be reading: between two uses of a buffer every rank has entered the
+    other seam."""
+    seams = ([("o_part", (batch, cfg.hidden), torch.float32), ("down_part", (batch, cfg.hidden), torch.float32)]
+             if pulled else
+             [("slots_o", (world, batch, cfg.hidden), torch.float32),
+              ("slots", (world, batch, cfg.hidden), torch.float32)])
+    return [("resid", (batch, cfg.hidden), torch.float32)] + seams + [("logits", (batch, cfg.vocab), torch.float32)]
 
 
 class TPDecoder:
@@ -189,7 +192,11 @@ class TPDecoder:
                     stream (summed in rank order, so every copy is bit-identical): two
                     small kernels per layer that store straight into the other GPUs'
                     memory, captured in the step's CUDA graph; the logits are gathered
-                    once per step.
+                    once per step.  On the GEMM path with pulled seams (the GPU default
+                    there) the all-reduces have no kernel of their own: each projection
+                    leaves its partial in the peer region and the next GEMM's x pre-pass
+                    signals it, waits for every rank's and adds them, in rank order, into
+                    the residual before its RMSNorm (b2_gemm_rmsnorm_seam).
       "collective"  torch.distributed all_gather / all_reduce (NCCL on GPUs, gloo on CPU).
     `xchg` (comm="peer"): an exchange object with .buffers, .gather(src, name, add_base)
     and .allreduce_add(src, name, y); built from peer.PeerRegion when not given.
@@ -201,7 +208,8 @@ class TPDecoder:
     would fill at most half the SMs."""
 
     def __init__(self, cfg, batch: int, ctx_max: int, shard: dict, plan: ShardPlan, device=None, ops=None,
-                 comm: str | None = None, xchg=None, gemm_min_batch: int = 9, swiglu_split: bool | None = None):
+                 comm: str | None = None, xchg=None, gemm_min_batch: int = 9, swiglu_split: bool | None = None,
+                 pulled: bool | None = None):
         if ops is None:
             from . import ops  # the GPU path; tests of the host logic may pass another implementation
         self.ops = ops
@@ -235,13 +243,25 @@ class TPDecoder:
         self.down = torch.zeros(batch, c.hidden, dtype=torch.float32, device=dev)
         self.logits_local = torch.zeros(batch, c.vocab // W, dtype=torch.float32, device=dev)
         self.pos = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.use_gemm = batch >= gemm_min_batch
+        # pulled seams: the O and down all-reduces inside the next GEMM's x pre-pass
+        if pulled is None:
+            pulled = comm == "peer" and self.use_gemm and xchg is None and dev.type == "cuda" and W > 1
+        if pulled and not (comm == "peer" and self.use_gemm):
+            raise ValueError("pulled seams need comm='peer' and the GEMM path")
+        self.pulled = bool(pulled)
         if comm == "peer":
             if xchg is None:
                 from .peer import PeerExchange
-                xchg = PeerExchange(tp_exchange_layout(cfg, batch, W), device=dev)
+                xchg = PeerExchange(tp_exchange_layout(cfg, batch, W, self.pulled), device=dev)
             self.xchg = xchg
             self.resid = xchg.buffers["resid"]
             self.logits = xchg.buffers["logits"]
+            if self.pulled:
+                self.o_part = xchg.buffers["o_part"]
+                self.down = xchg.buffers["down_part"]
+                self.ps_o = ops.PeerSum(xchg.region, "o_part", 0)
+                self.ps_down = ops.PeerSum(xchg.region, "down_part", 1)
         else:
             self.xchg = None
             # gathered buffers are [W*B, n] (rank-major), viewed as [W, B, n] when merged
@@ -250,7 +270,6 @@ class TPDecoder:
             self.logits = torch.zeros(batch, c.vocab, dtype=torch.float32, device=dev)
         ws = ops.gqa_decode_workspace_bytes(batch, p.q_local, p.kv_local, d, ctx_max)
         self.attn_ws = torch.empty(max(ws, 1), dtype=torch.uint8, device=dev)
-        self.use_gemm = batch >= gemm_min_batch
         self.swiglu_split = False
         if self.use_gemm:
             nbytes = ops.gemm_workspace_bytes(batch, max(self.kt_h, self.kt_o_local, self.kt_i_local))
@@ -314,11 +333,14 @@ class TPDecoder:
         qd, kd = p.q_local * d, p.kv_local * d
         ws = self.gemm_ws if self.use_gemm else None
         self.resid.copy_(self.x_in)
+        pulled = self.pulled
         for li, L in enumerate(self.w["layers"]):
             G = self.wg[li] if self.use_gemm else None
             if self.use_gemm:
+                # pulled: the previous layer's down seam summed into the residual here
                 ops.q4_gemm(G["qkv"], self.nt_qkv_local, self.kt_h, self.resid, out=self.qkv, workspace=ws,
-                            prefetch=True, norm_w=L["attn_norm"], eps=c.rms_eps, packed=True)
+                            prefetch=True, norm_w=L["attn_norm"], eps=c.rms_eps, packed=True,
+                            peer_sum=self.ps_down if pulled and li > 0 else None)
             else:
                 ops.gemv_rmsnorm(L["qkv"], self.nt_qkv_local, self.kt_h, self.resid, L["attn_norm"], c.rms_eps,
                                  out=self.qkv, prefetch=True)
@@ -332,25 +354,30 @@ class TPDecoder:
             else:
                 ops.q4_gemv(L["o"], c.hidden // TILE_ROWS, self.kt_o_local, self.attn_local, out=self.o_part,
                             prefetch=True)
-            self._reduce_o()
+            if not pulled:
+                self._reduce_o()
+            ps_o = self.ps_o if pulled else None  # pulled: the O seam summed in the next pre-pass
             if self.swiglu_split:
                 ops.q4_gemm(G["gu"], 2 * self.nt_i_local, self.kt_h, self.resid, out=self.gu, workspace=ws,
-                            prefetch=True, norm_w=L["mlp_norm"], eps=c.rms_eps, packed=True)
+                            prefetch=True, norm_w=L["mlp_norm"], eps=c.rms_eps, packed=True, peer_sum=ps_o)
                 ops.q4_gemm(G["down"], c.hidden // TILE_ROWS, self.kt_i_local, self.gu, out=self.down, workspace=ws,
                             prefetch=True, packed=True, swiglu_in=True)
             elif self.use_gemm:
                 ops.q4_swiglu_gemm(G["gate"], G["up"], self.nt_i_local, self.kt_h, self.resid, out=self.h,
-                                   workspace=ws, prefetch=True, norm_w=L["mlp_norm"], eps=c.rms_eps, packed=True)
+                                   workspace=ws, prefetch=True, norm_w=L["mlp_norm"], eps=c.rms_eps, packed=True,
+                                   peer_sum=ps_o)
                 ops.q4_gemm(G["down"], c.hidden // TILE_ROWS, self.kt_i_local, self.h, out=self.down, workspace=ws,
                             prefetch=True, packed=True)
             else:
                 ops.swiglu_gemv_rmsnorm(L["gate"], L["up"], self.nt_i_local, self.kt_h, self.resid, L["mlp_norm"],
                                         c.rms_eps, out=self.h, prefetch=True)
                 ops.q4_gemv(L["down"], c.hidden // TILE_ROWS, self.kt_i_local, self.h, out=self.down, prefetch=True)
-            self._reduce_down()
+            if not pulled:
+                self._reduce_down()
         if self.use_gemm:
             ops.q8_gemm(self.lm_packed, self.nt_v_local, self.kt_h, self.resid, out=self.logits_local, workspace=ws,
-                        prefetch=True, norm_w=self.w["final_norm"], eps=c.rms_eps)
+                        prefetch=True, norm_w=self.w["final_norm"], eps=c.rms_eps,
+                        peer_sum=self.ps_down if pulled and self.w["layers"] else None)
         else:
             ops.gemv_rmsnorm(self.w["lm_head"], self.nt_v_local, self.kt_h, self.resid, self.w["final_norm"],
                              c.rms_eps, out=self.logits_local, prefetch=True, q8=True)
