@@ -34,6 +34,8 @@ unsigned long long g_peer_timeout_ns = B2_WAIT_TIMEOUT_NS;  // bounded waits on 
 
 // A pulled seam for the _rmsnorm GEMMs' x pre-pass (tensor-parallel decode): the residual
 // rows gain the sum over ranks of the fp32 partials at part_off of every peer region.
+// a seam's rows from every rank are staged in the pre-pass's shared memory up to this size
+constexpr size_t kSeamStageMax = 160 * 1024;
 struct SeamArgs {
   void* const* peers;
   int world, rank, seam, ld_part;
@@ -592,6 +594,20 @@ int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_row
     pp.part_off = seam->part_off;
     pp.xf_out = const_cast<float*>(xf);
     pp.timeout_ns = g_peer_timeout_ns;
+    const size_t stage_bytes = static_cast<size_t>(seam->world) * k_tiles * 256 * sizeof(float);
+    if (stage_bytes <= kSeamStageMax) {
+      static int prep_attr[64] = {0};
+      int dev = 0;
+      cudaGetDevice(&dev);
+      if (!prep_attr[dev]) {
+        cudaError_t ea = cudaFuncSetAttribute(b2::tc_x_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              static_cast<int>(kSeamStageMax));
+        if (ea != cudaSuccess) return cuda_fail(ea, "cudaFuncSetAttribute(x pre-pass)");
+        prep_attr[dev] = 1;
+      }
+      pp.stage = 1;
+      cfg.dynamicSmemBytes = stage_bytes;
+    }
   }
   pp.norm_w = reinterpret_cast<const __nv_bfloat16*>(norm_w);
   pp.eps = eps;
@@ -630,6 +646,12 @@ int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_row
   p.n_nsplit = n_nsplit;
   p.ncta = ncta;
   p.prefetch = (flags & B2_GEMV_PREFETCH) ? 1 : 0;
+  if (seam) {  // the GEMM advances the seam its pre-pass consumed
+    p.seam_peers = seam->peers;
+    p.seam = seam->seam;
+    p.seam_rank = seam->rank;
+    p.seam_world = seam->world;
+  }
   {
     const int nc = ncta <= 32 ? 32 : (ncta <= 64 ? 64 : (ncta <= 128 ? 128 : 256));
     // packed: two MMA issuers (two partials) while 2 x N columns fit the D region, and two

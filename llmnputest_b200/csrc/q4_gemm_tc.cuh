@@ -113,6 +113,8 @@ struct TcParams {
                     // dequantised) before the wait on the preceding kernel
   int d_bufs;       // accumulator buffers in TMEM (2, or 1 for 256 columns in the packed form)
   int n_issuers;    // packed form: MMA issuing threads (1 or 2), each with its own partial
+  void* const* seam_peers;  // non-null: advance pulled seam `seam` of rank `seam_rank` (its pre-pass consumed it)
+  int seam, seam_rank, seam_world;
 };
 
 struct TcSmem {
@@ -239,6 +241,7 @@ struct TcPrep {
   long long part_off;
   float* xf_out;
   unsigned long long timeout_ns;
+  int stage;  // stage every rank's row in dynamic shared memory (world * k floats), one round trip
 };
 
 // Rows of up to kPrepRegChunks * 256 chunks of 8 (K <= 16384) are read from global
@@ -247,6 +250,7 @@ constexpr int kPrepRegChunks = 8;
 
 __global__ void __launch_bounds__(256) tc_x_prep_kernel(const TcPrep a) {
   __shared__ float wred[8];
+  extern __shared__ __align__(16) float4 seam_rows[];  // [world][k / 4] when a.stage
   const int n = blockIdx.x;
   const int k = a.k;
   const int nc = k / 8;  // chunks of 8 values
@@ -263,13 +267,32 @@ __global__ void __launch_bounds__(256) tc_x_prep_kernel(const TcPrep a) {
     // it, then wait until every rank's has landed
     if (blockIdx.x == 0) tp_seam_post(a.peers, a.world, a.rank, a.seam);
     tp_seam_wait(a.peers, a.world, a.rank, a.seam, a.timeout_ns);
+    if (a.stage && live) {
+      // every rank's row in flight at once (one NVLink round trip, not one per rank)
+      const int k4 = k / 4;
+      for (int q = 0; q < a.world; ++q) {
+        const float* pr = reinterpret_cast<const float*>(static_cast<const uint8_t*>(a.peers[q]) + a.part_off) +
+                          static_cast<size_t>(n) * a.ld_part;
+        for (int u = threadIdx.x; u < k4; u += blockDim.x) cp_async16(smem_u32(&seam_rows[q * k4 + u]), pr + u * 4);
+      }
+      cp_async_commit();
+      cp_async_wait<0>();
+    }
+    __syncthreads();
   }
   // chunk c (8 values) of the seam's sum over ranks, in rank order
   auto seam_sum = [&](int c, float4& s0, float4& s1) {
     const size_t e = static_cast<size_t>(n) * a.ld_part + c * 8;
     for (int q = 0; q < a.world; ++q) {
-      const float* pr = reinterpret_cast<const float*>(static_cast<const uint8_t*>(a.peers[q]) + a.part_off) + e;
-      const float4 t0 = *reinterpret_cast<const float4*>(pr), t1 = *reinterpret_cast<const float4*>(pr + 4);
+      float4 t0, t1;
+      if (a.stage) {
+        t0 = seam_rows[q * (k / 4) + 2 * c];
+        t1 = seam_rows[q * (k / 4) + 2 * c + 1];
+      } else {
+        const float* pr = reinterpret_cast<const float*>(static_cast<const uint8_t*>(a.peers[q]) + a.part_off) + e;
+        t0 = *reinterpret_cast<const float4*>(pr);
+        t1 = *reinterpret_cast<const float4*>(pr + 4);
+      }
       if (q == 0) {
         s0 = t0;
         s1 = t1;
@@ -349,8 +372,14 @@ __global__ void __launch_bounds__(256) tc_x_prep_kernel(const TcPrep a) {
   auto finish_row = [&](float m) {  // exponent, and the zeroed output row for split-K
     const int e = live ? gemv_scale_exp(__float_as_uint(m)) : 0;
     if (threadIdx.x == 0) a.xexp[n] = e;
-    if (a.yzero && live)  // split-K partials are added into y: start it at zero
-      for (int i = threadIdx.x; i < a.n_out; i += blockDim.x) a.yzero[static_cast<size_t>(n) * a.ldy + i] = 0.f;
+    if (a.yzero && live) {  // split-K partials are added into y: start it at zero
+      float* yr = a.yzero + static_cast<size_t>(n) * a.ldy;
+      if ((reinterpret_cast<uintptr_t>(yr) & 15) == 0)  // n_out is a multiple of 32
+        for (int i = threadIdx.x; i < a.n_out / 4; i += blockDim.x)
+          reinterpret_cast<float4*>(yr)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      else
+        for (int i = threadIdx.x; i < a.n_out; i += blockDim.x) yr[i] = 0.f;
+    }
     return pow2f(e);
   };
 
@@ -589,6 +618,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
           advance_r();
         }
       pdl_wait();  // x image comes from the pre-pass
+      if (p.seam_peers && blockIdx.x == 0) tp_seam_advance(p.seam_peers, p.seam_world, p.seam_rank, p.seam);
       int it_x = blockIdx.x, kt_x = it_x < n_items ? item_k0(it_x) : 0, js_x = 0;  // x cursor
       uint32_t x_next = 0;
       // stages: one 64-k slice, or (packed form) the four slices of a K-tile

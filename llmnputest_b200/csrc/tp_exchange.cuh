@@ -257,21 +257,22 @@ __global__ void __launch_bounds__(kXchgThreads) tp_allreduce_kernel(const XchgPa
 // are summed by the kernel that consumes them (the tensor-core GEMM's x pre-pass), so
 // the all-reduce costs no kernel of its own.  Per use of seam z:
 //   post  (one thread per rank q, in the consumer, once the producer grid has
-//         completed): a system-scope fence, then seam_sig[rank][z] += 1 on rank q;
+//         completed): seam_sig[rank][z] += 1 on rank q, a system-scope release;
 //   wait  (thread s of every consumer CTA): until seam_sig[s][z] here exceeds
 //         seam_exp[s][z] (bounded; device error kDevTimeoutPeer);
-//   done  (every consumer CTA after its waits): the last CTA advances seam_exp[.][z].
+//   advance (one thread of the next kernel, past its PDL wait): seam_exp[.][z] += 1.
 // A rank rewrites its partial only in a later use of the same seam, after it has
 // waited in another seam that every rank posts only after finishing this one's reads:
 // decoders alternate two seams (O and down) per layer.
 __device__ __forceinline__ void tp_seam_post(void* const* peers, int world, int rank, int z) {
-  if (threadIdx.x < world) {
-    __threadfence_system();  // the producer grid's partial (complete at our PDL wait) before the signal
-    red_release_sys(&peer_ctl(peers[threadIdx.x])->seam_sig[rank][z]);
-  }
+  // the release orders the producer grid's partial (complete at our PDL wait) before the
+  // signal; one system-scope fence, no second one before it (it costs ~1.5 us)
+  if (threadIdx.x < world) red_release_sys(&peer_ctl(peers[threadIdx.x])->seam_sig[rank][z]);
 }
 
-// Every thread of the CTA calls it; true when every rank's partial has landed.
+// Every thread of the CTA calls it; true when every rank's partial has landed.  The
+// consumed counts seam_exp[.][z] stay as they are for the whole consumer grid: the kernel
+// after it advances them (tp_seam_advance), so no CTA contends on a shared counter here.
 __device__ __forceinline__ bool tp_seam_wait(void* const* peers, int world, int rank, int z,
                                              unsigned long long timeout_ns) {
   __shared__ int ok;
@@ -291,18 +292,14 @@ __device__ __forceinline__ bool tp_seam_wait(void* const* peers, int world, int 
     }
   }
   __syncthreads();
-  const bool r = ok != 0;
-  if (threadIdx.x == 0) {
-    // the last CTA past its waits advances the consumed counts for the next use
-    PeerCtl* ctl = peer_ctl(peers[rank]);
-    __threadfence();
-    if (atomicAdd(&ctl->seam_done[z], 1ull) == gridDim.x - 1ull) {
-      __threadfence();
-      for (int q = 0; q < world; ++q) ctl->seam_exp[q][z] += 1ull;
-      ctl->seam_done[z] = 0ull;
-    }
-  }
-  return r;
+  return ok != 0;
+}
+
+// One thread of the kernel launched right after the consumer grid (which has completed
+// once that kernel is past its PDL wait): every rank's use of seam z counted consumed.
+__device__ __forceinline__ void tp_seam_advance(void* const* peers, int world, int rank, int z) {
+  PeerCtl* ctl = peer_ctl(peers[rank]);
+  for (int q = 0; q < world; ++q) ctl->seam_exp[q][z] += 1ull;
 }
 
 }  // namespace b2
