@@ -127,6 +127,22 @@ def test_gqa_prefetch_kv(ops, bsz, ctx, lens):
         assert_close(got[b], ref[b], NS_COS, NS_REL, f"seq {b} len {lens[b]}")
 
 
+@pytest.mark.parametrize("bsz,ctx,lens", [
+    (32, 4096, None),                                   # the B = 32 decode shape, ragged lengths
+    (7, 9000, [9000, 1, 64, 65, 4097, 8999, 128]),      # lengths at and around 64-position edges
+    (48, 2048, [2048] * 48),                            # equal lengths, more pairs than CTA slots
+])
+def test_gqa_large_kv_vs_oracle(ops, bsz, ctx, lens):
+    """Launches whose K/V exceed 64 MB: unclustered, capped at one wave of CTAs, merged by
+    the combine kernel where a sequence is split.  Every sequence and head against the
+    oracle."""
+    lens = lens or [int(v) for v in np.random.default_rng(bsz).integers(1, ctx + 1, bsz)]
+    got, ref = _gqa_case(ops, bsz, 40, 8, ctx, lens, seed=ctx + 3 * bsz)
+    for b in range(bsz):
+        assert_close(got[b], ref[b], NS_COS, NS_REL, f"seq {b} len {lens[b]}")
+    assert ops.device_error() == 0
+
+
 def test_gqa_batch16_bf16_out(ops):
     lens = list(np.random.default_rng(5).integers(1, 4097, 16))
     got, ref = _gqa_case(ops, 16, 40, 8, 4096, lens, seed=16, out_f32=False)
