@@ -47,8 +47,8 @@ Q4_TILE, Q8_TILE = 5120, 8704
 # dram__bytes_read.sum + dram__bytes_write.sum over tile bytes for the GEMV launches
 # that stream from DRAM (one ncu capture of a layer's four GEMVs)
 GEMV_DRAM_RATIO = 1.003
-# the same ratio for the step's kernels (one ncu capture each, bench.py --profile-case,
-# summaries under profiles/): attention at B=32 ctx 4096 (268.94 MB read + 4.18 MB written
+# the same ratio for the step's kernels (one ncu capture each of bench.py --profile-case):
+# attention at B=32 ctx 4096 (268.94 MB read + 4.18 MB written
 # over 268.44 MB of K/V), the packed SwiGLU GEMM (26.44 over 26.21 MB of tiles), the q8
 # lm_head GEMM (273.19 + 9.50 over 273.11 MB of tiles; the logits are written)
 DRAM_RATIO = {"gqa_decode": 1.0175, "q4_swiglu_gemm": 1.009, "lm_head_q8_gemm": 1.035}
