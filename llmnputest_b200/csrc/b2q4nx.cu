@@ -410,6 +410,9 @@ AttnPlan attn_plan(int batch, int hq, int hkv, int head_dim, int max_len, int sm
       sl = (sl + 63) / 64 * 64;
       S = (max_len + sl - 1) / sl;
     }
+    // a one-wave launch with few splits merges them in a cluster (DSMEM) rather than
+    // through the workspace and a second kernel
+    if (S > 1 && S <= 16) pl.clustered = 1;
   }
   pl.n_splits = S;
   pl.split_len = sl;

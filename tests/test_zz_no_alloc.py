@@ -68,11 +68,11 @@ def _with_workspace(qkv, kc, vc, pos, hq, hkv, max_len):
 
 def test_static_scratch_matches_workspace_entry_point(lib):
     from llmnputest_b200 import ops
-    # Long contexts: the split partials go through the scratch (b2_gqa_decode_workspace_size is
-    # this entry point's own scratch need, both plan alike).  The short one merges its splits
-    # inside a thread-block cluster and needs no scratch at all.
-    cases = [(2, 40, 8, 32768, [32768, 20000], 11, True), (3, 40, 8, 32768, [32768, 100, 5000], 12, True),
-             (1, 40, 8, 512, [512], 13, False)]
+    # Long contexts with more than 16 splits: the split partials go through the scratch
+    # (b2_gqa_decode_workspace_size is this entry point's own scratch need, both plan alike).
+    # Up to 16 splits merge inside a thread-block cluster and need no scratch at all.
+    cases = [(2, 40, 8, 32768, [32768, 20000], 11, True), (1, 40, 8, 32768, [32768], 12, True),
+             (3, 40, 8, 32768, [32768, 100, 5000], 14, False), (1, 40, 8, 512, [512], 13, False)]
     for bsz, hq, hkv, ctx, lens, seed, uses_scratch in cases:  # calls in a row through the shared scratch
         assert (ops.gqa_decode_workspace_bytes(bsz, hq, hkv, 64, max(lens)) > 0) == uses_scratch
         qkv, kc, vc, pos = _case(bsz, hq, hkv, ctx, lens, seed)
