@@ -4,8 +4,9 @@ Value (the metric's "decode tokens/s at 1/2/4/8 B200")
 full random-init decode step of the dense GQA 3B -- 40 layers of RMSNorm, q4nx QKV,
 RoPE + GQA flash-decode, q4nx O, RMSNorm + fused SwiGLU gate/up, q4nx down; final
 RMSNorm and q8 lm_head -- at batch 32 (--batch) and context 4096, one CUDA graph per
-step, tensor-parallel over the ranks at N > 1 (kv heads, O rows, FFN rows / down
-K-tiles, vocab rows; the seams are peer-memory exchanges over NVLink).  Strong
+step, tensor-parallel over the ranks at N > 1 (kv heads, O input columns, FFN rows /
+down K-tiles, vocab rows; the O and down all-reduces summed over NVLink by the next
+GEMM's x pre-pass, the logits gathered by a peer-memory exchange).  Strong
 scaling: the same step, split over more GPUs.  tokens/s = batch / step time (max over
 ranks).  `roofline` is the step's dominant kernel, timed alone on the step's own
 buffers; `e2e` is the same step with its inputs copied in from pinned host memory and
@@ -1300,7 +1301,8 @@ def run_b200(args, rank: int, world: int) -> dict | None:
             "bytes_per_step": head["bytes_per_step"],
             "l2": f"inputs larger than L2 ({head['bytes_per_step'] / 1e9:.1f} GB of weights and KV cache per step)",
             "parallelism": "1 GPU" if world == 1 else
-                           f"tp{world}: kv heads, O rows, FFN rows / down K-tiles, vocab rows; peer exchanges over NVLink",
+                           f"tp{world}: kv heads, O input columns, FFN rows / down K-tiles, vocab rows; all-reduces "
+                           "summed over NVLink in the next GEMM's x pre-pass",
         },
         "gpu_launches": head["kernels_per_step"] * args.steps if head["kernels_per_step"] else None,
         "e2e": {"value": round(head["e2e_tok_s"], 1), "unit": "tok/s", "h2d_bytes_per_step": int(head["h2d"]),
