@@ -232,3 +232,22 @@ def test_tp_step_gloo_matches_single_rank(tmp_path, comm):
     a, b = torch.load(out1), torch.load(out2)
     cos, rel = orc.compare(b.numpy(), a.numpy())
     assert cos >= 0.99999 and rel <= 1e-3, (cos, rel)
+
+
+def test_pulled_seam_layout_and_peer_sum_checks():
+    """The peer region of the pulled-seam decoder holds each seam's partial (not a slot
+    array), and ops.PeerSum takes only fp32 [rows, cols] region buffers."""
+    from llmnputest_b200.ops import PeerSum
+    layout = tp_exchange_layout(CFG, 4, 2, pulled=True)
+    names = [n for n, _, _ in layout]
+    assert names == ["resid", "o_part", "down_part", "logits"]
+    assert dict((n, s) for n, s, _ in layout)["o_part"] == (4, CFG.hidden)
+    assert [n for n, _, _ in tp_exchange_layout(CFG, 4, 2)] == ["resid", "slots_o", "slots", "logits"]
+    region = SimpleNamespace(offsets={"o_part": (65536, (4, CFG.hidden), torch.float32),
+                                      "slots": (131072, (2, 4, CFG.hidden), torch.float32),
+                                      "attn": (196608, (4, 512), torch.bfloat16)})
+    ps = PeerSum(region, "o_part", 1)
+    assert (ps.offset, ps.ld, ps.rows, ps.seam) == (65536, CFG.hidden, 4, 1)
+    for bad in ("slots", "attn"):
+        with pytest.raises(ValueError):
+            PeerSum(region, bad, 0)
