@@ -3,13 +3,15 @@
 One process per GPU.  Every rank allocates one region (b2_peer_alloc), the ranks swap
 their CUDA IPC handles over the process group (all_gather_object: the host channel
 torch.distributed already has), and each maps the others' (b2_peer_open).  Buffers
-that other ranks write into -- the gathered attention heads, the residual stream, the
-all-reduce slots, the gathered logits -- are carved out of the region at the same
-offsets on every rank and wrapped as torch tensors without a copy.
+that other ranks read or write -- the residual stream, the all-reduce slots or the
+partials a pulled seam reads, the gathered logits -- are carved out of the region at
+the same offsets on every rank and wrapped as torch tensors without a copy.
 
-The exchanges replace the NCCL calls of a tensor-parallel decode step (all_gather of
-heads / rows / vocab, all_reduce of the K-sharded down projection); each is one small
-kernel that stores straight into the peers' memory and waits, bounded, for theirs.
+The exchanges replace the NCCL calls of a tensor-parallel decode step (all-reduce of
+the K-sharded O and down projections, all-gather of the vocab-sharded logits); each is
+one small kernel that stores straight into the peers' memory and waits, bounded, for
+theirs.  On the GEMM path the all-reduces need no kernel: ops.PeerSum hands a region
+buffer to the next GEMM's x pre-pass, which sums every rank's partial itself.
 """
 
 from __future__ import annotations
