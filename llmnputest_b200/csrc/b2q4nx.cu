@@ -99,7 +99,7 @@ inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_
 //   B2Q4NX_CTAS_PER_SM   force 1 or 2 GEMV CTAs per SM (default: 2 when they fit)
 //   B2Q4NX_MAX_STAGES    cap on the shared-memory pipeline depth (1..8)
 //   B2Q4NX_TC_SPLITS / _TC_RAW / _TC_XSTAGES / _TC_ABUFS   tensor-core GEMM split-K
-//                        count, raw and x pipeline depths, A buffers per slice
+//                        count, raw (<= 10) and x pipeline depths, A buffers per slice
 //   B2Q4NX_TC_PRE_RAW    raw stages the GEMM issues before its PDL wait (default: its
 //                        whole raw ring; 2-4 measured the same, 1 slower)
 //   B2Q4NX_TC_PREP_EARLY 1: the GEMM's x pre-pass releases the GEMM before its own wait
@@ -143,7 +143,7 @@ const Tuning& tuning() {
     if (const char* e = getenv("B2Q4NX_CTAS_PER_SM")) v.ctas_per_sm = std::max(0, std::min(2, atoi(e)));
     if (const char* e = getenv("B2Q4NX_MAX_STAGES")) v.max_stages = std::max(1, std::min(b2::kMaxStages, atoi(e)));
     if (const char* e = getenv("B2Q4NX_TC_SPLITS")) v.tc_splits = std::max(0, atoi(e));
-    if (const char* e = getenv("B2Q4NX_TC_RAW")) v.tc_raw = std::max(0, std::min(4, atoi(e)));
+    if (const char* e = getenv("B2Q4NX_TC_RAW")) v.tc_raw = std::max(0, std::min(10, atoi(e)));
     if (const char* e = getenv("B2Q4NX_TC_XSTAGES")) v.tc_xst = std::max(0, std::min(8, atoi(e)));
     if (const char* e = getenv("B2Q4NX_TC_ABUFS")) v.tc_abufs = std::max(0, std::min(2, atoi(e)));
     if (const char* e = getenv("B2Q4NX_TC_PRE_RAW")) v.tc_pre_raw = std::max(0, std::min(8, atoi(e)));
