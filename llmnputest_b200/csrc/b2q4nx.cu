@@ -662,6 +662,10 @@ int tc_gemm_common(int epi, const uint8_t* w0, const uint8_t* w1, int n_tile_row
     // accumulator buffers while those fit too
     p.n_issuers = (packed && 2 * nc <= b2::kTcTmemACol) ? 2 : 1;
     p.d_bufs = (!packed || 2 * p.n_issuers * nc <= b2::kTcTmemACol) ? 2 : 1;
+    // packed: a third A buffer when the accumulators leave 3 x 128 TMEM columns, so the
+    // dequant of K-tile j + 2 need not wait for the MMAs of K-tile j (B2Q4NX_TC_ABUFS=2: two)
+    if (packed)
+      p.a_bufs = (p.d_bufs * p.n_issuers * nc + 3 * b2::kTcTmemABuf <= 512 && tuning().tc_abufs != 2) ? 3 : 2;
   }
   auto kernel = qt == b2::kQ8 ? b2::q4_gemm_tc_kernel<b2::kTcEpiF32, true, b2::kQ8>
                 : epi == b2::kTcEpiSwiglu

@@ -62,8 +62,10 @@ constexpr int kTcRawStage = 4 * kTcRawSlot;
 constexpr int kTcMaxN = 256;
 constexpr int kTcXchgStride = 33;            // SwiGLU exchange row stride in floats (bank spread)
 constexpr int kTcXchgBytes = 64 * kTcXchgStride * 4 + 256 * 4;  // 64 rows x 32 tokens, then 2^-e per token
-constexpr int kTcTmemACol = 256;             // packed form: first A column in TMEM
+constexpr int kTcTmemACol = 256;             // packed form: first A column in TMEM with 2 A buffers
 constexpr int kTcTmemABuf = 128;             // packed form: columns per A buffer (one K-tile)
+// packed form: the a_bufs A buffers take the top a_bufs x 128 of the 512 TMEM columns (2:
+// from column 256; 3, when the accumulators fit in 128 columns: from column 128)
 
 // Packed weight: the tiles of a [n_tile_rows][k_tiles] weight reordered pair-major,
 // tile (tr, kt) at position (tr/2)*2*k_tiles + kt*np + tr%2 (np = tiles in tr's pair,
@@ -549,6 +551,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
   const int KT = p.k_tiles;
   const int n_items = p.n_row_tiles * p.n_splits * p.n_nsplit;  // -> (row tile, K-tile range, column block)
   const int AB = p.a_bufs;
+  const uint32_t a_base = TA ? 512u - static_cast<uint32_t>(AB) * kTcTmemABuf : 0u;  // first A column
   auto item_tile = [&](int it) { return (it / p.n_nsplit) / p.n_splits; };
   auto item_k0 = [&](int it) { return ((it / p.n_nsplit) % p.n_splits) * p.kt_per_split; };
   auto item_n0 = [&](int it) { return (it % p.n_nsplit) * ncta; };
@@ -689,6 +692,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
       const uint32_t xbytes = static_cast<uint32_t>(ncta) * 128;
       bool issued_any = false;
       uint32_t rseq = 0, t_it = 0;
+      int ab_c = 0;          // A buffer of K-tile rseq
+      uint32_t aph_c = 0u;   // its phase
       for (int it = blockIdx.x; it < n_items && !*abort_flag; it += gridDim.x, ++t_it) {
         const int buf = DB == 2 ? static_cast<int>(t_it & 1) : 0;
         const uint32_t uses = DB == 2 ? t_it >> 1 : t_it;  // earlier items on this buffer
@@ -698,9 +703,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
         const int k0 = item_k0(it), k1 = item_k1(it);
         uint32_t acc = 0;  // the partial's first MMA of the item starts it
         for (int kt = k0; kt < k1; ++kt, ++rseq) {
+          // A buffer rseq % AB and its phase, kept by increments (no division here)
+          const int ab = ab_c;
+          const uint32_t aph = aph_c;
+          if (++ab_c == AB) {
+            ab_c = 0;
+            aph_c ^= 1u;
+          }
           if ((kt - k0) % NI != e) continue;
-          const int ab = static_cast<int>(rseq & 1);  // AB == 2 in the packed form
-          const uint32_t aph = (rseq >> 1) & 1;
           const int xs = static_cast<int>(rseq % XS);
           const uint32_t xph = (rseq / XS) & 1;
           // a failed wait has set the abort flag, checked below
@@ -708,7 +718,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
               !mbar_wait_bounded(smem_u32(&x_full[xs]), xph, abort_flag, kDevTimeoutFull))
             break;
           tc_fence_after();
-          const uint32_t a_tmem = tmem_base + kTcTmemACol + ab * kTcTmemABuf;
+          const uint32_t a_tmem = tmem_base + a_base + ab * kTcTmemABuf;
 #pragma unroll
           for (int js = 0; js < 4; ++js) {
             const uint64_t bd = umma_desc_sw128(x0 + (4 * xs + js) * xbytes);
@@ -929,7 +939,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) q4_gemm_tc_kernel(const TcParam
         if (ok) {
           tc_fence_after();  // the MMAs that read this A buffer have completed
           const uint8_t* tl = smem + L.raw + rs * RAW_STAGE + q * TILE;
-          const uint32_t a_col = tmem_base + t_lane + kTcTmemACol + abuf * kTcTmemABuf;
+          const uint32_t a_col = tmem_base + t_lane + a_base + abuf * kTcTmemABuf;
 #pragma unroll
           for (int sb = 0; sb < 4; ++sb) {
             const int s = 4 * hh + sb;  // 32-k block of the K-tile
